@@ -1,0 +1,422 @@
+#!/usr/bin/env python
+"""Benchmark of the sqmix attention-mixer hot path (BASELINE.json metric).
+
+Workload: one decode token through all 10 full-attention layers
+of qwen35moe at 172032 keys per layer -- per layer the q4_0 KV append of the new
+token (with fused partial RoPE) and split-KV FlashAttention over the q4_0 cache
+with the sigmoid output gate.  Inputs are seeded synthetic N(0,1) tensors with the
+reference's shapes (no model weights are involved in the mixer).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sqmix|reference]
+
+N > 1 (under torchrun): the 172032 keys of every layer are split across the ranks;
+each rank attends over its slice and the (O, LSE) partials are all-gathered over
+NCCL and merged before the gate (strong scaling: total work fixed).
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "sqwen-moe-3090_b200"))
+
+N_LAYERS = 10
+N_KV = 172032
+HEAD_DIM = 256
+N_HEAD = 16
+N_HEAD_KV = 2
+N_ROT = 64
+FREQ_BASE = 1e7
+METRIC = "attn-mixer us/token @172K ctx decode (10 full-attn layers, q4_0 KV)"
+BYTES_PER_KEY = 576  # K + V q4_0 per token per layer
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        smax = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for s in self.samples:
+            for n, v in zip(names, s[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------------- #
+# CPU legs (oracle): cpu_baseline and --impl reference                          #
+# --------------------------------------------------------------------------- #
+
+def cpu_layer_inputs(n_kv: int, seed: int = 0):
+    import oracle
+
+    rng = np.random.default_rng(seed)
+    k = rng.standard_normal((n_kv, 512), dtype=np.float32)
+    v = rng.standard_normal((n_kv, 512), dtype=np.float32)
+    kq = oracle.q4_0_quantize(k)
+    vq = oracle.q4_0_quantize(v)
+    q = rng.standard_normal((1, N_HEAD, HEAD_DIM), dtype=np.float32)
+    gate = rng.standard_normal((1, N_HEAD, HEAD_DIM), dtype=np.float32)
+    return kq, vq, q, gate
+
+
+def cpu_layer(kq, vq, q, gate, n_kv):
+    """One layer on the CPU restatement: dequantise the q4_0 cache, RoPE Q, attend."""
+    import oracle
+
+    kd = oracle.q4_0_dequantize(kq, 512).reshape(n_kv, N_HEAD_KV, HEAD_DIM)
+    vd = oracle.q4_0_dequantize(vq, 512).reshape(n_kv, N_HEAD_KV, HEAD_DIM)
+    qr = oracle.rope_text(q, n_kv - 1, FREQ_BASE, N_ROT)
+    return oracle.attn(qr, kd, vd, gate, q_pos0=n_kv - 1, scale=1.0 / 16)
+
+
+def cpu_baseline(budget_s: float = 12.0):
+    import oracle
+
+    oracle.build()
+    cores = oracle.set_threads(os.cpu_count() or 1)
+    kq, vq, q, gate = cpu_layer_inputs(N_KV)
+    cpu_layer(kq, vq, q, gate, N_KV)  # warm
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        cpu_layer(kq, vq, q, gate, N_KV)
+        n += 1
+        if time.perf_counter() - t0 > budget_s or n >= N_LAYERS:
+            break
+    per_layer = (time.perf_counter() - t0) / n
+    return {"value": per_layer * N_LAYERS * 1e6, "unit": "us/token", "cores": cores, "kind": "port",
+            "sample": f"{n} layer(s) of 172032 q4_0 keys (dequant + RoPE + attention + gate), "
+                      f"scaled x{N_LAYERS / n:g} to 10 layers; C restatement of the ggml CPU nodes"}
+
+
+def run_reference(args, rank: int):
+    if rank != 0:
+        return None
+    import oracle
+
+    oracle.build()
+    cores = oracle.set_threads(os.cpu_count() or 1)
+    kq, vq, q, gate = cpu_layer_inputs(N_KV)
+    for _ in range(args.warmup):
+        cpu_layer(kq, vq, q, gate, N_KV)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_layer(kq, vq, q, gate, N_KV)  # one of the 10 layers per step
+    per_layer = (time.perf_counter() - t0) / args.steps
+    v = per_layer * N_LAYERS * 1e6
+    sample = (f"each step = 1 of the 10 layers (172032 q4_0 keys, dequant + RoPE + attention + gate) "
+              f"on {cores} threads, scaled x10; C restatement of the ggml CPU nodes "
+              "(ggml itself is not in this image)")
+    return {"metric": METRIC, "value": v, "unit": "us/token", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * 1e3,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic N(0,1), seed 0",
+            "config": {"workload": "config3: decode, 10 layers x 172032 q4_0 keys, 16/2 heads, d=256, n_q=1"},
+            "cpu_baseline": {"value": v, "unit": "us/token", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# --------------------------------------------------------------------------- #
+# GPU arm                                                                       #
+# --------------------------------------------------------------------------- #
+
+def run_gpu(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    import sqmix
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    n_local = N_KV // world
+    assert n_local * world == N_KV
+    cap = (n_local + 255) // 256 * 256
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+
+    # ---- resident state: 10 layers of q4_0 K/V for this rank's key slice ------
+    kv = sqmix.KvCache(n_layers=N_LAYERS, kv_cap=cap, device=local_rank)
+    kc = [kv.k_state(l) for l in range(N_LAYERS)]
+    vc = [kv.v_state(l) for l in range(N_LAYERS)]
+    chunk = 16384
+    for l in range(N_LAYERS):
+        for a in range(0, n_local, chunk):
+            n = min(chunk, n_local - a)
+            kk = torch.randn((n, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+            vv = torch.randn((n, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+            rows = torch.arange(a, a + n, device=dev)
+            sqmix.set_rows_q4_0(kk, vv, rows, kc[l], vc[l], cap, rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE,
+                                rope_pos_offset=rank * n_local)
+    # the new token is written at the last position of the last rank's slice
+    owner = world - 1
+    pos_new = N_KV - 1
+    local_row = pos_new - owner * n_local
+    q = torch.randn((N_LAYERS, 1, N_HEAD, HEAD_DIM), generator=g, device=dev)
+    gate = torch.randn((N_LAYERS, 1, N_HEAD, HEAD_DIM), generator=g, device=dev)
+    k_new = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+    v_new = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+    out = torch.empty((N_LAYERS, 1, N_HEAD, HEAD_DIM), device=dev)
+    step = torch.tensor([n_local, pos_new - rank * n_local], dtype=torch.int64, device=dev)
+    d_nkv, d_qpos = step[0:1], step[1:2]
+    d_row = torch.tensor([local_row], dtype=torch.int64, device=dev)
+    n_splits = sqmix.lib().sqmix_device_sm_count(local_rank)
+    ws = sqmix.new_fa_workspace(1, n_splits, dev)
+    torch.cuda.synchronize()
+
+    if world > 1:
+        o_loc = torch.empty((N_LAYERS, N_HEAD, HEAD_DIM), device=dev)
+        l_loc = torch.empty((N_LAYERS, N_HEAD), device=dev)
+        o_all = torch.empty((world, N_HEAD, HEAD_DIM), device=dev)
+        l_all = torch.empty((world, N_HEAD), device=dev)
+
+    def layer(l):
+        if rank == owner:
+            sqmix.set_rows_q4_0(k_new[l], v_new[l], d_row, kc[l], vc[l], cap, rope_n_rot=N_ROT,
+                                rope_freq_base=FREQ_BASE,
+                                rope_pos_offset=owner * n_local)
+        if world == 1:
+            sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=gate[l], rope_n_rot=N_ROT,
+                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=out[l], workspace=ws,
+                                 n_splits=n_splits)
+        else:
+            sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=None, rope_n_rot=N_ROT,
+                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=o_loc[l], lse=l_loc[l],
+                                 workspace=ws,
+                                 n_splits=n_splits)
+            dist.all_gather_into_tensor(o_all, o_loc[l])
+            dist.all_gather_into_tensor(l_all, l_loc[l])
+            sqmix.attn_merge_lse(o_all, l_all, gate=gate[l, 0], out=out[l, 0])
+
+    def step_fn():
+        for l in range(N_LAYERS):
+            layer(l)
+
+    stream = torch.cuda.current_stream()
+    graph = None
+    if world == 1 and not args.no_graph:
+        s = torch.cuda.Stream()
+        s.wait_stream(stream)
+        with torch.cuda.stream(s):
+            step_fn()  # warm the launch path outside capture
+        stream.wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step_fn()
+        torch.cuda.synchronize()
+
+    run = graph.replay if graph is not None else step_fn
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    sampler = ClockSampler(local_rank)
+    with sampler:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    us_per_token = ms * 1e3 / args.steps
+    launches_per_step = N_LAYERS * ((1 if rank == owner else 0) + 2 + (1 if world > 1 else 0))
+
+    # ---- dominant kernel alone: flash_attn_ext over each layer in turn ---------
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    reps = max(3, args.steps)
+    for l in range(N_LAYERS):
+        sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=gate[l], rope_n_rot=N_ROT,
+                             rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=out[l], workspace=ws,
+                                 n_splits=n_splits)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        for l in range(N_LAYERS):
+            sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=gate[l], rope_n_rot=N_ROT,
+                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=out[l], workspace=ws,
+                                 n_splits=n_splits)
+    e1.record()
+    torch.cuda.synchronize()
+    fa_us = e0.elapsed_time(e1) * 1e3 / (reps * N_LAYERS)
+    alg_bytes = n_local * BYTES_PER_KEY + 3 * N_HEAD * HEAD_DIM * 4
+    hbm, peak_kind = peaks()
+    achieved = alg_bytes / (fa_us * 1e-6) / 1e9
+
+    # ---- end to end through the public API with host buffers -------------------
+    h_q = torch.randn((N_LAYERS, 1, N_HEAD, HEAD_DIM)).pin_memory()
+    h_gate = torch.randn((N_LAYERS, 1, N_HEAD, HEAD_DIM)).pin_memory()
+    h_k = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM)).pin_memory()
+    h_v = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM)).pin_memory()
+    h_out = torch.empty((N_LAYERS, 1, N_HEAD, HEAD_DIM)).pin_memory()
+    h_step = torch.tensor([n_local, pos_new - rank * n_local], dtype=torch.int64).pin_memory()
+    h2d = (h_q.numel() + h_gate.numel()) * 4 + (h_k.numel() + h_v.numel()) * 4 * (1 if rank == owner else 0) + 16
+    d2h = h_out.numel() * 4
+
+    def e2e_step():
+        q.copy_(h_q, non_blocking=True)
+        gate.copy_(h_gate, non_blocking=True)
+        if rank == owner:
+            k_new.copy_(h_k, non_blocking=True)
+            v_new.copy_(h_v, non_blocking=True)
+        step.copy_(h_step, non_blocking=True)
+        run()
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_us = e2e_ms * 1e3 / args.steps
+
+    if graph is not None:
+        del graph
+    if rank != 0:
+        return None
+    res = {
+        "metric": METRIC, "value": us_per_token, "unit": "us/token", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": us_per_token / 1e3, "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "q4_0 KV x f16 tensor-core fragments, f32 accum",
+        "data": "synthetic N(0,1) K/V/Q/gate (seeded), q4_0-quantised by the append kernel",
+        "config": {"workload": "config3: decode 1 token, 10 full-attn layers x 172032 q4_0 keys, "
+                               "16 Q / 2 KV heads, d=256, RoPE 64/1e7, sigmoid gate",
+                   "n_q": 1, "keys_per_layer": N_KV, "keys_per_gpu": n_local, "parallelism": f"split-KV x{world}",
+                   "l2": "inputs larger than L2: 10 x 99 MB of KV cycled per step",
+                   "cuda_graph": graph is not None or False},
+        "tokens_per_s": 1e6 / us_per_token,
+        "roofline": {"bound": "hbm", "kernel": "sqmix_fa_decode (split-KV decode + merge)",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": peak_kind, "traffic": None, "alg_bytes_per_launch": alg_bytes,
+                     "launch_us": fa_us},
+        "clocks": sampler.summary(),
+        "gpu_launches": launches_per_step * args.steps,
+        "e2e": {"value": e2e_us, "unit": "us/token", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+    }
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="sqmix", choices=["sqmix", "reference"])
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+    res = run_gpu(args, rank, world, local_rank)
+    if res is not None:
+        if cpu is not None:
+            res["cpu_baseline"] = cpu
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

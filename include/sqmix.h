@@ -1,0 +1,258 @@
+/*
+ * sqmix.h -- C ABI of the B200 (sm_100a) attention-mixer kernels for qwen35moe.
+ *
+ * This library replaces, for exactly these nodes, the ggml FFI that sqwen's graph
+ * builder calls (src/backend/ffi.rs:232-481):
+ *
+ *   ggml_set_rows (q4_0 KV append)      -> sqmix_kv_append_q4_0
+ *   ggml_rope_multi (IMROPE, text pos)  -> fused into sqmix_kv_append_q4_0 (K)
+ *                                          and sqmix_fa_decode (Q)
+ *   ggml_flash_attn_ext + sigmoid gate  -> sqmix_fa_decode, sqmix_attn_merge_lse
+ *   ggml_gated_delta_net (+ state cpy)  -> sqmix_gdn_decode
+ *   ggml_get_rows (state plane select)  -> the `sel` argument of sqmix_gdn_decode
+ *   ggml_cpy of GDN snapshot planes     -> written in place by sqmix_gdn_decode
+ *
+ * and the engine-side bookkeeping that feeds them (src/engine/kv.rs KvCache,
+ * src/model/gdn.rs GdnState, src/model/graph.rs snapshot_gdn/restore_gdn).
+ *
+ * Conventions (all entry points):
+ *   - Return int status: SQMIX_OK (0) or a negative SQMIX_E* code; a message for
+ *     the last failure on the calling thread is in sqmix_last_error().  Nothing
+ *     aborts the process (unlike ggml's GGML_ABORT on unsupported FA).
+ *   - Kernel entry points take device pointers, launch on the given stream, never
+ *     allocate, never synchronise, and read positions/lengths from device scalars
+ *     so they can be replayed from a CUDA graph with fixed pointers
+ *     (the same constraint sqwen meets with set_rows: src/engine/kv.rs:300-312).
+ *   - Geometry is qwen35moe's: head_dim 256, 16 query heads over 2 KV heads
+ *     (block GQA, kv_head = h / 8), GDN d_k = d_v = 128.
+ *   - `sqmix_stream_t` is a cudaStream_t (NULL = legacy default stream).
+ */
+#ifndef SQMIX_H
+#define SQMIX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *sqmix_stream_t;
+
+/* ---- status codes ------------------------------------------------------- */
+#define SQMIX_OK 0
+#define SQMIX_EINVAL (-1)    /* bad argument (null pointer, unsupported shape, ...) */
+#define SQMIX_ECUDA (-2)     /* a CUDA runtime call failed */
+#define SQMIX_ETIMEOUT (-3)  /* a bounded device-side wait gave up */
+#define SQMIX_ENOSPC (-4)    /* workspace or host buffer too small */
+#define SQMIX_EOVERFLOW (-5) /* KV cache overflow (kv.rs:240-245) */
+#define SQMIX_ERANGE (-6)    /* position out of range (kv.rs:284-297) */
+
+/* ---- element types (ggml type ids, src/backend/ffi.rs:44-101) ----------- */
+#define SQMIX_F32 0
+#define SQMIX_F16 1
+#define SQMIX_BF16 30
+
+/* ---- fixed geometry ----------------------------------------------------- */
+#define SQMIX_HEAD_DIM 256     /* full-attention head_dim (arch.rs validates 256) */
+#define SQMIX_N_HEAD 16        /* query heads */
+#define SQMIX_N_HEAD_KV 2      /* KV heads */
+#define SQMIX_QK4_0 32         /* q4_0 block (kv.rs:33) */
+#define SQMIX_KV_GROUP 16      /* tokens per tile group of the tiled q4_0 cache */
+#define SQMIX_KV_PAD 256       /* n_kv padding / capacity alignment (kv.rs:37) */
+#define SQMIX_GDN_D 128        /* GDN head_k_dim == head_v_dim */
+
+const char *sqmix_version(void);
+/* Message for the last failing call on this thread ("" if none). */
+const char *sqmix_last_error(void);
+/* Number of SMs of `device` (sizes split-KV grids). */
+int sqmix_device_sm_count(int device);
+
+/* ========================================================================
+ * q4_0 KV cache: tiled layout
+ *
+ * Each layer owns a K cache and a V cache of `capacity` token rows (capacity a
+ * multiple of SQMIX_KV_PAD).  Every 32-element block is the ggml q4_0 block
+ * bit-for-bit (fp16 d, 16 nibble bytes: element j low nibble of byte j, element
+ * j+16 high nibble), 576 bytes per token per layer for K+V, as in
+ * kv.rs:179-189.  Blocks are arranged in 16-token groups so that the decode
+ * kernel's 128-bit shared-memory loads land directly in tensor-core fragments.
+ * sqmix_kv_convert_rows translates to and from ggml's row layout
+ * ([n_embd_k_gqa=512, cap] q4_0, kv.rs:124-134).
+ * ======================================================================== */
+
+/* Bytes of ONE K (or V) cache of `capacity` rows with SQMIX_N_HEAD_KV heads. */
+size_t sqmix_kv_cache_bytes(int64_t capacity);
+
+typedef struct sqmix_kv_append_args {
+    const void *k;          /* [T][2][256] new K rows (before RoPE) */
+    const void *v;          /* [T][2][256] new V rows */
+    int32_t dtype;          /* SQMIX_F32 / SQMIX_F16 / SQMIX_BF16 for k and v */
+    int64_t k_stride_tok;   /* elements between consecutive tokens of k (>= 512) */
+    int64_t v_stride_tok;   /* same for v */
+    int32_t n_tokens;       /* T >= 1 */
+    const int64_t *rows;    /* device I64 [T]: destination row = absolute position
+                               (ggml_set_rows idxs, kv.rs:313-320, graph.rs:476-480) */
+    void *k_cache;          /* tiled q4_0 K cache of this layer */
+    void *v_cache;          /* tiled q4_0 V cache of this layer */
+    int64_t capacity;       /* rows in each cache */
+    int32_t rope_n_rot;     /* > 0: rotate K dims [0, n_rot) at text position
+                               rows[t] + rope_pos_offset */
+    float rope_freq_base;   /* theta base (qwen35moe: 1e7) */
+    int64_t rope_pos_offset;/* absolute position of row 0 (0 unless the cache holds a
+                               slice of the sequence, e.g. split-KV across GPUs) */
+} sqmix_kv_append_args;
+
+/* KvCache::append -> ggml_set_rows(q4_0) (kv.rs:313-399), with the IMROPE of K
+ * (attn.rs:183-204, text positions) fused in front of quantisation.  Quantisation
+ * is bit-exact with ggml quantize_row_q4_0 for the same f32 input. */
+int sqmix_kv_append_q4_0(const sqmix_kv_append_args *args, sqmix_stream_t stream);
+
+/* Translate rows [row0, row0+n_rows) between a tiled cache and ggml row layout
+ * (n_rows x 288 bytes, row r at rows_buf + (r-row0)*288).  which: 0 = K cache,
+ * 1 = V cache (their tilings differ).  to_rows != 0: tiled -> rows; 0: rows ->
+ * tiled (imports a ggml cache).  Device pointers. */
+int sqmix_kv_convert_rows(void *tiled_cache, void *rows_buf, int64_t capacity, int64_t row0,
+                          int64_t n_rows, int32_t which, int32_t to_rows, sqmix_stream_t stream);
+
+/* ========================================================================
+ * Split-KV attention decode (ggml_flash_attn_ext, attn.rs:238-249) with the
+ * sigmoid output gate (attn.rs:282-283) fused into the merge.
+ * ======================================================================== */
+
+typedef struct sqmix_fa_args {
+    const void *q;            /* [n_q][16][256] queries (before RoPE) */
+    int32_t q_dtype;
+    int64_t q_stride_tok;     /* elements between tokens */
+    int64_t q_stride_head;    /* elements between heads (512 for the QG-interleaved
+                                 projection of attn.rs:131-158) */
+    const void *gate;         /* nullable: [n_q][16][256], out *= sigmoid(gate) */
+    int32_t gate_dtype;
+    int64_t gate_stride_tok;
+    int64_t gate_stride_head;
+    const void *k_cache;      /* tiled q4_0 caches of this layer */
+    const void *v_cache;
+    int64_t capacity;
+    const int64_t *n_kv;      /* device scalar: keys [0, n_kv) are stored */
+    const int64_t *q_pos0;    /* device scalar: absolute position of query 0;
+                                 query t sees keys j <= q_pos0 + t (graph.rs:553-559) */
+    int32_t n_q;              /* 1 or 2 (decode, MTP verify) */
+    float scale;              /* softmax scale (1/sqrt(256) = 1/16) */
+    int32_t rope_n_rot;       /* > 0: rotate Q dims [0, n_rot) at positions
+                                 q_pos0 + t + rope_pos_offset */
+    float rope_freq_base;
+    int64_t rope_pos_offset;  /* as in sqmix_kv_append_args */
+    float *out;               /* [n_q][16][256] f32 */
+    float *lse;               /* nullable [n_q][16]: ln sum_j exp(scale * s_j) */
+    void *workspace;          /* device scratch, sqmix_fa_workspace_bytes(); its
+                                 first 256 bytes must be zero before first use */
+    size_t workspace_bytes;
+    int32_t n_splits;         /* 0 = one split per SM; else the split count */
+} sqmix_fa_args;
+
+size_t sqmix_fa_workspace_bytes(int32_t n_splits, int32_t n_q);
+int sqmix_fa_decode(const sqmix_fa_args *args, sqmix_stream_t stream);
+
+/* Merge n_parts normalised partial attentions (O_p, lse_p) over disjoint key sets
+ * (split-KV across GPUs): out = sum_p O_p exp(lse_p - L) with L = log sum exp(lse_p),
+ * then out *= sigmoid(gate) when gate != NULL.  o_parts [n_parts][n_rows][256],
+ * lse_parts [n_parts][n_rows]; gate [n_rows][256] f32 or NULL; lse_out nullable. */
+int sqmix_attn_merge_lse(int32_t n_parts, int32_t n_rows, const float *o_parts,
+                         const float *lse_parts, const float *gate, float *out, float *lse_out,
+                         sqmix_stream_t stream);
+
+/* ========================================================================
+ * Gated delta net (ggml_gated_delta_net, gdn.rs:489-500; recurrence gdn.rs:9-24)
+ *
+ * State planes: [n_seqs][n_planes][H_v][128 (value j)][128 (key i)] f32; element
+ * S[i][j] of head h sits at ((h*128 + j)*128 + i).  n_planes = 1 + n_rs
+ * (gdn.rs:71-106).  The kernel reads plane sel[seq] (MTP rollback, gdn.rs:445-463,
+ * graph.rs:190-196) and writes the state after T-s tokens into plane s for
+ * s < n_snap (slot 0 = final; gdn.rs:484-538, graph.rs:884-912).
+ * ======================================================================== */
+
+typedef struct sqmix_gdn_args {
+    const void *q;            /* [n_seqs][T][H_k][128] */
+    const void *k;            /* [n_seqs][T][H_k][128] */
+    const void *v;            /* [n_seqs][T][H_v][128] */
+    int32_t dtype;            /* of q, k, v */
+    int64_t qk_stride_tok;    /* elements between tokens of q and k */
+    int64_t v_stride_tok;
+    int64_t qk_stride_seq;
+    int64_t v_stride_seq;
+    const float *g;           /* [n_seqs][T][H_v] log-decay (<= 0) */
+    const float *beta;        /* [n_seqs][T][H_v] */
+    float *state;             /* [n_seqs][n_planes][H_v][128][128] */
+    int32_t n_planes;
+    const int32_t *sel;       /* device I32 [n_seqs] plane to read; NULL = plane 0 */
+    int32_t n_seqs;
+    int32_t n_tokens;
+    int32_t h_k;              /* q/k heads (16); value head hv reads q/k head hv % h_k */
+    int32_t h_v;              /* value heads (32) */
+    int32_t n_snap;           /* 1 <= n_snap <= min(T, n_planes) */
+    float l2_eps;             /* > 0: L2-normalise q and k per head first (gdn.rs:126-142) */
+    float *out;               /* [n_seqs][T][H_v][128] f32 */
+} sqmix_gdn_args;
+
+int sqmix_gdn_decode(const sqmix_gdn_args *args, sqmix_stream_t stream);
+
+/* Copy whole planes: dst[i] <- src[i] for n_planes planes of `plane_elems` f32
+ * (the state ggml_cpy of graph.rs:884-912 and get_rows of gdn.rs:445-463 when a
+ * caller wants a materialised plane).  Device pointers. */
+int sqmix_gdn_state_copy(float *dst, const float *src, int64_t plane_elems, int32_t n_planes,
+                         sqmix_stream_t stream);
+
+/* ========================================================================
+ * Host-side state objects (the engine's bookkeeping, in C++)
+ * ======================================================================== */
+
+/* KvCache (kv.rs:67-448): per-layer tiled q4_0 K/V caches + shared cursor. */
+typedef struct sqmix_kvcache sqmix_kvcache;
+
+int sqmix_kvcache_create(int32_t n_layers, int64_t kv_cap, int32_t device, sqmix_kvcache **out);
+void sqmix_kvcache_destroy(sqmix_kvcache *kv);
+int sqmix_kvcache_zero(sqmix_kvcache *kv, sqmix_stream_t stream);       /* kv.rs:160-170 */
+int sqmix_kvcache_begin_step(sqmix_kvcache *kv, int32_t n_tokens);    /* kv.rs:239-253 */
+int sqmix_kvcache_rewind_to(sqmix_kvcache *kv, int64_t pos);          /* kv.rs:284-297 */
+void sqmix_kvcache_reset(sqmix_kvcache *kv);                           /* kv.rs:274-278 */
+int64_t sqmix_kvcache_n_used(const sqmix_kvcache *kv);
+int64_t sqmix_kvcache_step_start(const sqmix_kvcache *kv);
+int64_t sqmix_kvcache_n_kv_padded(const sqmix_kvcache *kv);           /* kv.rs:224-226 */
+int64_t sqmix_kvcache_capacity(const sqmix_kvcache *kv);              /* logical kv_cap */
+int64_t sqmix_kvcache_capacity_alloc(const sqmix_kvcache *kv);        /* padded to 256 */
+size_t sqmix_kvcache_bytes_per_token(const sqmix_kvcache *kv);        /* kv.rs:179-189 */
+void *sqmix_kvcache_k(sqmix_kvcache *kv, int32_t layer);
+void *sqmix_kvcache_v(sqmix_kvcache *kv, int32_t layer);
+/* Device I64 block {n_kv, q_pos0, rows[0..max_tokens)} for the current step;
+ * refreshed by sqmix_kvcache_upload_step (one async H2D from pinned memory,
+ * the analogue of fill_inputs, graph.rs:394-428). */
+const int64_t *sqmix_kvcache_device_step(const sqmix_kvcache *kv);
+int sqmix_kvcache_upload_step(sqmix_kvcache *kv, sqmix_stream_t stream);
+int32_t sqmix_kvcache_max_step_tokens(const sqmix_kvcache *kv);
+
+/* GdnState (gdn.rs:71-120) for n_layers GDN layers: 1 + n_rs planes per layer. */
+typedef struct sqmix_gdnstate sqmix_gdnstate;
+
+int sqmix_gdnstate_create(int32_t n_layers, int32_t h_v, int32_t n_rs, int32_t device,
+                          sqmix_gdnstate **out);
+void sqmix_gdnstate_destroy(sqmix_gdnstate *st);
+int sqmix_gdnstate_zero(sqmix_gdnstate *st, sqmix_stream_t stream);   /* graph.rs:206-222 */
+float *sqmix_gdnstate_planes(sqmix_gdnstate *st, int32_t layer);
+int32_t sqmix_gdnstate_n_planes(const sqmix_gdnstate *st);
+/* set_recurrent_sel (graph.rs:190-196): clamps to n_rs; one-shot, consumed by the
+ * next upload.  Returns the stored value. */
+int32_t sqmix_gdnstate_set_sel(sqmix_gdnstate *st, int32_t sel);
+int32_t sqmix_gdnstate_sel(const sqmix_gdnstate *st);
+const int32_t *sqmix_gdnstate_device_sel(const sqmix_gdnstate *st);
+int sqmix_gdnstate_upload_sel(sqmix_gdnstate *st, sqmix_stream_t stream);
+/* Checkpoint of plane 0 of every layer: u64 little-endian payload length, then
+ * the raw f32 planes (graph.rs:316-350).  snapshot: D2H + stream sync. */
+size_t sqmix_gdnstate_snapshot_bytes(const sqmix_gdnstate *st);
+int sqmix_gdnstate_snapshot(sqmix_gdnstate *st, void *host_buf, size_t bytes, sqmix_stream_t stream);
+int sqmix_gdnstate_restore(sqmix_gdnstate *st, const void *host_buf, size_t bytes,
+                           sqmix_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SQMIX_H */

@@ -1,0 +1,174 @@
+"""CPU parity oracle for the sqmix attention-mixer kernels.
+
+TEST INFRASTRUCTURE ONLY.  Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU
+legs of ``bench.py`` (``cpu_baseline`` and ``--impl reference``) may import this
+package.  The product library (``libsqmix.so`` and the ``sqmix`` host package) never
+imports, links or calls it.
+
+The arithmetic lives in ``sqmix_oracle.c`` (a C restatement of the ggml nodes that
+sqwen calls; see that file's header for the reference citations and for which
+nodes are pinned by golden vectors).  This module is a thin numpy/ctypes wrapper.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libsqmix_oracle.so")
+_lib = None
+
+QK4_0 = 32
+Q4_0_BLOCK_BYTES = 18
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (gcc; no GPU needed)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        f32p = ctypes.POINTER(ctypes.c_float)
+        u8p = ctypes.POINTER(ctypes.c_uint8)
+        i32p = ctypes.POINTER(ctypes.c_int32)
+        i64 = ctypes.c_int64
+        L.oracle_f32_to_f16.argtypes = [ctypes.c_float]
+        L.oracle_f32_to_f16.restype = ctypes.c_uint16
+        L.oracle_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.oracle_f16_to_f32.restype = ctypes.c_float
+        L.oracle_q4_0_quantize_rows.argtypes = [f32p, i64, i64, u8p]
+        L.oracle_q4_0_dequantize_rows.argtypes = [u8p, i64, i64, f32p]
+        L.oracle_rope_imrope.argtypes = [f32p, i64, i64, i64, i32p, i32p, ctypes.c_float,
+                                         ctypes.c_int32]
+        L.oracle_rope_text.argtypes = [f32p, i64, i64, i64, i64, ctypes.c_float, ctypes.c_int32]
+        L.oracle_attn.argtypes = [f32p, f32p, f32p, f32p, i64, i64, i64, i64, i64, i64,
+                                  ctypes.c_float, f32p, f32p]
+        L.oracle_l2norm_rows.argtypes = [f32p, i64, i64, ctypes.c_float]
+        L.oracle_gdn.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, i64, i64, i64, i64, i64,
+                                 f32p, f32p]
+        L.oracle_set_threads.argtypes = [ctypes.c_int]
+        L.oracle_set_threads.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _f32(a):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    return a, a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+def _nullf32():
+    return ctypes.POINTER(ctypes.c_float)()
+
+
+def set_threads(n: int) -> int:
+    """Set the OpenMP thread count; returns the count now in effect."""
+    return lib().oracle_set_threads(int(n))
+
+
+def f32_to_f16_bits(x: float) -> int:
+    return int(lib().oracle_f32_to_f16(float(x)))
+
+
+def f16_bits_to_f32(h: int) -> float:
+    return float(lib().oracle_f16_to_f32(int(h)))
+
+
+def q4_0_quantize(x: np.ndarray) -> np.ndarray:
+    """Rows of f32 (last dim a multiple of 32) -> ggml q4_0 rows (uint8, 18 B/block)."""
+    x = np.asarray(x, dtype=np.float32)
+    n = x.shape[-1]
+    assert n % QK4_0 == 0
+    rows = int(np.prod(x.shape[:-1])) if x.ndim > 1 else 1
+    xs, xp = _f32(x.reshape(rows, n))
+    out = np.zeros((rows, n // QK4_0 * Q4_0_BLOCK_BYTES), dtype=np.uint8)
+    lib().oracle_q4_0_quantize_rows(xp, rows, n, out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)))
+    return out.reshape(*x.shape[:-1], n // QK4_0 * Q4_0_BLOCK_BYTES)
+
+
+def q4_0_dequantize(q: np.ndarray, n_per_row: int) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    rows = q.size // (n_per_row // QK4_0 * Q4_0_BLOCK_BYTES)
+    out = np.zeros((rows, n_per_row), dtype=np.float32)
+    lib().oracle_q4_0_dequantize_rows(q.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), rows,
+                                      n_per_row, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return out.reshape(*q.shape[:-1], n_per_row)
+
+
+def rope_imrope(x: np.ndarray, pos: np.ndarray, sections, freq_base: float, n_rot: int) -> np.ndarray:
+    """x [T][H][D]; pos i32 [4*T] (t/h/w/e streams). Returns a rotated copy."""
+    xs, xp = _f32(np.array(x, dtype=np.float32, copy=True))
+    T, H, D = xs.shape
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    sec = np.ascontiguousarray(sections, dtype=np.int32)
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    lib().oracle_rope_imrope(xp, T, H, D, pos.ctypes.data_as(i32p), sec.ctypes.data_as(i32p),
+                             float(freq_base), int(n_rot))
+    return xs
+
+
+def rope_text(x: np.ndarray, pos0: int, freq_base: float, n_rot: int) -> np.ndarray:
+    """x [T][H][D], text positions pos0 + t in all four streams. Returns a copy."""
+    xs, xp = _f32(np.array(x, dtype=np.float32, copy=True))
+    T, H, D = xs.shape
+    lib().oracle_rope_text(xp, T, H, D, int(pos0), float(freq_base), int(n_rot))
+    return xs
+
+
+def attn(q, k, v, gate=None, q_pos0: int = 0, scale: float | None = None, want_lse=False):
+    """q [T][Hq][D]; k, v [n_kv][Hkv][D] (dequantised); gate [T][Hq][D] or None."""
+    qs, qp = _f32(q)
+    ks, kp = _f32(k)
+    vs, vp = _f32(v)
+    T, Hq, D = qs.shape
+    n_kv, Hkv, _ = ks.shape
+    if scale is None:
+        scale = 1.0 / np.sqrt(D)
+    if gate is not None:
+        gs, gp = _f32(gate)
+    else:
+        gp = _nullf32()
+    out = np.zeros((T, Hq, D), dtype=np.float32)
+    lse = np.zeros((T, Hq), dtype=np.float32)
+    f32p = ctypes.POINTER(ctypes.c_float)
+    lib().oracle_attn(qp, kp, vp, gp, T, Hq, Hkv, D, n_kv, int(q_pos0), float(scale),
+                      out.ctypes.data_as(f32p), lse.ctypes.data_as(f32p))
+    return (out, lse) if want_lse else out
+
+
+def l2norm(x: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+    xs, xp = _f32(np.array(x, dtype=np.float32, copy=True))
+    n = xs.shape[-1]
+    lib().oracle_l2norm_rows(xp, xs.size // n, n, float(eps))
+    return xs
+
+
+def gdn(q, k, v, g, beta, state, n_snap: int = 1):
+    """Sequential gated delta rule.
+
+    q, k [T][Hk][d]; v [T][Hv][d]; g, beta [T][Hv]; state [Hv][d(j)][d(i)].
+    Returns (out [T][Hv][d], snaps [n_snap][Hv][d][d]).
+    """
+    qs, qp = _f32(q)
+    ks, kp = _f32(k)
+    vs, vp = _f32(v)
+    gs, gp = _f32(g)
+    bs, bp = _f32(beta)
+    ss, sp = _f32(state)
+    T, Hk, d = qs.shape
+    Hv = vs.shape[1]
+    out = np.zeros((T, Hv, d), dtype=np.float32)
+    snaps = np.zeros((n_snap, Hv, d, d), dtype=np.float32)
+    f32p = ctypes.POINTER(ctypes.c_float)
+    lib().oracle_gdn(qp, kp, vp, gp, bp, sp, T, Hk, Hv, d, int(n_snap),
+                     out.ctypes.data_as(f32p), snaps.ctypes.data_as(f32p))
+    return out, snaps

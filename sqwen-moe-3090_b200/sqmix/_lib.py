@@ -1,0 +1,156 @@
+"""ctypes binding of libsqmix.so (declared in include/sqmix.h).
+
+The library is built in-tree by ``sqwen-moe-3090_b200/build.py``.  There is no
+fallback: if the shared library is missing or fails to load, every entry point
+raises, so a GPU run can never silently take another code path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libsqmix.so")
+
+SQMIX_OK = 0
+SQMIX_EINVAL = -1
+SQMIX_ECUDA = -2
+SQMIX_ETIMEOUT = -3
+SQMIX_ENOSPC = -4
+SQMIX_EOVERFLOW = -5
+SQMIX_ERANGE = -6
+
+SQMIX_F32 = 0
+SQMIX_F16 = 1
+SQMIX_BF16 = 30
+
+ERROR_NAMES = {
+    SQMIX_EINVAL: "SQMIX_EINVAL",
+    SQMIX_ECUDA: "SQMIX_ECUDA",
+    SQMIX_ETIMEOUT: "SQMIX_ETIMEOUT",
+    SQMIX_ENOSPC: "SQMIX_ENOSPC",
+    SQMIX_EOVERFLOW: "SQMIX_EOVERFLOW",
+    SQMIX_ERANGE: "SQMIX_ERANGE",
+}
+
+
+class SqmixError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERROR_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+c_void_p = ctypes.c_void_p
+c_int32 = ctypes.c_int32
+c_int64 = ctypes.c_int64
+c_float = ctypes.c_float
+c_size_t = ctypes.c_size_t
+
+
+class KvAppendArgs(ctypes.Structure):
+    _fields_ = [
+        ("k", c_void_p), ("v", c_void_p), ("dtype", c_int32),
+        ("k_stride_tok", c_int64), ("v_stride_tok", c_int64), ("n_tokens", c_int32),
+        ("rows", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p), ("capacity", c_int64),
+        ("rope_n_rot", c_int32), ("rope_freq_base", c_float), ("rope_pos_offset", c_int64),
+    ]
+
+
+class FaArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("q_dtype", c_int32), ("q_stride_tok", c_int64), ("q_stride_head", c_int64),
+        ("gate", c_void_p), ("gate_dtype", c_int32), ("gate_stride_tok", c_int64),
+        ("gate_stride_head", c_int64),
+        ("k_cache", c_void_p), ("v_cache", c_void_p), ("capacity", c_int64),
+        ("n_kv", c_void_p), ("q_pos0", c_void_p), ("n_q", c_int32), ("scale", c_float),
+        ("rope_n_rot", c_int32), ("rope_freq_base", c_float), ("rope_pos_offset", c_int64),
+        ("out", c_void_p), ("lse", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("n_splits", c_int32),
+    ]
+
+
+class GdnArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("dtype", c_int32),
+        ("qk_stride_tok", c_int64), ("v_stride_tok", c_int64), ("qk_stride_seq", c_int64),
+        ("v_stride_seq", c_int64), ("g", c_void_p), ("beta", c_void_p), ("state", c_void_p),
+        ("n_planes", c_int32), ("sel", c_void_p), ("n_seqs", c_int32), ("n_tokens", c_int32),
+        ("h_k", c_int32), ("h_v", c_int32), ("n_snap", c_int32), ("l2_eps", c_float),
+        ("out", c_void_p),
+    ]
+
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    "sqmix_version": (ctypes.c_char_p, []),
+    "sqmix_last_error": (ctypes.c_char_p, []),
+    "sqmix_device_sm_count": (ctypes.c_int, [ctypes.c_int]),
+    "sqmix_kv_cache_bytes": (c_size_t, [c_int64]),
+    "sqmix_kv_append_q4_0": (ctypes.c_int, [ctypes.POINTER(KvAppendArgs), c_void_p]),
+    "sqmix_kv_convert_rows": (ctypes.c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32,
+                                             c_int32, c_void_p]),
+    "sqmix_fa_workspace_bytes": (c_size_t, [c_int32, c_int32]),
+    "sqmix_fa_decode": (ctypes.c_int, [ctypes.POINTER(FaArgs), c_void_p]),
+    "sqmix_attn_merge_lse": (ctypes.c_int, [c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
+                                            c_void_p, c_void_p]),
+    "sqmix_gdn_decode": (ctypes.c_int, [ctypes.POINTER(GdnArgs), c_void_p]),
+    "sqmix_gdn_state_copy": (ctypes.c_int, [c_void_p, c_void_p, c_int64, c_int32, c_void_p]),
+    "sqmix_kvcache_create": (ctypes.c_int, [c_int32, c_int64, c_int32, ctypes.POINTER(c_void_p)]),
+    "sqmix_kvcache_destroy": (None, [c_void_p]),
+    "sqmix_kvcache_zero": (ctypes.c_int, [c_void_p, c_void_p]),
+    "sqmix_kvcache_begin_step": (ctypes.c_int, [c_void_p, c_int32]),
+    "sqmix_kvcache_rewind_to": (ctypes.c_int, [c_void_p, c_int64]),
+    "sqmix_kvcache_reset": (None, [c_void_p]),
+    "sqmix_kvcache_n_used": (c_int64, [c_void_p]),
+    "sqmix_kvcache_step_start": (c_int64, [c_void_p]),
+    "sqmix_kvcache_n_kv_padded": (c_int64, [c_void_p]),
+    "sqmix_kvcache_capacity": (c_int64, [c_void_p]),
+    "sqmix_kvcache_capacity_alloc": (c_int64, [c_void_p]),
+    "sqmix_kvcache_bytes_per_token": (c_size_t, [c_void_p]),
+    "sqmix_kvcache_k": (c_void_p, [c_void_p, c_int32]),
+    "sqmix_kvcache_v": (c_void_p, [c_void_p, c_int32]),
+    "sqmix_kvcache_device_step": (c_void_p, [c_void_p]),
+    "sqmix_kvcache_upload_step": (ctypes.c_int, [c_void_p, c_void_p]),
+    "sqmix_kvcache_max_step_tokens": (c_int32, [c_void_p]),
+    "sqmix_gdnstate_create": (ctypes.c_int, [c_int32, c_int32, c_int32, c_int32, ctypes.POINTER(c_void_p)]),
+    "sqmix_gdnstate_destroy": (None, [c_void_p]),
+    "sqmix_gdnstate_zero": (ctypes.c_int, [c_void_p, c_void_p]),
+    "sqmix_gdnstate_planes": (c_void_p, [c_void_p, c_int32]),
+    "sqmix_gdnstate_n_planes": (c_int32, [c_void_p]),
+    "sqmix_gdnstate_set_sel": (c_int32, [c_void_p, c_int32]),
+    "sqmix_gdnstate_sel": (c_int32, [c_void_p]),
+    "sqmix_gdnstate_device_sel": (c_void_p, [c_void_p]),
+    "sqmix_gdnstate_upload_sel": (ctypes.c_int, [c_void_p, c_void_p]),
+    "sqmix_gdnstate_snapshot_bytes": (c_size_t, [c_void_p]),
+    "sqmix_gdnstate_snapshot": (ctypes.c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "sqmix_gdnstate_restore": (ctypes.c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libsqmix.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python sqwen-moe-3090_b200/build.py` "
+                "(there is no CPU fallback for the sqmix kernels)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != SQMIX_OK:
+        msg = lib().sqmix_last_error().decode(errors="replace")
+        raise SqmixError(rc, f"{what}: {msg}" if what else msg)

@@ -1,0 +1,214 @@
+"""Kernel entry points over torch tensors (thin wrappers of the sqmix C ABI).
+
+Names follow the ggml nodes they replace on sqwen's attention-mixer path:
+
+  set_rows_q4_0    <- ggml_set_rows into the q4_0 KV cache (src/engine/kv.rs:367-396),
+                      with ggml_rope_multi on K fused in (src/model/attn.rs:183-204)
+  flash_attn_ext   <- ggml_flash_attn_ext (src/model/attn.rs:238-249) + the sigmoid
+                      gate (attn.rs:282-283), split-KV decode for 1-2 query tokens
+  attn_merge_lse   <- merge of split-KV partials that live on different GPUs
+  gated_delta_net  <- ggml_gated_delta_net (src/model/gdn.rs:489-500) with the
+                      snapshot write-back (src/model/graph.rs:884-912) and plane
+                      select (gdn.rs:445-463) done in place
+
+Every function launches on torch's current CUDA stream and raises SqmixError on a
+non-zero status, mirroring how the reference turns ggml failures into Err.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from ._lib import (SQMIX_BF16, SQMIX_F16, SQMIX_F32, FaArgs, GdnArgs, KvAppendArgs, check, lib)
+
+HEAD_DIM = 256
+N_HEAD = 16
+N_HEAD_KV = 2
+GDN_D = 128
+KV_PAD = 256
+
+_DTYPES = {torch.float32: SQMIX_F32, torch.float16: SQMIX_F16, torch.bfloat16: SQMIX_BF16}
+
+
+def _dt(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError as e:
+        raise TypeError(f"unsupported dtype {t.dtype}") from e
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("sqmix kernels take CUDA tensors (there is no CPU path)")
+
+
+def kv_cache_bytes(capacity: int) -> int:
+    return int(lib().sqmix_kv_cache_bytes(int(capacity)))
+
+
+def new_kv_cache(capacity: int, device="cuda") -> torch.Tensor:
+    """A zeroed tiled q4_0 cache (one of K or V) for `capacity` rows."""
+    if capacity % KV_PAD:
+        raise ValueError(f"capacity must be a multiple of {KV_PAD}")
+    return torch.zeros(kv_cache_bytes(capacity), dtype=torch.uint8, device=device)
+
+
+def set_rows_q4_0(k: torch.Tensor, v: torch.Tensor, rows: torch.Tensor, k_cache: torch.Tensor,
+                  v_cache: torch.Tensor, capacity: int, rope_n_rot: int = 0,
+                  rope_freq_base: float = 1e7, rope_pos_offset: int = 0, stream=None) -> None:
+    """Quantise new K/V rows [T][2][256] to q4_0 and write them at rows[t] (I64, device)."""
+    _require_cuda(k, v, rows, k_cache, v_cache)
+    if k.dim() == 2:
+        k = k.view(k.shape[0], N_HEAD_KV, HEAD_DIM)
+    if v.dim() == 2:
+        v = v.view(v.shape[0], N_HEAD_KV, HEAD_DIM)
+    if k.stride(-1) != 1 or k.stride(-2) != HEAD_DIM or v.stride(-1) != 1 or v.stride(-2) != HEAD_DIM:
+        raise ValueError("each token's K/V must be 2 x 256 contiguous values")
+    if k.dtype != v.dtype:
+        raise TypeError("k and v must share a dtype")
+    if rows.dtype != torch.int64 or rows.numel() != k.shape[0]:
+        raise ValueError("rows must be int64 [T]")
+    a = KvAppendArgs(
+        k=_ptr(k), v=_ptr(v), dtype=_dt(k), k_stride_tok=k.stride(0), v_stride_tok=v.stride(0),
+        n_tokens=k.shape[0], rows=_ptr(rows), k_cache=_ptr(k_cache), v_cache=_ptr(v_cache),
+        capacity=int(capacity), rope_n_rot=int(rope_n_rot), rope_freq_base=float(rope_freq_base),
+        rope_pos_offset=int(rope_pos_offset))
+    check(lib().sqmix_kv_append_q4_0(ctypes.byref(a), _stream(stream)), "set_rows_q4_0")
+
+
+def kv_convert_rows(tiled: torch.Tensor, capacity: int, which: str, row0: int, n_rows: int,
+                    rows_buf: torch.Tensor | None = None, to_rows: bool = True,
+                    stream=None) -> torch.Tensor:
+    """Tiled cache <-> ggml q4_0 rows ([n_rows][288] uint8).  which: 'k' or 'v'."""
+    _require_cuda(tiled)
+    if rows_buf is None:
+        rows_buf = torch.empty((n_rows, 288), dtype=torch.uint8, device=tiled.device)
+    w = {"k": 0, "v": 1}[which]
+    check(lib().sqmix_kv_convert_rows(_ptr(tiled), _ptr(rows_buf), int(capacity), int(row0), int(n_rows),
+                                      w, 1 if to_rows else 0, _stream(stream)), "kv_convert_rows")
+    return rows_buf
+
+
+def fa_workspace_bytes(n_q: int, n_splits: int = 0) -> int:
+    return int(lib().sqmix_fa_workspace_bytes(int(n_splits), int(n_q)))
+
+
+def new_fa_workspace(n_q: int = 2, n_splits: int = 0, device="cuda") -> torch.Tensor:
+    """Scratch for flash_attn_ext; zeroed once (its header holds the error word)."""
+    return torch.zeros(fa_workspace_bytes(n_q, n_splits), dtype=torch.uint8, device=device)
+
+
+def flash_attn_ext(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, capacity: int,
+                   n_kv: torch.Tensor, q_pos0: torch.Tensor, gate: torch.Tensor | None = None,
+                   scale: float = 1.0 / 16.0, rope_n_rot: int = 0, rope_freq_base: float = 1e7,
+                   rope_pos_offset: int = 0, out: torch.Tensor | None = None,
+                   lse: torch.Tensor | None = None,
+                   workspace: torch.Tensor | None = None, n_splits: int = 0,
+                   stream=None) -> torch.Tensor:
+    """Split-KV attention of q [n_q][16][256] (n_q in {1, 2}) over the tiled q4_0 caches.
+
+    n_kv and q_pos0 are device int64 scalars (CUDA-graph friendly).  Query t sees keys
+    j <= q_pos0 + t and j < n_kv.  Returns out [n_q][16][256] f32 (gated if `gate`).
+    """
+    _require_cuda(q, k_cache, v_cache, n_kv, q_pos0, gate)
+    if q.dim() == 2:
+        q = q.view(q.shape[0], N_HEAD, HEAD_DIM)
+    n_q = q.shape[0]
+    if q.stride(-1) != 1:
+        raise ValueError("q rows must be contiguous along head_dim")
+    if out is None:
+        out = torch.empty((n_q, N_HEAD, HEAD_DIM), dtype=torch.float32, device=q.device)
+    if workspace is None:
+        workspace = new_fa_workspace(n_q, n_splits, q.device)
+    if gate is not None:
+        if gate.dim() == 2:
+            gate = gate.view(gate.shape[0], N_HEAD, HEAD_DIM)
+        if gate.stride(-1) != 1:
+            raise ValueError("gate rows must be contiguous along head_dim")
+    a = FaArgs(
+        q=_ptr(q), q_dtype=_dt(q), q_stride_tok=q.stride(0), q_stride_head=q.stride(1),
+        gate=_ptr(gate), gate_dtype=_dt(gate) if gate is not None else 0,
+        gate_stride_tok=gate.stride(0) if gate is not None else 0,
+        gate_stride_head=gate.stride(1) if gate is not None else 0,
+        k_cache=_ptr(k_cache), v_cache=_ptr(v_cache), capacity=int(capacity), n_kv=_ptr(n_kv),
+        q_pos0=_ptr(q_pos0), n_q=n_q, scale=float(scale), rope_n_rot=int(rope_n_rot),
+        rope_freq_base=float(rope_freq_base), rope_pos_offset=int(rope_pos_offset), out=_ptr(out), lse=_ptr(lse), workspace=_ptr(workspace),
+        workspace_bytes=workspace.numel(), n_splits=int(n_splits))
+    check(lib().sqmix_fa_decode(ctypes.byref(a), _stream(stream)), "flash_attn_ext")
+    return out
+
+
+def attn_merge_lse(o_parts: torch.Tensor, lse_parts: torch.Tensor, gate: torch.Tensor | None = None,
+                   out: torch.Tensor | None = None, lse_out: torch.Tensor | None = None,
+                   stream=None) -> torch.Tensor:
+    """o_parts [P][rows][256] f32, lse_parts [P][rows] f32 -> out [rows][256]."""
+    _require_cuda(o_parts, lse_parts, gate)
+    P = o_parts.shape[0]
+    rows = o_parts[0].numel() // HEAD_DIM
+    if out is None:
+        out = torch.empty((rows, HEAD_DIM), dtype=torch.float32, device=o_parts.device)
+    if gate is not None and (gate.dtype != torch.float32 or not gate.is_contiguous()):
+        gate = gate.float().contiguous()
+    check(lib().sqmix_attn_merge_lse(P, rows, _ptr(o_parts.contiguous()), _ptr(lse_parts.contiguous()),
+                                     _ptr(gate), _ptr(out), _ptr(lse_out), _stream(stream)),
+          "attn_merge_lse")
+    return out
+
+
+def gated_delta_net(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
+                    beta: torch.Tensor, state: torch.Tensor, n_planes: int = 1,
+                    sel: torch.Tensor | None = None, n_snap: int = 1, l2_eps: float = 0.0,
+                    out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Gated delta rule over T tokens for n_seqs sequences.
+
+    q, k [n_seqs][T][H_k][128]; v [n_seqs][T][H_v][128] (f32/bf16/f16); g, beta
+    [n_seqs][T][H_v] f32; state [n_seqs][n_planes][H_v][128][128] f32 (updated in place:
+    plane s <- state after T - s tokens for s < n_snap; the input plane is sel[seq]).
+    3-D q/k/v/g/beta (no sequence dim) are accepted for n_seqs = 1.
+    """
+    _require_cuda(q, k, v, g, beta, state, sel)
+    if q.dim() == 3:
+        q, k, v, g, beta = q[None], k[None], v[None], g[None], beta[None]
+    n_seqs, T, H_k, d = q.shape
+    H_v = v.shape[2]
+    if d != GDN_D or v.shape[3] != GDN_D:
+        raise ValueError("GDN head dim must be 128")
+    if q.stride() != k.stride() or q.stride(-1) != 1 or q.stride(-2) != GDN_D or v.stride(-1) != 1:
+        raise ValueError("q and k must share a [seq][tok][head][128] layout with contiguous heads")
+    if g.dtype != torch.float32 or beta.dtype != torch.float32:
+        raise TypeError("g and beta must be float32")
+    g = g.contiguous()
+    beta = beta.contiguous()
+    if out is None:
+        out = torch.empty((n_seqs, T, H_v, GDN_D), dtype=torch.float32, device=q.device)
+    a = GdnArgs(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), dtype=_dt(q), qk_stride_tok=q.stride(1), v_stride_tok=v.stride(1),
+        qk_stride_seq=q.stride(0), v_stride_seq=v.stride(0), g=_ptr(g), beta=_ptr(beta),
+        state=_ptr(state), n_planes=int(n_planes), sel=_ptr(sel), n_seqs=n_seqs, n_tokens=T, h_k=H_k,
+        h_v=H_v, n_snap=int(n_snap), l2_eps=float(l2_eps), out=_ptr(out))
+    check(lib().sqmix_gdn_decode(ctypes.byref(a), _stream(stream)), "gated_delta_net")
+    return out
+
+
+def gdn_state_copy(dst: torch.Tensor, src: torch.Tensor, plane_elems: int, n_planes: int,
+                   stream=None) -> None:
+    _require_cuda(dst, src)
+    check(lib().sqmix_gdn_state_copy(_ptr(dst), _ptr(src), int(plane_elems), int(n_planes),
+                                     _stream(stream)), "gdn_state_copy")
+
+
+def rope_theta_scale(freq_base: float, n_rot: int) -> float:
+    return math.pow(freq_base, -2.0 / n_rot)

@@ -1,0 +1,133 @@
+"""C-ABI checks that need no GPU: exports, argument validation, host bookkeeping."""
+import ctypes
+import os
+import re
+import struct
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "sqmix.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sqmix_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol(sqmix_lib):
+    L = sqmix_lib.lib()
+    names = declared_functions()
+    assert len(names) >= 30
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_python_mirror_binds_every_declared_symbol(sqmix_lib):
+    assert sorted(sqmix_lib.exported_symbols()) == declared_functions()
+
+
+def test_version(sqmix_lib):
+    assert b"sm_100a" in sqmix_lib.lib().sqmix_version()
+
+
+def test_argument_validation_without_gpu(sqmix_lib):
+    from sqmix._lib import FaArgs, KvAppendArgs
+
+    L = sqmix_lib.lib()
+    a = FaArgs(n_q=3)
+    assert L.sqmix_fa_decode(ctypes.byref(a), None) == sqmix_lib.SQMIX_EINVAL
+    assert b"null" in L.sqmix_last_error() or b"n_q" in L.sqmix_last_error()
+    # all pointers set (fake), bad n_q
+    fake = ctypes.c_void_p(256)
+    a = FaArgs(q=fake, k_cache=fake, v_cache=fake, n_kv=fake, q_pos0=fake, out=fake, workspace=fake,
+               n_q=3, capacity=256, scale=0.0625)
+    assert L.sqmix_fa_decode(ctypes.byref(a), None) == sqmix_lib.SQMIX_EINVAL
+    assert b"n_q=3" in L.sqmix_last_error()
+    # workspace too small -> ENOSPC (checked before any launch)
+    a = FaArgs(q=fake, k_cache=fake, v_cache=fake, n_kv=fake, q_pos0=fake, out=fake, workspace=fake,
+               n_q=1, capacity=256, scale=0.0625, workspace_bytes=16, n_splits=4)
+    assert L.sqmix_fa_decode(ctypes.byref(a), None) == sqmix_lib.SQMIX_ENOSPC
+    b = KvAppendArgs(k=fake, v=fake, rows=fake, k_cache=fake, v_cache=fake, dtype=0, n_tokens=1,
+                     k_stride_tok=512, v_stride_tok=512, capacity=100)
+    assert L.sqmix_kv_append_q4_0(ctypes.byref(b), None) == sqmix_lib.SQMIX_EINVAL
+    assert b"capacity" in L.sqmix_last_error()
+    assert L.sqmix_kv_convert_rows(fake, fake, 256, 200, 100, 0, 1, None) == sqmix_lib.SQMIX_EINVAL
+
+
+def test_workspace_sizes(sqmix_lib):
+    assert sqmix_lib.fa_workspace_bytes(1, 148) >= 148 * 16 * 256 * 4
+    assert sqmix_lib.fa_workspace_bytes(2, 148) >= 2 * 148 * 16 * 256 * 4
+    assert sqmix_lib.kv_cache_bytes(172032) == 172032 * 288
+
+
+# ------------------------------------------------- KvCache bookkeeping (kv.rs) --
+
+def _kv(L, n_layers, cap):
+    h = ctypes.c_void_p()
+    assert L.sqmix_kvcache_create(n_layers, cap, -1, ctypes.byref(h)) == 0
+    return h
+
+
+def test_kvcache_cursor_semantics(sqmix_lib):
+    L = sqmix_lib.lib()
+    h = _kv(L, 10, 1000)
+    try:
+        assert L.sqmix_kvcache_capacity(h) == 1000
+        assert L.sqmix_kvcache_capacity_alloc(h) == 1024  # kv.rs:119 ceil to 256
+        assert L.sqmix_kvcache_bytes_per_token(h) == 10 * 576  # 5.6 KiB/token over 10 layers
+        assert L.sqmix_kvcache_n_kv_padded(h) == 0
+        assert L.sqmix_kvcache_begin_step(h, 300) == 0
+        assert (L.sqmix_kvcache_step_start(h), L.sqmix_kvcache_n_used(h)) == (0, 300)
+        assert L.sqmix_kvcache_n_kv_padded(h) == 512
+        assert L.sqmix_kvcache_begin_step(h, 2) == 0
+        assert (L.sqmix_kvcache_step_start(h), L.sqmix_kvcache_n_used(h)) == (300, 302)
+        # overflow is an error and leaves the cursor alone (kv.rs:240-245)
+        assert L.sqmix_kvcache_begin_step(h, 699) == sqmix_lib.SQMIX_EOVERFLOW
+        assert b"overflow" in L.sqmix_last_error()
+        assert L.sqmix_kvcache_n_used(h) == 302
+        assert L.sqmix_kvcache_begin_step(h, 698) == 0
+        # rewind moves the cursor only, never forward (kv.rs:284-297)
+        assert L.sqmix_kvcache_rewind_to(h, 1001) == sqmix_lib.SQMIX_ERANGE
+        assert L.sqmix_kvcache_rewind_to(h, 301) == 0
+        assert (L.sqmix_kvcache_step_start(h), L.sqmix_kvcache_n_used(h)) == (301, 301)
+        assert L.sqmix_kvcache_rewind_to(h, 302) == sqmix_lib.SQMIX_ERANGE
+        L.sqmix_kvcache_reset(h)
+        assert L.sqmix_kvcache_n_used(h) == 0
+        assert L.sqmix_kvcache_upload_step(h, None) == 0  # bookkeeping-only: no device copy
+    finally:
+        L.sqmix_kvcache_destroy(h)
+
+
+def test_gdnstate_selector_and_snapshot_header(sqmix_lib):
+    L = sqmix_lib.lib()
+    h = ctypes.c_void_p()
+    assert L.sqmix_gdnstate_create(30, 32, 1, -1, ctypes.byref(h)) == 0
+    try:
+        assert L.sqmix_gdnstate_n_planes(h) == 2
+        # set_recurrent_sel clamps to n_rs (graph.rs:190-196) and is one-shot
+        assert L.sqmix_gdnstate_set_sel(h, 5) == 1
+        assert L.sqmix_gdnstate_sel(h) == 1
+        assert L.sqmix_gdnstate_upload_sel(h, None) == 0
+        assert L.sqmix_gdnstate_sel(h) == 0
+        plane = 32 * 128 * 128 * 4
+        n = L.sqmix_gdnstate_snapshot_bytes(h)
+        assert n == 8 + 30 * plane  # ~63 MiB with conv state in the reference; planes only here
+        good = struct.pack("<Q", n - 8) + bytes(n - 8)
+        assert L.sqmix_gdnstate_restore(h, good, len(good), None) == 0
+        bad_len = struct.pack("<Q", n - 8) + bytes(n - 9)
+        assert L.sqmix_gdnstate_restore(h, bad_len, len(bad_len), None) == sqmix_lib.SQMIX_EINVAL
+        assert b"length mismatch" in L.sqmix_last_error()
+        bad_hdr = struct.pack("<Q", n) + bytes(n - 8)
+        assert L.sqmix_gdnstate_restore(h, bad_hdr, len(bad_hdr), None) == sqmix_lib.SQMIX_EINVAL
+        assert L.sqmix_gdnstate_restore(h, b"1234", 4, None) == sqmix_lib.SQMIX_EINVAL
+    finally:
+        L.sqmix_gdnstate_destroy(h)
+
+
+def test_kvcache_rejects_bad_shapes(sqmix_lib):
+    L = sqmix_lib.lib()
+    h = ctypes.c_void_p()
+    assert L.sqmix_kvcache_create(0, 100, -1, ctypes.byref(h)) == sqmix_lib.SQMIX_EINVAL
+    assert L.sqmix_kvcache_create(1, 0, -1, ctypes.byref(h)) == sqmix_lib.SQMIX_EINVAL

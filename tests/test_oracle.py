@@ -1,0 +1,266 @@
+"""Pin the CPU oracle before trusting it.
+
+* q4_0: bit-exact against gguf-py's Q4_0 (golden fixtures, tests/golden/) and the
+  reference's own round-trip bound (tests/attn_test.rs:781-833).
+* RoPE / attention / gated delta rule: there are no golden vectors in the reference,
+  so the oracle is checked against independent float64 numpy restatements of the
+  formulas the reference's tests restate (attn_test.rs:148-359, gdn.rs:9-24) and
+  against the reference's invariants (gdn_test.rs:282-378,
+  gdn_prod_dim_test.rs:245-326).
+"""
+import os
+
+import numpy as np
+import pytest
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "q4_0_golden.npz")
+
+
+def lcg_pseudo(n, seed, scale=1.0):
+    """tests/attn_test.rs:67-75 (and gdn_test.rs:94-103 with scale 0.5)."""
+    s = (seed * 2654435761 + 1) & 0xFFFFFFFF
+    out = np.empty(n, dtype=np.float32)
+    for i in range(n):
+        s = (s * 1664525 + 1013904223) & 0xFFFFFFFF
+        out[i] = np.float32((s >> 8) / 8388608.0 - 1.0)
+    return out * np.float32(scale)
+
+
+def ramp(n, lo, hi):
+    """tests/gdn_test.rs:84-88."""
+    i = np.arange(n, dtype=np.float32)
+    return (np.float32(lo) + np.float32(hi - lo) * (i + 1) / np.float32(n + 1)).astype(np.float32)
+
+
+# ----------------------------------------------------------------- q4_0 ---
+
+def test_q4_0_bit_exact_vs_gguf_golden(oracle):
+    d = np.load(GOLDEN)
+    q = oracle.q4_0_quantize(d["x"])
+    mism = np.where(~(q == d["q"]).all(axis=1))[0]
+    assert mism.size == 0, f"{mism.size} blocks differ, first {mism[:5]}"
+
+
+def test_q4_0_dequant_vs_gguf_golden(oracle):
+    d = np.load(GOLDEN)
+    deq = oracle.q4_0_dequantize(d["q"], 32)
+    assert np.array_equal(deq.view(np.uint32), d["deq"].view(np.uint32))
+
+
+def test_q4_0_roundtrip_error_bound(oracle):
+    # tests/attn_test.rs:789-833: err <= |d| and 0.1 < mean(err/d) < 0.4
+    data = lcg_pseudo(32 * 8, 7)
+    deq = oracle.q4_0_dequantize(oracle.q4_0_quantize(data.reshape(8, 32)), 32).reshape(-1)
+    rel = []
+    for r in range(8):
+        blk, dq = data[r * 32:(r + 1) * 32], deq[r * 32:(r + 1) * 32]
+        d = np.abs(dq).max() / 8.0
+        if d == 0:
+            continue
+        rel.extend(np.abs(dq - blk) / d)
+    rel = np.array(rel)
+    assert rel.max() <= 1.0 + 1e-3
+    assert 0.1 < rel.mean() < 0.4
+
+
+def test_q4_0_layout(oracle):
+    # element j -> low nibble of qs[j], element j+16 -> high nibble (kernel_verify.rs:270-292)
+    x = np.zeros(32, dtype=np.float32)
+    x[0] = -8.0  # d = 1
+    x[3] = 3.0
+    x[19] = -5.0
+    q = oracle.q4_0_quantize(x[None])[0]
+    assert int(q[0]) | (int(q[1]) << 8) == 0x3C00  # fp16(1.0)
+    assert q[2 + 3] & 0x0F == 3 + 8
+    assert q[2 + 3] >> 4 == -5 + 8
+
+
+def test_f16_conversion_matches_numpy(oracle):
+    rng = np.random.default_rng(1)
+    vals = np.concatenate([
+        rng.standard_normal(2000).astype(np.float32) * np.float32(10.0) ** rng.integers(-9, 6, 2000),
+        np.array([0.0, -0.0, 65504, 65519.99, 65520, 1e9, -1e9, 2 ** -25, 2 ** -24, 3 * 2 ** -26,
+                  6.1e-5, np.inf, -np.inf], dtype=np.float32)])
+    with np.errstate(over="ignore"):
+        want = vals.astype(np.float16).view(np.uint16)
+    got = np.array([oracle.f32_to_f16_bits(float(v)) for v in vals], dtype=np.uint16)
+    assert np.array_equal(got, want)
+    allbits = np.arange(0, 65536, 97, dtype=np.uint16)
+    back = np.array([oracle.f16_bits_to_f32(int(b)) for b in allbits], dtype=np.float32)
+    ref = allbits.view(np.float16).astype(np.float32)
+    ok = (back == ref) | (np.isnan(back) & np.isnan(ref))
+    assert ok.all()
+
+
+# ----------------------------------------------------------------- rope ---
+
+def rope_numpy(x, pos0, base, n_rot):
+    """NEOX pair rotation with theta_i = p * s^i by repeated float32 multiplication."""
+    x = x.astype(np.float32).copy()
+    T, H, D = x.shape
+    s = np.float32(np.power(np.float32(base), np.float32(-2.0 / n_rot), dtype=np.float32))
+    half = n_rot // 2
+    for t in range(T):
+        th = np.float32(pos0 + t)
+        for i in range(half):
+            c, sn = np.float32(np.cos(np.float64(th))), np.float32(np.sin(np.float64(th)))
+            x0, x1 = x[t, :, i].copy(), x[t, :, i + half].copy()
+            x[t, :, i] = x0 * c - x1 * sn
+            x[t, :, i + half] = x0 * sn + x1 * c
+            th = np.float32(th * s)
+    return x
+
+
+def test_rope_text_matches_formula(oracle):
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((5, 3, 256)).astype(np.float32)
+    got = oracle.rope_text(x, 170000, 1e7, 64)
+    want = rope_numpy(x, 170000, 1e7, 64)
+    assert np.abs(got - want).max() < 2e-5
+    assert np.array_equal(got[..., 64:], x[..., 64:])  # dims >= n_rot untouched
+
+
+def test_imrope_sections_reduce_to_text(oracle):
+    # graph.rs:457-467 writes equal positions in all four streams -> sections irrelevant
+    rng = np.random.default_rng(3)
+    for D, n_rot, sec in ((256, 64, (11, 11, 10, 0)), (64, 16, (3, 3, 2, 0))):
+        x = rng.standard_normal((4, 2, D)).astype(np.float32)
+        pos = np.tile(np.arange(9, 13, dtype=np.int32), 4)
+        a = oracle.rope_imrope(x, pos, sec, 1e7, n_rot)
+        b = oracle.rope_text(x, 9, 1e7, n_rot)
+        assert np.array_equal(a, b)
+
+
+# ------------------------------------------------------------ attention ---
+
+def attn_numpy(q, k, v, gate, q_pos0, scale):
+    T, Hq, D = q.shape
+    n_kv, Hkv, _ = k.shape
+    G = Hq // Hkv
+    out = np.zeros((T, Hq, D))
+    lse = np.zeros((T, Hq))
+    for t in range(T):
+        lim = min(q_pos0 + t + 1, n_kv)
+        for h in range(Hq):
+            s = k[:lim, h // G, :].astype(np.float64) @ q[t, h].astype(np.float64) * scale
+            m = s.max()
+            p = np.exp(s - m)
+            o = p @ v[:lim, h // G, :].astype(np.float64) / p.sum()
+            if gate is not None:
+                o = o / (1 + np.exp(-gate[t, h].astype(np.float64)))
+            out[t, h] = o
+            lse[t, h] = m + np.log(p.sum())
+    return out, lse
+
+
+def test_attn_oracle_vs_numpy(oracle):
+    rng = np.random.default_rng(4)
+    q = rng.standard_normal((3, 16, 256)).astype(np.float32)
+    k = rng.standard_normal((77, 2, 256)).astype(np.float32)
+    v = rng.standard_normal((77, 2, 256)).astype(np.float32)
+    gate = rng.standard_normal((3, 16, 256)).astype(np.float32)
+    for q_pos0 in (0, 40, 74, 200):
+        got, lse = oracle.attn(q, k, v, gate, q_pos0=q_pos0, scale=1 / 16, want_lse=True)
+        want, wl = attn_numpy(q, k, v, gate, q_pos0, 1 / 16)
+        assert np.abs(got - want).max() < 1e-5
+        assert np.abs(lse - wl).max() < 1e-4
+
+
+def test_attn_oracle_gqa_block_mapping(oracle):
+    # kv_head = h / (Hq / Hkv) (tests/attn_test.rs:306-312): heads 0-7 -> 0, 8-15 -> 1
+    rng = np.random.default_rng(5)
+    q = rng.standard_normal((1, 16, 256)).astype(np.float32)
+    k = rng.standard_normal((10, 2, 256)).astype(np.float32)
+    v = np.zeros((10, 2, 256), dtype=np.float32)
+    v[:, 0, :] = 1.0
+    v[:, 1, :] = 2.0
+    out = oracle.attn(q, k, v, None, q_pos0=9)
+    assert np.allclose(out[0, :8], 1.0) and np.allclose(out[0, 8:], 2.0)
+
+
+# ------------------------------------------------------------------ gdn ---
+
+def gdn_numpy(q, k, v, g, beta, S0):
+    """float64 restatement of gdn.rs:9-24 with S[i][j] stored as S0[h][j][i]."""
+    T, Hk, d = q.shape
+    Hv = v.shape[1]
+    S = S0.astype(np.float64).transpose(0, 2, 1).copy()  # [h][i][j]
+    out = np.zeros((T, Hv, d))
+    for t in range(T):
+        for h in range(Hv):
+            kk, qq = k[t, h % Hk].astype(np.float64), q[t, h % Hk].astype(np.float64)
+            S[h] *= np.exp(np.float64(g[t, h]))
+            delta = (v[t, h] - S[h].T @ kk) * beta[t, h]
+            S[h] += np.outer(kk, delta)
+            out[t, h] = S[h].T @ qq / np.sqrt(d)
+    return out, S.transpose(0, 2, 1)
+
+
+def gdn_inputs(rng, T, Hk, Hv, d, state_scale=0.02):
+    q = rng.standard_normal((T, Hk, d)).astype(np.float32)
+    k = rng.standard_normal((T, Hk, d)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.standard_normal((T, Hv, d)).astype(np.float32)
+    a_log = rng.uniform(0, 2.7, Hv).astype(np.float32)
+    dt_bias = rng.standard_normal(Hv).astype(np.float32)
+    g = (-np.exp(a_log) * np.log1p(np.exp(rng.standard_normal((T, Hv)) + dt_bias))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((T, Hv))))).astype(np.float32)
+    S0 = (rng.standard_normal((Hv, d, d)) * state_scale).astype(np.float32)
+    return q, k, v, g, beta, S0
+
+
+def test_gdn_oracle_vs_numpy(oracle):
+    rng = np.random.default_rng(6)
+    q, k, v, g, beta, S0 = gdn_inputs(rng, 7, 2, 4, 16)
+    out, snaps = oracle.gdn(q, k, v, g, beta, S0, n_snap=1)
+    want, Sw = gdn_numpy(q, k, v, g, beta, S0)
+    assert np.abs(out - want).max() < 1e-5
+    assert np.abs(snaps[0] - Sw).max() < 1e-5
+
+
+def test_gdn_fused_chunk_equivalence(oracle):
+    # tests/gdn_test.rs:282-378: s_v 8, h_v 4, h_k 2, 32 tokens vs 16 + 16, <= 1e-5
+    s_v, h_v, h_k, n, cs = 8, 4, 2, 32, 16
+    q = ramp(s_v * h_k * n, -0.5, 0.5).reshape(n, h_k, s_v)
+    k = ramp(s_v * h_k * n, 0.5, -0.5).reshape(n, h_k, s_v)
+    v = ramp(s_v * h_v * n, -1.0, 1.0).reshape(n, h_v, s_v)
+    g = ramp(h_v * n, -0.5, 0.0).reshape(n, h_v)
+    b = ramp(h_v * n, 0.1, 0.9).reshape(n, h_v)
+    s0 = np.zeros((h_v, s_v, s_v), dtype=np.float32)
+    full, _ = oracle.gdn(q, k, v, g, b, s0)
+    _, sa = oracle.gdn(q[:cs], k[:cs], v[:cs], g[:cs], b[:cs], s0)
+    ob, _ = oracle.gdn(q[cs:], k[cs:], v[cs:], g[cs:], b[cs:], sa[0])
+    rel = np.abs(ob - full[cs:]) / np.maximum(np.abs(full[cs:]), 1.0)
+    assert rel.max() <= 1e-5
+
+
+def test_gdn_rollback_snapshots_match_shorter_runs(oracle):
+    # tests/gdn_prod_dim_test.rs:245-292 at production dims: slot s == state after N - s
+    rng = np.random.default_rng(7)
+    N = 4
+    q, k, v, g, beta, S0 = gdn_inputs(rng, N, 16, 32, 128)
+    _, snaps = oracle.gdn(q, k, v, g, beta, S0, n_snap=N)
+    for s in range(N):
+        n = N - s
+        _, ref = oracle.gdn(q[:n], k[:n], v[:n], g[:n], beta[:n], S0, n_snap=1)
+        scale = np.abs(ref[0]).max()
+        assert np.abs(snaps[s] - ref[0]).max() <= 1e-5 * scale
+
+
+def test_gdn_5_plus_1_equals_6(oracle):
+    # tests/gdn_prod_dim_test.rs:294-326 (op level): <= 1e-4 * scale
+    rng = np.random.default_rng(8)
+    q, k, v, g, beta, S0 = gdn_inputs(rng, 6, 16, 32, 128)
+    full, _ = oracle.gdn(q, k, v, g, beta, S0)
+    _, s5 = oracle.gdn(q[:5], k[:5], v[:5], g[:5], beta[:5], S0)
+    o6, _ = oracle.gdn(q[5:], k[5:], v[5:], g[5:], beta[5:], s5[0])
+    scale = np.abs(full[5]).max()
+    assert np.abs(o6[0] - full[5]).max() <= 1e-4 * scale
+
+
+def test_l2norm_is_unit(oracle):
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((10, 128)).astype(np.float32) * 3
+    y = oracle.l2norm(x, 1e-6)
+    assert np.allclose(np.linalg.norm(y, axis=-1), 1.0, atol=1e-5)
