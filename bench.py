@@ -226,20 +226,20 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         o_all = torch.empty((world, N_HEAD, HEAD_DIM), device=dev)
         l_all = torch.empty((world, N_HEAD), device=dev)
 
+    own = rank == owner  # the rank whose key slice holds the new token appends it (fused)
+
     def layer(l):
-        if rank == owner:
-            sqmix.set_rows_q4_0(k_new[l], v_new[l], d_row, kc[l], vc[l], cap, rope_n_rot=N_ROT,
-                                rope_freq_base=FREQ_BASE,
-                                rope_pos_offset=owner * n_local)
         if world == 1:
             sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=gate[l], rope_n_rot=N_ROT,
-                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=out[l], workspace=ws,
-                                 n_splits=n_splits)
+                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=out[l],
+                                 workspace=ws, n_splits=n_splits, k_new=k_new[l], v_new=v_new[l],
+                                 overlap_prev=True)
         else:
             sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=None, rope_n_rot=N_ROT,
-                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=o_loc[l], lse=l_loc[l],
-                                 workspace=ws,
-                                 n_splits=n_splits)
+                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=o_loc[l],
+                                 lse=l_loc[l], workspace=ws, n_splits=n_splits,
+                                 k_new=k_new[l] if own else None, v_new=v_new[l] if own else None,
+                                 overlap_prev=True)
             dist.all_gather_into_tensor(o_all, o_loc[l])
             dist.all_gather_into_tensor(l_all, l_loc[l])
             sqmix.attn_merge_lse(o_all, l_all, gate=gate[l, 0], out=out[l, 0])
@@ -287,26 +287,37 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     us_per_token = ms * 1e3 / args.steps
-    launches_per_step = N_LAYERS * ((1 if rank == owner else 0) + 2 + (1 if world > 1 else 0))
+    launches_per_step = N_LAYERS * (1 + (1 if world > 1 else 0))  # fused decode (+ merge_lse)
 
     # ---- dominant kernel alone: flash_attn_ext over each layer in turn ---------
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     reps = max(3, args.steps)
-    for l in range(N_LAYERS):
-        sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=gate[l], rope_n_rot=N_ROT,
-                             rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=out[l], workspace=ws,
-                                 n_splits=n_splits)
+    # (graph-captured so that host launch cost is not mistaken for kernel time)
+    def fa_only():
+        for l in range(N_LAYERS):
+            sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=gate[l], rope_n_rot=N_ROT,
+                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=out[l],
+                                 workspace=ws, n_splits=n_splits, overlap_prev=True)
+    s2 = torch.cuda.Stream()
+    s2.wait_stream(stream)
+    with torch.cuda.stream(s2):
+        fa_only()
+    stream.wait_stream(s2)
+    torch.cuda.synchronize()
+    g_fa = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_fa):
+        fa_only()
+    g_fa.replay()
     torch.cuda.synchronize()
     e0.record()
     for _ in range(reps):
-        for l in range(N_LAYERS):
-            sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=gate[l], rope_n_rot=N_ROT,
-                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=out[l], workspace=ws,
-                                 n_splits=n_splits)
+        g_fa.replay()
     e1.record()
     torch.cuda.synchronize()
+    g_fa = None
     fa_us = e0.elapsed_time(e1) * 1e3 / (reps * N_LAYERS)
+    sqmix.fa_status(ws)
     alg_bytes = n_local * BYTES_PER_KEY + 3 * N_HEAD * HEAD_DIM * 4
     hbm, peak_kind = peaks()
     achieved = alg_bytes / (fa_us * 1e-6) / 1e9
@@ -348,8 +359,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         e2e_ms = float(t.item())
     e2e_us = e2e_ms * 1e3 / args.steps
 
-    if graph is not None:
-        del graph
+    used_graph = graph is not None
+    graph = None  # release the captured graph before the process group goes away
     if rank != 0:
         return None
     res = {
@@ -361,9 +372,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                "16 Q / 2 KV heads, d=256, RoPE 64/1e7, sigmoid gate",
                    "n_q": 1, "keys_per_layer": N_KV, "keys_per_gpu": n_local, "parallelism": f"split-KV x{world}",
                    "l2": "inputs larger than L2: 10 x 99 MB of KV cycled per step",
-                   "cuda_graph": graph is not None or False},
+                   "cuda_graph": used_graph},
         "tokens_per_s": 1e6 / us_per_token,
-        "roofline": {"bound": "hbm", "kernel": "sqmix_fa_decode (split-KV decode + merge)",
+        "roofline": {"bound": "hbm", "kernel": "fa_decode_kernel (append + split-KV attention + merge, one launch)",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": peak_kind, "traffic": None, "alg_bytes_per_launch": alg_bytes,
                      "launch_us": fa_us},
@@ -374,6 +385,44 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     return res
 
 
+def run_profile_case(case: str):
+    """Small fixed workloads for ncu captures (one kernel, a few launches, ~0.3 GB)."""
+    import torch
+
+    import sqmix
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    if case == "fa":
+        kc, vc = sqmix.new_kv_cache(N_KV), sqmix.new_kv_cache(N_KV)
+        for a in range(0, N_KV, 16384):
+            n = min(16384, N_KV - a)
+            sqmix.set_rows_q4_0(torch.randn((n, 2, 256), generator=g, device=dev),
+                                torch.randn((n, 2, 256), generator=g, device=dev),
+                                torch.arange(a, a + n, device=dev), kc, vc, N_KV)
+        q = torch.randn((1, N_HEAD, HEAD_DIM), generator=g, device=dev)
+        gate = torch.randn((1, N_HEAD, HEAD_DIM), generator=g, device=dev)
+        d = torch.tensor([N_KV, N_KV - 1], dtype=torch.int64, device=dev)
+        ws = sqmix.new_fa_workspace(1, 0, dev)
+        for _ in range(3):
+            sqmix.flash_attn_ext(q, kc, vc, N_KV, d[0:1], d[1:2], gate=gate, rope_n_rot=N_ROT,
+                                 rope_freq_base=FREQ_BASE, workspace=ws)
+    elif case == "gdn":
+        S = torch.randn((1, 1, 32, 128, 128), generator=g, device=dev) * 0.02
+        q = torch.nn.functional.normalize(torch.randn((1, 1, 16, 128), generator=g, device=dev), dim=-1)
+        k = torch.nn.functional.normalize(torch.randn((1, 1, 16, 128), generator=g, device=dev), dim=-1)
+        v = torch.randn((1, 1, 32, 128), generator=g, device=dev)
+        gg = -torch.rand((1, 1, 32), generator=g, device=dev)
+        b = torch.rand((1, 1, 32), generator=g, device=dev)
+        for _ in range(3):
+            sqmix.gated_delta_net(q, k, v, gg, b, S)
+    else:
+        raise SystemExit(f"unknown profile case {case}")
+    torch.cuda.synchronize()
+    print(f"profile case {case} done")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -382,7 +431,11 @@ def main():
     ap.add_argument("--impl", default="sqmix", choices=["sqmix", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | gdn) and exit")
     args = ap.parse_args()
+    if args.profile:
+        run_profile_case(args.profile)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

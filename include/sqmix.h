@@ -116,8 +116,10 @@ int sqmix_kv_convert_rows(void *tiled_cache, void *rows_buf, int64_t capacity, i
                           int64_t n_rows, int32_t which, int32_t to_rows, sqmix_stream_t stream);
 
 /* ========================================================================
- * Split-KV attention decode (ggml_flash_attn_ext, attn.rs:238-249) with the
- * sigmoid output gate (attn.rs:282-283) fused into the merge.
+ * Split-KV attention decode: one cooperative launch per layer and step that does
+ * the q4_0 append of the step's rows (ggml_set_rows, kv.rs:367-396), attention over
+ * the cache (ggml_flash_attn_ext, attn.rs:238-249), the split merge and the sigmoid
+ * output gate (attn.rs:282-283).
  * ======================================================================== */
 
 typedef struct sqmix_fa_args {
@@ -147,11 +149,38 @@ typedef struct sqmix_fa_args {
     void *workspace;          /* device scratch, sqmix_fa_workspace_bytes(); its
                                  first 256 bytes must be zero before first use */
     size_t workspace_bytes;
-    int32_t n_splits;         /* 0 = one split per SM; else the split count */
+    int32_t n_splits;         /* 0 = one split per SM */
+    int32_t config;           /* kernel configuration, 0 = auto (see fa_decode.cu) */
+    /* Fused append (n_new > 0): rows q_pos0 + t, t < n_new <= n_q, of the caches are
+     * first written from k_new/v_new [n_new][2][256] (K rotated like Q), exactly as
+     * sqmix_kv_append_q4_0 would write them; n_kv must already count them. */
+    const void *k_new;
+    const void *v_new;
+    int32_t kv_new_dtype;
+    int64_t k_new_stride_tok;
+    int64_t v_new_stride_tok;
+    int32_t n_new;
+    int32_t flags;            /* SQMIX_FA_* bits below, 0 = none */
 } sqmix_fa_args;
 
+/* The decode and merge kernels are launched with programmatic stream serialisation:
+ * each starts while the kernel before it on the stream drains and waits for it
+ * (griddepcontrol.wait) before reading q, gate, k_new/v_new or the workspace.
+ * SQMIX_FA_OVERLAP_PREV also lets the decode kernel read *n_kv, *q_pos0 and request
+ * cache rows below *q_pos0 BEFORE that wait, overlapping the previous kernel's tail.
+ * Set it only when none of those is written by the kernel launched immediately before
+ * this call on the stream (a copy, or a kernel two or more launches back, is fine):
+ * the engine's step loop uploads the scalars with a copy and writes the step's rows
+ * (>= q_pos0) with the fused append. */
+#define SQMIX_FA_OVERLAP_PREV 1
+
+/* Workspace for n_splits splits (0 = enough for every configuration's default). */
 size_t sqmix_fa_workspace_bytes(int32_t n_splits, int32_t n_q);
 int sqmix_fa_decode(const sqmix_fa_args *args, sqmix_stream_t stream);
+/* Reads (and clears) the device status word of a workspace: SQMIX_OK, SQMIX_ETIMEOUT
+ * when a bounded device-side wait gave up, SQMIX_ERANGE when n_kv exceeded the
+ * capacity.  Synchronises the stream. */
+int sqmix_fa_status(void *workspace, sqmix_stream_t stream);
 
 /* Merge n_parts normalised partial attentions (O_p, lse_p) over disjoint key sets
  * (split-KV across GPUs): out = sum_p O_p exp(lse_p - L) with L = log sum exp(lse_p),

@@ -128,6 +128,27 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return h2_as_u32(__floats2half2_rn(lo, hi));
 }
 
+// ------------------------------------------------------------------ RoPE ----
+// Angle of rotation pair i at text position `pos`: theta = pos * scale^i with the
+// power built by repeated float multiplication (as ggml-cpu builds its rope cache,
+// tests/attn_test.rs:173-193); cos/sin of that float angle are evaluated in double
+// after a Cody-Waite reduction modulo 2*pi (2*pi split into a 34-bit head, exact for
+// multiples k < 2^19, plus a double tail) and rounded to float.  The results are
+// within an ulp of libm's cosf/sinf, and the reduction keeps positions ~1.7e5 on the
+// fast path of sincos().
+__device__ __forceinline__ float2 rope_cos_sin(int64_t pos, float theta_scale, int i) {
+    float th = static_cast<float>(static_cast<int32_t>(pos));
+    for (int k = 0; k < i; ++k) th = __fmul_rn(th, theta_scale);
+    const double x = static_cast<double>(th);
+    const double kq = rint(x * 0.15915494309189535);  // x / (2 pi)
+    const double two_pi_hi = 6.2831853069365025;     // 2 pi truncated to 34 significant bits
+    const double two_pi_lo = 2.430840202602477e-10;  // 2 pi - two_pi_hi
+    const double r = __dsub_rn(__dsub_rn(x, kq * two_pi_hi), kq * two_pi_lo);
+    double sd, cd;
+    sincos(r, &sd, &cd);
+    return make_float2(static_cast<float>(cd), static_cast<float>(sd));
+}
+
 // ---------------------------------------------------- tiled q4_0 layout ------
 //
 // The cache is a sequence of 16-token groups.  Group gr (tokens 16gr..16gr+15)
@@ -187,6 +208,61 @@ __host__ __device__ __forceinline__ int64_t v_scale_offset(int64_t t, int h, int
     const int c = lo >> 1, odd = lo & 1;
     const int jj = hi8 * 2 + odd;  // 2c -> 0, 2c+1 -> 1, 2c+8 -> 2, 2c+9 -> 3
     return (gr * kHeadsKV + h) * kUnitBytes + kUnitQsBytes + c * 64 + 8 * b + 2 * jj;
+}
+
+// ------------------------------------------------------- q4_0 block store ---
+// One element of a new K/V row: head h, dim `dim` of token row `base` (element
+// offset of the head's first value) in `src`; K rows get the partial RoPE of
+// attn.rs:183-204 (NEOX pairs (i, i + n_rot/2)) with cos/sin from `rope_tab`.
+__device__ __forceinline__ float kv_row_elem(const void *src, int64_t base, int dim, int dtype,
+                                             int rope_n_rot, const float2 *rope_tab) {
+    float x = load_act(src, base + dim, dtype);
+    if (dim < rope_n_rot) {
+        const int half = rope_n_rot >> 1;
+        const int i = dim < half ? dim : dim - half;
+        const float partner = load_act(src, base + (dim < half ? dim + half : dim - half), dtype);
+        const float2 cs = rope_tab[i];
+        x = dim < half ? __fsub_rn(__fmul_rn(x, cs.x), __fmul_rn(partner, cs.y))   // x0 c - x1 s
+                       : __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(x, cs.x));  // x0 s + x1 c
+    }
+    return x;
+}
+
+// One warp quantises one 32-element block (lane j holds element j) of token `row`,
+// head h, block b into the tiled cache.  quantize_row_q4_0 rounding: the signed value
+// of largest magnitude (first index on ties) gives d = max / -8, id = 1/d (0 if d == 0),
+// nibble = min(15, trunc(x * id + 8.5)), every step an IEEE single op (no contraction),
+// d stored as fp16 (RNE).  Bit-exact with ggml's CPU reference for the same input.
+__device__ __forceinline__ void q4_0_store_block(float x, int lane, uint8_t *cache, int64_t row, int h,
+                                                 int b, bool is_v) {
+    float amax = fabsf(x);
+    float vmax = x;
+    int idx = lane;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+        const float ov = __shfl_xor_sync(0xffffffffu, vmax, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+        if (oa > amax || (oa == amax && oi < idx)) {
+            amax = oa;
+            vmax = ov;
+            idx = oi;
+        }
+    }
+    // A block whose every |x| is 0 keeps max = 0 (the reference starts from amax = max = 0).
+    if (amax == 0.0f) vmax = 0.0f;
+    const float d = __fdiv_rn(vmax, -8.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    int q = __float2int_rz(__fadd_rn(__fmul_rn(x, id), 8.5f));
+    q = min(15, max(0, q));
+    const int qhi = __shfl_down_sync(0xffffffffu, q, 16);
+    if (lane < 16) {
+        const uint8_t byte = static_cast<uint8_t>(q | (qhi << 4));
+        cache[is_v ? v_qs_offset(row, h, b, lane) : k_qs_offset(row, h, b, lane)] = byte;
+    }
+    if (lane == 0)
+        *reinterpret_cast<__half *>(cache + (is_v ? v_scale_offset(row, h, b) : k_scale_offset(row, h, b))) =
+            __float2half_rn(d);
 }
 
 }  // namespace sqmix

@@ -1,71 +1,97 @@
 // fa_decode.cu -- split-KV FlashAttention decode over the tiled q4_0 KV cache.
 //
-// Replaces ggml_flash_attn_ext (src/model/attn.rs:238-249; the op's contract is
-// restated at src/backend/ffi.rs:363-377) for 1 or 2 query tokens (decode, MTP
-// verify), plus the sigmoid output gate of attn.rs:282-283 (fused in the merge).
+// Replaces, for 1 or 2 query tokens (decode, MTP verify), the per-layer chain
+//   ggml_set_rows (q4_0 KV append, src/engine/kv.rs:367-396) ->
+//   ggml_flash_attn_ext (src/model/attn.rs:238-249; contract at src/backend/ffi.rs:363-377) ->
+//   sigmoid gate (attn.rs:282-283)
+// with ONE cooperative kernel launch:
 //
-// Design (per CTA = one split of the key range):
-//   * lane 0 of warp 0 streams 64-token tiles of K and V (18 KiB each) with 1-D
-//     TMA bulk copies into a 4-stage shared-memory ring (mbarrier full/empty);
-//   * warps 0..7 (warp w handles KV head w/4 and 16-token group w%4 of
-//     each tile) dequantise q4_0 nibbles straight into mma.m16n8k16 A-fragments
-//     (no dequantised tile is ever written to shared memory), compute
-//     S^T = K Q^T with M = 16 tokens x N = 8 query heads (GQA packing: no padding
-//     at n_q = 1), apply the per-block K scale in fp32, run an online softmax with
-//     warp shuffles, transpose P with movmatrix, fold the per-block V scale into P
-//     and accumulate O^T = V^T P^T;
-//   * the 4 warps of a KV head merge through shared memory and the CTA writes one
-//     (O, m, l) partial; fa_merge_kernel combines the splits (log-sum-exp merge),
-//     applies sigmoid(gate) and writes out / lse.
+//   1. the CTA whose key range holds the step's new rows quantises them into the
+//      cache (bit-exact quantize_row_q4_0, RoPE on K) before streaming them;
+//   2. every CTA streams its contiguous run of 16-token groups of K and V with 1-D
+//      TMA bulk copies (lane 0 of warp 0 is the producer) through an NSTAGE ring;
+//   3. warp w handles KV head w / WPH and group w % WPH of each tile: q4_0 nibbles go
+//      straight from shared memory into mma.m16n8k16 A fragments as f16 subnormals
+//      (one LOP3 per pair; the q4_0 offset of -8 is restored exactly on the
+//      accumulator side), S^T = K Q^T with M = 16 tokens x N = 8 query heads (GQA
+//      packing), per-block K scales applied in fp32, online softmax with warp
+//      shuffles, P transposed with movmatrix, per-block V scales folded into P,
+//      O^T += V^T P^T;
+//   4. the warps of a KV head combine through shared memory into one (O, m, l)
+//      partial per CTA;
+//   5. after a bounded grid barrier (monotonic ticket counter in the workspace)
+//      each CTA merges a 32-dim slice of the output across all splits (log-sum-exp),
+//      applies sigmoid(gate) and writes out / lse.
+//
 // Keys are never read beyond min(n_kv, q_pos0 + n_q): the causal limit of
-// graph.rs:553-559 is applied implicitly, so no mask tensor exists.
+// graph.rs:553-559 is applied implicitly, so no mask tensor exists.  When the split
+// count exceeds what can be co-resident, step 5 runs as a separate merge kernel.
+//
+// Pipeline: a 5-slot ring of 64-token slots (36.9 KB of K+V each); a compute step of
+// n_q = 1 consumes two slots (each warp takes two groups of its KV head: one online-
+// softmax update per 32 tokens, two independent MMA streams), so three slots stay in
+// flight while the warps compute; n_q = 2 needs twice the accumulators and consumes
+// one slot per step.
 #include <math.h>
 
 #include "common.cuh"
 
 namespace sqmix {
 
-constexpr int kFaStages = 4;
-constexpr int kFaTileGroups = 4;                           // 64 tokens per stage
-constexpr int kFaTileBytes = kFaTileGroups * kGroupBytes;  // 18432 per cache
-constexpr int kFaConsumerWarps = 8;
-constexpr int kFaThreads = kFaConsumerWarps * 32;
-constexpr int kFaWsHeader = 256;  // error word + reserved
+constexpr int kFaWsHeader = 256;  // [0] u32 error bits
 
 struct FaDecodeParams {
     const void *q;
     int q_dtype;
     int64_t q_st;
     int64_t q_sh;
-    const uint8_t *k_cache;
-    const uint8_t *v_cache;
+    uint8_t *k_cache;
+    uint8_t *v_cache;
     const int64_t *n_kv;
     const int64_t *q_pos0;
     int64_t capacity;  // rows in each cache: device-side n_kv is clamped to it
-    float c;  // scale * log2(e)
+    float c;           // scale * log2(e)
+    float scale;
     int rope_n_rot;
     float rope_theta_scale;
     int64_t rope_pos_offset;
+    // fused append of the step's rows (rows q_pos0 + t, t < n_new)
+    const void *k_new;
+    const void *v_new;
+    int kv_dtype;
+    int64_t k_new_st;
+    int64_t v_new_st;
+    int n_new;
+    // partials and fused merge
     float *part_o;   // [splits][nq][16][256]
     float *part_ml;  // [splits][nq][16][2]
     uint32_t *err;
+    int overlap_prev;  // SQMIX_FA_OVERLAP_PREV: prefetch before the grid dependency wait
 };
 
-template <int NQ>
-struct FaSmem {
-    static constexpr int kStageBytes = 2 * kFaTileBytes;
-    static constexpr int kRingBytes = kFaStages * kStageBytes;             // 147456
-    static constexpr int kQBytes = NQ * 16 * 256 * 4;                       // f32 staging
-    static constexpr int kRedOBytes = kFaConsumerWarps * NQ * 8 * 256 * 4;  // reuses the ring
+template <int NQ, int WPH, int GPW, int NSTAGE, int MINB>
+struct FaCfg {
+    static constexpr int kWarps = 2 * WPH;
+    static constexpr int kThreads = kWarps * 32;
+    // One ring slot holds WPH groups (16 * WPH tokens) of K and of V; a compute step
+    // consumes GPW consecutive slots, warp (h, u) taking group u of each.
+    static constexpr int kTileGroups = WPH;
+    static constexpr int kTileBytes = kTileGroups * kGroupBytes;  // per cache
+    static constexpr int kStageBytes = 2 * kTileBytes;
+    static constexpr int kRingBytes = NSTAGE * kStageBytes;
+    static_assert(NSTAGE > GPW, "the ring must hold more slots than one compute step uses");
+    static constexpr int kRedStride = 260;  // floats per (warp, qi, head) row: conflict-free stores
+    static constexpr int kRedOBytes = kWarps * NQ * 8 * kRedStride * 4;  // reuses the ring
     static_assert(kRedOBytes <= kRingBytes, "reduction buffer must fit in the ring");
-    // n_q = 2 keeps the Q^T fragments in shared memory ([kvh][qi][b][s][lane] uint2):
-    // in registers they push the kernel past 224 registers and into spills.
-    static constexpr bool kQfSmem = NQ >= 2;
-    static constexpr int kQfBytes = kQfSmem ? 2 * NQ * 8 * 2 * 32 * 8 : 0;
-    static constexpr int kQfOffset = kRingBytes + kQBytes;
-    static constexpr int kBarOffset = kQfOffset + kQfBytes;
-    static constexpr int kRedMlOffset = kBarOffset + 128;
-    static constexpr int kTotal = kRedMlOffset + kFaConsumerWarps * NQ * 8 * 2 * 4;
+    static constexpr int kQfOffset = kRingBytes;                  // [kvh][qi][b][s][lane] uint2
+    static constexpr int kQfBytes = 2 * NQ * 8 * 2 * 32 * 8;
+    static constexpr int kKinitOffset = kQfOffset + kQfBytes;     // [kvh][qi][b][8] f32
+    static constexpr int kRopeOffset = kKinitOffset + 2 * NQ * 8 * 8 * 4;  // [qi][32] float2
+    static constexpr int kBarOffset = kRopeOffset + NQ * 32 * 8;
+    static constexpr int kRelOffset = kBarOffset + 2 * NSTAGE * 8;  // [NSTAGE] release counters
+    static constexpr int kRedMlOffset = kRelOffset + ((NSTAGE * 4 + 15) / 16) * 16;
+    static constexpr int kWtsOffset = kRedMlOffset + kWarps * NQ * 8 * 2 * 4;  // [qi][16][WPH + 2]
+    static constexpr int kTotal = kWtsOffset + NQ * 16 * (WPH + 2) * 4;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -74,30 +100,117 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// Nibble-pair extraction.  With w = 4 bytes {b0, b1, b2, b3}:
-//   lo(w)   = {b0 & 15, b2 & 15} - 8          (exact in f16)
-//   hi16(w) = 16 * ({b0 >> 4, b2 >> 4} - 8)   (exact; the x16 is undone elsewhere)
-__device__ __forceinline__ uint32_t nib_lo(uint32_t w) {
-    const __half2 v = u32_as_h2(lop3_and_or(w, 0x000F000Fu, 0x64006400u));
-    return h2_as_u32(__hsub2(v, __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408))));
-}
-__device__ __forceinline__ uint32_t nib_hi16(uint32_t w) {
-    const __half2 v = u32_as_h2(lop3_and_or(w, 0x00F000F0u, 0x64006400u));
-    return h2_as_u32(__hsub2(v, __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480))));
+// Nibble pairs as f16 subnormals.  With w = 4 bytes {b0, b1, b2, b3}:
+//   sub_lo(w) = {b0 & 15, b2 & 15} * 2^-24          (bit pattern = the nibble)
+//   sub_hi(w) = 16 * {b0 >> 4, b2 >> 4} * 2^-24     (the x16 is undone elsewhere)
+// Both are exact, cost one LOP3 per pair, and the q4_0 offset of -8 is restored
+// exactly on the accumulator side (see the QK and PV steps).
+__device__ __forceinline__ uint32_t sub_lo(uint32_t w) { return w & 0x000F000Fu; }
+__device__ __forceinline__ uint32_t sub_hi(uint32_t w) { return w & 0x00F000F0u; }
+
+// A operand of the V offset correction: rows g (lo nibbles) = -8 * 2^-24,
+// rows g+8 (hi nibbles, x16) = -128 * 2^-24, in every token column.
+constexpr uint32_t kVOffLo = 0x80088008u;
+constexpr uint32_t kVOffHi = 0x80808080u;
+constexpr float kTwo24 = 16777216.0f;
+
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// Log-sum-exp merge of the split partials for one 32-dim slice of one output row:
+// warp w folds splits w, w + nwarps, ... with an online (max, sum) update, 8 splits
+// in flight at a time; the warps then combine through shared memory `red`
+// (nwarps * 34 floats).  Reads bypass L1: the partials were written by other CTAs.
+__device__ void merge_slice(const float *part_o, const float *part_ml, int n_splits, int n_rows, int row,
+                            int slice, float c, float scale, const void *gate, int gate_dtype, int64_t g_st,
+                            int64_t g_sh, float *out, float *lse, float *red, int nwarps) {
+    constexpr int kChunk = 24;  // splits per warp per round: 8 warps x 24 covers 192 splits at once
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int d = slice * 32 + lane;
+    const size_t sstride = static_cast<size_t>(n_rows) * 256;
+    const float *po = part_o + static_cast<size_t>(row) * 256 + d;
+    const float *pml = part_ml + static_cast<size_t>(row) * 2;
+    float M = -INFINITY, Ls = 0.f, acc = 0.f;
+    if (warp < nwarps) {
+        for (int s0 = warp; s0 < n_splits; s0 += kChunk * nwarps) {
+            float mv[kChunk], lv[kChunk], ov[kChunk];
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) {
+                const int s = s0 + nwarps * j;
+                if (s < n_splits) {
+                    const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pml + static_cast<size_t>(s) * n_rows * 2));
+                    mv[j] = ml.x;
+                    lv[j] = ml.y;
+                    ov[j] = __ldcg(po + s * sstride);
+                } else {
+                    mv[j] = -INFINITY;
+                    lv[j] = 0.f;
+                    ov[j] = 0.f;
+                }
+            }
+            float mc = M;
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) mc = fmaxf(mc, mv[j]);
+            if (mc != -INFINITY) {
+                const float r = (M == -INFINITY) ? 0.f : ex2((M - mc) * c);
+                Ls *= r;
+                acc *= r;
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) {
+                    const float w = (mv[j] == -INFINITY) ? 0.f : ex2((mv[j] - mc) * c);
+                    Ls = fmaf(lv[j], w, Ls);
+                    acc = fmaf(ov[j], w, acc);
+                }
+                M = mc;
+            }
+        }
+        red[warp * 34 + lane] = acc;
+        if (lane == 0) {
+            red[warp * 34 + 32] = M;
+            red[warp * 34 + 33] = Ls;
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float Mt = -INFINITY;
+        for (int w = 0; w < nwarps; ++w) Mt = fmaxf(Mt, red[w * 34 + 32]);
+        float L = 0.f, y = 0.f;
+        for (int w = 0; w < nwarps; ++w) {
+            const float mw = red[w * 34 + 32];
+            const float wt = (mw == -INFINITY) ? 0.f : ex2((mw - Mt) * c);
+            L = fmaf(red[w * 34 + 33], wt, L);
+            y = fmaf(red[w * 34 + lane], wt, y);
+        }
+        y = L > 0.f ? y / L : 0.f;
+        if (gate) {
+            const int qi = row >> 4, h = row & 15;
+            const float gv = load_act(gate, qi * g_st + h * g_sh + d, gate_dtype);
+            y *= 1.0f / (1.0f + expf(-gv));
+        }
+        out[static_cast<size_t>(row) * 256 + d] = y;
+        if (lse && slice == 0 && lane == 0) lse[row] = L > 0.f ? Mt * scale + logf(L) : -INFINITY;
+    }
+    __syncthreads();  // `red` is reused by the next slice
 }
 
-template <int NQ>
-__global__ void __launch_bounds__(kFaThreads, 1) fa_decode_kernel(FaDecodeParams p) {
+template <int NQ, int WPH, int GPW, int NSTAGE, int MINB>
+__global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, MINB)
+    fa_decode_kernel(FaDecodeParams p) {
+    using L = FaCfg<NQ, WPH, GPW, NSTAGE, MINB>;
     extern __shared__ __align__(1024) uint8_t smem[];
-    using L = FaSmem<NQ>;
     uint8_t *ring = smem;
-    float *q_s = reinterpret_cast<float *>(smem + L::kRingBytes);
+    uint2 *qf_s = reinterpret_cast<uint2 *>(smem + L::kQfOffset);
+    float2 *rope_s = reinterpret_cast<float2 *>(smem + L::kRopeOffset);
     uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + L::kBarOffset);
-    uint64_t *empty_bar = full_bar + kFaStages;
+    uint64_t *empty_bar = full_bar + NSTAGE;
+    int *rel_cnt = reinterpret_cast<int *>(smem + L::kRelOffset);
     float *red_ml = reinterpret_cast<float *>(smem + L::kRedMlOffset);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+
+    // Without SQMIX_FA_OVERLAP_PREV nothing is read before the previous kernel is done.
+    if (!p.overlap_prev) grid_dependency_wait();
 
     // ---- work range: a contiguous run of 16-token groups ---------------------
     int64_t n_kv = *p.n_kv;
@@ -110,193 +223,347 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_decode_kernel(FaDecodeParams
     if (n_keys > n_kv) n_keys = n_kv;
     if (n_keys < 0) n_keys = 0;
     const int64_t n_groups = (n_keys + kGroupTokens - 1) / kGroupTokens;
-    const int64_t g_begin = (static_cast<int64_t>(blockIdx.x) * n_groups) / gridDim.x;
-    const int64_t g_end = (static_cast<int64_t>(blockIdx.x + 1) * n_groups) / gridDim.x;
-    const int n_tiles = static_cast<int>((g_end - g_begin + kFaTileGroups - 1) / kFaTileGroups);
+    // The split holding the step's new rows (the last one) also quantises them: it
+    // gets kAppendGroups fewer groups so that it finishes with the others.
+    constexpr int64_t kAppendGroups = 8;
+    const int64_t n_virt = n_groups + (p.n_new > 0 ? kAppendGroups : 0);
+    int64_t g_begin = (static_cast<int64_t>(blockIdx.x) * n_virt) / gridDim.x;
+    int64_t g_end = (static_cast<int64_t>(blockIdx.x + 1) * n_virt) / gridDim.x;
+    if (g_begin > n_groups) g_begin = n_groups;
+    if (g_end > n_groups) g_end = n_groups;
+    const int n_tiles = static_cast<int>((g_end - g_begin + L::kTileGroups - 1) / L::kTileGroups);
+    // Rows [q_pos0, q_pos0 + n_new) are written by this launch (fused append); the CTA
+    // whose range holds them writes them before it may stream them.
+    const int64_t row_lo = g_begin * kGroupTokens, row_hi = g_end * kGroupTokens;
+    const bool has_fresh = p.n_new > 0 && q_pos0 < row_hi && q_pos0 + p.n_new > row_lo;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kFaStages; ++s) {
+        for (int s = 0; s < NSTAGE; ++s) {
             mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], kFaConsumerWarps);
+            mbar_init(&empty_bar[s], L::kWarps);
+            rel_cnt[s] = 0;
         }
         fence_mbar_init();
     }
     __syncthreads();
 
-    // Lane 0 of warp 0 doubles as the TMA producer (a separate producer warp would
-    // put 3 warps on one SM sub-partition and cap every thread at 168 registers).
+    // Thread 0 fills the ring initially; afterwards the warp that releases a slot last
+    // refills it (elected with a shared-memory counter), so no warp ever waits for the
+    // others to finish a tile and the refill starts as early as possible.  The last
+    // kStagingSlots slots first serve as staging for Q and the new rows.
     const bool producer = threadIdx.x == 0;
     auto issue = [&](int it) {
-        const int s = it % kFaStages;
-        const int64_t gr0 = g_begin + static_cast<int64_t>(it) * kFaTileGroups;
+        const int s = it % NSTAGE;
+        const int64_t gr0 = g_begin + static_cast<int64_t>(it) * L::kTileGroups;
         int64_t ng = g_end - gr0;
-        if (ng > kFaTileGroups) ng = kFaTileGroups;
+        if (ng > L::kTileGroups) ng = L::kTileGroups;
         const uint32_t bytes = static_cast<uint32_t>(ng) * kGroupBytes;
         mbar_arrive_expect_tx(&full_bar[s], 2 * bytes);
         uint8_t *dst = ring + s * L::kStageBytes;
         bulk_g2s(dst, p.k_cache + gr0 * kGroupBytes, bytes, &full_bar[s]);
-        bulk_g2s(dst + kFaTileBytes, p.v_cache + gr0 * kGroupBytes, bytes, &full_bar[s]);
+        bulk_g2s(dst + L::kTileBytes, p.v_cache + gr0 * kGroupBytes, bytes, &full_bar[s]);
     };
-    if (producer)
-        for (int it = 0; it < n_tiles && it < kFaStages; ++it) issue(it);
+    constexpr int kStagingBytes = (NQ * 16 * 256 + NQ * 2 * 512) * 4;
+    constexpr int kStagingSlots = (kStagingBytes + L::kStageBytes - 1) / L::kStageBytes;
+    static_assert(kStagingSlots < NSTAGE, "staging must leave ring slots for the first tiles");
+    // Slots filled before the dependency wait: the ring minus the staging slots, at most
+    // two (73.7 KB per SM), so that the Q loads after the wait do not queue behind a
+    // long fill.
+    constexpr int kEarlySlots = (NSTAGE - kStagingSlots) < 2 ? (NSTAGE - kStagingSlots) : 2;
+    // Initial fill of the ring, minus the staging slots.  Rows from q_pos0 on belong to
+    // this step: they are written by this launch (fused append, deferred until then) or
+    // by the kernel just before it (streamed only after the dependency wait).  With
+    // SQMIX_FA_OVERLAP_PREV the first kEarlySlots tiles below q_pos0 are requested
+    // before that wait, overlapping the tail of the previous kernel.
+    int issued = 0;  // meaningful in the producer thread only
+    auto fill = [&](int upto, int64_t row_limit) {
+        const int first = n_tiles < upto ? n_tiles : upto;
+        while (issued < first) {
+            int64_t tile_end = (g_begin + static_cast<int64_t>(issued + 1) * L::kTileGroups) * kGroupTokens;
+            if (tile_end > row_hi) tile_end = row_hi;
+            if (tile_end > row_limit) break;
+            issue(issued++);
+        }
+    };
+    if (producer && p.overlap_prev) fill(kEarlySlots, q_pos0);
+    // From here on the previous kernel's results (Q, the new rows, a free workspace) are
+    // visible.  The trigger comes after the wait, so a kernel may run its pre-wait part
+    // only once everything two launches back has completed.
+    grid_dependency_wait();
+    launch_dependents();
 
-    // ================= consumers =================
-    const int kvh = warp >> 2;  // KV head
-    const int u = warp & 3;     // group within the tile
+    // ---- Q and the step's new K/V rows (produced by earlier kernels: after the wait) --
+    constexpr int kQPer = NQ * 16 * 256 / L::kThreads;
+    float qv[kQPer];
+#pragma unroll
+    for (int k = 0; k < kQPer; ++k) {
+        const int e = threadIdx.x + k * L::kThreads;  // [qi][head][256]
+        qv[k] = load_act(p.q, (e >> 12) * p.q_st + ((e >> 8) & 15) * p.q_sh + (e & 255), p.q_dtype);
+    }
+    constexpr int kKvPer = NQ * 2 * 512 / L::kThreads;
+    float kvv[kKvPer];
+    if (has_fresh) {
+#pragma unroll
+        for (int k = 0; k < kKvPer; ++k) {
+            const int e = threadIdx.x + k * L::kThreads;  // [t][k|v][512]
+            const int t = e >> 10, is_v = (e >> 9) & 1;
+            kvv[k] = t < p.n_new ? load_act(is_v ? p.v_new : p.k_new,
+                                            t * (is_v ? p.v_new_st : p.k_new_st) + (e & 511), p.kv_dtype)
+                                 : 0.f;
+        }
+    }
+    if (producer) fill(NSTAGE - kStagingSlots, has_fresh ? q_pos0 : INT64_MAX);
+
+
+    const int kvh = warp / WPH;  // KV head
+    const int u = warp % WPH;    // first group of this warp within the tile
     const int g = lane >> 2;
     const int c = lane & 3;
 
-    // ---- stage Q (f32) with RoPE, then build the B fragments ------------------
-    for (int i = threadIdx.x; i < NQ * 16 * 256; i += kFaConsumerWarps * 32) {
-        const int qi = i / (16 * 256);
-        const int h = (i / 256) & 15;
-        const int d = i & 255;
-        q_s[i] = load_act(p.q, qi * p.q_st + h * p.q_sh + d, p.q_dtype);
+    float *q_stage = reinterpret_cast<float *>(ring + (NSTAGE - kStagingSlots) * L::kStageBytes);
+    float *kv_stage = q_stage + NQ * 16 * 256;
+#pragma unroll
+    for (int k = 0; k < kQPer; ++k) q_stage[threadIdx.x + k * L::kThreads] = qv[k];
+    if (has_fresh) {
+#pragma unroll
+        for (int k = 0; k < kKvPer; ++k) kv_stage[threadIdx.x + k * L::kThreads] = kvv[k];
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(kFaConsumerWarps * 32));
-    if (p.rope_n_rot > 0) {
-        const int half = p.rope_n_rot >> 1;
-        for (int i = threadIdx.x; i < NQ * 16 * half; i += kFaConsumerWarps * 32) {
-            const int qi = i / (16 * half);
-            const int h = (i / half) & 15;
-            const int pi = i % half;
-            float th = static_cast<float>(static_cast<int32_t>(q_pos0 + qi + p.rope_pos_offset));
-            for (int k = 0; k < pi; ++k) th = __fmul_rn(th, p.rope_theta_scale);
-            float sn, cs;
-            sincosf(th, &sn, &cs);
-            float *row = q_s + (qi * 16 + h) * 256;
-            const float x0 = row[pi], x1 = row[pi + half];
-            row[pi] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-            row[pi + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+    (void)kvv;
+
+    // ---- RoPE angles of the step's positions (shared by Q and the new K rows) ----
+    const int half = p.rope_n_rot >> 1;
+    if (p.rope_n_rot > 0 && threadIdx.x < NQ * 32) {
+        const int qi = threadIdx.x >> 5, i = threadIdx.x & 31;
+        if (i < half)
+            rope_s[qi * 32 + i] = rope_cos_sin(q_pos0 + qi + p.rope_pos_offset, p.rope_theta_scale, i);
+    }
+    __syncthreads();
+
+    // ---- fused append: quantise the step's new K/V rows held by this CTA ----------
+    if (has_fresh) {
+        for (int task = warp; task < 32 * p.n_new; task += L::kWarps) {
+            const int t = task >> 5, r = task & 31;
+            const bool is_v = r >> 4;
+            const int h = (r >> 3) & 1, b = r & 7;
+            const int64_t row = q_pos0 + t;
+            if (row < row_lo || row >= row_hi) continue;  // another CTA's row
+            const float x = kv_row_elem(kv_stage, ((t * 2 + is_v) * 2 + h) * 256, b * 32 + lane, SQMIX_F32,
+                                        is_v ? 0 : p.rope_n_rot, rope_s + t * 32);
+            q4_0_store_block(x, lane, is_v ? p.v_cache : p.k_cache, row, h, b, is_v);
         }
-        asm volatile("bar.sync 1, %0;" ::"n"(kFaConsumerWarps * 32));
+        // the bulk copies (async proxy) that stream these rows must see the stores
+        asm volatile("fence.proxy.async.global;" ::: "memory");
     }
-    // B fragment of Q^T for block b, k-slice s: k-slot kappa of slice s maps to
-    // dim 32b + (kappa < 8 ? 4(kappa/2) + 2(kappa%2) : 16 + 4((kappa-8)/2) + 2(kappa%2)) + s;
-    // lane (g, c) supplies head 8*kvh + g, k-slots {2c, 2c+1} and {2c+8, 2c+9}.
-    constexpr int kQfN = L::kQfSmem ? 1 : NQ;  // register copy unused when in smem
-    uint32_t qf[kQfN][8][2][2];
-    uint2 *qf_s = reinterpret_cast<uint2 *>(smem + L::kQfOffset);
+
+    // ---- Q^T fragments (f16) with RoPE -------------------------------------------
+    // k-slot kappa of k-slice s of block b maps to dim
+    //   32b + (kappa < 8 ? 4(kappa/2) + 2(kappa%2) : 16 + 4((kappa-8)/2) + 2(kappa%2)) + s
+    // (the order in which a 32-bit load of qs[4c..4c+3] delivers nibbles); lane (g, c)
+    // supplies head 8*kvh + g, k-slots {2c, 2c+1} and {2c+8, 2c+9} (the latter / 16).
+    for (int item = threadIdx.x; item < 2 * NQ * 8 * 2 * 32; item += L::kThreads) {
+        const int ln = item & 31;
+        const int s = (item >> 5) & 1;
+        const int b = (item >> 6) & 7;
+        const int qi = (item >> 9) % NQ;
+        const int kh = (item >> 9) / NQ;
+        const int gg = ln >> 2, cc = ln & 3;
+        const int qrow = (qi * 16 + kh * 8 + gg) * 256;
+        const int d0 = 32 * b + 4 * cc + s;
+        const int dims[4] = {d0, d0 + 2, d0 + 16, d0 + 18};
+        float v[4];
 #pragma unroll
-    for (int qi = 0; qi < NQ; ++qi) {
-        const float *row = q_s + (qi * 16 + kvh * 8 + g) * 256;
+        for (int e = 0; e < 4; ++e) v[e] = kv_row_elem(q_stage, qrow, dims[e], SQMIX_F32, p.rope_n_rot, rope_s + qi * 32);
+        qf_s[item] = make_uint2(pack_half2(v[0], v[1]), pack_half2(v[2] * 0.0625f, v[3] * 0.0625f));
+    }
+    __syncthreads();
+    // K offset term per (kvh, query, block, head): -8 * 2^-24 * sum_j q_j over the
+    // block, from the exact f16 values the MMA consumes (hi slots hold q / 16).
+    float *kinit_s = reinterpret_cast<float *>(smem + L::kKinitOffset);
+    if (threadIdx.x < 2 * NQ * 8 * 8) {
+        const int h8 = threadIdx.x & 7;
+        const int b = (threadIdx.x >> 3) & 7;
+        const int qk = threadIdx.x >> 6;  // kvh * NQ + qi
+        float sum = 0.f;
 #pragma unroll
-        for (int b = 0; b < 8; ++b) {
+        for (int ss = 0; ss < 2; ++ss)
 #pragma unroll
-            for (int s = 0; s < 2; ++s) {
-                const int d0 = 32 * b + 4 * c + s;
-                const uint32_t lo = pack_half2(row[d0], row[d0 + 2]);
-                const uint32_t hi = pack_half2(row[d0 + 16] * 0.0625f, row[d0 + 18] * 0.0625f);
-                if constexpr (L::kQfSmem) {
-                    if (u == 0) qf_s[(((kvh * NQ + qi) * 8 + b) * 2 + s) * 32 + lane] = make_uint2(lo, hi);
-                } else {
-                    qf[qi][b][0 + s][0] = lo;
-                    qf[qi][b][0 + s][1] = hi;
-                }
+            for (int cc = 0; cc < 4; ++cc) {
+                const uint2 x = qf_s[((qk * 8 + b) * 2 + ss) * 32 + 4 * h8 + cc];
+                const float2 lo = __half22float2(u32_as_h2(x.x));
+                const float2 hi = __half22float2(u32_as_h2(x.y));
+                sum += (lo.x + lo.y) + 16.0f * (hi.x + hi.y);
             }
-        }
+        kinit_s[threadIdx.x] = -8.0f / kTwo24 * sum;
     }
-    if constexpr (L::kQfSmem) asm volatile("bar.sync 1, %0;" ::"n"(kFaConsumerWarps * 32));
+    __syncthreads();  // the staging slots are free from here on
+    if (producer) {  // staging slots and tiles held back for the fused append
+        const int first = n_tiles < NSTAGE ? n_tiles : NSTAGE;
+        while (issued < first) issue(issued++);
+    }
 
     float o[NQ][8][2][4];
+    float vcorr[NQ][8][4];  // per block: -8 * 2^-24 * sum_t P'_b[t] (rows g), x16 (rows g+8)
     float m_run[NQ][2], l_run[NQ][2];
 #pragma unroll
     for (int qi = 0; qi < NQ; ++qi) {
         m_run[qi][0] = m_run[qi][1] = -INFINITY;
         l_run[qi][0] = l_run[qi][1] = 0.f;
 #pragma unroll
-        for (int b = 0; b < 8; ++b)
+        for (int b = 0; b < 8; ++b) {
+#pragma unroll
+            for (int r = 0; r < 4; ++r) vcorr[qi][b][r] = 0.f;
 #pragma unroll
             for (int m = 0; m < 2; ++m)
 #pragma unroll
                 for (int r = 0; r < 4; ++r) o[qi][b][m][r] = 0.f;
+        }
     }
-    const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint2 *qf_w = qf_s + (kvh * NQ) * 8 * 2 * 32 + lane;
+    const float2 *kinit_w = reinterpret_cast<const float2 *>(kinit_s) + (kvh * NQ) * 8 * 4 + c;
+    const float craw = p.c * kTwo24;  // scores below are in units of 2^-24
+    const uint32_t voff[4] = {kVOffLo, kVOffHi, kVOffLo, kVOffHi};
     bool ok = true;
 
-    for (int it = 0; it < n_tiles; ++it) {
-        const int s = it % kFaStages;
-        if (!mbar_wait(&full_bar[s], (it / kFaStages) & 1)) {
-            ok = false;
-            break;
-        }
-        const int64_t gr = g_begin + static_cast<int64_t>(it) * kFaTileGroups + u;
-        const int64_t tok0 = gr * kGroupTokens;
-        if (gr < g_end && tok0 < n_keys) {
-            const uint8_t *kunit = ring + s * L::kStageBytes + (u * 2 + kvh) * kUnitBytes;
-            const uint8_t *vunit = kunit + kFaTileBytes;
-
-            // ---------------- S^T = K Q^T ----------------
-            const uint4 *kq4 = reinterpret_cast<const uint4 *>(kunit);
-            uint32_t kw[16];
+    // S^T = K Q^T for one 16-token group of this warp's KV head (result in 2^-24 units).
+    // Two halves of 4 blocks each keep only 8 nibble words live at a time.
+    auto qk_unit = [&](const uint8_t *kunit, float (&sc)[NQ][4]) {
+        const uint4 *kq4 = reinterpret_cast<const uint4 *>(kunit);
+        const uint4 *ksc = reinterpret_cast<const uint4 *>(kunit + kUnitQsBytes + g * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint4 x = kq4[i * 32 + lane];
-                kw[4 * i + 0] = x.x;
-                kw[4 * i + 1] = x.y;
-                kw[4 * i + 2] = x.z;
-                kw[4 * i + 3] = x.w;
-            }
-            const uint4 *ksc = reinterpret_cast<const uint4 *>(kunit + kUnitQsBytes + g * 32);
-            const uint4 kd0 = ksc[0], kd1 = ksc[1];
-            const uint32_t kdl[4] = {kd0.x, kd0.y, kd0.z, kd0.w};
-            const uint32_t kdh[4] = {kd1.x, kd1.y, kd1.z, kd1.w};
-
-            float sc[NQ][4];
+        for (int qi = 0; qi < NQ; ++qi)
 #pragma unroll
-            for (int qi = 0; qi < NQ; ++qi)
+            for (int r = 0; r < 4; ++r) sc[qi][r] = 0.f;
 #pragma unroll
-                for (int r = 0; r < 4; ++r) sc[qi][r] = 0.f;
+        for (int hb = 0; hb < 2; ++hb) {
+            const uint4 xl = kq4[hb * 32 + lane];        // token g, blocks 4hb..4hb+3
+            const uint4 xh = kq4[(2 + hb) * 32 + lane];  // token g+8
+            const uint32_t kwl[4] = {xl.x, xl.y, xl.z, xl.w};
+            const uint32_t kwh[4] = {xh.x, xh.y, xh.z, xh.w};
+            const uint2 dlw = reinterpret_cast<const uint2 *>(ksc)[hb];      // 4 scales, token g
+            const uint2 dhw = reinterpret_cast<const uint2 *>(ksc + 1)[hb];  // token g+8
+            const uint32_t kdl[2] = {dlw.x, dlw.y};
+            const uint32_t kdh[2] = {dhw.x, dhw.y};
 #pragma unroll
-            for (int b = 0; b < 8; ++b) {
-                const uint32_t wl = kw[(b >> 2) * 4 + (b & 3)];      // token g
-                const uint32_t wh = kw[8 + (b >> 2) * 4 + (b & 3)];  // token g+8
+            for (int bq = 0; bq < 4; ++bq) {
+                const int b = 4 * hb + bq;
+                const uint32_t wl = kwl[bq], wh = kwh[bq];
                 const uint32_t wl8 = wl >> 8, wh8 = wh >> 8;
-                const uint32_t a0[4] = {nib_lo(wl), nib_lo(wh), nib_hi16(wl), nib_hi16(wh)};
-                const uint32_t a1[4] = {nib_lo(wl8), nib_lo(wh8), nib_hi16(wl8), nib_hi16(wh8)};
-                const __half2 dl2 = u32_as_h2(kdl[b >> 1]);
-                const __half2 dh2 = u32_as_h2(kdh[b >> 1]);
-                const float dl = (b & 1) ? __high2float(dl2) : __low2float(dl2);
-                const float dh = (b & 1) ? __high2float(dh2) : __low2float(dh2);
+                const uint32_t a0[4] = {sub_lo(wl), sub_lo(wh), sub_hi(wl), sub_hi(wh)};
+                const uint32_t a1[4] = {sub_lo(wl8), sub_lo(wh8), sub_hi(wl8), sub_hi(wh8)};
+                const __half2 dl2 = u32_as_h2(kdl[bq >> 1]);
+                const __half2 dh2 = u32_as_h2(kdh[bq >> 1]);
+                const float dl = (bq & 1) ? __high2float(dl2) : __low2float(dl2);
+                const float dh = (bq & 1) ? __high2float(dh2) : __low2float(dh2);
 #pragma unroll
                 for (int qi = 0; qi < NQ; ++qi) {
-                    uint32_t b00, b01, b10, b11;
-                    if constexpr (L::kQfSmem) {
-                        const uint2 *qb = qf_s + ((kvh * NQ + qi) * 8 + b) * 2 * 32 + lane;
-                        const uint2 x0 = qb[0], x1 = qb[32];
-                        b00 = x0.x;
-                        b01 = x0.y;
-                        b10 = x1.x;
-                        b11 = x1.y;
-                    } else {
-                        b00 = qf[qi][b][0][0];
-                        b01 = qf[qi][b][0][1];
-                        b10 = qf[qi][b][1][0];
-                        b11 = qf[qi][b][1][1];
-                    }
+                    const uint2 x0 = qf_w[((qi * 8 + b) * 2 + 0) * 32];
+                    const uint2 x1 = qf_w[((qi * 8 + b) * 2 + 1) * 32];
+                    const float2 ki = kinit_w[(qi * 8 + b) * 4];
+                    const float init[4] = {ki.x, ki.y, ki.x, ki.y};
                     float acc[4];
-                    mma_f16_16816(acc, a0, b00, b01, zero4);
-                    mma_f16_16816(acc, a1, b10, b11, acc);
+                    mma_f16_16816(acc, a0, x0.x, x0.y, init);
+                    mma_f16_16816(acc, a1, x1.x, x1.y, acc);
                     sc[qi][0] = fmaf(dl, acc[0], sc[qi][0]);
                     sc[qi][1] = fmaf(dl, acc[1], sc[qi][1]);
                     sc[qi][2] = fmaf(dh, acc[2], sc[qi][2]);
                     sc[qi][3] = fmaf(dh, acc[3], sc[qi][3]);
                 }
             }
+        }
+    };
+    // O^T += V^T P'^T for one group (P' = P scaled by the per-block V scales).  The
+    // nibble MMAs of the 16 (block, M-tile) accumulators are independent chains; the
+    // q4_0 offset term -8 * sum_t P'_b[t] is the same for both M-tiles of a block and
+    // is accumulated once per block in vcorr (added to O in the epilogue).
+    auto pv_unit = [&](const uint8_t *vunit, const uint32_t (&pb)[NQ][2]) {
+        const uint4 *vq4 = reinterpret_cast<const uint4 *>(vunit);
+        const uint4 *vsc = reinterpret_cast<const uint4 *>(vunit + kUnitQsBytes + c * 64);
+        uint32_t vw[16], vd[16];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // blocks 2i, 2i+1
+            const uint4 x = vq4[i * 32 + lane];
+            const uint4 sx = vsc[i];
+            vw[4 * i + 0] = x.x;
+            vw[4 * i + 1] = x.y;
+            vw[4 * i + 2] = x.z;
+            vw[4 * i + 3] = x.w;
+            vd[4 * i + 0] = sx.x;
+            vd[4 * i + 1] = sx.y;
+            vd[4 * i + 2] = sx.z;
+            vd[4 * i + 3] = sx.w;
+        }
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            const __half2 s0 = u32_as_h2(vd[2 * b]);      // tokens 2c, 2c+1
+            const __half2 s1 = u32_as_h2(vd[2 * b + 1]);  // tokens 2c+8, 2c+9
+            uint32_t pbs[NQ][2];
+#pragma unroll
+            for (int qi = 0; qi < NQ; ++qi) {
+                pbs[qi][0] = h2_as_u32(__hmul2(u32_as_h2(pb[qi][0]), s0));
+                pbs[qi][1] = h2_as_u32(__hmul2(u32_as_h2(pb[qi][1]), s1));
+            }
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const uint32_t w = vw[2 * b + m];  // word (row b/2, slot 2(b&1) + m)
+                const uint32_t w8 = w >> 8;
+                const uint32_t a[4] = {sub_lo(w), sub_hi(w), sub_lo(w8), sub_hi(w8)};
+#pragma unroll
+                for (int qi = 0; qi < NQ; ++qi)
+                    mma_f16_16816(o[qi][b][m], a, pbs[qi][0], pbs[qi][1], o[qi][b][m]);
+            }
+#pragma unroll
+            for (int qi = 0; qi < NQ; ++qi)
+                mma_f16_16816(vcorr[qi][b], voff, pbs[qi][0], pbs[qi][1], vcorr[qi][b]);
+        }
+    };
 
-            // ---------------- online softmax ----------------
-            const int64_t t_lo = tok0 + g, t_hi = tok0 + g + 8;
-            uint32_t pb[NQ][2];
+    const int n_steps = (n_tiles + GPW - 1) / GPW;
+    for (int step = 0; step < n_steps; ++step) {
+        bool uv[GPW];
+        int64_t tok0[GPW];
+        const uint8_t *slot[GPW];
+        bool any = false;
+#pragma unroll
+        for (int j = 0; j < GPW; ++j) {
+            const int t = step * GPW + j;
+            uv[j] = false;
+            tok0[j] = 0;
+            slot[j] = ring;
+            if (t < n_tiles) {
+                const int s = t % NSTAGE;
+                if (!mbar_wait(&full_bar[s], (t / NSTAGE) & 1)) ok = false;
+                const int64_t gr = g_begin + static_cast<int64_t>(t) * L::kTileGroups + u;
+                tok0[j] = gr * kGroupTokens;
+                uv[j] = ok && gr < g_end && tok0[j] < n_keys;
+                slot[j] = ring + s * L::kStageBytes;
+            }
+            any = any || uv[j];
+        }
+        if (!ok) break;
+        if (any) {
+            float sc[GPW][NQ][4];
+#pragma unroll
+            for (int j = 0; j < GPW; ++j)
+                if (uv[j]) qk_unit(slot[j] + (u * 2 + kvh) * kUnitBytes, sc[j]);
+
+            // ---------------- online softmax over this warp's GPW groups ----------------
+            uint32_t pb[GPW][NQ][2];
 #pragma unroll
             for (int qi = 0; qi < NQ; ++qi) {
                 int64_t lim = q_pos0 + qi;  // inclusive
                 if (lim > n_kv - 1) lim = n_kv - 1;
-                const bool vlo = t_lo <= lim, vhi = t_hi <= lim;
-                const float x0 = vlo ? sc[qi][0] : -INFINITY;
-                const float x1 = vlo ? sc[qi][1] : -INFINITY;
-                const float x2 = vhi ? sc[qi][2] : -INFINITY;
-                const float x3 = vhi ? sc[qi][3] : -INFINITY;
-                float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+                float x[GPW][4];
+                float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < GPW; ++j) {
+                    const bool vlo = uv[j] && tok0[j] + g <= lim, vhi = uv[j] && tok0[j] + g + 8 <= lim;
+                    x[j][0] = vlo ? sc[j][qi][0] : -INFINITY;
+                    x[j][1] = vlo ? sc[j][qi][1] : -INFINITY;
+                    x[j][2] = vhi ? sc[j][qi][2] : -INFINITY;
+                    x[j][3] = vhi ? sc[j][qi][3] : -INFINITY;
+                    mx0 = fmaxf(mx0, fmaxf(x[j][0], x[j][2]));
+                    mx1 = fmaxf(mx1, fmaxf(x[j][1], x[j][3]));
+                }
 #pragma unroll
                 for (int off = 4; off < 32; off <<= 1) {
                     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
@@ -304,19 +571,29 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_decode_kernel(FaDecodeParams
                 }
                 const float mn0 = fmaxf(m_run[qi][0], mx0);
                 const float mn1 = fmaxf(m_run[qi][1], mx1);
-                const float al0 = (mn0 == m_run[qi][0]) ? 1.f : ex2((m_run[qi][0] - mn0) * p.c);
-                const float al1 = (mn1 == m_run[qi][1]) ? 1.f : ex2((m_run[qi][1] - mn1) * p.c);
-                const float p0 = vlo ? ex2((x0 - mn0) * p.c) : 0.f;
-                const float p1 = vlo ? ex2((x1 - mn1) * p.c) : 0.f;
-                const float p2 = vhi ? ex2((x2 - mn0) * p.c) : 0.f;
-                const float p3 = vhi ? ex2((x3 - mn1) * p.c) : 0.f;
-                l_run[qi][0] = fmaf(l_run[qi][0], al0, p0 + p2);
-                l_run[qi][1] = fmaf(l_run[qi][1], al1, p1 + p3);
+                const float al0 = (mn0 == m_run[qi][0]) ? 1.f : ex2((m_run[qi][0] - mn0) * craw);
+                const float al1 = (mn1 == m_run[qi][1]) ? 1.f : ex2((m_run[qi][1] - mn1) * craw);
+                float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+                for (int j = 0; j < GPW; ++j) {
+                    // masked entries give 0 (mn is finite whenever any entry is)
+                    const float p0 = x[j][0] == -INFINITY ? 0.f : ex2((x[j][0] - mn0) * craw);
+                    const float p1 = x[j][1] == -INFINITY ? 0.f : ex2((x[j][1] - mn1) * craw);
+                    const float p2 = x[j][2] == -INFINITY ? 0.f : ex2((x[j][2] - mn0) * craw);
+                    const float p3 = x[j][3] == -INFINITY ? 0.f : ex2((x[j][3] - mn1) * craw);
+                    ls0 += p0 + p2;
+                    ls1 += p1 + p3;
+                    // P^T as the B operand: transpose the two 8x8 halves of the C fragment.
+                    pb[j][qi][0] = movmatrix_trans(pack_half2(p0, p1));
+                    pb[j][qi][1] = movmatrix_trans(pack_half2(p2, p3));
+                }
+                l_run[qi][0] = fmaf(l_run[qi][0], al0, ls0);
+                l_run[qi][1] = fmaf(l_run[qi][1], al1, ls1);
                 m_run[qi][0] = mn0;
                 m_run[qi][1] = mn1;
                 if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
 #pragma unroll
-                    for (int b = 0; b < 8; ++b)
+                    for (int b = 0; b < 8; ++b) {
 #pragma unroll
                         for (int m = 0; m < 2; ++m) {
                             o[qi][b][m][0] *= al0;
@@ -324,72 +601,47 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_decode_kernel(FaDecodeParams
                             o[qi][b][m][2] *= al0;
                             o[qi][b][m][3] *= al1;
                         }
-                }
-                // P^T as the B operand: transpose the two 8x8 halves of the C fragment.
-                pb[qi][0] = movmatrix_trans(pack_half2(p0, p1));
-                pb[qi][1] = movmatrix_trans(pack_half2(p2, p3));
-            }
-
-            // ---------------- O^T += V^T P'^T ----------------
-            const uint4 *vq4 = reinterpret_cast<const uint4 *>(vunit);
-            uint32_t vw[16];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint4 x = vq4[i * 32 + lane];
-                vw[4 * i + 0] = x.x;
-                vw[4 * i + 1] = x.y;
-                vw[4 * i + 2] = x.z;
-                vw[4 * i + 3] = x.w;
-            }
-            const uint4 *vsc = reinterpret_cast<const uint4 *>(vunit + kUnitQsBytes + c * 64);
-            uint32_t vd[16];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint4 x = vsc[i];
-                vd[4 * i + 0] = x.x;
-                vd[4 * i + 1] = x.y;
-                vd[4 * i + 2] = x.z;
-                vd[4 * i + 3] = x.w;
-            }
-#pragma unroll
-            for (int b = 0; b < 8; ++b) {
-                const __half2 s0 = u32_as_h2(vd[2 * b]);      // tokens 2c, 2c+1
-                const __half2 s1 = u32_as_h2(vd[2 * b + 1]);  // tokens 2c+8, 2c+9
-                uint32_t pbs[NQ][2];
-#pragma unroll
-                for (int qi = 0; qi < NQ; ++qi) {
-                    pbs[qi][0] = h2_as_u32(__hmul2(u32_as_h2(pb[qi][0]), s0));
-                    pbs[qi][1] = h2_as_u32(__hmul2(u32_as_h2(pb[qi][1]), s1));
-                }
-#pragma unroll
-                for (int m = 0; m < 2; ++m) {
-                    const uint32_t w = vw[2 * b + m];
-                    const uint32_t w8 = w >> 8;
-                    const uint32_t a[4] = {nib_lo(w), nib_hi16(w), nib_lo(w8), nib_hi16(w8)};
-#pragma unroll
-                    for (int qi = 0; qi < NQ; ++qi)
-                        mma_f16_16816(o[qi][b][m], a, pbs[qi][0], pbs[qi][1], o[qi][b][m]);
+                        vcorr[qi][b][0] *= al0;
+                        vcorr[qi][b][1] *= al1;
+                        vcorr[qi][b][2] *= al0;
+                        vcorr[qi][b][3] *= al1;
+                    }
                 }
             }
+#pragma unroll
+            for (int j = 0; j < GPW; ++j)
+                if (uv[j]) pv_unit(slot[j] + L::kTileBytes + (u * 2 + kvh) * kUnitBytes, pb[j]);
         }
+        // ---- release this step's slots; the last warp to release a slot refills it ----
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[s]);
-        if (producer && it + kFaStages < n_tiles) {
-            // Refill this stage once all 8 warps have released it.
-            if (!mbar_wait(&empty_bar[s], (it / kFaStages) & 1)) {
-                ok = false;
-                break;
+#pragma unroll
+        for (int j = 0; j < GPW; ++j) {
+            const int t = step * GPW + j;
+            if (t >= n_tiles) continue;
+            const int s = t % NSTAGE;
+            if (lane == 0) {
+                mbar_arrive(&empty_bar[s]);
+                if (atomicAdd(&rel_cnt[s], 1) == L::kWarps - 1) {
+                    rel_cnt[s] = 0;
+                    if (t + NSTAGE < n_tiles) {
+                        // every warp has arrived: this wait returns at once
+                        if (mbar_wait(&empty_bar[s], (t / NSTAGE) & 1))
+                            issue(t + NSTAGE);
+                        else
+                            atomicOr(p.err, 1u);
+                    }
+                }
             }
-            issue(it + kFaStages);
         }
     }
-    if (!ok) {
+    if (__syncthreads_or(!ok)) {
         if (lane == 0) atomicOr(p.err, 4u);
-        // Never leave the CTA with a bulk copy still writing into shared memory.
+        // Never leave the CTA with a bulk copy still writing into shared memory: wait
+        // (bounded) for the last slots of the ring.
         if (producer) {
-            const int first = n_tiles > kFaStages ? n_tiles - kFaStages : 0;
+            const int first = n_tiles > NSTAGE ? n_tiles - NSTAGE : 0;
             for (int it = first; it < n_tiles; ++it)
-                if (!mbar_wait(&full_bar[it % kFaStages], (it / kFaStages) & 1)) break;
+                if (!mbar_wait(&full_bar[it % NSTAGE], (it / NSTAGE) & 1)) break;
         }
     }
 
@@ -403,62 +655,78 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_decode_kernel(FaDecodeParams
                 l_run[qi][j] += __shfl_xor_sync(0xffffffffu, l_run[qi][j], off);
 
     __syncthreads();  // ring is free: every issued tile has been consumed
-    // red_o[warp][qi][head8][256]
+    // red_o[warp][qi][head8][kRedStride], in output units (o is in 2^-24 units and
+    // its hi-nibble rows carry an extra x16)
     float *red_o = reinterpret_cast<float *>(ring);
 #pragma unroll
     for (int qi = 0; qi < NQ; ++qi) {
-        float *base = red_o + (static_cast<size_t>(warp) * NQ + qi) * 8 * 256;
+        float *base = red_o + (static_cast<size_t>(warp) * NQ + qi) * 8 * L::kRedStride;
 #pragma unroll
         for (int b = 0; b < 8; ++b)
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
                 const int d_lo = 32 * b + 8 * m + g;
                 const int d_hi = d_lo + 16;
-                base[(2 * c) * 256 + d_lo] = o[qi][b][m][0];
-                base[(2 * c + 1) * 256 + d_lo] = o[qi][b][m][1];
-                base[(2 * c) * 256 + d_hi] = o[qi][b][m][2] * 0.0625f;
-                base[(2 * c + 1) * 256 + d_hi] = o[qi][b][m][3] * 0.0625f;
+                base[(2 * c) * L::kRedStride + d_lo] = (o[qi][b][m][0] + vcorr[qi][b][0]) * kTwo24;
+                base[(2 * c + 1) * L::kRedStride + d_lo] = (o[qi][b][m][1] + vcorr[qi][b][1]) * kTwo24;
+                base[(2 * c) * L::kRedStride + d_hi] = (o[qi][b][m][2] + vcorr[qi][b][2]) * (kTwo24 / 16.0f);
+                base[(2 * c + 1) * L::kRedStride + d_hi] = (o[qi][b][m][3] + vcorr[qi][b][3]) * (kTwo24 / 16.0f);
             }
         if (g == 0) {
             float *ml = red_ml + ((warp * NQ + qi) * 8) * 2;
-            ml[(2 * c) * 2 + 0] = m_run[qi][0];
+            ml[(2 * c) * 2 + 0] = m_run[qi][0] * kTwo24;  // back to score units
             ml[(2 * c) * 2 + 1] = l_run[qi][0];
-            ml[(2 * c + 1) * 2 + 0] = m_run[qi][1];
+            ml[(2 * c + 1) * 2 + 0] = m_run[qi][1] * kTwo24;
             ml[(2 * c + 1) * 2 + 1] = l_run[qi][1];
         }
     }
     __syncthreads();
 
-    // ---- combine the 4 warps of each KV head, write this split's partial ------
-    float *po = p.part_o + static_cast<size_t>(blockIdx.x) * NQ * 16 * 256;
-    float *pml = p.part_ml + static_cast<size_t>(blockIdx.x) * NQ * 16 * 2;
-    for (int i = threadIdx.x; i < NQ * 2 * 8 * 256; i += kFaConsumerWarps * 32) {
-        const int d = i & 255;
-        const int h8 = (i >> 8) & 7;
-        const int kh = (i >> 11) & 1;
-        const int qi = i >> 12;
+    // ---- combine the warps of each KV head, write this split's partial --------
+    // One thread per (query, head) turns the warps' running maxima into weights.
+    float *wts = reinterpret_cast<float *>(smem + L::kWtsOffset);
+    if (threadIdx.x < NQ * 16) {
+        const int qi = threadIdx.x >> 4, head = threadIdx.x & 15;
+        const int kh = head >> 3, h8 = head & 7;
         float M = -INFINITY;
 #pragma unroll
-        for (int w4 = 0; w4 < 4; ++w4) M = fmaxf(M, red_ml[(((kh * 4 + w4) * NQ + qi) * 8 + h8) * 2]);
-        float acc = 0.f, lsum = 0.f;
+        for (int wv = 0; wv < WPH; ++wv) M = fmaxf(M, red_ml[(((kh * WPH + wv) * NQ + qi) * 8 + h8) * 2]);
+        float lsum = 0.f;
+        float *wrow = wts + (qi * 16 + head) * (WPH + 2);
 #pragma unroll
-        for (int w4 = 0; w4 < 4; ++w4) {
-            const int wv = kh * 4 + w4;
-            const float mw = red_ml[((wv * NQ + qi) * 8 + h8) * 2];
-            const float wgt = (mw == -INFINITY) ? 0.f : ex2((mw - M) * p.c);
-            acc = fmaf(red_o[((static_cast<size_t>(wv) * NQ + qi) * 8 + h8) * 256 + d], wgt, acc);
-            lsum = fmaf(red_ml[((wv * NQ + qi) * 8 + h8) * 2 + 1], wgt, lsum);
+        for (int wv = 0; wv < WPH; ++wv) {
+            const float *ml = red_ml + (((kh * WPH + wv) * NQ + qi) * 8 + h8) * 2;
+            const float w = (ml[0] == -INFINITY) ? 0.f : ex2((ml[0] - M) * p.c);
+            wrow[wv] = w;
+            lsum = fmaf(ml[1], w, lsum);
         }
-        const int head = kh * 8 + h8;
+        wrow[WPH] = M;
+        wrow[WPH + 1] = lsum;
+    }
+    __syncthreads();
+    float *po = p.part_o + static_cast<size_t>(blockIdx.x) * NQ * 16 * 256;
+    float *pml = p.part_ml + static_cast<size_t>(blockIdx.x) * NQ * 16 * 2;
+    for (int i = threadIdx.x; i < NQ * 16 * 256; i += L::kThreads) {
+        const int d = i & 255;
+        const int head = (i >> 8) & 15;
+        const int qi = i >> 12;
+        const int kh = head >> 3, h8 = head & 7;
+        const float *wrow = wts + (qi * 16 + head) * (WPH + 2);
+        float acc = 0.f;
+#pragma unroll
+        for (int wv = 0; wv < WPH; ++wv)
+            acc = fmaf(red_o[((static_cast<size_t>(kh * WPH + wv) * NQ + qi) * 8 + h8) * L::kRedStride + d],
+                       wrow[wv], acc);
         po[(qi * 16 + head) * 256 + d] = acc;
         if (d == 0) {
-            pml[(qi * 16 + head) * 2 + 0] = M;
-            pml[(qi * 16 + head) * 2 + 1] = lsum;
+            pml[(qi * 16 + head) * 2 + 0] = wrow[WPH];
+            pml[(qi * 16 + head) * 2 + 1] = wrow[WPH + 1];
         }
     }
 }
 
-// out[row][d] = sigmoid(gate) * sum_s O_s exp2((m_s - M) c) / sum_s l_s exp2((m_s - M) c)
+// Split merge, launched right behind the decode kernel (programmatic dependent launch:
+// its CTAs are scheduled as soon as the decode grid starts and wait for it to finish).
 struct FaMergeParams {
     const float *part_o;
     const float *part_ml;
@@ -474,51 +742,12 @@ struct FaMergeParams {
     float *lse;
 };
 
-__global__ void __launch_bounds__(64) fa_merge_kernel(FaMergeParams p) {
-    extern __shared__ float wts[];  // [n_splits]
-    __shared__ float s_M, s_L;
-    const int row = blockIdx.x;
-    const int d = blockIdx.y * 64 + threadIdx.x;
-    if (threadIdx.x < 32) {
-        float M = -INFINITY;
-        for (int sidx = threadIdx.x; sidx < p.n_splits; sidx += 32)
-            M = fmaxf(M, p.part_ml[(static_cast<size_t>(sidx) * p.n_rows + row) * 2]);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-        float Ls = 0.f;
-        for (int sidx = threadIdx.x; sidx < p.n_splits; sidx += 32) {
-            const float mw = p.part_ml[(static_cast<size_t>(sidx) * p.n_rows + row) * 2];
-            const float w = (mw == -INFINITY) ? 0.f : ex2((mw - M) * p.c);
-            wts[sidx] = w;
-            Ls = fmaf(p.part_ml[(static_cast<size_t>(sidx) * p.n_rows + row) * 2 + 1], w, Ls);
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, off);
-        if (threadIdx.x == 0) {
-            s_M = M;
-            s_L = Ls;
-        }
-    }
-    __syncthreads();
-    float acc0 = 0.f, acc1 = 0.f;
-    int sidx = 0;
-    for (; sidx + 1 < p.n_splits; sidx += 2) {
-        acc0 = fmaf(p.part_o[(static_cast<size_t>(sidx) * p.n_rows + row) * 256 + d], wts[sidx], acc0);
-        acc1 = fmaf(p.part_o[(static_cast<size_t>(sidx + 1) * p.n_rows + row) * 256 + d], wts[sidx + 1],
-                    acc1);
-    }
-    if (sidx < p.n_splits)
-        acc0 = fmaf(p.part_o[(static_cast<size_t>(sidx) * p.n_rows + row) * 256 + d], wts[sidx], acc0);
-    const float Lsum = s_L;
-    float y = Lsum > 0.f ? (acc0 + acc1) / Lsum : 0.f;
-    if (p.gate) {
-        const int qi = row >> 4, h = row & 15;
-        const float gv = load_act(p.gate, qi * p.g_st + h * p.g_sh + d, p.gate_dtype);
-        y *= 1.0f / (1.0f + expf(-gv));
-    }
-    p.out[static_cast<size_t>(row) * 256 + d] = y;
-    if (p.lse && blockIdx.y == 0 && threadIdx.x == 0)
-        p.lse[row] = Lsum > 0.f ? s_M * p.scale + logf(Lsum) : -INFINITY;
+__global__ void __launch_bounds__(256) fa_merge_kernel(FaMergeParams p) {
+    __shared__ float red[8 * 34];
+    grid_dependency_wait();
+    launch_dependents();
+    merge_slice(p.part_o, p.part_ml, p.n_splits, p.n_rows, blockIdx.x, blockIdx.y, p.c, p.scale, p.gate,
+                p.gate_dtype, p.g_st, p.g_sh, p.out, p.lse, red, 8);
 }
 
 // Merge of normalised partials across GPUs: O = sum_p O_p e^(lse_p - L).
@@ -555,19 +784,19 @@ static size_t fa_ws_layout(int32_t n_splits, int32_t n_q, size_t *off_ml, size_t
 }
 
 extern "C" size_t sqmix_fa_workspace_bytes(int32_t n_splits, int32_t n_q) {
-    if (n_splits <= 0) n_splits = sqmix_device_sm_count(-1);
+    if (n_splits <= 0) n_splits = 2 * sqmix_device_sm_count(-1);  // covers every config
     if (n_q < 1) n_q = 1;
     size_t a, b;
     return fa_ws_layout(n_splits, n_q, &a, &b);
 }
 
-template <int NQ>
+template <int NQ, int WPH, int GPW, int NSTAGE, int MINB>
 static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st) {
+    using L = FaCfg<NQ, WPH, GPW, NSTAGE, MINB>;
+    auto kernel = fa_decode_kernel<NQ, WPH, GPW, NSTAGE, MINB>;
     static bool attr_set = false;
-    using L = FaSmem<NQ>;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(fa_decode_kernel<NQ>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
         if (e != cudaSuccess) return cuda_status(e, "fa_decode smem attribute");
         attr_set = true;
     }
@@ -579,21 +808,41 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st) {
     p.q_dtype = a->q_dtype;
     p.q_st = a->q_stride_tok;
     p.q_sh = a->q_stride_head;
-    p.k_cache = static_cast<const uint8_t *>(a->k_cache);
-    p.v_cache = static_cast<const uint8_t *>(a->v_cache);
+    p.k_cache = static_cast<uint8_t *>(const_cast<void *>(a->k_cache));
+    p.v_cache = static_cast<uint8_t *>(const_cast<void *>(a->v_cache));
     p.n_kv = a->n_kv;
     p.q_pos0 = a->q_pos0;
     p.capacity = a->capacity;
     p.c = a->scale * 1.4426950408889634f;
+    p.scale = a->scale;
     p.rope_n_rot = a->rope_n_rot;
     p.rope_pos_offset = a->rope_pos_offset;
     p.rope_theta_scale =
         a->rope_n_rot > 0 ? powf(a->rope_freq_base, -2.0f / static_cast<float>(a->rope_n_rot)) : 1.0f;
+    p.k_new = a->k_new;
+    p.v_new = a->v_new;
+    p.kv_dtype = a->kv_new_dtype;
+    p.k_new_st = a->k_new_stride_tok;
+    p.v_new_st = a->v_new_stride_tok;
+    p.n_new = a->n_new;
     p.part_o = reinterpret_cast<float *>(ws + off_o);
     p.part_ml = reinterpret_cast<float *>(ws + off_ml);
     p.err = reinterpret_cast<uint32_t *>(ws);
-    fa_decode_kernel<NQ><<<n_splits, kFaThreads, L::kTotal, st>>>(p);
-    cudaError_t e = cudaGetLastError();
+    p.overlap_prev = (a->flags & SQMIX_FA_OVERLAP_PREV) != 0;
+
+    // Both kernels are launched with programmatic stream serialisation so that each
+    // one's prologue overlaps the tail of the kernel before it (also inside CUDA graphs).
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_splits);
+    cfg.blockDim = dim3(L::kThreads);
+    cfg.dynamicSmemBytes = L::kTotal;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
     if (e != cudaSuccess) return cuda_status(e, "fa_decode launch");
 
     FaMergeParams mp;
@@ -609,9 +858,15 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st) {
     mp.scale = a->scale;
     mp.out = a->out;
     mp.lse = a->lse;
-    dim3 grid(NQ * 16, 4);
-    fa_merge_kernel<<<grid, 64, n_splits * sizeof(float), st>>>(mp);
-    return cuda_status(cudaGetLastError(), "fa_merge launch");
+    cudaLaunchConfig_t mcfg = {};
+    mcfg.gridDim = dim3(NQ * 16, 8);
+    mcfg.blockDim = dim3(256);
+    mcfg.dynamicSmemBytes = 0;
+    mcfg.stream = st;
+    mcfg.attrs = attr;
+    mcfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&mcfg, fa_merge_kernel, mp);
+    return cuda_status(e, "fa_merge launch");
 }
 
 extern "C" int sqmix_fa_decode(const sqmix_fa_args *a, sqmix_stream_t stream) {
@@ -629,10 +884,24 @@ extern "C" int sqmix_fa_decode(const sqmix_fa_args *a, sqmix_stream_t stream) {
     SQMIX_CHECK_ARG((reinterpret_cast<uintptr_t>(a->k_cache) & 15) == 0 &&
                         (reinterpret_cast<uintptr_t>(a->v_cache) & 15) == 0,
                     "fa_decode: caches must be 16-byte aligned");
+    SQMIX_CHECK_ARG((reinterpret_cast<uintptr_t>(a->workspace) & 15) == 0, "fa_decode: workspace alignment");
     SQMIX_CHECK_ARG(a->scale > 0.f, "fa_decode: scale must be positive");
-    SQMIX_CHECK_ARG(a->rope_n_rot >= 0 && a->rope_n_rot <= 256 && a->rope_n_rot % 2 == 0 &&
+    SQMIX_CHECK_ARG(a->rope_n_rot >= 0 && a->rope_n_rot <= 64 && a->rope_n_rot % 2 == 0 &&
                         (a->rope_n_rot == 0 || a->rope_freq_base > 0.f),
-                    "fa_decode: rope parameters");
+                    "fa_decode: rope parameters (n_rot <= 64)");
+    SQMIX_CHECK_ARG(a->n_new >= 0 && a->n_new <= a->n_q, "fa_decode: n_new=%d must be in [0, n_q]", a->n_new);
+    SQMIX_CHECK_ARG(a->n_new == 0 || (a->k_new && a->v_new && a->k_new_stride_tok >= 512 &&
+                                      a->v_new_stride_tok >= 512 &&
+                                      (a->kv_new_dtype == SQMIX_F32 || a->kv_new_dtype == SQMIX_F16 ||
+                                       a->kv_new_dtype == SQMIX_BF16)),
+                    "fa_decode: fused append needs k_new/v_new [n_new][2][256] and a float dtype");
+    // Kernel configurations (warps per KV head x groups per warp, ring stages):
+    //   1: n_q 1, 4 warps/head x 2 groups per step, 5 x 36.9 KB slots
+    //   2: n_q 2, 4 warps/head x 1 group per step, 5 x 36.9 KB slots
+    int cfg = a->config;
+    if (cfg == 0) cfg = a->n_q == 1 ? 1 : 2;
+    SQMIX_CHECK_ARG(cfg >= 1 && cfg <= 2 && (cfg == 2) == (a->n_q == 2),
+                    "fa_decode: config %d does not serve n_q=%d", a->config, a->n_q);
     int n_splits = a->n_splits > 0 ? a->n_splits : sqmix_device_sm_count(-1);
     SQMIX_CHECK_ARG(n_splits >= 1 && n_splits <= 4096, "fa_decode: n_splits=%d", n_splits);
     const size_t need = sqmix_fa_workspace_bytes(n_splits, a->n_q);
@@ -641,7 +910,26 @@ extern "C" int sqmix_fa_decode(const sqmix_fa_args *a, sqmix_stream_t stream) {
         return SQMIX_ENOSPC;
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    return a->n_q == 1 ? launch_fa<1>(a, n_splits, st) : launch_fa<2>(a, n_splits, st);
+    switch (cfg) {
+        case 1: return launch_fa<1, 4, 2, 5, 1>(a, n_splits, st);
+        default: return launch_fa<2, 4, 1, 5, 1>(a, n_splits, st);
+    }
+}
+
+extern "C" int sqmix_fa_status(void *workspace, sqmix_stream_t stream) {
+    SQMIX_CHECK_ARG(workspace, "fa_status: null workspace");
+    uint32_t bits = 0;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int rc = cuda_status(cudaMemcpyAsync(&bits, workspace, 4, cudaMemcpyDeviceToHost, st), "fa_status read");
+    if (rc == SQMIX_OK) rc = cuda_status(cudaStreamSynchronize(st), "fa_status sync");
+    if (rc != SQMIX_OK) return rc;
+    if (bits == 0) return SQMIX_OK;
+    const uint32_t zero = 0;
+    rc = cuda_status(cudaMemcpyAsync(workspace, &zero, 4, cudaMemcpyHostToDevice, st), "fa_status clear");
+    if (rc == SQMIX_OK) rc = cuda_status(cudaStreamSynchronize(st), "fa_status sync");
+    set_error("fa_decode device status bits 0x%x (1|2|4: a pipeline wait gave up, 8: n_kv > capacity, "
+              ")", bits);
+    return (bits & 8u) && !(bits & ~8u) ? SQMIX_ERANGE : SQMIX_ETIMEOUT;
 }
 
 extern "C" int sqmix_attn_merge_lse(int32_t n_parts, int32_t n_rows, const float *o_parts,

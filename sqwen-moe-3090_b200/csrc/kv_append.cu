@@ -38,62 +38,20 @@ __global__ void __launch_bounds__(1024) kv_append_kernel(AppendParams p) {
     const int64_t row = p.rows[t];
     if (row < 0 || row >= p.capacity) return;  // the host object validates rows
 
+    // One cos/sin table per token (the angles depend on the pair only, not on the head).
+    __shared__ float2 rope_tab[128];
+    if (p.rope_n_rot > 0 && wid == 0 && lane < (p.rope_n_rot >> 1))
+        rope_tab[lane] = rope_cos_sin(row + p.rope_pos_offset, p.rope_theta_scale, lane);
+    if (p.rope_n_rot > 64 && wid == 1 && lane + 32 < (p.rope_n_rot >> 1))
+        rope_tab[lane + 32] = rope_cos_sin(row + p.rope_pos_offset, p.rope_theta_scale, lane + 32);
+    if (p.rope_n_rot > 128 && wid >= 2 && wid < 4 && lane + 32 * wid < (p.rope_n_rot >> 1))
+        rope_tab[lane + 32 * wid] = rope_cos_sin(row + p.rope_pos_offset, p.rope_theta_scale, lane + 32 * wid);
+    __syncthreads();
+
     const void *src = is_v ? p.v : p.k;
     const int64_t base = t * (is_v ? p.v_st : p.k_st) + h * 256;
-    const int dim = b * 32 + lane;
-    float x = load_act(src, base + dim, p.dtype);
-
-    if (!is_v && dim < p.rope_n_rot) {
-        // IMROPE with equal text positions == NEOX pair rotation (i, i + n_rot/2).
-        // theta_i = pos * theta_scale^i by repeated multiplication, as ggml-cpu builds
-        // its rope cache (tests/attn_test.rs:173-193).
-        const int half = p.rope_n_rot >> 1;
-        const int i = dim < half ? dim : dim - half;
-        const float partner = load_act(src, base + (dim < half ? dim + half : dim - half), p.dtype);
-        float th = static_cast<float>(static_cast<int32_t>(row + p.rope_pos_offset));
-        for (int k = 0; k < i; ++k) th = __fmul_rn(th, p.rope_theta_scale);
-        float sn, cs;
-        sincosf(th, &sn, &cs);
-        if (dim < half)  // x0*c - x1*s
-            x = __fsub_rn(__fmul_rn(x, cs), __fmul_rn(partner, sn));
-        else             // x0*s + x1*c  (x is x1 here, partner is x0)
-            x = __fadd_rn(__fmul_rn(partner, sn), __fmul_rn(x, cs));
-    }
-
-    // quantize_row_q4_0: signed value of largest magnitude, first index on ties.
-    float amax = fabsf(x);
-    float vmax = x;
-    int idx = lane;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
-        const float ov = __shfl_xor_sync(0xffffffffu, vmax, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
-        if (oa > amax || (oa == amax && oi < idx)) {
-            amax = oa;
-            vmax = ov;
-            idx = oi;
-        }
-    }
-    // A block whose every |x| is 0 keeps max = 0 (ggml starts from amax = max = 0).
-    if (amax == 0.0f) vmax = 0.0f;
-    const float d = __fdiv_rn(vmax, -8.0f);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    int q = __float2int_rz(__fadd_rn(__fmul_rn(x, id), 8.5f));
-    q = min(15, max(0, q));
-    const int qhi = __shfl_down_sync(0xffffffffu, q, 16);
-
-    uint8_t *cache = is_v ? p.v_cache : p.k_cache;
-    if (lane < 16) {
-        const uint8_t byte = static_cast<uint8_t>(q | (qhi << 4));
-        const int64_t off = is_v ? v_qs_offset(row, h, b, lane) : k_qs_offset(row, h, b, lane);
-        cache[off] = byte;
-    }
-    if (lane == 0) {
-        const __half dh = __float2half_rn(d);
-        const int64_t off = is_v ? v_scale_offset(row, h, b) : k_scale_offset(row, h, b);
-        *reinterpret_cast<__half *>(cache + off) = dh;
-    }
+    const float x = kv_row_elem(src, base, b * 32 + lane, p.dtype, is_v ? 0 : p.rope_n_rot, rope_tab);
+    q4_0_store_block(x, lane, is_v ? p.v_cache : p.k_cache, row, h, b, is_v);
 }
 
 // tiled <-> ggml rows.  One thread per byte of a 288-byte row.

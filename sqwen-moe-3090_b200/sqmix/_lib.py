@@ -23,6 +23,7 @@ SQMIX_ERANGE = -6
 SQMIX_F32 = 0
 SQMIX_F16 = 1
 SQMIX_BF16 = 30
+SQMIX_FA_OVERLAP_PREV = 1
 
 ERROR_NAMES = {
     SQMIX_EINVAL: "SQMIX_EINVAL",
@@ -65,7 +66,9 @@ class FaArgs(ctypes.Structure):
         ("n_kv", c_void_p), ("q_pos0", c_void_p), ("n_q", c_int32), ("scale", c_float),
         ("rope_n_rot", c_int32), ("rope_freq_base", c_float), ("rope_pos_offset", c_int64),
         ("out", c_void_p), ("lse", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
-        ("n_splits", c_int32),
+        ("n_splits", c_int32), ("config", c_int32),
+        ("k_new", c_void_p), ("v_new", c_void_p), ("kv_new_dtype", c_int32), ("k_new_stride_tok", c_int64),
+        ("v_new_stride_tok", c_int64), ("n_new", c_int32), ("flags", c_int32),
     ]
 
 
@@ -91,6 +94,7 @@ _SIGNATURES = {
                                              c_int32, c_void_p]),
     "sqmix_fa_workspace_bytes": (c_size_t, [c_int32, c_int32]),
     "sqmix_fa_decode": (ctypes.c_int, [ctypes.POINTER(FaArgs), c_void_p]),
+    "sqmix_fa_status": (ctypes.c_int, [c_void_p, c_void_p]),
     "sqmix_attn_merge_lse": (ctypes.c_int, [c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                                             c_void_p, c_void_p]),
     "sqmix_gdn_decode": (ctypes.c_int, [ctypes.POINTER(GdnArgs), c_void_p]),

@@ -21,7 +21,7 @@ import math
 
 import torch
 
-from ._lib import (SQMIX_BF16, SQMIX_F16, SQMIX_F32, FaArgs, GdnArgs, KvAppendArgs, check, lib)
+from ._lib import (SQMIX_BF16, SQMIX_F16, SQMIX_F32, SQMIX_FA_OVERLAP_PREV, FaArgs, GdnArgs, KvAppendArgs, check, lib)
 
 HEAD_DIM = 256
 N_HEAD = 16
@@ -116,12 +116,17 @@ def flash_attn_ext(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor
                    scale: float = 1.0 / 16.0, rope_n_rot: int = 0, rope_freq_base: float = 1e7,
                    rope_pos_offset: int = 0, out: torch.Tensor | None = None,
                    lse: torch.Tensor | None = None,
-                   workspace: torch.Tensor | None = None, n_splits: int = 0,
-                   stream=None) -> torch.Tensor:
+                   workspace: torch.Tensor | None = None, n_splits: int = 0, config: int = 0,
+                   k_new: torch.Tensor | None = None, v_new: torch.Tensor | None = None,
+                   overlap_prev: bool = False, stream=None) -> torch.Tensor:
     """Split-KV attention of q [n_q][16][256] (n_q in {1, 2}) over the tiled q4_0 caches.
 
     n_kv and q_pos0 are device int64 scalars (CUDA-graph friendly).  Query t sees keys
     j <= q_pos0 + t and j < n_kv.  Returns out [n_q][16][256] f32 (gated if `gate`).
+    With k_new/v_new ([n_new][2][256], n_new <= n_q) the step's rows q_pos0 + t are
+    first quantised into the caches in the same launch (K rotated like Q).
+    overlap_prev sets SQMIX_FA_OVERLAP_PREV: n_kv, q_pos0 and the cache rows below
+    q_pos0 must then not be written by the kernel launched just before this call.
     """
     _require_cuda(q, k_cache, v_cache, n_kv, q_pos0, gate)
     if q.dim() == 2:
@@ -138,7 +143,21 @@ def flash_attn_ext(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor
             gate = gate.view(gate.shape[0], N_HEAD, HEAD_DIM)
         if gate.stride(-1) != 1:
             raise ValueError("gate rows must be contiguous along head_dim")
+    n_new = 0
+    if k_new is not None:
+        _require_cuda(k_new, v_new)
+        if k_new.dim() == 2:
+            k_new = k_new.view(k_new.shape[0], N_HEAD_KV, HEAD_DIM)
+        if v_new.dim() == 2:
+            v_new = v_new.view(v_new.shape[0], N_HEAD_KV, HEAD_DIM)
+        if (k_new.stride(-1) != 1 or k_new.stride(-2) != HEAD_DIM or v_new.stride(-1) != 1
+                or v_new.stride(-2) != HEAD_DIM or k_new.dtype != v_new.dtype):
+            raise ValueError("k_new/v_new must be [n_new][2][256] with contiguous heads and one dtype")
+        n_new = k_new.shape[0]
     a = FaArgs(
+        k_new=_ptr(k_new), v_new=_ptr(v_new), kv_new_dtype=_dt(k_new) if k_new is not None else 0,
+        k_new_stride_tok=k_new.stride(0) if k_new is not None else 0,
+        v_new_stride_tok=v_new.stride(0) if v_new is not None else 0, n_new=n_new,
         q=_ptr(q), q_dtype=_dt(q), q_stride_tok=q.stride(0), q_stride_head=q.stride(1),
         gate=_ptr(gate), gate_dtype=_dt(gate) if gate is not None else 0,
         gate_stride_tok=gate.stride(0) if gate is not None else 0,
@@ -146,9 +165,15 @@ def flash_attn_ext(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor
         k_cache=_ptr(k_cache), v_cache=_ptr(v_cache), capacity=int(capacity), n_kv=_ptr(n_kv),
         q_pos0=_ptr(q_pos0), n_q=n_q, scale=float(scale), rope_n_rot=int(rope_n_rot),
         rope_freq_base=float(rope_freq_base), rope_pos_offset=int(rope_pos_offset), out=_ptr(out), lse=_ptr(lse), workspace=_ptr(workspace),
-        workspace_bytes=workspace.numel(), n_splits=int(n_splits))
+        workspace_bytes=workspace.numel(), n_splits=int(n_splits), config=int(config),
+        flags=SQMIX_FA_OVERLAP_PREV if overlap_prev else 0)
     check(lib().sqmix_fa_decode(ctypes.byref(a), _stream(stream)), "flash_attn_ext")
     return out
+
+
+def fa_status(workspace: torch.Tensor, stream=None) -> None:
+    """Raise SqmixError if a bounded device-side wait in a flash_attn_ext call gave up."""
+    check(lib().sqmix_fa_status(_ptr(workspace), _stream(stream)), "flash_attn_ext device status")
 
 
 def attn_merge_lse(o_parts: torch.Tensor, lse_parts: torch.Tensor, gate: torch.Tensor | None = None,

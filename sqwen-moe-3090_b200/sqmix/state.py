@@ -129,20 +129,29 @@ class KvCache:
 
     # ---- layer ops --------------------------------------------------------------
     def append(self, slot: int, k_cur: torch.Tensor, v_cur: torch.Tensor, rope_n_rot: int = 0,
-               rope_freq_base: float = 1e7, stream=None) -> None:
+               rope_freq_base: float = 1e7, rope_pos_offset: int = 0, stream=None) -> None:
         """Write this step's K/V rows (after upload_step) into layer `slot`."""
         T = k_cur.shape[0]
-        ops.set_rows_q4_0(k_cur, v_cur, self.d_rows(T), self._k[slot], self._v[slot],
-                          self.capacity_alloc, rope_n_rot, rope_freq_base, stream)
+        ops.set_rows_q4_0(k_cur, v_cur, self.d_rows(T), self._k[slot], self._v[slot], self.capacity_alloc,
+                          rope_n_rot=rope_n_rot, rope_freq_base=rope_freq_base,
+                          rope_pos_offset=rope_pos_offset, stream=stream)
 
     def attention(self, slot: int, q: torch.Tensor, gate: torch.Tensor | None = None,
                   scale: float = 1.0 / 16.0, rope_n_rot: int = 0, rope_freq_base: float = 1e7,
-                  out=None, lse=None, workspace=None, n_splits: int = 0, stream=None) -> torch.Tensor:
-        """Causal attention of this step's queries over layer `slot` (after append)."""
+                  rope_pos_offset: int = 0, out=None, lse=None, workspace=None, n_splits: int = 0,
+                  k_new=None, v_new=None, overlap_prev: bool = False, stream=None) -> torch.Tensor:
+        """Causal attention of this step's queries over layer `slot`.
+
+        Either append first (KvCache.append), or pass the step's k_new/v_new to append
+        them inside the same launch.  overlap_prev (SQMIX_FA_OVERLAP_PREV) is safe when
+        the step's scalars were uploaded (upload_step) and the kernel just before this
+        call wrote no cache rows below the step start.
+        """
         return ops.flash_attn_ext(q, self._k[slot], self._v[slot], self.capacity_alloc, self.d_n_kv,
                                   self.d_q_pos0, gate=gate, scale=scale, rope_n_rot=rope_n_rot,
-                                  rope_freq_base=rope_freq_base, out=out, lse=lse, workspace=workspace,
-                                  n_splits=n_splits, stream=stream)
+                                  rope_freq_base=rope_freq_base, rope_pos_offset=rope_pos_offset, out=out,
+                                  lse=lse, workspace=workspace, n_splits=n_splits, k_new=k_new, v_new=v_new,
+                                  overlap_prev=overlap_prev, stream=stream)
 
     def export_rows(self, slot: int, which: str, row0: int, n_rows: int) -> torch.Tensor:
         cache = self._k[slot] if which == "k" else self._v[slot]

@@ -148,6 +148,54 @@ def run_fa(sq, q, kc, vc, cap, n_kv, q_pos0, gate=None, rope=0, n_splits=0, lse=
     return out.cpu().numpy(), (lse_t.cpu().numpy() if lse else None)
 
 
+def test_fa_decode_overlap_chain(sq, oracle):
+    """Back-to-back launches over several layers with SQMIX_FA_OVERLAP_PREV, eagerly and
+    replayed from a CUDA graph: each decode prefetches before the previous launch ends."""
+    rng = np.random.default_rng(21)
+    n_kv, n_layers = 3000, 3
+    cap = cap_for(n_kv)
+    layers = []
+    for _ in range(n_layers):
+        _, _, kq, vq, kd, vd = quantized_kv(oracle, rng, n_kv)
+        kc, vc = make_cache_from_rows(sq, kq, vq, cap)
+        q = rng.standard_normal((1, 16, 256)).astype(np.float32)
+        gate = rng.standard_normal((1, 16, 256)).astype(np.float32)
+        want = oracle.attn(q, kd, vd, gate, q_pos0=n_kv - 1, scale=1 / 16)
+        layers.append((kc, vc, torch.from_numpy(q).cuda(), torch.from_numpy(gate).cuda(), want))
+    d_nkv = torch.tensor([n_kv], dtype=torch.int64, device="cuda")
+    d_pos = torch.tensor([n_kv - 1], dtype=torch.int64, device="cuda")
+    ws = sq.new_fa_workspace(1, 0, "cuda")
+    outs = [torch.zeros((1, 16, 256), device="cuda") for _ in range(n_layers)]
+
+    def chain():
+        for (kc, vc, q, gate, _), out in zip(layers, outs):
+            sq.flash_attn_ext(q, kc, vc, cap, d_nkv, d_pos, gate=gate, out=out, workspace=ws,
+                              overlap_prev=True)
+
+    torch.cuda.synchronize()
+    chain()
+    torch.cuda.synchronize()
+    for (_, _, _, _, want), out in zip(layers, outs):
+        assert rel_err(out.cpu().numpy(), want) <= ATTN_TOL
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        chain()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        chain()
+    for _ in range(2):
+        for out in outs:
+            out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        for (_, _, _, _, want), out in zip(layers, outs):
+            assert rel_err(out.cpu().numpy(), want) <= ATTN_TOL
+    del graph
+    sq.fa_status(ws)
+
+
 def test_fa_decode_config0(sq, oracle):
     # BASELINE config 0: 1 query, 16/2 heads, d 256, 4096 q4_0 keys, scale 1/16, gate
     rng = np.random.default_rng(20)
@@ -402,3 +450,65 @@ def test_gdnstate_snapshot_restore_roundtrip(sq):
     with pytest.raises(sq.SqmixError):
         st.restore_gdn(blob[:-4])
     st.close()
+
+
+# ------------------------------------------------- fused append + attention ---
+
+@pytest.mark.parametrize("n_q,n_kv", [(1, 4096), (2, 1000), (2, 17), (1, 1), (2, 2)])
+def test_fa_decode_fused_append(sq, oracle, n_q, n_kv):
+    # one launch appends the step's rows (q4_0, RoPE on K) and attends over the cache:
+    # the rows must equal what the standalone append kernel writes, and the output the
+    # oracle's attention over the quantised cache
+    rng = np.random.default_rng(70 + n_kv + n_q)
+    cap = cap_for(n_kv)
+    q_pos0 = n_kv - n_q
+    k = rng.standard_normal((n_kv, 2, 256)).astype(np.float32)
+    v = rng.standard_normal((n_kv, 2, 256)).astype(np.float32)
+    kc, vc = sq.new_kv_cache(cap), sq.new_kv_cache(cap)
+    kc2, vc2 = sq.new_kv_cache(cap), sq.new_kv_cache(cap)
+    rows = torch.arange(n_kv, dtype=torch.int64, device="cuda")
+    kd_t, vd_t = torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda()
+    # reference path: everything through the standalone append
+    sq.set_rows_q4_0(kd_t, vd_t, rows, kc2, vc2, cap, rope_n_rot=64, rope_freq_base=1e7)
+    # fused path: history through the append kernel, the step's rows inside attention
+    if q_pos0 > 0:
+        sq.set_rows_q4_0(kd_t[:q_pos0], vd_t[:q_pos0], rows[:q_pos0], kc, vc, cap, rope_n_rot=64,
+                         rope_freq_base=1e7)
+    q = rng.standard_normal((n_q, 16, 256)).astype(np.float32)
+    gate = rng.standard_normal((n_q, 16, 256)).astype(np.float32)
+    ws = sq.new_fa_workspace(n_q)
+    out = sq.flash_attn_ext(torch.from_numpy(q).cuda(), kc, vc, cap,
+                            torch.tensor([n_kv], dtype=torch.int64, device="cuda"),
+                            torch.tensor([q_pos0], dtype=torch.int64, device="cuda"),
+                            gate=torch.from_numpy(gate).cuda(), rope_n_rot=64, rope_freq_base=1e7,
+                            k_new=kd_t[q_pos0:], v_new=vd_t[q_pos0:], workspace=ws)
+    torch.cuda.synchronize()
+    sq.fa_status(ws)
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    kq = sq.kv_convert_rows(kc, cap, "k", 0, n_kv).cpu().numpy()
+    vq = sq.kv_convert_rows(vc, cap, "v", 0, n_kv).cpu().numpy()
+    kd = oracle.q4_0_dequantize(kq, 512).reshape(n_kv, 2, 256)
+    vd = oracle.q4_0_dequantize(vq, 512).reshape(n_kv, 2, 256)
+    want = oracle.attn(oracle.rope_text(q, q_pos0, 1e7, 64), kd, vd, gate, q_pos0=q_pos0, scale=1 / 16)
+    assert rel_err(out.cpu().numpy(), want) <= ATTN_TOL
+
+
+def test_fa_status_clean_after_runs(sq, oracle):
+    rng = np.random.default_rng(80)
+    n_kv = 600
+    _, _, kq, vq, kd, vd = quantized_kv(oracle, rng, n_kv)
+    cap = cap_for(n_kv)
+    kc, vc = make_cache_from_rows(sq, kq, vq, cap)
+    ws = sq.new_fa_workspace(2)
+    q = torch.from_numpy(rng.standard_normal((2, 16, 256)).astype(np.float32)).cuda()
+    for _ in range(3):
+        sq.flash_attn_ext(q, kc, vc, cap, torch.tensor([n_kv], device="cuda"),
+                          torch.tensor([n_kv - 2], device="cuda"), workspace=ws)
+    sq.fa_status(ws)  # raises on any device-side error bit
+    # n_kv beyond the capacity is clamped on the device and reported, not read out of bounds
+    sq.flash_attn_ext(q, kc, vc, cap, torch.tensor([cap + 5000], device="cuda"),
+                      torch.tensor([n_kv - 2], device="cuda"), workspace=ws)
+    with pytest.raises(sq.SqmixError) as e:
+        sq.fa_status(ws)
+    assert e.value.code == sq.SQMIX_ERANGE
+    sq.fa_status(ws)  # cleared
