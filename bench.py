@@ -32,6 +32,9 @@ sys.path.insert(0, os.path.join(REPO, "sqwen-moe-3090_b200"))
 
 N_LAYERS = 10
 N_KV = 172032
+# DRAM bytes of one decode launch at N_KV keys, from one ncu capture
+# (profiles/fa_decode_kernel_172k.txt): 99.17 MB read + 3.46 MB written.
+FA_NCU_TRAFFIC = 102_630_000
 HEAD_DIM = 256
 N_HEAD = 16
 N_HEAD_KV = 2
@@ -374,9 +377,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                    "l2": "inputs larger than L2: 10 x 99 MB of KV cycled per step",
                    "cuda_graph": used_graph},
         "tokens_per_s": 1e6 / us_per_token,
-        "roofline": {"bound": "hbm", "kernel": "fa_decode_kernel (append + split-KV attention + merge, one launch)",
+        "roofline": {"bound": "hbm",
+                     "kernel": "fa_decode_kernel + fa_merge_kernel (split-KV attention, PDL-chained pair)",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": peak_kind, "traffic": None, "alg_bytes_per_launch": alg_bytes,
+                     "peak_kind": peak_kind, "traffic": FA_NCU_TRAFFIC if n_local == N_KV else None,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode launch "
+                                       "at 172032 keys (profiles/fa_decode_kernel_172k.txt)", "alg_bytes_per_launch": alg_bytes,
                      "launch_us": fa_us},
         "clocks": sampler.summary(),
         "gpu_launches": launches_per_step * args.steps,
