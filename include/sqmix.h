@@ -182,6 +182,26 @@ int sqmix_fa_decode(const sqmix_fa_args *args, sqmix_stream_t stream);
  * capacity.  Synchronises the stream. */
 int sqmix_fa_status(void *workspace, sqmix_stream_t stream);
 
+/* sqmix_fa_decode without a caller workspace (no reference counterpart: ggml_flash_attn_ext
+ * takes its scratch from ggml's graph allocator).  For callers that cannot allocate
+ * device memory at the call site, e.g. a callback inside a graph executor whose buffers
+ * are all planned before compute (cudaMalloc would synchronise the device and break a
+ * replayed CUDA graph's fixed addresses).  The split partials live in a file-scope
+ * __device__ array of SQMIX_FA_NOALLOC_SCRATCH_BYTES (the workspace of
+ * SQMIX_FA_NOALLOC_MAX_SPLITS splits at n_q 2, about 5 MiB); args->workspace and
+ * workspace_bytes are ignored.  Split counts above the maximum (explicit, or one per SM
+ * when n_splits is 0) are rejected with SQMIX_EINVAL / SQMIX_ENOSPC and a message.
+ * The array's status header must start at zero: static device storage is
+ * zero-initialised at module load, and the kernels write it only on a device-side wait
+ * failure, which this entry point does not read back.  The first call on each device
+ * does the setup (symbol lookup with that device current, possibly a module load, the
+ * kernel's shared-memory attribute) and should precede any stream capture.  All calls
+ * on a device share the one array: calls that overlap in time (other streams, other
+ * threads) race on it and must be serialised by the caller. */
+#define SQMIX_FA_NOALLOC_MAX_SPLITS 160
+#define SQMIX_FA_NOALLOC_SCRATCH_BYTES 5284096
+int sqmix_fa_decode_noalloc(const sqmix_fa_args *args, sqmix_stream_t stream);
+
 /* Merge n_parts normalised partial attentions (O_p, lse_p) over disjoint key sets
  * (split-KV across GPUs): out = sum_p O_p exp(lse_p - L) with L = log sum exp(lse_p),
  * then out *= sigmoid(gate) when gate != NULL.  o_parts [n_parts][n_rows][256],

@@ -34,6 +34,8 @@
 // one slot per step.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace sqmix {
@@ -940,4 +942,60 @@ extern "C" int sqmix_attn_merge_lse(int32_t n_parts, int32_t n_rows, const float
     merge_lse_kernel<<<n_rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         n_parts, n_rows, o_parts, lse_parts, gate, out, lse_out);
     return cuda_status(cudaGetLastError(), "merge_lse launch");
+}
+
+// ---------------------------------------------------------------------------
+// No-allocation variant: sqmix_fa_decode with a file-scope device scratch array in
+// place of the caller's workspace.  The array is sized for SQMIX_FA_NOALLOC_MAX_SPLITS
+// splits at n_q = 2; its 256-byte status header starts at zero because static device
+// storage is zero-initialised when the module is loaded.
+// ---------------------------------------------------------------------------
+static_assert(SQMIX_FA_NOALLOC_SCRATCH_BYTES ==
+                  kFaWsHeader + ((SQMIX_FA_NOALLOC_MAX_SPLITS * 2 * 16 * 2 * 4 + 255) / 256) * 256 +
+                      static_cast<size_t>(SQMIX_FA_NOALLOC_MAX_SPLITS) * 2 * 16 * 256 * 4,
+              "no-alloc scratch size must equal the workspace of the maximum split count at n_q 2");
+static __device__ __align__(256) uint8_t g_fa_noalloc_scratch[SQMIX_FA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_scratch[kNoAllocMaxDevices] = {};
+}  // namespace
+
+extern "C" int sqmix_fa_decode_noalloc(const sqmix_fa_args *a, sqmix_stream_t stream) {
+    SQMIX_CHECK_ARG(a != nullptr, "fa_decode_noalloc: null args");
+    // Explicit split counts are checked before any CUDA call.
+    SQMIX_CHECK_ARG(a->n_splits <= SQMIX_FA_NOALLOC_MAX_SPLITS,
+                    "fa_decode_noalloc: n_splits=%d exceeds the static scratch (max %d splits)", a->n_splits,
+                    SQMIX_FA_NOALLOC_MAX_SPLITS);
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e, "fa_decode_noalloc: current device");
+    SQMIX_CHECK_ARG(dev >= 0 && dev < kNoAllocMaxDevices, "fa_decode_noalloc: device %d", dev);
+    const int n_splits = a->n_splits > 0 ? a->n_splits : sqmix_device_sm_count(dev);
+    if (n_splits > SQMIX_FA_NOALLOC_MAX_SPLITS) {
+        set_error("fa_decode_noalloc: %d splits (one per SM) exceed the static scratch (max %d); pass "
+                  "n_splits <= %d",
+                  n_splits, SQMIX_FA_NOALLOC_MAX_SPLITS, SQMIX_FA_NOALLOC_MAX_SPLITS);
+        return SQMIX_ENOSPC;
+    }
+    void *scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_scratch[dev]) {
+            // Once per device, with that device current: resolves (and, with lazy module
+            // loading, loads) the array.
+            e = cudaGetSymbolAddress(&g_noalloc_scratch[dev], g_fa_noalloc_scratch);
+            if (e != cudaSuccess) {
+                g_noalloc_scratch[dev] = nullptr;
+                return cuda_status(e, "fa_decode_noalloc: scratch symbol address");
+            }
+        }
+        scratch = g_noalloc_scratch[dev];
+    }
+    sqmix_fa_args b = *a;
+    b.workspace = scratch;
+    b.workspace_bytes = SQMIX_FA_NOALLOC_SCRATCH_BYTES;
+    b.n_splits = n_splits;
+    return sqmix_fa_decode(&b, stream);
 }
