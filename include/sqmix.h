@@ -182,6 +182,17 @@ int sqmix_fa_decode(const sqmix_fa_args *args, sqmix_stream_t stream);
  * capacity.  Synchronises the stream. */
 int sqmix_fa_status(void *workspace, sqmix_stream_t stream);
 
+/* Prefill attention on the tcgen05 tensor cores: the same arguments as sqmix_fa_decode
+ * for n_q = T in 1..4096 query tokens (ggml_flash_attn_ext of a prefill chunk,
+ * attn.rs:238-249, causal mask graph.rs:553-559).  The step's rows must already be in
+ * the cache (sqmix_kv_append_q4_0; n_new must be 0).  n_splits = number of persistent
+ * CTAs (0 = one per SM); config and flags are ignored.  Launches a setup, a main and a
+ * merge kernel.  The workspace (sqmix_fa_prefill_workspace_bytes, 256-byte aligned)
+ * needs no initialisation; its first word holds device status bits as for decode
+ * (read with sqmix_fa_status). */
+size_t sqmix_fa_prefill_workspace_bytes(int32_t n_q, int32_t n_ctas);
+int sqmix_fa_prefill(const sqmix_fa_args *args, sqmix_stream_t stream);
+
 /* sqmix_fa_decode without a caller workspace (no reference counterpart: ggml_flash_attn_ext
  * takes its scratch from ggml's graph allocator).  For callers that cannot allocate
  * device memory at the call site, e.g. a callback inside a graph executor whose buffers

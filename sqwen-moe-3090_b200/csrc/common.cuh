@@ -124,6 +124,13 @@ __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) {
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) {
     return *reinterpret_cast<__half2 *>(&u);
 }
+// 2^x (MUFU approximation; 2^-inf = 0)
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return h2_as_u32(__floats2half2_rn(lo, hi));
 }

@@ -96,11 +96,6 @@ struct FaCfg {
     static constexpr int kTotal = kWtsOffset + NQ * 16 * (WPH + 2) * 4;
 };
 
-__device__ __forceinline__ float ex2(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
 
 // Nibble pairs as f16 subnormals.  With w = 4 bytes {b0, b1, b2, b3}:
 //   sub_lo(w) = {b0 & 15, b2 & 15} * 2^-24          (bit pattern = the nibble)

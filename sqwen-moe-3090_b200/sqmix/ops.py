@@ -111,23 +111,9 @@ def new_fa_workspace(n_q: int = 2, n_splits: int = 0, device="cuda") -> torch.Te
     return torch.zeros(fa_workspace_bytes(n_q, n_splits), dtype=torch.uint8, device=device)
 
 
-def flash_attn_ext(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, capacity: int,
-                   n_kv: torch.Tensor, q_pos0: torch.Tensor, gate: torch.Tensor | None = None,
-                   scale: float = 1.0 / 16.0, rope_n_rot: int = 0, rope_freq_base: float = 1e7,
-                   rope_pos_offset: int = 0, out: torch.Tensor | None = None,
-                   lse: torch.Tensor | None = None,
-                   workspace: torch.Tensor | None = None, n_splits: int = 0, config: int = 0,
-                   k_new: torch.Tensor | None = None, v_new: torch.Tensor | None = None,
-                   overlap_prev: bool = False, stream=None) -> torch.Tensor:
-    """Split-KV attention of q [n_q][16][256] (n_q in {1, 2}) over the tiled q4_0 caches.
-
-    n_kv and q_pos0 are device int64 scalars (CUDA-graph friendly).  Query t sees keys
-    j <= q_pos0 + t and j < n_kv.  Returns out [n_q][16][256] f32 (gated if `gate`).
-    With k_new/v_new ([n_new][2][256], n_new <= n_q) the step's rows q_pos0 + t are
-    first quantised into the caches in the same launch (K rotated like Q).
-    overlap_prev sets SQMIX_FA_OVERLAP_PREV: n_kv, q_pos0 and the cache rows below
-    q_pos0 must then not be written by the kernel launched just before this call.
-    """
+def _fa_args(q, k_cache, v_cache, capacity, n_kv, q_pos0, gate, scale, rope_n_rot, rope_freq_base,
+             rope_pos_offset, out, lse, workspace, n_splits, config, k_new, v_new, flags):
+    """Validate tensors and build the sqmix_fa_args struct shared by decode and prefill."""
     _require_cuda(q, k_cache, v_cache, n_kv, q_pos0, gate)
     if q.dim() == 2:
         q = q.view(q.shape[0], N_HEAD, HEAD_DIM)
@@ -136,8 +122,6 @@ def flash_attn_ext(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor
         raise ValueError("q rows must be contiguous along head_dim")
     if out is None:
         out = torch.empty((n_q, N_HEAD, HEAD_DIM), dtype=torch.float32, device=q.device)
-    if workspace is None:
-        workspace = new_fa_workspace(n_q, n_splits, q.device)
     if gate is not None:
         if gate.dim() == 2:
             gate = gate.view(gate.shape[0], N_HEAD, HEAD_DIM)
@@ -164,10 +148,61 @@ def flash_attn_ext(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor
         gate_stride_head=gate.stride(1) if gate is not None else 0,
         k_cache=_ptr(k_cache), v_cache=_ptr(v_cache), capacity=int(capacity), n_kv=_ptr(n_kv),
         q_pos0=_ptr(q_pos0), n_q=n_q, scale=float(scale), rope_n_rot=int(rope_n_rot),
-        rope_freq_base=float(rope_freq_base), rope_pos_offset=int(rope_pos_offset), out=_ptr(out), lse=_ptr(lse), workspace=_ptr(workspace),
-        workspace_bytes=workspace.numel(), n_splits=int(n_splits), config=int(config),
-        flags=SQMIX_FA_OVERLAP_PREV if overlap_prev else 0)
+        rope_freq_base=float(rope_freq_base), rope_pos_offset=int(rope_pos_offset), out=_ptr(out),
+        lse=_ptr(lse), workspace=_ptr(workspace), workspace_bytes=workspace.numel(), n_splits=int(n_splits),
+        config=int(config), flags=int(flags))
+    return a, out
+
+
+def flash_attn_ext(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, capacity: int,
+                   n_kv: torch.Tensor, q_pos0: torch.Tensor, gate: torch.Tensor | None = None,
+                   scale: float = 1.0 / 16.0, rope_n_rot: int = 0, rope_freq_base: float = 1e7,
+                   rope_pos_offset: int = 0, out: torch.Tensor | None = None,
+                   lse: torch.Tensor | None = None,
+                   workspace: torch.Tensor | None = None, n_splits: int = 0, config: int = 0,
+                   k_new: torch.Tensor | None = None, v_new: torch.Tensor | None = None,
+                   overlap_prev: bool = False, stream=None) -> torch.Tensor:
+    """Split-KV attention of q [n_q][16][256] (n_q in {1, 2}) over the tiled q4_0 caches.
+
+    n_kv and q_pos0 are device int64 scalars (CUDA-graph friendly).  Query t sees keys
+    j <= q_pos0 + t and j < n_kv.  Returns out [n_q][16][256] f32 (gated if `gate`).
+    With k_new/v_new ([n_new][2][256], n_new <= n_q) the step's rows q_pos0 + t are
+    first quantised into the caches in the same launch (K rotated like Q).
+    overlap_prev sets SQMIX_FA_OVERLAP_PREV: n_kv, q_pos0 and the cache rows below
+    q_pos0 must then not be written by the kernel launched just before this call.
+    """
+    if workspace is None:
+        workspace = new_fa_workspace(q.shape[0], n_splits, q.device)
+    a, out = _fa_args(q, k_cache, v_cache, capacity, n_kv, q_pos0, gate, scale, rope_n_rot, rope_freq_base,
+                      rope_pos_offset, out, lse, workspace, n_splits, config, k_new, v_new,
+                      SQMIX_FA_OVERLAP_PREV if overlap_prev else 0)
     check(lib().sqmix_fa_decode(ctypes.byref(a), _stream(stream)), "flash_attn_ext")
+    return out
+
+
+def fa_prefill_workspace_bytes(n_q: int, n_ctas: int = 0) -> int:
+    return int(lib().sqmix_fa_prefill_workspace_bytes(int(n_q), int(n_ctas)))
+
+
+def new_fa_prefill_workspace(n_q: int, n_ctas: int = 0, device="cuda") -> torch.Tensor:
+    """Scratch for flash_attn_prefill (item table and split partials); needs no init."""
+    return torch.zeros(fa_prefill_workspace_bytes(n_q, n_ctas), dtype=torch.uint8, device=device)
+
+
+def flash_attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, capacity: int,
+                       n_kv: torch.Tensor, q_pos0: torch.Tensor, gate: torch.Tensor | None = None,
+                       scale: float = 1.0 / 16.0, rope_n_rot: int = 0, rope_freq_base: float = 1e7,
+                       rope_pos_offset: int = 0, out: torch.Tensor | None = None,
+                       lse: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                       n_ctas: int = 0, stream=None) -> torch.Tensor:
+    """Causal attention of T query tokens q [T][16][256] over the tiled q4_0 caches on the
+    tensor cores (the step's rows must already be appended).  Same semantics as
+    flash_attn_ext: query t sees keys j <= q_pos0 + t and j < n_kv."""
+    if workspace is None:
+        workspace = new_fa_prefill_workspace(q.shape[0], n_ctas, q.device)
+    a, out = _fa_args(q, k_cache, v_cache, capacity, n_kv, q_pos0, gate, scale, rope_n_rot, rope_freq_base,
+                      rope_pos_offset, out, lse, workspace, n_ctas, 0, None, None, 0)
+    check(lib().sqmix_fa_prefill(ctypes.byref(a), _stream(stream)), "flash_attn_prefill")
     return out
 
 
