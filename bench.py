@@ -53,6 +53,16 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16 TFLOP/s: the burst figure (a kernel timed alone) and its source."""
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled during the timed region."""
 
@@ -391,6 +401,69 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     return res
 
 
+PF_PREFIX = 32768  # config 2: pp512 and pp2048 appended onto a 32768-token q4_0 prefix
+
+
+def bench_prefill(steps: int, warmup: int):
+    """Config 2: one full-attention layer's prefill chunk of T tokens (append + attention
+    + gate) after a 32768-token q4_0 prefix; tokens/s and tensor-core roofline."""
+    import torch
+
+    import sqmix
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    res = {}
+    peak, peak_kind = tensor_peak()
+    for T in (512, 2048):
+        n_kv = PF_PREFIX + T
+        cap = (n_kv + 255) // 256 * 256
+        kc, vc = sqmix.new_kv_cache(cap), sqmix.new_kv_cache(cap)
+        for a in range(0, PF_PREFIX, 8192):
+            sqmix.set_rows_q4_0(torch.randn((8192, 2, 256), generator=g, device=dev),
+                                torch.randn((8192, 2, 256), generator=g, device=dev),
+                                torch.arange(a, a + 8192, device=dev), kc, vc, cap, rope_n_rot=N_ROT,
+                                rope_freq_base=FREQ_BASE)
+        q = torch.randn((T, N_HEAD, HEAD_DIM), generator=g, device=dev).to(torch.bfloat16)
+        gate = torch.randn((T, N_HEAD, HEAD_DIM), generator=g, device=dev).to(torch.bfloat16)
+        k_new = torch.randn((T, 2, 256), generator=g, device=dev)
+        v_new = torch.randn((T, 2, 256), generator=g, device=dev)
+        rows = torch.arange(PF_PREFIX, n_kv, device=dev)
+        d = torch.tensor([n_kv, PF_PREFIX], dtype=torch.int64, device=dev)
+        ws = sqmix.new_fa_prefill_workspace(T)
+        out = torch.empty((T, N_HEAD, HEAD_DIM), device=dev)
+
+        def step():
+            sqmix.set_rows_q4_0(k_new, v_new, rows, kc, vc, cap, rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE)
+            sqmix.flash_attn_prefill(q, kc, vc, cap, d[0:1], d[1:2], gate=gate, rope_n_rot=N_ROT,
+                                     rope_freq_base=FREQ_BASE, out=out, workspace=ws)
+
+        for _ in range(max(warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(3, steps)
+        e0.record()
+        for _ in range(reps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        sqmix.fa_status(ws)
+        flops = 16384 * sum(PF_PREFIX + t + 1 for t in range(T))
+        tflops = flops / us / 1e6
+        res[f"pp{T}"] = {"us": us, "tok_s": T / us * 1e6, "tflops": tflops,
+                         "frac_of_measured_bf16_peak": tflops / peak if peak else None,
+                         "flops": flops}
+        del kc, vc, ws
+    res["config"] = "config2: 1 layer, prefix 32768 q4_0 keys, T new tokens appended (q4_0, RoPE) then " \
+                    "causal GQA attention with sigmoid gate; Q bf16; flops = 4*256*16*sum_t(prefix+t+1)"
+    res["peak_tflops"] = peak
+    res["peak_kind"] = peak_kind
+    return res
+
+
 def run_profile_case(case: str):
     """Small fixed workloads for ncu captures (one kernel, a few launches, ~0.3 GB)."""
     import torch
@@ -414,6 +487,21 @@ def run_profile_case(case: str):
         for _ in range(3):
             sqmix.flash_attn_ext(q, kc, vc, N_KV, d[0:1], d[1:2], gate=gate, rope_n_rot=N_ROT,
                                  rope_freq_base=FREQ_BASE, workspace=ws)
+    elif case == "pf":
+        P, T = 8192, 512
+        n_kv = P + T
+        cap = (n_kv + 255) // 256 * 256
+        kc, vc = sqmix.new_kv_cache(cap), sqmix.new_kv_cache(cap)
+        sqmix.set_rows_q4_0(torch.randn((n_kv, 2, 256), generator=g, device=dev),
+                            torch.randn((n_kv, 2, 256), generator=g, device=dev),
+                            torch.arange(n_kv, device=dev), kc, vc, cap, rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE)
+        q = torch.randn((T, N_HEAD, HEAD_DIM), generator=g, device=dev).to(torch.bfloat16)
+        gate = torch.randn((T, N_HEAD, HEAD_DIM), generator=g, device=dev).to(torch.bfloat16)
+        d = torch.tensor([n_kv, P], dtype=torch.int64, device=dev)
+        ws = sqmix.new_fa_prefill_workspace(T)
+        for _ in range(3):
+            sqmix.flash_attn_prefill(q, kc, vc, cap, d[0:1], d[1:2], gate=gate, rope_n_rot=N_ROT,
+                                     rope_freq_base=FREQ_BASE, workspace=ws)
     elif case == "gdn":
         S = torch.randn((1, 1, 32, 128, 128), generator=g, device=dev) * 0.02
         q = torch.nn.functional.normalize(torch.randn((1, 1, 16, 128), generator=g, device=dev), dim=-1)
@@ -437,7 +525,8 @@ def main():
     ap.add_argument("--impl", default="sqmix", choices=["sqmix", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | gdn) and exit")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill measurement")
+    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn) and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)
@@ -466,6 +555,8 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline()
     res = run_gpu(args, rank, world, local_rank)
+    if res is not None and world == 1 and not args.no_prefill:
+        res["prefill"] = bench_prefill(args.steps, args.warmup)
     if res is not None:
         if cpu is not None:
             res["cpu_baseline"] = cpu
