@@ -16,14 +16,18 @@
 //
 // One CTA (13 warps):
 //   warp 0      TMEM allocation; lane 0 issues the MMAs: S = Q K^T (M 128, N 64,
-//               K 256) into one of two TMEM S buffers, then O += P V (M 128, N 256,
-//               K 64) into the TMEM O accumulator;
+//               K 256; Q read from tensor memory) into one of two TMEM S buffers,
+//               then O += P V (M 128, N 256, K 64) into the TMEM O accumulator, in
+//               the order S(0) S(1) PV(0) S(2) PV(1) ... so that the tensor core
+//               computes the next S while the softmax warps work on the current one;
 //   warps 1-4   softmax: thread = row; reads S from TMEM, online softmax in the
 //               log2 domain with lazy rescaling (O is rescaled only when the row
 //               maximum grows by more than 2^8), writes P (f16) to shared memory,
 //               and at the end of an item reads O and writes the partials;
-//   warps 5-12  producers: load Q (RoPE, f16) and dequantise K and V tiles from q4_0
-//               into 128-byte-swizzled shared memory, two stages.
+//   warps 5-12  producers: build Q (RoPE, f16) through a shared staging buffer into
+//               tensor memory, and dequantise K and V tiles from q4_0 into
+//               128-byte-swizzled shared memory (three stages; the raw q4_0 of the
+//               next tile is loaded while the current one is converted).
 // The contraction order of the head dimension is permuted so that each 16-byte
 // chunk of the tiled cache dequantises into one 16-byte shared-memory chunk; Q uses
 // the same permutation (K side) and the merge undoes the V-side one.
@@ -45,14 +49,14 @@ constexpr int kProdThreads = 256;
 constexpr int kMaxMtiles = 512;  // T <= 4096
 
 // shared memory (offsets from a 1024-byte aligned base)
-constexpr uint32_t kQOff = 0;           // 4 regions (64 contraction dims) x 128 rows x 128 B
-constexpr uint32_t kQRegion = 16384;
-constexpr uint32_t kStageOff = 65536;   // 2 stages: K (4 x 8 KB regions) | V (4 x 8 KB)
+constexpr int kNStage = 3;
+constexpr uint32_t kStageOff = 0;       // 3 stages: K (4 x 8 KB regions) | V (4 x 8 KB)
 constexpr uint32_t kStageBytes = 65536;
 constexpr uint32_t kVInStage = 32768;
 constexpr uint32_t kKvRegion = 8192;    // 64 keys x 128 B
-constexpr uint32_t kPOff = 196608;      // 2 P buffers: 128 rows x 64 keys f16
-constexpr uint32_t kPBytes = 16384;
+constexpr uint32_t kPOff = 196608;      // 2 P buffers: 128 rows x 64 keys f16; at the
+constexpr uint32_t kPBytes = 16384;     // start of an item, the Q staging buffer
+constexpr uint32_t kRopeOff = 2 * kStageBytes + kVInStage;  // RoPE table while Q is built
 constexpr uint32_t kBarOff = 229376;
 constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
 
@@ -60,6 +64,7 @@ constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOCol = 0;    // O: 256 columns f32
 constexpr uint32_t kSCol = 256;  // S buffers: 2 x 64 columns
+constexpr uint32_t kQCol = 384;  // Q: 128 columns (256 f16 per row, two per column)
 
 constexpr float kRescaleLog2 = 8.0f;
 
@@ -212,8 +217,8 @@ __device__ __forceinline__ int v_real_dim(int v) {
 }
 
 struct SmemCtl {
-    uint64_t kv_full[2];
-    uint64_t pv_done[2];
+    uint64_t kv_full[kNStage];
+    uint64_t pv_done[kNStage];
     uint64_t s_full[2];
     uint64_t s_free[2];
     uint64_t p_full[2];
@@ -223,11 +228,18 @@ struct SmemCtl {
     uint64_t item_empty[2];
     uint64_t final_bar;
     uint64_t rope_bar;
+    uint64_t qs_bar;
     int4 item[2];
     uint32_t tmem_base;
     int abort_flag;
 };
 static_assert(sizeof(SmemCtl) <= 256, "control block");
+
+// Raw q4_0 of one 64-key tile for one producer thread (2 K jobs + 2 V jobs).
+struct RawTile {
+    uint4 kn[2], vn[2], vs[2];
+    uint2 ks[2];
+};
 
 __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -241,9 +253,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < kNStage; ++s) {
             mbar_init(&ctl->kv_full[s], kProdThreads);
             mbar_init(&ctl->pv_done[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
             mbar_init(&ctl->s_full[s], 1);
             mbar_init(&ctl->s_free[s], kPfRows);
             mbar_init(&ctl->p_full[s], kPfRows);
@@ -254,6 +268,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
         mbar_init(&ctl->o_free, kPfRows);
         mbar_init(&ctl->final_bar, 1);
         mbar_init(&ctl->rope_bar, kProdThreads);
+        mbar_init(&ctl->qs_bar, kProdThreads);
         ctl->abort_flag = 0;
         fence_mbar_init();
     }
@@ -296,6 +311,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
         mbar_arrive(&ctl->item_empty[slot]);
         return it.x >= 0;
     };
+    // parity of the completion of tile jj on a barrier used once per kNStage tiles
+    auto stage_parity = [](int jj) -> uint32_t { return static_cast<uint32_t>(jj / kNStage) & 1u; };
 
     const uint32_t idesc_s = tc::idesc_f16_f32(128, kPfKeys, 0, 0);
     const uint32_t idesc_pv = tc::idesc_f16_f32(128, 256, 0, 1);
@@ -305,49 +322,49 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
         if (lane == 0) {
             int j = 0;
             bool ok = true;
+            auto issue_s = [&](int jj) -> bool {
+                const int sb = jj & 1, st = jj % kNStage;
+                if (!wait_or_abort(&ctl->kv_full[st], stage_parity(jj), abort_flag, err, 1u)) return false;
+                if (jj >= 2 && !wait_or_abort(&ctl->s_free[sb], ((jj - 2) >> 1) & 1, abort_flag, err, 1u))
+                    return false;
+                tc::fence_after();
+#pragma unroll
+                for (int ks = 0; ks < 16; ++ks) {
+                    const uint64_t b = tc::desc_sw128(
+                        base_s + kStageOff + st * kStageBytes + (ks >> 2) * kKvRegion + (ks & 3) * 32, 16, 1024);
+                    tc::mma_ts(tmem + kSCol + sb * kPfKeys, tmem + kQCol + ks * 8, b, idesc_s, ks > 0 ? 1u : 0u);
+                }
+                tc::commit(&ctl->s_full[sb]);
+                return true;
+            };
             auto issue_pv = [&](int jj, bool first) -> bool {
-                const int bb = jj & 1;
+                const int bb = jj & 1, st = jj % kNStage;
                 if (!wait_or_abort(&ctl->p_full[bb], (jj >> 1) & 1, abort_flag, err, 1u)) return false;
                 tc::fence_after();
 #pragma unroll
                 for (int ks = 0; ks < kPfKeys / 16; ++ks) {
                     const uint64_t a = tc::desc_sw128(base_s + kPOff + bb * kPBytes + ks * 32, 16, 1024);
                     const uint64_t b =
-                        tc::desc_sw128(base_s + kStageOff + bb * kStageBytes + kVInStage + ks * 2048, kKvRegion, 1024);
+                        tc::desc_sw128(base_s + kStageOff + st * kStageBytes + kVInStage + ks * 2048, kKvRegion, 1024);
                     tc::mma_ss(tmem + kOCol, a, b, idesc_pv, (!first || ks > 0) ? 1u : 0u);
                 }
-                tc::commit(&ctl->pv_done[bb]);
+                tc::commit(&ctl->pv_done[st]);
                 return true;
             };
             for (int iter = 0; ok; ++iter) {
                 int4 it;
                 if (!get_item(iter, it, false)) break;
-                const int kt0 = it.y, kt1 = it.z;
+                const int n = it.z - it.y;
                 if (!wait_or_abort(&ctl->q_full, iter & 1, abort_flag, err, 1u)) break;
                 if (iter > 0 && !wait_or_abort(&ctl->o_free, (iter - 1) & 1, abort_flag, err, 1u)) break;
                 tc::fence_after();
-                const int jfirst = j;
-                for (int kt = kt0; kt < kt1; ++kt, ++j) {
-                    const int s = j & 1;
-                    if (!wait_or_abort(&ctl->kv_full[s], (j >> 1) & 1, abort_flag, err, 1u)) { ok = false; break; }
-                    if (j >= 2 && !wait_or_abort(&ctl->s_free[s], ((j - 2) >> 1) & 1, abort_flag, err, 1u)) {
-                        ok = false;
-                        break;
-                    }
-                    tc::fence_after();
-#pragma unroll
-                    for (int ks = 0; ks < 16; ++ks) {
-                        const uint32_t koff = (ks >> 2) * kQRegion + (ks & 3) * 32;
-                        const uint64_t a = tc::desc_sw128(base_s + kQOff + koff, 16, 1024);
-                        const uint64_t b = tc::desc_sw128(
-                            base_s + kStageOff + s * kStageBytes + (ks >> 2) * kKvRegion + (ks & 3) * 32, 16, 1024);
-                        tc::mma_ss(tmem + kSCol + s * kPfKeys, a, b, idesc_s, ks > 0 ? 1u : 0u);
-                    }
-                    tc::commit(&ctl->s_full[s]);
-                    if (j > jfirst && !issue_pv(j - 1, j - 1 == jfirst)) { ok = false; break; }
+                const int jf = j;
+                if (!issue_s(jf)) break;
+                for (int t = 0; t < n; ++t) {
+                    if (t + 1 < n && !issue_s(jf + t + 1)) { ok = false; break; }
+                    if (!issue_pv(jf + t, t == 0)) { ok = false; break; }
                 }
-                if (!ok) break;
-                if (j > jfirst && !issue_pv(j - 1, j - 1 == jfirst)) break;
+                j = jf + n;
             }
             // drain: every MMA issued so far completes before TMEM is released
             tc::commit(&ctl->final_bar);
@@ -385,25 +402,31 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                 tc::fence_before();
                 mbar_arrive(&ctl->s_free[b]);
                 const int64_t key0 = static_cast<int64_t>(kt) * kPfKeys;
-                float x[64];
-                float mt = -INFINITY;
-                const bool partial = key0 + kPfKeys - 1 > lim;
+                float x[64];  // raw scores (scale applied below), -inf where masked
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    float v = __uint_as_float(sr[i >> 5][i & 31]) * p.c;
-                    if (partial && key0 + i > lim) v = -INFINITY;
-                    x[i] = v;
-                    mt = fmaxf(mt, v);
+                for (int i = 0; i < 64; ++i) x[i] = __uint_as_float(sr[i >> 5][i & 31]);
+                if (key0 + kPfKeys - 1 > lim) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i)
+                        if (key0 + i > lim) x[i] = -INFINITY;
                 }
+                float mx[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) mx[i] = x[i];
+#pragma unroll
+                for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], x[i]);
+                const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                       fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
+                                 p.c;
                 const bool grow = mt > m_run + kRescaleLog2 || (m_run == -INFINITY && mt > -INFINITY);
                 const float m_new = grow ? mt : m_run;
                 const bool first = kt == kt0;
                 const bool need = grow && m_run > -INFINITY && !first;
-                float alpha = need ? ex2(m_run - m_new) : 1.f;
+                const float alpha = need ? ex2(m_run - m_new) : 1.f;
                 if (__any_sync(0xffffffffu, need)) {
                     // O holds the PV of the previous tile once it completes
                     const int jp = j - 1;
-                    if (!wwait(&ctl->pv_done[jp & 1], (jp >> 1) & 1)) {
+                    if (!wwait(&ctl->pv_done[jp % kNStage], stage_parity(jp))) {
                         ok = false;
                         break;
                     }
@@ -420,18 +443,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                 }
                 l_run *= alpha;
                 m_run = m_new;
-                float ls = 0.f;
+                // p = 2^(c s - m): masked entries give 2^-inf = 0; a row with nothing
+                // visible yet subtracts 0 instead of -inf
+                const float msub = m_run == -INFINITY ? 0.f : m_run;
+                float lsum[8];
                 uint32_t ph[32];
 #pragma unroll
                 for (int i = 0; i < 64; i += 2) {
-                    const float p0 = x[i] == -INFINITY ? 0.f : ex2(x[i] - m_run);
-                    const float p1 = x[i + 1] == -INFINITY ? 0.f : ex2(x[i + 1] - m_run);
-                    ls += p0 + p1;
+                    const float p0 = ex2(fmaf(x[i], p.c, -msub));
+                    const float p1 = ex2(fmaf(x[i + 1], p.c, -msub));
+                    lsum[(i >> 1) & 7] = (i < 16) ? p0 + p1 : lsum[(i >> 1) & 7] + (p0 + p1);
                     ph[i >> 1] = pack_half2(p0, p1);
                 }
-                l_run += ls;
+                l_run += ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3])) + ((lsum[4] + lsum[5]) + (lsum[6] + lsum[7]));
                 // P buffer b was read by the PV of tile j - 2
-                if (j >= 2 && !wwait(&ctl->pv_done[b], ((j - 2) >> 1) & 1)) {
+                if (j >= 2 && !wwait(&ctl->pv_done[(j - 2) % kNStage], stage_parity(j - 2))) {
                     ok = false;
                     break;
                 }
@@ -446,7 +472,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
             if (!ok) break;
             // ---- item epilogue: partial (m, l, O) of every row ----
             const int jl = j - 1;
-            if (!wwait(&ctl->pv_done[jl & 1], (jl >> 1) & 1)) break;
+            if (!wwait(&ctl->pv_done[jl % kNStage], stage_parity(jl))) break;
             tc::fence_after();
             float *orow = part_o + (static_cast<size_t>(item) * kPfRows + r) * 256;
 #pragma unroll 1
@@ -468,17 +494,39 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
         // =========================== producers ===========================
         const int pt = threadIdx.x - kProdWarp0 * 32;  // 0..255
         const bool leader = pt == 0;
-        float2 *rope_tab = reinterpret_cast<float2 *>(base + kPOff);  // 16 tokens x 32 pairs
+        float2 *rope_tab = reinterpret_cast<float2 *>(base + kRopeOff);  // 16 tokens x 32 pairs
+        // TMEM rows this warp may write (its lane quarter) and which half of a staged block
+        const int sp = warp & 3, hw = (warp - kProdWarp0) >> 2;
         int j = 0;
+        uint32_t qph = 0;  // phases of qs_bar completed so far
+        auto load_raw = [&](int kt, int kvh, RawTile &rw) {
+            const int64_t key0 = static_cast<int64_t>(kt) * kPfKeys;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int job = pt + kProdThreads * u;
+                const int gi = job >> 7, ch = job & 127;
+                const int i = ch >> 5, g = (ch >> 2) & 7, c = ch & 3;
+                const int64_t unit = ((key0 / kGroupTokens + gi) * kHeadsKV + kvh) * kUnitBytes;
+                rw.kn[u] = __ldg(reinterpret_cast<const uint4 *>(p.k_cache + unit + i * 512 + (4 * g + c) * 16));
+                rw.ks[u] = __ldg(reinterpret_cast<const uint2 *>(p.k_cache + unit + kUnitQsBytes + g * 32 +
+                                                                  (i >> 1) * 16 + 8 * (i & 1)));
+                rw.vn[u] = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + unit + i * 512 + (4 * g + c) * 16));
+                rw.vs[u] = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + unit + kUnitQsBytes + c * 64 + 16 * i));
+            }
+        };
         for (int iter = 0;; ++iter) {
             int4 it;
             if (!get_item(iter, it, leader)) break;
             const int m = it.x, kt0 = it.y, kt1 = it.z;
             const int kvh = m & 1;
             const int tok0 = 16 * (m >> 1);
-            // previous item's MMAs (Q, P buffers) are complete
-            if (j > 0 && !wait_or_abort(&ctl->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, err, 4u)) break;
-            // ---- Q tile: RoPE, f16, contraction permutation, swizzled ----
+            RawTile cur;
+            load_raw(kt0, kvh, cur);  // first tile in flight while Q is built
+            // previous item's MMAs are complete: Q (TMEM), stages and P buffers are free
+            if (j > 0 && !wait_or_abort(&ctl->pv_done[(j - 1) % kNStage], stage_parity(j - 1), abort_flag, err, 4u))
+                break;
+            // ---- Q: RoPE, f16, contraction permutation; staged in shared memory, then
+            // each thread moves its row's half into tensor memory ----
             const int half = p.rope_n_rot >> 1;
             for (int e = pt; e < kPfTok * 32; e += kProdThreads) {
                 const int t = e >> 5, i = e & 31;
@@ -489,46 +537,66 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
             // every producer's part of the RoPE table is written (bounded, unlike bar.sync)
             mbar_arrive(&ctl->rope_bar);
             if (!wait_or_abort(&ctl->rope_bar, iter & 1, abort_flag, err, 4u)) break;
-            for (int job = pt; job < kPfRows * 32; job += kProdThreads) {
-                const int r = job >> 5, vc = job & 31;
-                const int token = tok0 + (r >> 3);
-                const int head = kvh * 8 + (r & 7);
-                uint32_t hv[4] = {0u, 0u, 0u, 0u};
-                if (token < p.T) {
-                    const int64_t rbase = token * p.q_st + head * p.q_sh;
-                    float v[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        v[e] = kv_row_elem(p.q, rbase, k_real_dim(vc * 8 + e), p.q_dtype, p.rope_n_rot,
-                                           rope_tab + (r >> 3) * 32);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) hv[e] = pack_half2(v[2 * e], v[2 * e + 1]);
-                }
-                sts128(base_s + kQOff + (vc >> 3) * kQRegion + swz(r, vc & 7), make_uint4(hv[0], hv[1], hv[2], hv[3]));
-            }
-            tc::fence_proxy_async_smem();
-            mbar_arrive(&ctl->q_full);
-            // ---- K / V tiles ----
             bool ok = true;
-            for (int kt = kt0; kt < kt1; ++kt, ++j) {
-                const int s = j & 1;
-                // loads first (their latency overlaps the wait for the stage)
-                const int64_t key0 = static_cast<int64_t>(kt) * kPfKeys;
-                uint4 kn[2], vn[2], vs[2];
-                uint2 ks[2];
+            for (int h = 0; h < 2 && ok; ++h) {
+                // staging: 128 rows x 16 chunks (8 contraction positions each), 256 B per
+                // row, chunk c of row r at position c ^ (r & 15)
+#pragma unroll 4
+                for (int job = pt; job < kPfRows * 16; job += kProdThreads) {
+                    const int r = job >> 4, cl = job & 15, vc = h * 16 + cl;
+                    const int token = tok0 + (r >> 3);
+                    const int head = kvh * 8 + (r & 7);
+                    uint32_t hv[4] = {0u, 0u, 0u, 0u};
+                    if (token < p.T) {
+                        const int64_t rbase = token * p.q_st + head * p.q_sh;
+                        float v[8];
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int job = pt + kProdThreads * u;
-                    const int gi = job >> 7, ch = job & 127;
-                    const int i = ch >> 5, g = (ch >> 2) & 7, c = ch & 3;
-                    const int64_t unit = ((key0 / kGroupTokens + gi) * kHeadsKV + kvh) * kUnitBytes;
-                    kn[u] = __ldg(reinterpret_cast<const uint4 *>(p.k_cache + unit + i * 512 + (4 * g + c) * 16));
-                    ks[u] = __ldg(reinterpret_cast<const uint2 *>(p.k_cache + unit + kUnitQsBytes + g * 32 +
-                                                                   (i >> 1) * 16 + 8 * (i & 1)));
-                    vn[u] = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + unit + i * 512 + (4 * g + c) * 16));
-                    vs[u] = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + unit + kUnitQsBytes + c * 64 + 16 * i));
+                        for (int e = 0; e < 8; ++e)
+                            v[e] = kv_row_elem(p.q, rbase, k_real_dim(vc * 8 + e), p.q_dtype, p.rope_n_rot,
+                                               rope_tab + (r >> 3) * 32);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) hv[e] = pack_half2(v[2 * e], v[2 * e + 1]);
+                    }
+                    sts128(base_s + kPOff + r * 256 + ((cl ^ (r & 15)) << 4), make_uint4(hv[0], hv[1], hv[2], hv[3]));
                 }
-                if (j >= 2 && !wait_or_abort(&ctl->pv_done[s], ((j - 2) >> 1) & 1, abort_flag, err, 4u)) {
+                mbar_arrive(&ctl->qs_bar);
+                if (!wait_or_abort(&ctl->qs_bar, qph & 1, abort_flag, err, 4u)) { ok = false; break; }
+                ++qph;
+                {
+                    const int r = 32 * sp + lane;
+                    uint32_t qv[32];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int cl = hw * 8 + k;
+                        uint4 x;
+                        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                                     : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w)
+                                     : "r"(base_s + kPOff + r * 256 + ((cl ^ (r & 15)) << 4)));
+                        qv[4 * k] = x.x;
+                        qv[4 * k + 1] = x.y;
+                        qv[4 * k + 2] = x.z;
+                        qv[4 * k + 3] = x.w;
+                    }
+                    tc::st32(tmem + (static_cast<uint32_t>(32 * sp) << 16) + kQCol + h * 64 + hw * 32, qv);
+                    tc::wait_st();
+                }
+                if (h == 0) {  // the staging buffer is rewritten for the second half
+                    mbar_arrive(&ctl->qs_bar);
+                    if (!wait_or_abort(&ctl->qs_bar, qph & 1, abort_flag, err, 4u)) { ok = false; break; }
+                    ++qph;
+                }
+            }
+            if (!ok) break;
+            tc::fence_before();
+            mbar_arrive(&ctl->q_full);
+            // ---- K / V tiles: the raw q4_0 of tile kt+1 is loaded while tile kt is converted ----
+            for (int kt = kt0; kt < kt1; ++kt, ++j) {
+                const int s = j % kNStage;
+                RawTile nxt;
+                if (kt + 1 < kt1) load_raw(kt + 1, kvh, nxt);
+                const int64_t key0 = static_cast<int64_t>(kt) * kPfKeys;
+                if (j >= kNStage &&
+                    !wait_or_abort(&ctl->pv_done[s], stage_parity(j - kNStage), abort_flag, err, 4u)) {
                     ok = false;
                     break;
                 }
@@ -543,8 +611,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                     {
                         const int row = gi * 16 + g + 8 * (i >> 1);
                         const bool live = key0 + row < n_kv;
-                        const uint32_t w4[4] = {kn[u].x, kn[u].y, kn[u].z, kn[u].w};
-                        const uint32_t d4[2] = {ks[u].x, ks[u].y};
+                        const uint32_t w4[4] = {cur.kn[u].x, cur.kn[u].y, cur.kn[u].z, cur.kn[u].w};
+                        const uint32_t d4[2] = {cur.ks[u].x, cur.ks[u].y};
                         const uint32_t rb = kst + ((i & 1) * 2 + (c >> 1)) * kKvRegion;
 #pragma unroll
                         for (int w = 0; w < 4; ++w) {
@@ -563,9 +631,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                     }
                     // V: tokens {2c, 2c+8, 2c+1, 2c+9} (byte positions 0..3); blocks 2i + (w>>1)
                     {
-                        const uint32_t w4[4] = {vn[u].x, vn[u].y, vn[u].z, vn[u].w};
-                        const uint32_t d4[4] = {vs[u].x, vs[u].y, vs[u].z, vs[u].w};
+                        const uint32_t w4[4] = {cur.vn[u].x, cur.vn[u].y, cur.vn[u].z, cur.vn[u].w};
+                        const uint32_t d4[4] = {cur.vs[u].x, cur.vs[u].y, cur.vs[u].z, cur.vs[u].w};
                         const uint32_t rb = vst + i * kKvRegion;
+                        // lo/hi nibbles of the 4 tokens, token-interleaved: [l0 h0 l1 h1], [l2 h2 l3 h3]
+                        uint32_t xy[4][2];
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) {
+                            const uint32_t lo = w4[w] & 0x0F0F0F0Fu;
+                            const uint32_t hi = (w4[w] >> 4) & 0x0F0F0F0Fu;
+                            asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(xy[w][0]) : "r"(lo), "r"(hi));
+                            asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(xy[w][1]) : "r"(lo), "r"(hi));
+                        }
 #pragma unroll
                         for (int pos = 0; pos < 4; ++pos) {
                             const int tt = (pos & 1) * 8 + 2 * c + (pos >> 1);
@@ -580,9 +657,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                                     const int hidx = (w >> 1) * 4 + jj;
                                     const __half2 dd = u32_as_h2(d4[hidx >> 1]);
                                     const __half d1 = (hidx & 1) ? __high2half(dd) : __low2half(dd);
-                                    const uint32_t byte = (w4[w] >> (8 * pos)) & 0xFFu;
-                                    const uint32_t x = (byte & 0x0Fu) | ((byte >> 4) << 8);
-                                    o4[w] = nib_pair(x, 0x4140u, __half2half2(d1));
+                                    o4[w] = nib_pair(xy[w][pos >> 1], (pos & 1) ? 0x4342u : 0x4140u,
+                                                     __half2half2(d1));
                                 }
                                 outv = make_uint4(o4[0], o4[1], o4[2], o4[3]);
                             }
@@ -592,6 +668,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                 }
                 tc::fence_proxy_async_smem();
                 mbar_arrive(&ctl->kv_full[s]);
+                if (kt + 1 < kt1) cur = nxt;
             }
             if (!ok) break;
         }
