@@ -256,6 +256,17 @@ typedef struct sqmix_gdn_args {
 
 int sqmix_gdn_decode(const sqmix_gdn_args *args, sqmix_stream_t stream);
 
+/* Chunked prefill form of sqmix_gdn_decode for long T (gdn.rs:489-500 over a prompt
+ * chunk): the same arguments and results, computed 64 tokens at a time (the
+ * chunk-parallel form of the delta rule: a unit lower-triangular solve per chunk and
+ * dense chunk products), the last n_snap - 1 tokens recurrently for the snapshot
+ * slots.  workspace: sqmix_gdn_prefill_workspace_bytes(n_seqs, T, h_v) bytes, 16-byte
+ * aligned, no initialisation needed.  The input plane is sel[seq] (or 0); like
+ * sqmix_gdn_decode the result planes are 0..n_snap-1. */
+size_t sqmix_gdn_prefill_workspace_bytes(int32_t n_seqs, int32_t n_tokens, int32_t h_v);
+int sqmix_gdn_prefill(const sqmix_gdn_args *args, void *workspace, size_t workspace_bytes,
+                      sqmix_stream_t stream);
+
 /* Copy whole planes: dst[i] <- src[i] for n_planes planes of `plane_elems` f32
  * (the state ggml_cpy of graph.rs:884-912 and get_rows of gdn.rs:445-463 when a
  * caller wants a materialised plane).  Device pointers. */

@@ -35,6 +35,9 @@ struct GdnParams {
     int n_seqs, T, h_k, h_v, n_snap;
     float l2_eps;
     float *out;
+    int plane0;   // input plane when sel is NULL
+    int T_all;    // tokens per sequence in g, beta and out
+    int64_t tok0; // first token of this launch within the sequence
 };
 
 __device__ __forceinline__ float4 load4(const void *p, int64_t i, int dtype) {
@@ -77,7 +80,7 @@ __global__ void __launch_bounds__(256) gdn_recurrent_kernel(GdnParams p) {
     if (seq >= p.n_seqs) return;
     const int hk = h % p.h_k;
 
-    int plane = p.sel ? p.sel[seq] : 0;
+    int plane = p.sel ? p.sel[seq] : p.plane0;
     plane = min(max(plane, 0), p.n_planes - 1);
     const int64_t plane_elems = static_cast<int64_t>(p.h_v) * 128 * 128;
     float *st_seq = p.state + seq * p.n_planes * plane_elems;
@@ -86,17 +89,18 @@ __global__ void __launch_bounds__(256) gdn_recurrent_kernel(GdnParams p) {
 
     const float inv_sqrt_d = 1.0f / sqrtf(128.0f);
     for (int t = 0; t < p.T; ++t) {
-        const int64_t qk_off = seq * p.qk_sseq + t * p.qk_st + static_cast<int64_t>(hk) * 128 + 4 * lane;
+        const int64_t tt = p.tok0 + t;
+        const int64_t qk_off = seq * p.qk_sseq + tt * p.qk_st + static_cast<int64_t>(hk) * 128 + 4 * lane;
         float4 kk = load4(p.k, qk_off, p.dtype);
         float4 qq = load4(p.q, qk_off, p.dtype);
         if (p.l2_eps > 0.f) {
             kk = l2norm4(kk, p.l2_eps);
             qq = l2norm4(qq, p.l2_eps);
         }
-        const int64_t gb = (seq * p.T + t) * p.h_v + h;
+        const int64_t gb = (seq * p.T_all + tt) * p.h_v + h;
         const float decay = expf(p.g[gb]);
         const float bt = p.beta[gb];
-        const float vj = load_act(p.v, seq * p.v_sseq + t * p.v_st + static_cast<int64_t>(h) * 128 + j, p.dtype);
+        const float vj = load_act(p.v, seq * p.v_sseq + tt * p.v_st + static_cast<int64_t>(h) * 128 + j, p.dtype);
         S.x *= decay;
         S.y *= decay;
         S.z *= decay;
@@ -116,7 +120,7 @@ __global__ void __launch_bounds__(256) gdn_recurrent_kernel(GdnParams p) {
         S.z = fmaf(kk.z, delta, S.z);
         S.w = fmaf(kk.w, delta, S.w);
         if (lane == 0)
-            p.out[((seq * p.T + t) * p.h_v + h) * 128 + j] = fmaf(delta, kq, sq) * inv_sqrt_d;
+            p.out[((seq * p.T_all + tt) * p.h_v + h) * 128 + j] = fmaf(delta, kq, sq) * inv_sqrt_d;
         const int slot = p.T - 1 - t;
         if (slot < p.n_snap)
             *reinterpret_cast<float4 *>(st_seq + slot * plane_elems + col_off) = S;
@@ -129,6 +133,39 @@ __global__ void copy_f32x4_kernel(float4 *dst, const float4 *src, int64_t n4) {
         dst[i] = src[i];
 }
 
+}  // namespace sqmix
+
+namespace sqmix {
+int gdn_launch_recurrent(const sqmix_gdn_args *a, int plane_in, int64_t tok_off, int n_tok, int n_snap,
+                         cudaStream_t st) {
+    GdnParams p;
+    p.q = a->q;
+    p.k = a->k;
+    p.v = a->v;
+    p.dtype = a->dtype;
+    p.qk_st = a->qk_stride_tok;
+    p.v_st = a->v_stride_tok;
+    p.qk_sseq = a->qk_stride_seq;
+    p.v_sseq = a->v_stride_seq;
+    p.g = a->g;
+    p.beta = a->beta;
+    p.state = a->state;
+    p.n_planes = a->n_planes;
+    p.sel = plane_in < 0 ? a->sel : nullptr;
+    p.plane0 = plane_in < 0 ? 0 : plane_in;
+    p.n_seqs = a->n_seqs;
+    p.T = n_tok;
+    p.T_all = a->n_tokens;
+    p.tok0 = tok_off;
+    p.h_k = a->h_k;
+    p.h_v = a->h_v;
+    p.n_snap = n_snap;
+    p.l2_eps = a->l2_eps;
+    p.out = a->out;
+    const int64_t warps = static_cast<int64_t>(a->n_seqs) * a->h_v * 128;
+    gdn_recurrent_kernel<<<static_cast<unsigned>(warps / 8), 256, 0, st>>>(p);
+    return cuda_status(cudaGetLastError(), "gdn recurrent launch");
+}
 }  // namespace sqmix
 
 using namespace sqmix;
@@ -158,31 +195,7 @@ extern "C" int sqmix_gdn_decode(const sqmix_gdn_args *a, sqmix_stream_t stream) 
         SQMIX_CHECK_ARG(((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k)) & align) == 0,
                         "gdn_decode: q/k base pointers must be %d-byte aligned", (int)align + 1);
     }
-    GdnParams p;
-    p.q = a->q;
-    p.k = a->k;
-    p.v = a->v;
-    p.dtype = a->dtype;
-    p.qk_st = a->qk_stride_tok;
-    p.v_st = a->v_stride_tok;
-    p.qk_sseq = a->qk_stride_seq;
-    p.v_sseq = a->v_stride_seq;
-    p.g = a->g;
-    p.beta = a->beta;
-    p.state = a->state;
-    p.n_planes = a->n_planes;
-    p.sel = a->sel;
-    p.n_seqs = a->n_seqs;
-    p.T = a->n_tokens;
-    p.h_k = a->h_k;
-    p.h_v = a->h_v;
-    p.n_snap = a->n_snap;
-    p.l2_eps = a->l2_eps;
-    p.out = a->out;
-    const int64_t warps = static_cast<int64_t>(a->n_seqs) * a->h_v * 128;
-    gdn_recurrent_kernel<<<static_cast<unsigned>(warps / 8), 256, 0,
-                           reinterpret_cast<cudaStream_t>(stream)>>>(p);
-    return cuda_status(cudaGetLastError(), "gdn_decode launch");
+    return gdn_launch_recurrent(a, -1, 0, a->n_tokens, a->n_snap, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int sqmix_gdn_state_copy(float *dst, const float *src, int64_t plane_elems, int32_t n_planes,

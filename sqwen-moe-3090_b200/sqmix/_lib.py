@@ -98,6 +98,8 @@ _SIGNATURES = {
     "sqmix_fa_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(FaArgs), c_void_p]),
     "sqmix_fa_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32]),
     "sqmix_fa_prefill": (ctypes.c_int, [ctypes.POINTER(FaArgs), c_void_p]),
+    "sqmix_gdn_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
+    "sqmix_gdn_prefill": (ctypes.c_int, [ctypes.POINTER(GdnArgs), c_void_p, c_size_t, c_void_p]),
     "sqmix_attn_merge_lse": (ctypes.c_int, [c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                                             c_void_p, c_void_p]),
     "sqmix_gdn_decode": (ctypes.c_int, [ctypes.POINTER(GdnArgs), c_void_p]),

@@ -228,16 +228,26 @@ def attn_merge_lse(o_parts: torch.Tensor, lse_parts: torch.Tensor, gate: torch.T
     return out
 
 
+GDN_CHUNK_MIN_T = 64  # from this many tokens on, gated_delta_net uses the chunked kernels
+
+
+def gdn_prefill_workspace_bytes(n_seqs: int, n_tokens: int, h_v: int) -> int:
+    return int(lib().sqmix_gdn_prefill_workspace_bytes(int(n_seqs), int(n_tokens), int(h_v)))
+
+
 def gated_delta_net(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
                     beta: torch.Tensor, state: torch.Tensor, n_planes: int = 1,
                     sel: torch.Tensor | None = None, n_snap: int = 1, l2_eps: float = 0.0,
-                    out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+                    out: torch.Tensor | None = None, chunked: bool | None = None,
+                    workspace: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     """Gated delta rule over T tokens for n_seqs sequences.
 
     q, k [n_seqs][T][H_k][128]; v [n_seqs][T][H_v][128] (f32/bf16/f16); g, beta
     [n_seqs][T][H_v] f32; state [n_seqs][n_planes][H_v][128][128] f32 (updated in place:
     plane s <- state after T - s tokens for s < n_snap; the input plane is sel[seq]).
     3-D q/k/v/g/beta (no sequence dim) are accepted for n_seqs = 1.
+    chunked: None picks the chunked prefill kernels (sqmix_gdn_prefill) for
+    T >= GDN_CHUNK_MIN_T and the recurrent kernel (sqmix_gdn_decode) below.
     """
     _require_cuda(q, k, v, g, beta, state, sel)
     if q.dim() == 3:
@@ -259,7 +269,16 @@ def gated_delta_net(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.
         qk_stride_seq=q.stride(0), v_stride_seq=v.stride(0), g=_ptr(g), beta=_ptr(beta),
         state=_ptr(state), n_planes=int(n_planes), sel=_ptr(sel), n_seqs=n_seqs, n_tokens=T, h_k=H_k,
         h_v=H_v, n_snap=int(n_snap), l2_eps=float(l2_eps), out=_ptr(out))
-    check(lib().sqmix_gdn_decode(ctypes.byref(a), _stream(stream)), "gated_delta_net")
+    if chunked is None:
+        chunked = T >= GDN_CHUNK_MIN_T
+    if chunked:
+        need = gdn_prefill_workspace_bytes(n_seqs, T, H_v)
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        check(lib().sqmix_gdn_prefill(ctypes.byref(a), _ptr(workspace), workspace.numel(), _stream(stream)),
+              "gated_delta_net (chunked)")
+    else:
+        check(lib().sqmix_gdn_decode(ctypes.byref(a), _stream(stream)), "gated_delta_net")
     return out
 
 
