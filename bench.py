@@ -464,6 +464,95 @@ def bench_prefill(steps: int, warmup: int):
     return res
 
 
+GDN_STATE_BYTES = 32 * 128 * 128 * 4  # one GDN layer's recurrent state (2 MiB)
+
+
+def gdn_inputs(g, dev, T: int, n_layers: int):
+    """Config-1 inputs: state N(0, 0.02) [32][128][128] per layer, q/k bf16 N(0,1)
+    (L2-normalised inside the kernel), v bf16 N(0,1), beta = sigmoid(N(0,1)),
+    g = -exp(A_log) softplus(N(0,1) + dt_bias), A_log ~ U(0, 2.7), dt_bias ~ N(0,1)."""
+    import torch
+
+    S = torch.randn((n_layers, 1, 1, 32, 128, 128), generator=g, device=dev) * 0.02
+    q = torch.randn((1, T, 16, 128), generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn((1, T, 16, 128), generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn((1, T, 32, 128), generator=g, device=dev).to(torch.bfloat16)
+    a_log = torch.rand((32,), generator=g, device=dev) * 2.7
+    dt_bias = torch.randn((32,), generator=g, device=dev)
+    sp = torch.nn.functional.softplus(torch.randn((1, T, 32), generator=g, device=dev) + dt_bias)
+    gg = (-torch.exp(a_log) * sp).contiguous()
+    beta = torch.sigmoid(torch.randn((1, T, 32), generator=g, device=dev)).contiguous()
+    return S, q, k, v, gg, beta
+
+
+def bench_gdn(steps: int, warmup: int):
+    """Config 1: GDN decode (one token per layer; the states of 96 layers, 201 MB, are
+    cycled so that each layer's state comes from HBM) and a 512-token chunked prefill."""
+    import torch
+
+    import sqmix
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(13)
+    res = {}
+    hbm, hbm_kind = peaks()
+    n_layers = 96
+    S, q, k, v, gg, beta = gdn_inputs(g, dev, 1, n_layers)
+    out = torch.empty((1, 1, 32, 128), device=dev)
+
+    def decode_all():
+        for l in range(n_layers):
+            sqmix.gated_delta_net(q, k, v, gg, beta, S[l], l2_eps=1e-6, out=out)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        decode_all()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        decode_all()
+    for _ in range(max(warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(3, steps)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * n_layers)
+    alg = 2 * GDN_STATE_BYTES + 1 * (2 * 16 * 128 * 2 + 32 * 128 * 2 + 32 * 128 * 4 + 2 * 32 * 4)
+    res["decode"] = {"us_per_layer_token": us, "alg_bytes": alg, "achieved_gbs": alg / us / 1e3,
+                     "frac_of_hbm": alg / us / 1e3 / hbm, "peak_gbs": hbm, "peak_kind": hbm_kind,
+                     "note": "CUDA graph of 96 single-token layer updates (states cycled through HBM)"}
+    del graph, S
+    T = 512
+    S, q, k, v, gg, beta = gdn_inputs(g, dev, T, 1)
+    out = torch.empty((1, T, 32, 128), device=dev)
+    ws = torch.zeros(sqmix.gdn_prefill_workspace_bytes(1, T, 32), dtype=torch.uint8, device=dev)
+
+    def prefill():
+        sqmix.gated_delta_net(q, k, v, gg, beta, S[0], l2_eps=1e-6, out=out, chunked=True, workspace=ws)
+
+    for _ in range(max(warmup, 3)):
+        prefill()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        prefill()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    flops = 2.68e9  # chunked form, 8 chunks x 32 heads (C = 64, d = 128)
+    res["prefill512"] = {"us": us, "tok_s": T / us * 1e6, "tflops_chunked_form": flops / us / 1e6,
+                         "note": "one layer, chunk 64, eager launches"}
+    res["config"] = "config1: 32 value heads over 16 q/k heads, d 128, bf16 q/k/v, fused L2 norm"
+    return res
+
+
 def run_profile_case(case: str):
     """Small fixed workloads for ncu captures (one kernel, a few launches, ~0.3 GB)."""
     import torch
@@ -502,6 +591,10 @@ def run_profile_case(case: str):
         for _ in range(3):
             sqmix.flash_attn_prefill(q, kc, vc, cap, d[0:1], d[1:2], gate=gate, rope_n_rot=N_ROT,
                                      rope_freq_base=FREQ_BASE, workspace=ws)
+    elif case == "gdnp":
+        S, q, k, v, gg, beta = gdn_inputs(g, dev, 512, 1)
+        for _ in range(3):
+            sqmix.gated_delta_net(q, k, v, gg, beta, S[0], l2_eps=1e-6, chunked=True)
     elif case == "gdn":
         S = torch.randn((1, 1, 32, 128, 128), generator=g, device=dev) * 0.02
         q = torch.nn.functional.normalize(torch.randn((1, 1, 16, 128), generator=g, device=dev), dim=-1)
@@ -526,7 +619,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill measurement")
-    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn) and exit")
+    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn | gdnp) and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)
@@ -557,6 +650,7 @@ def main():
     res = run_gpu(args, rank, world, local_rank)
     if res is not None and world == 1 and not args.no_prefill:
         res["prefill"] = bench_prefill(args.steps, args.warmup)
+        res["gdn"] = bench_gdn(args.steps, args.warmup)
     if res is not None:
         if cpu is not None:
             res["cpu_baseline"] = cpu

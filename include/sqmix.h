@@ -261,8 +261,9 @@ int sqmix_gdn_decode(const sqmix_gdn_args *args, sqmix_stream_t stream);
  * chunk-parallel form of the delta rule: a unit lower-triangular solve per chunk and
  * dense chunk products), the last n_snap - 1 tokens recurrently for the snapshot
  * slots.  workspace: sqmix_gdn_prefill_workspace_bytes(n_seqs, T, h_v) bytes, 16-byte
- * aligned, no initialisation needed.  The input plane is sel[seq] (or 0); like
- * sqmix_gdn_decode the result planes are 0..n_snap-1. */
+ * aligned, its first 256 bytes zero before first use (a device status word that
+ * sqmix_fa_status reads and clears, as for the decode workspace).  The input plane is
+ * sel[seq] (or 0); like sqmix_gdn_decode the result planes are 0..n_snap-1. */
 size_t sqmix_gdn_prefill_workspace_bytes(int32_t n_seqs, int32_t n_tokens, int32_t h_v);
 int sqmix_gdn_prefill(const sqmix_gdn_args *args, void *workspace, size_t workspace_bytes,
                       sqmix_stream_t stream);

@@ -38,14 +38,16 @@ namespace {
 constexpr int kC = 64;     // chunk length
 constexpr int kD = 128;    // head dim
 constexpr int kJB = 32;    // value columns per scan CTA
-// per (sequence, head, chunk) in the workspace, in floats
-constexpr int64_t kOffW = 0;
-constexpr int64_t kOffU = kOffW + kC * kD;
-constexpr int64_t kOffQ = kOffU + kC * kD;
-constexpr int64_t kOffK = kOffQ + kC * kD;
-constexpr int64_t kOffM = kOffK + kC * kD;
+// per (sequence, head, chunk) in the workspace, in floats; W, Q and M are stored
+// transposed (contraction index major) so that the scan reads 4 rows per vector load
+constexpr int64_t kOffW = 0;                // W^T  [128 i][64 t]
+constexpr int64_t kOffU = kOffW + kC * kD;  // U    [64 t][128 j]
+constexpr int64_t kOffQ = kOffU + kC * kD;  // Qs^T [128 i][64 t]  q e^G / sqrt(128)
+constexpr int64_t kOffK = kOffQ + kC * kD;  // K'   [64 t][128 i]  k e^{G_C - G}
+constexpr int64_t kOffM = kOffK + kC * kD;  // M^T  [64 s][64 t]   (Q K^T o D)^T / sqrt(128)
 constexpr int64_t kOffS = kOffM + kC * kC;  // scalars: [0] e^{G_C}
 constexpr int64_t kChunkFloats = kOffS + 64;
+constexpr int64_t kWsHeaderFloats = 64;  // [0] u32 device status bits (bounded waits)
 
 struct ChunkParams {
     const void *q, *k, *v;
@@ -68,18 +70,37 @@ __device__ __forceinline__ float warp_sum32(float x) {
     return x;
 }
 
+// 4 consecutive elements of a q/k/v row (offset a multiple of 4) as f32
+__device__ __forceinline__ float4 load4v(const void *p, int64_t i, int dtype) {
+    if (dtype == SQMIX_F32) return *reinterpret_cast<const float4 *>(static_cast<const float *>(p) + i);
+    const uint2 r = *reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(p) + i);
+    if (dtype == SQMIX_BF16) {
+        const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162 *>(&r.x);
+        const __nv_bfloat162 y = *reinterpret_cast<const __nv_bfloat162 *>(&r.y);
+        return make_float4(__low2float(x), __high2float(x), __low2float(y), __high2float(y));
+    }
+    const __half2 x = *reinterpret_cast<const __half2 *>(&r.x);
+    const __half2 y = *reinterpret_cast<const __half2 *>(&r.y);
+    return make_float4(__low2float(x), __high2float(x), __low2float(y), __high2float(y));
+}
+
+__device__ __forceinline__ float *chunk_ws(const ChunkParams &p, int seq, int h, int c) {
+    return p.ws + kWsHeaderFloats + ((static_cast<int64_t>(seq) * p.h_v + h) * p.n_chunks + c) * kChunkFloats;
+}
+
 // ---- phase 1: state-independent chunk quantities -----------------------------------
 // grid (n_chunks, h_v, n_seqs), 256 threads, dynamic smem kPrepSmem
-constexpr int kLd = kD + 4;  // padded row stride of the [64][128] tiles
-constexpr size_t kPrepSmem = (3 * kC * kLd + 2 * kC * (kC + 1) + 4 * kC) * sizeof(float);
+constexpr int kLd = kD + 4;   // padded row stride of the [64][128] tiles
+constexpr int kLdA = kC + 4;  // row stride of A (16-byte row quads)
+constexpr size_t kPrepSmem = (3 * kC * kLd + kC * kLdA + kC * (kC + 1) + 4 * kC) * sizeof(float);
 
 __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
-    extern __shared__ float sm[];
-    float *Ks = sm;                  // [64][kLd]  k, later beta e^G k -> W
+    extern __shared__ __align__(16) float sm[];
+    float *Ks = sm;                  // [64][kLd]  k (L2-normalised)
     float *Qs = Ks + kC * kLd;       // [64][kLd]  q
-    float *Vs = Qs + kC * kLd;       // [64][kLd]  beta v -> U
-    float *A = Vs + kC * kLd;        // [64][65]
-    float *Mq = A + kC * (kC + 1);   // [64][65]
+    float *Vs = Qs + kC * kLd;       // [64][kLd]  v
+    float *A = Vs + kC * kLd;        // [64][kLdA] beta_t e^{G_t - G_s} k_t.k_s, s < t (0 elsewhere)
+    float *Mq = A + kC * kLdA;       // [64][65]   e^{G_t - G_s} q_t.k_s / sqrt(128), s <= t
     float *G = Mq + kC * (kC + 1);   // [64] cumulative log decay
     float *bt = G + kC;              // [64] beta
     float *gg = bt + kC;             // [64] g
@@ -89,31 +110,38 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     const int t0 = c * kC;
     const int n_valid = min(kC, p.T - t0);
 
-    // rows: warp w loads rows w, w+8, ...; 4 elements per lane
-    for (int t = warp; t < kC; t += 8) {
-        float4 kk = make_float4(0.f, 0.f, 0.f, 0.f), qq = kk, vv = kk;
-        if (t < n_valid) {
-            const int64_t qk_off = seq * p.qk_sseq + (t0 + t) * p.qk_st + static_cast<int64_t>(hk) * kD + 4 * lane;
-            const int64_t v_off = seq * p.v_sseq + (t0 + t) * p.v_st + static_cast<int64_t>(h) * kD + 4 * lane;
-            kk = make_float4(load_act(p.k, qk_off, p.dtype), load_act(p.k, qk_off + 1, p.dtype),
-                             load_act(p.k, qk_off + 2, p.dtype), load_act(p.k, qk_off + 3, p.dtype));
-            qq = make_float4(load_act(p.q, qk_off, p.dtype), load_act(p.q, qk_off + 1, p.dtype),
-                             load_act(p.q, qk_off + 2, p.dtype), load_act(p.q, qk_off + 3, p.dtype));
-            vv = make_float4(load_act(p.v, v_off, p.dtype), load_act(p.v, v_off + 1, p.dtype),
-                             load_act(p.v, v_off + 2, p.dtype), load_act(p.v, v_off + 3, p.dtype));
-            if (p.l2_eps > 0.f) {  // rms_norm(x, eps/n) * n^-1/2 (gdn.rs:133-142)
-                const float sk = warp_sum32(kk.x * kk.x + kk.y * kk.y + kk.z * kk.z + kk.w * kk.w);
-                const float sq = warp_sum32(qq.x * qq.x + qq.y * qq.y + qq.z * qq.z + qq.w * qq.w);
+    // rows: warp w loads rows w, w+8, ..., w+56 (all loads issued before use)
+    {
+        float4 kk[8], qq[8], vv[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const int t = warp + 8 * r;
+            kk[r] = qq[r] = vv[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t < n_valid) {
+                const int64_t qk_off = seq * p.qk_sseq + (t0 + t) * p.qk_st + static_cast<int64_t>(hk) * kD + 4 * lane;
+                const int64_t v_off = seq * p.v_sseq + (t0 + t) * p.v_st + static_cast<int64_t>(h) * kD + 4 * lane;
+                kk[r] = load4v(p.k, qk_off, p.dtype);
+                qq[r] = load4v(p.q, qk_off, p.dtype);
+                vv[r] = load4v(p.v, v_off, p.dtype);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const int t = warp + 8 * r;
+            float4 k4 = kk[r], q4 = qq[r];
+            if (p.l2_eps > 0.f && t < n_valid) {  // rms_norm(x, eps/n) * n^-1/2 (gdn.rs:133-142)
+                const float sk = warp_sum32(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w);
+                const float sq = warp_sum32(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
                 const float r2 = 1.0f / sqrtf(128.0f);
                 const float fk = 1.0f / sqrtf(sk / 128.0f + p.l2_eps / 128.0f) * r2;
                 const float fq = 1.0f / sqrtf(sq / 128.0f + p.l2_eps / 128.0f) * r2;
-                kk = make_float4(kk.x * fk, kk.y * fk, kk.z * fk, kk.w * fk);
-                qq = make_float4(qq.x * fq, qq.y * fq, qq.z * fq, qq.w * fq);
+                k4 = make_float4(k4.x * fk, k4.y * fk, k4.z * fk, k4.w * fk);
+                q4 = make_float4(q4.x * fq, q4.y * fq, q4.z * fq, q4.w * fq);
             }
+            *reinterpret_cast<float4 *>(Ks + t * kLd + 4 * lane) = k4;
+            *reinterpret_cast<float4 *>(Qs + t * kLd + 4 * lane) = q4;
+            *reinterpret_cast<float4 *>(Vs + t * kLd + 4 * lane) = vv[r];
         }
-        *reinterpret_cast<float4 *>(Ks + t * kLd + 4 * lane) = kk;
-        *reinterpret_cast<float4 *>(Qs + t * kLd + 4 * lane) = qq;
-        *reinterpret_cast<float4 *>(Vs + t * kLd + 4 * lane) = vv;
     }
     if (tid < kC) {
         const int64_t gb = (static_cast<int64_t>(seq) * p.T_all + t0 + tid) * p.h_v + h;
@@ -123,22 +151,23 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     __syncthreads();
     if (warp == 0) {  // inclusive scan of g over the chunk (two values per lane)
         float a0 = gg[2 * lane], a1 = gg[2 * lane + 1];
-        float s = a0 + a1;
+        float sc = a0 + a1;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
-            const float y = __shfl_up_sync(0xffffffffu, s, off);
-            if (lane >= off) s += y;
+            const float y = __shfl_up_sync(0xffffffffu, sc, off);
+            if (lane >= off) sc += y;
         }
-        const float excl = s - (a0 + a1);
+        const float excl = sc - (a0 + a1);
         G[2 * lane] = excl + a0;
         G[2 * lane + 1] = excl + a0 + a1;
     }
     __syncthreads();
 
-    // K K^T and Q K^T, 4x4 outputs per thread
+    // K K^T and Q K^T, 4x4 outputs per thread: rows tb + 16a, columns sb + 16b
     {
-        const int tb = tid >> 4, sb = tid & 15;  // rows tb + 16a, columns sb + 16b
+        const int tb = tid >> 4, sb = tid & 15;
         float kk[4][4] = {}, qk[4][4] = {};
+#pragma unroll 4
         for (int i = 0; i < kD; ++i) {
             float kt[4], qt[4], ks[4];
 #pragma unroll
@@ -160,187 +189,237 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
         for (int a = 0; a < 4; ++a)
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
-                const int t = tb + 16 * a, s = sb + 16 * b;
-                const float dec = s <= t ? expf(G[t] - G[s]) : 0.f;
-                A[t * (kC + 1) + s] = s < t ? bt[t] * dec * kk[a][b] : 0.f;
-                Mq[t * (kC + 1) + s] = dec * qk[a][b] * rsd;
+                const int t = tb + 16 * a, s2 = sb + 16 * b;
+                const float dec = s2 <= t ? expf(G[t] - G[s2]) : 0.f;
+                A[t * kLdA + s2] = s2 < t ? bt[t] * dec * kk[a][b] : 0.f;
+                Mq[t * (kC + 1) + s2] = dec * qk[a][b] * rsd;
             }
     }
     __syncthreads();
-    // right-hand sides: beta e^G k and beta v
-    for (int e = tid; e < kC * kD; e += 256) {
-        const int t = e >> 7, i = e & 127;
-        Ks[t * kLd + i] *= bt[t] * expf(G[t]);
-        Vs[t * kLd + i] *= bt[t];
-    }
-    __syncthreads();
-    // forward substitution, one thread per column of [W | U]: X_t -= sum_{s<t} A_ts X_s
+    float *wsc = chunk_ws(p, seq, h, c);
+    // forward substitution of (I + A) X = [beta e^G K | beta V], one thread per column,
+    // the column held in registers; A_ts = 0 for s >= t, so whole 4-groups are summed
     {
-        float *X = tid < kD ? Ks + tid : Vs + (tid - kD);
+        const int col = tid & 127;
+        const bool is_w = tid < kD;
+        const float *src = is_w ? Ks : Vs;
+        float x[kC];
+#pragma unroll
+        for (int t = 0; t < kC; ++t) x[t] = src[t * kLd + col] * bt[t] * (is_w ? expf(G[t]) : 1.f);
+#pragma unroll
         for (int t = 1; t < kC; ++t) {
-            float acc = X[t * kLd];
-            const float *Ar = A + t * (kC + 1);
-            for (int s = 0; s < t; ++s) acc = fmaf(-Ar[s], X[s * kLd], acc);
-            X[t * kLd] = acc;
-        }
-    }
-    __syncthreads();
-    // outputs: W, U, Q e^G / sqrt(d), K e^{G_C - G}, M
-    float *wsc = p.ws + ((static_cast<int64_t>(seq) * p.h_v + h) * p.n_chunks + c) * kChunkFloats;
-    const float GC = G[kC - 1];
-    const float rsd = 1.0f / sqrtf(128.0f);
-    for (int e = tid; e < kC * kD / 4; e += 256) {
-        const int t = e >> 5, i4 = (e & 31) * 4;
-        const float4 w = *reinterpret_cast<const float4 *>(Ks + t * kLd + i4);
-        const float4 u = *reinterpret_cast<const float4 *>(Vs + t * kLd + i4);
-        float4 qv = *reinterpret_cast<const float4 *>(Qs + t * kLd + i4);
-        const float fq = expf(G[t]) * rsd;
-        qv = make_float4(qv.x * fq, qv.y * fq, qv.z * fq, qv.w * fq);
-        *reinterpret_cast<float4 *>(wsc + kOffW + t * kD + i4) = w;
-        *reinterpret_cast<float4 *>(wsc + kOffU + t * kD + i4) = u;
-        *reinterpret_cast<float4 *>(wsc + kOffQ + t * kD + i4) = qv;
-    }
-    __syncthreads();
-    // K e^{G_C - G}: Ks was overwritten by W, so reload k rows (l2-normalised again)
-    for (int t = warp; t < kC; t += 8) {
-        float4 kk = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < n_valid) {
-            const int64_t qk_off = seq * p.qk_sseq + (t0 + t) * p.qk_st + static_cast<int64_t>(hk) * kD + 4 * lane;
-            kk = make_float4(load_act(p.k, qk_off, p.dtype), load_act(p.k, qk_off + 1, p.dtype),
-                             load_act(p.k, qk_off + 2, p.dtype), load_act(p.k, qk_off + 3, p.dtype));
-            if (p.l2_eps > 0.f) {
-                const float sk = warp_sum32(kk.x * kk.x + kk.y * kk.y + kk.z * kk.z + kk.w * kk.w);
-                const float fk = 1.0f / sqrtf(sk / 128.0f + p.l2_eps / 128.0f) / sqrtf(128.0f);
-                kk = make_float4(kk.x * fk, kk.y * fk, kk.z * fk, kk.w * fk);
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int s4 = 0; s4 < t; s4 += 4) {
+                const float4 a = *reinterpret_cast<const float4 *>(A + t * kLdA + s4);
+                float &ac = acc[(s4 >> 2) & 3];
+                ac = fmaf(a.x, x[s4], ac);
+                ac = fmaf(a.y, x[s4 + 1], ac);
+                ac = fmaf(a.z, x[s4 + 2], ac);
+                ac = fmaf(a.w, x[s4 + 3], ac);
             }
+            x[t] -= (acc[0] + acc[1]) + (acc[2] + acc[3]);
         }
-        const float f = expf(GC - G[t]);
-        *reinterpret_cast<float4 *>(wsc + kOffK + t * kD + 4 * lane) =
-            make_float4(kk.x * f, kk.y * f, kk.z * f, kk.w * f);
+        if (is_w) {  // W^T row col: 64 contiguous floats
+#pragma unroll
+            for (int t = 0; t < kC; t += 4)
+                *reinterpret_cast<float4 *>(wsc + kOffW + col * kC + t) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
+        } else {
+#pragma unroll
+            for (int t = 0; t < kC; ++t) wsc[kOffU + t * kD + col] = x[t];
+        }
     }
-    for (int e = tid; e < kC * kC; e += 256) wsc[kOffM + e] = Mq[(e >> 6) * (kC + 1) + (e & 63)];
-    if (tid == 0) wsc[kOffS] = expf(GC);
+    // Qs^T (threads 0..127) and K' (threads 128..255), from the tiles still in shared memory
+    {
+        const float GC = G[kC - 1];
+        const int col = tid & 127;
+        if (tid < kD) {
+            const float rsd = 1.0f / sqrtf(128.0f);
+#pragma unroll 4
+            for (int t = 0; t < kC; t += 4) {
+                float4 v;
+                v.x = Qs[t * kLd + col] * expf(G[t]) * rsd;
+                v.y = Qs[(t + 1) * kLd + col] * expf(G[t + 1]) * rsd;
+                v.z = Qs[(t + 2) * kLd + col] * expf(G[t + 2]) * rsd;
+                v.w = Qs[(t + 3) * kLd + col] * expf(G[t + 3]) * rsd;
+                *reinterpret_cast<float4 *>(wsc + kOffQ + col * kC + t) = v;
+            }
+        } else {
+            for (int t = 0; t < kC; ++t) wsc[kOffK + t * kD + col] = Ks[t * kLd + col] * expf(GC - G[t]);
+        }
+        for (int e = tid; e < kC * kC; e += 256) wsc[kOffM + e] = Mq[(e & 63) * (kC + 1) + (e >> 6)];
+        if (tid == 0) wsc[kOffS] = expf(GC);
+    }
 }
 
 // ---- phase 2: walk the chunks of one (sequence, head, 32 value columns) -------------
-// grid (kD / kJB, h_v, n_seqs), 256 threads, dynamic smem kScanSmem
-constexpr int kLdS = kJB + 1;
-constexpr size_t kScanSmem =
-    (static_cast<size_t>(kD) * kLdS + kC * kLdS + 3 * kC * kLd + kC * (kC + 1)) * sizeof(float);
+// grid (kD / kJB, h_v, n_seqs), 256 threads, dynamic smem kScanSmem.  The chunk tiles
+// are brought in by 1-D bulk copies (TMA, no multicast): W^T and Q^T of chunk c+1 as
+// soon as chunk c has used them, M^T and K' likewise.
+constexpr int kLdS = kJB + 2;  // S and Delta rows (float2 column pairs)
+constexpr size_t kScanFloats = static_cast<size_t>(kD) * kLdS + kC * kLdS + 3 * kD * kC + kC * kC;
+constexpr size_t kScanSmem = kScanFloats * sizeof(float) + 64;
+constexpr uint32_t kBytesWQ = 2 * kD * kC * sizeof(float);
+constexpr uint32_t kBytesMK = (kC * kC + kC * kD) * sizeof(float);
 
 __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
-    extern __shared__ float sm[];
-    float *S = sm;                  // [128][kLdS]   S[i][j] of this column block
-    float *Dl = S + kD * kLdS;      // [64][kLdS]    Delta
-    float *Wt = Dl + kC * kLdS;     // [64][kLd]
-    float *Qt = Wt + kC * kLd;      // [64][kLd]
-    float *Kt = Qt + kC * kLd;      // [64][kLd]
-    float *Mt = Kt + kC * kLd;      // [64][65]
+    extern __shared__ __align__(16) float sm[];
+    float *S = sm;                  // [128 i][kLdS]  state columns of this block
+    float *Dl = S + kD * kLdS;      // [64 t][kLdS]   Delta
+    float *WT = Dl + kC * kLdS;     // [128 i][64 t]
+    float *QT = WT + kD * kC;       // [128 i][64 t]  (contiguous after WT: one W|Q copy pair)
+    float *MT = QT + kD * kC;       // [64 s][64 t]
+    float *Kp = MT + kC * kC;       // [64 t][128 i]  (contiguous after MT)
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kScanFloats);  // [0] W|Q, [1] M|K'
+    __shared__ int abort_flag;
+    uint32_t *err = reinterpret_cast<uint32_t *>(p.ws);
     const int jb = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
     const int tid = threadIdx.x;
+    auto issue_wq = [&](int c) {
+        const float *w = chunk_ws(p, seq, h, c);
+        mbar_arrive_expect_tx(&bars[0], kBytesWQ);
+        bulk_g2s(WT, w + kOffW, kD * kC * sizeof(float), &bars[0]);
+        bulk_g2s(QT, w + kOffQ, kD * kC * sizeof(float), &bars[0]);
+    };
+    auto issue_mk = [&](int c) {
+        const float *w = chunk_ws(p, seq, h, c);
+        mbar_arrive_expect_tx(&bars[1], kBytesMK);
+        bulk_g2s(MT, w + kOffM, kC * kC * sizeof(float), &bars[1]);
+        bulk_g2s(Kp, w + kOffK, kC * kD * sizeof(float), &bars[1]);
+    };
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        issue_wq(0);
+        issue_mk(0);
+    }
     const int64_t plane_elems = static_cast<int64_t>(p.h_v) * kD * kD;
     float *st_seq = p.state + static_cast<int64_t>(seq) * p.n_planes * plane_elems;
     int plane = p.sel ? p.sel[seq] : 0;
     plane = min(max(plane, 0), p.n_planes - 1);
-    // S[i][j] at ((h*128 + j)*128 + i): thread loads column j rows i
+    // S[i][j] at ((h*128 + j)*128 + i)
     for (int e = tid; e < kD * kJB; e += 256) {
         const int j = e >> 7, i = e & 127;
         S[i * kLdS + j] = st_seq[plane * plane_elems + (static_cast<int64_t>(h) * kD + jb * kJB + j) * kD + i];
     }
-    // thread tiles: Delta / O: rows 4*(tid>>4)..+3, cols 2*(tid&15)..+1 (64 x 32 outputs)
+    __syncthreads();
+    // Delta / O tiles: rows r0..r0+3 (tokens), columns c0, c0+1; S tile: rows i0..i0+7
     const int r0 = 4 * (tid >> 4), c0 = 2 * (tid & 15);
-    // S update: rows 8*(tid>>4)..+7 (i), cols 2*(tid&15)..+1 (j) -> 16 outputs
     const int i0 = 8 * (tid >> 4);
-    for (int c = 0; c < p.n_chunks; ++c) {
-        const float *wsc = p.ws + ((static_cast<int64_t>(seq) * p.h_v + h) * p.n_chunks + c) * kChunkFloats;
-        __syncthreads();  // previous chunk finished with the tiles
-        for (int e = tid; e < kC * kD / 4; e += 256) {
-            const int t = e >> 5, i4 = (e & 31) * 4;
-            *reinterpret_cast<float4 *>(Wt + t * kLd + i4) = *reinterpret_cast<const float4 *>(wsc + kOffW + t * kD + i4);
-            *reinterpret_cast<float4 *>(Qt + t * kLd + i4) = *reinterpret_cast<const float4 *>(wsc + kOffQ + t * kD + i4);
-            *reinterpret_cast<float4 *>(Kt + t * kLd + i4) = *reinterpret_cast<const float4 *>(wsc + kOffK + t * kD + i4);
+    bool ok = true;
+    int last_wq = 0, last_mk = 0;  // chunk of the latest copies issued (thread 0)
+    // every thread takes the same branch after a wait (the loop has block barriers)
+    auto wait = [&](int which, int c) -> bool {
+        bool r = !abort_flag;
+        if (r && !mbar_wait(&bars[which], c & 1)) {
+            atomicOr(err, 1u);
+            abort_flag = 1;
+            r = false;
         }
-        for (int e = tid; e < kC * kC; e += 256) Mt[(e >> 6) * (kC + 1) + (e & 63)] = wsc[kOffM + e];
+        return __syncthreads_and(r) != 0;
+    };
+    int c = 0;
+    for (; c < p.n_chunks; ++c) {
+        const float *wsc = chunk_ws(p, seq, h, c);
         const float eGC = wsc[kOffS];
-        __syncthreads();
-        // Delta = U - W S0
-        {
-            float acc[4][2];
+        float2 u[4];
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
+        for (int a = 0; a < 4; ++a) u[a] = *reinterpret_cast<const float2 *>(wsc + kOffU + (r0 + a) * kD + jb * kJB + c0);
+        if (!wait(0, c)) { ok = false; break; }
+        // Delta = U - W S0 and the first part of O = Qs S0
+        float d[4][2], o[4][2];
 #pragma unroll
-                for (int b = 0; b < 2; ++b) acc[a][b] = wsc[kOffU + (r0 + a) * kD + jb * kJB + c0 + b];
-            for (int i = 0; i < kD; ++i) {
-                const float s0 = S[i * kLdS + c0], s1 = S[i * kLdS + c0 + 1];
-#pragma unroll
-                for (int a = 0; a < 4; ++a) {
-                    const float w = Wt[(r0 + a) * kLd + i];
-                    acc[a][0] = fmaf(-w, s0, acc[a][0]);
-                    acc[a][1] = fmaf(-w, s1, acc[a][1]);
-                }
-            }
-#pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 2; ++b) Dl[(r0 + a) * kLdS + c0 + b] = acc[a][b];
+        for (int a = 0; a < 4; ++a) {
+            d[a][0] = u[a].x;
+            d[a][1] = u[a].y;
+            o[a][0] = o[a][1] = 0.f;
         }
-        __syncthreads();
-        // O = Qs S0 + M Delta
-        {
-            float acc[4][2] = {};
-            for (int i = 0; i < kD; ++i) {
-                const float s0 = S[i * kLdS + c0], s1 = S[i * kLdS + c0 + 1];
-#pragma unroll
-                for (int a = 0; a < 4; ++a) {
-                    const float q = Qt[(r0 + a) * kLd + i];
-                    acc[a][0] = fmaf(q, s0, acc[a][0]);
-                    acc[a][1] = fmaf(q, s1, acc[a][1]);
-                }
-            }
-            for (int s = 0; s < kC; ++s) {
-                const float d0 = Dl[s * kLdS + c0], d1 = Dl[s * kLdS + c0 + 1];
-#pragma unroll
-                for (int a = 0; a < 4; ++a) {
-                    const float mv = Mt[(r0 + a) * (kC + 1) + s];
-                    acc[a][0] = fmaf(mv, d0, acc[a][0]);
-                    acc[a][1] = fmaf(mv, d1, acc[a][1]);
-                }
-            }
+#pragma unroll 4
+        for (int i = 0; i < kD; ++i) {
+            const float2 sv = *reinterpret_cast<const float2 *>(S + i * kLdS + c0);
+            const float4 w = *reinterpret_cast<const float4 *>(WT + i * kC + r0);
+            const float4 q = *reinterpret_cast<const float4 *>(QT + i * kC + r0);
+            const float wv[4] = {w.x, w.y, w.z, w.w}, qv[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int a = 0; a < 4; ++a) {
-                const int t = c * kC + r0 + a;
-                if (t < p.T) {
-#pragma unroll
-                    for (int b = 0; b < 2; ++b)
-                        p.out[((static_cast<int64_t>(seq) * p.T_all + t) * p.h_v + h) * kD + jb * kJB + c0 + b] =
-                            acc[a][b];
-                }
+                d[a][0] = fmaf(-wv[a], sv.x, d[a][0]);
+                d[a][1] = fmaf(-wv[a], sv.y, d[a][1]);
+                o[a][0] = fmaf(qv[a], sv.x, o[a][0]);
+                o[a][1] = fmaf(qv[a], sv.y, o[a][1]);
             }
         }
-        __syncthreads();  // S0 fully read
-        // S = e^{G_C} S0 + K'^T Delta
+#pragma unroll
+        for (int a = 0; a < 4; ++a) *reinterpret_cast<float2 *>(Dl + (r0 + a) * kLdS + c0) = make_float2(d[a][0], d[a][1]);
+        __syncthreads();  // Delta complete; S0, W and Q fully read
+        if (tid == 0 && c + 1 < p.n_chunks) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_wq(c + 1);
+            last_wq = c + 1;
+        }
+        if (!wait(1, c)) { ok = false; break; }
+        // O += M Delta
+#pragma unroll 4
+        for (int s2 = 0; s2 < kC; ++s2) {
+            const float2 dv = *reinterpret_cast<const float2 *>(Dl + s2 * kLdS + c0);
+            const float4 m = *reinterpret_cast<const float4 *>(MT + s2 * kC + r0);
+            const float mv[4] = {m.x, m.y, m.z, m.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                o[a][0] = fmaf(mv[a], dv.x, o[a][0]);
+                o[a][1] = fmaf(mv[a], dv.y, o[a][1]);
+            }
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const int t = c * kC + r0 + a;
+            if (t < p.T)
+                *reinterpret_cast<float2 *>(p.out + ((static_cast<int64_t>(seq) * p.T_all + t) * p.h_v + h) * kD +
+                                            jb * kJB + c0) = make_float2(o[a][0], o[a][1]);
+        }
+        // S = e^{G_C} S0 + K'^T Delta (each thread rewrites only its own entries)
         {
             float acc[8][2];
 #pragma unroll
             for (int a = 0; a < 8; ++a) {
-                acc[a][0] = eGC * S[(i0 + a) * kLdS + c0];
-                acc[a][1] = eGC * S[(i0 + a) * kLdS + c0 + 1];
+                const float2 sv = *reinterpret_cast<const float2 *>(S + (i0 + a) * kLdS + c0);
+                acc[a][0] = eGC * sv.x;
+                acc[a][1] = eGC * sv.y;
             }
+#pragma unroll 2
             for (int t = 0; t < kC; ++t) {
-                const float d0 = Dl[t * kLdS + c0], d1 = Dl[t * kLdS + c0 + 1];
+                const float2 dv = *reinterpret_cast<const float2 *>(Dl + t * kLdS + c0);
+                const float4 k0 = *reinterpret_cast<const float4 *>(Kp + t * kD + i0);
+                const float4 k1 = *reinterpret_cast<const float4 *>(Kp + t * kD + i0 + 4);
+                const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
                 for (int a = 0; a < 8; ++a) {
-                    const float kv = Kt[t * kLd + i0 + a];
-                    acc[a][0] = fmaf(kv, d0, acc[a][0]);
-                    acc[a][1] = fmaf(kv, d1, acc[a][1]);
+                    acc[a][0] = fmaf(kv[a], dv.x, acc[a][0]);
+                    acc[a][1] = fmaf(kv[a], dv.y, acc[a][1]);
                 }
             }
 #pragma unroll
-            for (int a = 0; a < 8; ++a) {
-                S[(i0 + a) * kLdS + c0] = acc[a][0];
-                S[(i0 + a) * kLdS + c0 + 1] = acc[a][1];
-            }
+            for (int a = 0; a < 8; ++a)
+                *reinterpret_cast<float2 *>(S + (i0 + a) * kLdS + c0) = make_float2(acc[a][0], acc[a][1]);
         }
+        __syncthreads();  // M, K' and Delta fully read; S updated
+        if (tid == 0 && c + 1 < p.n_chunks) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_mk(c + 1);
+            last_mk = c + 1;
+        }
+    }
+    if (!ok) {
+        // never exit with a bulk copy still writing into shared memory
+        if (tid == 0) {
+            mbar_wait(&bars[0], last_wq & 1);
+            mbar_wait(&bars[1], last_mk & 1);
+        }
+        return;
     }
     __syncthreads();
     for (int e = tid; e < kD * kJB; e += 256) {
@@ -357,7 +436,7 @@ using namespace sqmix;
 extern "C" size_t sqmix_gdn_prefill_workspace_bytes(int32_t n_seqs, int32_t n_tokens, int32_t h_v) {
     if (n_seqs < 1 || n_tokens < 1 || h_v < 1) return 0;
     const int64_t n_chunks = (n_tokens + kC - 1) / kC;
-    return static_cast<size_t>(n_seqs) * h_v * n_chunks * kChunkFloats * sizeof(float);
+    return (kWsHeaderFloats + static_cast<size_t>(n_seqs) * h_v * n_chunks * kChunkFloats) * sizeof(float);
 }
 
 extern "C" int sqmix_gdn_prefill(const sqmix_gdn_args *a, void *workspace, size_t workspace_bytes,
@@ -380,6 +459,15 @@ extern "C" int sqmix_gdn_prefill(const sqmix_gdn_args *a, void *workspace, size_
     SQMIX_CHECK_ARG((reinterpret_cast<uintptr_t>(a->state) & 15) == 0 &&
                         (reinterpret_cast<uintptr_t>(workspace) & 15) == 0,
                     "gdn_prefill: state and workspace must be 16-byte aligned");
+    SQMIX_CHECK_ARG(a->qk_stride_tok % 4 == 0 && a->qk_stride_seq % 4 == 0 && a->v_stride_tok % 4 == 0 &&
+                        a->v_stride_seq % 4 == 0,
+                    "gdn_prefill: q/k/v strides must be multiples of 4 elements");
+    {
+        const uintptr_t align = a->dtype == SQMIX_F32 ? 15 : 7;
+        SQMIX_CHECK_ARG(((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k) |
+                          reinterpret_cast<uintptr_t>(a->v)) & align) == 0,
+                        "gdn_prefill: q/k/v base pointers must be %d-byte aligned", (int)align + 1);
+    }
     const size_t need = sqmix_gdn_prefill_workspace_bytes(a->n_seqs, a->n_tokens, a->h_v);
     if (workspace_bytes < need) {
         set_error("gdn_prefill: workspace %zu bytes < %zu needed", workspace_bytes, need);

@@ -274,7 +274,7 @@ def gated_delta_net(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.
     if chunked:
         need = gdn_prefill_workspace_bytes(n_seqs, T, H_v)
         if workspace is None or workspace.numel() < need:
-            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+            workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
         check(lib().sqmix_gdn_prefill(ctypes.byref(a), _ptr(workspace), workspace.numel(), _stream(stream)),
               "gated_delta_net (chunked)")
     else:
