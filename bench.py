@@ -198,9 +198,11 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    n_local = N_KV // world
-    assert n_local * world == N_KV
-    cap = (n_local + 255) // 256 * 256
+    from sqmix import split_kv
+
+    shard = split_kv.plan(N_KV, world, rank)  # this rank's contiguous key slice
+    n_local, k0 = shard.length, shard.start
+    cap = shard.capacity
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
 
@@ -216,17 +218,17 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             vv = torch.randn((n, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
             rows = torch.arange(a, a + n, device=dev)
             sqmix.set_rows_q4_0(kk, vv, rows, kc[l], vc[l], cap, rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE,
-                                rope_pos_offset=rank * n_local)
+                                rope_pos_offset=k0)
     # the new token is written at the last position of the last rank's slice
-    owner = world - 1
     pos_new = N_KV - 1
-    local_row = pos_new - owner * n_local
+    owner = split_kv.owner(N_KV, world, pos_new)
+    local_row = pos_new - split_kv.plan(N_KV, world, owner).start
     q = torch.randn((N_LAYERS, 1, N_HEAD, HEAD_DIM), generator=g, device=dev)
     gate = torch.randn((N_LAYERS, 1, N_HEAD, HEAD_DIM), generator=g, device=dev)
     k_new = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
     v_new = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
     out = torch.empty((N_LAYERS, 1, N_HEAD, HEAD_DIM), device=dev)
-    step = torch.tensor([n_local, pos_new - rank * n_local], dtype=torch.int64, device=dev)
+    step = torch.tensor(list(shard.local_step(N_KV, pos_new)), dtype=torch.int64, device=dev)
     d_nkv, d_qpos = step[0:1], step[1:2]
     d_row = torch.tensor([local_row], dtype=torch.int64, device=dev)
     n_splits = sqmix.lib().sqmix_device_sm_count(local_rank)
@@ -244,12 +246,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     def layer(l):
         if world == 1:
             sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=gate[l], rope_n_rot=N_ROT,
-                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=out[l],
+                                 rope_freq_base=FREQ_BASE, rope_pos_offset=k0, out=out[l],
                                  workspace=ws, n_splits=n_splits, k_new=k_new[l], v_new=v_new[l],
                                  overlap_prev=True)
         else:
             sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=None, rope_n_rot=N_ROT,
-                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=o_loc[l],
+                                 rope_freq_base=FREQ_BASE, rope_pos_offset=k0, out=o_loc[l],
                                  lse=l_loc[l], workspace=ws, n_splits=n_splits,
                                  k_new=k_new[l] if own else None, v_new=v_new[l] if own else None,
                                  overlap_prev=True)
@@ -300,7 +302,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     us_per_token = ms * 1e3 / args.steps
-    launches_per_step = N_LAYERS * (1 + (1 if world > 1 else 0))  # fused decode (+ merge_lse)
+    # per layer: decode + split merge (PDL pair), plus the cross-rank merge_lse for N > 1
+    launches_per_step = N_LAYERS * (2 + (1 if world > 1 else 0))
 
     # ---- dominant kernel alone: flash_attn_ext over each layer in turn ---------
     e0 = torch.cuda.Event(enable_timing=True)
@@ -310,7 +313,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     def fa_only():
         for l in range(N_LAYERS):
             sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=gate[l], rope_n_rot=N_ROT,
-                                 rope_freq_base=FREQ_BASE, rope_pos_offset=rank * n_local, out=out[l],
+                                 rope_freq_base=FREQ_BASE, rope_pos_offset=k0, out=out[l],
                                  workspace=ws, n_splits=n_splits, overlap_prev=True)
     s2 = torch.cuda.Stream()
     s2.wait_stream(stream)
@@ -331,6 +334,43 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     g_fa = None
     fa_us = e0.elapsed_time(e1) * 1e3 / (reps * N_LAYERS)
     sqmix.fa_status(ws)
+
+    # ---- MTP verify (config 3's 2-token query) over the same caches ------------
+    mtp = None
+    if world == 1:
+        q2 = torch.randn((N_LAYERS, 2, N_HEAD, HEAD_DIM), generator=g, device=dev)
+        gate2 = torch.randn((N_LAYERS, 2, N_HEAD, HEAD_DIM), generator=g, device=dev)
+        out2 = torch.empty((N_LAYERS, 2, N_HEAD, HEAD_DIM), device=dev)
+        step2 = torch.tensor([n_local, n_local - 2], dtype=torch.int64, device=dev)
+        ws2 = sqmix.new_fa_workspace(2, n_splits, dev)
+
+        def mtp_step():
+            for l in range(N_LAYERS):
+                sqmix.flash_attn_ext(q2[l], kc[l], vc[l], cap, step2[0:1], step2[1:2], gate=gate2[l],
+                                     rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE, out=out2[l], workspace=ws2,
+                                     n_splits=n_splits, overlap_prev=True)
+        s3 = torch.cuda.Stream()
+        s3.wait_stream(stream)
+        with torch.cuda.stream(s3):
+            mtp_step()
+        stream.wait_stream(s3)
+        torch.cuda.synchronize()
+        g_mtp = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_mtp):
+            mtp_step()
+        g_mtp.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            g_mtp.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        mtp_us = e0.elapsed_time(e1) * 1e3 / reps
+        g_mtp = None
+        sqmix.fa_status(ws2)
+        mtp = {"us_per_step": mtp_us, "query_tokens": 2,
+               "achieved_gbs": N_LAYERS * (n_local * BYTES_PER_KEY + 6 * N_HEAD * HEAD_DIM * 4) / mtp_us / 1e3,
+               "note": "10 layers x 172032 keys, n_q = 2 (MTP verification query), CUDA graph, no append"}
     alg_bytes = n_local * BYTES_PER_KEY + 3 * N_HEAD * HEAD_DIM * 4
     hbm, peak_kind = peaks()
     achieved = alg_bytes / (fa_us * 1e-6) / 1e9
@@ -341,7 +381,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     h_k = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM)).pin_memory()
     h_v = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM)).pin_memory()
     h_out = torch.empty((N_LAYERS, 1, N_HEAD, HEAD_DIM)).pin_memory()
-    h_step = torch.tensor([n_local, pos_new - rank * n_local], dtype=torch.int64).pin_memory()
+    h_step = torch.tensor(list(shard.local_step(N_KV, pos_new)), dtype=torch.int64).pin_memory()
     h2d = (h_q.numel() + h_gate.numel()) * 4 + (h_k.numel() + h_v.numel()) * 4 * (1 if rank == owner else 0) + 16
     d2h = h_out.numel() * 4
 
@@ -398,6 +438,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         "gpu_launches": launches_per_step * args.steps,
         "e2e": {"value": e2e_us, "unit": "us/token", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
     }
+    if mtp is not None:
+        res["mtp_verify"] = mtp
     return res
 
 

@@ -172,3 +172,23 @@ def gdn(q, k, v, g, beta, state, n_snap: int = 1):
     lib().oracle_gdn(qp, kp, vp, gp, bp, sp, T, Hk, Hv, d, int(n_snap),
                      out.ctypes.data_as(f32p), snaps.ctypes.data_as(f32p))
     return out, snaps
+
+
+def merge_lse(o_parts, lse_parts, gate=None):
+    """Merge normalised partial attentions over disjoint key sets (split-KV):
+    out = sum_p O_p exp(lse_p - L) with L = log sum_p exp(lse_p), then * sigmoid(gate).
+    o_parts [P][rows][D], lse_parts [P][rows]; parts with lse = -inf carry no weight.
+    Restates the merge of the split-KV decode (the LSE combination of flash-decoding)."""
+    o = np.asarray(o_parts, dtype=np.float64)
+    lse = np.asarray(lse_parts, dtype=np.float64)
+    L = np.max(lse, axis=0)
+    finite = np.isfinite(L)
+    Ls = np.where(finite, L, 0.0)
+    w = np.where(np.isfinite(lse), np.exp(lse - Ls[None]), 0.0)
+    tot = w.sum(axis=0)
+    out = (o * w[..., None]).sum(axis=0) / np.where(tot > 0, tot, 1.0)[..., None]
+    out = np.where(finite[..., None], out, 0.0)
+    if gate is not None:
+        out = out / (1.0 + np.exp(-np.asarray(gate, dtype=np.float64)))
+    lse_out = np.where(finite, Ls + np.log(np.where(tot > 0, tot, 1.0)), -np.inf)
+    return out.astype(np.float32), lse_out.astype(np.float32)
