@@ -236,10 +236,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     torch.cuda.synchronize()
 
     if world > 1:
-        o_loc = torch.empty((N_LAYERS, N_HEAD, HEAD_DIM), device=dev)
-        l_loc = torch.empty((N_LAYERS, N_HEAD), device=dev)
-        o_all = torch.empty((world, N_HEAD, HEAD_DIM), device=dev)
-        l_all = torch.empty((world, N_HEAD), device=dev)
+        # (O, LSE) partials packed per layer so that one all-gather moves both
+        rows = N_HEAD
+        pk_loc = torch.empty((N_LAYERS, rows * (HEAD_DIM + 1)), device=dev)
+        pk_all = torch.empty((world, rows * (HEAD_DIM + 1)), device=dev)
+        o_loc = [pk_loc[l, :rows * HEAD_DIM].view(1, N_HEAD, HEAD_DIM) for l in range(N_LAYERS)]
+        l_loc = [pk_loc[l, rows * HEAD_DIM:].view(1, N_HEAD) for l in range(N_LAYERS)]
 
     own = rank == owner  # the rank whose key slice holds the new token appends it (fused)
 
@@ -255,9 +257,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                  lse=l_loc[l], workspace=ws, n_splits=n_splits,
                                  k_new=k_new[l] if own else None, v_new=v_new[l] if own else None,
                                  overlap_prev=True)
-            dist.all_gather_into_tensor(o_all, o_loc[l])
-            dist.all_gather_into_tensor(l_all, l_loc[l])
-            sqmix.attn_merge_lse(o_all, l_all, gate=gate[l, 0], out=out[l, 0])
+            dist.all_gather_into_tensor(pk_all, pk_loc[l])
+            sqmix.attn_merge_lse(pk_all[:, :rows * HEAD_DIM].view(world, rows, HEAD_DIM),
+                                 pk_all[:, rows * HEAD_DIM:], gate=gate[l, 0], out=out[l, 0])
 
     def step_fn():
         for l in range(N_LAYERS):
@@ -265,7 +267,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
     stream = torch.cuda.current_stream()
     graph = None
-    if world == 1 and not args.no_graph:
+    if not args.no_graph:  # N > 1: the NCCL all-gathers are captured too
         s = torch.cuda.Stream()
         s.wait_stream(stream)
         with torch.cuda.stream(s):
