@@ -573,6 +573,34 @@ def bench_gdn(steps: int, warmup: int):
                      "frac_of_hbm": alg / us / 1e3 / hbm, "peak_gbs": hbm, "peak_kind": hbm_kind,
                      "note": "CUDA graph of 96 single-token layer updates (states cycled through HBM)"}
     del graph, S
+    # batched decode (config 4's 64 sequences, one token each): 64 x 4.2 MB per layer
+    nb, n_lb = 64, 4
+    Sb = torch.randn((n_lb, nb, 1, 32, 128, 128), generator=g, device=dev) * 0.02
+    qb = torch.randn((nb, 1, 16, 128), generator=g, device=dev).to(torch.bfloat16)
+    kb = torch.randn((nb, 1, 16, 128), generator=g, device=dev).to(torch.bfloat16)
+    vb = torch.randn((nb, 1, 32, 128), generator=g, device=dev).to(torch.bfloat16)
+    gb = -torch.rand((nb, 1, 32), generator=g, device=dev)
+    bb = torch.rand((nb, 1, 32), generator=g, device=dev)
+    ob = torch.empty((nb, 1, 32, 128), device=dev)
+
+    def decode_batch():
+        for l in range(n_lb):
+            sqmix.gated_delta_net(qb, kb, vb, gb, bb, Sb[l], l2_eps=1e-6, out=ob)
+
+    for _ in range(max(warmup, 3)):
+        decode_batch()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        decode_batch()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * n_lb)
+    algb = nb * alg
+    res["decode_batch64"] = {"us_per_layer": us, "alg_bytes": algb, "achieved_gbs": algb / us / 1e3,
+                             "frac_of_hbm": algb / us / 1e3 / hbm, "peak_gbs": hbm, "peak_kind": hbm_kind,
+                             "note": "64 sequences x 1 token per launch (config 4 shape), 4 layer states cycled"}
+    del Sb
     T = 512
     S, q, k, v, gg, beta = gdn_inputs(g, dev, T, 1)
     out = torch.empty((1, T, 32, 128), device=dev)

@@ -69,23 +69,35 @@ __device__ __forceinline__ float4 l2norm4(float4 x, float eps) {
     return make_float4(x.x * s * s2, x.y * s * s2, x.z * s * s2, x.w * s * s2);
 }
 
-// grid: (n_seqs * h_v * 128 / 8), block 256: warp -> (seq, head, column j).
+// grid: (n_seqs * h_v * 128 / JW / 8), block 256: warp -> (seq, head, JW consecutive
+// value columns).  q, k, their norms and k.q are shared by the warp's columns; each
+// lane keeps keys 4*lane..4*lane+3 of every column, so a warp has JW 16-byte loads
+// in flight per lane (more columns per warp where there is enough work to spread).
+template <int JW>
 __global__ void __launch_bounds__(256) gdn_recurrent_kernel(GdnParams p) {
     const int lane = threadIdx.x & 31;
     const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-    const int j = static_cast<int>(wid & 127);
-    const int64_t hs = wid >> 7;
+    constexpr int kGroups = 128 / JW;
+    const int j0 = static_cast<int>(wid % kGroups) * JW;
+    const int64_t hs = wid / kGroups;
     const int h = static_cast<int>(hs % p.h_v);
     const int64_t seq = hs / p.h_v;
     if (seq >= p.n_seqs) return;
     const int hk = h % p.h_k;
+    // launched with programmatic stream serialisation: the launch overlaps the tail of
+    // the kernel before it; everything below may depend on that kernel's results
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
 
     int plane = p.sel ? p.sel[seq] : p.plane0;
     plane = min(max(plane, 0), p.n_planes - 1);
     const int64_t plane_elems = static_cast<int64_t>(p.h_v) * 128 * 128;
     float *st_seq = p.state + seq * p.n_planes * plane_elems;
-    const int64_t col_off = (static_cast<int64_t>(h) * 128 + j) * 128 + 4 * lane;
-    float4 S = *reinterpret_cast<const float4 *>(st_seq + plane * plane_elems + col_off);
+    const int64_t col_off = (static_cast<int64_t>(h) * 128 + j0) * 128 + 4 * lane;  // column j0
+    float4 S[JW];
+#pragma unroll
+    for (int c = 0; c < JW; ++c)
+        S[c] = *reinterpret_cast<const float4 *>(st_seq + plane * plane_elems + col_off + c * 128);
 
     const float inv_sqrt_d = 1.0f / sqrtf(128.0f);
     for (int t = 0; t < p.T; ++t) {
@@ -100,30 +112,51 @@ __global__ void __launch_bounds__(256) gdn_recurrent_kernel(GdnParams p) {
         const int64_t gb = (seq * p.T_all + tt) * p.h_v + h;
         const float decay = expf(p.g[gb]);
         const float bt = p.beta[gb];
-        const float vj = load_act(p.v, seq * p.v_sseq + tt * p.v_st + static_cast<int64_t>(h) * 128 + j, p.dtype);
-        S.x *= decay;
-        S.y *= decay;
-        S.z *= decay;
-        S.w *= decay;
-        float skv = S.x * kk.x + S.y * kk.y + S.z * kk.z + S.w * kk.w;
-        float sq = S.x * qq.x + S.y * qq.y + S.z * qq.z + S.w * qq.w;
+        const int64_t v_off = seq * p.v_sseq + tt * p.v_st + static_cast<int64_t>(h) * 128 + j0;
+        float vj[JW];
+#pragma unroll
+        for (int c = 0; c < JW; ++c) vj[c] = load_act(p.v, v_off + c, p.dtype);
+        float skv[JW], sq[JW];
+#pragma unroll
+        for (int c = 0; c < JW; ++c) {
+            S[c].x *= decay;
+            S[c].y *= decay;
+            S[c].z *= decay;
+            S[c].w *= decay;
+            skv[c] = S[c].x * kk.x + S[c].y * kk.y + S[c].z * kk.z + S[c].w * kk.w;
+            sq[c] = S[c].x * qq.x + S[c].y * qq.y + S[c].z * qq.z + S[c].w * qq.w;
+        }
         float kq = kk.x * qq.x + kk.y * qq.y + kk.z * qq.z + kk.w * qq.w;
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) {
-            skv += __shfl_xor_sync(0xffffffffu, skv, off);
-            sq += __shfl_xor_sync(0xffffffffu, sq, off);
+#pragma unroll
+            for (int c = 0; c < JW; ++c) {
+                skv[c] += __shfl_xor_sync(0xffffffffu, skv[c], off);
+                sq[c] += __shfl_xor_sync(0xffffffffu, sq[c], off);
+            }
             kq += __shfl_xor_sync(0xffffffffu, kq, off);
         }
-        const float delta = (vj - skv) * bt;
-        S.x = fmaf(kk.x, delta, S.x);
-        S.y = fmaf(kk.y, delta, S.y);
-        S.z = fmaf(kk.z, delta, S.z);
-        S.w = fmaf(kk.w, delta, S.w);
-        if (lane == 0)
-            p.out[((seq * p.T_all + tt) * p.h_v + h) * 128 + j] = fmaf(delta, kq, sq) * inv_sqrt_d;
+        float o[JW];
+#pragma unroll
+        for (int c = 0; c < JW; ++c) {
+            const float delta = (vj[c] - skv[c]) * bt;
+            S[c].x = fmaf(kk.x, delta, S[c].x);
+            S[c].y = fmaf(kk.y, delta, S[c].y);
+            S[c].z = fmaf(kk.z, delta, S[c].z);
+            S[c].w = fmaf(kk.w, delta, S[c].w);
+            o[c] = fmaf(delta, kq, sq[c]) * inv_sqrt_d;
+        }
+        if (lane == 0) {
+            float *orow = p.out + ((seq * p.T_all + tt) * p.h_v + h) * 128 + j0;
+#pragma unroll
+            for (int c = 0; c < JW; ++c) orow[c] = o[c];
+        }
         const int slot = p.T - 1 - t;
-        if (slot < p.n_snap)
-            *reinterpret_cast<float4 *>(st_seq + slot * plane_elems + col_off) = S;
+        if (slot < p.n_snap) {
+#pragma unroll
+            for (int c = 0; c < JW; ++c)
+                *reinterpret_cast<float4 *>(st_seq + slot * plane_elems + col_off + c * 128) = S[c];
+        }
     }
 }
 
@@ -162,9 +195,29 @@ int gdn_launch_recurrent(const sqmix_gdn_args *a, int plane_in, int64_t tok_off,
     p.n_snap = n_snap;
     p.l2_eps = a->l2_eps;
     p.out = a->out;
-    const int64_t warps = static_cast<int64_t>(a->n_seqs) * a->h_v * 128;
-    gdn_recurrent_kernel<<<static_cast<unsigned>(warps / 8), 256, 0, st>>>(p);
-    return cuda_status(cudaGetLastError(), "gdn recurrent launch");
+    // columns per warp: as many as keep about two waves of resident warps busy
+    const int64_t cols = static_cast<int64_t>(a->n_seqs) * a->h_v * 128;
+    const int64_t resident = static_cast<int64_t>(sqmix_device_sm_count(-1)) * 64;
+    const int jw = cols / 8 >= 2 * resident ? 8 : cols / 4 >= 2 * resident ? 4 : cols / 2 >= 2 * resident ? 2 : 1;
+    const int64_t warps = cols / jw;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(warps / 8));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    switch (jw) {
+        case 8: e = cudaLaunchKernelEx(&cfg, gdn_recurrent_kernel<8>, p); break;
+        case 4: e = cudaLaunchKernelEx(&cfg, gdn_recurrent_kernel<4>, p); break;
+        case 2: e = cudaLaunchKernelEx(&cfg, gdn_recurrent_kernel<2>, p); break;
+        default: e = cudaLaunchKernelEx(&cfg, gdn_recurrent_kernel<1>, p); break;
+    }
+    return cuda_status(e, "gdn recurrent launch");
 }
 }  // namespace sqmix
 
