@@ -193,6 +193,50 @@ int sqmix_fa_status(void *workspace, sqmix_stream_t stream);
 size_t sqmix_fa_prefill_workspace_bytes(int32_t n_q, int32_t n_ctas);
 int sqmix_fa_prefill(const sqmix_fa_args *args, sqmix_stream_t stream);
 
+/* Sequence-batched decode (the batched decode step of many independent sequences,
+ * one query token each; the engine's per-sequence ggml_flash_attn_ext calls,
+ * attn.rs:238-249).  Sequence s uses tiled caches k_caches[s] / v_caches[s] with
+ * capacities[s] rows, device scalars n_kv[s], q_pos0[s], query q + s*q_stride_seq
+ * ([16][256]), gate likewise, output out + s*4096 ([16][256] f32) and lse + s*16.
+ * k_new/v_new (n_new = 1): [n_seqs][2][256] with new_stride_seq, written at row
+ * q_pos0[s] first.  The pointer and scalar arrays live in device memory.  Split
+ * partials of all sequences share the workspace (sqmix_fa_batch_workspace_bytes, first
+ * 256 bytes zero before first use).  splits_per_seq 0 = about 4 CTAs per SM over the
+ * batch.  flags as for sqmix_fa_decode. */
+typedef struct sqmix_fa_batch_args {
+    int32_t n_seqs;
+    const void *q;
+    int32_t q_dtype;
+    int64_t q_stride_seq;
+    int64_t q_stride_head;
+    const void *gate;         /* nullable */
+    int32_t gate_dtype;
+    int64_t gate_stride_seq;
+    int64_t gate_stride_head;
+    const void *const *k_caches;
+    const void *const *v_caches;
+    const int64_t *capacities;
+    const int64_t *n_kv;
+    const int64_t *q_pos0;
+    float scale;
+    int32_t rope_n_rot;
+    float rope_freq_base;
+    float *out;
+    float *lse;               /* nullable */
+    void *workspace;
+    size_t workspace_bytes;
+    int32_t splits_per_seq;
+    const void *k_new;
+    const void *v_new;
+    int32_t kv_new_dtype;
+    int64_t new_stride_seq;
+    int32_t n_new;
+    int32_t flags;
+} sqmix_fa_batch_args;
+
+size_t sqmix_fa_batch_workspace_bytes(int32_t n_seqs, int32_t splits_per_seq);
+int sqmix_fa_decode_batch(const sqmix_fa_batch_args *args, sqmix_stream_t stream);
+
 /* sqmix_fa_decode without a caller workspace (no reference counterpart: ggml_flash_attn_ext
  * takes its scratch from ggml's graph allocator).  For callers that cannot allocate
  * device memory at the call site, e.g. a callback inside a graph executor whose buffers

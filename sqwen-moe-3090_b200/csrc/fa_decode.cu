@@ -69,6 +69,13 @@ struct FaDecodeParams {
     float *part_ml;  // [splits][nq][16][2]
     uint32_t *err;
     int overlap_prev;  // SQMIX_FA_OVERLAP_PREV: prefetch before the grid dependency wait
+    // sequence batch (sqmix_fa_decode_batch; blockIdx.y = sequence).  NULL arrays: one
+    // sequence with k_cache / v_cache / capacity above.
+    const uint8_t *const *k_caches;
+    const uint8_t *const *v_caches;
+    const int64_t *caps;
+    int64_t q_sseq;    // elements between sequences of q
+    int64_t new_sseq;  // elements between sequences of k_new / v_new
 };
 
 template <int NQ, int WPH, int GPW, int NSTAGE, int MINB>
@@ -209,13 +216,19 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     // Without SQMIX_FA_OVERLAP_PREV nothing is read before the previous kernel is done.
     if (!p.overlap_prev) grid_dependency_wait();
 
+    // ---- this CTA's sequence (a batch launch has one grid row per sequence) -------
+    const int seq = blockIdx.y;
+    uint8_t *const kcache = p.k_caches ? const_cast<uint8_t *>(p.k_caches[seq]) : p.k_cache;
+    uint8_t *const vcache = p.v_caches ? const_cast<uint8_t *>(p.v_caches[seq]) : p.v_cache;
+    const int64_t capacity = p.caps ? p.caps[seq] : p.capacity;
+
     // ---- work range: a contiguous run of 16-token groups ---------------------
-    int64_t n_kv = *p.n_kv;
-    if (n_kv > p.capacity) {
+    int64_t n_kv = p.n_kv[seq];
+    if (n_kv > capacity) {
         if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(p.err, 8u);
-        n_kv = p.capacity;
+        n_kv = capacity;
     }
-    const int64_t q_pos0 = *p.q_pos0;
+    const int64_t q_pos0 = p.q_pos0[seq];
     int64_t n_keys = q_pos0 + NQ;  // causal: query NQ-1 sees keys <= q_pos0 + NQ - 1
     if (n_keys > n_kv) n_keys = n_kv;
     if (n_keys < 0) n_keys = 0;
@@ -257,8 +270,8 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
         const uint32_t bytes = static_cast<uint32_t>(ng) * kGroupBytes;
         mbar_arrive_expect_tx(&full_bar[s], 2 * bytes);
         uint8_t *dst = ring + s * L::kStageBytes;
-        bulk_g2s(dst, p.k_cache + gr0 * kGroupBytes, bytes, &full_bar[s]);
-        bulk_g2s(dst + L::kTileBytes, p.v_cache + gr0 * kGroupBytes, bytes, &full_bar[s]);
+        bulk_g2s(dst, kcache + gr0 * kGroupBytes, bytes, &full_bar[s]);
+        bulk_g2s(dst + L::kTileBytes, vcache + gr0 * kGroupBytes, bytes, &full_bar[s]);
     };
     constexpr int kStagingBytes = (NQ * 16 * 256 + NQ * 2 * 512) * 4;
     constexpr int kStagingSlots = (kStagingBytes + L::kStageBytes - 1) / L::kStageBytes;
@@ -295,7 +308,8 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
 #pragma unroll
     for (int k = 0; k < kQPer; ++k) {
         const int e = threadIdx.x + k * L::kThreads;  // [qi][head][256]
-        qv[k] = load_act(p.q, (e >> 12) * p.q_st + ((e >> 8) & 15) * p.q_sh + (e & 255), p.q_dtype);
+        qv[k] = load_act(p.q, seq * p.q_sseq + (e >> 12) * p.q_st + ((e >> 8) & 15) * p.q_sh + (e & 255),
+                         p.q_dtype);
     }
     constexpr int kKvPer = NQ * 2 * 512 / L::kThreads;
     float kvv[kKvPer];
@@ -305,7 +319,8 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
             const int e = threadIdx.x + k * L::kThreads;  // [t][k|v][512]
             const int t = e >> 10, is_v = (e >> 9) & 1;
             kvv[k] = t < p.n_new ? load_act(is_v ? p.v_new : p.k_new,
-                                            t * (is_v ? p.v_new_st : p.k_new_st) + (e & 511), p.kv_dtype)
+                                            seq * p.new_sseq + t * (is_v ? p.v_new_st : p.k_new_st) + (e & 511),
+                                            p.kv_dtype)
                                  : 0.f;
         }
     }
@@ -346,7 +361,7 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
             if (row < row_lo || row >= row_hi) continue;  // another CTA's row
             const float x = kv_row_elem(kv_stage, ((t * 2 + is_v) * 2 + h) * 256, b * 32 + lane, SQMIX_F32,
                                         is_v ? 0 : p.rope_n_rot, rope_s + t * 32);
-            q4_0_store_block(x, lane, is_v ? p.v_cache : p.k_cache, row, h, b, is_v);
+            q4_0_store_block(x, lane, is_v ? vcache : kcache, row, h, b, is_v);
         }
         // the bulk copies (async proxy) that stream these rows must see the stores
         asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -701,8 +716,9 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
         wrow[WPH + 1] = lsum;
     }
     __syncthreads();
-    float *po = p.part_o + static_cast<size_t>(blockIdx.x) * NQ * 16 * 256;
-    float *pml = p.part_ml + static_cast<size_t>(blockIdx.x) * NQ * 16 * 2;
+    const size_t split = static_cast<size_t>(seq) * gridDim.x + blockIdx.x;
+    float *po = p.part_o + split * NQ * 16 * 256;
+    float *pml = p.part_ml + split * NQ * 16 * 2;
     for (int i = threadIdx.x; i < NQ * 16 * 256; i += L::kThreads) {
         const int d = i & 255;
         const int head = (i >> 8) & 15;
@@ -737,14 +753,23 @@ struct FaMergeParams {
     float scale;
     float *out;
     float *lse;
+    int64_t g_sseq;  // gate elements between sequences (batch: blockIdx.z = sequence)
 };
 
 __global__ void __launch_bounds__(256) fa_merge_kernel(FaMergeParams p) {
     __shared__ float red[8 * 34];
     grid_dependency_wait();
     launch_dependents();
-    merge_slice(p.part_o, p.part_ml, p.n_splits, p.n_rows, blockIdx.x, blockIdx.y, p.c, p.scale, p.gate,
-                p.gate_dtype, p.g_st, p.g_sh, p.out, p.lse, red, 8);
+    const size_t seq = blockIdx.z;
+    const size_t parts = seq * p.n_splits * p.n_rows;
+    const void *gate = p.gate;
+    if (gate && seq) {
+        const int esz = p.gate_dtype == SQMIX_F32 ? 4 : 2;
+        gate = static_cast<const uint8_t *>(gate) + seq * p.g_sseq * esz;
+    }
+    merge_slice(p.part_o + parts * 256, p.part_ml + parts * 2, p.n_splits, p.n_rows, blockIdx.x, blockIdx.y, p.c,
+                p.scale, gate, p.gate_dtype, p.g_st, p.g_sh, p.out + seq * p.n_rows * 256,
+                p.lse ? p.lse + seq * p.n_rows : nullptr, red, 8);
 }
 
 // Merge of normalised partials across GPUs: O = sum_p O_p e^(lse_p - L).
@@ -787,8 +812,17 @@ extern "C" size_t sqmix_fa_workspace_bytes(int32_t n_splits, int32_t n_q) {
     return fa_ws_layout(n_splits, n_q, &a, &b);
 }
 
+// Sequence batch of one launch (sqmix_fa_decode_batch); the default is one sequence.
+struct FaBatch {
+    int n_seqs = 1;
+    const uint8_t *const *k_caches = nullptr;
+    const uint8_t *const *v_caches = nullptr;
+    const int64_t *caps = nullptr;
+    int64_t q_sseq = 0, new_sseq = 0, g_sseq = 0;
+};
+
 template <int NQ, int WPH, int GPW, int NSTAGE, int MINB>
-static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st) {
+static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, const FaBatch &bt = FaBatch()) {
     using L = FaCfg<NQ, WPH, GPW, NSTAGE, MINB>;
     auto kernel = fa_decode_kernel<NQ, WPH, GPW, NSTAGE, MINB>;
     static bool attr_set = false;
@@ -798,7 +832,7 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st) {
         attr_set = true;
     }
     size_t off_ml, off_o;
-    fa_ws_layout(n_splits, NQ, &off_ml, &off_o);
+    fa_ws_layout(n_splits * bt.n_seqs, NQ, &off_ml, &off_o);
     uint8_t *ws = static_cast<uint8_t *>(a->workspace);
     FaDecodeParams p;
     p.q = a->q;
@@ -826,6 +860,11 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st) {
     p.part_ml = reinterpret_cast<float *>(ws + off_ml);
     p.err = reinterpret_cast<uint32_t *>(ws);
     p.overlap_prev = (a->flags & SQMIX_FA_OVERLAP_PREV) != 0;
+    p.k_caches = bt.k_caches;
+    p.v_caches = bt.v_caches;
+    p.caps = bt.caps;
+    p.q_sseq = bt.q_sseq;
+    p.new_sseq = bt.new_sseq;
 
     // Both kernels are launched with programmatic stream serialisation so that each
     // one's prologue overlaps the tail of the kernel before it (also inside CUDA graphs).
@@ -833,7 +872,7 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(n_splits);
+    cfg.gridDim = dim3(n_splits, bt.n_seqs);
     cfg.blockDim = dim3(L::kThreads);
     cfg.dynamicSmemBytes = L::kTotal;
     cfg.stream = st;
@@ -855,8 +894,9 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st) {
     mp.scale = a->scale;
     mp.out = a->out;
     mp.lse = a->lse;
+    mp.g_sseq = bt.g_sseq;
     cudaLaunchConfig_t mcfg = {};
-    mcfg.gridDim = dim3(NQ * 16, 8);
+    mcfg.gridDim = dim3(NQ * 16, 8, bt.n_seqs);
     mcfg.blockDim = dim3(256);
     mcfg.dynamicSmemBytes = 0;
     mcfg.stream = st;
@@ -993,4 +1033,88 @@ extern "C" int sqmix_fa_decode_noalloc(const sqmix_fa_args *a, sqmix_stream_t st
     b.workspace_bytes = SQMIX_FA_NOALLOC_SCRATCH_BYTES;
     b.n_splits = n_splits;
     return sqmix_fa_decode(&b, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Sequence-batched decode: one launch pair for n_seqs independent sequences, each
+// with its own tiled caches and device scalars (the batched decode of config 4).
+// ---------------------------------------------------------------------------
+extern "C" size_t sqmix_fa_batch_workspace_bytes(int32_t n_seqs, int32_t splits_per_seq) {
+    if (n_seqs < 1) n_seqs = 1;
+    if (splits_per_seq <= 0) splits_per_seq = 64;  // covers the automatic choice
+    size_t a, b;
+    return fa_ws_layout(n_seqs * splits_per_seq, 1, &a, &b);
+}
+
+extern "C" int sqmix_fa_decode_batch(const sqmix_fa_batch_args *b, sqmix_stream_t stream) {
+    SQMIX_CHECK_ARG(b != nullptr, "fa_decode_batch: null args");
+    SQMIX_CHECK_ARG(b->n_seqs >= 1 && b->n_seqs <= 65535, "fa_decode_batch: n_seqs=%d", b->n_seqs);
+    SQMIX_CHECK_ARG(b->q && b->k_caches && b->v_caches && b->capacities && b->n_kv && b->q_pos0 && b->out &&
+                        b->workspace,
+                    "fa_decode_batch: null pointer argument");
+    SQMIX_CHECK_ARG(b->q_dtype == SQMIX_F32 || b->q_dtype == SQMIX_F16 || b->q_dtype == SQMIX_BF16,
+                    "fa_decode_batch: q dtype %d", b->q_dtype);
+    SQMIX_CHECK_ARG(!b->gate || b->gate_dtype == SQMIX_F32 || b->gate_dtype == SQMIX_F16 ||
+                        b->gate_dtype == SQMIX_BF16,
+                    "fa_decode_batch: gate dtype %d", b->gate_dtype);
+    SQMIX_CHECK_ARG(b->scale > 0.f, "fa_decode_batch: scale must be positive");
+    SQMIX_CHECK_ARG(b->rope_n_rot >= 0 && b->rope_n_rot <= 64 && b->rope_n_rot % 2 == 0 &&
+                        (b->rope_n_rot == 0 || b->rope_freq_base > 0.f),
+                    "fa_decode_batch: rope parameters (n_rot <= 64)");
+    SQMIX_CHECK_ARG(b->n_new == 0 || (b->n_new == 1 && b->k_new && b->v_new &&
+                                      (b->kv_new_dtype == SQMIX_F32 || b->kv_new_dtype == SQMIX_F16 ||
+                                       b->kv_new_dtype == SQMIX_BF16)),
+                    "fa_decode_batch: n_new must be 0 or 1 (with k_new/v_new [n_seqs][2][256])");
+    int splits = b->splits_per_seq;
+    if (splits <= 0) {  // about four CTAs per SM over the batch, at least one per sequence
+        const int sms = sqmix_device_sm_count(-1);
+        splits = (4 * sms + b->n_seqs - 1) / b->n_seqs;
+        if (splits > 64) splits = 64;
+        if (splits < 1) splits = 1;
+    }
+    SQMIX_CHECK_ARG(splits >= 1 && splits <= 4096, "fa_decode_batch: splits_per_seq=%d", splits);
+    const size_t need = sqmix_fa_batch_workspace_bytes(b->n_seqs, splits);
+    if (b->workspace_bytes < need) {
+        set_error("fa_decode_batch: workspace %zu bytes < %zu needed", b->workspace_bytes, need);
+        return SQMIX_ENOSPC;
+    }
+    sqmix_fa_args a = {};
+    a.q = b->q;
+    a.q_dtype = b->q_dtype;
+    a.q_stride_tok = 0;  // one query token per sequence
+    a.q_stride_head = b->q_stride_head;
+    a.gate = b->gate;
+    a.gate_dtype = b->gate_dtype;
+    a.gate_stride_tok = 0;
+    a.gate_stride_head = b->gate_stride_head;
+    a.k_cache = nullptr;
+    a.v_cache = nullptr;
+    a.capacity = 0;
+    a.n_kv = b->n_kv;
+    a.q_pos0 = b->q_pos0;
+    a.n_q = 1;
+    a.scale = b->scale;
+    a.rope_n_rot = b->rope_n_rot;
+    a.rope_freq_base = b->rope_freq_base;
+    a.rope_pos_offset = 0;
+    a.out = b->out;
+    a.lse = b->lse;
+    a.workspace = b->workspace;
+    a.workspace_bytes = b->workspace_bytes;
+    a.k_new = b->k_new;
+    a.v_new = b->v_new;
+    a.kv_new_dtype = b->kv_new_dtype;
+    a.k_new_stride_tok = 0;
+    a.v_new_stride_tok = 0;
+    a.n_new = b->n_new;
+    a.flags = b->flags;
+    FaBatch bt;
+    bt.n_seqs = b->n_seqs;
+    bt.k_caches = reinterpret_cast<const uint8_t *const *>(b->k_caches);
+    bt.v_caches = reinterpret_cast<const uint8_t *const *>(b->v_caches);
+    bt.caps = b->capacities;
+    bt.q_sseq = b->q_stride_seq;
+    bt.new_sseq = b->new_stride_seq;
+    bt.g_sseq = b->gate_stride_seq;
+    return launch_fa<1, 4, 2, 5, 1>(&a, splits, reinterpret_cast<cudaStream_t>(stream), bt);
 }

@@ -72,6 +72,18 @@ class FaArgs(ctypes.Structure):
     ]
 
 
+class FaBatchArgs(ctypes.Structure):
+    _fields_ = [
+        ("n_seqs", c_int32), ("q", c_void_p), ("q_dtype", c_int32), ("q_stride_seq", c_int64),
+        ("q_stride_head", c_int64), ("gate", c_void_p), ("gate_dtype", c_int32), ("gate_stride_seq", c_int64),
+        ("gate_stride_head", c_int64), ("k_caches", c_void_p), ("v_caches", c_void_p), ("capacities", c_void_p),
+        ("n_kv", c_void_p), ("q_pos0", c_void_p), ("scale", c_float), ("rope_n_rot", c_int32),
+        ("rope_freq_base", c_float), ("out", c_void_p), ("lse", c_void_p), ("workspace", c_void_p),
+        ("workspace_bytes", c_size_t), ("splits_per_seq", c_int32), ("k_new", c_void_p), ("v_new", c_void_p),
+        ("kv_new_dtype", c_int32), ("new_stride_seq", c_int64), ("n_new", c_int32), ("flags", c_int32),
+    ]
+
+
 class GdnArgs(ctypes.Structure):
     _fields_ = [
         ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("dtype", c_int32),
@@ -99,6 +111,8 @@ _SIGNATURES = {
     "sqmix_fa_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32]),
     "sqmix_fa_prefill": (ctypes.c_int, [ctypes.POINTER(FaArgs), c_void_p]),
     "sqmix_gdn_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
+    "sqmix_fa_batch_workspace_bytes": (c_size_t, [c_int32, c_int32]),
+    "sqmix_fa_decode_batch": (ctypes.c_int, [ctypes.POINTER(FaBatchArgs), c_void_p]),
     "sqmix_gdn_prefill": (ctypes.c_int, [ctypes.POINTER(GdnArgs), c_void_p, c_size_t, c_void_p]),
     "sqmix_attn_merge_lse": (ctypes.c_int, [c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                                             c_void_p, c_void_p]),

@@ -21,7 +21,7 @@ import math
 
 import torch
 
-from ._lib import (SQMIX_BF16, SQMIX_F16, SQMIX_F32, SQMIX_FA_OVERLAP_PREV, FaArgs, GdnArgs, KvAppendArgs, check, lib)
+from ._lib import (SQMIX_BF16, SQMIX_F16, SQMIX_F32, SQMIX_FA_OVERLAP_PREV, FaArgs, FaBatchArgs, GdnArgs, KvAppendArgs, check, lib)
 
 HEAD_DIM = 256
 N_HEAD = 16
@@ -177,6 +177,60 @@ def flash_attn_ext(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor
                       rope_pos_offset, out, lse, workspace, n_splits, config, k_new, v_new,
                       SQMIX_FA_OVERLAP_PREV if overlap_prev else 0)
     check(lib().sqmix_fa_decode(ctypes.byref(a), _stream(stream)), "flash_attn_ext")
+    return out
+
+
+def fa_batch_workspace_bytes(n_seqs: int, splits_per_seq: int = 0) -> int:
+    return int(lib().sqmix_fa_batch_workspace_bytes(int(n_seqs), int(splits_per_seq)))
+
+
+def flash_attn_decode_batch(q: torch.Tensor, k_caches: torch.Tensor, v_caches: torch.Tensor,
+                            capacities: torch.Tensor, n_kv: torch.Tensor, q_pos0: torch.Tensor,
+                            gate: torch.Tensor | None = None, scale: float = 1.0 / 16.0, rope_n_rot: int = 0,
+                            rope_freq_base: float = 1e7, out: torch.Tensor | None = None,
+                            lse: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                            splits_per_seq: int = 0, k_new: torch.Tensor | None = None,
+                            v_new: torch.Tensor | None = None, overlap_prev: bool = False,
+                            stream=None) -> torch.Tensor:
+    """One decode token for each of n_seqs sequences: q [n_seqs][16][256]; k_caches /
+    v_caches: device int64 tensors [n_seqs] holding the data pointers of each sequence's
+    tiled caches (capacities [n_seqs] rows); n_kv, q_pos0 device int64 [n_seqs].
+    k_new / v_new [n_seqs][2][256] are appended at row q_pos0[s] in the same launch."""
+    _require_cuda(q, k_caches, v_caches, capacities, n_kv, q_pos0, gate)
+    n_seqs = q.shape[0]
+    if q.dim() == 2:
+        q = q.view(n_seqs, N_HEAD, HEAD_DIM)
+    if q.stride(-1) != 1:
+        raise ValueError("q rows must be contiguous along head_dim")
+    for t in (k_caches, v_caches, capacities, n_kv, q_pos0):
+        if t.dtype != torch.int64 or t.numel() != n_seqs or not t.is_contiguous():
+            raise ValueError("pointer / scalar arrays must be contiguous int64 [n_seqs]")
+    if out is None:
+        out = torch.empty((n_seqs, N_HEAD, HEAD_DIM), dtype=torch.float32, device=q.device)
+    if workspace is None:
+        workspace = torch.zeros(fa_batch_workspace_bytes(n_seqs, splits_per_seq), dtype=torch.uint8,
+                                device=q.device)
+    n_new = 0
+    if k_new is not None:
+        _require_cuda(k_new, v_new)
+        k_new = k_new.reshape(n_seqs, N_HEAD_KV * HEAD_DIM)
+        v_new = v_new.reshape(n_seqs, N_HEAD_KV * HEAD_DIM)
+        if k_new.stride(0) != v_new.stride(0) or k_new.dtype != v_new.dtype:
+            raise ValueError("k_new and v_new must share dtype and layout")
+        n_new = 1
+    a = FaBatchArgs(
+        n_seqs=n_seqs, q=_ptr(q), q_dtype=_dt(q), q_stride_seq=q.stride(0), q_stride_head=q.stride(1),
+        gate=_ptr(gate), gate_dtype=_dt(gate) if gate is not None else 0,
+        gate_stride_seq=gate.stride(0) if gate is not None else 0,
+        gate_stride_head=gate.stride(1) if gate is not None else 0,
+        k_caches=_ptr(k_caches), v_caches=_ptr(v_caches), capacities=_ptr(capacities), n_kv=_ptr(n_kv),
+        q_pos0=_ptr(q_pos0), scale=float(scale), rope_n_rot=int(rope_n_rot), rope_freq_base=float(rope_freq_base),
+        out=_ptr(out), lse=_ptr(lse), workspace=_ptr(workspace), workspace_bytes=workspace.numel(),
+        splits_per_seq=int(splits_per_seq), k_new=_ptr(k_new), v_new=_ptr(v_new),
+        kv_new_dtype=_dt(k_new) if k_new is not None else 0,
+        new_stride_seq=k_new.stride(0) if k_new is not None else 0, n_new=n_new,
+        flags=SQMIX_FA_OVERLAP_PREV if overlap_prev else 0)
+    check(lib().sqmix_fa_decode_batch(ctypes.byref(a), _stream(stream)), "flash_attn_decode_batch")
     return out
 
 
