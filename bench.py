@@ -625,6 +625,103 @@ def bench_gdn(steps: int, warmup: int):
     return res
 
 
+def bench_stack(steps: int, warmup: int, splits_per_seq: int = 0):
+    """Config 4: batched hybrid mixer stack, 40 layers (3 GDN + 1 full attention, x10),
+    64 sequences decoding one token each; per-sequence q4_0 KV lengths ~U[1024, 32768]
+    (seeded), each sequence with its own GDN states.  Caches hold random q4_0 codes with
+    fp16 scales ~U(0.05, 0.3) (filling 6 GB through the quantiser would dominate the
+    run); the attention arithmetic does not depend on where the codes came from."""
+    import numpy as np
+    import torch
+
+    import sqmix
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(17)
+    rng = np.random.default_rng(17)
+    n_seqs, n_fa, n_gdn = 64, 10, 30
+    # the batch is ordered longest first, as an engine that knows its sequence lengths
+    # would submit it: CTAs are scheduled in grid order, so the long splits start first
+    lens = np.sort(rng.integers(1024, 32768 + 1, n_seqs))[::-1]
+    caps = [int((n + 1 + 255) // 256 * 256) for n in lens]
+    offs = np.concatenate([[0], np.cumsum(caps)])
+    rows_total = int(offs[-1])
+    unit_rows = 16  # a 4608-byte group holds 16 tokens of both heads
+    kc, vc = [], []
+    for _ in range(n_fa):
+        for lst in (kc, vc):
+            buf = torch.randint(0, 256, (rows_total * 288,), dtype=torch.uint8, generator=g, device=dev)
+            units = buf.view(-1, 2304)
+            sc = (torch.rand((units.shape[0], 128), generator=g, device=dev) * 0.25 + 0.05).half()
+            units[:, 2048:] = sc.view(torch.uint8)
+            lst.append(buf)
+    i64 = lambda xs: torch.tensor([int(x) for x in xs], dtype=torch.int64, device=dev)
+    kp = [i64([kc[l].data_ptr() + int(offs[s]) * 288 for s in range(n_seqs)]) for l in range(n_fa)]
+    vp = [i64([vc[l].data_ptr() + int(offs[s]) * 288 for s in range(n_seqs)]) for l in range(n_fa)]
+    capt = i64(caps)
+    n_kv = i64([n + 1 for n in lens])
+    q_pos0 = i64(list(lens))
+    q = torch.randn((n_fa, n_seqs, N_HEAD, HEAD_DIM), generator=g, device=dev)
+    gate = torch.randn((n_fa, n_seqs, N_HEAD, HEAD_DIM), generator=g, device=dev)
+    k_new = torch.randn((n_fa, n_seqs, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+    v_new = torch.randn((n_fa, n_seqs, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+    out = torch.empty((n_fa, n_seqs, N_HEAD, HEAD_DIM), device=dev)
+    ws = torch.zeros(sqmix.fa_batch_workspace_bytes(n_seqs, splits_per_seq), dtype=torch.uint8, device=dev)
+    S = torch.randn((n_gdn, n_seqs, 1, 32, 128, 128), generator=g, device=dev) * 0.02
+    gq = torch.randn((n_gdn, n_seqs, 1, 16, 128), generator=g, device=dev).to(torch.bfloat16)
+    gk = torch.randn((n_gdn, n_seqs, 1, 16, 128), generator=g, device=dev).to(torch.bfloat16)
+    gv = torch.randn((n_gdn, n_seqs, 1, 32, 128), generator=g, device=dev).to(torch.bfloat16)
+    gg = -torch.rand((n_gdn, n_seqs, 1, 32), generator=g, device=dev)
+    gb = torch.rand((n_gdn, n_seqs, 1, 32), generator=g, device=dev)
+    go = torch.empty((n_gdn, n_seqs, 1, 32, 128), device=dev)
+
+    def step():
+        fa = gd = 0
+        for layer in range(n_fa + n_gdn):
+            if layer % 4 == 3:
+                sqmix.flash_attn_decode_batch(q[fa], kp[fa], vp[fa], capt, n_kv, q_pos0, gate=gate[fa],
+                                              rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE, out=out[fa],
+                                              workspace=ws, k_new=k_new[fa], v_new=v_new[fa],
+                                              splits_per_seq=splits_per_seq)
+                fa += 1
+            else:
+                sqmix.gated_delta_net(gq[gd], gk[gd], gv[gd], gg[gd], gb[gd], S[gd], l2_eps=1e-6, out=go[gd])
+                gd += 1
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(3, steps)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    graph = None
+    sqmix.fa_status(ws)
+    hbm, hbm_kind = peaks()
+    fa_bytes = n_fa * float(sum(int(n) + 1 for n in lens)) * BYTES_PER_KEY
+    gdn_bytes = n_gdn * n_seqs * 2.0 * GDN_STATE_BYTES
+    alg = fa_bytes + gdn_bytes
+    return {"us_per_step": us, "tok_s": n_seqs / us * 1e6, "alg_bytes_per_step": alg,
+            "achieved_gbs": alg / us / 1e3, "frac_of_hbm": alg / us / 1e3 / hbm, "peak_kind": hbm_kind,
+            "kv_len_mean": float(np.mean(lens)),
+            "config": "config4: 64 sequences x 1 token, 40 layers (30 GDN + 10 full attention), q4_0 KV "
+                      "U[1024, 32768] per sequence, batched kernels, CUDA graph"}
+
+
 def run_profile_case(case: str):
     """Small fixed workloads for ncu captures (one kernel, a few launches, ~0.3 GB)."""
     import torch
@@ -723,6 +820,7 @@ def main():
     if res is not None and world == 1 and not args.no_prefill:
         res["prefill"] = bench_prefill(args.steps, args.warmup)
         res["gdn"] = bench_gdn(args.steps, args.warmup)
+        res["stack"] = bench_stack(args.steps, args.warmup)
     if res is not None:
         if cpu is not None:
             res["cpu_baseline"] = cpu
