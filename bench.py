@@ -242,6 +242,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         pk_all = torch.empty((world, rows * (HEAD_DIM + 1)), device=dev)
         o_loc = [pk_loc[l, :rows * HEAD_DIM].view(1, N_HEAD, HEAD_DIM) for l in range(N_LAYERS)]
         l_loc = [pk_loc[l, rows * HEAD_DIM:].view(1, N_HEAD) for l in range(N_LAYERS)]
+        # default: the fused peer-memory merge (one kernel per layer, partials read
+        # over NVLink); --nccl-merge: all-gather + merge kernel
+        peer = None if args.nccl_merge else split_kv.PeerMerge(n_slots=N_LAYERS, rows=N_HEAD, device=dev)
 
     own = rank == owner  # the rank whose key slice holds the new token appends it (fused)
 
@@ -257,9 +260,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                  lse=l_loc[l], workspace=ws, n_splits=n_splits,
                                  k_new=k_new[l] if own else None, v_new=v_new[l] if own else None,
                                  overlap_prev=True)
-            dist.all_gather_into_tensor(pk_all, pk_loc[l])
-            sqmix.attn_merge_lse(pk_all[:, :rows * HEAD_DIM].view(world, rows, HEAD_DIM),
-                                 pk_all[:, rows * HEAD_DIM:], gate=gate[l, 0], out=out[l, 0])
+            if peer is not None:
+                peer.merge(o_loc[l], l_loc[l], l, gate=gate[l, 0], out=out[l, 0])
+            else:
+                dist.all_gather_into_tensor(pk_all, pk_loc[l])
+                sqmix.attn_merge_lse(pk_all[:, :rows * HEAD_DIM].view(world, rows, HEAD_DIM),
+                                     pk_all[:, rows * HEAD_DIM:], gate=gate[l, 0], out=out[l, 0])
 
     def step_fn():
         for l in range(N_LAYERS):
@@ -416,6 +422,13 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
     used_graph = graph is not None
     graph = None  # release the captured graph before the process group goes away
+    merge_kind = None
+    if world > 1:
+        merge_kind = "nccl all-gather + merge kernel" if peer is None else "peer-memory merge kernel (NVLink P2P)"
+        if peer is not None:
+            if not peer.ok():
+                raise RuntimeError("peer merge: a bounded wait for a peer gave up")
+            peer.close()
     if rank != 0:
         return None
     res = {
@@ -427,7 +440,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                "16 Q / 2 KV heads, d=256, RoPE 64/1e7, sigmoid gate",
                    "n_q": 1, "keys_per_layer": N_KV, "keys_per_gpu": n_local, "parallelism": f"split-KV x{world}",
                    "l2": "inputs larger than L2: 10 x 99 MB of KV cycled per step",
-                   "cuda_graph": used_graph},
+                   "cuda_graph": used_graph, "cross_gpu_merge": merge_kind},
         "tokens_per_s": 1e6 / us_per_token,
         "roofline": {"bound": "hbm",
                      "kernel": "fa_decode_kernel + fa_merge_kernel (split-KV attention, PDL-chained pair)",
@@ -788,6 +801,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill measurement")
+    ap.add_argument("--nccl-merge", action="store_true", help="N > 1: all-gather + merge instead of the peer merge")
     ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn | gdnp) and exit")
     args = ap.parse_args()
     if args.profile:

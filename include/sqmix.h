@@ -237,6 +237,40 @@ typedef struct sqmix_fa_batch_args {
 size_t sqmix_fa_batch_workspace_bytes(int32_t n_seqs, int32_t splits_per_seq);
 int sqmix_fa_decode_batch(const sqmix_fa_batch_args *args, sqmix_stream_t stream);
 
+/* Cross-GPU merge of split-KV partials over peer memory (NVLink P2P), for
+ * long-context decode split across ranks (one process per GPU).  Each rank creates
+ * one peer buffer (n_slots = layers it merges per step), shares the IPC handle with
+ * the other ranks (any host channel), opens theirs, and puts the n_ranks pointers
+ * (its own at [rank]) in a device array.  sqmix_attn_merge_peers then publishes this
+ * rank's normalised partial (o_local [rows][256], lse_local [rows], natural log) in
+ * slot `slot`, waits (bounded, 2 s) for every peer's publication of the same slot and
+ * merges all of them: out = sum_r O_r e^{lse_r - L} (* sigmoid(gate)), lse_out = L.
+ * Every rank must call it once per slot per step, in the same order.  A wait that
+ * gives up sets bit 1 of *status (nullable) and leaves out unwritten.  Buffers start
+ * zeroed; destroy them only after every rank has finished its last merge. */
+#define SQMIX_IPC_HANDLE_BYTES 64
+typedef struct sqmix_peer_merge_args {
+    int32_t n_ranks;          /* <= 8 */
+    int32_t rank;
+    int32_t slot;
+    int32_t n_slots;
+    int32_t rows;             /* 16 x n_q, <= 32 */
+    const void *const *buffers; /* device array [n_ranks] of peer buffers as mapped here */
+    const float *o_local;
+    const float *lse_local;
+    const float *gate;        /* nullable [rows][256] f32 */
+    float *out;               /* [rows][256] */
+    float *lse_out;           /* nullable [rows] */
+    void *status;             /* nullable device u32 */
+} sqmix_peer_merge_args;
+
+size_t sqmix_peer_buffer_bytes(int32_t n_slots);
+int sqmix_peer_buffer_create(int32_t n_slots, void **dev_ptr, void *ipc_handle /* 64 bytes out */);
+int sqmix_peer_buffer_open(const void *ipc_handle, void **peer_ptr);
+int sqmix_peer_buffer_close(void *peer_ptr);
+int sqmix_peer_buffer_destroy(void *dev_ptr);
+int sqmix_attn_merge_peers(const sqmix_peer_merge_args *args, sqmix_stream_t stream);
+
 /* sqmix_fa_decode without a caller workspace (no reference counterpart: ggml_flash_attn_ext
  * takes its scratch from ggml's graph allocator).  For callers that cannot allocate
  * device memory at the call site, e.g. a callback inside a graph executor whose buffers

@@ -84,6 +84,14 @@ class FaBatchArgs(ctypes.Structure):
     ]
 
 
+class PeerMergeArgs(ctypes.Structure):
+    _fields_ = [
+        ("n_ranks", c_int32), ("rank", c_int32), ("slot", c_int32), ("n_slots", c_int32), ("rows", c_int32),
+        ("buffers", c_void_p), ("o_local", c_void_p), ("lse_local", c_void_p), ("gate", c_void_p),
+        ("out", c_void_p), ("lse_out", c_void_p), ("status", c_void_p),
+    ]
+
+
 class GdnArgs(ctypes.Structure):
     _fields_ = [
         ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("dtype", c_int32),
@@ -112,6 +120,12 @@ _SIGNATURES = {
     "sqmix_fa_prefill": (ctypes.c_int, [ctypes.POINTER(FaArgs), c_void_p]),
     "sqmix_gdn_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
     "sqmix_fa_batch_workspace_bytes": (c_size_t, [c_int32, c_int32]),
+    "sqmix_peer_buffer_bytes": (c_size_t, [c_int32]),
+    "sqmix_peer_buffer_create": (ctypes.c_int, [c_int32, ctypes.POINTER(c_void_p), c_void_p]),
+    "sqmix_peer_buffer_open": (ctypes.c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "sqmix_peer_buffer_close": (ctypes.c_int, [c_void_p]),
+    "sqmix_peer_buffer_destroy": (ctypes.c_int, [c_void_p]),
+    "sqmix_attn_merge_peers": (ctypes.c_int, [ctypes.POINTER(PeerMergeArgs), c_void_p]),
     "sqmix_fa_decode_batch": (ctypes.c_int, [ctypes.POINTER(FaBatchArgs), c_void_p]),
     "sqmix_gdn_prefill": (ctypes.c_int, [ctypes.POINTER(GdnArgs), c_void_p, c_size_t, c_void_p]),
     "sqmix_attn_merge_lse": (ctypes.c_int, [c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -11,11 +11,13 @@ collective; with NCCL it runs over NVLink, with gloo on the host (tests).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
 
-from .ops import KV_PAD
+from ._lib import PeerMergeArgs, check, lib
+from .ops import KV_PAD, _ptr, _stream
 
 GROUP = 16  # slices start on 16-token groups of the tiled cache
 
@@ -83,3 +85,81 @@ def gather(o_local: torch.Tensor, lse_local: torch.Tensor, group=None) -> tuple[
     dist.all_gather(list(o_all.unbind(0)), o_local.contiguous(), group=group)
     dist.all_gather(list(l_all.unbind(0)), lse_local.contiguous(), group=group)
     return o_all, l_all
+
+
+class PeerMerge:
+    """The (O, LSE) exchange of split-KV decode over peer memory (NVLink P2P): one
+    peer buffer per rank, IPC handles swapped through the process group, and one
+    sqmix_attn_merge_peers launch per layer that publishes this rank's partial and
+    merges everyone's.  Replaces gather() + attn_merge_lse with a single kernel.
+
+    n_slots: merges per step (one per layer).  Every rank calls merge() for the same
+    slots in the same order.  close() after the last step (all ranks)."""
+
+    IPC_BYTES = 64
+
+    def __init__(self, n_slots: int, rows: int = 16, group=None, device=None):
+        import torch.distributed as dist
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.n_slots = int(n_slots)
+        self.rows = int(rows)
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(self.IPC_BYTES)
+        check(lib().sqmix_peer_buffer_create(self.n_slots, ctypes.byref(own), handle), "peer_buffer_create")
+        self._own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._opened = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            check(lib().sqmix_peer_buffer_open(ctypes.create_string_buffer(h, self.IPC_BYTES), ctypes.byref(p)),
+                  "peer_buffer_open")
+            self._opened.append(p.value)
+            ptrs.append(p.value)
+        self.ptrs = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def merge(self, o_local: torch.Tensor, lse_local: torch.Tensor, slot: int, gate: torch.Tensor | None = None,
+              out: torch.Tensor | None = None, lse_out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """o_local [rows][256] f32 and lse_local [rows] (natural log) of this rank's key
+        slice -> out [rows][256] over all ranks (* sigmoid(gate) when given)."""
+        o_local = o_local.reshape(self.rows, 256)
+        lse_local = lse_local.reshape(self.rows)
+        if out is None:
+            out = torch.empty((self.rows, 256), dtype=torch.float32, device=o_local.device)
+        if gate is not None:
+            gate = gate.reshape(self.rows, 256)
+            if gate.dtype != torch.float32 or not gate.is_contiguous():
+                gate = gate.float().contiguous()
+        a = PeerMergeArgs(n_ranks=self.world, rank=self.rank, slot=int(slot), n_slots=self.n_slots, rows=self.rows,
+                          buffers=_ptr(self.ptrs), o_local=_ptr(o_local), lse_local=_ptr(lse_local), gate=_ptr(gate),
+                          out=_ptr(out), lse_out=_ptr(lse_out), status=_ptr(self.status))
+        check(lib().sqmix_attn_merge_peers(ctypes.byref(a), _stream(stream)), "attn_merge_peers")
+        return out
+
+    def ok(self) -> bool:
+        """False if a bounded wait for a peer gave up (synchronises)."""
+        return int(self.status.item()) == 0
+
+    def close(self):
+        """Unmap the peers and free this rank's buffer, after every rank is done."""
+        import torch.distributed as dist
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            check(lib().sqmix_peer_buffer_close(ctypes.c_void_p(p)), "peer_buffer_close")
+        self._opened = []
+        dist.barrier(group=self.group)
+        check(lib().sqmix_peer_buffer_destroy(ctypes.c_void_p(self._own)), "peer_buffer_destroy")
+        self._own = None
