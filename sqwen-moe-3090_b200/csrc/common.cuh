@@ -272,4 +272,53 @@ __device__ __forceinline__ void q4_0_store_block(float x, int lane, uint8_t *cac
             __float2half_rn(d);
 }
 
+// N blocks at once (one per value of x[k], lane j holding element j of each), with the
+// reductions of the blocks interleaved: the same rounding as q4_0_store_block.
+// Blocks with live[k] false are skipped.
+template <int N>
+__device__ __forceinline__ void q4_0_store_blocks(const float (&x)[N], int lane, uint8_t *kcache, uint8_t *vcache,
+                                                  const int64_t (&row)[N], const int (&h)[N], const int (&b)[N],
+                                                  const bool (&is_v)[N], const bool (&live)[N]) {
+    float amax[N], vmax[N];
+    int idx[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+        amax[k] = fabsf(x[k]);
+        vmax[k] = x[k];
+        idx[k] = lane;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            const float oa = __shfl_xor_sync(0xffffffffu, amax[k], off);
+            const float ov = __shfl_xor_sync(0xffffffffu, vmax[k], off);
+            const int oi = __shfl_xor_sync(0xffffffffu, idx[k], off);
+            if (oa > amax[k] || (oa == amax[k] && oi < idx[k])) {
+                amax[k] = oa;
+                vmax[k] = ov;
+                idx[k] = oi;
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+        if (amax[k] == 0.0f) vmax[k] = 0.0f;
+        const float d = __fdiv_rn(vmax[k], -8.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        int q = __float2int_rz(__fadd_rn(__fmul_rn(x[k], id), 8.5f));
+        q = min(15, max(0, q));
+        const int qhi = __shfl_down_sync(0xffffffffu, q, 16);
+        if (!live[k]) continue;
+        uint8_t *cache = is_v[k] ? vcache : kcache;
+        if (lane < 16) {
+            const uint8_t byte = static_cast<uint8_t>(q | (qhi << 4));
+            cache[is_v[k] ? v_qs_offset(row[k], h[k], b[k], lane) : k_qs_offset(row[k], h[k], b[k], lane)] = byte;
+        }
+        if (lane == 0)
+            *reinterpret_cast<__half *>(cache + (is_v[k] ? v_scale_offset(row[k], h[k], b[k])
+                                                         : k_scale_offset(row[k], h[k], b[k]))) = __float2half_rn(d);
+    }
+}
+
 }  // namespace sqmix

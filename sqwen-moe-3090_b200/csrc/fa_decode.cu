@@ -125,9 +125,11 @@ __device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontr
 // warp w folds splits w, w + nwarps, ... with an online (max, sum) update, 8 splits
 // in flight at a time; the warps then combine through shared memory `red`
 // (nwarps * 34 floats).  Reads bypass L1: the partials were written by other CTAs.
+// gate_factor: sigmoid(gate) of this thread's output element (1 without a gate),
+// computed by the caller ahead of time.
 __device__ void merge_slice(const float *part_o, const float *part_ml, int n_splits, int n_rows, int row,
-                            int slice, float c, float scale, const void *gate, int gate_dtype, int64_t g_st,
-                            int64_t g_sh, float *out, float *lse, float *red, int nwarps) {
+                            int slice, float c, float scale, float gate_factor, float *out, float *lse, float *red,
+                            int nwarps) {
     constexpr int kChunk = 24;  // splits per warp per round: 8 warps x 24 covers 192 splits at once
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = slice * 32 + lane;
@@ -186,12 +188,7 @@ __device__ void merge_slice(const float *part_o, const float *part_ml, int n_spl
             y = fmaf(red[w * 34 + lane], wt, y);
         }
         y = L > 0.f ? y / L : 0.f;
-        if (gate) {
-            const int qi = row >> 4, h = row & 15;
-            const float gv = load_act(gate, qi * g_st + h * g_sh + d, gate_dtype);
-            y *= 1.0f / (1.0f + expf(-gv));
-        }
-        out[static_cast<size_t>(row) * 256 + d] = y;
+        out[static_cast<size_t>(row) * 256 + d] = y * gate_factor;
         if (lse && slice == 0 && lane == 0) lse[row] = L > 0.f ? Mt * scale + logf(L) : -INFINITY;
     }
     __syncthreads();  // `red` is reused by the next slice
@@ -246,6 +243,16 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     // whose range holds them writes them before it may stream them.
     const int64_t row_lo = g_begin * kGroupTokens, row_hi = g_end * kGroupTokens;
     const bool has_fresh = p.n_new > 0 && q_pos0 < row_hi && q_pos0 + p.n_new > row_lo;
+
+    // ---- RoPE angles of the step's positions (shared by Q and the new K rows); they
+    // depend on q_pos0 only, so under SQMIX_FA_OVERLAP_PREV they overlap the previous
+    // kernel's tail ----
+    const int half = p.rope_n_rot >> 1;
+    if (p.rope_n_rot > 0 && threadIdx.x < NQ * 32) {
+        const int qi = threadIdx.x >> 5, i = threadIdx.x & 31;
+        if (i < half)
+            rope_s[qi * 32 + i] = rope_cos_sin(q_pos0 + qi + p.rope_pos_offset, p.rope_theta_scale, i);
+    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSTAGE; ++s) {
@@ -342,26 +349,33 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     }
     (void)kvv;
 
-    // ---- RoPE angles of the step's positions (shared by Q and the new K rows) ----
-    const int half = p.rope_n_rot >> 1;
-    if (p.rope_n_rot > 0 && threadIdx.x < NQ * 32) {
-        const int qi = threadIdx.x >> 5, i = threadIdx.x & 31;
-        if (i < half)
-            rope_s[qi * 32 + i] = rope_cos_sin(q_pos0 + qi + p.rope_pos_offset, p.rope_theta_scale, i);
-    }
-    __syncthreads();
+    __syncthreads();  // staged Q / new rows and the RoPE table are visible
 
     // ---- fused append: quantise the step's new K/V rows held by this CTA ----------
     if (has_fresh) {
-        for (int task = warp; task < 32 * p.n_new; task += L::kWarps) {
-            const int t = task >> 5, r = task & 31;
-            const bool is_v = r >> 4;
-            const int h = (r >> 3) & 1, b = r & 7;
+        // 32 blocks per new row; each warp quantises 4 of them at once (interleaved
+        // reductions), rows of another CTA's range are skipped
+        constexpr int kPerWarp = 32 / L::kWarps;
+        static_assert(32 % L::kWarps == 0, "blocks of a row per warp");
+        for (int t = 0; t < p.n_new; ++t) {
             const int64_t row = q_pos0 + t;
-            if (row < row_lo || row >= row_hi) continue;  // another CTA's row
-            const float x = kv_row_elem(kv_stage, ((t * 2 + is_v) * 2 + h) * 256, b * 32 + lane, SQMIX_F32,
-                                        is_v ? 0 : p.rope_n_rot, rope_s + t * 32);
-            q4_0_store_block(x, lane, is_v ? vcache : kcache, row, h, b, is_v);
+            const bool mine = row >= row_lo && row < row_hi;
+            float x[kPerWarp];
+            int64_t rows[kPerWarp];
+            int hh[kPerWarp], bb[kPerWarp];
+            bool isv[kPerWarp], live[kPerWarp];
+#pragma unroll
+            for (int k = 0; k < kPerWarp; ++k) {
+                const int r = warp + L::kWarps * k;
+                isv[k] = r >> 4;
+                hh[k] = (r >> 3) & 1;
+                bb[k] = r & 7;
+                rows[k] = row;
+                live[k] = mine;
+                x[k] = kv_row_elem(kv_stage, ((t * 2 + isv[k]) * 2 + hh[k]) * 256, bb[k] * 32 + lane, SQMIX_F32,
+                                   isv[k] ? 0 : p.rope_n_rot, rope_s + t * 32);
+            }
+            q4_0_store_blocks<kPerWarp>(x, lane, kcache, vcache, rows, hh, bb, isv, live);
         }
         // the bulk copies (async proxy) that stream these rows must see the stores
         asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -758,18 +772,23 @@ struct FaMergeParams {
 
 __global__ void __launch_bounds__(256) fa_merge_kernel(FaMergeParams p) {
     __shared__ float red[8 * 34];
+    const size_t seq = blockIdx.z;
+    // The gate is an input of the decode call, produced before the decode kernel; the
+    // decode kernel triggers this launch only after its own dependency wait, so the
+    // gate is complete here and its load can overlap the decode grid's tail.
+    float gate_factor = 1.f;
+    if (p.gate && threadIdx.x < 32) {
+        const int row = blockIdx.x, qi = row >> 4, h = row & 15, d = blockIdx.y * 32 + threadIdx.x;
+        const float gv = load_act(p.gate, static_cast<int64_t>(seq) * p.g_sseq + qi * p.g_st + h * p.g_sh + d,
+                                  p.gate_dtype);
+        gate_factor = 1.0f / (1.0f + expf(-gv));
+    }
     grid_dependency_wait();
     launch_dependents();
-    const size_t seq = blockIdx.z;
     const size_t parts = seq * p.n_splits * p.n_rows;
-    const void *gate = p.gate;
-    if (gate && seq) {
-        const int esz = p.gate_dtype == SQMIX_F32 ? 4 : 2;
-        gate = static_cast<const uint8_t *>(gate) + seq * p.g_sseq * esz;
-    }
     merge_slice(p.part_o + parts * 256, p.part_ml + parts * 2, p.n_splits, p.n_rows, blockIdx.x, blockIdx.y, p.c,
-                p.scale, gate, p.gate_dtype, p.g_st, p.g_sh, p.out + seq * p.n_rows * 256,
-                p.lse ? p.lse + seq * p.n_rows : nullptr, red, 8);
+                p.scale, gate_factor, p.out + seq * p.n_rows * 256, p.lse ? p.lse + seq * p.n_rows : nullptr, red,
+                8);
 }
 
 // Merge of normalised partials across GPUs: O = sum_p O_p e^(lse_p - L).
