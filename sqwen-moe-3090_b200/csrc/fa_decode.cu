@@ -4,7 +4,8 @@
 //   ggml_set_rows (q4_0 KV append, src/engine/kv.rs:367-396) ->
 //   ggml_flash_attn_ext (src/model/attn.rs:238-249; contract at src/backend/ffi.rs:363-377) ->
 //   sigmoid gate (attn.rs:282-283)
-// with ONE cooperative kernel launch:
+// with a pair of launches (decode kernel, then merge kernel, chained by programmatic
+// dependent launch):
 //
 //   1. the CTA whose key range holds the step's new rows quantises them into the
 //      cache (bit-exact quantize_row_q4_0, RoPE on K) before streaming them;
@@ -19,13 +20,16 @@
 //      O^T += V^T P^T;
 //   4. the warps of a KV head combine through shared memory into one (O, m, l)
 //      partial per CTA;
-//   5. after a bounded grid barrier (monotonic ticket counter in the workspace)
-//      each CTA merges a 32-dim slice of the output across all splits (log-sum-exp),
-//      applies sigmoid(gate) and writes out / lse.
+//   5. fa_merge_kernel (one CTA per output row and 32-dim slice) merges the partials
+//      of all splits (log-sum-exp), applies sigmoid(gate) and writes out / lse.  Its
+//      CTAs are resident while the decode grid drains and wait for it with
+//      griddepcontrol.wait.  (Merging inside the decode grid -- the last CTAs to
+//      finish combining the partials behind a ticket counter -- measured 1.5 us per
+//      launch slower on B200: the fence, the ticket and the wait for the last split
+//      cost more than the kernel boundary.)
 //
 // Keys are never read beyond min(n_kv, q_pos0 + n_q): the causal limit of
-// graph.rs:553-559 is applied implicitly, so no mask tensor exists.  When the split
-// count exceeds what can be co-resident, step 5 runs as a separate merge kernel.
+// graph.rs:553-559 is applied implicitly, so no mask tensor exists.
 //
 // Pipeline: a 5-slot ring of 64-token slots (36.9 KB of K+V each); a compute step of
 // n_q = 1 consumes two slots (each warp takes two groups of its KV head: one online-
@@ -733,18 +737,30 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     const size_t split = static_cast<size_t>(seq) * gridDim.x + blockIdx.x;
     float *po = p.part_o + split * NQ * 16 * 256;
     float *pml = p.part_ml + split * NQ * 16 * 2;
-    for (int i = threadIdx.x; i < NQ * 16 * 256; i += L::kThreads) {
-        const int d = i & 255;
-        const int head = (i >> 8) & 15;
-        const int qi = i >> 12;
+    // four consecutive dims per thread (16-byte shared loads and global stores), all
+    // of a thread's rows in flight at once
+    constexpr int kVec4 = NQ * 16 * 64;
+    static_assert(kVec4 % L::kThreads == 0, "partial rows per thread");
+#pragma unroll
+    for (int k = 0; k < kVec4 / L::kThreads; ++k) {
+        const int i = threadIdx.x + k * L::kThreads;
+        const int d = (i & 63) * 4;
+        const int head = (i >> 6) & 15;
+        const int qi = i >> 10;
         const int kh = head >> 3, h8 = head & 7;
         const float *wrow = wts + (qi * 16 + head) * (WPH + 2);
-        float acc = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int wv = 0; wv < WPH; ++wv)
-            acc = fmaf(red_o[((static_cast<size_t>(kh * WPH + wv) * NQ + qi) * 8 + h8) * L::kRedStride + d],
-                       wrow[wv], acc);
-        po[(qi * 16 + head) * 256 + d] = acc;
+        for (int wv = 0; wv < WPH; ++wv) {
+            const float4 x = *reinterpret_cast<const float4 *>(
+                red_o + ((static_cast<size_t>(kh * WPH + wv) * NQ + qi) * 8 + h8) * L::kRedStride + d);
+            const float w = wrow[wv];
+            acc.x = fmaf(x.x, w, acc.x);
+            acc.y = fmaf(x.y, w, acc.y);
+            acc.z = fmaf(x.z, w, acc.z);
+            acc.w = fmaf(x.w, w, acc.w);
+        }
+        *reinterpret_cast<float4 *>(po + (qi * 16 + head) * 256 + d) = acc;
         if (d == 0) {
             pml[(qi * 16 + head) * 2 + 0] = wrow[WPH];
             pml[(qi * 16 + head) * 2 + 1] = wrow[WPH + 1];
