@@ -353,6 +353,69 @@ int sqmix_gdn_state_copy(float *dst, const float *src, int64_t plane_elems, int3
                          sqmix_stream_t stream);
 
 /* ========================================================================
+ * GDN front end and the mixers' per-head norms
+ * ======================================================================== */
+
+/* Short causal convolution of the GDN qkv projection with its history planes:
+ *   conv_input = concat(plane sel[seq] [C][K-1], x^T)          (gdn.rs:290-356)
+ *   out[t][c]  = silu(sum_k conv_input[c][t + k] * weight[c][k])
+ *                (ggml_ssm_conv + ggml_silu, gdn.rs:358-360)
+ * then, when l2_eps > 0, the first n_qk_channels channels (q and k, 2*H_k*d) are
+ * L2-normalised per head of head_dim (gdn.rs:436-441), and the history planes are
+ * written back: plane s < n_snap <- conv_input rows [max(T - s, 0), +K-1)
+ * (plane 0 = the tail; slot s = the history s tokens back, graph.rs:913-961).
+ * Conv history: [n_seqs][n_planes][C][K-1] f32, i.e. ggml's [K-1, C, 1+n_rs] per
+ * sequence.  The plane read may be among the planes written (updated in place). */
+typedef struct sqmix_gdn_conv_args {
+    const void *x;            /* [n_seqs][T][C] qkv_mixed (ggml [C, T]) */
+    int32_t x_dtype;
+    int64_t x_stride_tok;     /* elements between tokens (>= C) */
+    int64_t x_stride_seq;     /* elements between sequences */
+    const float *weight;      /* [C][K] ssm_conv1d (ggml [K, C]) */
+    float *conv_state;        /* [n_seqs][n_planes][C][K-1] */
+    int32_t n_planes;
+    const int32_t *sel;       /* device I32 [n_seqs]: plane read as history; NULL = 0 */
+    int32_t n_snap;           /* planes written, 1 <= n_snap <= n_planes */
+    int32_t n_seqs;
+    int32_t n_tokens;         /* T >= 1 */
+    int32_t channels;         /* C = 2*H_k*d + H_v*d (8192), a multiple of head_dim */
+    int32_t kernel;           /* K in 2..8 (4: ssm_d_conv) */
+    int32_t head_dim;         /* d (128): a multiple of 32 in [32, 256] */
+    int32_t n_qk_channels;    /* leading channels normalised per head (2*H_k*d) */
+    float l2_eps;             /* > 0: L2 norm of those channels (norm_rms_eps); 0: none */
+    float *out;               /* [n_seqs][T][C] f32 */
+} sqmix_gdn_conv_args;
+
+int sqmix_gdn_conv(const sqmix_gdn_conv_args *args, sqmix_stream_t stream);
+
+/* Per-head RMS norm y = x / sqrt(mean(x^2) + eps) over head_dim, then * weight (the
+ * per-head Q/K norm of the attention layers, attn.rs:66-84 and :166-175) and
+ * * silu(z) (norm_gated of the GDN output, gdn.rs:150-181 and :565-573).
+ * x, z [T][H][head_dim] with element strides; out f32.  out may equal x (f32, same
+ * strides): each row is read completely before it is written. */
+typedef struct sqmix_head_norm_args {
+    const void *x;
+    int32_t x_dtype;
+    int64_t x_stride_tok;
+    int64_t x_stride_head;
+    const float *weight;        /* nullable: [head_dim], or per head (weight_stride_head) */
+    int64_t weight_stride_head; /* 0: one weight row shared by all heads */
+    const void *z;              /* nullable gate */
+    int32_t z_dtype;
+    int64_t z_stride_tok;
+    int64_t z_stride_head;
+    int32_t n_tokens;
+    int32_t n_heads;
+    int32_t head_dim;
+    float eps;                  /* norm_rms_eps */
+    float *out;
+    int64_t out_stride_tok;
+    int64_t out_stride_head;
+} sqmix_head_norm_args;
+
+int sqmix_head_norm(const sqmix_head_norm_args *args, sqmix_stream_t stream);
+
+/* ========================================================================
  * Host-side state objects (the engine's bookkeeping, in C++)
  * ======================================================================== */
 

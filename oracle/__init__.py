@@ -55,6 +55,10 @@ def lib():
         L.oracle_l2norm_rows.argtypes = [f32p, i64, i64, ctypes.c_float]
         L.oracle_gdn.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, i64, i64, i64, i64, i64,
                                  f32p, f32p]
+        L.oracle_ssm_conv.argtypes = [f32p, i64, i64, i64, f32p, f32p]
+        L.oracle_gdn_conv.argtypes = [f32p, i64, i64, i64, f32p, f32p, i64, i64, i64, i64, i64, ctypes.c_float,
+                                      f32p]
+        L.oracle_rms_norm_rows.argtypes = [f32p, i64, i64, ctypes.c_float, f32p, i64, i64, f32p, f32p]
         L.oracle_set_threads.argtypes = [ctypes.c_int]
         L.oracle_set_threads.restype = ctypes.c_int
         _lib = L
@@ -172,6 +176,55 @@ def gdn(q, k, v, g, beta, state, n_snap: int = 1):
     lib().oracle_gdn(qp, kp, vp, gp, bp, sp, T, Hk, Hv, d, int(n_snap),
                      out.ctypes.data_as(f32p), snaps.ctypes.data_as(f32p))
     return out, snaps
+
+
+def ssm_conv(sx: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """ggml_ssm_conv: sx [C][K-1+T], w [C][K] -> out [T][C]."""
+    sxs, sxp = _f32(sx)
+    ws, wp = _f32(w)
+    C, ncs = sxs.shape
+    K = ws.shape[1]
+    T = ncs - (K - 1)
+    out = np.zeros((T, C), dtype=np.float32)
+    lib().oracle_ssm_conv(sxp, C, T, K, wp, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return out
+
+
+def gdn_conv(x, w, state, sel: int = 0, n_snap: int = 1, n_qk: int = 0, d: int = 128, eps: float = 1e-6):
+    """GDN front end of one sequence: x [T][C], w [C][K], state [n_planes][C][K-1]
+    (not modified).  Returns (out [T][C] = silu(conv) with the first n_qk channels
+    L2-normalised per head of d, new state [n_planes][C][K-1] with slots
+    0..n_snap-1 rewritten)."""
+    xs, xp = _f32(x)
+    ws, wp = _f32(w)
+    st = np.array(state, dtype=np.float32, copy=True)
+    sp = st.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    T, C = xs.shape
+    K = ws.shape[1]
+    out = np.zeros((T, C), dtype=np.float32)
+    lib().oracle_gdn_conv(xp, T, C, K, wp, sp, st.shape[0], int(sel), int(n_snap), int(n_qk), int(d),
+                          float(eps), out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return out, st
+
+
+def rms_norm(x, eps: float = 1e-6, w=None, z=None):
+    """Per-row RMS norm over the last axis, then * w (broadcast over rows: [n], or
+    [H][n] cycling with the second-to-last axis) and * silu(z) (same shape as x)."""
+    xs, xp = _f32(x)
+    n = xs.shape[-1]
+    nrows = xs.size // n
+    f32p = ctypes.POINTER(ctypes.c_float)
+    wp, w_stride, w_period = _nullf32(), 0, 0
+    if w is not None:
+        ws, wp = _f32(w)
+        if ws.ndim == 2:
+            w_stride, w_period = n, ws.shape[0]
+    zp = _nullf32()
+    if z is not None:
+        zs, zp = _f32(z)
+    out = np.zeros(xs.shape, dtype=np.float32)
+    lib().oracle_rms_norm_rows(xp, nrows, n, float(eps), wp, w_stride, w_period, zp, out.ctypes.data_as(f32p))
+    return out
 
 
 def merge_lse(o_parts, lse_parts, gate=None):

@@ -363,6 +363,89 @@ void oracle_gdn(const float *q, const float *k, const float *v, const float *g,
     }
 }
 
+/* ------------------------------------------------------ gdn front end ---- */
+
+/*
+ * ggml_ssm_conv, as the reference's own kernel test states it
+ * (tests/kernel_verify.rs:840-853):
+ *     out[t][c] = sum_{k < K} sx[c][t + k] * w[c][k]
+ * sx [C][K-1+T] (ggml [K-1+T, C]), w [C][K] (ggml [K, C]), out [T][C] (ggml [C, T]);
+ * float accumulation in tap order.
+ */
+void oracle_ssm_conv(const float *sx, int64_t C, int64_t T, int64_t K, const float *w, float *out) {
+    const int64_t ncs = K - 1 + T;
+    for (int64_t t = 0; t < T; t++)
+        for (int64_t c = 0; c < C; c++) {
+            float s = 0.0f;
+            for (int64_t k = 0; k < K; k++) s += sx[c * ncs + t + k] * w[c * K + k];
+            out[t * C + c] = s;
+        }
+}
+
+/* ggml_silu: x / (1 + exp(-x))  (tests/kernel_verify.rs:989). */
+static float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+/*
+ * The GDN front end of build_gdn_layer for one sequence (gdn.rs:290-441):
+ *   conv_input = concat(history plane `sel` [C][K-1], x^T)      (gdn.rs:353-356)
+ *   y = silu(ssm_conv(conv_input, w))                           (gdn.rs:358-360)
+ *   q, k = channels [0, n_qk/2), [n_qk/2, n_qk) L2-normalised per head of d
+ *                                                                (gdn.rs:436-441)
+ * and the conv-history writeback of gdn_step (graph.rs:913-961): with n_snap == 1
+ * plane 0 <- conv_input rows [T, T+K-1); otherwise slot s < n_snap <- rows
+ * [max(T-s, 0), +K-1) ("s tokens back").  Every slot is computed from the input
+ * history and x before any plane is written.
+ *   x [T][C]; state [n_planes][C][K-1]; out [T][C].
+ */
+void oracle_gdn_conv(const float *x, int64_t T, int64_t C, int64_t K, const float *w, float *state,
+                     int64_t n_planes, int64_t sel, int64_t n_snap, int64_t n_qk, int64_t d, float eps,
+                     float *out) {
+    const int64_t ncs = K - 1 + T;
+    float *sx = (float *)malloc(sizeof(float) * (size_t)(C * ncs));
+    for (int64_t c = 0; c < C; c++) {
+        for (int64_t r = 0; r < K - 1; r++) sx[c * ncs + r] = state[(sel * C + c) * (K - 1) + r];
+        for (int64_t t = 0; t < T; t++) sx[c * ncs + K - 1 + t] = x[t * C + c];
+    }
+    oracle_ssm_conv(sx, C, T, K, w, out);
+    for (int64_t i = 0; i < T * C; i++) out[i] = silu_f(out[i]);
+    for (int64_t t = 0; t < T; t++)
+        if (n_qk > 0) oracle_l2norm_rows(out + t * C, n_qk / d, d, eps);
+    (void)n_planes;
+    for (int64_t s = 0; s < n_snap; s++) {
+        int64_t r0 = T - s;
+        if (r0 < 0) r0 = 0;
+        for (int64_t c = 0; c < C; c++)
+            for (int64_t r = 0; r < K - 1; r++) state[(s * C + c) * (K - 1) + r] = sx[c * ncs + r0 + r];
+    }
+    free(sx);
+}
+
+/*
+ * ggml_rms_norm over rows of n (sum of squares in double, as ggml-cpu's ggml_float;
+ * y = x * (1/sqrtf(mean + eps))), then optionally * w[i] (per-head RMS norm of Q/K,
+ * attn.rs:66-84) and * silu(z[i]) (norm_gated, gdn.rs:150-181: rms_norm(x) * w, then
+ * * silu(z)).  w and z may be NULL.  w_stride: elements between the weight rows of
+ * consecutive rows' heads (0 = one shared [n] weight); rows of w cycle with period
+ * w_period rows (the head index).
+ */
+void oracle_rms_norm_rows(const float *x, int64_t nrows, int64_t n, float eps, const float *w,
+                          int64_t w_stride, int64_t w_period, const float *z, float *out) {
+    for (int64_t r = 0; r < nrows; r++) {
+        const float *a = x + r * n;
+        double sum = 0.0;
+        for (int64_t i = 0; i < n; i++) sum += (double)a[i] * (double)a[i];
+        const float mean = (float)(sum / (double)n);
+        const float scale = 1.0f / sqrtf(mean + eps);
+        const float *wr = w ? w + (w_period > 0 ? r % w_period : 0) * w_stride : NULL;
+        for (int64_t i = 0; i < n; i++) {
+            float y = a[i] * scale;
+            if (wr) y = y * wr[i];
+            if (z) y = y * silu_f(z[r * n + i]);
+            out[r * n + i] = y;
+        }
+    }
+}
+
 /* Thread control for the timed CPU baseline. */
 int oracle_set_threads(int n) {
 #ifdef _OPENMP

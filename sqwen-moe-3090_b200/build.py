@@ -19,7 +19,8 @@ BUILD = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "sqmix", "libsqmix.so")
 INCLUDE = os.path.join(REPO, "include")
 
-SOURCES = ["host.cpp", "kv_append.cu", "fa_decode.cu", "fa_prefill.cu", "gdn.cu", "gdn_chunk.cu", "peer_merge.cu"]
+SOURCES = ["host.cpp", "kv_append.cu", "fa_decode.cu", "fa_prefill.cu", "gdn.cu", "gdn_chunk.cu", "gdn_front.cu",
+           "peer_merge.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", INCLUDE, "-I", CSRC,
          "--expt-relaxed-constexpr"]

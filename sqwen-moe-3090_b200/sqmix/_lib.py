@@ -103,6 +103,26 @@ class GdnArgs(ctypes.Structure):
     ]
 
 
+class GdnConvArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", c_void_p), ("x_dtype", c_int32), ("x_stride_tok", c_int64), ("x_stride_seq", c_int64),
+        ("weight", c_void_p), ("conv_state", c_void_p), ("n_planes", c_int32), ("sel", c_void_p),
+        ("n_snap", c_int32), ("n_seqs", c_int32), ("n_tokens", c_int32), ("channels", c_int32),
+        ("kernel", c_int32), ("head_dim", c_int32), ("n_qk_channels", c_int32), ("l2_eps", c_float),
+        ("out", c_void_p),
+    ]
+
+
+class HeadNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", c_void_p), ("x_dtype", c_int32), ("x_stride_tok", c_int64), ("x_stride_head", c_int64),
+        ("weight", c_void_p), ("weight_stride_head", c_int64), ("z", c_void_p), ("z_dtype", c_int32),
+        ("z_stride_tok", c_int64), ("z_stride_head", c_int64), ("n_tokens", c_int32), ("n_heads", c_int32),
+        ("head_dim", c_int32), ("eps", c_float), ("out", c_void_p), ("out_stride_tok", c_int64),
+        ("out_stride_head", c_int64),
+    ]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "sqmix_version": (ctypes.c_char_p, []),
@@ -132,6 +152,8 @@ _SIGNATURES = {
                                             c_void_p, c_void_p]),
     "sqmix_gdn_decode": (ctypes.c_int, [ctypes.POINTER(GdnArgs), c_void_p]),
     "sqmix_gdn_state_copy": (ctypes.c_int, [c_void_p, c_void_p, c_int64, c_int32, c_void_p]),
+    "sqmix_gdn_conv": (ctypes.c_int, [ctypes.POINTER(GdnConvArgs), c_void_p]),
+    "sqmix_head_norm": (ctypes.c_int, [ctypes.POINTER(HeadNormArgs), c_void_p]),
     "sqmix_kvcache_create": (ctypes.c_int, [c_int32, c_int64, c_int32, ctypes.POINTER(c_void_p)]),
     "sqmix_kvcache_destroy": (None, [c_void_p]),
     "sqmix_kvcache_zero": (ctypes.c_int, [c_void_p, c_void_p]),

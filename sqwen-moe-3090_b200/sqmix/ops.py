@@ -21,7 +21,8 @@ import math
 
 import torch
 
-from ._lib import (SQMIX_BF16, SQMIX_F16, SQMIX_F32, SQMIX_FA_OVERLAP_PREV, FaArgs, FaBatchArgs, GdnArgs, KvAppendArgs, check, lib)
+from ._lib import (SQMIX_BF16, SQMIX_F16, SQMIX_F32, SQMIX_FA_OVERLAP_PREV, FaArgs, FaBatchArgs, GdnArgs, GdnConvArgs,
+                   HeadNormArgs, KvAppendArgs, check, lib)
 
 HEAD_DIM = 256
 N_HEAD = 16
@@ -341,6 +342,69 @@ def gdn_state_copy(dst: torch.Tensor, src: torch.Tensor, plane_elems: int, n_pla
     _require_cuda(dst, src)
     check(lib().sqmix_gdn_state_copy(_ptr(dst), _ptr(src), int(plane_elems), int(n_planes),
                                      _stream(stream)), "gdn_state_copy")
+
+
+def gdn_conv(x: torch.Tensor, weight: torch.Tensor, conv_state: torch.Tensor, n_planes: int = 1,
+             sel: torch.Tensor | None = None, n_snap: int = 1, n_qk_channels: int = 0, l2_eps: float = 0.0,
+             head_dim: int = GDN_D, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """GDN short convolution (ggml_ssm_conv + silu, gdn.rs:290-360) with the history
+    planes, plus the per-head L2 norm of the first n_qk_channels channels when l2_eps > 0.
+
+    x [n_seqs][T][C] qkv_mixed (f32/bf16/f16, rows contiguous); weight [C][K] f32;
+    conv_state [n_seqs][n_planes][C][K-1] f32, updated in place (plane s <- the history
+    s tokens back for s < n_snap; the input plane is sel[seq]).  2-D x is one sequence.
+    Returns out [n_seqs][T][C] f32."""
+    _require_cuda(x, weight, conv_state, sel)
+    if x.dim() == 2:
+        x = x[None]
+    n_seqs, T, C = x.shape
+    if x.stride(-1) != 1:
+        raise ValueError("x rows must be contiguous")
+    if weight.dtype != torch.float32 or weight.dim() != 2 or weight.shape[0] != C or not weight.is_contiguous():
+        raise ValueError("weight must be contiguous float32 [C][K]")
+    K = weight.shape[1]
+    if (conv_state.dtype != torch.float32 or not conv_state.is_contiguous()
+            or conv_state.numel() != n_seqs * n_planes * C * (K - 1)):
+        raise ValueError("conv_state must be contiguous float32 [n_seqs][n_planes][C][K-1]")
+    if out is None:
+        out = torch.empty((n_seqs, T, C), dtype=torch.float32, device=x.device)
+    a = GdnConvArgs(x=_ptr(x), x_dtype=_dt(x), x_stride_tok=x.stride(1), x_stride_seq=x.stride(0),
+                    weight=_ptr(weight), conv_state=_ptr(conv_state), n_planes=int(n_planes), sel=_ptr(sel),
+                    n_snap=int(n_snap), n_seqs=n_seqs, n_tokens=T, channels=C, kernel=K, head_dim=int(head_dim),
+                    n_qk_channels=int(n_qk_channels), l2_eps=float(l2_eps), out=_ptr(out))
+    check(lib().sqmix_gdn_conv(ctypes.byref(a), _stream(stream)), "gdn_conv")
+    return out
+
+
+def head_norm(x: torch.Tensor, eps: float = 1e-6, weight: torch.Tensor | None = None,
+              z: torch.Tensor | None = None, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Per-head RMS norm over the last axis of x [T][H][d] (any strides with a unit
+    last stride): x / sqrt(mean(x^2) + eps), then * weight ([d] or [H][d], f32) and
+    * silu(z) (z shaped like x).  Q/K norm of the attention layers (attn.rs:66-84) and
+    norm_gated of the GDN output (gdn.rs:150-181).  Returns out f32 [T][H][d]."""
+    _require_cuda(x, weight, z)
+    if x.dim() == 2:
+        x = x[:, None]
+    T, H, d = x.shape
+    if x.stride(-1) != 1 or (z is not None and (z.shape != x.shape or z.stride(-1) != 1)):
+        raise ValueError("x and z must be [T][H][d] with a unit last stride")
+    w_sh = 0
+    if weight is not None:
+        if weight.dtype != torch.float32 or not weight.is_contiguous():
+            raise ValueError("weight must be contiguous float32")
+        if weight.numel() == H * d:
+            w_sh = d
+        elif weight.numel() != d:
+            raise ValueError("weight must be [d] or [H][d]")
+    if out is None:
+        out = torch.empty((T, H, d), dtype=torch.float32, device=x.device)
+    a = HeadNormArgs(x=_ptr(x), x_dtype=_dt(x), x_stride_tok=x.stride(0), x_stride_head=x.stride(1),
+                     weight=_ptr(weight), weight_stride_head=w_sh, z=_ptr(z), z_dtype=_dt(z) if z is not None else 0,
+                     z_stride_tok=z.stride(0) if z is not None else 0, z_stride_head=z.stride(1) if z is not None else 0,
+                     n_tokens=T, n_heads=H, head_dim=d, eps=float(eps), out=_ptr(out),
+                     out_stride_tok=out.stride(0), out_stride_head=out.stride(1))
+    check(lib().sqmix_head_norm(ctypes.byref(a), _stream(stream)), "head_norm")
+    return out
 
 
 def rope_theta_scale(freq_base: float, n_rot: int) -> float:

@@ -56,6 +56,28 @@ def test_argument_validation_without_gpu(sqmix_lib):
     assert L.sqmix_kv_convert_rows(fake, fake, 256, 200, 100, 0, 1, None) == sqmix_lib.SQMIX_EINVAL
 
 
+def test_front_end_argument_validation_without_gpu(sqmix_lib):
+    from sqmix._lib import GdnConvArgs, HeadNormArgs
+
+    L = sqmix_lib.lib()
+    fake = ctypes.c_void_p(256)
+    ok = dict(x=fake, x_dtype=0, x_stride_tok=8192, x_stride_seq=8192, weight=fake, conv_state=fake, n_planes=2,
+              n_snap=1, n_seqs=1, n_tokens=1, channels=8192, kernel=4, head_dim=128, n_qk_channels=4096,
+              l2_eps=1e-6, out=fake)
+    for bad, what in ((dict(kernel=9), b"kernel=9"), (dict(head_dim=100), b"head_dim=100"),
+                      (dict(channels=8000), b"channels=8000"), (dict(n_snap=3), b"n_snap=3"),
+                      (dict(n_qk_channels=100), b"n_qk_channels=100"), (dict(out=None), b"null"),
+                      (dict(x_stride_tok=100), b"x strides")):
+        a = GdnConvArgs(**{**ok, **bad})
+        assert L.sqmix_gdn_conv(ctypes.byref(a), None) == sqmix_lib.SQMIX_EINVAL, bad
+        assert what in L.sqmix_last_error(), (bad, L.sqmix_last_error())
+    h = HeadNormArgs(x=fake, x_dtype=7, out=fake, n_tokens=1, n_heads=1, head_dim=128)
+    assert L.sqmix_head_norm(ctypes.byref(h), None) == sqmix_lib.SQMIX_EINVAL
+    assert b"dtype 7" in L.sqmix_last_error()
+    h = HeadNormArgs(x=fake, x_dtype=0, out=fake, n_tokens=1, n_heads=1, head_dim=128, eps=-1.0)
+    assert L.sqmix_head_norm(ctypes.byref(h), None) == sqmix_lib.SQMIX_EINVAL
+
+
 def test_workspace_sizes(sqmix_lib):
     assert sqmix_lib.fa_workspace_bytes(1, 148) >= 148 * 16 * 256 * 4
     assert sqmix_lib.fa_workspace_bytes(2, 148) >= 2 * 148 * 16 * 256 * 4

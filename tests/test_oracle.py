@@ -264,3 +264,117 @@ def test_l2norm_is_unit(oracle):
     x = rng.standard_normal((10, 128)).astype(np.float32) * 3
     y = oracle.l2norm(x, 1e-6)
     assert np.allclose(np.linalg.norm(y, axis=-1), 1.0, atol=1e-5)
+
+
+# ------------------------------------------------------- gdn front end ---
+
+class KvRng:
+    """The reference's test generator (tests/kernel_verify.rs:228-245), restated so
+    that the front-end checks below run on the very inputs of its kernel tests."""
+
+    def __init__(self, seed):
+        self.s = (seed ^ 0x9E3779B97F4A7C15) & 0xFFFFFFFFFFFFFFFF
+
+    def next_u32(self):
+        self.s = (self.s * 6364136223846793005 + 1442695040888963407) & 0xFFFFFFFFFFFFFFFF
+        return self.s >> 33
+
+    def f32(self, lo, hi, n):
+        out = np.empty(n, dtype=np.float32)
+        for i in range(n):
+            u = np.float32((self.next_u32() >> 8) / float(1 << 24))
+            out[i] = np.float32(lo) + np.float32(hi - lo) * u
+        return out
+
+
+def test_ssm_conv_reference_case(oracle):
+    # tests/kernel_verify.rs:827-867: d_conv 4, n_t 3, d_inner 128, Rng(8) in [-1, 1)
+    K, T, C = 4, 3, 128
+    ncs = K - 1 + T
+    rng = KvRng(8)
+    sx = rng.f32(-1.0, 1.0, ncs * C).reshape(C, ncs)
+    c = rng.f32(-1.0, 1.0, K * C).reshape(C, K)
+    want = np.zeros((T, C), dtype=np.float32)
+    for t in range(T):
+        for i in range(C):
+            s = np.float32(0.0)
+            for k in range(K):
+                s = np.float32(s + np.float32(sx[i, t + k] * c[i, k]))
+            want[t, i] = s
+    got = oracle.ssm_conv(sx, c)
+    assert np.array_equal(got, want)
+
+
+def test_silu_reference_case(oracle):
+    # tests/kernel_verify.rs:981-989: Rng(11) in [-4, 4), silu = x / (1 + exp(-x))
+    x = KvRng(11).f32(-4.0, 4.0, 32)
+    sx = np.zeros((32, 4), dtype=np.float32)
+    sx[:, 3] = x  # a conv with the single tap w = 1 is the identity: silu(conv) = silu(x)
+    w = np.zeros((32, 4), dtype=np.float32)
+    w[:, 3] = 1.0
+    out, _ = oracle.gdn_conv(x[None, :], w, np.zeros((1, 32, 3), np.float32))
+    want = x / (1.0 + np.exp(-x.astype(np.float64)))
+    assert np.abs(out[0] - want).max() <= 1e-6 * np.abs(want).max()
+
+
+def _conv_case(T, C=256, K=4, n_planes=3, seed=0):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, C)).astype(np.float32)
+    w = (rng.standard_normal((C, K)) * 0.5).astype(np.float32)
+    st = rng.standard_normal((n_planes, C, K - 1)).astype(np.float32)
+    return x, w, st
+
+
+def test_gdn_conv_vs_numpy(oracle):
+    # conv over concat(history, x), silu, per-head L2 norm of the q/k channels
+    T, C, K, d, n_qk = 5, 256, 4, 64, 128
+    x, w, st = _conv_case(T, C, K)
+    out, new = oracle.gdn_conv(x, w, st, sel=1, n_snap=1, n_qk=n_qk, d=d)
+    sx = np.concatenate([st[1].astype(np.float64), x.T.astype(np.float64)], axis=1)  # [C][K-1+T]
+    y = np.stack([(sx[:, t:t + K] * w).sum(axis=1) for t in range(T)])
+    y = y / (1.0 + np.exp(-y))
+    for h in range(n_qk // d):
+        blk = y[:, h * d:(h + 1) * d]
+        y[:, h * d:(h + 1) * d] = blk / np.sqrt((blk * blk).sum(axis=1, keepdims=True) + 1e-6)
+    assert np.abs(out - y).max() <= 1e-5 * np.abs(y).max()
+    # n_snap 1: plane 0 <- the last K-1 conv inputs, other planes untouched
+    assert np.array_equal(new[0], sx[:, T:T + K - 1].astype(np.float32))
+    assert np.array_equal(new[1:], st[1:])
+
+
+def test_gdn_conv_chunk_carry_and_rollback_slots(oracle):
+    # T tokens at once == T one-token steps (the conv tail carries the history), and
+    # slot s of an n_snap run == the plane-0 tail of a run over the first T - s tokens
+    # (graph.rs:913-961; slots with s > T keep the input history)
+    T, C, K = 6, 128, 4
+    x, w, st = _conv_case(T, C, K, n_planes=4, seed=3)
+    out_all, new_all = oracle.gdn_conv(x, w, st, sel=0, n_snap=4)
+    cur = st.copy()
+    outs = []
+    for t in range(T):
+        o, cur = oracle.gdn_conv(x[t:t + 1], w, cur, sel=0, n_snap=1)
+        outs.append(o[0])
+    assert np.array_equal(np.stack(outs), out_all)
+    assert np.array_equal(cur[0], new_all[0])
+    for s in range(4):
+        _, short = oracle.gdn_conv(x[:T - s], w, st, sel=0, n_snap=1)
+        assert np.array_equal(new_all[s], short[0]), s
+    _, tiny = oracle.gdn_conv(x[:2], w, st, sel=0, n_snap=4)
+    assert np.array_equal(tiny[3], st[0])  # s = 3 > T = 2: the input history
+
+
+def test_rms_norm_and_norm_gated_vs_numpy(oracle):
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((3, 4, 128)).astype(np.float32)
+    z = rng.standard_normal((3, 4, 128)).astype(np.float32)
+    w1 = rng.standard_normal(128).astype(np.float32)
+    w2 = rng.standard_normal((4, 128)).astype(np.float32)
+    xd = x.astype(np.float64)
+    r = xd / np.sqrt((xd * xd).mean(axis=-1, keepdims=True) + 1e-6)
+    silu = z / (1.0 + np.exp(-z.astype(np.float64)))
+    for w, wb in ((w1, w1[None, None]), (w2, w2[None])):
+        got = oracle.rms_norm(x, 1e-6, w=w, z=z)
+        want = r * wb * silu
+        assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
+    got = oracle.rms_norm(x, 1e-6)
+    assert np.abs(got - r).max() <= 1e-5 * np.abs(r).max()
