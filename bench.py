@@ -634,7 +634,76 @@ def bench_gdn(steps: int, warmup: int):
     flops = 2.68e9  # chunked form, 8 chunks x 32 heads (C = 64, d = 128)
     res["prefill512"] = {"us": us, "tok_s": T / us * 1e6, "tflops_chunked_form": flops / us / 1e6,
                          "note": "one layer, chunk 64, eager launches"}
+    res["front_end"] = bench_gdn_front(g, dev, steps, warmup, hbm, hbm_kind)
     res["config"] = "config1: 32 value heads over 16 q/k heads, d 128, bf16 q/k/v, fused L2 norm"
+    return res
+
+
+def _graph_us(fn, n_calls: int, reps: int, warmup: int) -> float:
+    """Device time per call of fn (n_calls launches captured in one CUDA graph)."""
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    for _ in range(max(warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del graph
+    return e0.elapsed_time(e1) * 1e3 / (reps * n_calls)
+
+
+def bench_gdn_front(g, dev, steps: int, warmup: int, hbm: float, hbm_kind: str) -> dict:
+    """The GDN front end around the recurrence (config 1 shapes): short conv + SiLU + q/k
+    L2 norm with the conv history (C = 8192 channels, K = 4), and norm_gated of the
+    output (32 heads x 128, bf16 gate z); decode (1 token, 30 layers' buffers cycled) and
+    a 512-token prefill chunk."""
+    import torch
+
+    import sqmix
+
+    C, K, n_layers, reps = 8192, 4, 30, max(3, steps)
+    res = {}
+    for T in (1, 512):
+        x = torch.randn((n_layers, 1, T, C), generator=g, device=dev).to(torch.bfloat16)
+        w = torch.randn((n_layers, C, K), generator=g, device=dev) * 0.5
+        st = torch.randn((n_layers, 1, 1, C, K - 1), generator=g, device=dev)
+        out = torch.empty((1, T, C), device=dev)
+        z = torch.randn((n_layers, T, 32, 128), generator=g, device=dev).to(torch.bfloat16)
+        o = torch.randn((n_layers, T, 32, 128), generator=g, device=dev)
+        wn = torch.randn((128,), generator=g, device=dev)
+        y = torch.empty((T, 32, 128), device=dev)
+
+        def conv_all():
+            for l in range(n_layers):
+                sqmix.gdn_conv(x[l], w[l], st[l], n_qk_channels=4096, l2_eps=1e-6, out=out)
+
+        def norm_all():
+            for l in range(n_layers):
+                sqmix.head_norm(o[l], 1e-6, weight=wn, z=z[l], out=y)
+
+        us_c = _graph_us(conv_all, n_layers, reps, warmup)
+        us_n = _graph_us(norm_all, n_layers, reps, warmup)
+        alg_c = T * C * (2 + 4) + C * K * 4 + 2 * C * (K - 1) * 4  # x bf16 in, out f32, taps, history r+w
+        alg_n = T * 32 * 128 * (4 + 2 + 4) + 128 * 4  # o f32 in, z bf16 in, y f32 out
+        key = "decode" if T == 1 else f"prefill{T}"
+        res[key] = {
+            "conv_us": us_c, "conv_alg_bytes": alg_c, "conv_frac_of_hbm": alg_c / us_c / 1e3 / hbm,
+            "norm_gated_us": us_n, "norm_gated_alg_bytes": alg_n,
+            "norm_gated_frac_of_hbm": alg_n / us_n / 1e3 / hbm, "peak_gbs": hbm, "peak_kind": hbm_kind}
+    res["note"] = ("CUDA graphs of 30 PDL-chained launches (one per GDN layer, buffers cycled); decode is "
+                   "launch/latency bound (a few hundred KB per launch)")
     return res
 
 

@@ -365,7 +365,10 @@ int sqmix_gdn_state_copy(float *dst, const float *src, int64_t plane_elems, int3
  * written back: plane s < n_snap <- conv_input rows [max(T - s, 0), +K-1)
  * (plane 0 = the tail; slot s = the history s tokens back, graph.rs:913-961).
  * Conv history: [n_seqs][n_planes][C][K-1] f32, i.e. ggml's [K-1, C, 1+n_rs] per
- * sequence.  The plane read may be among the planes written (updated in place). */
+ * sequence.  The plane read may be among the planes written (updated in place).
+ * x, weight, conv_state and out 16-byte aligned; x strides multiples of 4 elements.
+ * Launched with programmatic stream serialisation (the taps are read before the wait
+ * on the previous kernel; x and the history after it). */
 typedef struct sqmix_gdn_conv_args {
     const void *x;            /* [n_seqs][T][C] qkv_mixed (ggml [C, T]) */
     int32_t x_dtype;
@@ -374,13 +377,14 @@ typedef struct sqmix_gdn_conv_args {
     const float *weight;      /* [C][K] ssm_conv1d (ggml [K, C]) */
     float *conv_state;        /* [n_seqs][n_planes][C][K-1] */
     int32_t n_planes;
-    const int32_t *sel;       /* device I32 [n_seqs]: plane read as history; NULL = 0 */
+    const int32_t *sel;       /* device I32 [n_seqs]: plane read as history (clamped to
+                                 [0, n_planes)); NULL = 0 */
     int32_t n_snap;           /* planes written, 1 <= n_snap <= n_planes */
     int32_t n_seqs;
     int32_t n_tokens;         /* T >= 1 */
     int32_t channels;         /* C = 2*H_k*d + H_v*d (8192), a multiple of head_dim */
     int32_t kernel;           /* K in 2..8 (4: ssm_d_conv) */
-    int32_t head_dim;         /* d (128): a multiple of 32 in [32, 256] */
+    int32_t head_dim;         /* d: 128 (ssm_d_state) */
     int32_t n_qk_channels;    /* leading channels normalised per head (2*H_k*d) */
     float l2_eps;             /* > 0: L2 norm of those channels (norm_rms_eps); 0: none */
     float *out;               /* [n_seqs][T][C] f32 */
@@ -392,7 +396,9 @@ int sqmix_gdn_conv(const sqmix_gdn_conv_args *args, sqmix_stream_t stream);
  * per-head Q/K norm of the attention layers, attn.rs:66-84 and :166-175) and
  * * silu(z) (norm_gated of the GDN output, gdn.rs:150-181 and :565-573).
  * x, z [T][H][head_dim] with element strides; out f32.  out may equal x (f32, same
- * strides): each row is read completely before it is written. */
+ * strides): each row is read completely before it is written.  head_dim 128 or 256;
+ * pointers 16-byte aligned, strides multiples of 4 elements.  Launched with
+ * programmatic stream serialisation. */
 typedef struct sqmix_head_norm_args {
     const void *x;
     int32_t x_dtype;
