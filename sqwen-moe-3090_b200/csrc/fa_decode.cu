@@ -125,77 +125,83 @@ constexpr float kTwo24 = 16777216.0f;
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
-// Log-sum-exp merge of the split partials for one 32-dim slice of one output row:
-// warp w folds splits w, w + nwarps, ... with an online (max, sum) update, 8 splits
-// in flight at a time; the warps then combine through shared memory `red`
-// (nwarps * 34 floats).  Reads bypass L1: the partials were written by other CTAs.
-// gate_factor: sigmoid(gate) of this thread's output element (1 without a gate),
-// computed by the caller ahead of time.
+// Log-sum-exp merge of the split partials for one 32-dim slice of one output row, by
+// a CTA of 256 threads (thread = dim lane x split group of 8).  The per-split weights
+// w_s = 2^((m_s - M) c) are computed once per split (not once per dim) into shared
+// memory; every partial load is issued before the first reduction, so a merge of up
+// to 8 * kPre splits costs one round trip to L2.  Reads bypass L1: the partials were
+// written by other CTAs.  gate_factor: sigmoid(gate) of this thread's output element
+// (1 without a gate), computed by the caller ahead of time.
+constexpr int kMergeMaxSplits = 4096;
+struct MergeSmem {
+    float w[kMergeMaxSplits];  // m_s, then the weight of split s
+    float l[kMergeMaxSplits];
+    float red[8][33];
+    float wm[8];
+};
+
 __device__ void merge_slice(const float *part_o, const float *part_ml, int n_splits, int n_rows, int row,
-                            int slice, float c, float scale, float gate_factor, float *out, float *lse, float *red,
-                            int nwarps) {
-    constexpr int kChunk = 24;  // splits per warp per round: 8 warps x 24 covers 192 splits at once
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+                            int slice, float c, float scale, float gate_factor, float *out, float *lse,
+                            MergeSmem &sm) {
+    constexpr int kPre = 24;  // o loads per thread issued up front (8 * 24 = 192 splits)
+    const int tid = threadIdx.x, lane = tid & 31, grp = tid >> 5;
     const int d = slice * 32 + lane;
     const size_t sstride = static_cast<size_t>(n_rows) * 256;
     const float *po = part_o + static_cast<size_t>(row) * 256 + d;
     const float *pml = part_ml + static_cast<size_t>(row) * 2;
-    float M = -INFINITY, Ls = 0.f, acc = 0.f;
-    if (warp < nwarps) {
-        for (int s0 = warp; s0 < n_splits; s0 += kChunk * nwarps) {
-            float mv[kChunk], lv[kChunk], ov[kChunk];
+    float ov[kPre];
 #pragma unroll
-            for (int j = 0; j < kChunk; ++j) {
-                const int s = s0 + nwarps * j;
-                if (s < n_splits) {
-                    const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pml + static_cast<size_t>(s) * n_rows * 2));
-                    mv[j] = ml.x;
-                    lv[j] = ml.y;
-                    ov[j] = __ldcg(po + s * sstride);
-                } else {
-                    mv[j] = -INFINITY;
-                    lv[j] = 0.f;
-                    ov[j] = 0.f;
-                }
-            }
-            float mc = M;
-#pragma unroll
-            for (int j = 0; j < kChunk; ++j) mc = fmaxf(mc, mv[j]);
-            if (mc != -INFINITY) {
-                const float r = (M == -INFINITY) ? 0.f : ex2((M - mc) * c);
-                Ls *= r;
-                acc *= r;
-#pragma unroll
-                for (int j = 0; j < kChunk; ++j) {
-                    const float w = (mv[j] == -INFINITY) ? 0.f : ex2((mv[j] - mc) * c);
-                    Ls = fmaf(lv[j], w, Ls);
-                    acc = fmaf(ov[j], w, acc);
-                }
-                M = mc;
-            }
-        }
-        red[warp * 34 + lane] = acc;
-        if (lane == 0) {
-            red[warp * 34 + 32] = M;
-            red[warp * 34 + 33] = Ls;
-        }
+    for (int j = 0; j < kPre; ++j) {
+        const int s = grp + 8 * j;
+        ov[j] = s < n_splits ? __ldcg(po + s * sstride) : 0.f;
     }
+    // running maxima: thread t holds splits t, t + 256, ...
+    float m_loc = -INFINITY;
+    for (int s = tid; s < n_splits; s += 256) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pml + static_cast<size_t>(s) * n_rows * 2));
+        sm.w[s] = ml.x;  // the weight replaces it below
+        sm.l[s] = ml.y;
+        m_loc = fmaxf(m_loc, ml.x);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m_loc = fmaxf(m_loc, __shfl_xor_sync(0xffffffffu, m_loc, off));
+    if (lane == 0) sm.wm[grp] = m_loc;
     __syncthreads();
-    if (warp == 0) {
-        float Mt = -INFINITY;
-        for (int w = 0; w < nwarps; ++w) Mt = fmaxf(Mt, red[w * 34 + 32]);
+    float M = sm.wm[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) M = fmaxf(M, sm.wm[i]);
+    // weights and the sum of l_s w_s
+    float l_loc = 0.f;
+    for (int s = tid; s < n_splits; s += 256) {
+        const float m = sm.w[s];
+        const float w = (m == -INFINITY) ? 0.f : ex2((m - M) * c);
+        sm.w[s] = w;
+        l_loc = fmaf(sm.l[s], w, l_loc);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) l_loc += __shfl_xor_sync(0xffffffffu, l_loc, off);
+    __syncthreads();  // weights visible; wm reused below
+    if (lane == 0) sm.wm[grp] = l_loc;
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+        const int s = grp + 8 * j;
+        if (s < n_splits) acc = fmaf(ov[j], sm.w[s], acc);
+    }
+    for (int s = grp + 8 * kPre; s < n_splits; s += 8) acc = fmaf(__ldcg(po + s * sstride), sm.w[s], acc);
+    sm.red[grp][lane] = acc;
+    __syncthreads();
+    if (grp == 0) {
         float L = 0.f, y = 0.f;
-        for (int w = 0; w < nwarps; ++w) {
-            const float mw = red[w * 34 + 32];
-            const float wt = (mw == -INFINITY) ? 0.f : ex2((mw - Mt) * c);
-            L = fmaf(red[w * 34 + 33], wt, L);
-            y = fmaf(red[w * 34 + lane], wt, y);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            L += sm.wm[i];
+            y += sm.red[i][lane];
         }
         y = L > 0.f ? y / L : 0.f;
         out[static_cast<size_t>(row) * 256 + d] = y * gate_factor;
-        if (lse && slice == 0 && lane == 0) lse[row] = L > 0.f ? Mt * scale + logf(L) : -INFINITY;
+        if (lse && slice == 0 && lane == 0) lse[row] = L > 0.f ? M * scale + logf(L) : -INFINITY;
     }
-    __syncthreads();  // `red` is reused by the next slice
 }
 
 template <int NQ, int WPH, int GPW, int NSTAGE, int MINB>
@@ -314,22 +320,25 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     launch_dependents();
 
     // ---- Q and the step's new K/V rows (produced by earlier kernels: after the wait) --
-    constexpr int kQPer = NQ * 16 * 256 / L::kThreads;
+    constexpr int kQElems = NQ * 16 * 256;
+    constexpr int kQPer = (kQElems + L::kThreads - 1) / L::kThreads;
     float qv[kQPer];
 #pragma unroll
     for (int k = 0; k < kQPer; ++k) {
         const int e = threadIdx.x + k * L::kThreads;  // [qi][head][256]
-        qv[k] = load_act(p.q, seq * p.q_sseq + (e >> 12) * p.q_st + ((e >> 8) & 15) * p.q_sh + (e & 255),
-                         p.q_dtype);
+        qv[k] = e < kQElems ? load_act(p.q, seq * p.q_sseq + (e >> 12) * p.q_st + ((e >> 8) & 15) * p.q_sh + (e & 255),
+                                       p.q_dtype)
+                            : 0.f;
     }
-    constexpr int kKvPer = NQ * 2 * 512 / L::kThreads;
+    constexpr int kKvElems = NQ * 2 * 512;
+    constexpr int kKvPer = (kKvElems + L::kThreads - 1) / L::kThreads;
     float kvv[kKvPer];
     if (has_fresh) {
 #pragma unroll
         for (int k = 0; k < kKvPer; ++k) {
             const int e = threadIdx.x + k * L::kThreads;  // [t][k|v][512]
             const int t = e >> 10, is_v = (e >> 9) & 1;
-            kvv[k] = t < p.n_new ? load_act(is_v ? p.v_new : p.k_new,
+            kvv[k] = e < kKvElems && t < p.n_new ? load_act(is_v ? p.v_new : p.k_new,
                                             seq * p.new_sseq + t * (is_v ? p.v_new_st : p.k_new_st) + (e & 511),
                                             p.kv_dtype)
                                  : 0.f;
@@ -346,10 +355,12 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     float *q_stage = reinterpret_cast<float *>(ring + (NSTAGE - kStagingSlots) * L::kStageBytes);
     float *kv_stage = q_stage + NQ * 16 * 256;
 #pragma unroll
-    for (int k = 0; k < kQPer; ++k) q_stage[threadIdx.x + k * L::kThreads] = qv[k];
+    for (int k = 0; k < kQPer; ++k)
+        if (threadIdx.x + k * L::kThreads < kQElems) q_stage[threadIdx.x + k * L::kThreads] = qv[k];
     if (has_fresh) {
 #pragma unroll
-        for (int k = 0; k < kKvPer; ++k) kv_stage[threadIdx.x + k * L::kThreads] = kvv[k];
+        for (int k = 0; k < kKvPer; ++k)
+            if (threadIdx.x + k * L::kThreads < kKvElems) kv_stage[threadIdx.x + k * L::kThreads] = kvv[k];
     }
     (void)kvv;
 
@@ -357,10 +368,9 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
 
     // ---- fused append: quantise the step's new K/V rows held by this CTA ----------
     if (has_fresh) {
-        // 32 blocks per new row; each warp quantises 4 of them at once (interleaved
-        // reductions), rows of another CTA's range are skipped
-        constexpr int kPerWarp = 32 / L::kWarps;
-        static_assert(32 % L::kWarps == 0, "blocks of a row per warp");
+        // 32 blocks per new row; each warp quantises up to ceil(32 / warps) of them at
+        // once (interleaved reductions), rows of another CTA's range are skipped
+        constexpr int kPerWarp = (32 + L::kWarps - 1) / L::kWarps;
         for (int t = 0; t < p.n_new; ++t) {
             const int64_t row = q_pos0 + t;
             const bool mine = row >= row_lo && row < row_hi;
@@ -370,12 +380,12 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
             bool isv[kPerWarp], live[kPerWarp];
 #pragma unroll
             for (int k = 0; k < kPerWarp; ++k) {
-                const int r = warp + L::kWarps * k;
+                const int r = (warp + L::kWarps * k) & 31;  // blocks past 31 are computed, not stored
                 isv[k] = r >> 4;
                 hh[k] = (r >> 3) & 1;
                 bb[k] = r & 7;
                 rows[k] = row;
-                live[k] = mine;
+                live[k] = mine && warp + L::kWarps * k < 32;
                 x[k] = kv_row_elem(kv_stage, ((t * 2 + isv[k]) * 2 + hh[k]) * 256, bb[k] * 32 + lane, SQMIX_F32,
                                    isv[k] ? 0 : p.rope_n_rot, rope_s + t * 32);
             }
@@ -740,10 +750,10 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     // four consecutive dims per thread (16-byte shared loads and global stores), all
     // of a thread's rows in flight at once
     constexpr int kVec4 = NQ * 16 * 64;
-    static_assert(kVec4 % L::kThreads == 0, "partial rows per thread");
 #pragma unroll
-    for (int k = 0; k < kVec4 / L::kThreads; ++k) {
+    for (int k = 0; k < (kVec4 + L::kThreads - 1) / L::kThreads; ++k) {
         const int i = threadIdx.x + k * L::kThreads;
+        if (i >= kVec4) break;
         const int d = (i & 63) * 4;
         const int head = (i >> 6) & 15;
         const int qi = i >> 10;
@@ -787,7 +797,7 @@ struct FaMergeParams {
 };
 
 __global__ void __launch_bounds__(256) fa_merge_kernel(FaMergeParams p) {
-    __shared__ float red[8 * 34];
+    __shared__ MergeSmem sm;
     const size_t seq = blockIdx.z;
     // The gate is an input of the decode call, produced before the decode kernel; the
     // decode kernel triggers this launch only after its own dependency wait, so the
@@ -803,8 +813,7 @@ __global__ void __launch_bounds__(256) fa_merge_kernel(FaMergeParams p) {
     launch_dependents();
     const size_t parts = seq * p.n_splits * p.n_rows;
     merge_slice(p.part_o + parts * 256, p.part_ml + parts * 2, p.n_splits, p.n_rows, blockIdx.x, blockIdx.y, p.c,
-                p.scale, gate_factor, p.out + seq * p.n_rows * 256, p.lse ? p.lse + seq * p.n_rows : nullptr, red,
-                8);
+                p.scale, gate_factor, p.out + seq * p.n_rows * 256, p.lse ? p.lse + seq * p.n_rows : nullptr, sm);
 }
 
 // Merge of normalised partials across GPUs: O = sum_p O_p e^(lse_p - L).
@@ -970,9 +979,10 @@ extern "C" int sqmix_fa_decode(const sqmix_fa_args *a, sqmix_stream_t stream) {
     // Kernel configurations (warps per KV head x groups per warp, ring stages):
     //   1: n_q 1, 4 warps/head x 2 groups per step, 5 x 36.9 KB slots
     //   2: n_q 2, 4 warps/head x 1 group per step, 5 x 36.9 KB slots
+    //   3: n_q 1, 6 warps/head x 1 group per step, 3 x 55.3 KB slots
     int cfg = a->config;
     if (cfg == 0) cfg = a->n_q == 1 ? 1 : 2;
-    SQMIX_CHECK_ARG(cfg >= 1 && cfg <= 2 && (cfg == 2) == (a->n_q == 2),
+    SQMIX_CHECK_ARG(cfg >= 1 && cfg <= 3 && (cfg == 2) == (a->n_q == 2),
                     "fa_decode: config %d does not serve n_q=%d", a->config, a->n_q);
     int n_splits = a->n_splits > 0 ? a->n_splits : sqmix_device_sm_count(-1);
     SQMIX_CHECK_ARG(n_splits >= 1 && n_splits <= 4096, "fa_decode: n_splits=%d", n_splits);
@@ -984,6 +994,7 @@ extern "C" int sqmix_fa_decode(const sqmix_fa_args *a, sqmix_stream_t stream) {
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     switch (cfg) {
         case 1: return launch_fa<1, 4, 2, 5, 1>(a, n_splits, st);
+        case 3: return launch_fa<1, 6, 1, 3, 1>(a, n_splits, st);
         default: return launch_fa<2, 4, 1, 5, 1>(a, n_splits, st);
     }
 }

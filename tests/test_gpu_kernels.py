@@ -239,6 +239,43 @@ def test_fa_decode_split_counts(sq, oracle, n_splits):
     assert rel_err(out, want) <= ATTN_TOL
 
 
+@pytest.mark.parametrize("n_kv,n_splits", [(1, 0), (17, 3), (257, 0), (1000, 7), (5000, 0), (5000, 300)])
+def test_fa_decode_config3_twelve_warps(sq, oracle, n_kv, n_splits):
+    """Configuration 3 (n_q 1, 6 warps per KV head, 3 x 55.3 KB ring slots): RoPE, gate,
+    lse and the fused append of the step's row, against the oracle."""
+    rng = np.random.default_rng(90 + n_kv + n_splits)
+    k = rng.standard_normal((n_kv, 2, 256)).astype(np.float32)
+    v = rng.standard_normal((n_kv, 2, 256)).astype(np.float32)
+    cap = cap_for(n_kv)
+    kc, vc = sq.new_kv_cache(cap), sq.new_kv_cache(cap)
+    kd_t, vd_t = torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda()
+    q_pos0 = n_kv - 1
+    if q_pos0 > 0:
+        sq.set_rows_q4_0(kd_t[:q_pos0], vd_t[:q_pos0], torch.arange(q_pos0, device="cuda"), kc, vc, cap,
+                         rope_n_rot=64, rope_freq_base=1e7)
+    q = rng.standard_normal((1, 16, 256)).astype(np.float32)
+    gate = rng.standard_normal((1, 16, 256)).astype(np.float32)
+    lse = torch.empty((1, 16), device="cuda")
+    ws = sq.new_fa_workspace(1, 300)
+    out = sq.flash_attn_ext(torch.from_numpy(q).cuda(), kc, vc, cap,
+                            torch.tensor([n_kv], dtype=torch.int64, device="cuda"),
+                            torch.tensor([q_pos0], dtype=torch.int64, device="cuda"),
+                            gate=torch.from_numpy(gate).cuda(), rope_n_rot=64, rope_freq_base=1e7, lse=lse,
+                            k_new=kd_t[q_pos0:], v_new=vd_t[q_pos0:], workspace=ws, n_splits=n_splits, config=3)
+    torch.cuda.synchronize()
+    sq.fa_status(ws)
+    kq = oracle.q4_0_quantize(oracle.rope_text(k, 0, 1e7, 64).reshape(n_kv, 512))
+    vq = oracle.q4_0_quantize(v.reshape(n_kv, 512))
+    assert np.array_equal(sq.kv_convert_rows(kc, cap, "k", 0, n_kv).cpu().numpy(), kq)
+    assert np.array_equal(sq.kv_convert_rows(vc, cap, "v", 0, n_kv).cpu().numpy(), vq)
+    kd = oracle.q4_0_dequantize(kq, 512).reshape(n_kv, 2, 256)
+    vd = oracle.q4_0_dequantize(vq, 512).reshape(n_kv, 2, 256)
+    want, wlse = oracle.attn(oracle.rope_text(q, q_pos0, 1e7, 64), kd, vd, gate, q_pos0=q_pos0, scale=1 / 16,
+                             want_lse=True)
+    assert rel_err(out.cpu().numpy(), want) <= ATTN_TOL
+    assert np.abs(lse.cpu().numpy() - wlse).max() < 1e-3
+
+
 def test_fa_decode_prefix_causal(sq, oracle):
     # queries at positions far below n_kv: only keys j <= q_pos0 + t count (graph.rs:553-559)
     rng = np.random.default_rng(40)
