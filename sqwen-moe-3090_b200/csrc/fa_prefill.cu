@@ -17,12 +17,14 @@
 // One CTA (13 warps):
 //   warp 0      TMEM allocation; lane 0 issues the MMAs: S = Q K^T (M 128, N 64,
 //               K 256; Q read from tensor memory) into one of two TMEM S buffers,
-//               then O += P V (M 128, N 256, K 64) into the TMEM O accumulator, in
+//               then O += P V (M 128, N 256, K 64; P read from tensor memory) into
+//               the TMEM O accumulator, in
 //               the order S(0) S(1) PV(0) S(2) PV(1) ... so that the tensor core
 //               computes the next S while the softmax warps work on the current one;
 //   warps 1-4   softmax: thread = row; reads S from TMEM, online softmax in the
 //               log2 domain with lazy rescaling (O is rescaled only when the row
-//               maximum grows by more than 2^8), writes P (f16) to shared memory,
+//               maximum grows by more than 2^8), writes P (f16, two keys per
+//               column) over the S buffer it has just read in tensor memory,
 //               and at the end of an item reads O and writes the partials;
 //   warps 5-12  producers: build Q (RoPE, f16) through a shared staging buffer into
 //               tensor memory, and dequantise K and V tiles from q4_0 into
@@ -54,8 +56,8 @@ constexpr uint32_t kStageOff = 0;       // 3 stages: K (4 x 8 KB regions) | V (4
 constexpr uint32_t kStageBytes = 65536;
 constexpr uint32_t kVInStage = 32768;
 constexpr uint32_t kKvRegion = 8192;    // 64 keys x 128 B
-constexpr uint32_t kPOff = 196608;      // 2 P buffers: 128 rows x 64 keys f16; at the
-constexpr uint32_t kPBytes = 16384;     // start of an item, the Q staging buffer
+constexpr uint32_t kPOff = 196608;      // Q staging buffer (128 rows x 512 B) at the
+                                        // start of an item
 constexpr uint32_t kRopeOff = 2 * kStageBytes + kVInStage;  // RoPE table while Q is built
 constexpr uint32_t kBarOff = 229376;
 constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
@@ -343,10 +345,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                 tc::fence_after();
 #pragma unroll
                 for (int ks = 0; ks < kPfKeys / 16; ++ks) {
-                    const uint64_t a = tc::desc_sw128(base_s + kPOff + bb * kPBytes + ks * 32, 16, 1024);
+                    // A = P (f16, two keys per column) in the first 32 columns of S buffer bb
                     const uint64_t b =
                         tc::desc_sw128(base_s + kStageOff + st * kStageBytes + kVInStage + ks * 2048, kKvRegion, 1024);
-                    tc::mma_ss(tmem + kOCol, a, b, idesc_pv, (!first || ks > 0) ? 1u : 0u);
+                    tc::mma_ts(tmem + kOCol, tmem + kSCol + bb * kPfKeys + ks * 8, b, idesc_pv,
+                               (!first || ks > 0) ? 1u : 0u);
                 }
                 tc::commit(&ctl->pv_done[st]);
                 return true;
@@ -456,16 +459,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                     ph[i >> 1] = pack_half2(p0, p1);
                 }
                 l_run += ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3])) + ((lsum[4] + lsum[5]) + (lsum[6] + lsum[7]));
-                // P buffer b was read by the PV of tile j - 2
-                if (j >= 2 && !wwait(&ctl->pv_done[(j - 2) % kNStage], stage_parity(j - 2))) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t prow = base_s + kPOff + b * kPBytes;
-#pragma unroll
-                for (int ch = 0; ch < 8; ++ch)
-                    sts128(prow + swz(r, ch), make_uint4(ph[4 * ch], ph[4 * ch + 1], ph[4 * ch + 2], ph[4 * ch + 3]));
-                tc::fence_proxy_async_smem();
+                // P replaces S in the first 32 columns of S buffer b (read above).  The PV
+                // of tile j - 2 that read the previous P there was issued before S(j),
+                // and the MMAs of one thread run in issue order.
+                tc::st32(tmem + lane_base + kSCol + b * kPfKeys, ph);
+                tc::wait_st();
                 tc::fence_before();
                 mbar_arrive(&ctl->p_full[b]);
             }
