@@ -161,6 +161,14 @@ typedef struct sqmix_fa_args {
     int64_t v_new_stride_tok;
     int32_t n_new;
     int32_t flags;            /* SQMIX_FA_* bits below, 0 = none */
+    /* Per-head RMS norm before RoPE (head_rms_norm of attn.rs:66-84, applied to Q and
+     * K at attn.rs:166-175): x / sqrt(mean(x^2) + norm_eps) * w over each 256-wide
+     * head, for the Q rows and for the fused-append K rows.  NULL: the inputs are
+     * already normalised.  Decode only: sqmix_fa_prefill rejects them (normalise with
+     * sqmix_head_norm first). */
+    const float *q_norm;      /* nullable [256] attn_q_norm weight */
+    const float *k_norm;      /* nullable [256] attn_k_norm weight */
+    float norm_eps;           /* norm_rms_eps */
 } sqmix_fa_args;
 
 /* The decode and merge kernels are launched with programmatic stream serialisation:

@@ -73,6 +73,10 @@ struct FaDecodeParams {
     float *part_ml;  // [splits][nq][16][2]
     uint32_t *err;
     int overlap_prev;  // SQMIX_FA_OVERLAP_PREV: prefetch before the grid dependency wait
+    // per-head RMS norm of the Q rows / the fused-append K rows before RoPE (NULL: off)
+    const float *q_norm;
+    const float *k_norm;
+    float norm_eps;
     // sequence batch (sqmix_fa_decode_batch; blockIdx.y = sequence).  NULL arrays: one
     // sequence with k_cache / v_cache / capacity above.
     const uint8_t *const *k_caches;
@@ -365,6 +369,38 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     (void)kvv;
 
     __syncthreads();  // staged Q / new rows and the RoPE table are visible
+
+    // ---- optional head RMS norm (attn.rs:66-84) of the staged Q rows and new K rows,
+    // in place before RoPE: one warp per 256-wide row, (x * (1 / sqrt(mean + eps))) * w ----
+    if (p.q_norm || (p.k_norm && has_fresh)) {
+        const int n_qrows = p.q_norm ? NQ * 16 : 0;
+        const int n_krows = p.k_norm && has_fresh ? p.n_new * 2 : 0;
+        for (int row = warp; row < n_qrows + n_krows; row += L::kWarps) {
+            float *x;
+            const float *w;
+            if (row < n_qrows) {
+                x = q_stage + row * 256;
+                w = p.q_norm;
+            } else {
+                const int kr = row - n_qrows;  // token kr / 2, head kr % 2 of the K rows
+                x = kv_stage + ((kr >> 1) * 2 * 2 + (kr & 1)) * 256;
+                w = p.k_norm;
+            }
+            float v[8];
+            float ss = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v[i] = x[lane + 32 * i];
+                ss = fmaf(v[i], v[i], ss);
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            const float sc = 1.0f / sqrtf(ss / 256.0f + p.norm_eps);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[lane + 32 * i] = (v[i] * sc) * w[lane + 32 * i];
+        }
+        __syncthreads();
+    }
 
     // ---- fused append: quantise the step's new K/V rows held by this CTA ----------
     if (has_fresh) {
@@ -904,6 +940,9 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, cons
     p.part_ml = reinterpret_cast<float *>(ws + off_ml);
     p.err = reinterpret_cast<uint32_t *>(ws);
     p.overlap_prev = (a->flags & SQMIX_FA_OVERLAP_PREV) != 0;
+    p.q_norm = a->q_norm;
+    p.k_norm = a->k_norm;
+    p.norm_eps = a->norm_eps;
     p.k_caches = bt.k_caches;
     p.v_caches = bt.v_caches;
     p.caps = bt.caps;
@@ -971,6 +1010,7 @@ extern "C" int sqmix_fa_decode(const sqmix_fa_args *a, sqmix_stream_t stream) {
                         (a->rope_n_rot == 0 || a->rope_freq_base > 0.f),
                     "fa_decode: rope parameters (n_rot <= 64)");
     SQMIX_CHECK_ARG(a->n_new >= 0 && a->n_new <= a->n_q, "fa_decode: n_new=%d must be in [0, n_q]", a->n_new);
+    SQMIX_CHECK_ARG(a->norm_eps >= 0.f, "fa_decode: norm_eps must be >= 0");
     SQMIX_CHECK_ARG(a->n_new == 0 || (a->k_new && a->v_new && a->k_new_stride_tok >= 512 &&
                                       a->v_new_stride_tok >= 512 &&
                                       (a->kv_new_dtype == SQMIX_F32 || a->kv_new_dtype == SQMIX_F16 ||

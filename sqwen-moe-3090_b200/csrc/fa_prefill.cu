@@ -749,6 +749,8 @@ extern "C" size_t sqmix_fa_prefill_workspace_bytes(int32_t n_q, int32_t n_ctas) 
 
 extern "C" int sqmix_fa_prefill(const sqmix_fa_args *a, sqmix_stream_t stream) {
     SQMIX_CHECK_ARG(a != nullptr, "fa_prefill: null args");
+    SQMIX_CHECK_ARG(!a->q_norm && !a->k_norm,
+                    "fa_prefill: q_norm / k_norm are decode-only; normalise with sqmix_head_norm first");
     SQMIX_CHECK_ARG(a->q && a->k_cache && a->v_cache && a->n_kv && a->q_pos0 && a->out && a->workspace,
                     "fa_prefill: null pointer argument");
     SQMIX_CHECK_ARG(a->n_q >= 1 && a->n_q <= kPfTok * kMaxMtiles / 2, "fa_prefill: n_q=%d (1..%d)", a->n_q,

@@ -69,6 +69,7 @@ class FaArgs(ctypes.Structure):
         ("n_splits", c_int32), ("config", c_int32),
         ("k_new", c_void_p), ("v_new", c_void_p), ("kv_new_dtype", c_int32), ("k_new_stride_tok", c_int64),
         ("v_new_stride_tok", c_int64), ("n_new", c_int32), ("flags", c_int32),
+        ("q_norm", c_void_p), ("k_norm", c_void_p), ("norm_eps", c_float),
     ]
 
 

@@ -113,7 +113,8 @@ def new_fa_workspace(n_q: int = 2, n_splits: int = 0, device="cuda") -> torch.Te
 
 
 def _fa_args(q, k_cache, v_cache, capacity, n_kv, q_pos0, gate, scale, rope_n_rot, rope_freq_base,
-             rope_pos_offset, out, lse, workspace, n_splits, config, k_new, v_new, flags):
+             rope_pos_offset, out, lse, workspace, n_splits, config, k_new, v_new, flags, q_norm=None,
+             k_norm=None, norm_eps=1e-6):
     """Validate tensors and build the sqmix_fa_args struct shared by decode and prefill."""
     _require_cuda(q, k_cache, v_cache, n_kv, q_pos0, gate)
     if q.dim() == 2:
@@ -151,7 +152,7 @@ def _fa_args(q, k_cache, v_cache, capacity, n_kv, q_pos0, gate, scale, rope_n_ro
         q_pos0=_ptr(q_pos0), n_q=n_q, scale=float(scale), rope_n_rot=int(rope_n_rot),
         rope_freq_base=float(rope_freq_base), rope_pos_offset=int(rope_pos_offset), out=_ptr(out),
         lse=_ptr(lse), workspace=_ptr(workspace), workspace_bytes=workspace.numel(), n_splits=int(n_splits),
-        config=int(config), flags=int(flags))
+        config=int(config), flags=int(flags), q_norm=_ptr(q_norm), k_norm=_ptr(k_norm), norm_eps=float(norm_eps))
     return a, out
 
 
@@ -162,7 +163,8 @@ def flash_attn_ext(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor
                    lse: torch.Tensor | None = None,
                    workspace: torch.Tensor | None = None, n_splits: int = 0, config: int = 0,
                    k_new: torch.Tensor | None = None, v_new: torch.Tensor | None = None,
-                   overlap_prev: bool = False, stream=None) -> torch.Tensor:
+                   overlap_prev: bool = False, q_norm: torch.Tensor | None = None,
+                   k_norm: torch.Tensor | None = None, norm_eps: float = 1e-6, stream=None) -> torch.Tensor:
     """Split-KV attention of q [n_q][16][256] (n_q in {1, 2}) over the tiled q4_0 caches.
 
     n_kv and q_pos0 are device int64 scalars (CUDA-graph friendly).  Query t sees keys
@@ -171,12 +173,17 @@ def flash_attn_ext(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor
     first quantised into the caches in the same launch (K rotated like Q).
     overlap_prev sets SQMIX_FA_OVERLAP_PREV: n_kv, q_pos0 and the cache rows below
     q_pos0 must then not be written by the kernel launched just before this call.
+    q_norm / k_norm ([256] f32): per-head RMS norm of Q and of the appended K rows
+    before RoPE (attn.rs:66-84), fused into the kernel.
     """
+    for w in (q_norm, k_norm):
+        if w is not None and (w.dtype != torch.float32 or w.numel() != HEAD_DIM or not w.is_contiguous()):
+            raise ValueError("q_norm / k_norm must be contiguous float32 [256]")
     if workspace is None:
         workspace = new_fa_workspace(q.shape[0], n_splits, q.device)
     a, out = _fa_args(q, k_cache, v_cache, capacity, n_kv, q_pos0, gate, scale, rope_n_rot, rope_freq_base,
                       rope_pos_offset, out, lse, workspace, n_splits, config, k_new, v_new,
-                      SQMIX_FA_OVERLAP_PREV if overlap_prev else 0)
+                      SQMIX_FA_OVERLAP_PREV if overlap_prev else 0, q_norm, k_norm, norm_eps)
     check(lib().sqmix_fa_decode(ctypes.byref(a), _stream(stream)), "flash_attn_ext")
     return out
 

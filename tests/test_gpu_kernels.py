@@ -276,6 +276,47 @@ def test_fa_decode_config3_twelve_warps(sq, oracle, n_kv, n_splits):
     assert np.abs(lse.cpu().numpy() - wlse).max() < 1e-3
 
 
+@pytest.mark.parametrize("n_q", [1, 2])
+def test_fa_decode_fused_head_rms_norm(sq, oracle, n_q):
+    """Q and the appended K rows RMS-normalised per head with the attn_q_norm /
+    attn_k_norm weights inside the decode kernel (attn.rs:66-84, :166-175), then
+    RoPE, append and attention, against the oracle chain rms_norm -> rope -> q4_0."""
+    rng = np.random.default_rng(70 + n_q)
+    n_kv = 1200
+    k = (rng.standard_normal((n_kv, 2, 256)) * 3.0).astype(np.float32)
+    v = rng.standard_normal((n_kv, 2, 256)).astype(np.float32)
+    wq = rng.uniform(0.5, 1.5, 256).astype(np.float32)
+    wk = rng.uniform(0.5, 1.5, 256).astype(np.float32)
+    q = (rng.standard_normal((n_q, 16, 256)) * 2.0).astype(np.float32)
+    gate = rng.standard_normal((n_q, 16, 256)).astype(np.float32)
+    q_pos0 = n_kv - n_q
+    kn = oracle.rms_norm(k, 1e-6, w=wk)  # the history rows were normalised when appended
+    cap = cap_for(n_kv)
+    kc, vc = sq.new_kv_cache(cap), sq.new_kv_cache(cap)
+    sq.set_rows_q4_0(torch.from_numpy(kn[:q_pos0]).cuda(), torch.from_numpy(v[:q_pos0]).cuda(),
+                     torch.arange(q_pos0, device="cuda"), kc, vc, cap, rope_n_rot=64, rope_freq_base=1e7)
+    out = sq.flash_attn_ext(torch.from_numpy(q).cuda(), kc, vc, cap,
+                            torch.tensor([n_kv], dtype=torch.int64, device="cuda"),
+                            torch.tensor([q_pos0], dtype=torch.int64, device="cuda"),
+                            gate=torch.from_numpy(gate).cuda(), rope_n_rot=64, rope_freq_base=1e7,
+                            k_new=torch.from_numpy(k[q_pos0:]).cuda(), v_new=torch.from_numpy(v[q_pos0:]).cuda(),
+                            q_norm=torch.from_numpy(wq).cuda(), k_norm=torch.from_numpy(wk).cuda(), norm_eps=1e-6)
+    torch.cuda.synchronize()
+    kq = oracle.q4_0_quantize(oracle.rope_text(kn, 0, 1e7, 64).reshape(n_kv, 512))
+    vq = oracle.q4_0_quantize(v.reshape(n_kv, 512))
+    got_k = sq.kv_convert_rows(kc, cap, "k", q_pos0, n_q).cpu().numpy()
+    # the appended rows, quantised from the device-normalised K: a last-bit difference
+    # in the norm may move a value across a rounding boundary, so almost all (not all)
+    # blocks must be bit-identical to the oracle's
+    same = (got_k.reshape(n_q * 16, 18) == kq[q_pos0:].reshape(n_q * 16, 18)).all(axis=1)
+    assert same.mean() >= 0.9, same
+    kd = oracle.q4_0_dequantize(np.concatenate([kq[:q_pos0], got_k]), 512).reshape(n_kv, 2, 256)
+    vd = oracle.q4_0_dequantize(vq, 512).reshape(n_kv, 2, 256)
+    qn = oracle.rope_text(oracle.rms_norm(q, 1e-6, w=wq), q_pos0, 1e7, 64)
+    want = oracle.attn(qn, kd, vd, gate, q_pos0=q_pos0, scale=1 / 16)
+    assert rel_err(out.cpu().numpy(), want) <= ATTN_TOL
+
+
 def test_fa_decode_prefix_causal(sq, oracle):
     # queries at positions far below n_kv: only keys j <= q_pos0 + t count (graph.rs:553-559)
     rng = np.random.default_rng(40)
