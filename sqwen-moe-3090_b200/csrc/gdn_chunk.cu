@@ -14,9 +14,11 @@
 //             D_ts = e^{G_t - G_s} (s <= t)
 //     S_C   = e^{G_C} S0 + (K o e^{G_C - G})^T Delta.
 // gdn_chunk_prep_kernel computes everything that does not depend on the state (W, U,
-// the scaled Q, K and the masked Q K^T) for all chunks and heads in parallel;
+// the scaled Q, K and the masked Q K^T) for all chunks and heads in parallel and
+// stores the matrices the scan multiplies with as split-bf16 tcgen05 operand images;
 // gdn_chunk_scan_kernel then walks the chunks of each head in order, one CTA per
-// (sequence, head, 32 value columns): value columns evolve independently.
+// (sequence, head, 64 value columns; value columns evolve independently), with the
+// three chunk products on the tensor cores (tcgen05, f32 accumulators in TMEM).
 // Every exponent is a difference G_t - G_s <= 0 or G_t <= 0, so nothing overflows.
 //
 // Snapshot planes (slot s = state after T - s tokens, gdn.rs:484-538) are produced by
@@ -25,6 +27,7 @@
 
 #include "common.cuh"
 #include "sqmix.h"
+#include "tc.cuh"
 
 namespace sqmix {
 
@@ -37,16 +40,26 @@ namespace {
 
 constexpr int kC = 64;     // chunk length
 constexpr int kD = 128;    // head dim
-constexpr int kJB = 32;    // value columns per scan CTA
-// per (sequence, head, chunk) in the workspace, in floats; W, Q and M are stored
-// transposed (contraction index major) so that the scan reads 4 rows per vector load
-constexpr int64_t kOffW = 0;                // W^T  [128 i][64 t]
-constexpr int64_t kOffU = kOffW + kC * kD;  // U    [64 t][128 j]
-constexpr int64_t kOffQ = kOffU + kC * kD;  // Qs^T [128 i][64 t]  q e^G / sqrt(128)
-constexpr int64_t kOffK = kOffQ + kC * kD;  // K'   [64 t][128 i]  k e^{G_C - G}
-constexpr int64_t kOffM = kOffK + kC * kD;  // M^T  [64 s][64 t]   (Q K^T o D)^T / sqrt(128)
-constexpr int64_t kOffS = kOffM + kC * kC;  // scalars: [0] e^{G_C}
-constexpr int64_t kChunkFloats = kOffS + 64;
+constexpr int kSN = 64;    // value columns per scan CTA
+// Per (sequence, head, chunk) in the workspace.  The four chunk matrices the scan
+// multiplies with are stored as bf16 pairs x = hi + lo (hi = bf16(x), lo = bf16(x - hi))
+// in the shared-memory image of the tcgen05 operand layout, so that one bulk copy
+// brings them in: MN-major, 128-byte swizzle, blocks of 64 MN elements x rows of the
+// contraction index (row r at r * 128 bytes, 16-byte chunk q stored at q ^ (r & 7)).
+//   A1 = [W ; Qs]  MN = token (W rows, then Qs rows), K = key index i (128 rows)
+//   A3 = M         MN = token t, K = token s            (64 rows)
+//   A4 = K'^T      MN = key index i (2 blocks), K = t   (64 rows)
+// U stays f32 [64 t][128 j]; scalars: [0] e^{G_C}.
+constexpr int64_t kA1Bytes = 2 * 2 * kD * 128;  // (hi | lo) x (W | Qs) blocks of 128 rows
+constexpr int64_t kA3Bytes = 2 * kC * 128;      // (hi | lo) x one block of 64 rows
+constexpr int64_t kA4Bytes = 2 * 2 * kC * 128;  // (hi | lo) x two blocks of 64 rows
+constexpr int64_t kOffA1 = 0;                   // byte offsets in the chunk record
+constexpr int64_t kOffA3 = kOffA1 + kA1Bytes;
+constexpr int64_t kOffA4 = kOffA3 + kA3Bytes;
+constexpr int64_t kOffUb = kOffA4 + kA4Bytes;   // U f32
+constexpr int64_t kOffSb = kOffUb + kC * kD * 4;  // scalars
+constexpr int64_t kChunkBytes = kOffSb + 256;
+constexpr int64_t kChunkFloats = kChunkBytes / 4;
 constexpr int64_t kWsHeaderFloats = 64;  // [0] u32 device status bits (bounded waits)
 
 struct ChunkParams {
@@ -84,8 +97,34 @@ __device__ __forceinline__ float4 load4v(const void *p, int64_t i, int dtype) {
     return make_float4(__low2float(x), __high2float(x), __low2float(y), __high2float(y));
 }
 
-__device__ __forceinline__ float *chunk_ws(const ChunkParams &p, int seq, int h, int c) {
-    return p.ws + kWsHeaderFloats + ((static_cast<int64_t>(seq) * p.h_v + h) * p.n_chunks + c) * kChunkFloats;
+__device__ __forceinline__ uint8_t *chunk_ws(const ChunkParams &p, int seq, int h, int c) {
+    return reinterpret_cast<uint8_t *>(p.ws + kWsHeaderFloats +
+                                       ((static_cast<int64_t>(seq) * p.h_v + h) * p.n_chunks + c) * kChunkFloats);
+}
+
+// bf16 pair of x: hi = bf16(x), lo = bf16(x - hi) (x = hi + lo to ~2^-16 relative)
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16 &hi, __nv_bfloat16 &lo) {
+    hi = __float2bfloat16_rn(x);
+    lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+}
+// One 64-element row r of an MN-major 128-byte-swizzled block, as hi and lo images
+// (generic-proxy stores; the row is 128 bytes, chunk q at q ^ (r & 7)).
+__device__ __forceinline__ void store_mn_row(uint8_t *blk_hi, uint8_t *blk_lo, int r, const float *v) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            __nv_bfloat16 h0, l0, h1, l1;
+            split_bf16(v[8 * q + 2 * e], h0, l0);
+            split_bf16(v[8 * q + 2 * e + 1], h1, l1);
+            h[e] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+            l[e] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+        }
+        const int off = r * 128 + ((q ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4 *>(blk_hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4 *>(blk_lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
 }
 
 // ---- phase 1: state-independent chunk quantities -----------------------------------
@@ -196,7 +235,8 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
             }
     }
     __syncthreads();
-    float *wsc = chunk_ws(p, seq, h, c);
+    uint8_t *wsc = chunk_ws(p, seq, h, c);
+    float *Ub = reinterpret_cast<float *>(wsc + kOffUb);
     // forward substitution of (I + A) X = [beta e^G K | beta V], one thread per column,
     // the column held in registers; A_ts = 0 for s >= t, so whole 4-groups are summed
     {
@@ -220,212 +260,258 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
             }
             x[t] -= (acc[0] + acc[1]) + (acc[2] + acc[3]);
         }
-        if (is_w) {  // W^T row col: 64 contiguous floats
-#pragma unroll
-            for (int t = 0; t < kC; t += 4)
-                *reinterpret_cast<float4 *>(wsc + kOffW + col * kC + t) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
+        if (is_w) {  // W column i = col: row col of A1's W block (MN = t)
+            store_mn_row(wsc + kOffA1, wsc + kOffA1 + kA1Bytes / 2, col, x);
         } else {
 #pragma unroll
-            for (int t = 0; t < kC; ++t) wsc[kOffU + t * kD + col] = x[t];
+            for (int t = 0; t < kC; ++t) Ub[t * kD + col] = x[t];
         }
     }
-    // Qs^T (threads 0..127) and K' (threads 128..255), from the tiles still in shared memory
+    // Qs (threads 0..127: row i of A1's Qs block), K'^T (threads 128..191: row t of A4),
+    // M (threads 192..255: row s of A3), from the tiles still in shared memory
     {
         const float GC = G[kC - 1];
-        const int col = tid & 127;
         if (tid < kD) {
+            const int col = tid;
             const float rsd = 1.0f / sqrtf(128.0f);
-#pragma unroll 4
-            for (int t = 0; t < kC; t += 4) {
-                float4 v;
-                v.x = Qs[t * kLd + col] * expf(G[t]) * rsd;
-                v.y = Qs[(t + 1) * kLd + col] * expf(G[t + 1]) * rsd;
-                v.z = Qs[(t + 2) * kLd + col] * expf(G[t + 2]) * rsd;
-                v.w = Qs[(t + 3) * kLd + col] * expf(G[t + 3]) * rsd;
-                *reinterpret_cast<float4 *>(wsc + kOffQ + col * kC + t) = v;
+            float v[kC];
+#pragma unroll
+            for (int t = 0; t < kC; ++t) v[t] = Qs[t * kLd + col] * expf(G[t]) * rsd;
+            store_mn_row(wsc + kOffA1 + kD * 128, wsc + kOffA1 + kA1Bytes / 2 + kD * 128, col, v);
+        } else if (tid < kD + kC) {
+            const int t = tid - kD;
+            const float dk = expf(GC - G[t]);
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                float v[64];
+#pragma unroll
+                for (int i = 0; i < 64; ++i) v[i] = Ks[t * kLd + 64 * blk + i] * dk;
+                store_mn_row(wsc + kOffA4 + blk * kC * 128, wsc + kOffA4 + kA4Bytes / 2 + blk * kC * 128, t, v);
             }
         } else {
-            for (int t = 0; t < kC; ++t) wsc[kOffK + t * kD + col] = Ks[t * kLd + col] * expf(GC - G[t]);
+            const int s2 = tid - kD - kC;
+            float v[kC];
+#pragma unroll
+            for (int t = 0; t < kC; ++t) v[t] = Mq[t * (kC + 1) + s2];
+            store_mn_row(wsc + kOffA3, wsc + kOffA3 + kA3Bytes / 2, s2, v);
         }
-        for (int e = tid; e < kC * kC; e += 256) wsc[kOffM + e] = Mq[(e & 63) * (kC + 1) + (e >> 6)];
-        if (tid == 0) wsc[kOffS] = expf(GC);
+        if (tid == 0) reinterpret_cast<float *>(wsc + kOffSb)[0] = expf(GC);
     }
 }
 
-// ---- phase 2: walk the chunks of one (sequence, head, 32 value columns) -------------
-// grid (kD / kJB, h_v, n_seqs), 256 threads, dynamic smem kScanSmem.  The chunk tiles
-// are brought in by 1-D bulk copies (TMA, no multicast): W^T and Q^T of chunk c+1 as
-// soon as chunk c has used them, M^T and K' likewise.
-constexpr int kLdS = kJB + 2;  // S and Delta rows (float2 column pairs)
-constexpr size_t kScanFloats = static_cast<size_t>(kD) * kLdS + kC * kLdS + 3 * kD * kC + kC * kC;
-constexpr size_t kScanSmem = kScanFloats * sizeof(float) + 64;
-constexpr uint32_t kBytesWQ = 2 * kD * kC * sizeof(float);
-constexpr uint32_t kBytesMK = (kC * kC + kC * kD) * sizeof(float);
+// ---- phase 2: walk the chunks of one (sequence, head, 64 value columns) -------------
+// grid (kD / kSN, h_v, n_seqs), 128 threads (thread = TMEM lane = row of the
+// accumulators), dynamic smem kScanSmem.  Per chunk, three split-bf16 tcgen05 MMA
+// groups (hi*hi + hi*lo + lo*hi, f32 accumulators in tensor memory):
+//   D1  = [W ; Qs] S0          M 128 (tokens of W, then of Qs), N 64, K 128
+//   Delta = U - D1[0:64]       (threads 0..63, written back as the bf16 B operand)
+//   D1 += [0 ; M] Delta        (the O half: O = Qs S0 + M Delta)
+//   D4  = K'^T Delta           M 128 (key index), N 64, K 64
+//   S  <- e^{G_C} S0 + D4      (thread i keeps row i of the f32 state in registers)
+// The operand images of chunk c+1 are brought in by 1-D bulk copies (TMA, no
+// multicast) as soon as the MMAs of chunk c have read the buffers.
+constexpr uint32_t kSmA1 = 0;                                   // 64 KB: hi | lo, each W | Qs
+constexpr uint32_t kSmA3 = kSmA1 + kA1Bytes;                    // 32 KB: hi | lo, each zero | M
+constexpr uint32_t kSmA4 = kSmA3 + 2 * kA3Bytes;                // 32 KB: hi | lo
+constexpr uint32_t kSmBS = kSmA4 + kA4Bytes;                    // 32 KB: S0 hi | lo (K = i, 128 rows)
+constexpr uint32_t kSmBD = kSmBS + 2 * kD * 128;                // 16 KB: Delta hi | lo (K = t, 64 rows)
+constexpr uint32_t kSmBar = kSmBD + 2 * kC * 128;
+constexpr size_t kScanSmem = kSmBar + 64 + 1024;                // + alignment slack
+constexpr uint32_t kTmemCols = 128;                              // D1 at 0, D4 at 64
 
-__global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
-    extern __shared__ __align__(16) float sm[];
-    float *S = sm;                  // [128 i][kLdS]  state columns of this block
-    float *Dl = S + kD * kLdS;      // [64 t][kLdS]   Delta
-    float *WT = Dl + kC * kLdS;     // [128 i][64 t]
-    float *QT = WT + kD * kC;       // [128 i][64 t]  (contiguous after WT: one W|Q copy pair)
-    float *MT = QT + kD * kC;       // [64 s][64 t]
-    float *Kp = MT + kC * kC;       // [64 t][128 i]  (contiguous after MT)
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kScanFloats);  // [0] W|Q, [1] M|K'
+__device__ __forceinline__ void ld64(uint32_t taddr, float (&v)[64]) {
+    uint32_t r[32];
+    tc::ld32(taddr, r);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    tc::ld32(taddr + 32, r);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(ChunkParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sb = smem_u32(sm);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kSmBar);  // [0] A1, [1] A3|A4, [2] MMA done
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kSmBar + 32);
     __shared__ int abort_flag;
     uint32_t *err = reinterpret_cast<uint32_t *>(p.ws);
     const int jb = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
-    const int tid = threadIdx.x;
-    auto issue_wq = [&](int c) {
-        const float *w = chunk_ws(p, seq, h, c);
-        mbar_arrive_expect_tx(&bars[0], kBytesWQ);
-        bulk_g2s(WT, w + kOffW, kD * kC * sizeof(float), &bars[0]);
-        bulk_g2s(QT, w + kOffQ, kD * kC * sizeof(float), &bars[0]);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    auto issue_a1 = [&](int c) {
+        const uint8_t *w = chunk_ws(p, seq, h, c);
+        mbar_arrive_expect_tx(&bars[0], static_cast<uint32_t>(kA1Bytes));
+        bulk_g2s(sm + kSmA1, w + kOffA1, static_cast<uint32_t>(kA1Bytes), &bars[0]);
     };
-    auto issue_mk = [&](int c) {
-        const float *w = chunk_ws(p, seq, h, c);
-        mbar_arrive_expect_tx(&bars[1], kBytesMK);
-        bulk_g2s(MT, w + kOffM, kC * kC * sizeof(float), &bars[1]);
-        bulk_g2s(Kp, w + kOffK, kC * kD * sizeof(float), &bars[1]);
+    auto issue_a34 = [&](int c) {
+        const uint8_t *w = chunk_ws(p, seq, h, c);
+        mbar_arrive_expect_tx(&bars[1], static_cast<uint32_t>(kA3Bytes + kA4Bytes));
+        // M into the second (non-zero) block of each of A3's hi and lo halves
+        bulk_g2s(sm + kSmA3 + kA3Bytes / 2, w + kOffA3, static_cast<uint32_t>(kA3Bytes / 2), &bars[1]);
+        bulk_g2s(sm + kSmA3 + kA3Bytes + kA3Bytes / 2, w + kOffA3 + kA3Bytes / 2, static_cast<uint32_t>(kA3Bytes / 2),
+                 &bars[1]);
+        bulk_g2s(sm + kSmA4, w + kOffA4, static_cast<uint32_t>(kA4Bytes), &bars[1]);
     };
+    // A3's first block (rows of tokens that receive no M Delta: the W half of D1) is zero
+    for (int e = tid; e < static_cast<int>(kA3Bytes / 2 / 16); e += 128) {
+        reinterpret_cast<uint4 *>(sm + kSmA3)[e] = make_uint4(0u, 0u, 0u, 0u);
+        reinterpret_cast<uint4 *>(sm + kSmA3 + kA3Bytes)[e] = make_uint4(0u, 0u, 0u, 0u);
+    }
     if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+        for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
         abort_flag = 0;
         fence_mbar_init();
     }
+    if (warp == 0) tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::fence_proxy_async_smem();
+    tc::fence_before();
     __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
     if (tid == 0) {
-        issue_wq(0);
-        issue_mk(0);
+        issue_a1(0);
+        issue_a34(0);
     }
+    // row i = tid of the state block: S[i][j] at ((h*128 + j)*128 + i)
     const int64_t plane_elems = static_cast<int64_t>(p.h_v) * kD * kD;
     float *st_seq = p.state + static_cast<int64_t>(seq) * p.n_planes * plane_elems;
     int plane = p.sel ? p.sel[seq] : 0;
     plane = min(max(plane, 0), p.n_planes - 1);
-    // S[i][j] at ((h*128 + j)*128 + i)
-    for (int e = tid; e < kD * kJB; e += 256) {
-        const int j = e >> 7, i = e & 127;
-        S[i * kLdS + j] = st_seq[plane * plane_elems + (static_cast<int64_t>(h) * kD + jb * kJB + j) * kD + i];
-    }
-    __syncthreads();
-    // Delta / O tiles: rows r0..r0+3 (tokens), columns c0, c0+1; S tile: rows i0..i0+7
-    const int r0 = 4 * (tid >> 4), c0 = 2 * (tid & 15);
-    const int i0 = 8 * (tid >> 4);
+    float srow[kSN];
+#pragma unroll
+    for (int j = 0; j < kSN; ++j)
+        srow[j] = st_seq[plane * plane_elems + (static_cast<int64_t>(h) * kD + jb * kSN + j) * kD + tid];
+    store_mn_row(sm + kSmBS, sm + kSmBS + kD * 128, tid, srow);
+
+    constexpr uint32_t idesc = tc::idesc_bf16_f32(128, kSN, 1, 1);
+    // split-bf16 products: (A hi, B hi), (A hi, B lo), (A lo, B hi)
+    auto mma3 = [&](uint32_t d, uint32_t a, uint32_t a_lo, uint32_t a_lbo, uint32_t b, uint32_t b_lo, int ksteps,
+                    bool accumulate) {
+#pragma unroll 1
+        for (int ks = 0; ks < ksteps; ++ks) {
+            const uint32_t ko = ks * 2048;  // 16 rows of the contraction index
+            const uint64_t ah = tc::desc_sw128(a + ko, a_lbo, 1024), al = tc::desc_sw128(a + a_lo + ko, a_lbo, 1024);
+            const uint64_t bh = tc::desc_sw128(b + ko, 8192, 1024), bl = tc::desc_sw128(b + b_lo + ko, 8192, 1024);
+            tc::mma_ss(d, al, bh, idesc, (accumulate || ks > 0) ? 1u : 0u);
+            tc::mma_ss(d, ah, bl, idesc, 1u);
+            tc::mma_ss(d, ah, bh, idesc, 1u);
+        }
+    };
     bool ok = true;
-    int last_wq = 0, last_mk = 0;  // chunk of the latest copies issued (thread 0)
+    int mma_phase = 0;
+    int last_a1 = 0, last_a34 = 0;  // chunk of the latest copies issued (thread 0)
     // every thread takes the same branch after a wait (the loop has block barriers)
-    auto wait = [&](int which, int c) -> bool {
+    auto wait_bar = [&](uint64_t *bar, uint32_t parity, uint32_t bit) -> bool {
         bool r = !abort_flag;
-        if (r && !mbar_wait(&bars[which], c & 1)) {
-            atomicOr(err, 1u);
+        if (r && !mbar_wait(bar, parity)) {
+            atomicOr(err, bit);
             abort_flag = 1;
             r = false;
         }
         return __syncthreads_and(r) != 0;
     };
-    int c = 0;
-    for (; c < p.n_chunks; ++c) {
-        const float *wsc = chunk_ws(p, seq, h, c);
-        const float eGC = wsc[kOffS];
-        float2 u[4];
+    tc::fence_proxy_async_smem();
+    __syncthreads();
+    for (int c = 0; c < p.n_chunks && ok; ++c) {
+        const uint8_t *wsc = chunk_ws(p, seq, h, c);
+        const float eGC = reinterpret_cast<const float *>(wsc + kOffSb)[0];
+        float u[kSN];
+        if (tid < kC) {
+            const float4 *ur = reinterpret_cast<const float4 *>(wsc + kOffUb + (static_cast<int64_t>(tid) * kD + jb * kSN) * 4);
 #pragma unroll
-        for (int a = 0; a < 4; ++a) u[a] = *reinterpret_cast<const float2 *>(wsc + kOffU + (r0 + a) * kD + jb * kJB + c0);
-        if (!wait(0, c)) { ok = false; break; }
-        // Delta = U - W S0 and the first part of O = Qs S0
-        float d[4][2], o[4][2];
-#pragma unroll
-        for (int a = 0; a < 4; ++a) {
-            d[a][0] = u[a].x;
-            d[a][1] = u[a].y;
-            o[a][0] = o[a][1] = 0.f;
-        }
-#pragma unroll 4
-        for (int i = 0; i < kD; ++i) {
-            const float2 sv = *reinterpret_cast<const float2 *>(S + i * kLdS + c0);
-            const float4 w = *reinterpret_cast<const float4 *>(WT + i * kC + r0);
-            const float4 q = *reinterpret_cast<const float4 *>(QT + i * kC + r0);
-            const float wv[4] = {w.x, w.y, w.z, w.w}, qv[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int a = 0; a < 4; ++a) {
-                d[a][0] = fmaf(-wv[a], sv.x, d[a][0]);
-                d[a][1] = fmaf(-wv[a], sv.y, d[a][1]);
-                o[a][0] = fmaf(qv[a], sv.x, o[a][0]);
-                o[a][1] = fmaf(qv[a], sv.y, o[a][1]);
+            for (int q = 0; q < kSN / 4; ++q) {
+                const float4 x = ur[q];
+                u[4 * q] = x.x;
+                u[4 * q + 1] = x.y;
+                u[4 * q + 2] = x.z;
+                u[4 * q + 3] = x.w;
             }
         }
-#pragma unroll
-        for (int a = 0; a < 4; ++a) *reinterpret_cast<float2 *>(Dl + (r0 + a) * kLdS + c0) = make_float2(d[a][0], d[a][1]);
-        __syncthreads();  // Delta complete; S0, W and Q fully read
-        if (tid == 0 && c + 1 < p.n_chunks) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue_wq(c + 1);
-            last_wq = c + 1;
+        if (!wait_bar(&bars[0], c & 1, 1u)) { ok = false; break; }
+        // ---- D1 = [W ; Qs] S0 ----
+        if (tid == 0) {
+            tc::fence_after();
+            mma3(tmem, sb + kSmA1, static_cast<uint32_t>(kA1Bytes / 2), kD * 128, sb + kSmBS, kD * 128, kD / 16, false);
+            tc::commit(&bars[2]);
         }
-        if (!wait(1, c)) { ok = false; break; }
-        // O += M Delta
-#pragma unroll 4
-        for (int s2 = 0; s2 < kC; ++s2) {
-            const float2 dv = *reinterpret_cast<const float2 *>(Dl + s2 * kLdS + c0);
-            const float4 m = *reinterpret_cast<const float4 *>(MT + s2 * kC + r0);
-            const float mv[4] = {m.x, m.y, m.z, m.w};
+        if (!wait_bar(&bars[2], mma_phase++ & 1, 2u)) { ok = false; break; }
+        tc::fence_after();
+        if (tid == 0 && c + 1 < p.n_chunks) {  // A1 has been read
+            issue_a1(c + 1);
+            last_a1 = c + 1;
+        }
+        // ---- Delta = U - W S0 (rows t = 0..63) as the bf16 B operand ----
+        if (tid < kC) {
+            float d[kSN];
+            ld64(tmem + lane_base, d);
 #pragma unroll
-            for (int a = 0; a < 4; ++a) {
-                o[a][0] = fmaf(mv[a], dv.x, o[a][0]);
-                o[a][1] = fmaf(mv[a], dv.y, o[a][1]);
+            for (int j = 0; j < kSN; ++j) d[j] = u[j] - d[j];
+            store_mn_row(sm + kSmBD, sm + kSmBD + kC * 128, tid, d);
+        } else {
+            // the other warps' lanes take part in no load here
+        }
+        tc::fence_proxy_async_smem();
+        tc::fence_before();
+        if (!wait_bar(&bars[1], c & 1, 4u)) { ok = false; break; }
+        // ---- D1 += [0 ; M] Delta ;  D4 = K'^T Delta ----
+        if (tid == 0) {
+            tc::fence_after();
+            mma3(tmem, sb + kSmA3, static_cast<uint32_t>(kA3Bytes), static_cast<uint32_t>(kA3Bytes / 2), sb + kSmBD,
+                 kC * 128, kC / 16, true);
+            mma3(tmem + kSN, sb + kSmA4, static_cast<uint32_t>(kA4Bytes / 2), kC * 128, sb + kSmBD, kC * 128, kC / 16,
+                 false);
+            tc::commit(&bars[2]);
+        }
+        if (!wait_bar(&bars[2], mma_phase++ & 1, 2u)) { ok = false; break; }
+        tc::fence_after();
+        if (tid == 0 && c + 1 < p.n_chunks) {  // A3 and A4 have been read
+            issue_a34(c + 1);
+            last_a34 = c + 1;
+        }
+        // ---- outputs O (rows 64..127 of D1 = tokens 0..63) ----
+        if (tid >= kC) {
+            const int t = c * kC + (tid - kC);
+            float o[kSN];
+            ld64(tmem + lane_base, o);
+            if (t < p.T) {
+                float4 *orow = reinterpret_cast<float4 *>(
+                    p.out + ((static_cast<int64_t>(seq) * p.T_all + t) * p.h_v + h) * kD + jb * kSN);
+#pragma unroll
+                for (int q = 0; q < kSN / 4; ++q) orow[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
             }
         }
-#pragma unroll
-        for (int a = 0; a < 4; ++a) {
-            const int t = c * kC + r0 + a;
-            if (t < p.T)
-                *reinterpret_cast<float2 *>(p.out + ((static_cast<int64_t>(seq) * p.T_all + t) * p.h_v + h) * kD +
-                                            jb * kJB + c0) = make_float2(o[a][0], o[a][1]);
-        }
-        // S = e^{G_C} S0 + K'^T Delta (each thread rewrites only its own entries)
+        // ---- S = e^{G_C} S0 + K'^T Delta (row i = tid) ----
         {
-            float acc[8][2];
+            float d4[kSN];
+            ld64(tmem + lane_base + kSN, d4);
 #pragma unroll
-            for (int a = 0; a < 8; ++a) {
-                const float2 sv = *reinterpret_cast<const float2 *>(S + (i0 + a) * kLdS + c0);
-                acc[a][0] = eGC * sv.x;
-                acc[a][1] = eGC * sv.y;
-            }
-#pragma unroll 2
-            for (int t = 0; t < kC; ++t) {
-                const float2 dv = *reinterpret_cast<const float2 *>(Dl + t * kLdS + c0);
-                const float4 k0 = *reinterpret_cast<const float4 *>(Kp + t * kD + i0);
-                const float4 k1 = *reinterpret_cast<const float4 *>(Kp + t * kD + i0 + 4);
-                const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
-#pragma unroll
-                for (int a = 0; a < 8; ++a) {
-                    acc[a][0] = fmaf(kv[a], dv.x, acc[a][0]);
-                    acc[a][1] = fmaf(kv[a], dv.y, acc[a][1]);
-                }
-            }
-#pragma unroll
-            for (int a = 0; a < 8; ++a)
-                *reinterpret_cast<float2 *>(S + (i0 + a) * kLdS + c0) = make_float2(acc[a][0], acc[a][1]);
+            for (int j = 0; j < kSN; ++j) srow[j] = fmaf(eGC, srow[j], d4[j]);
+            store_mn_row(sm + kSmBS, sm + kSmBS + kD * 128, tid, srow);
         }
-        __syncthreads();  // M, K' and Delta fully read; S updated
-        if (tid == 0 && c + 1 < p.n_chunks) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue_mk(c + 1);
-            last_mk = c + 1;
-        }
+        tc::fence_proxy_async_smem();
+        tc::fence_before();
+        __syncthreads();
     }
     if (!ok) {
-        // never exit with a bulk copy still writing into shared memory
+        // never exit with a bulk copy still writing into shared memory, nor before the
+        // issued MMAs are complete (their tensor memory is released below)
         if (tid == 0) {
-            mbar_wait(&bars[0], last_wq & 1);
-            mbar_wait(&bars[1], last_mk & 1);
+            mbar_wait(&bars[0], last_a1 & 1);
+            mbar_wait(&bars[1], last_a34 & 1);
+            tc::commit(&bars[2]);
+            mbar_wait(&bars[2], mma_phase & 1);
         }
-        return;
+    } else {
+#pragma unroll
+        for (int j = 0; j < kSN; ++j)
+            st_seq[p.plane_out * plane_elems + (static_cast<int64_t>(h) * kD + jb * kSN + j) * kD + tid] = srow[j];
     }
+    tc::fence_before();
     __syncthreads();
-    for (int e = tid; e < kD * kJB; e += 256) {
-        const int j = e >> 7, i = e & 127;
-        st_seq[p.plane_out * plane_elems + (static_cast<int64_t>(h) * kD + jb * kJB + j) * kD + i] = S[i * kLdS + j];
-    }
+    tc::fence_after();
+    if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
 }  // namespace
@@ -514,7 +600,7 @@ extern "C" int sqmix_gdn_prefill(const sqmix_gdn_args *a, void *workspace, size_
     gdn_chunk_prep_kernel<<<dim3(p.n_chunks, a->h_v, a->n_seqs), 256, kPrepSmem, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill prep launch");
-    gdn_chunk_scan_kernel<<<dim3(kD / kJB, a->h_v, a->n_seqs), 256, kScanSmem, st>>>(p);
+    gdn_chunk_scan_kernel<<<dim3(kD / kSN, a->h_v, a->n_seqs), 128, kScanSmem, st>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill scan launch");
     if (a->n_snap > 1)

@@ -53,6 +53,11 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, int a_mn, int
            (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// kind::f16 with bf16 A and B (both operands bf16), f32 accumulator.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n, int a_mn, int b_mn) {
+    return idesc_f16_f32(m, n, a_mn, b_mn) | (1u << 7) | (1u << 10);
+}
+
 // D[tmem] (+)= A[smem] * B[smem]; issued by one thread.
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
