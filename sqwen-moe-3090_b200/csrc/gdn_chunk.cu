@@ -77,26 +77,6 @@ struct ChunkParams {
     float *out;
 };
 
-__device__ __forceinline__ float warp_sum32(float x) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
-    return x;
-}
-
-// 4 consecutive elements of a q/k/v row (offset a multiple of 4) as f32
-__device__ __forceinline__ float4 load4v(const void *p, int64_t i, int dtype) {
-    if (dtype == SQMIX_F32) return *reinterpret_cast<const float4 *>(static_cast<const float *>(p) + i);
-    const uint2 r = *reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(p) + i);
-    if (dtype == SQMIX_BF16) {
-        const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162 *>(&r.x);
-        const __nv_bfloat162 y = *reinterpret_cast<const __nv_bfloat162 *>(&r.y);
-        return make_float4(__low2float(x), __high2float(x), __low2float(y), __high2float(y));
-    }
-    const __half2 x = *reinterpret_cast<const __half2 *>(&r.x);
-    const __half2 y = *reinterpret_cast<const __half2 *>(&r.y);
-    return make_float4(__low2float(x), __high2float(x), __low2float(y), __high2float(y));
-}
-
 __device__ __forceinline__ uint8_t *chunk_ws(const ChunkParams &p, int seq, int h, int c) {
     return reinterpret_cast<uint8_t *>(p.ws + kWsHeaderFloats +
                                        ((static_cast<int64_t>(seq) * p.h_v + h) * p.n_chunks + c) * kChunkFloats);
@@ -127,14 +107,44 @@ __device__ __forceinline__ void store_mn_row(uint8_t *blk_hi, uint8_t *blk_lo, i
     }
 }
 
+// Half of such a row: elements 32 * half .. 32 * half + 31 (chunks 4 half .. 4 half + 3).
+__device__ __forceinline__ void store_mn_half(uint8_t *blk_hi, uint8_t *blk_lo, int r, int half, const float *v) {
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq) {
+        const int q = 4 * half + qq;
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            __nv_bfloat16 h0, l0, h1, l1;
+            split_bf16(v[8 * qq + 2 * e], h0, l0);
+            split_bf16(v[8 * qq + 2 * e + 1], h1, l1);
+            h[e] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+            l[e] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+        }
+        const int off = r * 128 + ((q ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4 *>(blk_hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4 *>(blk_lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+}
+
 // ---- phase 1: state-independent chunk quantities -----------------------------------
 // grid (n_chunks, h_v, n_seqs), 256 threads, dynamic smem kPrepSmem
 constexpr int kLd = kD + 4;   // padded row stride of the [64][128] tiles
 constexpr int kLdA = kC + 4;  // row stride of A (16-byte row quads)
-constexpr size_t kPrepSmem = (3 * kC * kLd + kC * kLdA + kC * (kC + 1) + 4 * kC) * sizeof(float);
+// [K ; Q] as the split-bf16 K-major operand of the tcgen05 product [K ; Q] K^T: two
+// regions (key dims 0..63, 64..127) of 128 rows (K tokens, then Q tokens) x 128 bytes,
+// hi then lo; B = the first 64 rows (K) of the same image
+constexpr int kKQImgBytes = 2 * 2 * 128 * 128;
+constexpr size_t kPrepF32 = (3 * kC * kLd + kC * kLdA + kC * (kC + 1) + 4 * kC) * sizeof(float);
+constexpr size_t kPrepImg = (kPrepF32 + 1023) / 1024 * 1024;
+constexpr size_t kPrepSmem = kPrepImg + kKQImgBytes + 64 + 1024;  // + barrier, TMEM slot, alignment
 
 __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
-    extern __shared__ __align__(16) float sm[];
+    extern __shared__ uint8_t prep_raw[];
+    float *sm = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(prep_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *kq_img = reinterpret_cast<uint8_t *>(sm) + kPrepImg;
+    uint64_t *mma_bar = reinterpret_cast<uint64_t *>(kq_img + kKQImgBytes);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(kq_img + kKQImgBytes + 32);
     float *Ks = sm;                  // [64][kLd]  k (L2-normalised)
     float *Qs = Ks + kC * kLd;       // [64][kLd]  q
     float *Vs = Qs + kC * kLd;       // [64][kLd]  v
@@ -149,37 +159,105 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     const int t0 = c * kC;
     const int n_valid = min(kC, p.T - t0);
 
-    // rows: warp w loads rows w, w+8, ..., w+56 (all loads issued before use)
+    // rows: warp w loads rows w, w+8, ..., w+56.  The raw words of every row are loaded
+    // before any is converted, so all 24 loads of a thread are in flight together.
     {
         float4 kk[8], qq[8], vv[8];
+        const bool f32 = p.dtype == SQMIX_F32;
+        uint4 rk[8], rq[8], rv[8];  // f32: the values; 16-bit types: the first 8 bytes
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
             const int t = warp + 8 * r;
-            kk[r] = qq[r] = vv[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+            rk[r] = rq[r] = rv[r] = make_uint4(0u, 0u, 0u, 0u);
             if (t < n_valid) {
                 const int64_t qk_off = seq * p.qk_sseq + (t0 + t) * p.qk_st + static_cast<int64_t>(hk) * kD + 4 * lane;
                 const int64_t v_off = seq * p.v_sseq + (t0 + t) * p.v_st + static_cast<int64_t>(h) * kD + 4 * lane;
-                kk[r] = load4v(p.k, qk_off, p.dtype);
-                qq[r] = load4v(p.q, qk_off, p.dtype);
-                vv[r] = load4v(p.v, v_off, p.dtype);
+                if (f32) {
+                    rk[r] = *reinterpret_cast<const uint4 *>(static_cast<const float *>(p.k) + qk_off);
+                    rq[r] = *reinterpret_cast<const uint4 *>(static_cast<const float *>(p.q) + qk_off);
+                    rv[r] = *reinterpret_cast<const uint4 *>(static_cast<const float *>(p.v) + v_off);
+                } else {
+                    const uint2 a = *reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(p.k) + qk_off);
+                    const uint2 b = *reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(p.q) + qk_off);
+                    const uint2 c2 = *reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(p.v) + v_off);
+                    rk[r] = make_uint4(a.x, a.y, 0u, 0u);
+                    rq[r] = make_uint4(b.x, b.y, 0u, 0u);
+                    rv[r] = make_uint4(c2.x, c2.y, 0u, 0u);
+                }
+            }
+        }
+        auto cvt = [&](const uint4 &w) -> float4 {
+            if (f32) return make_float4(__uint_as_float(w.x), __uint_as_float(w.y), __uint_as_float(w.z), __uint_as_float(w.w));
+            if (p.dtype == SQMIX_BF16) {
+                const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w.x));
+                const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w.y));
+                return make_float4(a.x, a.y, b.x, b.y);
+            }
+            const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&w.y));
+            return make_float4(a.x, a.y, b.x, b.y);
+        };
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            kk[r] = cvt(rk[r]);
+            qq[r] = cvt(rq[r]);
+            vv[r] = cvt(rv[r]);
+        }
+        // L2 norm factors of the 16 rows (q and k), the 5-step reductions interleaved
+        float fk[8], fq[8];
+        if (p.l2_eps > 0.f) {  // rms_norm(x, eps/n) * n^-1/2 (gdn.rs:133-142)
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                fk[r] = kk[r].x * kk[r].x + kk[r].y * kk[r].y + kk[r].z * kk[r].z + kk[r].w * kk[r].w;
+                fq[r] = qq[r].x * qq[r].x + qq[r].y * qq[r].y + qq[r].z * qq[r].z + qq[r].w * qq[r].w;
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    fk[r] += __shfl_xor_sync(0xffffffffu, fk[r], off);
+                    fq[r] += __shfl_xor_sync(0xffffffffu, fq[r], off);
+                }
+            const float r2 = 1.0f / sqrtf(128.0f);
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                fk[r] = 1.0f / sqrtf(fk[r] / 128.0f + p.l2_eps / 128.0f) * r2;
+                fq[r] = 1.0f / sqrtf(fq[r] / 128.0f + p.l2_eps / 128.0f) * r2;
             }
         }
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
             const int t = warp + 8 * r;
             float4 k4 = kk[r], q4 = qq[r];
-            if (p.l2_eps > 0.f && t < n_valid) {  // rms_norm(x, eps/n) * n^-1/2 (gdn.rs:133-142)
-                const float sk = warp_sum32(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w);
-                const float sq = warp_sum32(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
-                const float r2 = 1.0f / sqrtf(128.0f);
-                const float fk = 1.0f / sqrtf(sk / 128.0f + p.l2_eps / 128.0f) * r2;
-                const float fq = 1.0f / sqrtf(sq / 128.0f + p.l2_eps / 128.0f) * r2;
-                k4 = make_float4(k4.x * fk, k4.y * fk, k4.z * fk, k4.w * fk);
-                q4 = make_float4(q4.x * fq, q4.y * fq, q4.z * fq, q4.w * fq);
+            if (p.l2_eps > 0.f && t < n_valid) {
+                k4 = make_float4(k4.x * fk[r], k4.y * fk[r], k4.z * fk[r], k4.w * fk[r]);
+                q4 = make_float4(q4.x * fq[r], q4.y * fq[r], q4.z * fq[r], q4.w * fq[r]);
             }
             *reinterpret_cast<float4 *>(Ks + t * kLd + 4 * lane) = k4;
             *reinterpret_cast<float4 *>(Qs + t * kLd + 4 * lane) = q4;
             *reinterpret_cast<float4 *>(Vs + t * kLd + 4 * lane) = vv[r];
+            // dims 4 lane .. 4 lane + 3: region lane / 16, 16-byte chunk (lane % 16) / 2,
+            // half (lane % 2); rows t (K) and 64 + t (Q)
+            const float kx[4] = {k4.x, k4.y, k4.z, k4.w}, qx[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+            for (int which = 0; which < 2; ++which) {
+                const float *xv = which ? qx : kx;
+                const int row = t + 64 * which;
+                uint32_t hw[2], lw[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    __nv_bfloat16 h0, l0, h1, l1;
+                    split_bf16(xv[2 * e], h0, l0);
+                    split_bf16(xv[2 * e + 1], h1, l1);
+                    hw[e] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) |
+                            (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+                    lw[e] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) |
+                            (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+                }
+                const int off = (lane >> 4) * 16384 + row * 128 + ((((lane & 15) >> 1) ^ (row & 7)) << 4) + (lane & 1) * 8;
+                *reinterpret_cast<uint2 *>(kq_img + off) = make_uint2(hw[0], hw[1]);
+                *reinterpret_cast<uint2 *>(kq_img + kKQImgBytes / 2 + off) = make_uint2(lw[0], lw[1]);
+            }
         }
     }
     if (tid < kC) {
@@ -199,30 +277,64 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
         const float excl = sc - (a0 + a1);
         G[2 * lane] = excl + a0;
         G[2 * lane + 1] = excl + a0 + a1;
+        // g is consumed: its slots now hold e^{G_t}
+        gg[2 * lane] = expf(excl + a0);
+        gg[2 * lane + 1] = expf(excl + a0 + a1);
     }
     __syncthreads();
+    const float *eG = gg;
 
-    // K K^T and Q K^T, 4x4 outputs per thread: rows tb + 16a, columns sb + 16b
+    // [K K^T ; Q K^T] = [K ; Q] K^T on the tensor cores (split bf16, f32 in TMEM), then
+    // thread = row: A_ts = beta_t e^{G_t - G_s} k_t.k_s (s < t), Mq_ts = e^{G_t - G_s}
+    // q_t.k_s / sqrt(128) (s <= t)
     {
-        const int tb = tid >> 4, sb = tid & 15;
-        float kk[4][4] = {}, qk[4][4] = {};
-#pragma unroll 4
-        for (int i = 0; i < kD; ++i) {
-            float kt[4], qt[4], ks[4];
-#pragma unroll
-            for (int a = 0; a < 4; ++a) {
-                kt[a] = Ks[(tb + 16 * a) * kLd + i];
-                qt[a] = Qs[(tb + 16 * a) * kLd + i];
-                ks[a] = Ks[(sb + 16 * a) * kLd + i];
-            }
-#pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    kk[a][b] = fmaf(kt[a], ks[b], kk[a][b]);
-                    qk[a][b] = fmaf(qt[a], ks[b], qk[a][b]);
-                }
+        if (tid == 0) {
+            mbar_init(mma_bar, 1);
+            fence_mbar_init();
         }
+        if (warp == 0) tc::tmem_alloc(tmem_slot, 64);
+        tc::fence_proxy_async_smem();  // the operand images (generic stores) -> tensor core
+        tc::fence_before();
+        __syncthreads();
+        tc::fence_after();
+        const uint32_t tmem = *tmem_slot;
+        if (tid == 0) {
+            const uint32_t img = smem_u32(kq_img);
+            constexpr uint32_t idesc = tc::idesc_bf16_f32(128, kC, 0, 0);
+#pragma unroll 1
+            for (int ks = 0; ks < kD / 16; ++ks) {
+                const uint32_t ko = (ks >> 2) * 16384 + (ks & 3) * 32;  // region, 16 dims within it
+                const uint64_t ah = tc::desc_sw128(img + ko, 16, 1024);
+                const uint64_t al = tc::desc_sw128(img + kKQImgBytes / 2 + ko, 16, 1024);
+                tc::mma_ss(tmem, al, ah, idesc, ks > 0 ? 1u : 0u);
+                tc::mma_ss(tmem, ah, al, idesc, 1u);
+                tc::mma_ss(tmem, ah, ah, idesc, 1u);
+            }
+            tc::commit(mma_bar);
+        }
+        bool mok = mbar_wait(mma_bar, 0);
+        if (!mok) atomicOr(reinterpret_cast<uint32_t *>(p.ws), 8u);
+        tc::fence_after();
+        if (warp < 4) {  // TMEM lanes 0..127 = rows: K K^T (0..63) into A, Q K^T (64..127) into Mq
+            const int t = tid & 63;
+            float *dst = tid < kC ? A + t * kLdA : Mq + t * (kC + 1);
+            uint32_t raw[32];
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                tc::ld32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + 32 * half, raw);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) dst[32 * half + i] = __uint_as_float(raw[i]);
+            }
+        }
+        tc::fence_before();
+        __syncthreads();
+        tc::fence_after();
+        if (warp == 0) {
+            if (!mok) mbar_wait(mma_bar, 0);  // never release TMEM under a running MMA
+            tc::tmem_dealloc(tmem, 64);
+        }
+        // decay, beta and the masks, 4 x 4 entries per thread
+        const int tb = tid >> 4, sb = tid & 15;
         const float rsd = 1.0f / sqrtf(128.0f);
 #pragma unroll
         for (int a = 0; a < 4; ++a)
@@ -230,11 +342,11 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
             for (int b = 0; b < 4; ++b) {
                 const int t = tb + 16 * a, s2 = sb + 16 * b;
                 const float dec = s2 <= t ? expf(G[t] - G[s2]) : 0.f;
-                A[t * kLdA + s2] = s2 < t ? bt[t] * dec * kk[a][b] : 0.f;
-                Mq[t * (kC + 1) + s2] = dec * qk[a][b] * rsd;
+                A[t * kLdA + s2] = s2 < t ? bt[t] * dec * A[t * kLdA + s2] : 0.f;
+                Mq[t * (kC + 1) + s2] = dec * Mq[t * (kC + 1) + s2] * rsd;
             }
+        __syncthreads();
     }
-    __syncthreads();
     uint8_t *wsc = chunk_ws(p, seq, h, c);
     float *Ub = reinterpret_cast<float *>(wsc + kOffUb);
     // forward substitution of (I + A) X = [beta e^G K | beta V], one thread per column,
@@ -245,7 +357,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
         const float *src = is_w ? Ks : Vs;
         float x[kC];
 #pragma unroll
-        for (int t = 0; t < kC; ++t) x[t] = src[t * kLd + col] * bt[t] * (is_w ? expf(G[t]) : 1.f);
+        for (int t = 0; t < kC; ++t) x[t] = src[t * kLd + col] * bt[t] * (is_w ? eG[t] : 1.f);
 #pragma unroll
         for (int t = 1; t < kC; ++t) {
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -276,7 +388,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
             const float rsd = 1.0f / sqrtf(128.0f);
             float v[kC];
 #pragma unroll
-            for (int t = 0; t < kC; ++t) v[t] = Qs[t * kLd + col] * expf(G[t]) * rsd;
+            for (int t = 0; t < kC; ++t) v[t] = Qs[t * kLd + col] * eG[t] * rsd;
             store_mn_row(wsc + kOffA1 + kD * 128, wsc + kOffA1 + kA1Bytes / 2 + kD * 128, col, v);
         } else if (tid < kD + kC) {
             const int t = tid - kD;
@@ -300,14 +412,15 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
 }
 
 // ---- phase 2: walk the chunks of one (sequence, head, 64 value columns) -------------
-// grid (kD / kSN, h_v, n_seqs), 128 threads (thread = TMEM lane = row of the
-// accumulators), dynamic smem kScanSmem.  Per chunk, three split-bf16 tcgen05 MMA
-// groups (hi*hi + hi*lo + lo*hi, f32 accumulators in tensor memory):
+// grid (kD / kSN, h_v, n_seqs), 256 threads: warp w reaches TMEM lanes 32 (w % 4) ..
+// (accumulator rows) and handles columns 32 (w / 4) .. + 31 of them; dynamic smem
+// kScanSmem.  Per chunk, three split-bf16 tcgen05 MMA groups (hi*hi + hi*lo + lo*hi,
+// f32 accumulators in tensor memory):
 //   D1  = [W ; Qs] S0          M 128 (tokens of W, then of Qs), N 64, K 128
-//   Delta = U - D1[0:64]       (threads 0..63, written back as the bf16 B operand)
+//   Delta = U - D1[0:64]       (rows 0..63, written back as the bf16 B operand)
 //   D1 += [0 ; M] Delta        (the O half: O = Qs S0 + M Delta)
 //   D4  = K'^T Delta           M 128 (key index), N 64, K 64
-//   S  <- e^{G_C} S0 + D4      (thread i keeps row i of the f32 state in registers)
+//   S  <- e^{G_C} S0 + D4      (each thread keeps its half row of the f32 state in registers)
 // The operand images of chunk c+1 are brought in by 1-D bulk copies (TMA, no
 // multicast) as soon as the MMAs of chunk c have read the buffers.
 constexpr uint32_t kSmA1 = 0;                                   // 64 KB: hi | lo, each W | Qs
@@ -319,17 +432,14 @@ constexpr uint32_t kSmBar = kSmBD + 2 * kC * 128;
 constexpr size_t kScanSmem = kSmBar + 64 + 1024;                // + alignment slack
 constexpr uint32_t kTmemCols = 128;                              // D1 at 0, D4 at 64
 
-__device__ __forceinline__ void ld64(uint32_t taddr, float (&v)[64]) {
+__device__ __forceinline__ void ld32f(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
     tc::ld32(taddr, r);
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-    tc::ld32(taddr + 32, r);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
 }
 
-__global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(ChunkParams p) {
+__global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb = smem_u32(sm);
@@ -354,7 +464,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(ChunkParams p) {
         bulk_g2s(sm + kSmA4, w + kOffA4, static_cast<uint32_t>(kA4Bytes), &bars[1]);
     };
     // A3's first block (rows of tokens that receive no M Delta: the W half of D1) is zero
-    for (int e = tid; e < static_cast<int>(kA3Bytes / 2 / 16); e += 128) {
+    for (int e = tid; e < static_cast<int>(kA3Bytes / 2 / 16); e += 256) {
         reinterpret_cast<uint4 *>(sm + kSmA3)[e] = make_uint4(0u, 0u, 0u, 0u);
         reinterpret_cast<uint4 *>(sm + kSmA3 + kA3Bytes)[e] = make_uint4(0u, 0u, 0u, 0u);
     }
@@ -369,21 +479,23 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(ChunkParams p) {
     __syncthreads();
     tc::fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+    const int row = 32 * (warp & 3) + (tid & 31);  // accumulator row (TMEM lane)
+    const int half = warp >> 2;                     // columns 32 half .. + 31
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
     if (tid == 0) {
         issue_a1(0);
         issue_a34(0);
     }
-    // row i = tid of the state block: S[i][j] at ((h*128 + j)*128 + i)
+    // row i = row of the state block, columns j0 .. j0 + 31: S[i][j] at ((h*128 + j)*128 + i)
     const int64_t plane_elems = static_cast<int64_t>(p.h_v) * kD * kD;
     float *st_seq = p.state + static_cast<int64_t>(seq) * p.n_planes * plane_elems;
     int plane = p.sel ? p.sel[seq] : 0;
     plane = min(max(plane, 0), p.n_planes - 1);
-    float srow[kSN];
+    const int j0 = jb * kSN + 32 * half;
+    float srow[32];
 #pragma unroll
-    for (int j = 0; j < kSN; ++j)
-        srow[j] = st_seq[plane * plane_elems + (static_cast<int64_t>(h) * kD + jb * kSN + j) * kD + tid];
-    store_mn_row(sm + kSmBS, sm + kSmBS + kD * 128, tid, srow);
+    for (int j = 0; j < 32; ++j) srow[j] = st_seq[plane * plane_elems + (static_cast<int64_t>(h) * kD + j0 + j) * kD + row];
+    store_mn_half(sm + kSmBS, sm + kSmBS + kD * 128, row, half, srow);
 
     constexpr uint32_t idesc = tc::idesc_bf16_f32(128, kSN, 1, 1);
     // split-bf16 products: (A hi, B hi), (A hi, B lo), (A lo, B hi)
@@ -417,11 +529,11 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(ChunkParams p) {
     for (int c = 0; c < p.n_chunks && ok; ++c) {
         const uint8_t *wsc = chunk_ws(p, seq, h, c);
         const float eGC = reinterpret_cast<const float *>(wsc + kOffSb)[0];
-        float u[kSN];
-        if (tid < kC) {
-            const float4 *ur = reinterpret_cast<const float4 *>(wsc + kOffUb + (static_cast<int64_t>(tid) * kD + jb * kSN) * 4);
+        float u[32];
+        if (row < kC) {
+            const float4 *ur = reinterpret_cast<const float4 *>(wsc + kOffUb + (static_cast<int64_t>(row) * kD + j0) * 4);
 #pragma unroll
-            for (int q = 0; q < kSN / 4; ++q) {
+            for (int q = 0; q < 8; ++q) {
                 const float4 x = ur[q];
                 u[4 * q] = x.x;
                 u[4 * q + 1] = x.y;
@@ -443,14 +555,12 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(ChunkParams p) {
             last_a1 = c + 1;
         }
         // ---- Delta = U - W S0 (rows t = 0..63) as the bf16 B operand ----
-        if (tid < kC) {
-            float d[kSN];
-            ld64(tmem + lane_base, d);
+        if (row < kC) {  // warps 0, 1, 4, 5
+            float d[32];
+            ld32f(tmem + lane_base + 32 * half, d);
 #pragma unroll
-            for (int j = 0; j < kSN; ++j) d[j] = u[j] - d[j];
-            store_mn_row(sm + kSmBD, sm + kSmBD + kC * 128, tid, d);
-        } else {
-            // the other warps' lanes take part in no load here
+            for (int j = 0; j < 32; ++j) d[j] = u[j] - d[j];
+            store_mn_half(sm + kSmBD, sm + kSmBD + kC * 128, row, half, d);
         }
         tc::fence_proxy_async_smem();
         tc::fence_before();
@@ -471,24 +581,24 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(ChunkParams p) {
             last_a34 = c + 1;
         }
         // ---- outputs O (rows 64..127 of D1 = tokens 0..63) ----
-        if (tid >= kC) {
-            const int t = c * kC + (tid - kC);
-            float o[kSN];
-            ld64(tmem + lane_base, o);
+        if (row >= kC) {  // warps 2, 3, 6, 7
+            const int t = c * kC + (row - kC);
+            float o[32];
+            ld32f(tmem + lane_base + 32 * half, o);
             if (t < p.T) {
                 float4 *orow = reinterpret_cast<float4 *>(
-                    p.out + ((static_cast<int64_t>(seq) * p.T_all + t) * p.h_v + h) * kD + jb * kSN);
+                    p.out + ((static_cast<int64_t>(seq) * p.T_all + t) * p.h_v + h) * kD + j0);
 #pragma unroll
-                for (int q = 0; q < kSN / 4; ++q) orow[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                for (int q = 0; q < 8; ++q) orow[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
             }
         }
         // ---- S = e^{G_C} S0 + K'^T Delta (row i = tid) ----
         {
-            float d4[kSN];
-            ld64(tmem + lane_base + kSN, d4);
+            float d4[32];
+            ld32f(tmem + lane_base + kSN + 32 * half, d4);
 #pragma unroll
-            for (int j = 0; j < kSN; ++j) srow[j] = fmaf(eGC, srow[j], d4[j]);
-            store_mn_row(sm + kSmBS, sm + kSmBS + kD * 128, tid, srow);
+            for (int j = 0; j < 32; ++j) srow[j] = fmaf(eGC, srow[j], d4[j]);
+            store_mn_half(sm + kSmBS, sm + kSmBS + kD * 128, row, half, srow);
         }
         tc::fence_proxy_async_smem();
         tc::fence_before();
@@ -505,8 +615,8 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(ChunkParams p) {
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < kSN; ++j)
-            st_seq[p.plane_out * plane_elems + (static_cast<int64_t>(h) * kD + jb * kSN + j) * kD + tid] = srow[j];
+        for (int j = 0; j < 32; ++j)
+            st_seq[p.plane_out * plane_elems + (static_cast<int64_t>(h) * kD + j0 + j) * kD + row] = srow[j];
     }
     tc::fence_before();
     __syncthreads();
@@ -600,7 +710,7 @@ extern "C" int sqmix_gdn_prefill(const sqmix_gdn_args *a, void *workspace, size_
     gdn_chunk_prep_kernel<<<dim3(p.n_chunks, a->h_v, a->n_seqs), 256, kPrepSmem, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill prep launch");
-    gdn_chunk_scan_kernel<<<dim3(kD / kSN, a->h_v, a->n_seqs), 128, kScanSmem, st>>>(p);
+    gdn_chunk_scan_kernel<<<dim3(kD / kSN, a->h_v, a->n_seqs), 256, kScanSmem, st>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill scan launch");
     if (a->n_snap > 1)
