@@ -44,9 +44,11 @@ constexpr int kSN = 64;    // value columns per scan CTA
 // Per (sequence, head, chunk) in the workspace.  The four chunk matrices the scan
 // multiplies with are stored as bf16 pairs x = hi + lo (hi = bf16(x), lo = bf16(x - hi))
 // in the shared-memory image of the tcgen05 operand layout, so that one bulk copy
-// brings them in: MN-major, 128-byte swizzle, blocks of 64 MN elements x rows of the
-// contraction index (row r at r * 128 bytes, 16-byte chunk q stored at q ^ (r & 7)).
-//   A1 = [W ; Qs]  MN = token (W rows, then Qs rows), K = key index i (128 rows)
+// brings them in: 128-byte swizzle, row r at r * 128 bytes, 16-byte chunk q stored at
+// q ^ (r & 7); MN-major images have blocks of 64 MN elements x rows of the contraction
+// index.
+//   A1 = [W ; Qs]  K-major: rows = tokens (W, then Qs; 128 rows), two regions of 64
+//                  key dims (the same 128-byte swizzle, rows of the M index)
 //   A3 = M         MN = token t, K = token s            (64 rows)
 //   A4 = K'^T      MN = key index i (2 blocks), K = t   (64 rows)
 // U stays f32 [64 t][128 j]; scalars: [0] e^{G_C}.
@@ -148,7 +150,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     float *Ks = sm;                  // [64][kLd]  k (L2-normalised)
     float *Qs = Ks + kC * kLd;       // [64][kLd]  q
     float *Vs = Qs + kC * kLd;       // [64][kLd]  v
-    float *A = Vs + kC * kLd;        // [64][kLdA] beta_t e^{G_t - G_s} k_t.k_s, s < t (0 elsewhere)
+    float *A = Vs + kC * kLd;        // [64][kLdA] (transposed) beta_t e^{G_t - G_s} k_t.k_s, s < t
     float *Mq = A + kC * kLdA;       // [64][65]   e^{G_t - G_s} q_t.k_s / sqrt(128), s <= t
     float *G = Mq + kC * (kC + 1);   // [64] cumulative log decay
     float *bt = G + kC;              // [64] beta
@@ -287,53 +289,53 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     // [K K^T ; Q K^T] = [K ; Q] K^T on the tensor cores (split bf16, f32 in TMEM), then
     // thread = row: A_ts = beta_t e^{G_t - G_s} k_t.k_s (s < t), Mq_ts = e^{G_t - G_s}
     // q_t.k_s / sqrt(128) (s <= t)
-    {
-        if (tid == 0) {
-            mbar_init(mma_bar, 1);
-            fence_mbar_init();
-        }
-        if (warp == 0) tc::tmem_alloc(tmem_slot, 64);
-        tc::fence_proxy_async_smem();  // the operand images (generic stores) -> tensor core
-        tc::fence_before();
-        __syncthreads();
-        tc::fence_after();
-        const uint32_t tmem = *tmem_slot;
-        if (tid == 0) {
-            const uint32_t img = smem_u32(kq_img);
-            constexpr uint32_t idesc = tc::idesc_bf16_f32(128, kC, 0, 0);
+    if (tid == 0) {
+        mbar_init(mma_bar, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) tc::tmem_alloc(tmem_slot, 256);
+    tc::fence_proxy_async_smem();  // the operand images (generic stores) -> tensor core
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t img = smem_u32(kq_img);
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    bool mok = true;
+    if (tid == 0) {
+        constexpr uint32_t idesc = tc::idesc_bf16_f32(128, kC, 0, 0);
 #pragma unroll 1
-            for (int ks = 0; ks < kD / 16; ++ks) {
-                const uint32_t ko = (ks >> 2) * 16384 + (ks & 3) * 32;  // region, 16 dims within it
-                const uint64_t ah = tc::desc_sw128(img + ko, 16, 1024);
-                const uint64_t al = tc::desc_sw128(img + kKQImgBytes / 2 + ko, 16, 1024);
-                tc::mma_ss(tmem, al, ah, idesc, ks > 0 ? 1u : 0u);
-                tc::mma_ss(tmem, ah, al, idesc, 1u);
-                tc::mma_ss(tmem, ah, ah, idesc, 1u);
-            }
-            tc::commit(mma_bar);
+        for (int ks = 0; ks < kD / 16; ++ks) {
+            const uint32_t ko = (ks >> 2) * 16384 + (ks & 3) * 32;  // region, 16 dims within it
+            const uint64_t ah = tc::desc_sw128(img + ko, 16, 1024);
+            const uint64_t al = tc::desc_sw128(img + kKQImgBytes / 2 + ko, 16, 1024);
+            tc::mma_ss(tmem, al, ah, idesc, ks > 0 ? 1u : 0u);
+            tc::mma_ss(tmem, ah, al, idesc, 1u);
+            tc::mma_ss(tmem, ah, ah, idesc, 1u);
         }
-        bool mok = mbar_wait(mma_bar, 0);
-        if (!mok) atomicOr(reinterpret_cast<uint32_t *>(p.ws), 8u);
-        tc::fence_after();
-        if (warp < 4) {  // TMEM lanes 0..127 = rows: K K^T (0..63) into A, Q K^T (64..127) into Mq
-            const int t = tid & 63;
-            float *dst = tid < kC ? A + t * kLdA : Mq + t * (kC + 1);
-            uint32_t raw[32];
+        tc::commit(mma_bar);
+    }
+    mok = mbar_wait(mma_bar, 0) && mok;
+    tc::fence_after();
+    float *At = A;  // [64 s][kLdA] holds A transposed: At[s][t] = A_ts
+    if (warp < 4) {  // TMEM lanes 0..127 = rows: K K^T (0..63) into At, Q K^T (64..127) into Mq
+        const int t = tid & 63;
+        uint32_t raw[32];
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                tc::ld32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + 32 * half, raw);
+        for (int hf = 0; hf < 2; ++hf) {
+            tc::ld32(tmem + lane_base + 32 * hf, raw);
+            if (tid < kC) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) dst[32 * half + i] = __uint_as_float(raw[i]);
+                for (int i = 0; i < 32; ++i) At[(32 * hf + i) * kLdA + t] = __uint_as_float(raw[i]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) Mq[t * (kC + 1) + 32 * hf + i] = __uint_as_float(raw[i]);
             }
         }
-        tc::fence_before();
-        __syncthreads();
-        tc::fence_after();
-        if (warp == 0) {
-            if (!mok) mbar_wait(mma_bar, 0);  // never release TMEM under a running MMA
-            tc::tmem_dealloc(tmem, 64);
-        }
-        // decay, beta and the masks, 4 x 4 entries per thread
+    }
+    tc::fence_before();
+    __syncthreads();
+    {  // decay, beta and the masks, 4 x 4 entries per thread
         const int tb = tid >> 4, sb = tid & 15;
         const float rsd = 1.0f / sqrtf(128.0f);
 #pragma unroll
@@ -342,72 +344,153 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
             for (int b = 0; b < 4; ++b) {
                 const int t = tb + 16 * a, s2 = sb + 16 * b;
                 const float dec = s2 <= t ? expf(G[t] - G[s2]) : 0.f;
-                A[t * kLdA + s2] = s2 < t ? bt[t] * dec * A[t * kLdA + s2] : 0.f;
+                At[s2 * kLdA + t] = s2 < t ? bt[t] * dec * At[s2 * kLdA + t] : 0.f;
                 Mq[t * (kC + 1) + s2] = dec * Mq[t * (kC + 1) + s2] * rsd;
             }
-        __syncthreads();
     }
+    // B = [diag(beta e^G) K | diag(beta) V] (K index s = token, N = 256) as the MN-major
+    // split-bf16 image over the consumed [K ; Q] image: 4 blocks of 64 columns x 64 rows
+    {
+        const int s2 = tid >> 2, blk = tid & 3;
+        const float *src = blk < 2 ? Ks + s2 * kLd + 64 * blk : Vs + s2 * kLd + 64 * (blk - 2);
+        const float f = bt[s2] * (blk < 2 ? eG[s2] : 1.f);
+        float v[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = src[i] * f;
+        store_mn_row(kq_img + blk * kC * 128, kq_img + 4 * kC * 128 + blk * kC * 128, s2, v);
+    }
+    __syncthreads();  // A complete; V consumed (its space takes the T image below)
+    // T = (I + A)^-1 by right-looking forward substitution: warp w solves columns
+    // 8w .. 8w + 7, lane l holding rows l and l + 32 of each.  At step s, row s of every
+    // column is final; it is broadcast from its lane and subtracted, times A_ts, from
+    // all rows t (A_ts = 0 for t <= s, so earlier rows are unchanged).  A is read
+    // transposed (At[s][t]: conflict-free).  Column j of T is row j of the MN-major
+    // image of T (K index j, M = t), written as split bf16.
+    uint8_t *t_img = reinterpret_cast<uint8_t *>(Vs);  // hi 8 KB | lo 8 KB (1024-aligned)
+    {
+        const int l = lane;
+        float x[8][2];
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            const int col = 8 * warp + cc;
+            x[cc][0] = l == col ? 1.f : 0.f;
+            x[cc][1] = l + 32 == col ? 1.f : 0.f;
+        }
+#pragma unroll 2
+        for (int s2 = 0; s2 < kC - 1; ++s2) {
+            const float a0 = At[s2 * kLdA + l], a1 = At[s2 * kLdA + l + 32];
+            const int src = s2 & 31;
+            const bool hi = s2 >= 32;
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                const float xs = __shfl_sync(0xffffffffu, hi ? x[cc][1] : x[cc][0], src);
+                x[cc][0] = fmaf(-a0, xs, x[cc][0]);
+                x[cc][1] = fmaf(-a1, xs, x[cc][1]);
+            }
+        }
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            const int col = 8 * warp + cc;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int t = l + 32 * e;
+                __nv_bfloat16 vh, vl;
+                split_bf16(x[cc][e], vh, vl);
+                const int off = col * 128 + ((((t >> 3) ^ (col & 7)) & 7) << 4) + (t & 7) * 2;
+                *reinterpret_cast<__nv_bfloat16 *>(t_img + off) = vh;
+                *reinterpret_cast<__nv_bfloat16 *>(t_img + kC * 128 + off) = vl;
+            }
+        }
+    }
+    tc::fence_proxy_async_smem();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    // [W | U] = T B: M 128 (rows 64..127 read the bytes after T and are ignored), N 256,
+    // K 64, into TMEM columns 0..255
+    if (tid == 0) {
+        constexpr uint32_t idesc = tc::idesc_bf16_f32(128, 256, 1, 1);
+        const uint32_t timg = smem_u32(t_img);
+#pragma unroll 1
+        for (int ks = 0; ks < kC / 16; ++ks) {
+            const uint32_t ko = ks * 2048;
+            const uint64_t ah = tc::desc_sw128(timg + ko, kC * 128, 1024);
+            const uint64_t al = tc::desc_sw128(timg + kC * 128 + ko, kC * 128, 1024);
+            const uint64_t bh = tc::desc_sw128(img + ko, kC * 128, 1024);
+            const uint64_t bl = tc::desc_sw128(img + 4 * kC * 128 + ko, kC * 128, 1024);
+            tc::mma_ss(tmem, al, bh, idesc, ks > 0 ? 1u : 0u);
+            tc::mma_ss(tmem, ah, bl, idesc, 1u);
+            tc::mma_ss(tmem, ah, bh, idesc, 1u);
+        }
+        tc::commit(mma_bar);
+    }
+    mok = mbar_wait(mma_bar, 1) && mok;
+    if (!mok && tid == 0) atomicOr(reinterpret_cast<uint32_t *>(p.ws), 8u);
+    tc::fence_after();
+
+    // ---- epilogue: the chunk record --------------------------------------------------
+    //   warps 0, 1: W rows t (TMEM lanes 0..63, columns 0..127) -> A1 rows t (K-major)
+    //   warps 4, 5: U rows t (TMEM lanes 0..63, columns 128..255) -> U f32
+    //   warps 2, 3: Qs rows t -> A1 rows 64 + t;  warps 6, 7: K' rows t (A4), M rows s (A3)
     uint8_t *wsc = chunk_ws(p, seq, h, c);
     float *Ub = reinterpret_cast<float *>(wsc + kOffUb);
-    // forward substitution of (I + A) X = [beta e^G K | beta V], one thread per column,
-    // the column held in registers; A_ts = 0 for s >= t, so whole 4-groups are summed
-    {
-        const int col = tid & 127;
-        const bool is_w = tid < kD;
-        const float *src = is_w ? Ks : Vs;
-        float x[kC];
+    const float GC = G[kC - 1];
+    if (warp == 0 || warp == 1 || warp == 4 || warp == 5) {
+        const int t = tid & 63;
+        const int cb = warp < 4 ? 0 : 128;
 #pragma unroll
-        for (int t = 0; t < kC; ++t) x[t] = src[t * kLd + col] * bt[t] * (is_w ? eG[t] : 1.f);
+        for (int hf = 0; hf < 2; ++hf) {  // 64 columns at a time
+            float v[64];
+            uint32_t raw[32];
+            tc::ld32(tmem + lane_base + cb + 64 * hf, raw);
 #pragma unroll
-        for (int t = 1; t < kC; ++t) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
+            tc::ld32(tmem + lane_base + cb + 64 * hf + 32, raw);
 #pragma unroll
-            for (int s4 = 0; s4 < t; s4 += 4) {
-                const float4 a = *reinterpret_cast<const float4 *>(A + t * kLdA + s4);
-                float &ac = acc[(s4 >> 2) & 3];
-                ac = fmaf(a.x, x[s4], ac);
-                ac = fmaf(a.y, x[s4 + 1], ac);
-                ac = fmaf(a.z, x[s4 + 2], ac);
-                ac = fmaf(a.w, x[s4 + 3], ac);
+            for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(raw[i]);
+            if (cb == 0) {
+                store_mn_row(wsc + kOffA1 + hf * 16384, wsc + kOffA1 + kA1Bytes / 2 + hf * 16384, t, v);
+            } else {
+                float4 *urow = reinterpret_cast<float4 *>(Ub + t * kD + 64 * hf);
+#pragma unroll
+                for (int q = 0; q < 16; ++q) urow[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
             }
-            x[t] -= (acc[0] + acc[1]) + (acc[2] + acc[3]);
         }
-        if (is_w) {  // W column i = col: row col of A1's W block (MN = t)
-            store_mn_row(wsc + kOffA1, wsc + kOffA1 + kA1Bytes / 2, col, x);
-        } else {
+    } else if (warp == 2 || warp == 3) {
+        const int t = tid - 64;
+        const float f = eG[t] * (1.0f / sqrtf(128.0f));
 #pragma unroll
-            for (int t = 0; t < kC; ++t) Ub[t * kD + col] = x[t];
+        for (int hf = 0; hf < 2; ++hf) {
+            float v[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) v[i] = Qs[t * kLd + 64 * hf + i] * f;
+            store_mn_row(wsc + kOffA1 + hf * 16384, wsc + kOffA1 + kA1Bytes / 2 + hf * 16384, 64 + t, v);
         }
+    } else {
+        const int t = tid - 192;
+        const float dk = expf(GC - G[t]);
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk) {
+            float v[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) v[i] = Ks[t * kLd + 64 * blk + i] * dk;
+            store_mn_row(wsc + kOffA4 + blk * kC * 128, wsc + kOffA4 + kA4Bytes / 2 + blk * kC * 128, t, v);
+        }
+        float v[kC];
+#pragma unroll
+        for (int t2 = 0; t2 < kC; ++t2) v[t2] = Mq[t2 * (kC + 1) + t];
+        store_mn_row(wsc + kOffA3, wsc + kOffA3 + kA3Bytes / 2, t, v);
     }
-    // Qs (threads 0..127: row i of A1's Qs block), K'^T (threads 128..191: row t of A4),
-    // M (threads 192..255: row s of A3), from the tiles still in shared memory
-    {
-        const float GC = G[kC - 1];
-        if (tid < kD) {
-            const int col = tid;
-            const float rsd = 1.0f / sqrtf(128.0f);
-            float v[kC];
-#pragma unroll
-            for (int t = 0; t < kC; ++t) v[t] = Qs[t * kLd + col] * eG[t] * rsd;
-            store_mn_row(wsc + kOffA1 + kD * 128, wsc + kOffA1 + kA1Bytes / 2 + kD * 128, col, v);
-        } else if (tid < kD + kC) {
-            const int t = tid - kD;
-            const float dk = expf(GC - G[t]);
-#pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-                float v[64];
-#pragma unroll
-                for (int i = 0; i < 64; ++i) v[i] = Ks[t * kLd + 64 * blk + i] * dk;
-                store_mn_row(wsc + kOffA4 + blk * kC * 128, wsc + kOffA4 + kA4Bytes / 2 + blk * kC * 128, t, v);
-            }
-        } else {
-            const int s2 = tid - kD - kC;
-            float v[kC];
-#pragma unroll
-            for (int t = 0; t < kC; ++t) v[t] = Mq[t * (kC + 1) + s2];
-            store_mn_row(wsc + kOffA3, wsc + kOffA3 + kA3Bytes / 2, s2, v);
+    if (tid == 0) reinterpret_cast<float *>(wsc + kOffSb)[0] = expf(GC);
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (warp == 0) {
+        if (!mok) {  // never release TMEM under a running MMA
+            tc::commit(mma_bar);
+            mbar_wait(mma_bar, 0);
         }
-        if (tid == 0) reinterpret_cast<float *>(wsc + kOffSb)[0] = expf(GC);
+        tc::tmem_dealloc(tmem, 256);
     }
 }
 
@@ -416,7 +499,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
 // (accumulator rows) and handles columns 32 (w / 4) .. + 31 of them; dynamic smem
 // kScanSmem.  Per chunk, three split-bf16 tcgen05 MMA groups (hi*hi + hi*lo + lo*hi,
 // f32 accumulators in tensor memory):
-//   D1  = [W ; Qs] S0          M 128 (tokens of W, then of Qs), N 64, K 128
+//   D1  = [W ; Qs] S0          M 128 (tokens of W, then of Qs; A K-major), N 64, K 128
 //   Delta = U - D1[0:64]       (rows 0..63, written back as the bf16 B operand)
 //   D1 += [0 ; M] Delta        (the O half: O = Qs S0 + M Delta)
 //   D4  = K'^T Delta           M 128 (key index), N 64, K 64
@@ -543,9 +626,20 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
         }
         if (!wait_bar(&bars[0], c & 1, 1u)) { ok = false; break; }
         // ---- D1 = [W ; Qs] S0 ----
-        if (tid == 0) {
+        if (tid == 0) {  // A1 is K-major: region ks / 4, 16 key dims within it
             tc::fence_after();
-            mma3(tmem, sb + kSmA1, static_cast<uint32_t>(kA1Bytes / 2), kD * 128, sb + kSmBS, kD * 128, kD / 16, false);
+            constexpr uint32_t idesc1 = tc::idesc_bf16_f32(128, kSN, 0, 1);
+#pragma unroll 1
+            for (int ks = 0; ks < kD / 16; ++ks) {
+                const uint32_t ka = (ks >> 2) * 16384 + (ks & 3) * 32, kb = ks * 2048;
+                const uint64_t ah = tc::desc_sw128(sb + kSmA1 + ka, 16, 1024);
+                const uint64_t al = tc::desc_sw128(sb + kSmA1 + kA1Bytes / 2 + ka, 16, 1024);
+                const uint64_t bh = tc::desc_sw128(sb + kSmBS + kb, 8192, 1024);
+                const uint64_t bl = tc::desc_sw128(sb + kSmBS + kD * 128 + kb, 8192, 1024);
+                tc::mma_ss(tmem, al, bh, idesc1, ks > 0 ? 1u : 0u);
+                tc::mma_ss(tmem, ah, bl, idesc1, 1u);
+                tc::mma_ss(tmem, ah, bh, idesc1, 1u);
+            }
             tc::commit(&bars[2]);
         }
         if (!wait_bar(&bars[2], mma_phase++ & 1, 2u)) { ok = false; break; }
