@@ -40,7 +40,7 @@ namespace {
 
 constexpr int kC = 64;     // chunk length
 constexpr int kD = 128;    // head dim
-constexpr int kSN = 64;    // value columns per scan CTA
+constexpr int kSN = 32;    // value columns per scan CTA
 // Per (sequence, head, chunk) in the workspace.  The four chunk matrices the scan
 // multiplies with are stored as bf16 pairs x = hi + lo (hi = bf16(x), lo = bf16(x - hi))
 // in the shared-memory image of the tcgen05 operand layout, so that one bulk copy
@@ -100,26 +100,6 @@ __device__ __forceinline__ void store_mn_row(uint8_t *blk_hi, uint8_t *blk_lo, i
             __nv_bfloat16 h0, l0, h1, l1;
             split_bf16(v[8 * q + 2 * e], h0, l0);
             split_bf16(v[8 * q + 2 * e + 1], h1, l1);
-            h[e] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
-            l[e] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
-        }
-        const int off = r * 128 + ((q ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4 *>(blk_hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4 *>(blk_lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
-    }
-}
-
-// Half of such a row: elements 32 * half .. 32 * half + 31 (chunks 4 half .. 4 half + 3).
-__device__ __forceinline__ void store_mn_half(uint8_t *blk_hi, uint8_t *blk_lo, int r, int half, const float *v) {
-#pragma unroll
-    for (int qq = 0; qq < 4; ++qq) {
-        const int q = 4 * half + qq;
-        uint32_t h[4], l[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            __nv_bfloat16 h0, l0, h1, l1;
-            split_bf16(v[8 * qq + 2 * e], h0, l0);
-            split_bf16(v[8 * qq + 2 * e + 1], h1, l1);
             h[e] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
             l[e] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
         }
@@ -495,25 +475,45 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
 }
 
 // ---- phase 2: walk the chunks of one (sequence, head, 64 value columns) -------------
-// grid (kD / kSN, h_v, n_seqs), 256 threads: warp w reaches TMEM lanes 32 (w % 4) ..
-// (accumulator rows) and handles columns 32 (w / 4) .. + 31 of them; dynamic smem
-// kScanSmem.  Per chunk, three split-bf16 tcgen05 MMA groups (hi*hi + hi*lo + lo*hi,
+// grid (kD / kSN, h_v, n_seqs), 128 threads (thread = TMEM lane = accumulator row,
+// all kSN columns of it); dynamic smem kScanSmem.  Per chunk, three split-bf16 tcgen05 MMA groups (hi*hi + hi*lo + lo*hi,
 // f32 accumulators in tensor memory):
-//   D1  = [W ; Qs] S0          M 128 (tokens of W, then of Qs; A K-major), N 64, K 128
+//   D1  = [W ; Qs] S0          M 128 (tokens of W, then of Qs; A K-major), N 32, K 128
 //   Delta = U - D1[0:64]       (rows 0..63, written back as the bf16 B operand)
 //   D1 += [0 ; M] Delta        (the O half: O = Qs S0 + M Delta)
-//   D4  = K'^T Delta           M 128 (key index), N 64, K 64
-//   S  <- e^{G_C} S0 + D4      (each thread keeps its half row of the f32 state in registers)
+//   D4  = K'^T Delta           M 128 (key index), N 32, K 64
+//   S  <- e^{G_C} S0 + D4      (thread i keeps row i of the f32 state block in registers)
 // The operand images of chunk c+1 are brought in by 1-D bulk copies (TMA, no
 // multicast) as soon as the MMAs of chunk c have read the buffers.
-constexpr uint32_t kSmA1 = 0;                                   // 64 KB: hi | lo, each W | Qs
+constexpr uint32_t kSmA1 = 0;                                   // 64 KB: hi | lo, each 2 regions
 constexpr uint32_t kSmA3 = kSmA1 + kA1Bytes;                    // 32 KB: hi | lo, each zero | M
 constexpr uint32_t kSmA4 = kSmA3 + 2 * kA3Bytes;                // 32 KB: hi | lo
-constexpr uint32_t kSmBS = kSmA4 + kA4Bytes;                    // 32 KB: S0 hi | lo (K = i, 128 rows)
-constexpr uint32_t kSmBD = kSmBS + 2 * kD * 128;                // 16 KB: Delta hi | lo (K = t, 64 rows)
-constexpr uint32_t kSmBar = kSmBD + 2 * kC * 128;
+// B operands K-major (rows = the kSN value columns j, 128-byte rows of 64 contraction
+// elements, same swizzle): S0 (K = key index i: 2 regions of kSN rows) and Delta
+// (K = token t: 1 region)
+constexpr uint32_t kBSRegion = kSN * 128;
+constexpr uint32_t kSmBS = kSmA4 + kA4Bytes;                    // 8 KB: hi | lo
+constexpr uint32_t kSmBD = kSmBS + 2 * 2 * kBSRegion;           // 4 KB: hi | lo
+constexpr uint32_t kSmBar = kSmBD + 2 * kBSRegion;
 constexpr size_t kScanSmem = kSmBar + 64 + 1024;                // + alignment slack
-constexpr uint32_t kTmemCols = 128;                              // D1 at 0, D4 at 64
+constexpr uint32_t kTmemCols = 2 * kSN;                          // D1 at 0, D4 at kSN
+
+// Column kidx (contraction index) of a K-major block whose rows are the kSN value
+// columns: v[j] -> row j, as split bf16 (2-byte stores; a warp's 32 consecutive kidx
+// fill 64 contiguous bytes of a row).
+__device__ __forceinline__ void store_k_col(uint8_t *hi, uint8_t *lo, uint32_t region_bytes, int kidx,
+                                            const float *v) {
+    const uint32_t base = (kidx >> 6) * region_bytes + (kidx & 7) * 2;
+    const int q = (kidx & 63) >> 3;
+#pragma unroll
+    for (int j = 0; j < kSN; ++j) {
+        __nv_bfloat16 vh, vl;
+        split_bf16(v[j], vh, vl);
+        const uint32_t off = base + j * 128 + ((q ^ (j & 7)) << 4);
+        *reinterpret_cast<__nv_bfloat16 *>(hi + off) = vh;
+        *reinterpret_cast<__nv_bfloat16 *>(lo + off) = vl;
+    }
+}
 
 __device__ __forceinline__ void ld32f(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
@@ -522,7 +522,7 @@ __device__ __forceinline__ void ld32f(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
+__global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(ChunkParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb = smem_u32(sm);
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
         bulk_g2s(sm + kSmA4, w + kOffA4, static_cast<uint32_t>(kA4Bytes), &bars[1]);
     };
     // A3's first block (rows of tokens that receive no M Delta: the W half of D1) is zero
-    for (int e = tid; e < static_cast<int>(kA3Bytes / 2 / 16); e += 256) {
+    for (int e = tid; e < static_cast<int>(kA3Bytes / 2 / 16); e += 128) {
         reinterpret_cast<uint4 *>(sm + kSmA3)[e] = make_uint4(0u, 0u, 0u, 0u);
         reinterpret_cast<uint4 *>(sm + kSmA3 + kA3Bytes)[e] = make_uint4(0u, 0u, 0u, 0u);
     }
@@ -562,33 +562,33 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
     __syncthreads();
     tc::fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int row = 32 * (warp & 3) + (tid & 31);  // accumulator row (TMEM lane)
-    const int half = warp >> 2;                     // columns 32 half .. + 31
-    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const int row = tid;  // accumulator row (TMEM lane)
+    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
     if (tid == 0) {
         issue_a1(0);
         issue_a34(0);
     }
-    // row i = row of the state block, columns j0 .. j0 + 31: S[i][j] at ((h*128 + j)*128 + i)
+    // row i = row of the state block, columns j0 .. j0 + kSN - 1: S[i][j] at ((h*128 + j)*128 + i)
     const int64_t plane_elems = static_cast<int64_t>(p.h_v) * kD * kD;
     float *st_seq = p.state + static_cast<int64_t>(seq) * p.n_planes * plane_elems;
     int plane = p.sel ? p.sel[seq] : 0;
     plane = min(max(plane, 0), p.n_planes - 1);
-    const int j0 = jb * kSN + 32 * half;
-    float srow[32];
+    const int j0 = jb * kSN;
+    float srow[kSN];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) srow[j] = st_seq[plane * plane_elems + (static_cast<int64_t>(h) * kD + j0 + j) * kD + row];
-    store_mn_half(sm + kSmBS, sm + kSmBS + kD * 128, row, half, srow);
+    for (int j = 0; j < kSN; ++j) srow[j] = st_seq[plane * plane_elems + (static_cast<int64_t>(h) * kD + j0 + j) * kD + row];
+    store_k_col(sm + kSmBS, sm + kSmBS + 2 * kBSRegion, kBSRegion, row, srow);
 
-    constexpr uint32_t idesc = tc::idesc_bf16_f32(128, kSN, 1, 1);
-    // split-bf16 products: (A hi, B hi), (A hi, B lo), (A lo, B hi)
+    constexpr uint32_t idesc = tc::idesc_bf16_f32(128, kSN, 1, 0);
+    // split-bf16 products: (A hi, B hi), (A hi, B lo), (A lo, B hi); A MN-major, B the
+    // K-major Delta (one region: 16 contraction elements = 32 bytes per step)
     auto mma3 = [&](uint32_t d, uint32_t a, uint32_t a_lo, uint32_t a_lbo, uint32_t b, uint32_t b_lo, int ksteps,
                     bool accumulate) {
 #pragma unroll 1
         for (int ks = 0; ks < ksteps; ++ks) {
             const uint32_t ko = ks * 2048;  // 16 rows of the contraction index
             const uint64_t ah = tc::desc_sw128(a + ko, a_lbo, 1024), al = tc::desc_sw128(a + a_lo + ko, a_lbo, 1024);
-            const uint64_t bh = tc::desc_sw128(b + ko, 8192, 1024), bl = tc::desc_sw128(b + b_lo + ko, 8192, 1024);
+            const uint64_t bh = tc::desc_sw128(b + ks * 32, 16, 1024), bl = tc::desc_sw128(b + b_lo + ks * 32, 16, 1024);
             tc::mma_ss(d, al, bh, idesc, (accumulate || ks > 0) ? 1u : 0u);
             tc::mma_ss(d, ah, bl, idesc, 1u);
             tc::mma_ss(d, ah, bh, idesc, 1u);
@@ -612,11 +612,11 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
     for (int c = 0; c < p.n_chunks && ok; ++c) {
         const uint8_t *wsc = chunk_ws(p, seq, h, c);
         const float eGC = reinterpret_cast<const float *>(wsc + kOffSb)[0];
-        float u[32];
+        float u[kSN];
         if (row < kC) {
             const float4 *ur = reinterpret_cast<const float4 *>(wsc + kOffUb + (static_cast<int64_t>(row) * kD + j0) * 4);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
+            for (int q = 0; q < kSN / 4; ++q) {
                 const float4 x = ur[q];
                 u[4 * q] = x.x;
                 u[4 * q + 1] = x.y;
@@ -628,14 +628,14 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
         // ---- D1 = [W ; Qs] S0 ----
         if (tid == 0) {  // A1 is K-major: region ks / 4, 16 key dims within it
             tc::fence_after();
-            constexpr uint32_t idesc1 = tc::idesc_bf16_f32(128, kSN, 0, 1);
+            constexpr uint32_t idesc1 = tc::idesc_bf16_f32(128, kSN, 0, 0);
 #pragma unroll 1
             for (int ks = 0; ks < kD / 16; ++ks) {
-                const uint32_t ka = (ks >> 2) * 16384 + (ks & 3) * 32, kb = ks * 2048;
+                const uint32_t ka = (ks >> 2) * 16384 + (ks & 3) * 32, kb = (ks >> 2) * kBSRegion + (ks & 3) * 32;
                 const uint64_t ah = tc::desc_sw128(sb + kSmA1 + ka, 16, 1024);
                 const uint64_t al = tc::desc_sw128(sb + kSmA1 + kA1Bytes / 2 + ka, 16, 1024);
-                const uint64_t bh = tc::desc_sw128(sb + kSmBS + kb, 8192, 1024);
-                const uint64_t bl = tc::desc_sw128(sb + kSmBS + kD * 128 + kb, 8192, 1024);
+                const uint64_t bh = tc::desc_sw128(sb + kSmBS + kb, 16, 1024);
+                const uint64_t bl = tc::desc_sw128(sb + kSmBS + 2 * kBSRegion + kb, 16, 1024);
                 tc::mma_ss(tmem, al, bh, idesc1, ks > 0 ? 1u : 0u);
                 tc::mma_ss(tmem, ah, bl, idesc1, 1u);
                 tc::mma_ss(tmem, ah, bh, idesc1, 1u);
@@ -649,12 +649,12 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
             last_a1 = c + 1;
         }
         // ---- Delta = U - W S0 (rows t = 0..63) as the bf16 B operand ----
-        if (row < kC) {  // warps 0, 1, 4, 5
-            float d[32];
-            ld32f(tmem + lane_base + 32 * half, d);
+        if (row < kC) {  // warps 0, 1
+            float d[kSN];
+            ld32f(tmem + lane_base, d);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) d[j] = u[j] - d[j];
-            store_mn_half(sm + kSmBD, sm + kSmBD + kC * 128, row, half, d);
+            for (int j = 0; j < kSN; ++j) d[j] = u[j] - d[j];
+            store_k_col(sm + kSmBD, sm + kSmBD + kBSRegion, kBSRegion, row, d);
         }
         tc::fence_proxy_async_smem();
         tc::fence_before();
@@ -663,8 +663,8 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
         if (tid == 0) {
             tc::fence_after();
             mma3(tmem, sb + kSmA3, static_cast<uint32_t>(kA3Bytes), static_cast<uint32_t>(kA3Bytes / 2), sb + kSmBD,
-                 kC * 128, kC / 16, true);
-            mma3(tmem + kSN, sb + kSmA4, static_cast<uint32_t>(kA4Bytes / 2), kC * 128, sb + kSmBD, kC * 128, kC / 16,
+                 kBSRegion, kC / 16, true);
+            mma3(tmem + kSN, sb + kSmA4, static_cast<uint32_t>(kA4Bytes / 2), kC * 128, sb + kSmBD, kBSRegion, kC / 16,
                  false);
             tc::commit(&bars[2]);
         }
@@ -675,24 +675,24 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
             last_a34 = c + 1;
         }
         // ---- outputs O (rows 64..127 of D1 = tokens 0..63) ----
-        if (row >= kC) {  // warps 2, 3, 6, 7
+        if (row >= kC) {  // warps 2, 3
             const int t = c * kC + (row - kC);
-            float o[32];
-            ld32f(tmem + lane_base + 32 * half, o);
+            float o[kSN];
+            ld32f(tmem + lane_base, o);
             if (t < p.T) {
                 float4 *orow = reinterpret_cast<float4 *>(
                     p.out + ((static_cast<int64_t>(seq) * p.T_all + t) * p.h_v + h) * kD + j0);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) orow[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                for (int q = 0; q < kSN / 4; ++q) orow[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
             }
         }
         // ---- S = e^{G_C} S0 + K'^T Delta (row i = tid) ----
         {
-            float d4[32];
-            ld32f(tmem + lane_base + kSN + 32 * half, d4);
+            float d4[kSN];
+            ld32f(tmem + lane_base + kSN, d4);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) srow[j] = fmaf(eGC, srow[j], d4[j]);
-            store_mn_half(sm + kSmBS, sm + kSmBS + kD * 128, row, half, srow);
+            for (int j = 0; j < kSN; ++j) srow[j] = fmaf(eGC, srow[j], d4[j]);
+            store_k_col(sm + kSmBS, sm + kSmBS + 2 * kBSRegion, kBSRegion, row, srow);
         }
         tc::fence_proxy_async_smem();
         tc::fence_before();
@@ -709,7 +709,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(ChunkParams p) {
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
+        for (int j = 0; j < kSN; ++j)
             st_seq[p.plane_out * plane_elems + (static_cast<int64_t>(h) * kD + j0 + j) * kD + row] = srow[j];
     }
     tc::fence_before();
@@ -804,7 +804,7 @@ extern "C" int sqmix_gdn_prefill(const sqmix_gdn_args *a, void *workspace, size_
     gdn_chunk_prep_kernel<<<dim3(p.n_chunks, a->h_v, a->n_seqs), 256, kPrepSmem, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill prep launch");
-    gdn_chunk_scan_kernel<<<dim3(kD / kSN, a->h_v, a->n_seqs), 256, kScanSmem, st>>>(p);
+    gdn_chunk_scan_kernel<<<dim3(kD / kSN, a->h_v, a->n_seqs), 128, kScanSmem, st>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill scan launch");
     if (a->n_snap > 1)
