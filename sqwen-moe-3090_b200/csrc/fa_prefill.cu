@@ -1,35 +1,47 @@
 // FlashAttention prefill over the tiled q4_0 cache on the sm_100a tensor cores
-// (tcgen05 / TMEM).  Replaces ggml_flash_attn_ext for T >= 1 query tokens
+// (tcgen05 / TMEM, CTA pairs).  Replaces ggml_flash_attn_ext for T >= 1 query tokens
 // (src/model/attn.rs:238-249) with the causal mask of src/model/graph.rs:553-559
 // (query t sees keys j <= q_pos0 + t, j < n_kv), GQA 16 / 2 heads, head_dim 256,
 // the partial RoPE of attn.rs:183-204 on Q and the sigmoid output gate of
 // attn.rs:282-283.
 //
-// Work decomposition.  An M-tile is 16 query tokens x the 8 query heads of one KV
-// head (128 rows, row r = 8 * token + head): the 8 heads share every K/V tile, so
-// each dequantised tile feeds 128 rows.  An M-tile's key range is cut into items of
-// L 64-key tiles (L chosen on the device so that there are about four items per
-// CTA); a persistent grid of one CTA per SM takes items from a queue.  Each item
-// leaves (m, l, O) partials per row; fa_prefill_merge_kernel combines the items of
-// an M-tile, applies the gate and writes the output.  pf_setup_kernel builds the
-// item table from the device scalars n_kv and q_pos0 (CUDA-graph friendly).
+// Work decomposition.  An M-tile is 32 query tokens x the 8 query heads of one KV
+// head (256 rows, row r = 8 * token + head), computed by a CTA pair (a cluster of
+// two): the even CTA holds rows 0-127 (tokens 0-15), the odd one rows 128-255, and
+// the even CTA's MMA thread issues cta_group::2 MMAs with M = 256.  Each CTA
+// dequantises only half of every K/V tile (its 32 keys of K, its 128 head dimensions
+// of V): the pair shares the operand, so the per-SM shared-memory traffic for K/V
+// (dequantised stores + tensor-core reads) is half that of one CTA doing M = 128.
+// The key tiles of all M-tiles, concatenated, are cut into one equal segment per
+// pair of the persistent grid (one pair per two SMs); a segment is one to a few items
+// (the part of one M-tile inside the segment).  Each item leaves (m, l, O) partials per
+// row; fa_prefill_merge_kernel combines the items of an M-tile, applies the gate and
+// writes the output.  pf_setup_kernel builds the item table from the device scalars
+// n_kv and q_pos0 (CUDA-graph friendly);
+// pf_qprep_kernel writes Q once per call in the operand layout.
 //
 // One CTA (13 warps):
-//   warp 0      TMEM allocation; lane 0 issues the MMAs: S = Q K^T (M 128, N 64,
-//               K 256; Q read from tensor memory) into one of two TMEM S buffers,
-//               then O += P V (M 128, N 256, K 64; P read from tensor memory) into
-//               the TMEM O accumulator, in
-//               the order S(0) S(1) PV(0) S(2) PV(1) ... so that the tensor core
-//               computes the next S while the softmax warps work on the current one;
+//   warp 0      TMEM allocation (pair form, both CTAs); in the even CTA lane 0 issues
+//               the MMAs: S = Q K^T (M 256, N 64, K 256; Q read from tensor memory)
+//               into one of two TMEM S buffers, then O += P V (M 256, N 256, K 64; P
+//               read from tensor memory) into the TMEM O accumulator, in the order
+//               S(0) S(1) PV(0) S(2) PV(1) ... so that the tensor cores compute the
+//               next S while the softmax warps work on the current one;
 //   warps 1-4   softmax: thread = row; reads S from TMEM, online softmax in the
 //               log2 domain with lazy rescaling (O is rescaled only when the row
 //               maximum grows by more than 2^8), writes P (f16, two keys per
 //               column) over the S buffer it has just read in tensor memory,
 //               and at the end of an item reads O and writes the partials;
-//   warps 5-12  producers: build Q (RoPE, f16) through a shared staging buffer into
-//               tensor memory, and dequantise K and V tiles from q4_0 into
-//               128-byte-swizzled shared memory (three stages; the raw q4_0 of the
-//               next tile is loaded while the current one is converted).
+//   warps 5-12  producers: copy the item's Q rows (prepared once per call by
+//               pf_qprep_kernel: RoPE, f16, contraction order) into tensor memory, and
+//               dequantise this CTA's half of the K and V tiles from q4_0 into
+//               128-byte-swizzled shared memory (six stages; the raw q4_0 of the next
+//               tile is loaded while the current one is converted).
+// Barriers that gate an MMA live in the even CTA; the odd CTA's warps arrive on them
+// remotely (one elected lane per warp, default release semantics, which do not wait for
+// the producers' prefetch loads in flight).  MMA completions are committed to the
+// barrier at the same offset in both CTAs.  The per-item broadcast (item slot written
+// into the peer) uses release / acquire at cluster scope.
 // The contraction order of the head dimension is permuted so that each 16-byte
 // chunk of the tiled cache dequantises into one 16-byte shared-memory chunk; Q uses
 // the same permutation (K side) and the merge undoes the V-side one.
@@ -42,24 +54,26 @@
 namespace sqmix {
 namespace {
 
-constexpr int kPfRows = 128;
+constexpr int kPfRows = 128;    // rows of one CTA (16 tokens x 8 heads)
+constexpr int kPairRows = 256;  // rows of an M-tile (the pair)
 constexpr int kPfTok = 16;
+constexpr int kPairTok = 32;
 constexpr int kPfKeys = 64;
 constexpr int kPfThreads = 13 * 32;
 constexpr int kProdWarp0 = 5;
 constexpr int kProdThreads = 256;
-constexpr int kMaxMtiles = 512;  // T <= 4096
+constexpr int kProdWarps = kProdThreads / 32;
+constexpr int kSoftWarps = 4;
+constexpr int kMaxMtiles = 512;  // setup block size; T <= 4096 gives <= 256 M-tiles
 
-// shared memory (offsets from a 1024-byte aligned base)
-constexpr int kNStage = 3;
-constexpr uint32_t kStageOff = 0;       // 3 stages: K (4 x 8 KB regions) | V (4 x 8 KB)
-constexpr uint32_t kStageBytes = 65536;
-constexpr uint32_t kVInStage = 32768;
-constexpr uint32_t kKvRegion = 8192;    // 64 keys x 128 B
-constexpr uint32_t kPOff = 196608;      // Q staging buffer (128 rows x 512 B) at the
-                                        // start of an item
-constexpr uint32_t kRopeOff = 2 * kStageBytes + kVInStage;  // RoPE table while Q is built
-constexpr uint32_t kBarOff = 229376;
+// shared memory (offsets from a 1024-byte aligned base; identical in both CTAs)
+constexpr int kNStage = 6;
+constexpr uint32_t kStageOff = 0;     // stage: K half (4 regions x 32 keys) | V half (2 regions x 64 keys)
+constexpr uint32_t kStageBytes = 32768;
+constexpr uint32_t kKRegion = 4096;   // 32 keys x 128 B (64 contraction positions)
+constexpr uint32_t kVInStage = 16384;
+constexpr uint32_t kVRegion = 8192;   // 64 keys x 128 B (64 output columns)
+constexpr uint32_t kBarOff = kNStage * kStageBytes;
 constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
 
 // TMEM columns
@@ -71,18 +85,27 @@ constexpr uint32_t kQCol = 384;  // Q: 128 columns (256 f16 per row, two per col
 constexpr float kRescaleLog2 = 8.0f;
 
 // workspace layout
-constexpr size_t kWsHeader = 256;  // [0] u32 err, [8] u32 queue, [12] u32 n_items, [16] u32 L
-constexpr size_t kWsMtab = kWsHeader;                        // int4 per M-tile
-constexpr size_t kWsItems = kWsMtab + kMaxMtiles * 16;       // int4 per item
+constexpr int kMaxPairs = 2048;
+constexpr size_t kWsHeader = 256;  // [0] u32 err, [12] u32 n_items, [16] u32 tiles per segment
+constexpr size_t kWsMtab = kWsHeader;                         // int4 per M-tile
+constexpr size_t kWsSegs = kWsMtab + kMaxMtiles * 16;         // int per pair + 1: first item of each segment
+constexpr size_t kWsItems = kWsSegs + (kMaxPairs + 64) * 4;   // int4 per item
 
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
-__host__ __device__ inline int pf_items_max(int n_ctas, int n_mtiles) { return 4 * n_ctas + n_mtiles + 1; }
-__host__ __device__ inline void pf_ws_layout(int n_ctas, int n_mtiles, size_t *ml, size_t *o, size_t *total) {
-    const size_t items = static_cast<size_t>(pf_items_max(n_ctas, n_mtiles));
+// every segment boundary inside an M-tile adds one item
+__host__ __device__ inline int pf_items_max(int n_pairs, int n_mtiles) { return n_pairs + n_mtiles + 1; }
+// Q image: per M-tile 256 rows x 128 u32 words (f16 pairs in contraction order, the
+// columns the tensor-memory copy of Q takes), RoPE applied
+constexpr size_t kQImgRowBytes = 512;
+__host__ __device__ inline void pf_ws_layout(int n_pairs, int n_mtiles, size_t *ml, size_t *o, size_t *qimg,
+                                             size_t *total) {
+    const size_t items = static_cast<size_t>(pf_items_max(n_pairs, n_mtiles));
     *ml = align256(kWsItems + items * 16);
-    *o = align256(*ml + items * kPfRows * 2 * sizeof(float));
-    *total = *o + items * kPfRows * 256 * sizeof(float);
+    *o = align256(*ml + items * kPairRows * 2 * sizeof(float));
+    *qimg = align256(*o + items * kPairRows * 256 * sizeof(float));
+    *total = *qimg + static_cast<size_t>(n_mtiles) * kPairRows * kQImgRowBytes;
 }
+__host__ __device__ inline int pf_n_mtiles(int T) { return 2 * ((T + kPairTok - 1) / kPairTok); }
 
 struct PfParams {
     const void *q;
@@ -99,10 +122,10 @@ struct PfParams {
     int64_t rope_pos_offset;
     uint8_t *ws;
     int items_max;
+    size_t qimg_off;  // workspace offset of the Q image
 };
 
 __device__ __forceinline__ uint32_t *ws_err(uint8_t *ws) { return reinterpret_cast<uint32_t *>(ws); }
-__device__ __forceinline__ uint32_t *ws_queue(uint8_t *ws) { return reinterpret_cast<uint32_t *>(ws + 8); }
 __device__ __forceinline__ uint32_t *ws_nitems(uint8_t *ws) { return reinterpret_cast<uint32_t *>(ws + 12); }
 
 __device__ __forceinline__ int64_t clamp_nkv(const PfParams &p, uint8_t *ws, bool report) {
@@ -115,70 +138,134 @@ __device__ __forceinline__ int64_t clamp_nkv(const PfParams &p, uint8_t *ws, boo
 }
 
 // ---- item table ------------------------------------------------------------------
-__global__ void __launch_bounds__(kMaxMtiles) pf_setup_kernel(PfParams p, int n_ctas) {
-    __shared__ int red[kMaxMtiles / 32];
-    __shared__ int scan_a[kMaxMtiles], scan_b[kMaxMtiles];
+// The M-tiles' key tiles, concatenated in M-tile order (W tiles in all), are cut into
+// n_pairs segments of ceil(W / n_pairs) tiles; pair q processes segment q.  An item is
+// the part of one M-tile inside one segment: (m, first tile, end tile, 0).  Items are
+// numbered in (M-tile, segment) order, which keeps each segment's items contiguous:
+// segs[q] .. segs[q + 1] - 1.  mtab[m] = (first item, item count, -1, tiles).
+__device__ __forceinline__ void block_scan_excl(int *buf, int m, int v, int &excl, int &total) {
+    buf[m] = v;
+    __syncthreads();
+    for (int off = 1; off < kMaxMtiles; off <<= 1) {
+        const int a = m >= off ? buf[m - off] : 0;
+        __syncthreads();
+        buf[m] += a;
+        __syncthreads();
+    }
+    excl = buf[m] - v;
+    total = buf[kMaxMtiles - 1];
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kMaxMtiles) pf_setup_kernel(PfParams p, int n_pairs) {
+    __shared__ int scan[kMaxMtiles];
     const int m = threadIdx.x;
     const int64_t n_kv = clamp_nkv(p, p.ws, m == 0);
     const int64_t q_pos0 = *p.q_pos0;
     int len = 0;  // 64-key tiles the M-tile sees
     if (m < p.n_mtiles) {
-        int t_last = 16 * (m >> 1) + 15;
+        int t_last = kPairTok * (m >> 1) + kPairTok - 1;
         if (t_last > p.T - 1) t_last = p.T - 1;
         int64_t lim = q_pos0 + t_last + 1;
         if (lim > n_kv) lim = n_kv;
         if (lim < 0) lim = 0;
         len = static_cast<int>((lim + kPfKeys - 1) / kPfKeys);
     }
-    // total work W
-    int v = len;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-    __syncthreads();
-    int W = 0;
-    for (int i = 0; i < kMaxMtiles / 32; ++i) W += red[i];
-    int L = (W + 4 * n_ctas - 1) / (4 * n_ctas);
-    if (L < 16) L = 16;
-    const int nfull = len / L;
-    const int rem = (len % L) > 0 ? 1 : 0;
-    // inclusive scans (Hillis-Steele) of nfull and rem
-    scan_a[m] = nfull;
-    scan_b[m] = rem;
-    __syncthreads();
-    for (int off = 1; off < kMaxMtiles; off <<= 1) {
-        const int a = m >= off ? scan_a[m - off] : 0;
-        const int b = m >= off ? scan_b[m - off] : 0;
-        __syncthreads();
-        scan_a[m] += a;
-        scan_b[m] += b;
-        __syncthreads();
-    }
-    const int total_full = scan_a[kMaxMtiles - 1];
-    const int total = total_full + scan_b[kMaxMtiles - 1];
-    const int fbase = scan_a[m] - nfull;
-    const int ritem = rem ? total_full + scan_b[m] - 1 : -1;
+    int off, W;
+    block_scan_excl(scan, m, len, off, W);
+    const int seg = W > 0 ? (W + n_pairs - 1) / n_pairs : 1;
+    const int q0 = off / seg;
+    const int n_it = len > 0 ? (off + len - 1) / seg - q0 + 1 : 0;
+    int ibase, total;
+    block_scan_excl(scan, m, n_it, ibase, total);
     int4 *mtab = reinterpret_cast<int4 *>(p.ws + kWsMtab);
+    int *segs = reinterpret_cast<int *>(p.ws + kWsSegs);
     int4 *items = reinterpret_cast<int4 *>(p.ws + kWsItems);
-    if (total > p.items_max) {  // cannot happen for L >= W / (4 n_ctas); guarded anyway
+    if (total > p.items_max) {  // cannot happen (at most n_mtiles + n_pairs items); guarded anyway
         if (m == 0) {
             atomicOr(ws_err(p.ws), 32u);
             *ws_nitems(p.ws) = 0;
-            *ws_queue(p.ws) = 0;
         }
+        for (int q = m; q <= n_pairs; q += blockDim.x) segs[q] = 0;
         if (m < p.n_mtiles) mtab[m] = make_int4(0, 0, -1, 0);
         return;
     }
     if (m < p.n_mtiles) {
-        mtab[m] = make_int4(fbase, nfull, ritem, len);
-        for (int k = 0; k < nfull; ++k) items[fbase + k] = make_int4(m, k * L, (k + 1) * L, 0);
-        if (rem) items[ritem] = make_int4(m, nfull * L, len, 0);
+        mtab[m] = make_int4(ibase, n_it, -1, len);
+        for (int k = 0; k < n_it; ++k) {
+            const int q = q0 + k;
+            const int lo = max(off, q * seg) - off, hi = min(off + len, (q + 1) * seg) - off;
+            items[ibase + k] = make_int4(m, lo, hi, 0);
+            if (q * seg >= off) segs[q] = ibase + k;  // segment q starts in this M-tile
+        }
     }
+    // segments past the end of the work are empty
+    const int q_used = (W + seg - 1) / seg;
+    for (int q = q_used + m; q <= n_pairs; q += blockDim.x) segs[q] = total;
     if (m == 0) {
         *ws_nitems(p.ws) = static_cast<uint32_t>(total);
-        *ws_queue(p.ws) = 0;
-        reinterpret_cast<uint32_t *>(p.ws)[4] = static_cast<uint32_t>(L);
+        reinterpret_cast<uint32_t *>(p.ws)[4] = static_cast<uint32_t>(seg);
     }
+}
+
+// ---- Q image ---------------------------------------------------------------------
+// real head dimension of contraction (K-side) position p, 0..255
+__device__ __forceinline__ int k_real_dim(int p) {
+    const int i1 = p >> 7, c = (p >> 5) & 3, w = (p >> 3) & 3, e = p & 7;
+    const int b = 4 * i1 + w;
+    return 32 * b + 4 * c + (e & 3) + 16 * (e >> 2);
+}
+
+// Elements d, d+1 (d even) of a Q row as floats.
+__device__ __forceinline__ float2 load_pair(const void *src, int64_t i, int dtype) {
+    if (dtype == SQMIX_F32) return *reinterpret_cast<const float2 *>(static_cast<const float *>(src) + i);
+    if (dtype == SQMIX_BF16)
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(static_cast<const __nv_bfloat16 *>(src) + i));
+    return __half22float2(*reinterpret_cast<const __half2 *>(static_cast<const __half *>(src) + i));
+}
+
+// Grid (query tokens padded to whole M-tiles, 8): block (t, b) writes the rows of
+// heads 2b, 2b+1 of token t, one word per thread: RoPE (the table of rope_cos_sin for
+// the position, as ggml builds its cache), f16, contraction permutation; word w of a
+// row holds positions 2w, 2w+1, which are the adjacent head dimensions
+// k_real_dim(2w), k_real_dim(2w) + 1.  Rows of padding tokens are zero.  Q rows must
+// be aligned to two elements (the host checks it).
+__global__ void __launch_bounds__(256) pf_qprep_kernel(PfParams p) {
+    __shared__ float2 rope_tab[32];
+    const int t = blockIdx.x;
+    const int half = p.rope_n_rot >> 1;
+    if (threadIdx.x < 32) {
+        const int i = threadIdx.x;
+        rope_tab[i] = (i < half && t < p.T) ? rope_cos_sin(*p.q_pos0 + t + p.rope_pos_offset, p.rope_theta_scale, i)
+                                            : make_float2(1.f, 0.f);
+    }
+    const int head = 2 * blockIdx.y + (threadIdx.x >> 7), w = threadIdx.x & 127;
+    const int dim = k_real_dim(2 * w);  // even; dim + 1 is position 2w + 1
+    float2 x = make_float2(0.f, 0.f), y = x;
+    const bool live = t < p.T;
+    const bool rot = dim < p.rope_n_rot;
+    const bool lo = dim < half;
+    if (live) {
+        const int64_t rbase = t * p.q_st + head * p.q_sh;
+        x = load_pair(p.q, rbase + dim, p.q_dtype);
+        if (rot) y = load_pair(p.q, rbase + (lo ? dim + half : dim - half), p.q_dtype);
+    }
+    __syncthreads();
+    uint32_t v = 0u;
+    if (live) {
+        if (rot) {
+            const int i = lo ? dim : dim - half;
+            const float2 c0 = rope_tab[i], c1 = rope_tab[i + 1];
+            x = lo ? make_float2(__fsub_rn(__fmul_rn(x.x, c0.x), __fmul_rn(y.x, c0.y)),
+                                 __fsub_rn(__fmul_rn(x.y, c1.x), __fmul_rn(y.y, c1.y)))
+                   : make_float2(__fadd_rn(__fmul_rn(y.x, c0.y), __fmul_rn(x.x, c0.x)),
+                                 __fadd_rn(__fmul_rn(y.y, c1.y), __fmul_rn(x.y, c1.x)));
+        }
+        v = pack_half2(x.x, x.y);
+    }
+    uint32_t *img = reinterpret_cast<uint32_t *>(p.ws + p.qimg_off);
+    const int m = (t / kPairTok) * 2 + (head >> 3), rr = (t % kPairTok) * 8 + (head & 7);
+    img[(static_cast<size_t>(m) * kPairRows + rr) * (kQImgRowBytes / 4) + w] = v;
 }
 
 // ---- helpers -----------------------------------------------------------------------
@@ -196,21 +283,31 @@ __device__ __forceinline__ uint32_t nib_pair(uint32_t x, uint32_t sel, __half2 d
     const __half2 v = __hsub2(u32_as_h2(h), __float2half2_rn(1032.0f));
     return h2_as_u32(__hmul2(v, d2));
 }
+// Bounded wait whose outcome is the same in every lane of the warp: all lanes wait,
+// then vote, so that a warp never splits on a timeout.  Every lane of the warp must
+// call it.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, uint32_t *err,
+                                          uint32_t bit) {
+    bool ok = false;
+    if (!*abort_flag) {
+        ok = mbar_wait(bar, parity);
+        if (!ok) {
+            atomicOr(err, bit);
+            *abort_flag = 1;
+        }
+    }
+    return __all_sync(0xffffffffu, ok);
+}
+// single-thread form (the MMA thread, the item ring); `cl`: acquire at cluster scope
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                              uint32_t *err, uint32_t bit) {
+                                              uint32_t *err, uint32_t bit, bool cl = false) {
     if (*abort_flag) return false;
-    if (mbar_wait(bar, parity)) return true;
+    if (cl ? mbar_wait_cl(bar, parity) : mbar_wait(bar, parity)) return true;
     atomicOr(err, bit);
     *abort_flag = 1;
     return false;
 }
 
-// real head dimension of contraction (K-side) position p, 0..255
-__device__ __forceinline__ int k_real_dim(int p) {
-    const int i1 = p >> 7, c = (p >> 5) & 3, w = (p >> 3) & 3, e = p & 7;
-    const int b = 4 * i1 + w;
-    return 32 * b + 4 * c + (e & 3) + 16 * (e >> 2);
-}
 // real head dimension of output (V-side) column v, 0..255
 __device__ __forceinline__ int v_real_dim(int v) {
     const int i = v >> 6, g = (v >> 3) & 7, w = (v >> 1) & 3, hi = v & 1;
@@ -219,31 +316,30 @@ __device__ __forceinline__ int v_real_dim(int v) {
 }
 
 struct SmemCtl {
-    uint64_t kv_full[kNStage];
-    uint64_t pv_done[kNStage];
-    uint64_t s_full[2];
-    uint64_t s_free[2];
-    uint64_t p_full[2];
-    uint64_t q_full;
-    uint64_t o_free;
-    uint64_t item_full[2];
-    uint64_t item_empty[2];
-    uint64_t final_bar;
-    uint64_t rope_bar;
-    uint64_t qs_bar;
+    uint64_t kv_full[kNStage];  // even CTA: producers of both CTAs
+    uint64_t pv_done[kNStage];  // both: MMA completion
+    uint64_t s_full[2];         // both: MMA completion
+    uint64_t s_free[2];         // even CTA: softmax warps of both CTAs
+    uint64_t p_full[2];         // even CTA: softmax warps of both CTAs
+    uint64_t q_full;            // even CTA: producer warps of both CTAs
+    uint64_t q_free;            // both: MMA completion of an item's last S (Q reusable)
+    uint64_t o_free;            // even CTA: softmax warps of both CTAs
+    uint64_t item_full[2];      // both: the fetcher
+    uint64_t item_empty[2];     // even CTA: every consumer thread of both CTAs
+    uint64_t final_bar;         // both: MMA completion
     int4 item[2];
     uint32_t tmem_base;
     int abort_flag;
 };
 static_assert(sizeof(SmemCtl) <= 256, "control block");
 
-// Raw q4_0 of one 64-key tile for one producer thread (2 K jobs + 2 V jobs).
+// Raw q4_0 of this CTA's half of one 64-key tile for one producer thread.
 struct RawTile {
-    uint4 kn[2], vn[2], vs[2];
-    uint2 ks[2];
+    uint4 kn, vn, vs;
+    uint2 ks;
 };
 
-__global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base_s = (raw + 1023u) & ~1023u;  // shared address of the aligned base
@@ -254,77 +350,91 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs; 1: its peer
+    // shared::cluster address of a barrier of the even CTA / of the peer CTA
+    auto lead = [&](uint64_t *bar) -> uint32_t { return mapa_shared(smem_u32(bar), 0); };
+    auto peer = [&](const void *x) -> uint32_t { return mapa_shared(smem_u32(x), rank ^ 1u); };
     if (threadIdx.x == 0) {
         for (int s = 0; s < kNStage; ++s) {
-            mbar_init(&ctl->kv_full[s], kProdThreads);
+            mbar_init(&ctl->kv_full[s], 2 * kProdWarps);
             mbar_init(&ctl->pv_done[s], 1);
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&ctl->s_full[s], 1);
-            mbar_init(&ctl->s_free[s], kPfRows);
-            mbar_init(&ctl->p_full[s], kPfRows);
+            mbar_init(&ctl->s_free[s], 2 * kSoftWarps);
+            mbar_init(&ctl->p_full[s], 2 * kSoftWarps);
             mbar_init(&ctl->item_full[s], 1);
-            mbar_init(&ctl->item_empty[s], kPfThreads - 31);  // MMA lane + softmax + producers
+            // even CTA: MMA lane + softmax + producers; odd CTA: softmax + producers
+            mbar_init(&ctl->item_empty[s], (kPfThreads - 31) + (kPfThreads - 32));
         }
-        mbar_init(&ctl->q_full, kProdThreads);
-        mbar_init(&ctl->o_free, kPfRows);
+        mbar_init(&ctl->q_full, 2 * kProdWarps);
+        mbar_init(&ctl->q_free, 1);
+        mbar_init(&ctl->o_free, 2 * kSoftWarps);
         mbar_init(&ctl->final_bar, 1);
-        mbar_init(&ctl->rope_bar, kProdThreads);
-        mbar_init(&ctl->qs_bar, kProdThreads);
         ctl->abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 0) {
-        tc::tmem_alloc(&ctl->tmem_base, kTmemCols);
-        tc::tmem_relinquish();
+        tc::tmem_alloc_pair(&ctl->tmem_base, kTmemCols);
+        tc::tmem_relinquish_pair();
     }
     tc::fence_before();
     __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
     tc::fence_after();
     const uint32_t tmem = ctl->tmem_base;
 
     const int64_t n_kv = clamp_nkv(p, p.ws, false);
     const int64_t q_pos0 = *p.q_pos0;
-    const int n_items = static_cast<int>(*ws_nitems(p.ws));
     const int4 *items = reinterpret_cast<const int4 *>(p.ws + kWsItems);
+    // this pair's segment of the item list
+    const int *segs = reinterpret_cast<const int *>(p.ws + kWsSegs);
+    const int pair = static_cast<int>(blockIdx.x >> 1);
+    const int seg_lo = segs[pair], seg_hi = segs[pair + 1];
     const size_t ml_off = align256(kWsItems + static_cast<size_t>(p.items_max) * 16);
-    const size_t o_off = align256(ml_off + static_cast<size_t>(p.items_max) * kPfRows * 2 * sizeof(float));
+    const size_t o_off = align256(ml_off + static_cast<size_t>(p.items_max) * kPairRows * 2 * sizeof(float));
     float *part_ml = reinterpret_cast<float *>(p.ws + ml_off);
     float *part_o = reinterpret_cast<float *>(p.ws + o_off);
 
-    // item ring: the producer leader fetches, every consumer thread copies and releases
-    auto get_item = [&](int iter, int4 &it, bool leader) -> bool {
+    // item ring: the even CTA's first producer fetches and writes the item into both
+    // CTAs; every consumer thread of both CTAs copies it and releases the slot
+    auto get_item = [&](int iter, int4 &it, bool fetcher) -> bool {
         const int slot = iter & 1;
-        if (leader) {
-            if (iter >= 2 && !wait_or_abort(&ctl->item_empty[slot], ((iter - 2) >> 1) & 1, abort_flag, err, 64u)) {
-                it = make_int4(-1, 0, 0, -1);
-                ctl->item[slot] = it;
-                mbar_arrive(&ctl->item_full[slot]);
-                return false;
+        if (fetcher) {
+            int4 e = make_int4(-1, 0, 0, -1);
+            if (iter < 2 ||
+                wait_or_abort(&ctl->item_empty[slot], ((iter - 2) >> 1) & 1, abort_flag, err, 64u, true)) {
+                const int q = seg_lo + iter;
+                e = q < seg_hi ? items[q] : make_int4(-1, 0, 0, 0);
+                e.w = q;
             }
-            const int q = static_cast<int>(atomicAdd(ws_queue(p.ws), 1u));
-            int4 e = q < n_items ? items[q] : make_int4(-1, 0, 0, 0);
-            e.w = q;
             ctl->item[slot] = e;
-            mbar_arrive(&ctl->item_full[slot]);
+            st_cluster_v4(peer(&ctl->item[slot]), e);
+            mbar_arrive_cl(lead(&ctl->item_full[slot]));
+            mbar_arrive_cl(peer(&ctl->item_full[slot]));
         }
-        if (!wait_or_abort(&ctl->item_full[slot], (iter >> 1) & 1, abort_flag, err, 64u)) return false;
+        if (!wait_or_abort(&ctl->item_full[slot], (iter >> 1) & 1, abort_flag, err, 64u, true)) return false;
         it = ctl->item[slot];
-        mbar_arrive(&ctl->item_empty[slot]);
+        mbar_arrive_cl(lead(&ctl->item_empty[slot]));
         return it.x >= 0;
     };
     // parity of the completion of tile jj on a barrier used once per kNStage tiles
     auto stage_parity = [](int jj) -> uint32_t { return static_cast<uint32_t>(jj / kNStage) & 1u; };
 
-    const uint32_t idesc_s = tc::idesc_f16_f32(128, kPfKeys, 0, 0);
-    const uint32_t idesc_pv = tc::idesc_f16_f32(128, 256, 0, 1);
+    const uint32_t idesc_s = tc::idesc_f16_f32(2 * 128, kPfKeys, 0, 0);
+    const uint32_t idesc_pv = tc::idesc_f16_f32(2 * 128, 256, 0, 1);
 
     if (warp == 0) {
-        // =========================== MMA issuer ===========================
-        if (lane == 0) {
+        // =========================== MMA issuer (even CTA) ===========================
+        if (rank == 0 && lane == 0) {
             int j = 0;
             bool ok = true;
-            auto issue_s = [&](int jj) -> bool {
+            // completion of the MMAs issued so far -> barrier `bar` in both CTAs
+            auto commit_both = [&](uint64_t *bar) {
+                tc::commit_pair(lead(bar));
+                tc::commit_pair(peer(bar));
+            };
+            auto issue_s = [&](int jj, bool last_of_item) -> bool {
                 const int sb = jj & 1, st = jj % kNStage;
                 if (!wait_or_abort(&ctl->kv_full[st], stage_parity(jj), abort_flag, err, 1u)) return false;
                 if (jj >= 2 && !wait_or_abort(&ctl->s_free[sb], ((jj - 2) >> 1) & 1, abort_flag, err, 1u))
@@ -332,11 +442,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                 tc::fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 16; ++ks) {
+                    // B = this CTA's 32 keys (K-major, 4 regions of 64 contraction positions)
                     const uint64_t b = tc::desc_sw128(
-                        base_s + kStageOff + st * kStageBytes + (ks >> 2) * kKvRegion + (ks & 3) * 32, 16, 1024);
-                    tc::mma_ts(tmem + kSCol + sb * kPfKeys, tmem + kQCol + ks * 8, b, idesc_s, ks > 0 ? 1u : 0u);
+                        base_s + kStageOff + st * kStageBytes + (ks >> 2) * kKRegion + (ks & 3) * 32, 16, 1024);
+                    tc::mma_ts_pair(tmem + kSCol + sb * kPfKeys, tmem + kQCol + ks * 8, b, idesc_s,
+                                    ks > 0 ? 1u : 0u);
                 }
-                tc::commit(&ctl->s_full[sb]);
+                commit_both(&ctl->s_full[sb]);
+                if (last_of_item) commit_both(&ctl->q_free);
                 return true;
             };
             auto issue_pv = [&](int jj, bool first) -> bool {
@@ -345,13 +458,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                 tc::fence_after();
 #pragma unroll
                 for (int ks = 0; ks < kPfKeys / 16; ++ks) {
-                    // A = P (f16, two keys per column) in the first 32 columns of S buffer bb
+                    // A = P (f16, two keys per column) in the first 32 columns of S buffer bb;
+                    // B = this CTA's 128 output columns (MN-major, 2 blocks of 64)
                     const uint64_t b =
-                        tc::desc_sw128(base_s + kStageOff + st * kStageBytes + kVInStage + ks * 2048, kKvRegion, 1024);
-                    tc::mma_ts(tmem + kOCol, tmem + kSCol + bb * kPfKeys + ks * 8, b, idesc_pv,
-                               (!first || ks > 0) ? 1u : 0u);
+                        tc::desc_sw128(base_s + kStageOff + st * kStageBytes + kVInStage + ks * 2048, kVRegion, 1024);
+                    tc::mma_ts_pair(tmem + kOCol, tmem + kSCol + bb * kPfKeys + ks * 8, b, idesc_pv,
+                                    (!first || ks > 0) ? 1u : 0u);
                 }
-                tc::commit(&ctl->pv_done[st]);
+                commit_both(&ctl->pv_done[st]);
                 return true;
             };
             for (int iter = 0; ok; ++iter) {
@@ -359,29 +473,38 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                 if (!get_item(iter, it, false)) break;
                 const int n = it.z - it.y;
                 if (!wait_or_abort(&ctl->q_full, iter & 1, abort_flag, err, 1u)) break;
-                if (iter > 0 && !wait_or_abort(&ctl->o_free, (iter - 1) & 1, abort_flag, err, 1u)) break;
                 tc::fence_after();
                 const int jf = j;
-                if (!issue_s(jf)) break;
+                if (!issue_s(jf, n == 1)) break;
                 for (int t = 0; t < n; ++t) {
-                    if (t + 1 < n && !issue_s(jf + t + 1)) { ok = false; break; }
+                    if (t + 1 < n && !issue_s(jf + t + 1, t + 2 == n)) { ok = false; break; }
+                    // the item's first PV overwrites O: the previous item's partials are read
+                    // (its S MMAs may run during that epilogue)
+                    if (t == 0 && iter > 0) {
+                        if (!wait_or_abort(&ctl->o_free, (iter - 1) & 1, abort_flag, err, 1u)) { ok = false; break; }
+                        tc::fence_after();
+                    }
                     if (!issue_pv(jf + t, t == 0)) { ok = false; break; }
                 }
                 j = jf + n;
             }
-            // drain: every MMA issued so far completes before TMEM is released
-            tc::commit(&ctl->final_bar);
+            // drain: every MMA issued so far completes before either CTA releases TMEM
+            commit_both(&ctl->final_bar);
             if (!mbar_wait(&ctl->final_bar, 0)) atomicOr(err, 128u);
         }
     } else if (warp < kProdWarp0) {
         // =========================== softmax ===========================
         const int r = 32 * (warp & 3) + lane;  // TMEM lane == row
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-        // waits of a softmax warp end alike in all lanes: the tcgen05.ld/st that follow
-        // are warp-collective
         auto wwait = [&](uint64_t *bar, uint32_t parity) -> bool {
-            const bool r_ok = wait_or_abort(bar, parity, abort_flag, err, 2u);
-            return __all_sync(0xffffffffu, r_ok);
+            return warp_wait(bar, parity, abort_flag, err, 2u);
+        };
+        // one elected arrival per warp on a barrier of the even CTA (after every lane's
+        // tcgen05 accesses are complete and fenced)
+        auto warp_arrive = [&](uint64_t *bar) {
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(lead(bar));
         };
         int j = 0;
         for (int iter = 0;; ++iter) {
@@ -389,7 +512,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
             const bool got = get_item(iter, it, false);
             if (!__all_sync(0xffffffffu, got)) break;
             const int m = it.x, kt0 = it.y, kt1 = it.z, item = it.w;
-            const int token = 16 * (m >> 1) + (r >> 3);
+            const int token = kPairTok * (m >> 1) + kPfTok * static_cast<int>(rank) + (r >> 3);
             int64_t lim = q_pos0 + token;
             if (lim > n_kv - 1) lim = n_kv - 1;
             if (token >= p.T) lim = -1;
@@ -402,8 +525,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                 uint32_t sr[2][32];
                 tc::ld32(tmem + lane_base + kSCol + b * kPfKeys, sr[0]);
                 tc::ld32(tmem + lane_base + kSCol + b * kPfKeys + 32, sr[1]);
-                tc::fence_before();
-                mbar_arrive(&ctl->s_free[b]);
+                warp_arrive(&ctl->s_free[b]);
                 const int64_t key0 = static_cast<int64_t>(kt) * kPfKeys;
                 float x[64];  // raw scores (scale applied below), -inf where masked
 #pragma unroll
@@ -464,220 +586,198 @@ __global__ void __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
                 // and the MMAs of one thread run in issue order.
                 tc::st32(tmem + lane_base + kSCol + b * kPfKeys, ph);
                 tc::wait_st();
-                tc::fence_before();
-                mbar_arrive(&ctl->p_full[b]);
+                warp_arrive(&ctl->p_full[b]);
             }
             if (!ok) break;
             // ---- item epilogue: partial (m, l, O) of every row ----
             const int jl = j - 1;
             if (!wwait(&ctl->pv_done[jl % kNStage], stage_parity(jl))) break;
             tc::fence_after();
-            float *orow = part_o + (static_cast<size_t>(item) * kPfRows + r) * 256;
+            // O partials column-chunk-major ([item][column / 4][row][4]): a warp's stores
+            // of one chunk cover 512 contiguous bytes
+            const int rowp = static_cast<int>(rank) * kPfRows + r;
+            float4 *ob = reinterpret_cast<float4 *>(part_o) + static_cast<size_t>(item) * 64 * kPairRows + rowp;
 #pragma unroll 1
             for (int ch = 0; ch < 8; ++ch) {
                 uint32_t o[32];
                 tc::ld32(tmem + lane_base + kOCol + ch * 32, o);
 #pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                    *reinterpret_cast<float4 *>(orow + ch * 32 + i) =
-                        make_float4(__uint_as_float(o[i]), __uint_as_float(o[i + 1]), __uint_as_float(o[i + 2]),
-                                    __uint_as_float(o[i + 3]));
+                for (int i = 0; i < 8; ++i)
+                    ob[(ch * 8 + i) * kPairRows] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                                               __uint_as_float(o[4 * i + 2]),
+                                                               __uint_as_float(o[4 * i + 3]));
             }
-            tc::fence_before();
-            mbar_arrive(&ctl->o_free);
-            *reinterpret_cast<float2 *>(part_ml + (static_cast<size_t>(item) * kPfRows + r) * 2) =
+            warp_arrive(&ctl->o_free);
+            *reinterpret_cast<float2 *>(part_ml + (static_cast<size_t>(item) * kPairRows + rowp) * 2) =
                 make_float2(m_run, l_run);
         }
     } else {
         // =========================== producers ===========================
         const int pt = threadIdx.x - kProdWarp0 * 32;  // 0..255
-        const bool leader = pt == 0;
-        float2 *rope_tab = reinterpret_cast<float2 *>(base + kRopeOff);  // 16 tokens x 32 pairs
-        // TMEM rows this warp may write (its lane quarter) and which half of a staged block
+        const bool fetcher = rank == 0 && pt == 0;
+        // TMEM rows this warp may write (its lane quarter) and which 32-word slice of each
+        // 64-word half of a Q row
         const int sp = warp & 3, hw = (warp - kProdWarp0) >> 2;
+        auto pwait = [&](uint64_t *bar, uint32_t parity) -> bool {
+            return warp_wait(bar, parity, abort_flag, err, 4u);
+        };
+        // K job: 16 B of nibbles of one of this CTA's 32 keys (group gi = 2 rank + gl)
+        const int k_gl = pt >> 7, k_ch = pt & 127;
+        const int k_i = k_ch >> 5, k_g = (k_ch >> 2) & 7, k_c = k_ch & 3;
+        const int k_gi = 2 * static_cast<int>(rank) + k_gl;
+        const int k_row = k_gl * 16 + k_g + 8 * (k_i >> 1);  // key row in this CTA's K half
+        // V job: 16 B of nibbles of one of the 64 keys in this CTA's segments 2 rank + il
+        const int v_gi = pt >> 6, v_rest = pt & 63;
+        const int v_il = v_rest >> 5, v_g = (v_rest >> 2) & 7, v_c = v_rest & 3;
+        const int v_i = 2 * static_cast<int>(rank) + v_il;
         int j = 0;
-        uint32_t qph = 0;  // phases of qs_bar completed so far
         auto load_raw = [&](int kt, int kvh, RawTile &rw) {
-            const int64_t key0 = static_cast<int64_t>(kt) * kPfKeys;
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int job = pt + kProdThreads * u;
-                const int gi = job >> 7, ch = job & 127;
-                const int i = ch >> 5, g = (ch >> 2) & 7, c = ch & 3;
-                const int64_t unit = ((key0 / kGroupTokens + gi) * kHeadsKV + kvh) * kUnitBytes;
-                rw.kn[u] = __ldg(reinterpret_cast<const uint4 *>(p.k_cache + unit + i * 512 + (4 * g + c) * 16));
-                rw.ks[u] = __ldg(reinterpret_cast<const uint2 *>(p.k_cache + unit + kUnitQsBytes + g * 32 +
-                                                                  (i >> 1) * 16 + 8 * (i & 1)));
-                rw.vn[u] = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + unit + i * 512 + (4 * g + c) * 16));
-                rw.vs[u] = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + unit + kUnitQsBytes + c * 64 + 16 * i));
-            }
+            const int64_t g0 = static_cast<int64_t>(kt) * (kPfKeys / kGroupTokens);
+            const int64_t ku = ((g0 + k_gi) * kHeadsKV + kvh) * kUnitBytes;
+            rw.kn = __ldg(reinterpret_cast<const uint4 *>(p.k_cache + ku + k_i * 512 + (4 * k_g + k_c) * 16));
+            rw.ks = __ldg(reinterpret_cast<const uint2 *>(p.k_cache + ku + kUnitQsBytes + k_g * 32 + (k_i >> 1) * 16 +
+                                                          8 * (k_i & 1)));
+            const int64_t vu = ((g0 + v_gi) * kHeadsKV + kvh) * kUnitBytes;
+            rw.vn = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + vu + v_i * 512 + (4 * v_g + v_c) * 16));
+            rw.vs = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + vu + kUnitQsBytes + v_c * 64 + 16 * v_i));
         };
         for (int iter = 0;; ++iter) {
             int4 it;
-            if (!get_item(iter, it, leader)) break;
+            const bool got = get_item(iter, it, fetcher);
+            if (!__all_sync(0xffffffffu, got)) break;
             const int m = it.x, kt0 = it.y, kt1 = it.z;
             const int kvh = m & 1;
-            const int tok0 = 16 * (m >> 1);
+            // ---- Q: this thread's row (its lane quarter) and 32-word slice of each half,
+            // read from the prepared image; in flight while the previous item drains ----
+            const int qrow = 32 * sp + lane;
+            const uint4 *qsrc = reinterpret_cast<const uint4 *>(
+                p.ws + p.qimg_off + (static_cast<size_t>(m) * kPairRows + rank * kPfRows + qrow) * kQImgRowBytes);
+            auto load_q = [&](int h, uint32_t (&qv)[32]) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const uint4 x = __ldcg(qsrc + h * 16 + hw * 8 + k);
+                    qv[4 * k] = x.x;
+                    qv[4 * k + 1] = x.y;
+                    qv[4 * k + 2] = x.z;
+                    qv[4 * k + 3] = x.w;
+                }
+            };
+            uint32_t qv[32];
+            load_q(0, qv);
+            // the previous item's S MMAs (the readers of Q) are complete; its PVs and
+            // softmax may still run
+            if (iter > 0 && !pwait(&ctl->q_free, (iter - 1) & 1)) break;
+            tc::st32(tmem + (static_cast<uint32_t>(32 * sp) << 16) + kQCol + hw * 32, qv);
+            load_q(1, qv);
+            tc::st32(tmem + (static_cast<uint32_t>(32 * sp) << 16) + kQCol + 64 + hw * 32, qv);
+            tc::wait_st();
             RawTile cur;
-            load_raw(kt0, kvh, cur);  // first tile in flight while Q is built
-            // previous item's MMAs are complete: Q (TMEM), stages and P buffers are free
-            if (j > 0 && !wait_or_abort(&ctl->pv_done[(j - 1) % kNStage], stage_parity(j - 1), abort_flag, err, 4u))
-                break;
-            // ---- Q: RoPE, f16, contraction permutation; staged in shared memory, then
-            // each thread moves its row's half into tensor memory ----
-            const int half = p.rope_n_rot >> 1;
-            for (int e = pt; e < kPfTok * 32; e += kProdThreads) {
-                const int t = e >> 5, i = e & 31;
-                rope_tab[e] = (i < half && tok0 + t < p.T)
-                                  ? rope_cos_sin(q_pos0 + tok0 + t + p.rope_pos_offset, p.rope_theta_scale, i)
-                                  : make_float2(1.f, 0.f);
-            }
-            // every producer's part of the RoPE table is written (bounded, unlike bar.sync)
-            mbar_arrive(&ctl->rope_bar);
-            if (!wait_or_abort(&ctl->rope_bar, iter & 1, abort_flag, err, 4u)) break;
+            load_raw(kt0, kvh, cur);  // (after Q: both at once exceed the 128 registers)
             bool ok = true;
-            for (int h = 0; h < 2 && ok; ++h) {
-                // staging: 128 rows x 16 chunks (8 contraction positions each), 256 B per
-                // row, chunk c of row r at position c ^ (r & 15)
-#pragma unroll 4
-                for (int job = pt; job < kPfRows * 16; job += kProdThreads) {
-                    const int r = job >> 4, cl = job & 15, vc = h * 16 + cl;
-                    const int token = tok0 + (r >> 3);
-                    const int head = kvh * 8 + (r & 7);
-                    uint32_t hv[4] = {0u, 0u, 0u, 0u};
-                    if (token < p.T) {
-                        const int64_t rbase = token * p.q_st + head * p.q_sh;
-                        float v[8];
-#pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            v[e] = kv_row_elem(p.q, rbase, k_real_dim(vc * 8 + e), p.q_dtype, p.rope_n_rot,
-                                               rope_tab + (r >> 3) * 32);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) hv[e] = pack_half2(v[2 * e], v[2 * e + 1]);
-                    }
-                    sts128(base_s + kPOff + r * 256 + ((cl ^ (r & 15)) << 4), make_uint4(hv[0], hv[1], hv[2], hv[3]));
-                }
-                mbar_arrive(&ctl->qs_bar);
-                if (!wait_or_abort(&ctl->qs_bar, qph & 1, abort_flag, err, 4u)) { ok = false; break; }
-                ++qph;
-                {
-                    const int r = 32 * sp + lane;
-                    uint32_t qv[32];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const int cl = hw * 8 + k;
-                        uint4 x;
-                        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                                     : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w)
-                                     : "r"(base_s + kPOff + r * 256 + ((cl ^ (r & 15)) << 4)));
-                        qv[4 * k] = x.x;
-                        qv[4 * k + 1] = x.y;
-                        qv[4 * k + 2] = x.z;
-                        qv[4 * k + 3] = x.w;
-                    }
-                    tc::st32(tmem + (static_cast<uint32_t>(32 * sp) << 16) + kQCol + h * 64 + hw * 32, qv);
-                    tc::wait_st();
-                }
-                if (h == 0) {  // the staging buffer is rewritten for the second half
-                    mbar_arrive(&ctl->qs_bar);
-                    if (!wait_or_abort(&ctl->qs_bar, qph & 1, abort_flag, err, 4u)) { ok = false; break; }
-                    ++qph;
-                }
-            }
             if (!ok) break;
             tc::fence_before();
-            mbar_arrive(&ctl->q_full);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(lead(&ctl->q_full));
             // ---- K / V tiles: the raw q4_0 of tile kt+1 is loaded while tile kt is converted ----
             for (int kt = kt0; kt < kt1; ++kt, ++j) {
                 const int s = j % kNStage;
                 RawTile nxt;
                 if (kt + 1 < kt1) load_raw(kt + 1, kvh, nxt);
                 const int64_t key0 = static_cast<int64_t>(kt) * kPfKeys;
-                if (j >= kNStage &&
-                    !wait_or_abort(&ctl->pv_done[s], stage_parity(j - kNStage), abort_flag, err, 4u)) {
+                if (j >= kNStage && !pwait(&ctl->pv_done[s], stage_parity(j - kNStage))) {
                     ok = false;
                     break;
                 }
                 const uint32_t kst = base_s + kStageOff + s * kStageBytes;
                 const uint32_t vst = kst + kVInStage;
+                // K: key row k_row (group k_gi); blocks 4*(i&1) + w -> region (i&1)*2 + (c>>1),
+                // chunks (c&1)*4 + w.  Lanes c and c+2 write the same chunks of different
+                // regions (same banks): they take the w in the order w ^ 2.
+                {
+                    const bool live = key0 + k_gi * 16 + k_g + 8 * (k_i >> 1) < n_kv;
+                    const uint32_t w4[4] = {cur.kn.x, cur.kn.y, cur.kn.z, cur.kn.w};
+                    const uint32_t d4[2] = {cur.ks.x, cur.ks.y};
+                    const uint32_t rb = kst + ((k_i & 1) * 2 + (k_c >> 1)) * kKRegion;
+                    uint4 outv[4];
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int job = pt + kProdThreads * u;
-                    const int gi = job >> 7, ch = job & 127;
-                    const int i = ch >> 5, g = (ch >> 2) & 7, c = ch & 3;
-                    // K: token row gi*16 + g + 8*(i>>1); blocks 4*(i&1) + w
-                    {
-                        const int row = gi * 16 + g + 8 * (i >> 1);
-                        const bool live = key0 + row < n_kv;
-                        const uint32_t w4[4] = {cur.kn[u].x, cur.kn[u].y, cur.kn[u].z, cur.kn[u].w};
-                        const uint32_t d4[2] = {cur.ks[u].x, cur.ks[u].y};
-                        const uint32_t rb = kst + ((i & 1) * 2 + (c >> 1)) * kKvRegion;
-#pragma unroll
-                        for (int w = 0; w < 4; ++w) {
-                            uint4 outv = make_uint4(0u, 0u, 0u, 0u);
-                            if (live) {
-                                const __half2 dd = u32_as_h2(d4[w >> 1]);
-                                const __half d1 = (w & 1) ? __high2half(dd) : __low2half(dd);
-                                const __half2 d2 = __half2half2(d1);
-                                const uint32_t lo = w4[w] & 0x0F0F0F0Fu;
-                                const uint32_t hi = (w4[w] >> 4) & 0x0F0F0F0Fu;
-                                outv = make_uint4(nib_pair(lo, 0x4140u, d2), nib_pair(lo, 0x4342u, d2),
-                                                  nib_pair(hi, 0x4140u, d2), nib_pair(hi, 0x4342u, d2));
-                            }
-                            sts128(rb + swz(row, (c & 1) * 4 + w), outv);
-                        }
-                    }
-                    // V: tokens {2c, 2c+8, 2c+1, 2c+9} (byte positions 0..3); blocks 2i + (w>>1)
-                    {
-                        const uint32_t w4[4] = {cur.vn[u].x, cur.vn[u].y, cur.vn[u].z, cur.vn[u].w};
-                        const uint32_t d4[4] = {cur.vs[u].x, cur.vs[u].y, cur.vs[u].z, cur.vs[u].w};
-                        const uint32_t rb = vst + i * kKvRegion;
-                        // lo/hi nibbles of the 4 tokens, token-interleaved: [l0 h0 l1 h1], [l2 h2 l3 h3]
-                        uint32_t xy[4][2];
-#pragma unroll
-                        for (int w = 0; w < 4; ++w) {
+                    for (int w = 0; w < 4; ++w) {
+                        outv[w] = make_uint4(0u, 0u, 0u, 0u);
+                        if (live) {
+                            const __half2 dd = u32_as_h2(d4[w >> 1]);
+                            const __half d1 = (w & 1) ? __high2half(dd) : __low2half(dd);
+                            const __half2 d2 = __half2half2(d1);
                             const uint32_t lo = w4[w] & 0x0F0F0F0Fu;
                             const uint32_t hi = (w4[w] >> 4) & 0x0F0F0F0Fu;
-                            asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(xy[w][0]) : "r"(lo), "r"(hi));
-                            asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(xy[w][1]) : "r"(lo), "r"(hi));
+                            outv[w] = make_uint4(nib_pair(lo, 0x4140u, d2), nib_pair(lo, 0x4342u, d2),
+                                                 nib_pair(hi, 0x4140u, d2), nib_pair(hi, 0x4342u, d2));
                         }
+                    }
+                    const bool rot = (k_c & 2) != 0;
 #pragma unroll
-                        for (int pos = 0; pos < 4; ++pos) {
-                            const int tt = (pos & 1) * 8 + 2 * c + (pos >> 1);
-                            const int row = gi * 16 + tt;
-                            const int jj = (pos >> 1) + 2 * (pos & 1);  // scale slot of this token
-                            uint4 outv = make_uint4(0u, 0u, 0u, 0u);
-                            if (key0 + row < n_kv) {
-                                uint32_t o4[4];
+                    for (int s4 = 0; s4 < 4; ++s4) {
+                        const uint4 o = rot ? outv[s4 ^ 2] : outv[s4];
+                        const int w = rot ? (s4 ^ 2) : s4;
+                        sts128(rb + swz(k_row, (k_c & 1) * 4 + w), o);
+                    }
+                }
+                // V: tokens {2c, 2c+8, 2c+1, 2c+9} (byte positions 0..3) of group v_gi;
+                // blocks 2i + (w>>1); region v_il, chunk g
+                {
+                    const uint32_t w4[4] = {cur.vn.x, cur.vn.y, cur.vn.z, cur.vn.w};
+                    const uint32_t d4[4] = {cur.vs.x, cur.vs.y, cur.vs.z, cur.vs.w};
+                    const uint32_t rb = vst + v_il * kVRegion;
+                    // lo/hi nibbles of the 4 tokens, token-interleaved: [l0 h0 l1 h1], [l2 h2 l3 h3]
+                    uint32_t xy[4][2];
 #pragma unroll
-                                for (int w = 0; w < 4; ++w) {
-                                    // scales: [b=2i: jj0..3][b=2i+1: jj0..3] as 8 halves
-                                    const int hidx = (w >> 1) * 4 + jj;
-                                    const __half2 dd = u32_as_h2(d4[hidx >> 1]);
-                                    const __half d1 = (hidx & 1) ? __high2half(dd) : __low2half(dd);
-                                    o4[w] = nib_pair(xy[w][pos >> 1], (pos & 1) ? 0x4342u : 0x4140u,
-                                                     __half2half2(d1));
-                                }
-                                outv = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+                    for (int w = 0; w < 4; ++w) {
+                        const uint32_t lo = w4[w] & 0x0F0F0F0Fu;
+                        const uint32_t hi = (w4[w] >> 4) & 0x0F0F0F0Fu;
+                        asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(xy[w][0]) : "r"(lo), "r"(hi));
+                        asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(xy[w][1]) : "r"(lo), "r"(hi));
+                    }
+#pragma unroll
+                    for (int pos = 0; pos < 4; ++pos) {
+                        const int tt = (pos & 1) * 8 + 2 * v_c + (pos >> 1);
+                        const int row = v_gi * 16 + tt;
+                        const int jj = (pos >> 1) + 2 * (pos & 1);  // scale slot of this token
+                        uint4 outv = make_uint4(0u, 0u, 0u, 0u);
+                        if (key0 + row < n_kv) {
+                            uint32_t o4[4];
+#pragma unroll
+                            for (int w = 0; w < 4; ++w) {
+                                // scales: [b=2i: jj0..3][b=2i+1: jj0..3] as 8 halves
+                                const int hidx = (w >> 1) * 4 + jj;
+                                const __half2 dd = u32_as_h2(d4[hidx >> 1]);
+                                const __half d1 = (hidx & 1) ? __high2half(dd) : __low2half(dd);
+                                o4[w] = nib_pair(xy[w][pos >> 1], (pos & 1) ? 0x4342u : 0x4140u,
+                                                 __half2half2(d1));
                             }
-                            sts128(rb + swz(row, g), outv);
+                            outv = make_uint4(o4[0], o4[1], o4[2], o4[3]);
                         }
+                        sts128(rb + swz(row, v_g), outv);
                     }
                 }
                 tc::fence_proxy_async_smem();
-                mbar_arrive(&ctl->kv_full[s]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(lead(&ctl->kv_full[s]));
                 if (kt + 1 < kt1) cur = nxt;
             }
             if (!ok) break;
         }
     }
 
+    // Neither CTA releases TMEM or exits while the pair's MMAs or remote arrivals may
+    // still touch its memory: past the cluster barrier the even CTA has seen its drain
+    // complete, and the odd CTA then takes the drain's arrival on its own barrier.
     tc::fence_before();
+    __syncthreads();
+    cluster_sync_all();
+    if (rank == 1 && threadIdx.x == 0 && !mbar_wait(&ctl->final_bar, 0)) atomicOr(err, 128u);
     __syncthreads();
     tc::fence_after();
     if (warp == 0) {
         __syncwarp();
-        tc::tmem_dealloc(tmem, kTmemCols);
+        tc::tmem_dealloc_pair(tmem, kTmemCols);
     }
 }
 
@@ -693,44 +793,91 @@ struct PfMergeParams {
     float *lse;
 };
 
-// grid (T, 2 KV heads), 256 threads: thread = output column (V-side order)
+// grid (T, 2 KV heads), 256 threads: one block merges the 8 rows (heads) of one token.
+// Thread i reads the 16-byte partial chunks (column chunk i / 8 and i / 8 + 32, row
+// i % 8), so that a warp's loads cover 128 contiguous bytes per chunk, and folds the
+// items in one online pass; the rows are then written through shared memory in head-
+// dimension order (1 KB contiguous per row).
 __global__ void __launch_bounds__(256) fa_prefill_merge_kernel(PfMergeParams p) {
-    const int t = blockIdx.x, kvh = blockIdx.y, v = threadIdx.x;
-    const int m = (t >> 4) * 2 + kvh;
+    __shared__ float orow[8][256];
+    __shared__ float lse_s[8];
+    const int t = blockIdx.x, kvh = blockIdx.y, i = threadIdx.x;
+    const int hq = i & 7, c4a = i >> 3;  // chunks c4a and c4a + 32
+    const int m = (t / kPairTok) * 2 + kvh;
     const int4 mt = reinterpret_cast<const int4 *>(p.ws + kWsMtab)[m];
     const size_t ml_off = align256(kWsItems + static_cast<size_t>(p.items_max) * 16);
-    const size_t o_off = align256(ml_off + static_cast<size_t>(p.items_max) * kPfRows * 2 * sizeof(float));
-    const float *part_ml = reinterpret_cast<const float *>(p.ws + ml_off);
-    const float *part_o = reinterpret_cast<const float *>(p.ws + o_off);
+    const size_t o_off = align256(ml_off + static_cast<size_t>(p.items_max) * kPairRows * 2 * sizeof(float));
+    const float2 *part_ml = reinterpret_cast<const float2 *>(p.ws + ml_off);
+    const float4 *part_o = reinterpret_cast<const float4 *>(p.ws + o_off);
     const int n_parts = mt.y + (mt.z >= 0 ? 1 : 0);
-    const int dim = v_real_dim(v);
-    for (int hq = 0; hq < 8; ++hq) {
-        const int r = (t & 15) * 8 + hq;
-        const int head = kvh * 8 + hq;
-        float M = -INFINITY;
-        for (int k = 0; k < n_parts; ++k) {
-            const int item = k < mt.y ? mt.x + k : mt.z;
-            M = fmaxf(M, __ldcg(part_ml + (static_cast<size_t>(item) * kPfRows + r) * 2));
-        }
-        float L = 0.f, acc = 0.f;
-        if (M > -INFINITY) {
-            for (int k = 0; k < n_parts; ++k) {
-                const int item = k < mt.y ? mt.x + k : mt.z;
-                const float2 ml = __ldcg(reinterpret_cast<const float2 *>(part_ml) + static_cast<size_t>(item) * kPfRows + r);
-                const float w = ex2(ml.x - M);
-                L += ml.y * w;
-                acc += __ldcg(part_o + (static_cast<size_t>(item) * kPfRows + r) * 256 + v) * w;
-            }
-        }
-        float o = L > 0.f ? acc / L : 0.f;
+    const int r = (t % kPairTok) * 8 + hq;  // row of the M-tile (odd CTA's rows from 128)
+    float M = -INFINITY, L = 0.f;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+#pragma unroll 2
+    for (int k = 0; k < n_parts; ++k) {
+        const size_t item = static_cast<size_t>(k < mt.y ? mt.x + k : mt.z);
+        const float2 ml = __ldcg(&part_ml[item * kPairRows + r]);
+        const float4 o0 = __ldcg(&part_o[(item * 64 + c4a) * kPairRows + r]);
+        const float4 o1 = __ldcg(&part_o[(item * 64 + c4a + 32) * kPairRows + r]);
+        if (ml.x == -INFINITY) continue;  // nothing visible in that item (l = 0, O = 0)
+        const float mn = fmaxf(M, ml.x);
+        const float sa = ex2(M - mn), sb = ex2(ml.x - mn);  // 2^-inf = 0 for the first item
+        M = mn;
+        L = L * sa + ml.y * sb;
+        a0 = make_float4(a0.x * sa + o0.x * sb, a0.y * sa + o0.y * sb, a0.z * sa + o0.z * sb, a0.w * sa + o0.w * sb);
+        a1 = make_float4(a1.x * sa + o1.x * sb, a1.y * sa + o1.y * sb, a1.z * sa + o1.z * sb, a1.w * sa + o1.w * sb);
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const float4 src[2] = {a0, a1};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int v0 = 4 * (c4a + 32 * h);
+        orow[hq][v_real_dim(v0)] = src[h].x * inv;
+        orow[hq][v_real_dim(v0 + 1)] = src[h].y * inv;
+        orow[hq][v_real_dim(v0 + 2)] = src[h].z * inv;
+        orow[hq][v_real_dim(v0 + 3)] = src[h].w * inv;
+    }
+    if (c4a == 0) lse_s[hq] = L > 0.f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
+    __syncthreads();
+    for (int h = 0; h < 8; ++h) {
+        const int head = kvh * 8 + h;
+        float o = orow[h][i];
         if (p.gate) {
-            const float gv = load_act(p.gate, t * p.g_st + head * p.g_sh + dim, p.gate_dtype);
+            const float gv = load_act(p.gate, t * p.g_st + head * p.g_sh + i, p.gate_dtype);
             o *= 1.f / (1.f + expf(-gv));
         }
-        p.out[(static_cast<size_t>(t) * 16 + head) * 256 + dim] = o;
-        if (p.lse && v == 0)
-            p.lse[t * 16 + head] = L > 0.f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
+        p.out[(static_cast<size_t>(t) * 16 + head) * 256 + i] = o;
     }
+    if (p.lse && i < 8) p.lse[t * 16 + kvh * 8 + i] = lse_s[i];
+}
+
+// CTA pairs of the persistent grid for a request of n_ctas CTAs (0 = as many pairs as
+// can be resident at once, at most one CTA per SM).
+int pf_pairs(int n_ctas) {
+    if (n_ctas > 0) return n_ctas >= 2 ? n_ctas / 2 : 1;
+    static int resident = 0;
+    if (resident == 0) {
+        int pairs = sqmix_device_sm_count(-1) / 2;
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(2 * pairs);
+        cfg.blockDim = dim3(kPfThreads);
+        cfg.dynamicSmemBytes = kSmemBytes;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kSmemBytes)) == cudaSuccess &&
+            cudaOccupancyMaxActiveClusters(&n, fa_prefill_kernel, &cfg) == cudaSuccess && n > 0 && n < pairs)
+            pairs = n;
+        cudaGetLastError();
+        resident = pairs < 1 ? 1 : pairs;
+    }
+    return resident;
 }
 
 }  // namespace
@@ -739,11 +886,10 @@ __global__ void __launch_bounds__(256) fa_prefill_merge_kernel(PfMergeParams p) 
 using namespace sqmix;
 
 extern "C" size_t sqmix_fa_prefill_workspace_bytes(int32_t n_q, int32_t n_ctas) {
-    if (n_ctas <= 0) n_ctas = sqmix_device_sm_count(-1);
+    const int n_pairs = pf_pairs(n_ctas);
     if (n_q < 1) n_q = 1;
-    const int n_mtiles = 2 * ((n_q + kPfTok - 1) / kPfTok);
-    size_t a, b, total;
-    pf_ws_layout(n_ctas, n_mtiles, &a, &b, &total);
+    size_t a, b, c, total;
+    pf_ws_layout(n_pairs, pf_n_mtiles(n_q), &a, &b, &c, &total);
     return total;
 }
 
@@ -753,8 +899,7 @@ extern "C" int sqmix_fa_prefill(const sqmix_fa_args *a, sqmix_stream_t stream) {
                     "fa_prefill: q_norm / k_norm are decode-only; normalise with sqmix_head_norm first");
     SQMIX_CHECK_ARG(a->q && a->k_cache && a->v_cache && a->n_kv && a->q_pos0 && a->out && a->workspace,
                     "fa_prefill: null pointer argument");
-    SQMIX_CHECK_ARG(a->n_q >= 1 && a->n_q <= kPfTok * kMaxMtiles / 2, "fa_prefill: n_q=%d (1..%d)", a->n_q,
-                    kPfTok * kMaxMtiles / 2);
+    SQMIX_CHECK_ARG(a->n_q >= 1 && a->n_q <= 4096, "fa_prefill: n_q=%d (1..4096)", a->n_q);
     SQMIX_CHECK_ARG(a->q_dtype == SQMIX_F32 || a->q_dtype == SQMIX_F16 || a->q_dtype == SQMIX_BF16,
                     "fa_prefill: q dtype %d", a->q_dtype);
     SQMIX_CHECK_ARG(!a->gate || a->gate_dtype == SQMIX_F32 || a->gate_dtype == SQMIX_F16 ||
@@ -765,14 +910,21 @@ extern "C" int sqmix_fa_prefill(const sqmix_fa_args *a, sqmix_stream_t stream) {
                         (reinterpret_cast<uintptr_t>(a->v_cache) & 15) == 0 &&
                         (reinterpret_cast<uintptr_t>(a->workspace) & 255) == 0,
                     "fa_prefill: caches must be 16-byte and the workspace 256-byte aligned");
+    {
+        const size_t esz = a->q_dtype == SQMIX_F32 ? 4 : 2;
+        SQMIX_CHECK_ARG(reinterpret_cast<uintptr_t>(a->q) % (2 * esz) == 0 && a->q_stride_tok % 2 == 0 &&
+                            a->q_stride_head % 2 == 0,
+                        "fa_prefill: q must be aligned to two elements with even strides (element pairs are "
+                        "read together)");
+    }
     SQMIX_CHECK_ARG(a->scale > 0.f, "fa_prefill: scale must be positive");
     SQMIX_CHECK_ARG(a->rope_n_rot >= 0 && a->rope_n_rot <= 64 && a->rope_n_rot % 2 == 0 &&
                         (a->rope_n_rot == 0 || a->rope_freq_base > 0.f),
                     "fa_prefill: rope parameters (n_rot <= 64)");
     SQMIX_CHECK_ARG(a->n_new == 0, "fa_prefill: append the step's rows first (sqmix_kv_append_q4_0)");
-    const int n_ctas = a->n_splits > 0 ? a->n_splits : sqmix_device_sm_count(-1);
-    SQMIX_CHECK_ARG(n_ctas >= 1 && n_ctas <= 4096, "fa_prefill: n_splits (CTAs) = %d", n_ctas);
-    const size_t need = sqmix_fa_prefill_workspace_bytes(a->n_q, n_ctas);
+    SQMIX_CHECK_ARG(a->n_splits >= 0 && a->n_splits <= 4096, "fa_prefill: n_splits (CTAs) = %d", a->n_splits);
+    const int n_pairs = pf_pairs(a->n_splits);
+    const size_t need = sqmix_fa_prefill_workspace_bytes(a->n_q, a->n_splits);
     if (a->workspace_bytes < need) {
         set_error("fa_prefill: workspace %zu bytes < %zu needed", a->workspace_bytes, need);
         return SQMIX_ENOSPC;
@@ -796,18 +948,25 @@ extern "C" int sqmix_fa_prefill(const sqmix_fa_args *a, sqmix_stream_t stream) {
     p.q_pos0 = a->q_pos0;
     p.capacity = a->capacity;
     p.T = a->n_q;
-    p.n_mtiles = 2 * ((a->n_q + kPfTok - 1) / kPfTok);
+    p.n_mtiles = pf_n_mtiles(a->n_q);
     p.c = a->scale * 1.4426950408889634f;
     p.rope_n_rot = a->rope_n_rot;
     p.rope_theta_scale =
         a->rope_n_rot > 0 ? powf(a->rope_freq_base, -2.0f / static_cast<float>(a->rope_n_rot)) : 1.0f;
     p.rope_pos_offset = a->rope_pos_offset;
     p.ws = static_cast<uint8_t *>(a->workspace);
-    p.items_max = pf_items_max(n_ctas, p.n_mtiles);
-    pf_setup_kernel<<<1, kMaxMtiles, 0, st>>>(p, n_ctas);
+    p.items_max = pf_items_max(n_pairs, p.n_mtiles);
+    {
+        size_t ml, o, total;
+        pf_ws_layout(n_pairs, p.n_mtiles, &ml, &o, &p.qimg_off, &total);
+    }
+    pf_setup_kernel<<<1, kMaxMtiles, 0, st>>>(p, n_pairs);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "fa_prefill setup launch");
-    fa_prefill_kernel<<<n_ctas, kPfThreads, kSmemBytes, st>>>(p);
+    pf_qprep_kernel<<<dim3(p.n_mtiles / 2 * kPairTok, 8), 256, 0, st>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e, "fa_prefill Q launch");
+    fa_prefill_kernel<<<2 * n_pairs, kPfThreads, kSmemBytes, st>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "fa_prefill launch");
     PfMergeParams mp;

@@ -112,6 +112,42 @@ __device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// ---- CTA pairs (cluster of 2, cta_group::2) ---------------------------------
+// A kernel uses one cta_group throughout: the pair forms below are the only tcgen05
+// instructions with a cta_group qualifier in a pair kernel.  Allocation and release
+// are executed by one warp in EACH CTA of the pair and give both the same columns;
+// the MMA is issued by one thread of the even CTA: A rows 0-127 come from the even
+// CTA and rows 128-255 from the odd one (same shared / tensor-memory address in
+// both), B columns 0..N/2-1 from the even CTA's shared memory and N/2..N-1 from the
+// odd one's, and each CTA's tensor memory receives its 128 rows x N of D.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem] over the pair (M = 256 in idesc).
+__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// One arrival on the mbarrier at shared::cluster address `bar_cl` (this CTA's or the
+// peer's) once every pair MMA issued so far by this thread is done.
+__device__ __forceinline__ void commit_pair(uint32_t bar_cl) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cl)
+                 : "memory");
+}
+
 // named barrier over `n` threads (a multiple of 32)
 __device__ __forceinline__ void named_sync(int id, int n) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");

@@ -68,9 +68,10 @@ def test_prefill_matches_oracle(sq, oracle, P, T):
     assert np.abs(lse - c["wlse"]).max() < 1e-3
 
 
-@pytest.mark.parametrize("n_ctas", [1, 3, 148])
+@pytest.mark.parametrize("n_ctas", [1, 3, 8, 148])
 def test_prefill_item_queue(sq, oracle, n_ctas):
-    """Few CTAs take many items each (item ring, Q reload, O hand-over between items)."""
+    """Few CTA pairs take many items each (item ring, Q reload, O hand-over between items;
+    segments spanning M-tiles)."""
     P, T = 1500, 96
     c = build_case(sq, oracle, P, T, seed=77 + n_ctas)
     out, lse = run_prefill(sq, c, P, n_ctas=n_ctas)
