@@ -58,7 +58,7 @@ constexpr int kPfRows = 128;    // rows of one CTA (16 tokens x 8 heads)
 constexpr int kPairRows = 256;  // rows of an M-tile (the pair)
 constexpr int kPfTok = 16;
 constexpr int kPairTok = 32;
-constexpr int kPfKeys = 64;
+constexpr int kPfKeys = 128;  // keys per tile
 constexpr int kPfThreads = 13 * 32;
 constexpr int kProdWarp0 = 5;
 constexpr int kProdThreads = 256;
@@ -66,21 +66,28 @@ constexpr int kProdWarps = kProdThreads / 32;
 constexpr int kSoftWarps = 4;
 constexpr int kMaxMtiles = 512;  // setup block size; T <= 4096 gives <= 256 M-tiles
 
-// shared memory (offsets from a 1024-byte aligned base; identical in both CTAs)
-constexpr int kNStage = 6;
-constexpr uint32_t kStageOff = 0;     // stage: K half (4 regions x 32 keys) | V half (2 regions x 64 keys)
-constexpr uint32_t kStageBytes = 32768;
-constexpr uint32_t kKRegion = 4096;   // 32 keys x 128 B (64 contraction positions)
-constexpr uint32_t kVInStage = 16384;
-constexpr uint32_t kVRegion = 8192;   // 64 keys x 128 B (64 output columns)
-constexpr uint32_t kBarOff = kNStage * kStageBytes;
+// shared memory (offsets from a 1024-byte aligned base; identical in both CTAs), all
+// operands 128-byte swizzled:
+//   Q      K-major, 4 regions (64 contraction positions) x 128 rows x 128 B
+//   K ring 2 buffers: this CTA's 64 keys of a tile, K-major, 4 regions x 64 keys x 128 B
+//   V ring 2 buffers: 128 keys x this CTA's 128 output columns, MN-major, 2 blocks of
+//          64 columns x 128 keys x 128 B
+constexpr uint32_t kQOff = 0;
+constexpr uint32_t kQBytes = 65536;
+constexpr uint32_t kQRegion = 16384;
+constexpr uint32_t kKOff = kQBytes;
+constexpr uint32_t kKBuf = 32768;
+constexpr uint32_t kKRegion = 8192;
+constexpr uint32_t kVOff = kKOff + 2 * kKBuf;
+constexpr uint32_t kVBuf = 32768;
+constexpr uint32_t kVBlock = 16384;
+constexpr uint32_t kBarOff = kVOff + 2 * kVBuf;
 constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
 
 // TMEM columns
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOCol = 0;    // O: 256 columns f32
-constexpr uint32_t kSCol = 256;  // S buffers: 2 x 64 columns
-constexpr uint32_t kQCol = 384;  // Q: 128 columns (256 f16 per row, two per column)
+constexpr uint32_t kSCol = 256;  // S buffers: 2 x 128 columns (P, f16 pairs, over the first 64)
 
 constexpr float kRescaleLog2 = 8.0f;
 
@@ -94,16 +101,16 @@ constexpr size_t kWsItems = kWsSegs + (kMaxPairs + 64) * 4;   // int4 per item
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 // every segment boundary inside an M-tile adds one item
 __host__ __device__ inline int pf_items_max(int n_pairs, int n_mtiles) { return n_pairs + n_mtiles + 1; }
-// Q image: per M-tile 256 rows x 128 u32 words (f16 pairs in contraction order, the
-// columns the tensor-memory copy of Q takes), RoPE applied
-constexpr size_t kQImgRowBytes = 512;
+// Q image: per M-tile and CTA the 64 KB shared-memory image of Q (f16, RoPE applied,
+// contraction order, K-major 128-byte swizzle), copied in by one bulk copy per item
+constexpr size_t kQImgBytes = kQBytes;
 __host__ __device__ inline void pf_ws_layout(int n_pairs, int n_mtiles, size_t *ml, size_t *o, size_t *qimg,
                                              size_t *total) {
     const size_t items = static_cast<size_t>(pf_items_max(n_pairs, n_mtiles));
     *ml = align256(kWsItems + items * 16);
     *o = align256(*ml + items * kPairRows * 2 * sizeof(float));
     *qimg = align256(*o + items * kPairRows * 256 * sizeof(float));
-    *total = *qimg + static_cast<size_t>(n_mtiles) * kPairRows * kQImgRowBytes;
+    *total = *qimg + static_cast<size_t>(n_mtiles) * 2 * kQImgBytes;
 }
 __host__ __device__ inline int pf_n_mtiles(int T) { return 2 * ((T + kPairTok - 1) / kPairTok); }
 
@@ -225,9 +232,9 @@ __device__ __forceinline__ float2 load_pair(const void *src, int64_t i, int dtyp
 }
 
 // Grid (query tokens padded to whole M-tiles, 8): block (t, b) writes the rows of
-// heads 2b, 2b+1 of token t, one word per thread: RoPE (the table of rope_cos_sin for
-// the position, as ggml builds its cache), f16, contraction permutation; word w of a
-// row holds positions 2w, 2w+1, which are the adjacent head dimensions
+// heads 2b, 2b+1 of token t, one f16 pair per thread: RoPE (the table of rope_cos_sin
+// for the position, as ggml builds its cache), f16, contraction permutation; pair w of
+// a row holds positions 2w, 2w+1, which are the adjacent head dimensions
 // k_real_dim(2w), k_real_dim(2w) + 1.  Rows of padding tokens are zero.  Q rows must
 // be aligned to two elements (the host checks it).
 __global__ void __launch_bounds__(256) pf_qprep_kernel(PfParams p) {
@@ -263,9 +270,13 @@ __global__ void __launch_bounds__(256) pf_qprep_kernel(PfParams p) {
         }
         v = pack_half2(x.x, x.y);
     }
-    uint32_t *img = reinterpret_cast<uint32_t *>(p.ws + p.qimg_off);
-    const int m = (t / kPairTok) * 2 + (head >> 3), rr = (t % kPairTok) * 8 + (head & 7);
-    img[(static_cast<size_t>(m) * kPairRows + rr) * (kQImgRowBytes / 4) + w] = v;
+    // pair row -> CTA and row; positions 2w, 2w+1 -> region, 16-byte chunk (swizzled)
+    const int m = (t / kPairTok) * 2 + (head >> 3), prr = (t % kPairTok) * 8 + (head & 7);
+    const int cta = prr >> 7, rr = prr & 127;
+    const int e = (2 * w) & 63, chunk = e >> 3;
+    const size_t byte = (static_cast<size_t>(m) * 2 + cta) * kQImgBytes + ((2 * w) >> 6) * kQRegion + rr * 128 +
+                        (((chunk ^ (rr & 7)) & 7) << 4) + (e & 7) * 2;
+    *reinterpret_cast<uint32_t *>(p.ws + p.qimg_off + byte) = v;
 }
 
 // ---- helpers -----------------------------------------------------------------------
@@ -316,27 +327,28 @@ __device__ __forceinline__ int v_real_dim(int v) {
 }
 
 struct SmemCtl {
-    uint64_t kv_full[kNStage];  // even CTA: producers of both CTAs
-    uint64_t pv_done[kNStage];  // both: MMA completion
-    uint64_t s_full[2];         // both: MMA completion
-    uint64_t s_free[2];         // even CTA: softmax warps of both CTAs
-    uint64_t p_full[2];         // even CTA: softmax warps of both CTAs
-    uint64_t q_full;            // even CTA: producer warps of both CTAs
-    uint64_t q_free;            // both: MMA completion of an item's last S (Q reusable)
-    uint64_t o_free;            // even CTA: softmax warps of both CTAs
-    uint64_t item_full[2];      // both: the fetcher
-    uint64_t item_empty[2];     // even CTA: every consumer thread of both CTAs
-    uint64_t final_bar;         // both: MMA completion
+    uint64_t k_full[2];     // even CTA: producer warps of both CTAs (K buffer filled)
+    uint64_t v_full[2];     // even CTA: producer warps of both CTAs (V buffer filled)
+    uint64_t s_full[2];     // both: S MMA complete (S ready; its K buffer free)
+    uint64_t pv_done[2];    // both: PV MMA complete (O updated; its V buffer free)
+    uint64_t p_full[2];     // even CTA: softmax warps of both CTAs (P written)
+    uint64_t q_load;        // local: bulk copy of Q
+    uint64_t q_full;        // even CTA: one arrival per CTA (Q in shared memory)
+    uint64_t q_free;        // both: MMA completion of an item's last S (Q reusable)
+    uint64_t o_free;        // even CTA: softmax warps of both CTAs (partials read)
+    uint64_t item_full[2];  // both: the fetcher
+    uint64_t item_empty[2]; // even CTA: every consumer thread of both CTAs
+    uint64_t final_bar;     // both: MMA completion
     int4 item[2];
     uint32_t tmem_base;
     int abort_flag;
 };
 static_assert(sizeof(SmemCtl) <= 256, "control block");
 
-// Raw q4_0 of this CTA's half of one 64-key tile for one producer thread.
+// Raw q4_0 of this CTA's part of one 128-key tile for one producer thread (2 K + 2 V jobs).
 struct RawTile {
-    uint4 kn, vn, vs;
-    uint2 ks;
+    uint4 kn[2], vn[2], vs[2];
+    uint2 ks[2];
 };
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_prefill_kernel(PfParams p) {
@@ -355,19 +367,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
     auto lead = [&](uint64_t *bar) -> uint32_t { return mapa_shared(smem_u32(bar), 0); };
     auto peer = [&](const void *x) -> uint32_t { return mapa_shared(smem_u32(x), rank ^ 1u); };
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kNStage; ++s) {
-            mbar_init(&ctl->kv_full[s], 2 * kProdWarps);
-            mbar_init(&ctl->pv_done[s], 1);
-        }
         for (int s = 0; s < 2; ++s) {
+            mbar_init(&ctl->k_full[s], 2 * kProdWarps);
+            mbar_init(&ctl->v_full[s], 2 * kProdWarps);
             mbar_init(&ctl->s_full[s], 1);
-            mbar_init(&ctl->s_free[s], 2 * kSoftWarps);
+            mbar_init(&ctl->pv_done[s], 1);
             mbar_init(&ctl->p_full[s], 2 * kSoftWarps);
             mbar_init(&ctl->item_full[s], 1);
             // even CTA: MMA lane + softmax + producers; odd CTA: softmax + producers
             mbar_init(&ctl->item_empty[s], (kPfThreads - 31) + (kPfThreads - 32));
         }
-        mbar_init(&ctl->q_full, 2 * kProdWarps);
+        mbar_init(&ctl->q_load, 1);
+        mbar_init(&ctl->q_full, 2);
         mbar_init(&ctl->q_free, 1);
         mbar_init(&ctl->o_free, 2 * kSoftWarps);
         mbar_init(&ctl->final_bar, 1);
@@ -418,8 +429,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
         mbar_arrive_cl(lead(&ctl->item_empty[slot]));
         return it.x >= 0;
     };
-    // parity of the completion of tile jj on a barrier used once per kNStage tiles
-    auto stage_parity = [](int jj) -> uint32_t { return static_cast<uint32_t>(jj / kNStage) & 1u; };
+    // parity of tile jj's completion on a barrier of a two-buffer ring (tiles b, b+2, ...)
+    auto ring_parity = [](int jj) -> uint32_t { return static_cast<uint32_t>(jj >> 1) & 1u; };
 
     const uint32_t idesc_s = tc::idesc_f16_f32(2 * 128, kPfKeys, 0, 0);
     const uint32_t idesc_pv = tc::idesc_f16_f32(2 * 128, 256, 0, 1);
@@ -435,37 +446,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
                 tc::commit_pair(peer(bar));
             };
             auto issue_s = [&](int jj, bool last_of_item) -> bool {
-                const int sb = jj & 1, st = jj % kNStage;
-                if (!wait_or_abort(&ctl->kv_full[st], stage_parity(jj), abort_flag, err, 1u)) return false;
-                if (jj >= 2 && !wait_or_abort(&ctl->s_free[sb], ((jj - 2) >> 1) & 1, abort_flag, err, 1u))
-                    return false;
+                const int sb = jj & 1;
+                if (!wait_or_abort(&ctl->k_full[sb], ring_parity(jj), abort_flag, err, 1u)) return false;
                 tc::fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 16; ++ks) {
-                    // B = this CTA's 32 keys (K-major, 4 regions of 64 contraction positions)
+                    // A = Q (this CTA's 128 rows), B = this CTA's 64 keys; both K-major
+                    const uint64_t a = tc::desc_sw128(base_s + kQOff + (ks >> 2) * kQRegion + (ks & 3) * 32, 16, 1024);
                     const uint64_t b = tc::desc_sw128(
-                        base_s + kStageOff + st * kStageBytes + (ks >> 2) * kKRegion + (ks & 3) * 32, 16, 1024);
-                    tc::mma_ts_pair(tmem + kSCol + sb * kPfKeys, tmem + kQCol + ks * 8, b, idesc_s,
-                                    ks > 0 ? 1u : 0u);
+                        base_s + kKOff + sb * kKBuf + (ks >> 2) * kKRegion + (ks & 3) * 32, 16, 1024);
+                    tc::mma_ss_pair(tmem + kSCol + sb * kPfKeys, a, b, idesc_s, ks > 0 ? 1u : 0u);
                 }
                 commit_both(&ctl->s_full[sb]);
                 if (last_of_item) commit_both(&ctl->q_free);
                 return true;
             };
             auto issue_pv = [&](int jj, bool first) -> bool {
-                const int bb = jj & 1, st = jj % kNStage;
-                if (!wait_or_abort(&ctl->p_full[bb], (jj >> 1) & 1, abort_flag, err, 1u)) return false;
+                const int bb = jj & 1;
+                if (!wait_or_abort(&ctl->p_full[bb], ring_parity(jj), abort_flag, err, 1u)) return false;
+                if (!wait_or_abort(&ctl->v_full[bb], ring_parity(jj), abort_flag, err, 1u)) return false;
                 tc::fence_after();
 #pragma unroll
                 for (int ks = 0; ks < kPfKeys / 16; ++ks) {
-                    // A = P (f16, two keys per column) in the first 32 columns of S buffer bb;
+                    // A = P (f16, two keys per column) in the first 64 columns of S buffer bb;
                     // B = this CTA's 128 output columns (MN-major, 2 blocks of 64)
-                    const uint64_t b =
-                        tc::desc_sw128(base_s + kStageOff + st * kStageBytes + kVInStage + ks * 2048, kVRegion, 1024);
+                    const uint64_t b = tc::desc_sw128(base_s + kVOff + bb * kVBuf + ks * 2048, kVBlock, 1024);
                     tc::mma_ts_pair(tmem + kOCol, tmem + kSCol + bb * kPfKeys + ks * 8, b, idesc_pv,
                                     (!first || ks > 0) ? 1u : 0u);
                 }
-                commit_both(&ctl->pv_done[st]);
+                commit_both(&ctl->pv_done[bb]);
                 return true;
             };
             for (int iter = 0; ok; ++iter) {
@@ -475,6 +484,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
                 if (!wait_or_abort(&ctl->q_full, iter & 1, abort_flag, err, 1u)) break;
                 tc::fence_after();
                 const int jf = j;
+                // S(jj) goes into the S buffer whose P was read by PV(jj - 2), issued earlier
                 if (!issue_s(jf, n == 1)) break;
                 for (int t = 0; t < n; ++t) {
                     if (t + 1 < n && !issue_s(jf + t + 1, t + 2 == n)) { ok = false; break; }
@@ -520,26 +530,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
             bool ok = true;
             for (int kt = kt0; kt < kt1; ++kt, ++j) {
                 const int b = j & 1;
-                if (!wwait(&ctl->s_full[b], (j >> 1) & 1)) { ok = false; break; }
+                const uint32_t sbuf = tmem + lane_base + kSCol + b * kPfKeys;
+                if (!wwait(&ctl->s_full[b], ring_parity(j))) { ok = false; break; }
                 tc::fence_after();
-                uint32_t sr[2][32];
-                tc::ld32(tmem + lane_base + kSCol + b * kPfKeys, sr[0]);
-                tc::ld32(tmem + lane_base + kSCol + b * kPfKeys + 32, sr[1]);
-                warp_arrive(&ctl->s_free[b]);
                 const int64_t key0 = static_cast<int64_t>(kt) * kPfKeys;
-                float x[64];  // raw scores (scale applied below), -inf where masked
-#pragma unroll
-                for (int i = 0; i < 64; ++i) x[i] = __uint_as_float(sr[i >> 5][i & 31]);
-                if (key0 + kPfKeys - 1 > lim) {
-#pragma unroll
-                    for (int i = 0; i < 64; ++i)
-                        if (key0 + i > lim) x[i] = -INFINITY;
-                }
+                // keys key0 + k with k <= vis_last are visible (clamped to -1 .. kPfKeys - 1)
+                int64_t vl = lim - key0;
+                vl = vl < -1 ? -1 : (vl > kPfKeys - 1 ? kPfKeys - 1 : vl);
+                const int vis_last = static_cast<int>(vl);
+                const bool any_masked = __any_sync(0xffffffffu, vis_last < kPfKeys - 1);
+                // pass 1: row maximum of the raw scores over the 128 keys
                 float mx[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) mx[i] = x[i];
+                for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
 #pragma unroll
-                for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], x[i]);
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t sr[64];
+                    tc::ld64(sbuf + 64 * h, sr);
+                    if (any_masked) {
+#pragma unroll
+                        for (int i = 0; i < 64; ++i)
+                            mx[i & 7] = fmaxf(mx[i & 7], 64 * h + i <= vis_last ? __uint_as_float(sr[i]) : -INFINITY);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sr[i]));
+                    }
+                }
                 const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                        fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
                                  p.c;
@@ -551,7 +567,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
                 if (__any_sync(0xffffffffu, need)) {
                     // O holds the PV of the previous tile once it completes
                     const int jp = j - 1;
-                    if (!wwait(&ctl->pv_done[jp % kNStage], stage_parity(jp))) {
+                    if (!wwait(&ctl->pv_done[jp & 1], ring_parity(jp))) {
                         ok = false;
                         break;
                     }
@@ -568,30 +584,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
                 }
                 l_run *= alpha;
                 m_run = m_new;
-                // p = 2^(c s - m): masked entries give 2^-inf = 0; a row with nothing
-                // visible yet subtracts 0 instead of -inf
+                // pass 2: p = 2^(c s - m), masked entries 2^-inf = 0 (a row with nothing
+                // visible yet subtracts 0 instead of -inf); P (f16 pairs) replaces S in the
+                // first 64 columns of the buffer, half h over columns already read
                 const float msub = m_run == -INFINITY ? 0.f : m_run;
                 float lsum[8];
-                uint32_t ph[32];
 #pragma unroll
-                for (int i = 0; i < 64; i += 2) {
-                    const float p0 = ex2(fmaf(x[i], p.c, -msub));
-                    const float p1 = ex2(fmaf(x[i + 1], p.c, -msub));
-                    lsum[(i >> 1) & 7] = (i < 16) ? p0 + p1 : lsum[(i >> 1) & 7] + (p0 + p1);
-                    ph[i >> 1] = pack_half2(p0, p1);
+                for (int i = 0; i < 8; ++i) lsum[i] = 0.f;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t sr[64];
+                    tc::ld64(sbuf + 64 * h, sr);
+                    if (any_masked) {
+#pragma unroll
+                        for (int i = 0; i < 64; ++i)
+                            if (64 * h + i > vis_last) sr[i] = 0xff800000u;  // -inf
+                    }
+                    uint32_t ph[32];
+#pragma unroll
+                    for (int i = 0; i < 64; i += 2) {
+                        const float p0 = ex2(fmaf(__uint_as_float(sr[i]), p.c, -msub));
+                        const float p1 = ex2(fmaf(__uint_as_float(sr[i + 1]), p.c, -msub));
+                        lsum[(i >> 1) & 7] += p0 + p1;
+                        ph[i >> 1] = pack_half2(p0, p1);
+                    }
+                    tc::st32(sbuf + 32 * h, ph);
                 }
                 l_run += ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3])) + ((lsum[4] + lsum[5]) + (lsum[6] + lsum[7]));
-                // P replaces S in the first 32 columns of S buffer b (read above).  The PV
-                // of tile j - 2 that read the previous P there was issued before S(j),
-                // and the MMAs of one thread run in issue order.
-                tc::st32(tmem + lane_base + kSCol + b * kPfKeys, ph);
                 tc::wait_st();
                 warp_arrive(&ctl->p_full[b]);
             }
             if (!ok) break;
             // ---- item epilogue: partial (m, l, O) of every row ----
             const int jl = j - 1;
-            if (!wwait(&ctl->pv_done[jl % kNStage], stage_parity(jl))) break;
+            if (!wwait(&ctl->pv_done[jl & 1], ring_parity(jl))) break;
             tc::fence_after();
             // O partials column-chunk-major ([item][column / 4][row][4]): a warp's stores
             // of one chunk cover 512 contiguous bytes
@@ -615,31 +641,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
         // =========================== producers ===========================
         const int pt = threadIdx.x - kProdWarp0 * 32;  // 0..255
         const bool fetcher = rank == 0 && pt == 0;
-        // TMEM rows this warp may write (its lane quarter) and which 32-word slice of each
-        // 64-word half of a Q row
-        const int sp = warp & 3, hw = (warp - kProdWarp0) >> 2;
         auto pwait = [&](uint64_t *bar, uint32_t parity) -> bool {
             return warp_wait(bar, parity, abort_flag, err, 4u);
         };
-        // K job: 16 B of nibbles of one of this CTA's 32 keys (group gi = 2 rank + gl)
-        const int k_gl = pt >> 7, k_ch = pt & 127;
-        const int k_i = k_ch >> 5, k_g = (k_ch >> 2) & 7, k_c = k_ch & 3;
-        const int k_gi = 2 * static_cast<int>(rank) + k_gl;
-        const int k_row = k_gl * 16 + k_g + 8 * (k_i >> 1);  // key row in this CTA's K half
-        // V job: 16 B of nibbles of one of the 64 keys in this CTA's segments 2 rank + il
-        const int v_gi = pt >> 6, v_rest = pt & 63;
-        const int v_il = v_rest >> 5, v_g = (v_rest >> 2) & 7, v_c = v_rest & 3;
-        const int v_i = 2 * static_cast<int>(rank) + v_il;
+        auto warp_arrive = [&](uint64_t *bar) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(lead(bar));
+        };
         int j = 0;
+        // K job u: 16 B of nibbles of one of this CTA's 64 keys of the tile (16-key groups
+        // 4 rank .. 4 rank + 3); V job u: 16 B of nibbles of one of the 128 keys, this
+        // CTA's segments 2 rank, 2 rank + 1
         auto load_raw = [&](int kt, int kvh, RawTile &rw) {
             const int64_t g0 = static_cast<int64_t>(kt) * (kPfKeys / kGroupTokens);
-            const int64_t ku = ((g0 + k_gi) * kHeadsKV + kvh) * kUnitBytes;
-            rw.kn = __ldg(reinterpret_cast<const uint4 *>(p.k_cache + ku + k_i * 512 + (4 * k_g + k_c) * 16));
-            rw.ks = __ldg(reinterpret_cast<const uint2 *>(p.k_cache + ku + kUnitQsBytes + k_g * 32 + (k_i >> 1) * 16 +
-                                                          8 * (k_i & 1)));
-            const int64_t vu = ((g0 + v_gi) * kHeadsKV + kvh) * kUnitBytes;
-            rw.vn = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + vu + v_i * 512 + (4 * v_g + v_c) * 16));
-            rw.vs = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + vu + kUnitQsBytes + v_c * 64 + 16 * v_i));
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int job = pt + kProdThreads * u;
+                {
+                    const int gl = job >> 7, ch = job & 127;
+                    const int i = ch >> 5, g = (ch >> 2) & 7, c = ch & 3;
+                    const int64_t ku = ((g0 + 4 * rank + gl) * kHeadsKV + kvh) * kUnitBytes;
+                    rw.kn[u] = __ldg(reinterpret_cast<const uint4 *>(p.k_cache + ku + i * 512 + (4 * g + c) * 16));
+                    rw.ks[u] = __ldg(reinterpret_cast<const uint2 *>(p.k_cache + ku + kUnitQsBytes + g * 32 +
+                                                                     (i >> 1) * 16 + 8 * (i & 1)));
+                }
+                {
+                    const int gi = job >> 6, rest = job & 63;
+                    const int i = 2 * static_cast<int>(rank) + (rest >> 5), g = (rest >> 2) & 7, c = rest & 3;
+                    const int64_t vu = ((g0 + gi) * kHeadsKV + kvh) * kUnitBytes;
+                    rw.vn[u] = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + vu + i * 512 + (4 * g + c) * 16));
+                    rw.vs[u] = __ldg(reinterpret_cast<const uint4 *>(p.v_cache + vu + kUnitQsBytes + c * 64 + 16 * i));
+                }
+            }
         };
         for (int iter = 0;; ++iter) {
             int4 it;
@@ -647,85 +680,76 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
             if (!__all_sync(0xffffffffu, got)) break;
             const int m = it.x, kt0 = it.y, kt1 = it.z;
             const int kvh = m & 1;
-            // ---- Q: this thread's row (its lane quarter) and 32-word slice of each half,
-            // read from the prepared image; in flight while the previous item drains ----
-            const int qrow = 32 * sp + lane;
-            const uint4 *qsrc = reinterpret_cast<const uint4 *>(
-                p.ws + p.qimg_off + (static_cast<size_t>(m) * kPairRows + rank * kPfRows + qrow) * kQImgRowBytes);
-            auto load_q = [&](int h, uint32_t (&qv)[32]) {
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const uint4 x = __ldcg(qsrc + h * 16 + hw * 8 + k);
-                    qv[4 * k] = x.x;
-                    qv[4 * k + 1] = x.y;
-                    qv[4 * k + 2] = x.z;
-                    qv[4 * k + 3] = x.w;
+            if (warp == kProdWarp0) {
+                // ---- Q: the item's prepared 64 KB image by one bulk copy, once the previous
+                // item's S MMAs (its readers) are complete ----
+                if (iter > 0 && !pwait(&ctl->q_free, (iter - 1) & 1)) break;
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&ctl->q_load, static_cast<uint32_t>(kQImgBytes));
+                    bulk_g2s(base + kQOff, p.ws + p.qimg_off + (static_cast<size_t>(m) * 2 + rank) * kQImgBytes,
+                             static_cast<uint32_t>(kQImgBytes), &ctl->q_load);
                 }
-            };
-            uint32_t qv[32];
-            load_q(0, qv);
-            // the previous item's S MMAs (the readers of Q) are complete; its PVs and
-            // softmax may still run
-            if (iter > 0 && !pwait(&ctl->q_free, (iter - 1) & 1)) break;
-            tc::st32(tmem + (static_cast<uint32_t>(32 * sp) << 16) + kQCol + hw * 32, qv);
-            load_q(1, qv);
-            tc::st32(tmem + (static_cast<uint32_t>(32 * sp) << 16) + kQCol + 64 + hw * 32, qv);
-            tc::wait_st();
+                if (!pwait(&ctl->q_load, iter & 1)) break;
+                if (lane == 0) mbar_arrive_remote(lead(&ctl->q_full));
+            }
             RawTile cur;
-            load_raw(kt0, kvh, cur);  // (after Q: both at once exceed the 128 registers)
+            load_raw(kt0, kvh, cur);
             bool ok = true;
-            if (!ok) break;
-            tc::fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_remote(lead(&ctl->q_full));
             // ---- K / V tiles: the raw q4_0 of tile kt+1 is loaded while tile kt is converted ----
             for (int kt = kt0; kt < kt1; ++kt, ++j) {
-                const int s = j % kNStage;
+                const int b = j & 1;
                 RawTile nxt;
                 if (kt + 1 < kt1) load_raw(kt + 1, kvh, nxt);
                 const int64_t key0 = static_cast<int64_t>(kt) * kPfKeys;
-                if (j >= kNStage && !pwait(&ctl->pv_done[s], stage_parity(j - kNStage))) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t kst = base_s + kStageOff + s * kStageBytes;
-                const uint32_t vst = kst + kVInStage;
-                // K: key row k_row (group k_gi); blocks 4*(i&1) + w -> region (i&1)*2 + (c>>1),
-                // chunks (c&1)*4 + w.  Lanes c and c+2 write the same chunks of different
-                // regions (same banks): they take the w in the order w ^ 2.
-                {
-                    const bool live = key0 + k_gi * 16 + k_g + 8 * (k_i >> 1) < n_kv;
-                    const uint32_t w4[4] = {cur.kn.x, cur.kn.y, cur.kn.z, cur.kn.w};
-                    const uint32_t d4[2] = {cur.ks.x, cur.ks.y};
-                    const uint32_t rb = kst + ((k_i & 1) * 2 + (k_c >> 1)) * kKRegion;
-                    uint4 outv[4];
+                // K buffer b: free once S(j - 2) is complete
+                if (j >= 2 && !pwait(&ctl->s_full[b], ring_parity(j - 2))) { ok = false; break; }
+                const uint32_t kst = base_s + kKOff + b * kKBuf;
 #pragma unroll
-                    for (int w = 0; w < 4; ++w) {
-                        outv[w] = make_uint4(0u, 0u, 0u, 0u);
-                        if (live) {
-                            const __half2 dd = u32_as_h2(d4[w >> 1]);
-                            const __half d1 = (w & 1) ? __high2half(dd) : __low2half(dd);
-                            const __half2 d2 = __half2half2(d1);
-                            const uint32_t lo = w4[w] & 0x0F0F0F0Fu;
-                            const uint32_t hi = (w4[w] >> 4) & 0x0F0F0F0Fu;
-                            outv[w] = make_uint4(nib_pair(lo, 0x4140u, d2), nib_pair(lo, 0x4342u, d2),
-                                                 nib_pair(hi, 0x4140u, d2), nib_pair(hi, 0x4342u, d2));
-                        }
-                    }
-                    const bool rot = (k_c & 2) != 0;
+                for (int u = 0; u < 2; ++u) {
+                    // key row gl*16 + g + 8*(i>>1) of this CTA's 64; blocks 4*(i&1) + w ->
+                    // region (i&1)*2 + (c>>1), chunks (c&1)*4 + w.  Lanes c and c+2 write the
+                    // same chunks of different regions (same banks): they take w in the order w ^ 2.
+                    const int job = pt + kProdThreads * u;
+                    const int gl = job >> 7, ch = job & 127;
+                    const int i = ch >> 5, g = (ch >> 2) & 7, c = ch & 3;
+                    const int row = gl * 16 + g + 8 * (i >> 1);
+                    const bool live = key0 + 64 * static_cast<int>(rank) + row < n_kv;
+                    // slot s holds word w = s ^ (rot ? 2 : 0) and its scale d[w >> 1]
+                    const bool rot = (c & 2) != 0;
+                    const uint32_t w4[4] = {rot ? cur.kn[u].z : cur.kn[u].x, rot ? cur.kn[u].w : cur.kn[u].y,
+                                            rot ? cur.kn[u].x : cur.kn[u].z, rot ? cur.kn[u].y : cur.kn[u].w};
+                    const uint32_t d4[2] = {rot ? cur.ks[u].y : cur.ks[u].x, rot ? cur.ks[u].x : cur.ks[u].y};
+                    const uint32_t rb = kst + ((i & 1) * 2 + (c >> 1)) * kKRegion;
 #pragma unroll
                     for (int s4 = 0; s4 < 4; ++s4) {
-                        const uint4 o = rot ? outv[s4 ^ 2] : outv[s4];
-                        const int w = rot ? (s4 ^ 2) : s4;
-                        sts128(rb + swz(k_row, (k_c & 1) * 4 + w), o);
+                        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+                        if (live) {
+                            const __half2 dd = u32_as_h2(d4[s4 >> 1]);
+                            const __half d1 = (s4 & 1) ? __high2half(dd) : __low2half(dd);
+                            const __half2 d2 = __half2half2(d1);
+                            const uint32_t lo = w4[s4] & 0x0F0F0F0Fu;
+                            const uint32_t hi = (w4[s4] >> 4) & 0x0F0F0F0Fu;
+                            o = make_uint4(nib_pair(lo, 0x4140u, d2), nib_pair(lo, 0x4342u, d2),
+                                           nib_pair(hi, 0x4140u, d2), nib_pair(hi, 0x4342u, d2));
+                        }
+                        sts128(rb + swz(row, (c & 1) * 4 + (rot ? (s4 ^ 2) : s4)), o);
                     }
                 }
-                // V: tokens {2c, 2c+8, 2c+1, 2c+9} (byte positions 0..3) of group v_gi;
-                // blocks 2i + (w>>1); region v_il, chunk g
-                {
-                    const uint32_t w4[4] = {cur.vn.x, cur.vn.y, cur.vn.z, cur.vn.w};
-                    const uint32_t d4[4] = {cur.vs.x, cur.vs.y, cur.vs.z, cur.vs.w};
-                    const uint32_t rb = vst + v_il * kVRegion;
+                tc::fence_proxy_async_smem();
+                warp_arrive(&ctl->k_full[b]);
+                // V buffer b: free once PV(j - 2) is complete
+                if (j >= 2 && !pwait(&ctl->pv_done[b], ring_parity(j - 2))) { ok = false; break; }
+                const uint32_t vst = base_s + kVOff + b * kVBuf;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    // tokens {2c, 2c+8, 2c+1, 2c+9} (byte positions 0..3) of group gi;
+                    // blocks 2i + (w>>1); block il, chunk g
+                    const int job = pt + kProdThreads * u;
+                    const int gi = job >> 6, rest = job & 63;
+                    const int il = rest >> 5, g = (rest >> 2) & 7, c = rest & 3;
+                    const uint32_t w4[4] = {cur.vn[u].x, cur.vn[u].y, cur.vn[u].z, cur.vn[u].w};
+                    const uint32_t d4[4] = {cur.vs[u].x, cur.vs[u].y, cur.vs[u].z, cur.vs[u].w};
+                    const uint32_t rb = vst + il * kVBlock;
                     // lo/hi nibbles of the 4 tokens, token-interleaved: [l0 h0 l1 h1], [l2 h2 l3 h3]
                     uint32_t xy[4][2];
 #pragma unroll
@@ -737,8 +761,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
                     }
 #pragma unroll
                     for (int pos = 0; pos < 4; ++pos) {
-                        const int tt = (pos & 1) * 8 + 2 * v_c + (pos >> 1);
-                        const int row = v_gi * 16 + tt;
+                        const int tt = (pos & 1) * 8 + 2 * c + (pos >> 1);
+                        const int row = gi * 16 + tt;
                         const int jj = (pos >> 1) + 2 * (pos & 1);  // scale slot of this token
                         uint4 outv = make_uint4(0u, 0u, 0u, 0u);
                         if (key0 + row < n_kv) {
@@ -754,12 +778,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
                             }
                             outv = make_uint4(o4[0], o4[1], o4[2], o4[3]);
                         }
-                        sts128(rb + swz(row, v_g), outv);
+                        sts128(rb + swz(row, g), outv);
                     }
                 }
                 tc::fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_remote(lead(&ctl->kv_full[s]));
+                warp_arrive(&ctl->v_full[b]);
                 if (kt + 1 < kt1) cur = nxt;
             }
             if (!ok) break;
