@@ -231,52 +231,61 @@ __device__ __forceinline__ float2 load_pair(const void *src, int64_t i, int dtyp
     return __half22float2(*reinterpret_cast<const __half2 *>(static_cast<const __half *>(src) + i));
 }
 
-// Grid (query tokens padded to whole M-tiles, 8): block (t, b) writes the rows of
-// heads 2b, 2b+1 of token t, one f16 pair per thread: RoPE (the table of rope_cos_sin
-// for the position, as ggml builds its cache), f16, contraction permutation; pair w of
-// a row holds positions 2w, 2w+1, which are the adjacent head dimensions
-// k_real_dim(2w), k_real_dim(2w) + 1.  Rows of padding tokens are zero.  Q rows must
-// be aligned to two elements (the host checks it).
+// One block per query token (padded to whole M-tiles), 8 f16 pairs per thread, all
+// loads issued before the RoPE table is needed: RoPE (the table of rope_cos_sin for the
+// position, as ggml builds its cache), f16, contraction permutation; pair w of a row
+// holds positions 2w, 2w+1, which are the adjacent head dimensions k_real_dim(2w),
+// k_real_dim(2w) + 1.  Rows of padding tokens are zero.  Q rows must be aligned to two
+// elements (the host checks it).
 __global__ void __launch_bounds__(256) pf_qprep_kernel(PfParams p) {
     __shared__ float2 rope_tab[32];
     const int t = blockIdx.x;
     const int half = p.rope_n_rot >> 1;
+    const bool live = t < p.T;
+    float2 x[8], y[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int e = threadIdx.x + 256 * k, head = e >> 7, w = e & 127;
+        const int dim = k_real_dim(2 * w);  // even; dim + 1 is position 2w + 1
+        x[k] = y[k] = make_float2(0.f, 0.f);
+        if (live) {
+            const int64_t rbase = t * p.q_st + head * p.q_sh;
+            x[k] = load_pair(p.q, rbase + dim, p.q_dtype);
+            if (dim < p.rope_n_rot) y[k] = load_pair(p.q, rbase + (dim < half ? dim + half : dim - half), p.q_dtype);
+        }
+    }
     if (threadIdx.x < 32) {
         const int i = threadIdx.x;
-        rope_tab[i] = (i < half && t < p.T) ? rope_cos_sin(*p.q_pos0 + t + p.rope_pos_offset, p.rope_theta_scale, i)
-                                            : make_float2(1.f, 0.f);
-    }
-    const int head = 2 * blockIdx.y + (threadIdx.x >> 7), w = threadIdx.x & 127;
-    const int dim = k_real_dim(2 * w);  // even; dim + 1 is position 2w + 1
-    float2 x = make_float2(0.f, 0.f), y = x;
-    const bool live = t < p.T;
-    const bool rot = dim < p.rope_n_rot;
-    const bool lo = dim < half;
-    if (live) {
-        const int64_t rbase = t * p.q_st + head * p.q_sh;
-        x = load_pair(p.q, rbase + dim, p.q_dtype);
-        if (rot) y = load_pair(p.q, rbase + (lo ? dim + half : dim - half), p.q_dtype);
+        rope_tab[i] = (i < half && live) ? rope_cos_sin(*p.q_pos0 + t + p.rope_pos_offset, p.rope_theta_scale, i)
+                                         : make_float2(1.f, 0.f);
     }
     __syncthreads();
-    uint32_t v = 0u;
-    if (live) {
-        if (rot) {
-            const int i = lo ? dim : dim - half;
-            const float2 c0 = rope_tab[i], c1 = rope_tab[i + 1];
-            x = lo ? make_float2(__fsub_rn(__fmul_rn(x.x, c0.x), __fmul_rn(y.x, c0.y)),
-                                 __fsub_rn(__fmul_rn(x.y, c1.x), __fmul_rn(y.y, c1.y)))
-                   : make_float2(__fadd_rn(__fmul_rn(y.x, c0.y), __fmul_rn(x.x, c0.x)),
-                                 __fadd_rn(__fmul_rn(y.y, c1.y), __fmul_rn(x.y, c1.x)));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int e = threadIdx.x + 256 * k, head = e >> 7, w = e & 127;
+        const int dim = k_real_dim(2 * w);
+        uint32_t v = 0u;
+        if (live) {
+            float2 z = x[k];
+            if (dim < p.rope_n_rot) {
+                const bool lo = dim < half;
+                const int i = lo ? dim : dim - half;
+                const float2 c0 = rope_tab[i], c1 = rope_tab[i + 1];
+                z = lo ? make_float2(__fsub_rn(__fmul_rn(x[k].x, c0.x), __fmul_rn(y[k].x, c0.y)),
+                                     __fsub_rn(__fmul_rn(x[k].y, c1.x), __fmul_rn(y[k].y, c1.y)))
+                       : make_float2(__fadd_rn(__fmul_rn(y[k].x, c0.y), __fmul_rn(x[k].x, c0.x)),
+                                     __fadd_rn(__fmul_rn(y[k].y, c1.y), __fmul_rn(x[k].y, c1.x)));
+            }
+            v = pack_half2(z.x, z.y);
         }
-        v = pack_half2(x.x, x.y);
+        // pair row -> CTA and row; positions 2w, 2w+1 -> region, 16-byte chunk (swizzled)
+        const int m = (t / kPairTok) * 2 + (head >> 3), prr = (t % kPairTok) * 8 + (head & 7);
+        const int cta = prr >> 7, rr = prr & 127;
+        const int el = (2 * w) & 63, chunk = el >> 3;
+        const size_t byte = (static_cast<size_t>(m) * 2 + cta) * kQImgBytes + ((2 * w) >> 6) * kQRegion + rr * 128 +
+                            (((chunk ^ (rr & 7)) & 7) << 4) + (el & 7) * 2;
+        *reinterpret_cast<uint32_t *>(p.ws + p.qimg_off + byte) = v;
     }
-    // pair row -> CTA and row; positions 2w, 2w+1 -> region, 16-byte chunk (swizzled)
-    const int m = (t / kPairTok) * 2 + (head >> 3), prr = (t % kPairTok) * 8 + (head & 7);
-    const int cta = prr >> 7, rr = prr & 127;
-    const int e = (2 * w) & 63, chunk = e >> 3;
-    const size_t byte = (static_cast<size_t>(m) * 2 + cta) * kQImgBytes + ((2 * w) >> 6) * kQRegion + rr * 128 +
-                        (((chunk ^ (rr & 7)) & 7) << 4) + (e & 7) * 2;
-    *reinterpret_cast<uint32_t *>(p.ws + p.qimg_off + byte) = v;
 }
 
 // ---- helpers -----------------------------------------------------------------------
@@ -986,7 +995,7 @@ extern "C" int sqmix_fa_prefill(const sqmix_fa_args *a, sqmix_stream_t stream) {
     pf_setup_kernel<<<1, kMaxMtiles, 0, st>>>(p, n_pairs);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "fa_prefill setup launch");
-    pf_qprep_kernel<<<dim3(p.n_mtiles / 2 * kPairTok, 8), 256, 0, st>>>(p);
+    pf_qprep_kernel<<<p.n_mtiles / 2 * kPairTok, 256, 0, st>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "fa_prefill Q launch");
     fa_prefill_kernel<<<2 * n_pairs, kPfThreads, kSmemBytes, st>>>(p);
