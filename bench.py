@@ -560,7 +560,7 @@ def bench_gdn(steps: int, warmup: int):
 
     def decode_all():
         for l in range(n_layers):
-            sqmix.gated_delta_net(q, k, v, gg, beta, S[l], l2_eps=1e-6, out=out)
+            sqmix.gated_delta_net(q, k, v, gg, beta, S[l], l2_eps=1e-6, out=out, state_ready=True)
 
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -598,7 +598,7 @@ def bench_gdn(steps: int, warmup: int):
 
     def decode_batch():
         for l in range(n_lb):
-            sqmix.gated_delta_net(qb, kb, vb, gb, bb, Sb[l], l2_eps=1e-6, out=ob)
+            sqmix.gated_delta_net(qb, kb, vb, gb, bb, Sb[l], l2_eps=1e-6, out=ob, state_ready=True)
 
     for _ in range(max(warmup, 3)):
         decode_batch()
@@ -768,7 +768,9 @@ def bench_stack(steps: int, warmup: int, splits_per_seq: int = 0):
                                               splits_per_seq=splits_per_seq)
                 fa += 1
             else:
-                sqmix.gated_delta_net(gq[gd], gk[gd], gv[gd], gg[gd], gb[gd], S[gd], l2_eps=1e-6, out=go[gd])
+                # the kernel before writes another layer's state or the KV cache, never S[gd]
+                sqmix.gated_delta_net(gq[gd], gk[gd], gv[gd], gg[gd], gb[gd], S[gd], l2_eps=1e-6, out=go[gd],
+                                      state_ready=True)
                 gd += 1
 
     s = torch.cuda.Stream()

@@ -340,7 +340,16 @@ typedef struct sqmix_gdn_args {
     int32_t n_snap;           /* 1 <= n_snap <= min(T, n_planes) */
     float l2_eps;             /* > 0: L2-normalise q and k per head first (gdn.rs:126-142) */
     float *out;               /* [n_seqs][T][H_v][128] f32 */
+    int32_t flags;            /* SQMIX_GDN_* bits (0 = none) */
 } sqmix_gdn_args;
+
+/* sqmix_gdn_decode: the kernel launched immediately before this call on the stream
+ * writes neither the state planes nor sel (in a decode step that kernel is the conv
+ * front end, sqmix_gdn_conv).  The recurrence then reads its input state before that
+ * kernel has finished (programmatic dependent launch), hiding the state load behind
+ * it.  Do not set it right after sqmix_gdn_state_copy into these planes.  Ignored by
+ * sqmix_gdn_prefill. */
+#define SQMIX_GDN_STATE_READY 1
 
 int sqmix_gdn_decode(const sqmix_gdn_args *args, sqmix_stream_t stream);
 

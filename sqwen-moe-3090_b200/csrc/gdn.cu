@@ -38,6 +38,7 @@ struct GdnParams {
     int plane0;   // input plane when sel is NULL
     int T_all;    // tokens per sequence in g, beta and out
     int64_t tok0; // first token of this launch within the sequence
+    int state_ready;  // read the input state before waiting on the preceding kernel
 };
 
 __device__ __forceinline__ float4 load4(const void *p, int64_t i, int dtype) {
@@ -85,9 +86,10 @@ __global__ void __launch_bounds__(256) gdn_recurrent_kernel(GdnParams p) {
     if (seq >= p.n_seqs) return;
     const int hk = h % p.h_k;
     // launched with programmatic stream serialisation: the launch overlaps the tail of
-    // the kernel before it; everything below may depend on that kernel's results
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" :::);
+    // the kernel before it, whose results everything after griddepcontrol.wait may
+    // use; with state_ready the caller guarantees that kernel writes neither the state
+    // nor sel, so the state is read before the wait
+    if (!p.state_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
 
     int plane = p.sel ? p.sel[seq] : p.plane0;
     plane = min(max(plane, 0), p.n_planes - 1);
@@ -98,6 +100,8 @@ __global__ void __launch_bounds__(256) gdn_recurrent_kernel(GdnParams p) {
 #pragma unroll
     for (int c = 0; c < JW; ++c)
         S[c] = *reinterpret_cast<const float4 *>(st_seq + plane * plane_elems + col_off + c * 128);
+    if (p.state_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
 
     const float inv_sqrt_d = 1.0f / sqrtf(128.0f);
     for (int t = 0; t < p.T; ++t) {
@@ -170,8 +174,9 @@ __global__ void copy_f32x4_kernel(float4 *dst, const float4 *src, int64_t n4) {
 
 namespace sqmix {
 int gdn_launch_recurrent(const sqmix_gdn_args *a, int plane_in, int64_t tok_off, int n_tok, int n_snap,
-                         cudaStream_t st) {
+                         bool state_ready, cudaStream_t st) {
     GdnParams p;
+    p.state_ready = state_ready ? 1 : 0;
     p.q = a->q;
     p.k = a->k;
     p.v = a->v;
@@ -248,7 +253,9 @@ extern "C" int sqmix_gdn_decode(const sqmix_gdn_args *a, sqmix_stream_t stream) 
         SQMIX_CHECK_ARG(((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k)) & align) == 0,
                         "gdn_decode: q/k base pointers must be %d-byte aligned", (int)align + 1);
     }
-    return gdn_launch_recurrent(a, -1, 0, a->n_tokens, a->n_snap, reinterpret_cast<cudaStream_t>(stream));
+    SQMIX_CHECK_ARG((a->flags & ~SQMIX_GDN_STATE_READY) == 0, "gdn_decode: unknown flags 0x%x", a->flags);
+    return gdn_launch_recurrent(a, -1, 0, a->n_tokens, a->n_snap, (a->flags & SQMIX_GDN_STATE_READY) != 0,
+                                reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int sqmix_gdn_state_copy(float *dst, const float *src, int64_t plane_elems, int32_t n_planes,

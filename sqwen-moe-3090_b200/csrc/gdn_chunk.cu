@@ -34,6 +34,7 @@ namespace sqmix {
 // gdn.cu: the recurrent kernel over tokens [tok_off, tok_off + n_tok) reading plane
 // plane_in (< 0: the caller's sel / plane 0) and writing n_snap snapshot slots
 int gdn_launch_recurrent(const sqmix_gdn_args *a, int plane_in, int64_t tok_off, int n_tok, int n_snap,
+                         bool state_ready,
                          cudaStream_t st);
 
 namespace {
@@ -808,6 +809,7 @@ extern "C" int sqmix_gdn_prefill(const sqmix_gdn_args *a, void *workspace, size_
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill scan launch");
     if (a->n_snap > 1)
-        return gdn_launch_recurrent(a, a->n_snap - 1, T_chunk, a->n_snap - 1, a->n_snap - 1, st);
+        // the tail reads the plane the scan kernel just wrote: no early state read
+        return gdn_launch_recurrent(a, a->n_snap - 1, T_chunk, a->n_snap - 1, a->n_snap - 1, false, st);
     return SQMIX_OK;
 }

@@ -100,7 +100,7 @@ class GdnArgs(ctypes.Structure):
         ("v_stride_seq", c_int64), ("g", c_void_p), ("beta", c_void_p), ("state", c_void_p),
         ("n_planes", c_int32), ("sel", c_void_p), ("n_seqs", c_int32), ("n_tokens", c_int32),
         ("h_k", c_int32), ("h_v", c_int32), ("n_snap", c_int32), ("l2_eps", c_float),
-        ("out", c_void_p),
+        ("out", c_void_p), ("flags", c_int32),
     ]
 
 

@@ -301,7 +301,8 @@ def gated_delta_net(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.
                     beta: torch.Tensor, state: torch.Tensor, n_planes: int = 1,
                     sel: torch.Tensor | None = None, n_snap: int = 1, l2_eps: float = 0.0,
                     out: torch.Tensor | None = None, chunked: bool | None = None,
-                    workspace: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+                    workspace: torch.Tensor | None = None, state_ready: bool = False,
+                    stream=None) -> torch.Tensor:
     """Gated delta rule over T tokens for n_seqs sequences.
 
     q, k [n_seqs][T][H_k][128]; v [n_seqs][T][H_v][128] (f32/bf16/f16); g, beta
@@ -310,6 +311,8 @@ def gated_delta_net(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.
     3-D q/k/v/g/beta (no sequence dim) are accepted for n_seqs = 1.
     chunked: None picks the chunked prefill kernels (sqmix_gdn_prefill) for
     T >= GDN_CHUNK_MIN_T and the recurrent kernel (sqmix_gdn_decode) below.
+    state_ready: the kernel launched just before on the stream writes neither the state
+    nor sel (SQMIX_GDN_STATE_READY: the recurrent kernel reads the state early).
     """
     _require_cuda(q, k, v, g, beta, state, sel)
     if q.dim() == 3:
@@ -330,7 +333,7 @@ def gated_delta_net(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.
         q=_ptr(q), k=_ptr(k), v=_ptr(v), dtype=_dt(q), qk_stride_tok=q.stride(1), v_stride_tok=v.stride(1),
         qk_stride_seq=q.stride(0), v_stride_seq=v.stride(0), g=_ptr(g), beta=_ptr(beta),
         state=_ptr(state), n_planes=int(n_planes), sel=_ptr(sel), n_seqs=n_seqs, n_tokens=T, h_k=H_k,
-        h_v=H_v, n_snap=int(n_snap), l2_eps=float(l2_eps), out=_ptr(out))
+        h_v=H_v, n_snap=int(n_snap), l2_eps=float(l2_eps), out=_ptr(out), flags=1 if state_ready else 0)
     if chunked is None:
         chunked = T >= GDN_CHUNK_MIN_T
     if chunked:

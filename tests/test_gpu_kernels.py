@@ -443,6 +443,36 @@ def test_gdn_snapshots_sel_and_batch(sq, oracle):
         assert rel_err(st_np[s, 1], snaps[1]) <= GDN_TOL
 
 
+def test_gdn_state_ready_chain_after_conv(sq, oracle):
+    """SQMIX_GDN_STATE_READY: the recurrence reads its state before the preceding kernel
+    (here the conv front end, then another layer's recurrence) finishes; results equal
+    the oracle for each layer of the chain, twice in a row (CUDA-graph-like reuse)."""
+    rng = np.random.default_rng(53)
+    n_layers, T = 4, 2
+    cases = [gdn_case(rng, 1, T, n_planes=2) for _ in range(n_layers)]
+    sel = torch.tensor([1], dtype=torch.int32, device="cuda")
+    C, K = 8192, 4
+    x = torch.from_numpy(rng.standard_normal((1, T, C)).astype(np.float32)).cuda()
+    w = torch.from_numpy((rng.standard_normal((C, K)) * 0.5).astype(np.float32)).cuda()
+    hist = torch.zeros((1, 1, C, K - 1), device="cuda")
+    for rep in range(2):
+        states = [torch.from_numpy(c[5]).cuda() for c in cases]
+        dev_in = [[torch.from_numpy(a).cuda() for a in c[:5]] for c in cases]
+        outs = []
+        for l in range(n_layers):
+            if l % 2 == 0:  # the conv front end (never touches the recurrent state) runs just before
+                sq.gdn_conv(x, w, hist, n_qk_channels=4096, l2_eps=1e-6)
+            outs.append(sq.gated_delta_net(*dev_in[l], states[l], n_planes=2, sel=sel, n_snap=2,
+                                           state_ready=True))
+        torch.cuda.synchronize()
+        for l, (q, k, v, g, beta, S) in enumerate(cases):
+            want, snaps = oracle.gdn(q[0], k[0], v[0], g[0], beta[0], S[0, 1], n_snap=2)
+            assert rel_err(outs[l].cpu().numpy()[0], want) <= GDN_TOL, (rep, l)
+            st_np = states[l].cpu().numpy()
+            assert rel_err(st_np[0, 0], snaps[0]) <= GDN_TOL
+            assert rel_err(st_np[0, 1], snaps[1]) <= GDN_TOL
+
+
 def test_gdn_fused_l2norm(sq, oracle):
     rng = np.random.default_rng(52)
     q, k, v, g, beta, S = gdn_case(rng, 1, 3)
