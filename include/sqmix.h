@@ -468,11 +468,19 @@ const int64_t *sqmix_kvcache_device_step(const sqmix_kvcache *kv);
 int sqmix_kvcache_upload_step(sqmix_kvcache *kv, sqmix_stream_t stream);
 int32_t sqmix_kvcache_max_step_tokens(const sqmix_kvcache *kv);
 
-/* GdnState (gdn.rs:71-120) for n_layers GDN layers: 1 + n_rs planes per layer. */
+/* GdnState (gdn.rs:71-120) for n_layers GDN layers: 1 + n_rs planes per layer of the
+ * recurrent state ([h_v][128][128] f32) and, when conv_channels > 0, of the short-conv
+ * history ([conv_channels][d_conv - 1] f32, taps fastest: the conv_state tensor
+ * [d_conv - 1, conv_channels, 1 + n_rs] of gdn.rs:76-104 and the state layout of
+ * sqmix_gdn_conv).  sqmix_gdnstate_create has no conv history. */
 typedef struct sqmix_gdnstate sqmix_gdnstate;
 
 int sqmix_gdnstate_create(int32_t n_layers, int32_t h_v, int32_t n_rs, int32_t device,
                           sqmix_gdnstate **out);
+int sqmix_gdnstate_create_conv(int32_t n_layers, int32_t h_v, int32_t n_rs, int32_t conv_channels,
+                               int32_t d_conv, int32_t device, sqmix_gdnstate **out);
+/* conv history planes of a layer (NULL without conv history) */
+float *sqmix_gdnstate_conv_planes(sqmix_gdnstate *st, int32_t layer);
 void sqmix_gdnstate_destroy(sqmix_gdnstate *st);
 int sqmix_gdnstate_zero(sqmix_gdnstate *st, sqmix_stream_t stream);   /* graph.rs:206-222 */
 float *sqmix_gdnstate_planes(sqmix_gdnstate *st, int32_t layer);
@@ -483,8 +491,11 @@ int32_t sqmix_gdnstate_set_sel(sqmix_gdnstate *st, int32_t sel);
 int32_t sqmix_gdnstate_sel(const sqmix_gdnstate *st);
 const int32_t *sqmix_gdnstate_device_sel(const sqmix_gdnstate *st);
 int sqmix_gdnstate_upload_sel(sqmix_gdnstate *st, sqmix_stream_t stream);
-/* Checkpoint of plane 0 of every layer: u64 little-endian payload length, then
- * the raw f32 planes (graph.rs:316-350).  snapshot: D2H + stream sync. */
+/* Checkpoint of plane 0 of every layer in the byte layout of snapshot_gdn /
+ * restore_gdn (graph.rs:301-350), which prompt-cache checkpoints store
+ * (prompt_cache.rs:38-48): a u64 little-endian payload length, then per layer the raw
+ * f32 state plane 0 followed by the conv history plane 0 (absent without conv
+ * history).  snapshot: D2H + stream sync; restore rejects a length mismatch. */
 size_t sqmix_gdnstate_snapshot_bytes(const sqmix_gdnstate *st);
 int sqmix_gdnstate_snapshot(sqmix_gdnstate *st, void *host_buf, size_t bytes, sqmix_stream_t stream);
 int sqmix_gdnstate_restore(sqmix_gdnstate *st, const void *host_buf, size_t bytes,

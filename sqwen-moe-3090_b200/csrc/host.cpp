@@ -247,15 +247,23 @@ struct sqmix_gdnstate {
     int32_t h_v = 0;
     int32_t n_rs = 0;
     int32_t sel = 0;
+    int32_t conv_channels = 0;  // 0: no conv history
+    int32_t d_conv = 0;
     std::vector<float *> planes;
+    std::vector<float *> conv_planes;
     int32_t *d_sel = nullptr;
     size_t plane_elems() const { return static_cast<size_t>(h_v) * SQMIX_GDN_D * SQMIX_GDN_D; }
+    size_t conv_plane_elems() const {
+        return conv_channels > 0 ? static_cast<size_t>(conv_channels) * (d_conv - 1) : 0;
+    }
 };
 
-extern "C" int sqmix_gdnstate_create(int32_t n_layers, int32_t h_v, int32_t n_rs, int32_t device,
-                                     sqmix_gdnstate **out) {
-    if (!out || n_layers <= 0 || h_v <= 0 || n_rs < 0) {
-        set_error("gdnstate_create: n_layers=%d h_v=%d n_rs=%d", n_layers, h_v, n_rs);
+extern "C" int sqmix_gdnstate_create_conv(int32_t n_layers, int32_t h_v, int32_t n_rs, int32_t conv_channels,
+                                          int32_t d_conv, int32_t device, sqmix_gdnstate **out) {
+    if (!out || n_layers <= 0 || h_v <= 0 || n_rs < 0 || conv_channels < 0 ||
+        (conv_channels > 0 && d_conv < 2)) {
+        set_error("gdnstate_create: n_layers=%d h_v=%d n_rs=%d conv_channels=%d d_conv=%d", n_layers, h_v, n_rs,
+                  conv_channels, d_conv);
         return SQMIX_EINVAL;
     }
     *out = nullptr;
@@ -264,18 +272,27 @@ extern "C" int sqmix_gdnstate_create(int32_t n_layers, int32_t h_v, int32_t n_rs
     st->n_layers = n_layers;
     st->h_v = h_v;
     st->n_rs = n_rs;
+    st->conv_channels = conv_channels;
+    st->d_conv = conv_channels > 0 ? d_conv : 0;
     if (device < 0) {  // bookkeeping only
         *out = st;
         return SQMIX_OK;
     }
     DeviceGuard guard(device);
     const size_t bytes = st->plane_elems() * sizeof(float) * (1 + n_rs);
+    const size_t conv_bytes = st->conv_plane_elems() * sizeof(float) * (1 + n_rs);
     int rc = SQMIX_OK;
     for (int32_t l = 0; l < n_layers && rc == SQMIX_OK; ++l) {
         float *p = nullptr;
         rc = cuda_status(cudaMalloc(&p, bytes), "gdnstate_create: cudaMalloc");
         if (p) st->planes.push_back(p);
         if (rc == SQMIX_OK) rc = cuda_status(cudaMemset(p, 0, bytes), "gdnstate_create: memset");
+        if (rc == SQMIX_OK && conv_bytes > 0) {
+            float *c = nullptr;
+            rc = cuda_status(cudaMalloc(&c, conv_bytes), "gdnstate_create: cudaMalloc (conv)");
+            if (c) st->conv_planes.push_back(c);
+            if (rc == SQMIX_OK) rc = cuda_status(cudaMemset(c, 0, conv_bytes), "gdnstate_create: memset (conv)");
+        }
     }
     if (rc == SQMIX_OK) rc = cuda_status(cudaMalloc(&st->d_sel, sizeof(int32_t)), "gdnstate_create: sel");
     if (rc == SQMIX_OK) rc = cuda_status(cudaMemset(st->d_sel, 0, sizeof(int32_t)), "gdnstate_create: sel");
@@ -287,6 +304,11 @@ extern "C" int sqmix_gdnstate_create(int32_t n_layers, int32_t h_v, int32_t n_rs
     return SQMIX_OK;
 }
 
+extern "C" int sqmix_gdnstate_create(int32_t n_layers, int32_t h_v, int32_t n_rs, int32_t device,
+                                     sqmix_gdnstate **out) {
+    return sqmix_gdnstate_create_conv(n_layers, h_v, n_rs, 0, 0, device, out);
+}
+
 extern "C" void sqmix_gdnstate_destroy(sqmix_gdnstate *st) {
     if (!st) return;
     if (st->device < 0) {
@@ -295,6 +317,7 @@ extern "C" void sqmix_gdnstate_destroy(sqmix_gdnstate *st) {
     }
     DeviceGuard guard(st->device);
     for (float *p : st->planes) cudaFree(p);
+    for (float *p : st->conv_planes) cudaFree(p);
     if (st->d_sel) cudaFree(st->d_sel);
     delete st;
 }
@@ -309,11 +332,21 @@ extern "C" int sqmix_gdnstate_zero(sqmix_gdnstate *st, sqmix_stream_t stream) {
                              "gdnstate_zero");
         if (rc != SQMIX_OK) return rc;
     }
+    const size_t conv_bytes = st->conv_plane_elems() * sizeof(float) * (1 + st->n_rs);
+    for (float *p : st->conv_planes) {
+        int rc = cuda_status(cudaMemsetAsync(p, 0, conv_bytes, reinterpret_cast<cudaStream_t>(stream)),
+                             "gdnstate_zero (conv)");
+        if (rc != SQMIX_OK) return rc;
+    }
     return SQMIX_OK;
 }
 
 extern "C" float *sqmix_gdnstate_planes(sqmix_gdnstate *st, int32_t layer) {
     return (st && layer >= 0 && layer < st->n_layers) ? st->planes[layer] : nullptr;
+}
+extern "C" float *sqmix_gdnstate_conv_planes(sqmix_gdnstate *st, int32_t layer) {
+    return (st && layer >= 0 && layer < static_cast<int32_t>(st->conv_planes.size())) ? st->conv_planes[layer]
+                                                                                      : nullptr;
 }
 extern "C" int32_t sqmix_gdnstate_n_planes(const sqmix_gdnstate *st) { return st ? 1 + st->n_rs : 0; }
 
@@ -341,7 +374,7 @@ extern "C" int sqmix_gdnstate_upload_sel(sqmix_gdnstate *st, sqmix_stream_t stre
 }
 
 extern "C" size_t sqmix_gdnstate_snapshot_bytes(const sqmix_gdnstate *st) {
-    return st ? 8 + st->plane_elems() * sizeof(float) * st->n_layers : 0;
+    return st ? 8 + (st->plane_elems() + st->conv_plane_elems()) * sizeof(float) * st->n_layers : 0;
 }
 
 extern "C" int sqmix_gdnstate_snapshot(sqmix_gdnstate *st, void *host_buf, size_t bytes,
@@ -360,11 +393,14 @@ extern "C" int sqmix_gdnstate_snapshot(sqmix_gdnstate *st, void *host_buf, size_
     const uint64_t payload = need - 8;
     uint8_t *dst = static_cast<uint8_t *>(host_buf);
     for (int i = 0; i < 8; ++i) dst[i] = static_cast<uint8_t>(payload >> (8 * i));  // little endian
-    const size_t pb = st->plane_elems() * sizeof(float);
+    const size_t pb = st->plane_elems() * sizeof(float), cb = st->conv_plane_elems() * sizeof(float);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     for (int32_t l = 0; l < st->n_layers; ++l) {
-        int rc = cuda_status(cudaMemcpyAsync(dst + 8 + l * pb, st->planes[l], pb, cudaMemcpyDeviceToHost, s),
-                             "gdnstate_snapshot");
+        uint8_t *lay = dst + 8 + l * (pb + cb);
+        int rc = cuda_status(cudaMemcpyAsync(lay, st->planes[l], pb, cudaMemcpyDeviceToHost, s), "gdnstate_snapshot");
+        if (rc == SQMIX_OK && cb > 0)
+            rc = cuda_status(cudaMemcpyAsync(lay + pb, st->conv_planes[l], cb, cudaMemcpyDeviceToHost, s),
+                             "gdnstate_snapshot (conv)");
         if (rc != SQMIX_OK) return rc;
     }
     return cuda_status(cudaStreamSynchronize(s), "gdnstate_snapshot sync");
@@ -388,11 +424,14 @@ extern "C" int sqmix_gdnstate_restore(sqmix_gdnstate *st, const void *host_buf, 
     }
     if (st->device < 0) return SQMIX_OK;  // header validated; nothing to write
     DeviceGuard guard(st->device);
-    const size_t pb = st->plane_elems() * sizeof(float);
+    const size_t pb = st->plane_elems() * sizeof(float), cb = st->conv_plane_elems() * sizeof(float);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     for (int32_t l = 0; l < st->n_layers; ++l) {
-        int rc = cuda_status(cudaMemcpyAsync(st->planes[l], src + 8 + l * pb, pb, cudaMemcpyHostToDevice, s),
-                             "gdnstate_restore");
+        const uint8_t *lay = src + 8 + l * (pb + cb);
+        int rc = cuda_status(cudaMemcpyAsync(st->planes[l], lay, pb, cudaMemcpyHostToDevice, s), "gdnstate_restore");
+        if (rc == SQMIX_OK && cb > 0)
+            rc = cuda_status(cudaMemcpyAsync(st->conv_planes[l], lay + pb, cb, cudaMemcpyHostToDevice, s),
+                             "gdnstate_restore (conv)");
         if (rc != SQMIX_OK) return rc;
     }
     return cuda_status(cudaStreamSynchronize(s), "gdnstate_restore sync");

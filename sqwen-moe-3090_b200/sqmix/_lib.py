@@ -173,6 +173,9 @@ _SIGNATURES = {
     "sqmix_kvcache_upload_step": (ctypes.c_int, [c_void_p, c_void_p]),
     "sqmix_kvcache_max_step_tokens": (c_int32, [c_void_p]),
     "sqmix_gdnstate_create": (ctypes.c_int, [c_int32, c_int32, c_int32, c_int32, ctypes.POINTER(c_void_p)]),
+    "sqmix_gdnstate_create_conv": (ctypes.c_int, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                                  ctypes.POINTER(c_void_p)]),
+    "sqmix_gdnstate_conv_planes": (c_void_p, [c_void_p, c_int32]),
     "sqmix_gdnstate_destroy": (None, [c_void_p]),
     "sqmix_gdnstate_zero": (ctypes.c_int, [c_void_p, c_void_p]),
     "sqmix_gdnstate_planes": (c_void_p, [c_void_p, c_int32]),

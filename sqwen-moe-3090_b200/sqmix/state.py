@@ -159,15 +159,20 @@ class KvCache:
 
 
 class GdnState:
-    """Recurrent GDN state with 1 + n_rs snapshot planes per layer."""
+    """Recurrent GDN state with 1 + n_rs snapshot planes per layer, and (conv_channels >
+    0) the short-conv history planes [1 + n_rs][conv_channels][d_conv - 1] that
+    sqmix_gdn_conv reads and writes; snapshots hold plane 0 of both per layer."""
 
-    def __init__(self, n_layers: int, h_v: int = 32, n_rs: int = 0, device: int | None = None):
+    def __init__(self, n_layers: int, h_v: int = 32, n_rs: int = 0, device: int | None = None,
+                 conv_channels: int = 0, d_conv: int = 4):
         if device is None:
             device = torch.cuda.current_device()
         self.device = int(device)
         h = ctypes.c_void_p()
-        check(lib().sqmix_gdnstate_create(int(n_layers), int(h_v), int(n_rs), self.device,
-                                          ctypes.byref(h)), "GdnState")
+        check(lib().sqmix_gdnstate_create_conv(int(n_layers), int(h_v), int(n_rs), int(conv_channels), int(d_conv),
+                                               self.device, ctypes.byref(h)), "GdnState")
+        self.conv_channels = int(conv_channels)
+        self.d_conv = int(d_conv) if conv_channels > 0 else 0
         self._h = h
         self.n_layers = int(n_layers)
         self.h_v = int(h_v)
@@ -179,6 +184,11 @@ class GdnState:
                            self.device).view(self.n_planes, self.h_v, ops.GDN_D, ops.GDN_D)
             for i in range(n_layers)]
         self._sel = _device_tensor(lib().sqmix_gdnstate_device_sel(h), 4, torch.int32, self.device)
+        conv_plane = self.conv_channels * (self.d_conv - 1) if self.conv_channels else 0
+        self._conv = [
+            _device_tensor(lib().sqmix_gdnstate_conv_planes(h, i), 4 * conv_plane * self.n_planes, torch.float32,
+                           self.device).view(self.n_planes, self.conv_channels, self.d_conv - 1)
+            for i in range(n_layers)] if conv_plane else []
 
     def close(self):
         if getattr(self, "_h", None):
@@ -193,6 +203,12 @@ class GdnState:
 
     def planes(self, layer: int) -> torch.Tensor:
         return self._planes[layer]
+
+    def conv_planes(self, layer: int) -> torch.Tensor:
+        """[1 + n_rs][conv_channels][d_conv - 1] f32 (the `state` argument of gdn_conv)."""
+        if not self._conv:
+            raise ValueError("this GdnState has no conv history (conv_channels = 0)")
+        return self._conv[layer]
 
     def zero_states(self, stream=None) -> None:
         check(lib().sqmix_gdnstate_zero(self._h, ops._stream(stream)), "GdnState.zero_states")

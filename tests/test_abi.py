@@ -148,7 +148,7 @@ def test_gdnstate_selector_and_snapshot_header(sqmix_lib):
         assert L.sqmix_gdnstate_sel(h) == 0
         plane = 32 * 128 * 128 * 4
         n = L.sqmix_gdnstate_snapshot_bytes(h)
-        assert n == 8 + 30 * plane  # ~63 MiB with conv state in the reference; planes only here
+        assert n == 8 + 30 * plane  # no conv history: state planes only
         good = struct.pack("<Q", n - 8) + bytes(n - 8)
         assert L.sqmix_gdnstate_restore(h, good, len(good), None) == 0
         bad_len = struct.pack("<Q", n - 8) + bytes(n - 9)
@@ -159,6 +159,27 @@ def test_gdnstate_selector_and_snapshot_header(sqmix_lib):
         assert L.sqmix_gdnstate_restore(h, b"1234", 4, None) == sqmix_lib.SQMIX_EINVAL
     finally:
         L.sqmix_gdnstate_destroy(h)
+
+
+def test_gdnstate_checkpoint_size_with_conv_history(sqmix_lib):
+    # the reference's checkpoint of the 30 GDN layers (graph.rs:301-350): per layer the
+    # 2 MiB state plane + the 8192 x 3 conv plane, about 63 MiB, behind a u64 header
+    L = sqmix_lib.lib()
+    h = ctypes.c_void_p()
+    assert L.sqmix_gdnstate_create_conv(30, 32, 1, 8192, 4, -1, ctypes.byref(h)) == 0
+    try:
+        n = L.sqmix_gdnstate_snapshot_bytes(h)
+        assert n == 8 + 30 * (32 * 128 * 128 + 8192 * 3) * 4
+        assert 62 * 2**20 < n < 64 * 2**20
+        good = struct.pack("<Q", n - 8) + bytes(n - 8)
+        assert L.sqmix_gdnstate_restore(h, good, len(good), None) == 0
+        no_conv = 8 + 30 * 32 * 128 * 128 * 4
+        short = struct.pack("<Q", no_conv - 8) + bytes(no_conv - 8)
+        assert L.sqmix_gdnstate_restore(h, short, len(short), None) == sqmix_lib.SQMIX_EINVAL
+    finally:
+        L.sqmix_gdnstate_destroy(h)
+    for bad in ((30, 32, 1, -1, 4), (30, 32, 1, 8192, 1)):
+        assert L.sqmix_gdnstate_create_conv(*bad, -1, ctypes.byref(h)) == sqmix_lib.SQMIX_EINVAL
 
 
 def test_kvcache_rejects_bad_shapes(sqmix_lib):

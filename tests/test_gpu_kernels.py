@@ -560,6 +560,47 @@ def test_gdnstate_snapshot_restore_roundtrip(sq):
     st.close()
 
 
+def test_gdnstate_checkpoint_layout_with_conv_history(sq, oracle):
+    """Checkpoint bytes as the reference lays them out (graph.rs:316-323): u64 length,
+    then per layer state plane 0 ++ conv plane 0; the conv planes are the ones
+    gdn_conv updates, and restore brings both back."""
+    C, K, n_layers = 8192, 4, 2
+    st = sq.GdnState(n_layers=n_layers, h_v=32, n_rs=1, conv_channels=C, d_conv=K)
+    rng = np.random.default_rng(54)
+    x = torch.from_numpy(rng.standard_normal((1, 3, C)).astype(np.float32)).cuda()
+    w = torch.from_numpy((rng.standard_normal((C, K)) * 0.5).astype(np.float32)).cuda()
+    for l in range(n_layers):
+        st.planes(l).copy_(torch.randn_like(st.planes(l)))
+        cp = st.conv_planes(l)
+        assert cp.shape == (2, C, K - 1)
+        cp.copy_(torch.randn_like(cp))
+        # the conv front end reads plane 0 and rewrites it (n_snap 1) in place
+        want_hist = cp[0].cpu().numpy().copy()
+        sq.gdn_conv(x, w, cp[None], n_planes=2, n_qk_channels=4096, l2_eps=1e-6)
+        torch.cuda.synchronize()
+        _, want_st = oracle.gdn_conv(x.cpu().numpy()[0], w.cpu().numpy(), np.stack([want_hist, cp[1].cpu().numpy()]),
+                                     n_qk=4096, d=128, eps=1e-6)
+        assert np.array_equal(cp.cpu().numpy(), want_st)
+    blob = st.snapshot_gdn()
+    pb, cb = 32 * 128 * 128 * 4, C * (K - 1) * 4
+    assert len(blob) == 8 + n_layers * (pb + cb)
+    assert int.from_bytes(blob[:8], "little") == len(blob) - 8
+    saved = []
+    for l in range(n_layers):
+        off = 8 + l * (pb + cb)
+        assert blob[off:off + pb] == st.planes(l)[0].cpu().numpy().tobytes()
+        assert blob[off + pb:off + pb + cb] == st.conv_planes(l)[0].cpu().numpy().tobytes()
+        saved.append((st.planes(l)[0].clone(), st.conv_planes(l)[0].clone()))
+    st.zero_states()
+    st.restore_gdn(blob)
+    torch.cuda.synchronize()
+    for l in range(n_layers):
+        assert torch.equal(st.planes(l)[0], saved[l][0])
+        assert torch.equal(st.conv_planes(l)[0], saved[l][1])
+        assert not st.conv_planes(l)[1].any()  # only plane 0 is checkpointed
+    st.close()
+
+
 # ------------------------------------------------- fused append + attention ---
 
 @pytest.mark.parametrize("n_q,n_kv", [(1, 4096), (2, 1000), (2, 17), (1, 1), (2, 2)])
