@@ -196,8 +196,9 @@ int sqmix_fa_status(void *workspace, sqmix_stream_t stream);
  * the cache (sqmix_kv_append_q4_0; n_new must be 0).  n_splits = number of persistent
  * CTAs, run as CTA pairs (rounded down to even, at least one pair; 0 = as many pairs as
  * are resident at once); config and flags are ignored.  q must be aligned to two
- * elements with even strides.  Launches a setup, a Q-preparation, a main and a merge
- * kernel.  The workspace (sqmix_fa_prefill_workspace_bytes, 256-byte aligned)
+ * elements with even strides.  Launches a preparation kernel (item table and Q), the
+ * main kernel and a merge kernel, the last two as programmatic dependents of the one
+ * before.  The workspace (sqmix_fa_prefill_workspace_bytes, 256-byte aligned)
  * needs no initialisation; its first word holds device status bits as for decode
  * (read with sqmix_fa_status). */
 size_t sqmix_fa_prefill_workspace_bytes(int32_t n_q, int32_t n_ctas);

@@ -16,9 +16,10 @@
 // pair of the persistent grid (one pair per two SMs); a segment is one to a few items
 // (the part of one M-tile inside the segment).  Each item leaves (m, l, O) partials per
 // row; fa_prefill_merge_kernel combines the items of an M-tile, applies the gate and
-// writes the output.  pf_setup_kernel builds the item table from the device scalars
-// n_kv and q_pos0 (CUDA-graph friendly);
-// pf_qprep_kernel writes Q once per call in the operand layout.
+// writes the output.  pf_prep_kernel builds the item table from the device scalars
+// n_kv and q_pos0 (CUDA-graph friendly) and writes Q once per call in the operand
+// layout; the main and merge kernels are its programmatic dependents (each waits for
+// its predecessor with griddepcontrol.wait after a prologue that overlaps it).
 //
 // One CTA (13 warps):
 //   warp 0      TMEM allocation (pair form, both CTAs); in the even CTA lane 0 issues
@@ -33,7 +34,7 @@
 //               column) over the S buffer it has just read in tensor memory,
 //               and at the end of an item reads O and writes the partials;
 //   warps 5-12  producers: copy the item's Q rows (prepared once per call by
-//               pf_qprep_kernel: RoPE, f16, contraction order) into tensor memory, and
+//               pf_prep_kernel: RoPE, f16, contraction order) into tensor memory, and
 //               dequantise this CTA's half of the K and V tiles from q4_0 into
 //               128-byte-swizzled shared memory (six stages; the raw q4_0 of the next
 //               tile is loaded while the current one is converted).
@@ -164,7 +165,7 @@ __device__ __forceinline__ void block_scan_excl(int *buf, int m, int v, int &exc
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(kMaxMtiles) pf_setup_kernel(PfParams p, int n_pairs) {
+__device__ void pf_setup_block(const PfParams &p, int n_pairs) {
     __shared__ int scan[kMaxMtiles];
     const int m = threadIdx.x;
     const int64_t n_kv = clamp_nkv(p, p.ws, m == 0);
@@ -237,15 +238,13 @@ __device__ __forceinline__ float2 load_pair(const void *src, int64_t i, int dtyp
 // holds positions 2w, 2w+1, which are the adjacent head dimensions k_real_dim(2w),
 // k_real_dim(2w) + 1.  Rows of padding tokens are zero.  Q rows must be aligned to two
 // elements (the host checks it).
-__global__ void __launch_bounds__(256) pf_qprep_kernel(PfParams p) {
-    __shared__ float2 rope_tab[32];
-    const int t = blockIdx.x;
+__device__ void pf_qprep_token(const PfParams &p, int t, int tid, float2 *rope_tab) {
     const int half = p.rope_n_rot >> 1;
     const bool live = t < p.T;
     float2 x[8], y[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        const int e = threadIdx.x + 256 * k, head = e >> 7, w = e & 127;
+        const int e = tid + 256 * k, head = e >> 7, w = e & 127;
         const int dim = k_real_dim(2 * w);  // even; dim + 1 is position 2w + 1
         x[k] = y[k] = make_float2(0.f, 0.f);
         if (live) {
@@ -254,15 +253,15 @@ __global__ void __launch_bounds__(256) pf_qprep_kernel(PfParams p) {
             if (dim < p.rope_n_rot) y[k] = load_pair(p.q, rbase + (dim < half ? dim + half : dim - half), p.q_dtype);
         }
     }
-    if (threadIdx.x < 32) {
-        const int i = threadIdx.x;
+    if (tid < 32) {
+        const int i = tid;
         rope_tab[i] = (i < half && live) ? rope_cos_sin(*p.q_pos0 + t + p.rope_pos_offset, p.rope_theta_scale, i)
                                          : make_float2(1.f, 0.f);
     }
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        const int e = threadIdx.x + 256 * k, head = e >> 7, w = e & 127;
+        const int e = tid + 256 * k, head = e >> 7, w = e & 127;
         const int dim = k_real_dim(2 * w);
         uint32_t v = 0u;
         if (live) {
@@ -286,6 +285,21 @@ __global__ void __launch_bounds__(256) pf_qprep_kernel(PfParams p) {
                             (((chunk ^ (rr & 7)) & 7) << 4) + (el & 7) * 2;
         *reinterpret_cast<uint32_t *>(p.ws + p.qimg_off + byte) = v;
     }
+}
+
+// One launch before the main kernel: blocks 0 .. T_pad/2 - 1 prepare Q for two tokens
+// each (256 threads per token), the last block builds the item table.  The main
+// kernel, launched as its programmatic dependent, runs its prologue meanwhile.
+constexpr int kPrepThreads = kMaxMtiles;  // 512
+__global__ void __launch_bounds__(kPrepThreads) pf_prep_kernel(PfParams p, int n_pairs) {
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+    if (blockIdx.x == gridDim.x - 1) {
+        pf_setup_block(p, n_pairs);
+        return;
+    }
+    __shared__ float2 rope_tab[2][32];
+    const int half_id = threadIdx.x >> 8;
+    pf_qprep_token(p, 2 * blockIdx.x + half_id, threadIdx.x & 255, rope_tab[half_id]);
 }
 
 // ---- helpers -----------------------------------------------------------------------
@@ -403,6 +417,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1) fa_pr
     cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
     tc::fence_after();
     const uint32_t tmem = ctl->tmem_base;
+    // launched as the programmatic dependent of pf_prep_kernel: the prologue above
+    // overlapped it; the item table and the Q image are read only after it completes
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
 
     const int64_t n_kv = clamp_nkv(p, p.ws, false);
     const int64_t q_pos0 = *p.q_pos0;
@@ -833,6 +851,8 @@ struct PfMergeParams {
 __global__ void __launch_bounds__(256) fa_prefill_merge_kernel(PfMergeParams p) {
     __shared__ float orow[8][256];
     __shared__ float lse_s[8];
+    // programmatic dependent of the main kernel: its partials are complete after this
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int t = blockIdx.x, kvh = blockIdx.y, i = threadIdx.x;
     const int hq = i & 7, c4a = i >> 3;  // chunks c4a and c4a + 32
     const int m = (t / kPairTok) * 2 + kvh;
@@ -992,15 +1012,23 @@ extern "C" int sqmix_fa_prefill(const sqmix_fa_args *a, sqmix_stream_t stream) {
         size_t ml, o, total;
         pf_ws_layout(n_pairs, p.n_mtiles, &ml, &o, &p.qimg_off, &total);
     }
-    pf_setup_kernel<<<1, kMaxMtiles, 0, st>>>(p, n_pairs);
+    pf_prep_kernel<<<p.n_mtiles / 2 * kPairTok / 2 + 1, kPrepThreads, 0, st>>>(p, n_pairs);
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_status(e, "fa_prefill setup launch");
-    pf_qprep_kernel<<<p.n_mtiles / 2 * kPairTok, 256, 0, st>>>(p);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_status(e, "fa_prefill Q launch");
-    fa_prefill_kernel<<<2 * n_pairs, kPfThreads, kSmemBytes, st>>>(p);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_status(e, "fa_prefill launch");
+    if (e != cudaSuccess) return cuda_status(e, "fa_prefill prep launch");
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * n_pairs);  // clusters of two (compile-time cluster dims)
+        cfg.blockDim = dim3(kPfThreads);
+        cfg.dynamicSmemBytes = kSmemBytes;
+        cfg.stream = st;
+        cfg.attrs = pdl;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, fa_prefill_kernel, p);
+        if (e != cudaSuccess) return cuda_status(e, "fa_prefill launch");
+    }
     PfMergeParams mp;
     mp.ws = p.ws;
     mp.items_max = p.items_max;
@@ -1011,6 +1039,11 @@ extern "C" int sqmix_fa_prefill(const sqmix_fa_args *a, sqmix_stream_t stream) {
     mp.g_sh = a->gate_stride_head;
     mp.out = a->out;
     mp.lse = a->lse;
-    fa_prefill_merge_kernel<<<dim3(a->n_q, 2), 256, 0, st>>>(mp);
-    return cuda_status(cudaGetLastError(), "fa_prefill merge launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a->n_q, 2);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, fa_prefill_merge_kernel, mp), "fa_prefill merge launch");
 }
