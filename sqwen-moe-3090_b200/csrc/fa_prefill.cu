@@ -23,21 +23,22 @@
 //
 // One CTA (13 warps):
 //   warp 0      TMEM allocation (pair form, both CTAs); in the even CTA lane 0 issues
-//               the MMAs: S = Q K^T (M 256, N 64, K 256; Q read from tensor memory)
-//               into one of two TMEM S buffers, then O += P V (M 256, N 256, K 64; P
-//               read from tensor memory) into the TMEM O accumulator, in the order
-//               S(0) S(1) PV(0) S(2) PV(1) ... so that the tensor cores compute the
-//               next S while the softmax warps work on the current one;
-//   warps 1-4   softmax: thread = row; reads S from TMEM, online softmax in the
-//               log2 domain with lazy rescaling (O is rescaled only when the row
-//               maximum grows by more than 2^8), writes P (f16, two keys per
-//               column) over the S buffer it has just read in tensor memory,
-//               and at the end of an item reads O and writes the partials;
-//   warps 5-12  producers: copy the item's Q rows (prepared once per call by
-//               pf_prep_kernel: RoPE, f16, contraction order) into tensor memory, and
-//               dequantise this CTA's half of the K and V tiles from q4_0 into
-//               128-byte-swizzled shared memory (six stages; the raw q4_0 of the next
-//               tile is loaded while the current one is converted).
+//               the MMAs: S = Q K^T (M 256, N 128, K 256; Q and K from shared memory)
+//               into one of two 128-column TMEM S buffers, then O += P V (M 256,
+//               N 256, K 128; P read from tensor memory) into the TMEM O accumulator,
+//               in the order S(0) S(1) PV(0) S(2) PV(1) ... so that the tensor cores
+//               compute the next S while the softmax warps work on the current one;
+//   warps 1-4   softmax: thread = row; reads S from TMEM in two passes (row maximum,
+//               then exponentials), online softmax in the log2 domain with lazy
+//               rescaling (O is rescaled only when the row maximum grows by more than
+//               2^8), writes P (f16, two keys per column) over the first half of the S
+//               buffer, and at the end of an item reads O and writes the partials;
+//   warps 5-12  producers: bring the item's Q image (prepared once per call by
+//               pf_prep_kernel: RoPE, f16, contraction order, swizzled) into shared
+//               memory with one bulk copy, and dequantise this CTA's half of each K and
+//               V tile from q4_0 into 128-byte-swizzled shared memory (two-buffer K and
+//               V rings; the raw q4_0 of the next tile is loaded while the current one
+//               is converted).
 // Barriers that gate an MMA live in the even CTA; the odd CTA's warps arrive on them
 // remotely (one elected lane per warp, default release semantics, which do not wait for
 // the producers' prefetch loads in flight).  MMA completions are committed to the
@@ -170,7 +171,7 @@ __device__ void pf_setup_block(const PfParams &p, int n_pairs) {
     const int m = threadIdx.x;
     const int64_t n_kv = clamp_nkv(p, p.ws, m == 0);
     const int64_t q_pos0 = *p.q_pos0;
-    int len = 0;  // 64-key tiles the M-tile sees
+    int len = 0;  // key tiles (kPfKeys keys each) the M-tile sees
     if (m < p.n_mtiles) {
         int t_last = kPairTok * (m >> 1) + kPairTok - 1;
         if (t_last > p.T - 1) t_last = p.T - 1;
