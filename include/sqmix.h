@@ -212,7 +212,7 @@ int sqmix_fa_prefill(const sqmix_fa_args *args, sqmix_stream_t stream);
  * k_new/v_new (n_new = 1): [n_seqs][2][256] with new_stride_seq, written at row
  * q_pos0[s] first.  The pointer and scalar arrays live in device memory.  Split
  * partials of all sequences share the workspace (sqmix_fa_batch_workspace_bytes, first
- * 256 bytes zero before first use).  splits_per_seq 0 = about 4 CTAs per SM over the
+ * 256 bytes zero before first use).  splits_per_seq 0 = about 2 CTAs per SM over the
  * batch.  flags as for sqmix_fa_decode. */
 typedef struct sqmix_fa_batch_args {
     int32_t n_seqs;

@@ -1152,9 +1152,10 @@ extern "C" int sqmix_fa_decode_batch(const sqmix_fa_batch_args *b, sqmix_stream_
                                        b->kv_new_dtype == SQMIX_BF16)),
                     "fa_decode_batch: n_new must be 0 or 1 (with k_new/v_new [n_seqs][2][256])");
     int splits = b->splits_per_seq;
-    if (splits <= 0) {  // about four CTAs per SM over the batch, at least one per sequence
+    if (splits <= 0) {  // about two CTAs per SM over the batch (one is resident per SM;
+                        // measured best for the 64-sequence stack), at least one per sequence
         const int sms = sqmix_device_sm_count(-1);
-        splits = (4 * sms + b->n_seqs - 1) / b->n_seqs;
+        splits = (2 * sms + b->n_seqs - 1) / b->n_seqs;
         if (splits > 64) splits = 64;
         if (splits < 1) splits = 1;
     }
@@ -1202,5 +1203,7 @@ extern "C" int sqmix_fa_decode_batch(const sqmix_fa_batch_args *b, sqmix_stream_
     bt.q_sseq = b->q_stride_seq;
     bt.new_sseq = b->new_stride_seq;
     bt.g_sseq = b->gate_stride_seq;
-    return launch_fa<1, 4, 2, 5, 1>(&a, splits, reinterpret_cast<cudaStream_t>(stream), bt);
+    // configuration 3 (6 warps per KV head, 3 x 55.3 KB slots): measured 4.5 % faster
+    // than configuration 1 on the 64-sequence batch of the mixer stack
+    return launch_fa<1, 6, 1, 3, 1>(&a, splits, reinterpret_cast<cudaStream_t>(stream), bt);
 }
