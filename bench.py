@@ -223,12 +223,24 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     pos_new = N_KV - 1
     owner = split_kv.owner(N_KV, world, pos_new)
     local_row = pos_new - split_kv.plan(N_KV, world, owner).start
-    q = torch.randn((N_LAYERS, 1, N_HEAD, HEAD_DIM), generator=g, device=dev)
-    gate = torch.randn((N_LAYERS, 1, N_HEAD, HEAD_DIM), generator=g, device=dev)
-    k_new = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
-    v_new = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+    # The step's inputs share one device buffer (so that the end-to-end measurement
+    # moves them with one host-to-device copy): q, gate, k_new, v_new (f32), then the
+    # step scalars {n_kv, q_pos0} (i64).
+    in_shapes = [(N_LAYERS, 1, N_HEAD, HEAD_DIM)] * 2 + [(N_LAYERS, 1, N_HEAD_KV, HEAD_DIM)] * 2
+    in_off = [0]
+    for shp in in_shapes:
+        in_off.append(in_off[-1] + 4 * shp[0] * shp[1] * shp[2] * shp[3])
+
+    def in_views(buf):
+        ts = [buf[in_off[i]:in_off[i + 1]].view(torch.float32).view(shp) for i, shp in enumerate(in_shapes)]
+        return ts + [buf[in_off[-1]:in_off[-1] + 16].view(torch.int64)]
+
+    inp = torch.empty(in_off[-1] + 16, dtype=torch.uint8, device=dev)
+    q, gate, k_new, v_new, step = in_views(inp)
+    for t_, shp in zip((q, gate, k_new, v_new), in_shapes):
+        t_.copy_(torch.randn(shp, generator=g, device=dev))
+    step.copy_(torch.tensor(list(shard.local_step(N_KV, pos_new)), dtype=torch.int64, device=dev))
     out = torch.empty((N_LAYERS, 1, N_HEAD, HEAD_DIM), device=dev)
-    step = torch.tensor(list(shard.local_step(N_KV, pos_new)), dtype=torch.int64, device=dev)
     d_nkv, d_qpos = step[0:1], step[1:2]
     d_row = torch.tensor([local_row], dtype=torch.int64, device=dev)
     n_splits = sqmix.lib().sqmix_device_sm_count(local_rank)
@@ -384,22 +396,17 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     achieved = alg_bytes / (fa_us * 1e-6) / 1e9
 
     # ---- end to end through the public API with host buffers -------------------
-    h_q = torch.randn((N_LAYERS, 1, N_HEAD, HEAD_DIM)).pin_memory()
-    h_gate = torch.randn((N_LAYERS, 1, N_HEAD, HEAD_DIM)).pin_memory()
-    h_k = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM)).pin_memory()
-    h_v = torch.randn((N_LAYERS, 1, N_HEAD_KV, HEAD_DIM)).pin_memory()
+    h_inp = torch.empty(inp.numel(), dtype=torch.uint8).pin_memory()  # same layout as inp
+    h_views = in_views(h_inp)
+    for t_, shp in zip(h_views[:4], in_shapes):
+        t_.copy_(torch.randn(shp))
+    h_views[4].copy_(torch.tensor(list(shard.local_step(N_KV, pos_new)), dtype=torch.int64))
     h_out = torch.empty((N_LAYERS, 1, N_HEAD, HEAD_DIM)).pin_memory()
-    h_step = torch.tensor(list(shard.local_step(N_KV, pos_new)), dtype=torch.int64).pin_memory()
-    h2d = (h_q.numel() + h_gate.numel()) * 4 + (h_k.numel() + h_v.numel()) * 4 * (1 if rank == owner else 0) + 16
+    h2d = h_inp.numel()
     d2h = h_out.numel() * 4
 
     def e2e_step():
-        q.copy_(h_q, non_blocking=True)
-        gate.copy_(h_gate, non_blocking=True)
-        if rank == owner:
-            k_new.copy_(h_k, non_blocking=True)
-            v_new.copy_(h_v, non_blocking=True)
-        step.copy_(h_step, non_blocking=True)
+        inp.copy_(h_inp, non_blocking=True)  # q, gate, k_new, v_new and the step scalars
         run()
         h_out.copy_(out, non_blocking=True)
 
