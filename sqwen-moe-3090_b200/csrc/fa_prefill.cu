@@ -288,19 +288,20 @@ __device__ void pf_qprep_token(const PfParams &p, int t, int tid, float2 *rope_t
     }
 }
 
-// One launch before the main kernel: blocks 0 .. T_pad/2 - 1 prepare Q for two tokens
-// each (256 threads per token), the last block builds the item table.  The main
-// kernel, launched as its programmatic dependent, runs its prologue meanwhile.
+// One launch before the main kernel: block 0 builds the item table (first in grid
+// order, so that its scan overlaps the Q blocks instead of trailing them), blocks
+// 1 .. T_pad/2 prepare Q for two tokens each (256 threads per token).  The main kernel,
+// launched as its programmatic dependent, runs its prologue meanwhile.
 constexpr int kPrepThreads = kMaxMtiles;  // 512
 __global__ void __launch_bounds__(kPrepThreads) pf_prep_kernel(PfParams p, int n_pairs) {
     asm volatile("griddepcontrol.launch_dependents;" :::);
-    if (blockIdx.x == gridDim.x - 1) {
+    if (blockIdx.x == 0) {
         pf_setup_block(p, n_pairs);
         return;
     }
     __shared__ float2 rope_tab[2][32];
     const int half_id = threadIdx.x >> 8;
-    pf_qprep_token(p, 2 * blockIdx.x + half_id, threadIdx.x & 255, rope_tab[half_id]);
+    pf_qprep_token(p, 2 * (blockIdx.x - 1) + half_id, threadIdx.x & 255, rope_tab[half_id]);
 }
 
 // ---- helpers -----------------------------------------------------------------------
@@ -852,33 +853,61 @@ struct PfMergeParams {
 __global__ void __launch_bounds__(256) fa_prefill_merge_kernel(PfMergeParams p) {
     __shared__ float orow[8][256];
     __shared__ float lse_s[8];
-    // programmatic dependent of the main kernel: its partials are complete after this
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int t = blockIdx.x, kvh = blockIdx.y, i = threadIdx.x;
     const int hq = i & 7, c4a = i >> 3;  // chunks c4a and c4a + 32
     const int m = (t / kPairTok) * 2 + kvh;
+    // The item table (prep kernel) and the gate (written before the call) are complete
+    // when this grid starts (its predecessor, the main kernel, waited for them before
+    // triggering it); only the partials need the grid-dependency wait.
     const int4 mt = reinterpret_cast<const int4 *>(p.ws + kWsMtab)[m];
+    float gs[8];
+#pragma unroll
+    for (int h = 0; h < 8; ++h)
+        gs[h] = p.gate ? load_act(p.gate, t * p.g_st + (kvh * 8 + h) * p.g_sh + i, p.gate_dtype) : 0.f;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const size_t ml_off = align256(kWsItems + static_cast<size_t>(p.items_max) * 16);
     const size_t o_off = align256(ml_off + static_cast<size_t>(p.items_max) * kPairRows * 2 * sizeof(float));
     const float2 *part_ml = reinterpret_cast<const float2 *>(p.ws + ml_off);
     const float4 *part_o = reinterpret_cast<const float4 *>(p.ws + o_off);
     const int n_parts = mt.y + (mt.z >= 0 ? 1 : 0);
     const int r = (t % kPairTok) * 8 + hq;  // row of the M-tile (odd CTA's rows from 128)
+    auto item_of = [&](int k) { return static_cast<size_t>(k < mt.y ? mt.x + k : mt.z); };
+    // the partials of up to kBatch items are loaded at once (one round trip), then folded
+    constexpr int kBatch = 4;
     float M = -INFINITY, L = 0.f;
     float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
-#pragma unroll 2
-    for (int k = 0; k < n_parts; ++k) {
-        const size_t item = static_cast<size_t>(k < mt.y ? mt.x + k : mt.z);
-        const float2 ml = __ldcg(&part_ml[item * kPairRows + r]);
-        const float4 o0 = __ldcg(&part_o[(item * 64 + c4a) * kPairRows + r]);
-        const float4 o1 = __ldcg(&part_o[(item * 64 + c4a + 32) * kPairRows + r]);
-        if (ml.x == -INFINITY) continue;  // nothing visible in that item (l = 0, O = 0)
-        const float mn = fmaxf(M, ml.x);
-        const float sa = ex2(M - mn), sb = ex2(ml.x - mn);  // 2^-inf = 0 for the first item
+    for (int k0 = 0; k0 < n_parts; k0 += kBatch) {
+        float2 ml[kBatch];
+        float4 o0[kBatch], o1[kBatch];
+#pragma unroll
+        for (int k = 0; k < kBatch; ++k) {
+            ml[k] = make_float2(-INFINITY, 0.f);
+            if (k0 + k < n_parts) {
+                const size_t item = item_of(k0 + k);
+                ml[k] = __ldcg(&part_ml[item * kPairRows + r]);
+                o0[k] = __ldcg(&part_o[(item * 64 + c4a) * kPairRows + r]);
+                o1[k] = __ldcg(&part_o[(item * 64 + c4a + 32) * kPairRows + r]);
+            }
+        }
+        float mn = M;
+#pragma unroll
+        for (int k = 0; k < kBatch; ++k) mn = fmaxf(mn, ml[k].x);
+        if (mn == -INFINITY) continue;  // nothing visible so far (l = 0, O = 0)
+        const float sa = ex2(M - mn);   // 2^-inf = 0 before the first visible item
         M = mn;
-        L = L * sa + ml.y * sb;
-        a0 = make_float4(a0.x * sa + o0.x * sb, a0.y * sa + o0.y * sb, a0.z * sa + o0.z * sb, a0.w * sa + o0.w * sb);
-        a1 = make_float4(a1.x * sa + o1.x * sb, a1.y * sa + o1.y * sb, a1.z * sa + o1.z * sb, a1.w * sa + o1.w * sb);
+        L *= sa;
+        a0 = make_float4(a0.x * sa, a0.y * sa, a0.z * sa, a0.w * sa);
+        a1 = make_float4(a1.x * sa, a1.y * sa, a1.z * sa, a1.w * sa);
+#pragma unroll
+        for (int k = 0; k < kBatch; ++k) {
+            if (ml[k].x == -INFINITY) continue;  // absent, or nothing visible in that item
+            const float w = ex2(ml[k].x - M);
+            L = fmaf(ml[k].y, w, L);
+            a0 = make_float4(fmaf(o0[k].x, w, a0.x), fmaf(o0[k].y, w, a0.y), fmaf(o0[k].z, w, a0.z),
+                             fmaf(o0[k].w, w, a0.w));
+            a1 = make_float4(fmaf(o1[k].x, w, a1.x), fmaf(o1[k].y, w, a1.y), fmaf(o1[k].z, w, a1.z),
+                             fmaf(o1[k].w, w, a1.w));
+        }
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
     const float4 src[2] = {a0, a1};
@@ -892,14 +921,11 @@ __global__ void __launch_bounds__(256) fa_prefill_merge_kernel(PfMergeParams p) 
     }
     if (c4a == 0) lse_s[hq] = L > 0.f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
     __syncthreads();
+#pragma unroll
     for (int h = 0; h < 8; ++h) {
-        const int head = kvh * 8 + h;
         float o = orow[h][i];
-        if (p.gate) {
-            const float gv = load_act(p.gate, t * p.g_st + head * p.g_sh + i, p.gate_dtype);
-            o *= 1.f / (1.f + expf(-gv));
-        }
-        p.out[(static_cast<size_t>(t) * 16 + head) * 256 + i] = o;
+        if (p.gate) o *= 1.f / (1.f + expf(-gs[h]));
+        p.out[(static_cast<size_t>(t) * 16 + kvh * 8 + h) * 256 + i] = o;
     }
     if (p.lse && i < 8) p.lse[t * 16 + kvh * 8 + i] = lse_s[i];
 }
