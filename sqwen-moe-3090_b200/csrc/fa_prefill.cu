@@ -225,13 +225,6 @@ __device__ __forceinline__ int k_real_dim(int p) {
     return 32 * b + 4 * c + (e & 3) + 16 * (e >> 2);
 }
 
-// Elements d, d+1 (d even) of a Q row as floats.
-__device__ __forceinline__ float2 load_pair(const void *src, int64_t i, int dtype) {
-    if (dtype == SQMIX_F32) return *reinterpret_cast<const float2 *>(static_cast<const float *>(src) + i);
-    if (dtype == SQMIX_BF16)
-        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(static_cast<const __nv_bfloat16 *>(src) + i));
-    return __half22float2(*reinterpret_cast<const __half2 *>(static_cast<const __half *>(src) + i));
-}
 
 // One block per query token (padded to whole M-tiles), 8 f16 pairs per thread, all
 // loads issued before the RoPE table is needed: RoPE (the table of rope_cos_sin for the
@@ -239,19 +232,34 @@ __device__ __forceinline__ float2 load_pair(const void *src, int64_t i, int dtyp
 // holds positions 2w, 2w+1, which are the adjacent head dimensions k_real_dim(2w),
 // k_real_dim(2w) + 1.  Rows of padding tokens are zero.  Q rows must be aligned to two
 // elements (the host checks it).
+template <int DT>
+__device__ __forceinline__ float2 load_pair_t(const void *src, int64_t i) {
+    if (DT == SQMIX_F32) return *reinterpret_cast<const float2 *>(static_cast<const float *>(src) + i);
+    if (DT == SQMIX_BF16)
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(static_cast<const __nv_bfloat16 *>(src) + i));
+    return __half22float2(*reinterpret_cast<const __half2 *>(static_cast<const __half *>(src) + i));
+}
+
+// Thread tid (0..255) of token t writes pair w = tid % 128 of the rows of heads
+// 2k + tid / 128, k = 0..7: everything but the head is the same for the eight pairs.
+template <int DT>
 __device__ void pf_qprep_token(const PfParams &p, int t, int tid, float2 *rope_tab) {
     const int half = p.rope_n_rot >> 1;
     const bool live = t < p.T;
+    const int w = tid & 127, hsel = tid >> 7;
+    const int dim = k_real_dim(2 * w);  // even; dim + 1 is position 2w + 1
+    const bool rot = dim < p.rope_n_rot, lo = dim < half;
+    const int pdim = lo ? dim + half : dim - half;  // RoPE partner
+    const int ri = lo ? dim : dim - half;
     float2 x[8], y[8];
+    const int64_t row0 = t * p.q_st + hsel * p.q_sh;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        const int e = tid + 256 * k, head = e >> 7, w = e & 127;
-        const int dim = k_real_dim(2 * w);  // even; dim + 1 is position 2w + 1
         x[k] = y[k] = make_float2(0.f, 0.f);
         if (live) {
-            const int64_t rbase = t * p.q_st + head * p.q_sh;
-            x[k] = load_pair(p.q, rbase + dim, p.q_dtype);
-            if (dim < p.rope_n_rot) y[k] = load_pair(p.q, rbase + (dim < half ? dim + half : dim - half), p.q_dtype);
+            const int64_t rbase = row0 + 2 * k * p.q_sh;
+            x[k] = load_pair_t<DT>(p.q, rbase + dim);
+            if (rot) y[k] = load_pair_t<DT>(p.q, rbase + pdim);
         }
     }
     if (tid < 32) {
@@ -260,31 +268,35 @@ __device__ void pf_qprep_token(const PfParams &p, int t, int tid, float2 *rope_t
                                          : make_float2(1.f, 0.f);
     }
     __syncthreads();
+    float2 c0 = make_float2(1.f, 0.f), c1 = c0;
+    if (rot) {
+        c0 = rope_tab[ri];
+        c1 = rope_tab[ri + 1];
+    }
+    // image address: M-tile m = (t / 32) * 2 + head / 8, pair row prr = (t % 32) * 8 + head % 8
+    // (its CTA = prr / 128 is the same for all eight heads), positions 2w, 2w+1 -> region,
+    // 16-byte chunk swizzled with row % 8 = (2k) % 8 + hsel
+    const int prr0 = (t % kPairTok) * 8;
+    const int cta = prr0 >> 7;
+    const int el = (2 * w) & 63, chunk = el >> 3;
+    uint8_t *img = p.ws + p.qimg_off + ((2 * w) >> 6) * kQRegion + (el & 7) * 2;
+    const size_t m0 = static_cast<size_t>(t / kPairTok) * 2;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        const int e = tid + 256 * k, head = e >> 7, w = e & 127;
-        const int dim = k_real_dim(2 * w);
         uint32_t v = 0u;
         if (live) {
             float2 z = x[k];
-            if (dim < p.rope_n_rot) {
-                const bool lo = dim < half;
-                const int i = lo ? dim : dim - half;
-                const float2 c0 = rope_tab[i], c1 = rope_tab[i + 1];
+            if (rot)
                 z = lo ? make_float2(__fsub_rn(__fmul_rn(x[k].x, c0.x), __fmul_rn(y[k].x, c0.y)),
                                      __fsub_rn(__fmul_rn(x[k].y, c1.x), __fmul_rn(y[k].y, c1.y)))
                        : make_float2(__fadd_rn(__fmul_rn(y[k].x, c0.y), __fmul_rn(x[k].x, c0.x)),
                                      __fadd_rn(__fmul_rn(y[k].y, c1.y), __fmul_rn(x[k].y, c1.x)));
-            }
             v = pack_half2(z.x, z.y);
         }
-        // pair row -> CTA and row; positions 2w, 2w+1 -> region, 16-byte chunk (swizzled)
-        const int m = (t / kPairTok) * 2 + (head >> 3), prr = (t % kPairTok) * 8 + (head & 7);
-        const int cta = prr >> 7, rr = prr & 127;
-        const int el = (2 * w) & 63, chunk = el >> 3;
-        const size_t byte = (static_cast<size_t>(m) * 2 + cta) * kQImgBytes + ((2 * w) >> 6) * kQRegion + rr * 128 +
-                            (((chunk ^ (rr & 7)) & 7) << 4) + (el & 7) * 2;
-        *reinterpret_cast<uint32_t *>(p.ws + p.qimg_off + byte) = v;
+        const int r7 = ((2 * k) & 7) + hsel;
+        const int rr = (prr0 & 127) + r7;
+        const size_t byte = ((m0 + (k >> 2)) * 2 + cta) * kQImgBytes + rr * 128 + (((chunk ^ r7) & 7) << 4);
+        *reinterpret_cast<uint32_t *>(img + byte) = v;
     }
 }
 
@@ -301,7 +313,13 @@ __global__ void __launch_bounds__(kPrepThreads) pf_prep_kernel(PfParams p, int n
     }
     __shared__ float2 rope_tab[2][32];
     const int half_id = threadIdx.x >> 8;
-    pf_qprep_token(p, 2 * (blockIdx.x - 1) + half_id, threadIdx.x & 255, rope_tab[half_id]);
+    const int t = 2 * (blockIdx.x - 1) + half_id, tid = threadIdx.x & 255;
+    if (p.q_dtype == SQMIX_F32)
+        pf_qprep_token<SQMIX_F32>(p, t, tid, rope_tab[half_id]);
+    else if (p.q_dtype == SQMIX_BF16)
+        pf_qprep_token<SQMIX_BF16>(p, t, tid, rope_tab[half_id]);
+    else
+        pf_qprep_token<SQMIX_F16>(p, t, tid, rope_tab[half_id]);
 }
 
 // ---- helpers -----------------------------------------------------------------------
