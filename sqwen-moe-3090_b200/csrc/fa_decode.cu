@@ -287,9 +287,11 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     constexpr int kStagingSlots = (kStagingBytes + L::kStageBytes - 1) / L::kStageBytes;
     static_assert(kStagingSlots < NSTAGE, "staging must leave ring slots for the first tiles");
     // Slots filled before the dependency wait: the ring minus the staging slots, at most
-    // two (73.7 KB per SM), so that the Q loads after the wait do not queue behind a
-    // long fill.
-    constexpr int kEarlySlots = (NSTAGE - kStagingSlots) < 2 ? (NSTAGE - kStagingSlots) : 2;
+    // ~74 KB per SM (two 36.9 KB slots, one 55.3 KB slot), so that the Q loads after the
+    // wait do not queue behind a long fill (measured: one slot more or less costs 1-3 %).
+    constexpr int kEarlyBySize = 75000 / L::kStageBytes > 0 ? 75000 / L::kStageBytes : 1;
+    constexpr int kEarlySlots =
+        (NSTAGE - kStagingSlots) < kEarlyBySize ? (NSTAGE - kStagingSlots) : kEarlyBySize;
     // Initial fill of the ring, minus the staging slots.  Rows from q_pos0 on belong to
     // this step: they are written by this launch (fused append, deferred until then) or
     // by the kernel just before it (streamed only after the dependency wait).  With
