@@ -90,6 +90,24 @@ def test_prefill_pp512_on_prefix(sq, oracle):
     sq.fa_status(ws)
 
 
+@pytest.mark.parametrize("layout", ["f16", "qg_view_bf16"])
+def test_prefill_q_dtype_and_strided_q(sq, oracle, layout):
+    """f16 Q, and Q read in place from the QG projection (per head [q(256), gate(256)],
+    attn.rs:131-175: head stride 512) -- the prep kernel's other dtype path and strides."""
+    P, T = 300, 40
+    dt = torch.float16 if layout == "f16" else torch.bfloat16
+    c = build_case(sq, oracle, P, T, seed=41 + len(layout), q_dtype=dt)
+    if layout == "qg_view_bf16":
+        qg = torch.empty((T, 16, 512), dtype=dt, device="cuda")
+        qg[:, :, :256] = c["q"]
+        qg[:, :, 256:] = 7.0  # never read
+        c["q"] = qg[:, :, :256]
+        assert c["q"].stride(1) == 512
+    out, lse = run_prefill(sq, c, P)
+    assert rel_err(out, c["want"]) <= ATTN_TOL
+    assert np.abs(lse - c["wlse"]).max() < 1e-3
+
+
 def test_prefill_agrees_with_decode(sq, oracle):
     P, T = 777, 2
     c = build_case(sq, oracle, P, T, seed=9, q_dtype=torch.float32)
