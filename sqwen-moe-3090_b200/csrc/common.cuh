@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "sqmix.h"
 
 namespace sqmix {
@@ -14,6 +16,25 @@ namespace sqmix {
 // Set by the C-ABI wrappers; read through sqmix_last_error().
 void set_error(const char *fmt, ...);
 int cuda_status(cudaError_t e, const char *what);
+
+// Function attributes such as cudaFuncAttributeMaxDynamicSharedMemorySize are per
+// device: a launcher records the devices it has set them on, one bit per ordinal.
+// Returns the current device's bit (0 if it cannot be represented: set every time).
+inline uint64_t current_device_bit() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d > 63) return 0;
+    return 1ull << d;
+}
+// Sets a dynamic shared memory limit on `kernel` once per device (mask: the caller's
+// per-kernel record).
+template <typename K>
+inline cudaError_t set_smem_once(std::atomic<uint64_t> &mask, K kernel, int bytes) {
+    const uint64_t bit = current_device_bit();
+    if (bit && (mask.load() & bit)) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) mask.fetch_or(bit);
+    return e;
+}
 
 #define SQMIX_CHECK_ARG(cond, ...)          \
     do {                                    \

@@ -907,11 +907,10 @@ template <int NQ, int WPH, int GPW, int NSTAGE, int MINB>
 static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, const FaBatch &bt = FaBatch()) {
     using L = FaCfg<NQ, WPH, GPW, NSTAGE, MINB>;
     auto kernel = fa_decode_kernel<NQ, WPH, GPW, NSTAGE, MINB>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+    static std::atomic<uint64_t> attr_devices{0};
+    {
+        const cudaError_t e = set_smem_once(attr_devices, kernel, L::kTotal);
         if (e != cudaSuccess) return cuda_status(e, "fa_decode smem attribute");
-        attr_set = true;
     }
     size_t off_ml, off_o;
     fa_ws_layout(n_splits * bt.n_seqs, NQ, &off_ml, &off_o);

@@ -1026,12 +1026,10 @@ extern "C" int sqmix_fa_prefill(const sqmix_fa_args *a, sqmix_stream_t stream) {
         set_error("fa_prefill: workspace %zu bytes < %zu needed", a->workspace_bytes, need);
         return SQMIX_ENOSPC;
     }
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmemBytes));
+    static std::atomic<uint64_t> attr_devices{0};
+    {
+        const cudaError_t e = set_smem_once(attr_devices, fa_prefill_kernel, static_cast<int>(kSmemBytes));
         if (e != cudaSuccess) return cuda_status(e, "fa_prefill smem attribute");
-        attr_set = true;
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     PfParams p;

@@ -768,15 +768,11 @@ extern "C" int sqmix_gdn_prefill(const sqmix_gdn_args *a, void *workspace, size_
     // tokens [0, T_chunk) go through the chunked form, the last n_snap - 1 through the
     // recurrent kernel, which writes the snapshot slots
     const int T_chunk = a->n_tokens - (a->n_snap - 1);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kPrepSmem));
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gdn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(kScanSmem));
+    static std::atomic<uint64_t> prep_devices{0}, scan_devices{0};
+    {
+        cudaError_t e = set_smem_once(prep_devices, gdn_chunk_prep_kernel, static_cast<int>(kPrepSmem));
+        if (e == cudaSuccess) e = set_smem_once(scan_devices, gdn_chunk_scan_kernel, static_cast<int>(kScanSmem));
         if (e != cudaSuccess) return cuda_status(e, "gdn_prefill smem attribute");
-        attr_set = true;
     }
     ChunkParams p;
     p.q = a->q;
