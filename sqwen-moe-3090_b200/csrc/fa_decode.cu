@@ -499,6 +499,11 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     const uint2 *qf_w = qf_s + (kvh * NQ) * 8 * 2 * 32 + lane;
     const float2 *kinit_w = reinterpret_cast<const float2 *>(kinit_s) + (kvh * NQ) * 8 * 4 + c;
     const float craw = p.c * kTwo24;  // scores below are in units of 2^-24
+    // P = 2^((x - m) craw) stays <= 2^kLazyLog2 = 8 between moves of the running maximum,
+    // so P * (V scale) stays finite in f16 for every V scale of an f16-range block
+    // (|d| <= 65504 / 8); craw > 0 (the host requires scale > 0).
+    constexpr float kLazyLog2 = 3.0f;
+    const float lazy_thr = kLazyLog2 / craw;
     const uint32_t voff[4] = {kVOffLo, kVOffHi, kVOffLo, kVOffHi};
     bool ok = true;
 
@@ -634,7 +639,10 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
                 float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
                 for (int j = 0; j < GPW; ++j) {
-                    const bool vlo = uv[j] && tok0[j] + g <= lim, vhi = uv[j] && tok0[j] + g + 8 <= lim;
+                    // rows g and g + 8 of the group are keys tok0 + g and tok0 + g + 8
+                    const int64_t rem64 = lim - tok0[j];
+                    const int rem = rem64 > 16 ? 16 : rem64 < -1 ? -1 : static_cast<int>(rem64);
+                    const bool vlo = uv[j] && g <= rem, vhi = uv[j] && g + 8 <= rem;
                     x[j][0] = vlo ? sc[j][qi][0] : -INFINITY;
                     x[j][1] = vlo ? sc[j][qi][1] : -INFINITY;
                     x[j][2] = vhi ? sc[j][qi][2] : -INFINITY;
@@ -642,15 +650,22 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
                     mx0 = fmaxf(mx0, fmaxf(x[j][0], x[j][2]));
                     mx1 = fmaxf(mx1, fmaxf(x[j][1], x[j][3]));
                 }
+                // Lazy maximum: the running maximum moves only when a score exceeds it by
+                // more than kLazyLog2 (in log2 units), so P <= 2^kLazyLog2 and, in the
+                // common case, one vote replaces the three shuffle rounds and the rescale.
+                float mn0 = m_run[qi][0], mn1 = m_run[qi][1];
+                float al0 = 1.f, al1 = 1.f;
+                if (__any_sync(0xffffffffu, mx0 > mn0 + lazy_thr || mx1 > mn1 + lazy_thr)) {
 #pragma unroll
-                for (int off = 4; off < 32; off <<= 1) {
-                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+                    for (int off = 4; off < 32; off <<= 1) {
+                        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+                    }
+                    mn0 = fmaxf(m_run[qi][0], mx0);
+                    mn1 = fmaxf(m_run[qi][1], mx1);
+                    al0 = (mn0 == m_run[qi][0]) ? 1.f : ex2((m_run[qi][0] - mn0) * craw);
+                    al1 = (mn1 == m_run[qi][1]) ? 1.f : ex2((m_run[qi][1] - mn1) * craw);
                 }
-                const float mn0 = fmaxf(m_run[qi][0], mx0);
-                const float mn1 = fmaxf(m_run[qi][1], mx1);
-                const float al0 = (mn0 == m_run[qi][0]) ? 1.f : ex2((m_run[qi][0] - mn0) * craw);
-                const float al1 = (mn1 == m_run[qi][1]) ? 1.f : ex2((m_run[qi][1] - mn1) * craw);
                 float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
                 for (int j = 0; j < GPW; ++j) {

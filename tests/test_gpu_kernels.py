@@ -277,6 +277,39 @@ def test_fa_decode_config3_twelve_warps(sq, oracle, n_kv, n_splits):
 
 
 @pytest.mark.parametrize("n_q", [1, 2])
+@pytest.mark.parametrize("n_splits", [1, 0])
+@pytest.mark.parametrize("v_amax", [1.0, 60000.0])
+def test_fa_decode_rising_scores(sq, oracle, n_q, n_splits, v_amax):
+    """Scores that climb along the cache (about 0.3 log2 units per 16-token group), so the
+    running maximum keeps moving past the lazy-update threshold in every warp, with V
+    blocks up to `v_amax` (60000: P * V scale stays near the top of the f16 range)."""
+    rng = np.random.default_rng(7 + n_q + n_splits + int(v_amax))
+    n_kv = 3000
+    u = rng.standard_normal(256)
+    u /= np.linalg.norm(u)
+    ramp = np.linspace(0.0, 40.0, n_kv)  # score of the aligned component, in nats
+    k = rng.standard_normal((n_kv, 2, 256)) + ramp[:, None, None] * u[None, None, :]
+    v = rng.standard_normal((n_kv, 2, 256))
+    v *= v_amax / np.abs(v).max()
+    q = 16.0 * u[None, None, :] + 0.5 * rng.standard_normal((n_q, 16, 256))
+    k, v, q = (x.astype(np.float32) for x in (k, v, q))
+    kq = oracle.q4_0_quantize(k.reshape(n_kv, 512))
+    vq = oracle.q4_0_quantize(v.reshape(n_kv, 512))
+    kd = oracle.q4_0_dequantize(kq, 512).reshape(n_kv, 2, 256)
+    vd = oracle.q4_0_dequantize(vq, 512).reshape(n_kv, 2, 256)
+    cap = cap_for(n_kv)
+    kc, vc = make_cache_from_rows(sq, kq, vq, cap)
+    q_pos0 = n_kv - n_q
+    out, lse = run_fa(sq, torch.from_numpy(q).cuda(), kc, vc, cap, n_kv, q_pos0, n_splits=n_splits, lse=True)
+    want, wlse = oracle.attn(q, kd, vd, None, q_pos0=q_pos0, scale=1 / 16, want_lse=True)
+    assert np.isfinite(out).all()
+    assert rel_err(out, want) <= ATTN_TOL
+    # lse here is ~45: rounding Q to f16 for the tensor cores alone moves it by ~2e-3
+    # (oracle with f16 Q), so its bound is relative to its size
+    assert np.abs(lse - wlse).max() < 1e-4 * np.abs(wlse).max()
+
+
+@pytest.mark.parametrize("n_q", [1, 2])
 def test_fa_decode_fused_head_rms_norm(sq, oracle, n_q):
     """Q and the appended K rows RMS-normalised per head with the attn_q_norm /
     attn_k_norm weights inside the decode kernel (attn.rs:66-84, :166-175), then
