@@ -33,8 +33,8 @@ sys.path.insert(0, os.path.join(REPO, "sqwen-moe-3090_b200"))
 N_LAYERS = 10
 N_KV = 172032
 # DRAM bytes of one decode launch at N_KV keys, from one ncu capture
-# (profiles/fa_decode_kernel_172k.txt): 99.17 MB read + 5.59 MB written.
-FA_NCU_TRAFFIC = 104_757_504
+# (profiles/fa_decode_kernel_172k.txt): 99.17 MB read + 3.65 MB written.
+FA_NCU_TRAFFIC = 102_818_048
 HEAD_DIM = 256
 N_HEAD = 16
 N_HEAD_KV = 2
