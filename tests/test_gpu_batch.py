@@ -66,7 +66,7 @@ def build(sq, oracle, lens, seed, fused):
     return d, caches, refs
 
 
-@pytest.mark.parametrize("splits", [0, 1, 3])
+@pytest.mark.parametrize("splits", [0, 1, 3, 16, 17])  # <= 16 splits: the per-thread merge
 def test_batch_decode_matches_oracle(sq, oracle, splits):
     lens = [100, 1000, 17, 3000, 256, 1]
     d, caches, refs = build(sq, oracle, lens, seed=31 + splits, fused=False)

@@ -226,7 +226,7 @@ def test_fa_decode_ragged(sq, oracle, n_kv, n_q):
     assert np.abs(lse - wlse).max() < 1e-3
 
 
-@pytest.mark.parametrize("n_splits", [1, 3, 7, 148, 300])
+@pytest.mark.parametrize("n_splits", [1, 3, 7, 16, 17, 148, 300])  # <= 16: the per-thread merge
 def test_fa_decode_split_counts(sq, oracle, n_splits):
     rng = np.random.default_rng(30 + n_splits)
     n_kv = 1500
@@ -234,9 +234,10 @@ def test_fa_decode_split_counts(sq, oracle, n_splits):
     cap = cap_for(n_kv)
     kc, vc = make_cache_from_rows(sq, kq, vq, cap)
     q = rng.standard_normal((2, 16, 256)).astype(np.float32)
-    out, _ = run_fa(sq, torch.from_numpy(q).cuda(), kc, vc, cap, n_kv, n_kv - 2, n_splits=n_splits)
-    want = oracle.attn(q, kd, vd, None, q_pos0=n_kv - 2, scale=1 / 16)
+    out, lse = run_fa(sq, torch.from_numpy(q).cuda(), kc, vc, cap, n_kv, n_kv - 2, n_splits=n_splits, lse=True)
+    want, wlse = oracle.attn(q, kd, vd, None, q_pos0=n_kv - 2, scale=1 / 16, want_lse=True)
     assert rel_err(out, want) <= ATTN_TOL
+    assert np.abs(lse - wlse).max() < 1e-3
 
 
 @pytest.mark.parametrize("n_kv,n_splits", [(1, 0), (17, 3), (257, 0), (1000, 7), (5000, 0), (5000, 300)])
