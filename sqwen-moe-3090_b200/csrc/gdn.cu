@@ -74,8 +74,12 @@ __device__ __forceinline__ float4 l2norm4(float4 x, float eps) {
 // value columns).  q, k, their norms and k.q are shared by the warp's columns; each
 // lane keeps keys 4*lane..4*lane+3 of every column, so a warp has JW 16-byte loads
 // in flight per lane (more columns per warp where there is enough work to spread).
+// 8 columns (large batches): at most 64 registers, so 4 blocks (32 warps) per SM keep
+// more state loads in flight (80 registers and 3 blocks measured 4.5 % slower for a
+// 64-sequence batch; no spills at 64).  4 columns carry no minimum (0): bounding them
+// measured 8 % slower for a single sequence, whose launch is latency bound.
 template <int JW>
-__global__ void __launch_bounds__(256) gdn_recurrent_kernel(GdnParams p) {
+__global__ void __launch_bounds__(256, JW == 8 ? 4 : 0) gdn_recurrent_kernel(GdnParams p) {
     const int lane = threadIdx.x & 31;
     const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
     constexpr int kGroups = 128 / JW;
