@@ -864,6 +864,16 @@ def run_profile_case(case: str):
         b = torch.rand((1, 1, 32), generator=g, device=dev)
         for _ in range(3):
             sqmix.gated_delta_net(q, k, v, gg, b, S)
+    elif case == "gdnb":  # the 64-sequence batch of config 4 (268 MB of state, > L2)
+        n = 64
+        S = torch.randn((n, 1, 32, 128, 128), generator=g, device=dev) * 0.02
+        q = torch.nn.functional.normalize(torch.randn((n, 1, 16, 128), generator=g, device=dev), dim=-1)
+        k = torch.nn.functional.normalize(torch.randn((n, 1, 16, 128), generator=g, device=dev), dim=-1)
+        v = torch.randn((n, 1, 32, 128), generator=g, device=dev)
+        gg = -torch.rand((n, 1, 32), generator=g, device=dev)
+        b = torch.rand((n, 1, 32), generator=g, device=dev)
+        for _ in range(3):
+            sqmix.gated_delta_net(q, k, v, gg, b, S)
     else:
         raise SystemExit(f"unknown profile case {case}")
     torch.cuda.synchronize()
@@ -880,7 +890,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill measurement")
     ap.add_argument("--nccl-merge", action="store_true", help="N > 1: all-gather + merge instead of the peer merge")
-    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn | gdnp) and exit")
+    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn | gdnb | gdnp) and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)
