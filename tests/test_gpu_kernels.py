@@ -477,6 +477,31 @@ def test_gdn_snapshots_sel_and_batch(sq, oracle):
         assert rel_err(st_np[s, 1], snaps[1]) <= GDN_TOL
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("state_ready", [False, True])
+def test_gdn_decode_large_batch(sq, oracle, dtype, state_ready):
+    """64 sequences x 1 token (the batch of config 4): the launch path for large batches
+    (8 value columns per warp), per-sequence input planes through sel, the update
+    written to plane 0; outputs and states against the oracle for every sequence."""
+    rng = np.random.default_rng(53 + int(state_ready))
+    n_seqs, n_planes = 64, 2
+    q, k, v, g, beta, S = gdn_case(rng, n_seqs, 1, n_planes=n_planes)
+    sel = rng.integers(0, n_planes, n_seqs).astype(np.int32)
+    qt, kt, vt = (torch.from_numpy(x).to(dtype).cuda() for x in (q, k, v))
+    st = torch.from_numpy(S).cuda()
+    out = sq.gated_delta_net(qt, kt, vt, torch.from_numpy(g).cuda(), torch.from_numpy(beta).cuda(), st,
+                             n_planes=n_planes, sel=torch.from_numpy(sel).cuda(), state_ready=state_ready)
+    torch.cuda.synchronize()
+    st_np, out_np = st.cpu().numpy(), out.cpu().numpy()
+    qf, kf, vf = (x.float().cpu().numpy() for x in (qt, kt, vt))
+    for s in range(n_seqs):
+        want, snaps = oracle.gdn(qf[s], kf[s], vf[s], g[s], beta[s], S[s, sel[s]], n_snap=1)
+        assert rel_err(out_np[s], want) <= GDN_TOL, s
+        assert rel_err(st_np[s, 0], snaps[0]) <= GDN_TOL, s
+        if n_planes > 1:  # plane 1 is never written
+            assert np.array_equal(st_np[s, 1], S[s, 1]), s
+
+
 def test_gdn_state_ready_chain_after_conv(sq, oracle):
     """SQMIX_GDN_STATE_READY: the recurrence reads its state before the preceding kernel
     (here the conv front end, then another layer's recurrence) finishes; results equal
