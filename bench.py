@@ -63,53 +63,94 @@ def tensor_peak():
         return 1590.0, "fallback"
 
 
+def tensor_peak_sustained():
+    """Dense bf16 TFLOP/s held for seconds under the power cap (a kernel timed in a long loop)."""
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 1400.0, "fallback"
+
+
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled during the timed region.
+
+    One streaming ``nvidia-smi --query-gpu ... -lms 100`` process is started on
+    entry and ``__enter__`` returns only after its first line has arrived, so the
+    sampler is running before the caller starts timing.  ``mark_start`` /
+    ``mark_end`` bracket the timed region on the host clock (call them after the
+    synchronize on each side); the summary keeps the samples whose arrival time
+    lies inside that window, and says how many there were.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 100
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
-        self.samples = []
-        self._stop = threading.Event()
+        self.samples = []  # (host time, fields)
+        self._proc = None
         self._t = None
+        self._first = threading.Event()
+        self.t0 = self.t1 = None
 
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                     timeout=5).stdout.strip()
-                if out:
-                    self.samples.append([x.strip() for x in out.split(",")])
-            except Exception:
-                pass
-            self._stop.wait(0.2)
+    def _read(self):
+        for line in self._proc.stdout:
+            line = line.strip()
+            if line:
+                self.samples.append((time.perf_counter(), [x.strip() for x in line.split(",")]))
+                self._first.set()
+        self._first.set()
 
     def __enter__(self):
-        self._t = threading.Thread(target=self._run, daemon=True)
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 f"-lms={self.INTERVAL_MS}"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self._proc = None
+            return self
+        self._t = threading.Thread(target=self._read, daemon=True)
         self._t.start()
+        self._first.wait(timeout=10)
         return self
 
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
+
     def __exit__(self, *exc):
-        self._stop.set()
-        self._t.join(timeout=10)
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=10)
+            except Exception:
+                self._proc.kill()
+            self._t.join(timeout=10)
 
     def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        smax = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        inside = [f for t, f in self.samples
+                  if self.t0 is not None and self.t1 is not None and self.t0 <= t <= self.t1]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0,
+                    "window_ms": None if self.t0 is None or self.t1 is None else (self.t1 - self.t0) * 1e3}
+        sm = [float(s[1]) for s in inside if s[1].replace(".", "").isdigit()]
+        smax = [float(s[2]) for s in inside if s[2].replace(".", "").isdigit()]
+        power = [float(s[3]) for s in inside if s[3].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = set()
-        for s in self.samples:
+        for s in inside:
             for n, v in zip(names, s[5:9]):
                 if v.strip().lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(self.samples)}
+                "power_w": float(np.median(power)) if power else None, "reasons": sorted(reasons),
+                "samples": len(inside), "window_ms": (self.t1 - self.t0) * 1e3}
 
 
 # --------------------------------------------------------------------------- #
@@ -159,6 +200,9 @@ def cpu_baseline(budget_s: float = 12.0):
                       f"scaled x{N_LAYERS / n:g} to 10 layers; C restatement of the ggml CPU nodes"}
 
 
+REF_BUDGET_S = 30.0
+
+
 def run_reference(args, rank: int):
     if rank != 0:
         return None
@@ -167,18 +211,25 @@ def run_reference(args, rank: int):
     oracle.build()
     cores = oracle.set_threads(os.cpu_count() or 1)
     kq, vq, q, gate = cpu_layer_inputs(N_KV)
-    for _ in range(args.warmup):
+    for _ in range(min(args.warmup, 3)):
         cpu_layer(kq, vq, q, gate, N_KV)
+    # A CPU layer takes ~0.1 s on 16 cores: the timed steps stop after REF_BUDGET_S so
+    # that a large --steps (the GPU arm's default) still ends within a minute.
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    n = 0
+    while n < args.steps:
         cpu_layer(kq, vq, q, gate, N_KV)  # one of the 10 layers per step
-    per_layer = (time.perf_counter() - t0) / args.steps
+        n += 1
+        if time.perf_counter() - t0 > REF_BUDGET_S:
+            break
+    per_layer = (time.perf_counter() - t0) / n
     v = per_layer * N_LAYERS * 1e6
     sample = (f"each step = 1 of the 10 layers (172032 q4_0 keys, dequant + RoPE + attention + gate) "
-              f"on {cores} threads, scaled x10; C restatement of the ggml CPU nodes "
+              f"on {cores} threads, scaled x10; {n} of {args.steps} requested steps timed "
+              f"(stopped after {REF_BUDGET_S:g} s); C restatement of the ggml CPU nodes "
               "(ggml itself is not in this image)")
     return {"metric": METRIC, "value": v, "unit": "us/token", "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * 1e3,
+            "steps": args.steps, "timed_steps": n, "warmup": args.warmup, "ms_per_step": per_layer * 1e3,
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic N(0,1), seed 0",
             "config": {"workload": "config3: decode, 10 layers x 172032 q4_0 keys, 16/2 heads, d=256, n_q=1"},
@@ -311,11 +362,13 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             dist.barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
+        sampler.mark_start()
         e0.record()
         for _ in range(args.steps):
             run()
         e1.record()
         torch.cuda.synchronize()
+        sampler.mark_end()
         ms = e0.elapsed_time(e1)
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -480,6 +533,7 @@ def bench_prefill(steps: int, warmup: int):
     g.manual_seed(11)
     res = {}
     peak, peak_kind = tensor_peak()
+    peak_sus, _ = tensor_peak_sustained()
     for T in (512, 2048):
         n_kv = PF_PREFIX + T
         cap = (n_kv + 255) // 256 * 256
@@ -519,12 +573,16 @@ def bench_prefill(steps: int, warmup: int):
         tflops = flops / us / 1e6
         res[f"pp{T}"] = {"us": us, "tok_s": T / us * 1e6, "tflops": tflops,
                          "frac_of_measured_bf16_peak": tflops / peak if peak else None,
-                         "flops": flops}
+                         "frac_of_measured_bf16_sustained": tflops / peak_sus,
+                         "timed_ms": us * reps / 1e3, "flops": flops}
         del kc, vc, ws
     res["config"] = "config2: 1 layer, prefix 32768 q4_0 keys, T new tokens appended (q4_0, RoPE) then " \
                     "causal GQA attention with sigmoid gate; Q bf16; flops = 4*256*16*sum_t(prefix+t+1)"
     res["peak_tflops"] = peak
     res["peak_kind"] = peak_kind
+    res["peak_tflops_sustained"] = peak_sus
+    res["peak_note"] = ("burst peak for a short timed loop, sustained peak (seconds of dense bf16 under the "
+                        "1 kW power cap) once timed_ms reaches about a second")
     return res
 
 
@@ -883,7 +941,7 @@ def run_profile_case(case: str):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="sqmix", choices=["sqmix", "reference"])
     ap.add_argument("--no-graph", action="store_true")
