@@ -68,6 +68,23 @@ const char *sqmix_last_error(void);
 /* Number of SMs of `device` (sizes split-KV grids). */
 int sqmix_device_sm_count(int device);
 
+/* ---- ABI layout table ----------------------------------------------------
+ * Size, field count and field byte offsets (declaration order) of the argument
+ * structs below, as compiled into the library, so that a binding in another language
+ * can check its own declaration of them (the role of the ggml header guard in
+ * src/backend/ffi.rs:516-588).  Unknown `which`: size 0, count -1; a field index out
+ * of range: offset -1. */
+#define SQMIX_ABI_KV_APPEND_ARGS 1
+#define SQMIX_ABI_FA_ARGS 2
+#define SQMIX_ABI_FA_BATCH_ARGS 3
+#define SQMIX_ABI_PEER_MERGE_ARGS 4
+#define SQMIX_ABI_GDN_ARGS 5
+#define SQMIX_ABI_GDN_CONV_ARGS 6
+#define SQMIX_ABI_HEAD_NORM_ARGS 7
+size_t sqmix_abi_struct_size(int32_t which);
+int32_t sqmix_abi_field_count(int32_t which);
+int64_t sqmix_abi_field_offset(int32_t which, int32_t field);
+
 /* ========================================================================
  * q4_0 KV cache: tiled layout
  *

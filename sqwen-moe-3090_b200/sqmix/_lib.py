@@ -25,6 +25,15 @@ SQMIX_F16 = 1
 SQMIX_BF16 = 30
 SQMIX_FA_OVERLAP_PREV = 1
 
+# struct ids of the library's ABI layout table (sqmix_abi_struct_size & co.)
+SQMIX_ABI_KV_APPEND_ARGS = 1
+SQMIX_ABI_FA_ARGS = 2
+SQMIX_ABI_FA_BATCH_ARGS = 3
+SQMIX_ABI_PEER_MERGE_ARGS = 4
+SQMIX_ABI_GDN_ARGS = 5
+SQMIX_ABI_GDN_CONV_ARGS = 6
+SQMIX_ABI_HEAD_NORM_ARGS = 7
+
 ERROR_NAMES = {
     SQMIX_EINVAL: "SQMIX_EINVAL",
     SQMIX_ECUDA: "SQMIX_ECUDA",
@@ -129,6 +138,9 @@ _SIGNATURES = {
     "sqmix_version": (ctypes.c_char_p, []),
     "sqmix_last_error": (ctypes.c_char_p, []),
     "sqmix_device_sm_count": (ctypes.c_int, [ctypes.c_int]),
+    "sqmix_abi_struct_size": (c_size_t, [c_int32]),
+    "sqmix_abi_field_count": (c_int32, [c_int32]),
+    "sqmix_abi_field_offset": (c_int64, [c_int32, c_int32]),
     "sqmix_kv_cache_bytes": (c_size_t, [c_int64]),
     "sqmix_kv_append_q4_0": (ctypes.c_int, [ctypes.POINTER(KvAppendArgs), c_void_p]),
     "sqmix_kv_convert_rows": (ctypes.c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32,

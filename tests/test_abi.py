@@ -187,3 +187,63 @@ def test_kvcache_rejects_bad_shapes(sqmix_lib):
     h = ctypes.c_void_p()
     assert L.sqmix_kvcache_create(0, 100, -1, ctypes.byref(h)) == sqmix_lib.SQMIX_EINVAL
     assert L.sqmix_kvcache_create(1, 0, -1, ctypes.byref(h)) == sqmix_lib.SQMIX_EINVAL
+
+
+def header_struct_fields():
+    """Field names of every `typedef struct X {...} X;` in sqmix.h, in order."""
+    text = open(HEADER).read()
+    out = {}
+    for m in re.finditer(r"typedef struct (\w+) \{(.*?)\} \w+;", text, re.S):
+        body = re.sub(r"/\*.*?\*/", "", m.group(2), flags=re.S)
+        out[m.group(1)] = [re.findall(r"(\w+)\s*$", d.strip())[0] for d in body.split(";") if d.strip()]
+    return out
+
+
+def _abi_structs():
+    from sqmix import _lib as L
+
+    return {
+        "sqmix_kv_append_args": (L.SQMIX_ABI_KV_APPEND_ARGS, L.KvAppendArgs),
+        "sqmix_fa_args": (L.SQMIX_ABI_FA_ARGS, L.FaArgs),
+        "sqmix_fa_batch_args": (L.SQMIX_ABI_FA_BATCH_ARGS, L.FaBatchArgs),
+        "sqmix_peer_merge_args": (L.SQMIX_ABI_PEER_MERGE_ARGS, L.PeerMergeArgs),
+        "sqmix_gdn_args": (L.SQMIX_ABI_GDN_ARGS, L.GdnArgs),
+        "sqmix_gdn_conv_args": (L.SQMIX_ABI_GDN_CONV_ARGS, L.GdnConvArgs),
+        "sqmix_head_norm_args": (L.SQMIX_ABI_HEAD_NORM_ARGS, L.HeadNormArgs),
+    }
+
+
+def test_abi_layout_table_matches_ctypes_mirror(sqmix_lib):
+    """Every argument struct: the library's compiled size, field count and offsets equal
+    the ctypes declaration's, and the ctypes field names follow the header's order.  A
+    field added to one side only fails here."""
+    L = sqmix_lib.lib()
+    hdr = header_struct_fields()
+    structs = _abi_structs()
+    assert set(structs) == set(hdr), "every struct of sqmix.h needs an ABI table entry and a ctypes mirror"
+    for name, (which, cls) in structs.items():
+        names = [f[0] for f in cls._fields_]
+        assert names == hdr[name], name
+        assert L.sqmix_abi_struct_size(which) == ctypes.sizeof(cls), name
+        assert L.sqmix_abi_field_count(which) == len(cls._fields_), name
+        for i, (fname, _) in enumerate(cls._fields_):
+            assert L.sqmix_abi_field_offset(which, i) == getattr(cls, fname).offset, (name, fname)
+        assert L.sqmix_abi_field_offset(which, len(cls._fields_)) == -1
+    assert L.sqmix_abi_struct_size(0) == 0 and L.sqmix_abi_field_count(99) == -1
+
+
+def test_integration_guide_rust_structs_match_header():
+    """The Rust #[repr(C)] structs in INTEGRATION.md declare the same fields, in the same
+    order, as sqmix.h (a binding copied from the guide must not be shorter than the C
+    struct the library reads)."""
+    guide = open(os.path.join(REPO, "INTEGRATION.md")).read()
+    hdr = header_struct_fields()
+    rust = {}
+    for m in re.finditer(r"pub struct (\w+) \{\n(.*?)\n\}", guide, re.S):
+        rust[m.group(1)] = re.findall(r"pub (\w+):", m.group(2))
+    for cname, fields in hdr.items():
+        rname = "".join(w.capitalize() for w in cname.split("_"))
+        assert rname in rust, f"INTEGRATION.md declares no {rname}"
+        assert rust[rname] == fields, rname
+    for name in declared_functions():
+        assert f"pub fn {name}(" in guide, f"INTEGRATION.md's extern block lacks {name}"
