@@ -10,8 +10,12 @@ reference's shapes (no model weights are involved in the mixer).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sqmix|reference]
 
 N > 1 (under torchrun): the 172032 keys of every layer are split across the ranks;
-each rank attends over its slice and the (O, LSE) partials are all-gathered over
-NCCL and merged before the gate (strong scaling: total work fixed).
+each rank attends over its slice and the ranks exchange their (O, LSE) partials over
+NVLink peer memory and merge them before the gate, one kernel per layer (strong
+scaling: total work fixed); NCCL only forms the process group and swaps the peer
+buffers' IPC handles (an NCCL all-gather of the partials is kept behind --nccl-merge).
+Rank 0 then checks layers 0 and 9 of the split result against a single-GPU decode over
+the whole cache.  Config 4 (the 64-sequence mixer stack) is sharded by sequence.
 
 Prints one JSON line (rank 0).
 """
@@ -74,48 +78,93 @@ def tensor_peak_sustained():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region.
+    """SM clocks, power and clock-event (throttle) reasons sampled DURING the timed region.
 
-    One streaming ``nvidia-smi --query-gpu ... -lms 100`` process is started on
-    entry and ``__enter__`` returns only after its first line has arrived, so the
-    sampler is running before the caller starts timing.  ``mark_start`` /
-    ``mark_end`` bracket the timed region on the host clock (call them after the
-    synchronize on each side); the summary keeps the samples whose arrival time
-    lies inside that window, and says how many there were.
+    A thread polls NVML (read-only queries: nvmlDeviceGetClockInfo, ...MaxClockInfo,
+    ...PowerUsage, ...CurrentClocksEventReasons) about every 2 ms for the GPU this rank
+    runs on (matched by UUID, so CUDA_VISIBLE_DEVICES remapping does not matter), so even
+    a few-millisecond timed window holds samples.  Without NVML it falls back to one
+    streaming ``nvidia-smi -lms 100``.  ``mark_start`` / ``mark_end`` bracket the timed
+    region on the host clock (after the synchronize on each side); the summary keeps the
+    samples taken inside that window.
     """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-    INTERVAL_MS = 100
+    POLL_S = 0.002
+    # NVML clock-event reason bits reported by name
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.samples = []  # (host time, fields)
-        self._proc = None
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.samples = []  # (host time, sm_mhz, max_mhz, power_w, set of reasons)
+        self._stop = threading.Event()
         self._t = None
-        self._first = threading.Event()
+        self._proc = None
+        self.source = None
         self.t0 = self.t1 = None
 
-    def _read(self):
+    def _uuid(self):
+        import torch
+
+        try:
+            u = str(torch.cuda.get_device_properties(self.dev).uuid)
+            return u if u.startswith("GPU-") else "GPU-" + u
+        except Exception:
+            return None
+
+    def _poll_nvml(self, nv, h):
+        while not self._stop.is_set():
+            try:
+                t = time.perf_counter()
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                rs = {n for n, b in self.REASON_BITS.items() if bits & b}
+                self.samples.append((t, float(sm), float(mx), pw, rs))
+            except Exception:
+                pass
+            time.sleep(self.POLL_S)
+
+    def _read_smi(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self._proc.stdout:
-            line = line.strip()
-            if line:
-                self.samples.append((time.perf_counter(), [x.strip() for x in line.split(",")]))
-                self._first.set()
-        self._first.set()
+            f = [x.strip() for x in line.strip().split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rs = {n for n, v in zip(names, f[5:9]) if v.lower() == "active"}
+                self.samples.append((time.perf_counter(), float(f[1]), float(f[2]), float(f[3]), rs))
+            except ValueError:
+                continue
 
     def __enter__(self):
+        uuid = self._uuid()
         try:
-            self._proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 f"-lms={self.INTERVAL_MS}"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByUUID(uuid) if uuid else nv.nvmlDeviceGetHandleByIndex(self.dev)
+            self._t = threading.Thread(target=self._poll_nvml, args=(nv, h), daemon=True)
+            self.source = "nvml"
+            self._t.start()
         except Exception:
-            self._proc = None
-            return self
-        self._t = threading.Thread(target=self._read, daemon=True)
-        self._t.start()
-        self._first.wait(timeout=10)
+            try:
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={uuid or self.dev}", f"--query-gpu={self.FIELDS}",
+                     "--format=csv,noheader,nounits", "-lms=100"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self._t = threading.Thread(target=self._read_smi, daemon=True)
+                self.source = "nvidia-smi"
+                self._t.start()
+            except Exception:
+                return self
+        t_wait = time.perf_counter()
+        while not self.samples and time.perf_counter() - t_wait < 10:
+            time.sleep(0.005)
         return self
 
     def mark_start(self):
@@ -125,121 +174,329 @@ class ClockSampler:
         self.t1 = time.perf_counter()
 
     def __exit__(self, *exc):
+        self._stop.set()
         if self._proc is not None:
             self._proc.terminate()
             try:
                 self._proc.wait(timeout=10)
             except Exception:
                 self._proc.kill()
+        if self._t is not None:
             self._t.join(timeout=10)
 
     def summary(self):
-        inside = [f for t, f in self.samples
-                  if self.t0 is not None and self.t1 is not None and self.t0 <= t <= self.t1]
+        inside = [s for s in self.samples
+                  if self.t0 is not None and self.t1 is not None and self.t0 <= s[0] <= self.t1]
+        window = None if self.t0 is None or self.t1 is None else (self.t1 - self.t0) * 1e3
         if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0,
-                    "window_ms": None if self.t0 is None or self.t1 is None else (self.t1 - self.t0) * 1e3}
-        sm = [float(s[1]) for s in inside if s[1].replace(".", "").isdigit()]
-        smax = [float(s[2]) for s in inside if s[2].replace(".", "").isdigit()]
-        power = [float(s[3]) for s in inside if s[3].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+                    "window_ms": window, "source": self.source}
         reasons = set()
         for s in inside:
-            for n, v in zip(names, s[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "power_w": float(np.median(power)) if power else None, "reasons": sorted(reasons),
-                "samples": len(inside), "window_ms": (self.t1 - self.t0) * 1e3}
+            reasons |= s[4]
+        return {"sm_mhz": float(np.median([s[1] for s in inside])), "sm_max_mhz": max(s[2] for s in inside),
+                "power_w": float(np.median([s[3] for s in inside])), "reasons": sorted(reasons),
+                "samples": len(inside), "window_ms": window, "source": self.source}
+
+
+def timed_window(fn, steps: int, device_index: int, world: int = 1):
+    """Run fn `steps` times between CUDA events (barrier + synchronize on both sides for
+    N > 1) with the clock sampler running; returns (device ms, clock summary).  The caller
+    takes the maximum over ranks."""
+    import torch
+
+    sampler = ClockSampler(device_index)
+    with sampler:
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        sampler.mark_start()
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        sampler.mark_end()
+    return e0.elapsed_time(e1), sampler.summary()
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 # --------------------------------------------------------------------------- #
 # CPU legs (oracle): cpu_baseline and --impl reference                          #
 # --------------------------------------------------------------------------- #
 
-def cpu_layer_inputs(n_kv: int, seed: int = 0):
-    import oracle
-
-    rng = np.random.default_rng(seed)
-    k = rng.standard_normal((n_kv, 512), dtype=np.float32)
-    v = rng.standard_normal((n_kv, 512), dtype=np.float32)
-    kq = oracle.q4_0_quantize(k)
-    vq = oracle.q4_0_quantize(v)
-    q = rng.standard_normal((1, N_HEAD, HEAD_DIM), dtype=np.float32)
-    gate = rng.standard_normal((1, N_HEAD, HEAD_DIM), dtype=np.float32)
-    return kq, vq, q, gate
+CPU_KIND = "port"
+CPU_NOTE = ("C restatement of ggml-cpu's execution of these nodes (oracle/cpu_ggml.c: q8_0 Q x q4_0 K integer "
+            "dots, f32 online softmax, per-key V dequant, rows split across threads); ggml itself is not in this "
+            "image")
 
 
-def cpu_layer(kq, vq, q, gate, n_kv):
-    """One layer on the CPU restatement: dequantise the q4_0 cache, RoPE Q, attend."""
-    import oracle
-
-    kd = oracle.q4_0_dequantize(kq, 512).reshape(n_kv, N_HEAD_KV, HEAD_DIM)
-    vd = oracle.q4_0_dequantize(vq, 512).reshape(n_kv, N_HEAD_KV, HEAD_DIM)
-    qr = oracle.rope_text(q, n_kv - 1, FREQ_BASE, N_ROT)
-    return oracle.attn(qr, kd, vd, gate, q_pos0=n_kv - 1, scale=1.0 / 16)
-
-
-def cpu_baseline(budget_s: float = 12.0):
+def cpu_setup():
     import oracle
 
     oracle.build()
-    cores = oracle.set_threads(os.cpu_count() or 1)
-    kq, vq, q, gate = cpu_layer_inputs(N_KV)
-    cpu_layer(kq, vq, q, gate, N_KV)  # warm
+    return oracle, oracle.set_threads(os.cpu_count() or 1)
+
+
+def cpu_kv_rows(n_kv: int, seed: int):
+    """q4_0 K and V caches in ggml row layout ([n_kv][288] bytes each) of N(0,1) values."""
+    import oracle
+
+    rng = np.random.default_rng(seed)
+    kq = np.empty((n_kv, 288), dtype=np.uint8)
+    vq = np.empty((n_kv, 288), dtype=np.uint8)
+    for a in range(0, n_kv, 32768):
+        n = min(32768, n_kv - a)
+        kq[a:a + n] = oracle.q4_0_quantize(rng.standard_normal((n, 512), dtype=np.float32))
+        vq[a:a + n] = oracle.q4_0_quantize(rng.standard_normal((n, 512), dtype=np.float32))
+    return kq, vq
+
+
+def cpu_decode_layer(oracle, kq, vq, q, gate, k_new, v_new, n_kv):
+    """One full-attention decode layer of one token the way ggml-cpu runs it: the append
+    (RoPE on K, quantize_row_q4_0 of the new row), RoPE on Q, flash attention over the
+    q4_0 cache, sigmoid gate."""
+    pos = n_kv - 1
+    kq[pos] = oracle.q4_0_quantize(oracle.rope_text(k_new, pos, FREQ_BASE, N_ROT).reshape(1, 512))[0]
+    vq[pos] = oracle.q4_0_quantize(v_new.reshape(1, 512))[0]
+    qr = oracle.rope_text(q, pos, FREQ_BASE, N_ROT)
+    return oracle.cpu_fa_q4_0(qr, kq[:n_kv], vq[:n_kv], gate, q_pos0=pos, scale=1.0 / 16)
+
+
+def cpu_decode_inputs(seed: int):
+    rng = np.random.default_rng(seed)
+    return (rng.standard_normal((1, N_HEAD, HEAD_DIM), dtype=np.float32),
+            rng.standard_normal((1, N_HEAD, HEAD_DIM), dtype=np.float32),
+            rng.standard_normal((1, N_HEAD_KV, HEAD_DIM), dtype=np.float32),
+            rng.standard_normal((1, N_HEAD_KV, HEAD_DIM), dtype=np.float32))
+
+
+def cpu_baseline_config3(budget_s: float = 12.0):
+    """Config 3 on the host cores: the 10 layers of one decode token (172032 keys each)."""
+    oracle, cores = cpu_setup()
+    kq, vq = cpu_kv_rows(N_KV, 0)
+    q, gate, kn, vn = cpu_decode_inputs(1)
+    cpu_decode_layer(oracle, kq, vq, q, gate, kn, vn, N_KV)  # warm
     t0 = time.perf_counter()
     n = 0
-    while True:
-        cpu_layer(kq, vq, q, gate, N_KV)
+    while n < N_LAYERS and (n == 0 or time.perf_counter() - t0 < budget_s):
+        cpu_decode_layer(oracle, kq, vq, q, gate, kn, vn, N_KV)
         n += 1
-        if time.perf_counter() - t0 > budget_s or n >= N_LAYERS:
-            break
     per_layer = (time.perf_counter() - t0) / n
-    return {"value": per_layer * N_LAYERS * 1e6, "unit": "us/token", "cores": cores, "kind": "port",
-            "sample": f"{n} layer(s) of 172032 q4_0 keys (dequant + RoPE + attention + gate), "
-                      f"scaled x{N_LAYERS / n:g} to 10 layers; C restatement of the ggml CPU nodes"}
+    return {"value": per_layer * N_LAYERS * 1e6, "unit": "us/token", "cores": cores, "kind": CPU_KIND,
+            "sample": f"{n} of the 10 layers (172032 q4_0 keys: append + RoPE + attention + gate), scaled to 10 "
+                      f"layers; {CPU_NOTE}"}
+
+
+def cpu_baseline_config0():
+    """Config 0 on the host cores: one decode layer over 4096 q4_0 keys."""
+    oracle, cores = cpu_setup()
+    n_kv = 4096
+    kq, vq = cpu_kv_rows(n_kv, 2)
+    q, gate, kn, vn = cpu_decode_inputs(3)
+    cpu_decode_layer(oracle, kq, vq, q, gate, kn, vn, n_kv)
+    reps, t0 = 0, time.perf_counter()
+    while reps < 20 or time.perf_counter() - t0 < 1.0:
+        cpu_decode_layer(oracle, kq, vq, q, gate, kn, vn, n_kv)
+        reps += 1
+    us = (time.perf_counter() - t0) / reps * 1e6
+    return {"value": us, "unit": "us/layer-token", "cores": cores, "kind": CPU_KIND,
+            "sample": f"{reps} decode layers of 4096 q4_0 keys (append + RoPE + attention + gate); {CPU_NOTE}"}
+
+
+def cpu_gdn_inputs(rng, T: int):
+    import oracle
+
+    S = (rng.standard_normal((32, 128, 128)) * 0.02).astype(np.float32)
+    q = oracle.l2norm(rng.standard_normal((T, 16, 128)).astype(np.float32))
+    k = oracle.l2norm(rng.standard_normal((T, 16, 128)).astype(np.float32))
+    v = rng.standard_normal((T, 32, 128)).astype(np.float32)
+    a_log = rng.uniform(0.0, 2.7, 32)
+    dt_bias = rng.standard_normal(32)
+    g = (-np.exp(a_log) * np.log1p(np.exp(rng.standard_normal((T, 32)) + dt_bias))).astype(np.float32)
+    beta = (1.0 / (1.0 + np.exp(-rng.standard_normal((T, 32))))).astype(np.float32)
+    return S, q, k, v, g, beta
+
+
+def cpu_baseline_config1():
+    """Config 1 on the host cores: GDN decode (one token) and the 512-token prefill, f32
+    token by token (ggml-cpu's gated_delta_net has no chunked form)."""
+    oracle, cores = cpu_setup()
+    rng = np.random.default_rng(4)
+    S, q, k, v, g, beta = cpu_gdn_inputs(rng, 1)
+    oracle.cpu_gdn_f32(q, k, v, g, beta, S)
+    reps, t0 = 0, time.perf_counter()
+    while reps < 50 or time.perf_counter() - t0 < 1.0:
+        oracle.cpu_gdn_f32(q, k, v, g, beta, S)
+        reps += 1
+    dec_us = (time.perf_counter() - t0) / reps * 1e6
+    S, q, k, v, g, beta = cpu_gdn_inputs(rng, 512)
+    t0 = time.perf_counter()
+    oracle.cpu_gdn_f32(q, k, v, g, beta, S)
+    pf_us = (time.perf_counter() - t0) * 1e6
+    return {"decode": {"value": dec_us, "unit": "us/layer-token"},
+            "prefill512": {"value": pf_us, "unit": "us/layer", "tok_s": 512 / pf_us * 1e6},
+            "cores": cores, "kind": CPU_KIND,
+            "sample": f"{reps} single-token updates of the [32][128][128] f32 state, then one 512-token pass; "
+                      "C restatement of the gated delta rule in f32 (oracle/cpu_ggml.c)"}
+
+
+def cpu_baseline_config2(n_sample: int = 16):
+    """Config 2 on the host cores: pp512 / pp2048 after a 32768-token prefix.  A bounded
+    sample of query tokens spread over the chunk (each token's cost grows with its
+    position) is timed and scaled to the chunk, plus the q4_0 append of the chunk's rows."""
+    oracle, cores = cpu_setup()
+    res = {}
+    for T in (512, 2048):
+        n_kv = PF_PREFIX + T
+        kq, vq = cpu_kv_rows(n_kv, 5 + T)
+        rng = np.random.default_rng(6 + T)
+        kn = rng.standard_normal((T, 2, 256), dtype=np.float32)
+        vn = rng.standard_normal((T, 2, 256), dtype=np.float32)
+        q = rng.standard_normal((T, N_HEAD, HEAD_DIM), dtype=np.float32)
+        gate = rng.standard_normal((T, N_HEAD, HEAD_DIM), dtype=np.float32)
+        t0 = time.perf_counter()
+        kq[PF_PREFIX:] = oracle.q4_0_quantize(oracle.rope_text(kn, PF_PREFIX, FREQ_BASE, N_ROT).reshape(T, 512))
+        vq[PF_PREFIX:] = oracle.q4_0_quantize(vn.reshape(T, 512))
+        qr = oracle.rope_text(q, PF_PREFIX, FREQ_BASE, N_ROT)
+        t_append = time.perf_counter() - t0
+        picks = np.linspace(0, T - 1, n_sample).astype(int)
+        t0 = time.perf_counter()
+        for t in picks:
+            oracle.cpu_fa_q4_0(qr[t:t + 1], kq, vq, gate[t:t + 1], q_pos0=PF_PREFIX + t, scale=1.0 / 16)
+        t_attn = (time.perf_counter() - t0) / n_sample * T
+        us = (t_append + t_attn) * 1e6
+        res[f"pp{T}"] = {"value": us, "unit": "us/chunk", "tok_s": T / us * 1e6}
+    res.update({"cores": cores, "kind": CPU_KIND,
+                "sample": f"{n_sample} query tokens spread over each chunk (16 head rows each, all threads), "
+                          f"scaled to the chunk, plus the chunk's append; {CPU_NOTE}"})
+    return res
+
+
+def cpu_baseline_config4(lens):
+    """Config 4 on the host cores: one sequence of the batch (the one at the median KV
+    length) through all 40 layers (10 attention decode layers + 30 GDN updates), scaled to
+    the batch by the sum of KV lengths (attention) and the sequence count (GDN)."""
+    oracle, cores = cpu_setup()
+    L = int(np.median(lens))
+    kq, vq = cpu_kv_rows(L + 1, 7)
+    q, gate, kn, vn = cpu_decode_inputs(8)
+    rng = np.random.default_rng(9)
+    S, gq, gk, gv, gg, gb = cpu_gdn_inputs(rng, 1)
+    cpu_decode_layer(oracle, kq, vq, q, gate, kn, vn, L + 1)
+    t0 = time.perf_counter()
+    for _ in range(10):
+        cpu_decode_layer(oracle, kq, vq, q, gate, kn, vn, L + 1)
+    t_fa = (time.perf_counter() - t0) / 10
+    t0 = time.perf_counter()
+    for _ in range(30):
+        oracle.cpu_gdn_f32(gq, gk, gv, gg, gb, S)
+    t_gdn = (time.perf_counter() - t0) / 30
+    n_seqs = len(lens)
+    us = (10 * t_fa * float(sum(int(n) + 1 for n in lens)) / (L + 1) + 30 * t_gdn * n_seqs) * 1e6
+    return {"value": us, "unit": "us/step", "tok_s": n_seqs / us * 1e6, "cores": cores, "kind": CPU_KIND,
+            "sample": f"one sequence (KV length {L}) through 10 attention + 30 GDN decode layers, scaled to the "
+                      f"{n_seqs}-sequence batch; {CPU_NOTE}"}
 
 
 REF_BUDGET_S = 30.0
 
 
 def run_reference(args, rank: int):
+    """--impl reference: config 3 on the host cores with the ggml-cpu restatement; each
+    step is one decode token through all 10 layers (append, RoPE, attention, gate), the
+    timed steps stopping after REF_BUDGET_S whatever --steps asks."""
     if rank != 0:
         return None
-    import oracle
+    oracle, cores = cpu_setup()
+    kqs, vqs = [], []
+    for l in range(N_LAYERS):
+        kq, vq = cpu_kv_rows(N_KV, 100 + l)
+        kqs.append(kq)
+        vqs.append(vq)
+    q, gate, kn, vn = cpu_decode_inputs(1)
 
-    oracle.build()
-    cores = oracle.set_threads(os.cpu_count() or 1)
-    kq, vq, q, gate = cpu_layer_inputs(N_KV)
+    def step():
+        for l in range(N_LAYERS):
+            cpu_decode_layer(oracle, kqs[l], vqs[l], q, gate, kn, vn, N_KV)
+
     for _ in range(min(args.warmup, 3)):
-        cpu_layer(kq, vq, q, gate, N_KV)
-    # A CPU layer takes ~0.1 s on 16 cores: the timed steps stop after REF_BUDGET_S so
-    # that a large --steps (the GPU arm's default) still ends within a minute.
+        step()
     t0 = time.perf_counter()
     n = 0
     while n < args.steps:
-        cpu_layer(kq, vq, q, gate, N_KV)  # one of the 10 layers per step
+        step()
         n += 1
         if time.perf_counter() - t0 > REF_BUDGET_S:
             break
-    per_layer = (time.perf_counter() - t0) / n
-    v = per_layer * N_LAYERS * 1e6
-    sample = (f"each step = 1 of the 10 layers (172032 q4_0 keys, dequant + RoPE + attention + gate) "
-              f"on {cores} threads, scaled x10; {n} of {args.steps} requested steps timed "
-              f"(stopped after {REF_BUDGET_S:g} s); C restatement of the ggml CPU nodes "
-              "(ggml itself is not in this image)")
+    per_step = (time.perf_counter() - t0) / n
+    v = per_step * 1e6
+    sample = (f"each step = one decode token through all 10 layers (172032 q4_0 keys each: append + RoPE + "
+              f"attention + gate) on {cores} threads; {n} of {args.steps} requested steps timed (stopped after "
+              f"{REF_BUDGET_S:g} s); {CPU_NOTE}")
     return {"metric": METRIC, "value": v, "unit": "us/token", "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "timed_steps": n, "warmup": args.warmup, "ms_per_step": per_layer * 1e3,
-            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic N(0,1), seed 0",
-            "config": {"workload": "config3: decode, 10 layers x 172032 q4_0 keys, 16/2 heads, d=256, n_q=1"},
-            "cpu_baseline": {"value": v, "unit": "us/token", "cores": cores, "kind": "port", "sample": sample},
+            "steps": args.steps, "timed_steps": n, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "q4_0 KV, q8_0 Q, f32",
+            "data": "synthetic N(0,1), seeded", "same_config": True,
+            "config": {"workload": "config3: decode 1 token, 10 full-attn layers x 172032 q4_0 keys, 16 Q / 2 KV "
+                                   "heads, d=256, RoPE 64/1e7, sigmoid gate"},
+            "cpu_baseline": {"value": v, "unit": "us/token", "cores": cores, "kind": CPU_KIND, "sample": sample},
             "e2e": {"value": v, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 # --------------------------------------------------------------------------- #
 # GPU arm                                                                       #
 # --------------------------------------------------------------------------- #
+
+KV_CHUNK = 1024  # keys per seeded chunk of the synthetic caches
+
+
+def kv_seed(layer: int, chunk: int) -> int:
+    return 1_000_003 * (layer + 1) + chunk
+
+
+def fill_kv_slice(layer: int, start: int, length: int, kc, vc, cap: int, dev):
+    """Rows [0, length) of the tiled caches (kc, vc) <- keys [start, start + length) of
+    `layer`, N(0,1) quantised to q4_0 by the append kernel with K rotated at its absolute
+    position.  Every KV_CHUNK-key chunk of the sequence has its own seed, so the slices
+    held by any number of ranks are the keys of one whole-sequence cache."""
+    import torch
+
+    import sqmix
+
+    block = 16384
+    g = torch.Generator(device=dev)
+    for b0 in range(start, start + length, block):
+        n = min(block, start + length - b0)
+        kk = torch.empty((n, N_HEAD_KV, HEAD_DIM), device=dev)
+        vv = torch.empty((n, N_HEAD_KV, HEAD_DIM), device=dev)
+        c = b0 // KV_CHUNK * KV_CHUNK
+        while c < b0 + n:
+            g.manual_seed(kv_seed(layer, c // KV_CHUNK))
+            ck = torch.randn((KV_CHUNK, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+            cv = torch.randn((KV_CHUNK, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+            lo, hi = max(c, b0), min(c + KV_CHUNK, b0 + n)
+            kk[lo - b0:hi - b0] = ck[lo - c:hi - c]
+            vv[lo - b0:hi - b0] = cv[lo - c:hi - c]
+            c += KV_CHUNK
+        rows = torch.arange(b0 - start, b0 - start + n, device=dev)
+        sqmix.set_rows_q4_0(kk, vv, rows, kc, vc, cap, rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE,
+                            rope_pos_offset=start)
+
 
 def run_gpu(args, rank: int, world: int, local_rank: int):
     import torch
@@ -254,29 +511,19 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     shard = split_kv.plan(N_KV, world, rank)  # this rank's contiguous key slice
     n_local, k0 = shard.length, shard.start
     cap = shard.capacity
-    g = torch.Generator(device=dev)
-    g.manual_seed(1234 + rank)
 
     # ---- resident state: 10 layers of q4_0 K/V for this rank's key slice ------
     kv = sqmix.KvCache(n_layers=N_LAYERS, kv_cap=cap, device=local_rank)
     kc = [kv.k_state(l) for l in range(N_LAYERS)]
     vc = [kv.v_state(l) for l in range(N_LAYERS)]
-    chunk = 16384
     for l in range(N_LAYERS):
-        for a in range(0, n_local, chunk):
-            n = min(chunk, n_local - a)
-            kk = torch.randn((n, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
-            vv = torch.randn((n, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
-            rows = torch.arange(a, a + n, device=dev)
-            sqmix.set_rows_q4_0(kk, vv, rows, kc[l], vc[l], cap, rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE,
-                                rope_pos_offset=k0)
+        fill_kv_slice(l, k0, n_local, kc[l], vc[l], cap, dev)
     # the new token is written at the last position of the last rank's slice
     pos_new = N_KV - 1
     owner = split_kv.owner(N_KV, world, pos_new)
-    local_row = pos_new - split_kv.plan(N_KV, world, owner).start
     # The step's inputs share one device buffer (so that the end-to-end measurement
     # moves them with one host-to-device copy): q, gate, k_new, v_new (f32), then the
-    # step scalars {n_kv, q_pos0} (i64).
+    # step scalars {n_kv, q_pos0} (i64).  Every rank draws the same inputs.
     in_shapes = [(N_LAYERS, 1, N_HEAD, HEAD_DIM)] * 2 + [(N_LAYERS, 1, N_HEAD_KV, HEAD_DIM)] * 2
     in_off = [0]
     for shp in in_shapes:
@@ -286,6 +533,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         ts = [buf[in_off[i]:in_off[i + 1]].view(torch.float32).view(shp) for i, shp in enumerate(in_shapes)]
         return ts + [buf[in_off[-1]:in_off[-1] + 16].view(torch.int64)]
 
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242)
     inp = torch.empty(in_off[-1] + 16, dtype=torch.uint8, device=dev)
     q, gate, k_new, v_new, step = in_views(inp)
     for t_, shp in zip((q, gate, k_new, v_new), in_shapes):
@@ -293,20 +542,18 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     step.copy_(torch.tensor(list(shard.local_step(N_KV, pos_new)), dtype=torch.int64, device=dev))
     out = torch.empty((N_LAYERS, 1, N_HEAD, HEAD_DIM), device=dev)
     d_nkv, d_qpos = step[0:1], step[1:2]
-    d_row = torch.tensor([local_row], dtype=torch.int64, device=dev)
     n_splits = sqmix.lib().sqmix_device_sm_count(local_rank)
-    ws = sqmix.new_fa_workspace(1, n_splits, dev)
+    ws = sqmix.new_fa_workspace(2, n_splits, dev)
     torch.cuda.synchronize()
 
     if world > 1:
-        # (O, LSE) partials packed per layer so that one all-gather moves both
         rows = N_HEAD
-        pk_loc = torch.empty((N_LAYERS, rows * (HEAD_DIM + 1)), device=dev)
+        o_loc = torch.empty((N_LAYERS, 1, N_HEAD, HEAD_DIM), device=dev)
+        l_loc = torch.empty((N_LAYERS, 1, N_HEAD), device=dev)
         pk_all = torch.empty((world, rows * (HEAD_DIM + 1)), device=dev)
-        o_loc = [pk_loc[l, :rows * HEAD_DIM].view(1, N_HEAD, HEAD_DIM) for l in range(N_LAYERS)]
-        l_loc = [pk_loc[l, rows * HEAD_DIM:].view(1, N_HEAD) for l in range(N_LAYERS)]
-        # default: the fused peer-memory merge (one kernel per layer, partials read
-        # over NVLink); --nccl-merge: all-gather + merge kernel
+        pk_loc = torch.empty((N_LAYERS, rows * (HEAD_DIM + 1)), device=dev)
+        # default: the peer-memory merge (one kernel per layer, partials read over
+        # NVLink); --nccl-merge: all-gather over NCCL + merge kernel
         peer = None if args.nccl_merge else split_kv.PeerMerge(n_slots=N_LAYERS, rows=N_HEAD, device=dev)
 
     own = rank == owner  # the rank whose key slice holds the new token appends it (fused)
@@ -317,18 +564,22 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                  rope_freq_base=FREQ_BASE, rope_pos_offset=k0, out=out[l],
                                  workspace=ws, n_splits=n_splits, k_new=k_new[l], v_new=v_new[l],
                                  overlap_prev=True)
+        elif peer is not None:
+            sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=None, rope_n_rot=N_ROT,
+                                 rope_freq_base=FREQ_BASE, rope_pos_offset=k0, out=o_loc[l], lse=l_loc[l],
+                                 workspace=ws, n_splits=n_splits, k_new=k_new[l] if own else None,
+                                 v_new=v_new[l] if own else None, overlap_prev=True)
+            peer.merge(o_loc[l], l_loc[l], l, gate=gate[l, 0], out=out[l, 0])
         else:
             sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=None, rope_n_rot=N_ROT,
-                                 rope_freq_base=FREQ_BASE, rope_pos_offset=k0, out=o_loc[l],
-                                 lse=l_loc[l], workspace=ws, n_splits=n_splits,
-                                 k_new=k_new[l] if own else None, v_new=v_new[l] if own else None,
-                                 overlap_prev=True)
-            if peer is not None:
-                peer.merge(o_loc[l], l_loc[l], l, gate=gate[l, 0], out=out[l, 0])
-            else:
-                dist.all_gather_into_tensor(pk_all, pk_loc[l])
-                sqmix.attn_merge_lse(pk_all[:, :rows * HEAD_DIM].view(world, rows, HEAD_DIM),
-                                     pk_all[:, rows * HEAD_DIM:], gate=gate[l, 0], out=out[l, 0])
+                                 rope_freq_base=FREQ_BASE, rope_pos_offset=k0,
+                                 out=pk_loc[l, :rows * HEAD_DIM].view(1, N_HEAD, HEAD_DIM),
+                                 lse=pk_loc[l, rows * HEAD_DIM:].view(1, N_HEAD), workspace=ws,
+                                 n_splits=n_splits, k_new=k_new[l] if own else None,
+                                 v_new=v_new[l] if own else None, overlap_prev=True)
+            dist.all_gather_into_tensor(pk_all, pk_loc[l])
+            sqmix.attn_merge_lse(pk_all[:, :rows * HEAD_DIM].view(world, rows, HEAD_DIM),
+                                 pk_all[:, rows * HEAD_DIM:], gate=gate[l, 0], out=out[l, 0])
 
     def step_fn():
         for l in range(N_LAYERS):
@@ -336,7 +587,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
     stream = torch.cuda.current_stream()
     graph = None
-    if not args.no_graph:  # N > 1: the NCCL all-gathers are captured too
+    if not args.no_graph:  # N > 1: the merges (peer kernels or NCCL all-gathers) are captured too
         s = torch.cuda.Stream()
         s.wait_stream(stream)
         with torch.cuda.stream(s):
@@ -354,58 +605,23 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-
-    sampler = ClockSampler(local_rank)
-    with sampler:
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        sampler.mark_start()
-        e0.record()
-        for _ in range(args.steps):
-            run()
-        e1.record()
-        torch.cuda.synchronize()
-        sampler.mark_end()
-        ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms, clocks = timed_window(run, args.steps, local_rank, world)
+    ms = max_over_ranks(ms, world, dev)
     us_per_token = ms * 1e3 / args.steps
-    # per layer: decode + split merge (PDL pair), plus the cross-rank merge_lse for N > 1
+    out_check = out.clone()  # the last timed step's output (parity check below)
+    # per layer: decode + split merge (PDL pair), plus the cross-rank merge for N > 1
     launches_per_step = N_LAYERS * (2 + (1 if world > 1 else 0))
 
     # ---- dominant kernel alone: flash_attn_ext over each layer in turn ---------
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
     reps = max(3, args.steps)
-    # (graph-captured so that host launch cost is not mistaken for kernel time)
+
     def fa_only():
         for l in range(N_LAYERS):
             sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=gate[l], rope_n_rot=N_ROT,
                                  rope_freq_base=FREQ_BASE, rope_pos_offset=k0, out=out[l],
                                  workspace=ws, n_splits=n_splits, overlap_prev=True)
-    s2 = torch.cuda.Stream()
-    s2.wait_stream(stream)
-    with torch.cuda.stream(s2):
-        fa_only()
-    stream.wait_stream(s2)
-    torch.cuda.synchronize()
-    g_fa = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_fa):
-        fa_only()
-    g_fa.replay()
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(reps):
-        g_fa.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    g_fa = None
-    fa_us = e0.elapsed_time(e1) * 1e3 / (reps * N_LAYERS)
+
+    fa_us = _graph_us(fa_only, N_LAYERS, reps, args.warmup)
     sqmix.fa_status(ws)
 
     # ---- MTP verify (config 3's 2-token query) over the same caches ------------
@@ -415,45 +631,27 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         gate2 = torch.randn((N_LAYERS, 2, N_HEAD, HEAD_DIM), generator=g, device=dev)
         out2 = torch.empty((N_LAYERS, 2, N_HEAD, HEAD_DIM), device=dev)
         step2 = torch.tensor([n_local, n_local - 2], dtype=torch.int64, device=dev)
-        ws2 = sqmix.new_fa_workspace(2, n_splits, dev)
 
         def mtp_step():
             for l in range(N_LAYERS):
                 sqmix.flash_attn_ext(q2[l], kc[l], vc[l], cap, step2[0:1], step2[1:2], gate=gate2[l],
-                                     rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE, out=out2[l], workspace=ws2,
+                                     rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE, out=out2[l], workspace=ws,
                                      n_splits=n_splits, overlap_prev=True)
-        s3 = torch.cuda.Stream()
-        s3.wait_stream(stream)
-        with torch.cuda.stream(s3):
-            mtp_step()
-        stream.wait_stream(s3)
-        torch.cuda.synchronize()
-        g_mtp = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_mtp):
-            mtp_step()
-        g_mtp.replay()
-        torch.cuda.synchronize()
-        e0.record()
-        for _ in range(reps):
-            g_mtp.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        mtp_us = e0.elapsed_time(e1) * 1e3 / reps
-        g_mtp = None
-        sqmix.fa_status(ws2)
-        mtp = {"us_per_step": mtp_us, "query_tokens": 2,
-               "achieved_gbs": N_LAYERS * (n_local * BYTES_PER_KEY + 6 * N_HEAD * HEAD_DIM * 4) / mtp_us / 1e3,
+
+        mtp_us = _graph_us(mtp_step, 1, reps, args.warmup)
+        sqmix.fa_status(ws)
+        mtp_bytes = N_LAYERS * (n_local * BYTES_PER_KEY + 6 * N_HEAD * HEAD_DIM * 4)
+        hbm_, _ = peaks()
+        mtp = {"us_per_step": mtp_us, "query_tokens": 2, "achieved_gbs": mtp_bytes / mtp_us / 1e3,
+               "frac_of_hbm": mtp_bytes / mtp_us / 1e3 / hbm_,
                "note": "10 layers x 172032 keys, n_q = 2 (MTP verification query), CUDA graph, no append"}
     alg_bytes = n_local * BYTES_PER_KEY + 3 * N_HEAD * HEAD_DIM * 4
     hbm, peak_kind = peaks()
     achieved = alg_bytes / (fa_us * 1e-6) / 1e9
 
     # ---- end to end through the public API with host buffers -------------------
-    h_inp = torch.empty(inp.numel(), dtype=torch.uint8).pin_memory()  # same layout as inp
-    h_views = in_views(h_inp)
-    for t_, shp in zip(h_views[:4], in_shapes):
-        t_.copy_(torch.randn(shp))
-    h_views[4].copy_(torch.tensor(list(shard.local_step(N_KV, pos_new)), dtype=torch.int64))
+    h_inp = torch.empty(inp.numel(), dtype=torch.uint8).pin_memory()  # same bytes as inp
+    h_inp.copy_(inp)
     h_out = torch.empty((N_LAYERS, 1, N_HEAD, HEAD_DIM)).pin_memory()
     h2d = h_inp.numel()
     d2h = h_out.numel() * 4
@@ -468,16 +666,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms, _ = timed_window(e2e_step, args.steps, local_rank, world)
+    e2e_ms = max_over_ranks(e2e_ms, world, dev)
     e2e_us = e2e_ms * 1e3 / args.steps
 
     used_graph = graph is not None
@@ -489,13 +679,18 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             if not peer.ok():
                 raise RuntimeError("peer merge: a bounded wait for a peer gave up")
             peer.close()
+    parity = None
+    if world > 1:
+        parity = split_kv_parity(rank, dev, q, gate, k_new, v_new, out_check)
+        dist.barrier()
     if rank != 0:
         return None
     res = {
         "metric": METRIC, "value": us_per_token, "unit": "us/token", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": us_per_token / 1e3, "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "q4_0 KV x f16 tensor-core fragments, f32 accum",
-        "data": "synthetic N(0,1) K/V/Q/gate (seeded), q4_0-quantised by the append kernel",
+        "data": "synthetic N(0,1) K/V/Q/gate (seeded per 1024-key chunk, identical on every rank), q4_0-quantised "
+                "by the append kernel",
         "config": {"workload": "config3: decode 1 token, 10 full-attn layers x 172032 q4_0 keys, "
                                "16 Q / 2 KV heads, d=256, RoPE 64/1e7, sigmoid gate",
                    "n_q": 1, "keys_per_layer": N_KV, "keys_per_gpu": n_local, "parallelism": f"split-KV x{world}",
@@ -507,15 +702,86 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": peak_kind, "traffic": FA_NCU_TRAFFIC if n_local == N_KV else None,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode launch "
-                                       "at 172032 keys (profiles/fa_decode_kernel_172k.txt)", "alg_bytes_per_launch": alg_bytes,
-                     "launch_us": fa_us},
-        "clocks": sampler.summary(),
+                                       "at 172032 keys (profiles/fa_decode_kernel_172k.txt)",
+                     "alg_bytes_per_launch": alg_bytes, "launch_us": fa_us},
+        "clocks": clocks,
         "gpu_launches": launches_per_step * args.steps,
         "e2e": {"value": e2e_us, "unit": "us/token", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
     }
     if mtp is not None:
         res["mtp_verify"] = mtp
+    if parity is not None:
+        res["parity"] = parity
     return res
+
+
+def split_kv_parity(rank: int, dev, q, gate, k_new, v_new, out_multi):
+    """N > 1: rank 0 rebuilds layers 0 and 9 as one whole-sequence cache from the same
+    per-chunk seeds, runs the single-GPU decode (fused append, RoPE, gate) over all
+    172032 keys and compares it with the split-KV output of the last timed step."""
+    import torch
+
+    import sqmix
+
+    if rank != 0:
+        return None
+    cap = (N_KV + 255) // 256 * 256
+    kc, vc = sqmix.new_kv_cache(cap, dev), sqmix.new_kv_cache(cap, dev)
+    d = torch.tensor([N_KV, N_KV - 1], dtype=torch.int64, device=dev)
+    errs = {}
+    for l in (0, N_LAYERS - 1):
+        fill_kv_slice(l, 0, N_KV, kc, vc, cap, dev)
+        ref = sqmix.flash_attn_ext(q[l], kc, vc, cap, d[0:1], d[1:2], gate=gate[l], rope_n_rot=N_ROT,
+                                   rope_freq_base=FREQ_BASE, k_new=k_new[l], v_new=v_new[l])
+        got = out_multi[l].double()
+        errs[l] = float((got - ref.double()).abs().max() / ref.double().abs().max())
+    worst = max(errs.values())
+    return {"max_rel_err": worst, "tol": 2e-3, "ok": worst <= 2e-3, "layers": sorted(errs),
+            "per_layer": {str(k): v for k, v in errs.items()},
+            "reference": "single-GPU sqmix_fa_decode over the whole 172032-key cache built from the same seeds "
+                         "(itself checked against the CPU oracle at this size by tests/test_gpu_headline.py)"}
+
+
+def bench_config0(steps: int, warmup: int):
+    """Config 0 on the GPU: one decode layer over 4096 q4_0 keys (append of the step's
+    row, RoPE, attention, gate).  One layer's cache is 2.4 MB, so 64 layers' caches
+    (151 MB, more than L2) are cycled and the time is per layer-token."""
+    import torch
+
+    import sqmix
+
+    dev = torch.device("cuda", 0)
+    n_kv, n_layers = 4096, 64
+    cap = n_kv
+    kc = [sqmix.new_kv_cache(cap, dev) for _ in range(n_layers)]
+    vc = [sqmix.new_kv_cache(cap, dev) for _ in range(n_layers)]
+    for l in range(n_layers):
+        fill_kv_slice(100 + l, 0, n_kv, kc[l], vc[l], cap, dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(20)
+    q = torch.randn((n_layers, 1, N_HEAD, HEAD_DIM), generator=g, device=dev)
+    gate = torch.randn((n_layers, 1, N_HEAD, HEAD_DIM), generator=g, device=dev)
+    k_new = torch.randn((n_layers, 1, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+    v_new = torch.randn((n_layers, 1, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+    out = torch.empty((n_layers, 1, N_HEAD, HEAD_DIM), device=dev)
+    d = torch.tensor([n_kv, n_kv - 1], dtype=torch.int64, device=dev)
+    ws = sqmix.new_fa_workspace(1, 0, dev)
+
+    def all_layers():
+        for l in range(n_layers):
+            sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d[0:1], d[1:2], gate=gate[l], rope_n_rot=N_ROT,
+                                 rope_freq_base=FREQ_BASE, out=out[l], workspace=ws, k_new=k_new[l],
+                                 v_new=v_new[l], overlap_prev=True)
+
+    us = _graph_us(all_layers, n_layers, max(3, steps // 10), warmup)
+    sqmix.fa_status(ws)
+    hbm, hbm_kind = peaks()
+    alg = n_kv * BYTES_PER_KEY + 3 * N_HEAD * HEAD_DIM * 4
+    return {"us_per_layer_token": us, "alg_bytes": alg, "achieved_gbs": alg / us / 1e3,
+            "frac_of_hbm": alg / us / 1e3 / hbm, "peak_gbs": hbm, "peak_kind": hbm_kind,
+            "config": "config0: 1 query token, 16/2 heads, d 256, 4096 q4_0 keys, scale 1/16, fused append, "
+                      "sigmoid gate; 64 layers' caches cycled (151 MB > L2), CUDA graph",
+            "note": "a 2.4 MB layer is bound by the launch and the fixed per-layer cost, not by HBM"}
 
 
 PF_PREFIX = 32768  # config 2: pp512 and pp2048 appended onto a 32768-token q4_0 prefix
@@ -772,43 +1038,59 @@ def bench_gdn_front(g, dev, steps: int, warmup: int, hbm: float, hbm_kind: str) 
     return res
 
 
-def bench_stack(steps: int, warmup: int, splits_per_seq: int = 0):
+STACK_SEQS = 64
+
+
+def stack_lengths():
+    """Config 4's per-sequence KV lengths, ~U[1024, 32768] (seeded), longest first as an
+    engine that knows its sequence lengths would submit them (CTAs are scheduled in grid
+    order, so the long splits start first)."""
+    rng = np.random.default_rng(17)
+    return np.sort(rng.integers(1024, 32768 + 1, STACK_SEQS))[::-1]
+
+
+def bench_stack(steps: int, warmup: int, rank: int = 0, world: int = 1, local_rank: int = 0,
+                splits_per_seq: int = 0):
     """Config 4: batched hybrid mixer stack, 40 layers (3 GDN + 1 full attention, x10),
-    64 sequences decoding one token each; per-sequence q4_0 KV lengths ~U[1024, 32768]
-    (seeded), each sequence with its own GDN states.  Caches hold random q4_0 codes with
-    fp16 scales ~U(0.05, 0.3) (filling 6 GB through the quantiser would dominate the
-    run); the attention arithmetic does not depend on where the codes came from."""
-    import numpy as np
+    64 sequences decoding one token each, each sequence with its own q4_0 KV caches
+    (N(0,1) K/V quantised by the append kernel, K rotated) and its own GDN states.  With
+    N ranks the sequences are sharded by sequence, round-robin over the length-sorted
+    batch (rank r takes sequences r, r + N, ...): no collective on the data path; the
+    aggregate is 64 tokens over the slowest rank's step time."""
     import torch
 
     import sqmix
 
-    dev = torch.device("cuda", 0)
-    g = torch.Generator(device=dev)
-    g.manual_seed(17)
-    rng = np.random.default_rng(17)
-    n_seqs, n_fa, n_gdn = 64, 10, 30
-    # the batch is ordered longest first, as an engine that knows its sequence lengths
-    # would submit it: CTAs are scheduled in grid order, so the long splits start first
-    lens = np.sort(rng.integers(1024, 32768 + 1, n_seqs))[::-1]
+    dev = torch.device("cuda", local_rank)
+    lens_all = stack_lengths()
+    mine = list(range(rank, STACK_SEQS, world))
+    lens = lens_all[mine]
+    n_seqs, n_fa, n_gdn = len(mine), 10, 30
     caps = [int((n + 1 + 255) // 256 * 256) for n in lens]
     offs = np.concatenate([[0], np.cumsum(caps)])
     rows_total = int(offs[-1])
-    unit_rows = 16  # a 4608-byte group holds 16 tokens of both heads
-    kc, vc = [], []
-    for _ in range(n_fa):
-        for lst in (kc, vc):
-            buf = torch.randint(0, 256, (rows_total * 288,), dtype=torch.uint8, generator=g, device=dev)
-            units = buf.view(-1, 2304)
-            sc = (torch.rand((units.shape[0], 128), generator=g, device=dev) * 0.25 + 0.05).half()
-            units[:, 2048:] = sc.view(torch.uint8)
-            lst.append(buf)
+    kc = [torch.empty(rows_total * 288, dtype=torch.uint8, device=dev) for _ in range(n_fa)]
+    vc = [torch.empty(rows_total * 288, dtype=torch.uint8, device=dev) for _ in range(n_fa)]
+    g = torch.Generator(device=dev)
+    for l in range(n_fa):
+        for i, s_glob in enumerate(mine):
+            a, b = int(offs[i]) * 288, int(offs[i] + caps[i]) * 288
+            kc[l][a:b].zero_()
+            vc[l][a:b].zero_()
+            g.manual_seed(7_000_003 * (l + 1) + s_glob)
+            n = int(lens[i])
+            kk = torch.randn((n, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+            vv = torch.randn((n, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
+            sqmix.set_rows_q4_0(kk, vv, torch.arange(n, device=dev), kc[l][a:b], vc[l][a:b], caps[i],
+                                rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE)
+            del kk, vv
     i64 = lambda xs: torch.tensor([int(x) for x in xs], dtype=torch.int64, device=dev)
     kp = [i64([kc[l].data_ptr() + int(offs[s]) * 288 for s in range(n_seqs)]) for l in range(n_fa)]
     vp = [i64([vc[l].data_ptr() + int(offs[s]) * 288 for s in range(n_seqs)]) for l in range(n_fa)]
     capt = i64(caps)
     n_kv = i64([n + 1 for n in lens])
     q_pos0 = i64(list(lens))
+    g.manual_seed(17 + rank)
     q = torch.randn((n_fa, n_seqs, N_HEAD, HEAD_DIM), generator=g, device=dev)
     gate = torch.randn((n_fa, n_seqs, N_HEAD, HEAD_DIM), generator=g, device=dev)
     k_new = torch.randn((n_fa, n_seqs, N_HEAD_KV, HEAD_DIM), generator=g, device=dev)
@@ -850,25 +1132,26 @@ def bench_stack(steps: int, warmup: int, splits_per_seq: int = 0):
     for _ in range(max(warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = max(3, steps)
-    e0.record()
-    for _ in range(reps):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / reps
+    ms, clocks = timed_window(graph.replay, reps, local_rank, world)
+    us_local = ms * 1e3 / reps
+    us = max_over_ranks(us_local, world, dev)
     graph = None
     sqmix.fa_status(ws)
     hbm, hbm_kind = peaks()
     fa_bytes = n_fa * float(sum(int(n) + 1 for n in lens)) * BYTES_PER_KEY
     gdn_bytes = n_gdn * n_seqs * 2.0 * GDN_STATE_BYTES
     alg = fa_bytes + gdn_bytes
-    return {"us_per_step": us, "tok_s": n_seqs / us * 1e6, "alg_bytes_per_step": alg,
-            "achieved_gbs": alg / us / 1e3, "frac_of_hbm": alg / us / 1e3 / hbm, "peak_kind": hbm_kind,
-            "kv_len_mean": float(np.mean(lens)),
-            "config": "config4: 64 sequences x 1 token, 40 layers (30 GDN + 10 full attention), q4_0 KV "
-                      "U[1024, 32768] per sequence, batched kernels, CUDA graph"}
+    all_bytes = n_fa * float(sum(int(n) + 1 for n in lens_all)) * BYTES_PER_KEY + \
+        n_gdn * STACK_SEQS * 2.0 * GDN_STATE_BYTES
+    return {"us_per_step": us, "tok_s": STACK_SEQS / us * 1e6, "n_gpus": world, "seqs_per_gpu": n_seqs,
+            "alg_bytes_per_step": all_bytes, "aggregate_gbs": all_bytes / us / 1e3,
+            "rank0_alg_bytes": alg, "rank0_us": us_local, "rank0_frac_of_hbm": alg / us_local / 1e3 / hbm,
+            "peak_kind": hbm_kind, "kv_len_mean": float(np.mean(lens_all)), "clocks": clocks,
+            "scaling": "strong", "parallelism": f"sequences sharded x{world} (round-robin), no collective",
+            "config": "config4: 64 sequences x 1 token, 40 layers (30 GDN + 10 full attention), q4_0 KV of N(0,1) "
+                      "(append kernel) with lengths U[1024, 32768] per sequence, batched kernels, CUDA graph; "
+                      "tok_s = 64 / the slowest rank's step time"}
 
 
 def run_profile_case(case: str):
@@ -946,7 +1229,8 @@ def main():
     ap.add_argument("--impl", default="sqmix", choices=["sqmix", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill measurement")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="config 3 only (skip configs 0, 1, 2 and 4)")
     ap.add_argument("--nccl-merge", action="store_true", help="N > 1: all-gather + merge instead of the peer merge")
     ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn | gdnb | gdnp) and exit")
     args = ap.parse_args()
@@ -973,14 +1257,22 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline()
+    cpu_on = rank == 0 and world == 1 and not args.no_cpu_baseline
+    cpu = cpu_baseline_config3() if cpu_on else None
     res = run_gpu(args, rank, world, local_rank)
-    if res is not None and world == 1 and not args.no_prefill:
-        res["prefill"] = bench_prefill(args.steps, args.warmup)
-        res["gdn"] = bench_gdn(args.steps, args.warmup)
-        res["stack"] = bench_stack(args.steps, args.warmup)
+    if not args.headline_only:
+        if world == 1:
+            res["config0"] = bench_config0(args.steps, args.warmup)
+            res["prefill"] = bench_prefill(args.steps, args.warmup)
+            res["gdn"] = bench_gdn(args.steps, args.warmup)
+        stack = bench_stack(args.steps, args.warmup, rank, world, local_rank)  # every rank (sharded)
+        if res is not None:
+            res["stack"] = stack
+        if cpu_on:
+            res["config0"]["cpu_baseline"] = cpu_baseline_config0()
+            res["gdn"]["cpu_baseline"] = cpu_baseline_config1()
+            res["prefill"]["cpu_baseline"] = cpu_baseline_config2()
+            res["stack"]["cpu_baseline"] = cpu_baseline_config4(stack_lengths())
     if res is not None:
         if cpu is not None:
             res["cpu_baseline"] = cpu

@@ -59,6 +59,8 @@ def lib():
         L.oracle_gdn_conv.argtypes = [f32p, i64, i64, i64, f32p, f32p, i64, i64, i64, i64, i64, ctypes.c_float,
                                       f32p]
         L.oracle_rms_norm_rows.argtypes = [f32p, i64, i64, ctypes.c_float, f32p, i64, i64, f32p, f32p]
+        L.cpu_fa_q4_0.argtypes = [f32p, u8p, u8p, f32p, i64, i64, i64, i64, i64, i64, ctypes.c_float, f32p, f32p]
+        L.cpu_gdn_f32.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, i64, i64, i64, i64, f32p]
         L.oracle_set_threads.argtypes = [ctypes.c_int]
         L.oracle_set_threads.restype = ctypes.c_int
         _lib = L
@@ -245,3 +247,47 @@ def merge_lse(o_parts, lse_parts, gate=None):
         out = out / (1.0 + np.exp(-np.asarray(gate, dtype=np.float64)))
     lse_out = np.where(finite, Ls + np.log(np.where(tot > 0, tot, 1.0)), -np.inf)
     return out.astype(np.float32), lse_out.astype(np.float32)
+
+
+# --------------------------------------------------------------------------- #
+# The timed CPU baseline (cpu_ggml.c): ggml-cpu's way of running the same nodes. #
+# Not the checker: these run in f32 with Q as q8_0, as ggml-cpu does.           #
+# --------------------------------------------------------------------------- #
+
+def cpu_fa_q4_0(q, k_rows, v_rows, gate=None, q_pos0: int = 0, scale: float = 1.0 / 16, want_lse=False):
+    """q [T][Hq][D] f32 (rotated); k_rows, v_rows [n_kv][Hkv*D/32*18] uint8 (ggml q4_0 rows);
+    gate [T][Hq][D] or None.  ggml-cpu flash attention (q8_0 Q, f32 online softmax)."""
+    qs, qp = _f32(q)
+    T, Hq, D = qs.shape
+    kr = np.ascontiguousarray(k_rows, dtype=np.uint8)
+    vr = np.ascontiguousarray(v_rows, dtype=np.uint8)
+    n_kv = kr.shape[0]
+    Hkv = kr.shape[1] * QK4_0 // Q4_0_BLOCK_BYTES // D
+    gp = _nullf32()
+    if gate is not None:
+        gs, gp = _f32(gate)
+    out = np.zeros((T, Hq, D), dtype=np.float32)
+    lse = np.zeros((T, Hq), dtype=np.float32)
+    f32p = ctypes.POINTER(ctypes.c_float)
+    u8p = ctypes.POINTER(ctypes.c_uint8)
+    lib().cpu_fa_q4_0(qp, kr.ctypes.data_as(u8p), vr.ctypes.data_as(u8p), gp, T, Hq, Hkv, D, n_kv, int(q_pos0),
+                      float(scale), out.ctypes.data_as(f32p), lse.ctypes.data_as(f32p))
+    return (out, lse) if want_lse else out
+
+
+def cpu_gdn_f32(q, k, v, g, beta, state):
+    """Token-by-token gated delta rule in f32; state [Hv][d][d] is updated in place
+    (must be a C-contiguous float32 array).  Returns out [T][Hv][d]."""
+    if not (isinstance(state, np.ndarray) and state.dtype == np.float32 and state.flags.c_contiguous):
+        raise TypeError("state must be a C-contiguous float32 array (updated in place)")
+    qs, qp = _f32(q)
+    ks, kp = _f32(k)
+    vs, vp = _f32(v)
+    gs, gp = _f32(g)
+    bs, bp = _f32(beta)
+    T, Hk, d = qs.shape
+    Hv = vs.shape[1]
+    out = np.zeros((T, Hv, d), dtype=np.float32)
+    f32p = ctypes.POINTER(ctypes.c_float)
+    lib().cpu_gdn_f32(qp, kp, vp, gp, bp, state.ctypes.data_as(f32p), T, Hk, Hv, d, out.ctypes.data_as(f32p))
+    return out

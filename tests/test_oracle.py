@@ -378,3 +378,33 @@ def test_rms_norm_and_norm_gated_vs_numpy(oracle):
         assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
     got = oracle.rms_norm(x, 1e-6)
     assert np.abs(got - r).max() <= 1e-5 * np.abs(r).max()
+
+
+def test_cpu_baseline_matches_checker(oracle):
+    """The timed CPU baseline (ggml-cpu's algorithm: q8_0 Q, f32 online softmax, per-key
+    V dequant) computes the same attention and GDN step as the double-precision checker,
+    within the error of Q's q8_0 rounding."""
+    rng = np.random.default_rng(5)
+    n_kv, T = 700, 3
+    k = rng.standard_normal((n_kv, 512)).astype(np.float32)
+    v = rng.standard_normal((n_kv, 512)).astype(np.float32)
+    kq, vq = oracle.q4_0_quantize(k), oracle.q4_0_quantize(v)
+    kd = oracle.q4_0_dequantize(kq, 512).reshape(n_kv, 2, 256)
+    vd = oracle.q4_0_dequantize(vq, 512).reshape(n_kv, 2, 256)
+    q = rng.standard_normal((T, 16, 256)).astype(np.float32)
+    gate = rng.standard_normal((T, 16, 256)).astype(np.float32)
+    want, wlse = oracle.attn(q, kd, vd, gate, q_pos0=n_kv - T, scale=1 / 16, want_lse=True)
+    got, glse = oracle.cpu_fa_q4_0(q, kq, vq, gate, q_pos0=n_kv - T, scale=1 / 16, want_lse=True)
+    assert np.abs(got - want).max() <= 2e-2 * np.abs(want).max()
+    assert np.abs(glse - wlse).max() < 5e-3
+    S = (rng.standard_normal((32, 128, 128)) * 0.02).astype(np.float32)
+    qg = oracle.l2norm(rng.standard_normal((4, 16, 128)).astype(np.float32))
+    kg = oracle.l2norm(rng.standard_normal((4, 16, 128)).astype(np.float32))
+    vg = rng.standard_normal((4, 32, 128)).astype(np.float32)
+    g = -rng.uniform(0.01, 1.0, (4, 32)).astype(np.float32)
+    b = rng.uniform(0.1, 0.9, (4, 32)).astype(np.float32)
+    want_o, snaps = oracle.gdn(qg, kg, vg, g, b, S, n_snap=1)
+    st = S.copy()
+    got_o = oracle.cpu_gdn_f32(qg, kg, vg, g, b, st)
+    assert np.abs(got_o - want_o).max() <= 1e-4 * np.abs(want_o).max()
+    assert np.abs(st - snaps[0]).max() <= 1e-4 * np.abs(snaps[0]).max()
