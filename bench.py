@@ -548,13 +548,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
     if world > 1:
         rows = N_HEAD
-        o_loc = torch.empty((N_LAYERS, 1, N_HEAD, HEAD_DIM), device=dev)
-        l_loc = torch.empty((N_LAYERS, 1, N_HEAD), device=dev)
         pk_all = torch.empty((world, rows * (HEAD_DIM + 1)), device=dev)
         pk_loc = torch.empty((N_LAYERS, rows * (HEAD_DIM + 1)), device=dev)
-        # default: the peer-memory merge (one kernel per layer, partials read over
-        # NVLink); --nccl-merge: all-gather over NCCL + merge kernel
-        peer = None if args.nccl_merge else split_kv.PeerMerge(n_slots=N_LAYERS, rows=N_HEAD, device=dev)
+        # default: the decode with its split merge fused to the exchange over peer memory
+        # (two kernels per layer; slots 0..9 for the 1-token step, 10..19 for the MTP
+        # query); --nccl-merge: decode, NCCL all-gather of the partials, merge kernel
+        peer = None if args.nccl_merge else split_kv.PeerMerge(n_slots=2 * N_LAYERS, rows=N_HEAD, device=dev)
 
     own = rank == owner  # the rank whose key slice holds the new token appends it (fused)
 
@@ -565,11 +564,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                  workspace=ws, n_splits=n_splits, k_new=k_new[l], v_new=v_new[l],
                                  overlap_prev=True)
         elif peer is not None:
-            sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=None, rope_n_rot=N_ROT,
-                                 rope_freq_base=FREQ_BASE, rope_pos_offset=k0, out=o_loc[l], lse=l_loc[l],
-                                 workspace=ws, n_splits=n_splits, k_new=k_new[l] if own else None,
-                                 v_new=v_new[l] if own else None, overlap_prev=True)
-            peer.merge(o_loc[l], l_loc[l], l, gate=gate[l, 0], out=out[l, 0])
+            peer.decode(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, l, gate=gate[l], out=out[l], rope_n_rot=N_ROT,
+                        rope_freq_base=FREQ_BASE, rope_pos_offset=k0, workspace=ws, n_splits=n_splits,
+                        k_new=k_new[l] if own else None, v_new=v_new[l] if own else None, overlap_prev=True)
         else:
             sqmix.flash_attn_ext(q[l], kc[l], vc[l], cap, d_nkv, d_qpos, gate=None, rope_n_rot=N_ROT,
                                  rope_freq_base=FREQ_BASE, rope_pos_offset=k0,
@@ -609,8 +606,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     ms = max_over_ranks(ms, world, dev)
     us_per_token = ms * 1e3 / args.steps
     out_check = out.clone()  # the last timed step's output (parity check below)
-    # per layer: decode + split merge (PDL pair), plus the cross-rank merge for N > 1
-    launches_per_step = N_LAYERS * (2 + (1 if world > 1 else 0))
+    # per layer: decode + split merge (PDL pair; for N > 1 the merge also does the
+    # exchange), plus the merge kernel after the all-gather with --nccl-merge
+    launches_per_step = N_LAYERS * (2 + (1 if world > 1 and peer is None else 0))
 
     # ---- dominant kernel alone: flash_attn_ext over each layer in turn ---------
     reps = max(3, args.steps)
@@ -626,25 +624,32 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
     # ---- MTP verify (config 3's 2-token query) over the same caches ------------
     mtp = None
-    if world == 1:
+    if world == 1 or peer is not None:
         q2 = torch.randn((N_LAYERS, 2, N_HEAD, HEAD_DIM), generator=g, device=dev)
         gate2 = torch.randn((N_LAYERS, 2, N_HEAD, HEAD_DIM), generator=g, device=dev)
         out2 = torch.empty((N_LAYERS, 2, N_HEAD, HEAD_DIM), device=dev)
-        step2 = torch.tensor([n_local, n_local - 2], dtype=torch.int64, device=dev)
+        step2 = torch.tensor(list(shard.local_step(N_KV, N_KV - 2)), dtype=torch.int64, device=dev)
 
         def mtp_step():
             for l in range(N_LAYERS):
-                sqmix.flash_attn_ext(q2[l], kc[l], vc[l], cap, step2[0:1], step2[1:2], gate=gate2[l],
-                                     rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE, out=out2[l], workspace=ws,
-                                     n_splits=n_splits, overlap_prev=True)
+                if world == 1:
+                    sqmix.flash_attn_ext(q2[l], kc[l], vc[l], cap, step2[0:1], step2[1:2], gate=gate2[l],
+                                         rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE, out=out2[l], workspace=ws,
+                                         n_splits=n_splits, overlap_prev=True)
+                else:
+                    peer.decode(q2[l], kc[l], vc[l], cap, step2[0:1], step2[1:2], N_LAYERS + l, gate=gate2[l],
+                                out=out2[l], rope_n_rot=N_ROT, rope_freq_base=FREQ_BASE, rope_pos_offset=k0,
+                                workspace=ws, n_splits=n_splits, overlap_prev=True)
 
-        mtp_us = _graph_us(mtp_step, 1, reps, args.warmup)
+        mtp_us = _graph_us(mtp_step, 1, reps, args.warmup, world)
+        mtp_us = max_over_ranks(mtp_us, world, dev)
         sqmix.fa_status(ws)
-        mtp_bytes = N_LAYERS * (n_local * BYTES_PER_KEY + 6 * N_HEAD * HEAD_DIM * 4)
+        mtp_bytes = N_LAYERS * (N_KV * BYTES_PER_KEY + 6 * N_HEAD * HEAD_DIM * 4)
         hbm_, _ = peaks()
         mtp = {"us_per_step": mtp_us, "query_tokens": 2, "achieved_gbs": mtp_bytes / mtp_us / 1e3,
-               "frac_of_hbm": mtp_bytes / mtp_us / 1e3 / hbm_,
-               "note": "10 layers x 172032 keys, n_q = 2 (MTP verification query), CUDA graph, no append"}
+               "frac_of_hbm_per_gpu": mtp_bytes / world / mtp_us / 1e3 / hbm_,
+               "note": f"10 layers x 172032 keys split over {world} GPU(s), n_q = 2 (MTP verification query), "
+                       "CUDA graph, no append"}
     alg_bytes = n_local * BYTES_PER_KEY + 3 * N_HEAD * HEAD_DIM * 4
     hbm, peak_kind = peaks()
     achieved = alg_bytes / (fa_us * 1e-6) / 1e9
@@ -970,8 +975,10 @@ def bench_gdn(steps: int, warmup: int):
     return res
 
 
-def _graph_us(fn, n_calls: int, reps: int, warmup: int) -> float:
-    """Device time per call of fn (n_calls launches captured in one CUDA graph)."""
+def _graph_us(fn, n_calls: int, reps: int, warmup: int, world: int = 1) -> float:
+    """Device time per call of fn (n_calls launches captured in one CUDA graph).  With
+    world > 1 every rank calls it (fn exchanges with the other ranks): the ranks meet at
+    a barrier before the first replay."""
     import torch
 
     s = torch.cuda.Stream()
@@ -982,6 +989,11 @@ def _graph_us(fn, n_calls: int, reps: int, warmup: int) -> float:
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
     for _ in range(max(warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()

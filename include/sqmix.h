@@ -190,13 +190,18 @@ typedef struct sqmix_fa_args {
 
 /* The decode and merge kernels are launched with programmatic stream serialisation:
  * each starts while the kernel before it on the stream drains and waits for it
- * (griddepcontrol.wait) before reading q, gate, k_new/v_new or the workspace.
+ * (griddepcontrol.wait) before reading q, gate, k_new/v_new or the workspace.  The
+ * merge kernel in turn lets the launch after it start as soon as it is resident, so
+ * the next kernel's prologue overlaps this call's tail; a kernel launched right after
+ * sqmix_fa_decode must read nothing this call writes (appended rows, workspace, out,
+ * lse) before its own dependency wait -- every sqmix kernel meets that.
  * SQMIX_FA_OVERLAP_PREV also lets the decode kernel read *n_kv, *q_pos0 and request
- * cache rows below *q_pos0 BEFORE that wait, overlapping the previous kernel's tail.
+ * cache rows below *q_pos0 BEFORE that wait, overlapping the previous kernels' tail.
  * Set it only when none of those is written by the kernel launched immediately before
- * this call on the stream (a copy, or a kernel two or more launches back, is fine):
- * the engine's step loop uploads the scalars with a copy and writes the step's rows
- * (>= q_pos0) with the fused append. */
+ * this call on the stream, nor by a sqmix_fa_decode call that immediately precedes it
+ * (a copy, or any other kernel two or more launches back, is fine): the engine's step
+ * loop uploads the scalars with a copy and writes the step's rows (>= q_pos0) with the
+ * fused append; consecutive layers use different caches. */
 #define SQMIX_FA_OVERLAP_PREV 1
 
 /* Workspace for n_splits splits (0 = enough for every configuration's default). */
@@ -269,13 +274,18 @@ int sqmix_fa_decode_batch(const sqmix_fa_batch_args *args, sqmix_stream_t stream
  * long-context decode split across ranks (one process per GPU).  Each rank creates
  * one peer buffer (n_slots = layers it merges per step), shares the IPC handle with
  * the other ranks (any host channel), opens theirs, and puts the n_ranks pointers
- * (its own at [rank]) in a device array.  sqmix_attn_merge_peers then publishes this
- * rank's normalised partial (o_local [rows][256], lse_local [rows], natural log) in
- * slot `slot`, waits (bounded, 2 s) for every peer's publication of the same slot and
- * merges all of them: out = sum_r O_r e^{lse_r - L} (* sigmoid(gate)), lse_out = L.
- * Every rank must call it once per slot per step, in the same order.  A wait that
- * gives up sets bit 1 of *status (nullable) and leaves out unwritten.  Buffers start
- * zeroed; destroy them only after every rank has finished its last merge. */
+ * (its own at [rank]) in a device array.  The ranks push: each writes its normalised
+ * partial for a slot into every other rank's buffer with 8-byte stores that pair each
+ * value with a publication tag, and waits (bounded, 2 s) in its own memory until every
+ * peer's words carry the tag; no flag, fence or remote polling is involved.  Then
+ * out = sum_r O_r e^{lse_r - L} (* sigmoid(gate)), lse_out = L (natural log).
+ * Every rank must call it once per slot per step, in the same order, and a slot is
+ * used with one entry point only (sqmix_attn_merge_peers or sqmix_fa_decode_peers).
+ * A wait that gives up sets bit 1 of *status (nullable) and leaves out unwritten; the
+ * buffers' publication counters then no longer agree across ranks, so after any
+ * nonzero status every rank resets its buffer (sqmix_peer_buffer_reset, after all
+ * ranks have stopped calling) before reusing it.  Buffers start zeroed; destroy them
+ * only after every rank has finished its last merge. */
 #define SQMIX_IPC_HANDLE_BYTES 64
 typedef struct sqmix_peer_merge_args {
     int32_t n_ranks;          /* <= 8 */
@@ -284,11 +294,11 @@ typedef struct sqmix_peer_merge_args {
     int32_t n_slots;
     int32_t rows;             /* 16 x n_q, <= 32 */
     const void *const *buffers; /* device array [n_ranks] of peer buffers as mapped here */
-    const float *o_local;
-    const float *lse_local;
-    const float *gate;        /* nullable [rows][256] f32 */
-    float *out;               /* [rows][256] */
-    float *lse_out;           /* nullable [rows] */
+    const float *o_local;     /* [rows][256] (sqmix_attn_merge_peers only) */
+    const float *lse_local;   /* [rows] (sqmix_attn_merge_peers only) */
+    const float *gate;        /* nullable [rows][256] f32 (sqmix_attn_merge_peers only) */
+    float *out;               /* [rows][256] (sqmix_attn_merge_peers only) */
+    float *lse_out;           /* nullable [rows] (sqmix_attn_merge_peers only) */
     void *status;             /* nullable device u32 */
 } sqmix_peer_merge_args;
 
@@ -297,7 +307,19 @@ int sqmix_peer_buffer_create(int32_t n_slots, void **dev_ptr, void *ipc_handle /
 int sqmix_peer_buffer_open(const void *ipc_handle, void **peer_ptr);
 int sqmix_peer_buffer_close(void *peer_ptr);
 int sqmix_peer_buffer_destroy(void *dev_ptr);
+/* Zeroes a buffer this rank created (async on stream): no publication, counters 0. */
+int sqmix_peer_buffer_reset(void *dev_ptr, int32_t n_slots, sqmix_stream_t stream);
 int sqmix_attn_merge_peers(const sqmix_peer_merge_args *args, sqmix_stream_t stream);
+
+/* Split-KV decode of one layer across ranks in two launches: the decode kernel over
+ * this rank's key slice (a: as for sqmix_fa_decode, with rope_pos_offset = the slice
+ * start and n_kv / q_pos0 in slice rows; the rank owning the step's rows passes
+ * k_new / v_new), then one kernel that merges the split partials of this rank, pushes
+ * the result into the peers' buffers, waits for theirs and writes the merged, gated
+ * output to a->out (and a->lse).  peers: n_ranks, rank, slot, n_slots, rows (= 16 n_q),
+ * buffers and status as for sqmix_attn_merge_peers; its o_local, lse_local, gate, out
+ * and lse_out are not used.  With n_ranks = 1 it equals sqmix_fa_decode. */
+int sqmix_fa_decode_peers(const sqmix_fa_args *a, const sqmix_peer_merge_args *peers, sqmix_stream_t stream);
 
 /* sqmix_fa_decode without a caller workspace (no reference counterpart: ggml_flash_attn_ext
  * takes its scratch from ggml's graph allocator).  For callers that cannot allocate
@@ -359,6 +381,21 @@ typedef struct sqmix_gdn_args {
     float l2_eps;             /* > 0: L2-normalise q and k per head first (gdn.rs:126-142) */
     float *out;               /* [n_seqs][T][H_v][128] f32 */
     int32_t flags;            /* SQMIX_GDN_* bits (0 = none) */
+    /* Value-head sharding (value heads split across ranks, no exchange in the
+     * recurrence): value head i of this call is head h_v_offset + i of the layer and
+     * reads q/k head (h_v_offset + i) % h_k; q and k hold all h_k heads, while v, g,
+     * beta, the state planes and out hold this call's h_v heads.  0 for a whole layer
+     * (which then needs h_v % h_k == 0, the tiling of gdn.rs:436-441). */
+    int32_t h_v_offset;
+    /* Gate epilogue of the projections (gdn.rs:268-287).  ssm_a == NULL: g and beta are
+     * the log-decay and beta themselves.  Otherwise g holds alpha = W_alpha h and beta
+     * holds b = W_beta h, and the kernels compute per token and value head (layer head
+     * index hg = h_v_offset + i):
+     *   beta = sigmoid(b),  g = softplus(alpha + dt_bias[hg]) * ssm_a[hg]
+     * with softplus(x) = log(1 + e^x) (x itself above 20) and ssm_a = -exp(A_log) as the
+     * model stores it (< 0).  dt_bias nullable (0). */
+    const float *dt_bias;     /* [layer value heads] ssm_dt */
+    const float *ssm_a;       /* [layer value heads] */
 } sqmix_gdn_args;
 
 /* sqmix_gdn_decode: the kernel launched immediately before this call on the stream

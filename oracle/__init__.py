@@ -291,3 +291,15 @@ def cpu_gdn_f32(q, k, v, g, beta, state):
     f32p = ctypes.POINTER(ctypes.c_float)
     lib().cpu_gdn_f32(qp, kp, vp, gp, bp, state.ctypes.data_as(f32p), T, Hk, Hv, d, out.ctypes.data_as(f32p))
     return out
+
+
+def gdn_gates(alpha, b, dt_bias, ssm_a):
+    """The gate epilogue of the GDN projections, src/model/gdn.rs:268-287 (ggml_sigmoid;
+    ggml_add, ggml_softplus, ggml_mul): beta = sigmoid(b), g = softplus(alpha + dt_bias)
+    * ssm_a, with ssm_a = -exp(A_log) as the model stores it.  alpha, b [..., H_v];
+    dt_bias, ssm_a [H_v].  softplus(x) = log1p(e^x), x itself above 20.  In double."""
+    a = np.asarray(alpha, dtype=np.float64) + np.asarray(dt_bias, dtype=np.float64)
+    sp = np.where(a > 20.0, a, np.log1p(np.exp(np.minimum(a, 20.0))))
+    g = sp * np.asarray(ssm_a, dtype=np.float64)
+    beta = 1.0 / (1.0 + np.exp(-np.asarray(b, dtype=np.float64)))
+    return g.astype(np.float32), beta.astype(np.float32)

@@ -83,7 +83,8 @@ const size_t kGdn[] = {
     OFF(sqmix_gdn_args, n_tokens),     OFF(sqmix_gdn_args, h_k),
     OFF(sqmix_gdn_args, h_v),          OFF(sqmix_gdn_args, n_snap),
     OFF(sqmix_gdn_args, l2_eps),       OFF(sqmix_gdn_args, out),
-    OFF(sqmix_gdn_args, flags),
+    OFF(sqmix_gdn_args, flags),        OFF(sqmix_gdn_args, h_v_offset),
+    OFF(sqmix_gdn_args, dt_bias),      OFF(sqmix_gdn_args, ssm_a),
 };
 
 const size_t kGdnConv[] = {

@@ -208,6 +208,17 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return h2_as_u32(__floats2half2_rn(lo, hi));
 }
 
+// ------------------------------------------------------- GDN gate epilogue ----
+// beta = sigmoid(b) and g = softplus(alpha + dt_bias) * ssm_a (gdn.rs:268-287:
+// ggml_sigmoid, ggml_add, ggml_softplus, ggml_mul); softplus(x) = log1p(e^x), x itself
+// above 20 (e^x no longer changes 1 + e^x in f32 there).
+__device__ __forceinline__ float gdn_softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ void gdn_gates(float &g, float &beta, const float *dt_bias, const float *ssm_a, int hg) {
+    if (!ssm_a) return;
+    g = gdn_softplus(g + (dt_bias ? dt_bias[hg] : 0.0f)) * ssm_a[hg];
+    beta = 1.0f / (1.0f + expf(-beta));
+}
+
 // ------------------------------------------------------------------ RoPE ----
 // Angle of rotation pair i at text position `pos`: theta = pos * scale^i with the
 // power built by repeated float multiplication (as ggml-cpu builds its rope cache,

@@ -41,6 +41,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace sqmix {
 
@@ -144,9 +145,10 @@ struct MergeSmem {
     float wm[8];
 };
 
-__device__ void merge_slice(const float *part_o, const float *part_ml, int n_splits, int n_rows, int row,
-                            int slice, float c, float scale, float gate_factor, float *out, float *lse,
-                            MergeSmem &sm) {
+// The merged values, valid in the first warp (lane = dim within the slice): y = the
+// normalised output of dim slice * 32 + lane, lse_row = the row's natural-log LSE.
+__device__ void merge_slice_values(const float *part_o, const float *part_ml, int n_splits, int n_rows, int row,
+                                   int slice, float c, float scale, MergeSmem &sm, float &y_out, float &lse_row) {
     constexpr int kPre = 24;  // o loads per thread issued up front (8 * 24 = 192 splits)
     const int tid = threadIdx.x, lane = tid & 31, grp = tid >> 5;
     const int d = slice * 32 + lane;
@@ -202,13 +204,34 @@ __device__ void merge_slice(const float *part_o, const float *part_ml, int n_spl
             L += sm.wm[i];
             y += sm.red[i][lane];
         }
-        y = L > 0.f ? y / L : 0.f;
-        out[static_cast<size_t>(row) * 256 + d] = y * gate_factor;
-        if (lse && slice == 0 && lane == 0) lse[row] = L > 0.f ? M * scale + logf(L) : -INFINITY;
+        y_out = L > 0.f ? y / L : 0.f;
+        lse_row = L > 0.f ? M * scale + logf(L) : -INFINITY;
     }
 }
 
-template <int NQ, int WPH, int GPW, int NSTAGE, int MINB>
+__device__ void merge_slice(const float *part_o, const float *part_ml, int n_splits, int n_rows, int row,
+                            int slice, float c, float scale, float gate_factor, float *out, float *lse,
+                            MergeSmem &sm) {
+    float y = 0.f, lse_row = 0.f;
+    merge_slice_values(part_o, part_ml, n_splits, n_rows, row, slice, c, scale, sm, y, lse_row);
+    if (threadIdx.x < 32) {
+        out[static_cast<size_t>(row) * 256 + slice * 32 + threadIdx.x] = y * gate_factor;
+        if (lse && slice == 0 && threadIdx.x == 0) lse[row] = lse_row;
+    }
+}
+
+// VC selects how the q4_0 offset of V (-8 per nibble) is restored:
+//   0: one correction MMA per block into its own accumulators (8 MMAs per group, 32
+//      registers per query token), added to O in the epilogue;
+//   1: the same MMAs straight into both O tiles of each block (no extra registers,
+//      16 MMAs per group);
+//   2: one MMA per group: C[block][head] += sum_t d_{block,t} P[t][head] (the V scales
+//      of the group as the A operand, P as the B operand it already is for PV), 4
+//      registers; the epilogue subtracts 8 C[block(dim)][head] from every dim of the
+//      block.  This pairs the unrounded products d P with the main term's rounded
+//      P' = f16(P d): the difference is the f16 rounding of P', about 2^-12 of each
+//      term, well inside the attention tolerance.
+template <int NQ, int WPH, int GPW, int NSTAGE, int MINB, int VC>
 __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, MINB)
     fa_decode_kernel(FaDecodeParams p) {
     using L = FaCfg<NQ, WPH, GPW, NSTAGE, MINB>;
@@ -481,17 +504,19 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
 
     float o[NQ][8][2][4];
     // The V offset term -8 * 2^-24 * sum_t P'_b[t] (rows g; x16 rows g+8) is the same for
-    // both M-tiles of block b.  One query token keeps it in its own accumulators (one
-    // MMA per block, added to O in the epilogue); two tokens, whose O accumulators
-    // leave no registers for it, add it to both M-tiles directly (measured 5 % faster
-    // for n_q = 2, 1.5 % slower for n_q = 1).
-    constexpr bool kVcorrRegs = NQ == 1;
+    // both M-tiles of block b: see VC above for the three ways of restoring it.
+    constexpr bool kVcorrRegs = VC == 0;
     float vcorr[kVcorrRegs ? NQ : 1][8][4];
+    float vcs[VC == 2 ? NQ : 1][4];  // VC 2: sum_t d_{g,t} P[t][2c | 2c+1] (lane g, c)
     float m_run[NQ][2], l_run[NQ][2];
 #pragma unroll
     for (int qi = 0; qi < NQ; ++qi) {
         m_run[qi][0] = m_run[qi][1] = -INFINITY;
         l_run[qi][0] = l_run[qi][1] = 0.f;
+        if constexpr (VC == 2) {
+#pragma unroll
+            for (int r = 0; r < 4; ++r) vcs[qi][r] = 0.f;
+        }
 #pragma unroll
         for (int b = 0; b < 8; ++b) {
             if constexpr (kVcorrRegs) {
@@ -602,15 +627,26 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
                 for (int qi = 0; qi < NQ; ++qi)
                     mma_f16_16816(o[qi][b][m], a, pbs[qi][0], pbs[qi][1], o[qi][b][m]);
             }
+            if constexpr (VC != 2) {
 #pragma unroll
-            for (int qi = 0; qi < NQ; ++qi) {
-                if constexpr (kVcorrRegs) {
-                    mma_f16_16816(vcorr[qi][b], voff, pbs[qi][0], pbs[qi][1], vcorr[qi][b]);
-                } else {
-                    mma_f16_16816(o[qi][b][0], voff, pbs[qi][0], pbs[qi][1], o[qi][b][0]);
-                    mma_f16_16816(o[qi][b][1], voff, pbs[qi][0], pbs[qi][1], o[qi][b][1]);
+                for (int qi = 0; qi < NQ; ++qi) {
+                    if constexpr (kVcorrRegs) {
+                        mma_f16_16816(vcorr[qi][b], voff, pbs[qi][0], pbs[qi][1], vcorr[qi][b]);
+                    } else {
+                        mma_f16_16816(o[qi][b][0], voff, pbs[qi][0], pbs[qi][1], o[qi][b][0]);
+                        mma_f16_16816(o[qi][b][1], voff, pbs[qi][0], pbs[qi][1], o[qi][b][1]);
+                    }
                 }
             }
+        }
+        if constexpr (VC == 2) {
+            // A = the group's V scales as [block g][token]: rows g hold block g's scales
+            // of tokens {2c, 2c+1} and {2c+8, 2c+9} (8 bytes at 2048 + 64c + 8g), rows g+8
+            // are zero; B = P^T, the unscaled B operand of PV.
+            const uint2 sd = *reinterpret_cast<const uint2 *>(vunit + kUnitQsBytes + c * 64 + 8 * g);
+            const uint32_t a[4] = {sd.x, 0u, sd.y, 0u};
+#pragma unroll
+            for (int qi = 0; qi < NQ; ++qi) mma_f16_16816(vcs[qi], a, pb[qi][0], pb[qi][1], vcs[qi]);
         }
     };
 
@@ -715,6 +751,10 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
                             vcorr[qi][b][3] *= al1;
                         }
                     }
+                    if constexpr (VC == 2) {
+                        vcs[qi][0] *= al0;
+                        vcs[qi][1] *= al1;
+                    }
                 }
             }
 #pragma unroll
@@ -771,7 +811,13 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     for (int qi = 0; qi < NQ; ++qi) {
         float *base = red_o + (static_cast<size_t>(warp) * NQ + qi) * 8 * L::kRedStride;
 #pragma unroll
-        for (int b = 0; b < 8; ++b)
+        for (int b = 0; b < 8; ++b) {
+            // VC 2: -8 sum_t d_{b,t} P[t][head] for heads 2c, 2c+1, held by lane (b, c)
+            float cr0 = 0.f, cr1 = 0.f;
+            if constexpr (VC == 2) {
+                cr0 = -8.0f * __shfl_sync(0xffffffffu, vcs[qi][0], 4 * b + c);
+                cr1 = -8.0f * __shfl_sync(0xffffffffu, vcs[qi][1], 4 * b + c);
+            }
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
                 const int d_lo = 32 * b + 8 * m + g;
@@ -782,11 +828,12 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
                     ov[r] = o[qi][b][m][r];
                     if constexpr (kVcorrRegs) ov[r] += vcorr[qi][b][r];
                 }
-                base[(2 * c) * L::kRedStride + d_lo] = ov[0] * kTwo24;
-                base[(2 * c + 1) * L::kRedStride + d_lo] = ov[1] * kTwo24;
-                base[(2 * c) * L::kRedStride + d_hi] = ov[2] * (kTwo24 / 16.0f);
-                base[(2 * c + 1) * L::kRedStride + d_hi] = ov[3] * (kTwo24 / 16.0f);
+                base[(2 * c) * L::kRedStride + d_lo] = fmaf(ov[0], kTwo24, cr0);
+                base[(2 * c + 1) * L::kRedStride + d_lo] = fmaf(ov[1], kTwo24, cr1);
+                base[(2 * c) * L::kRedStride + d_hi] = fmaf(ov[2], kTwo24 / 16.0f, cr0);
+                base[(2 * c + 1) * L::kRedStride + d_hi] = fmaf(ov[3], kTwo24 / 16.0f, cr1);
             }
+        }
         if (g == 0) {
             float *ml = red_ml + ((warp * NQ + qi) * 8) * 2;
             ml[(2 * c) * 2 + 0] = m_run[qi][0] * kTwo24;  // back to score units
@@ -884,8 +931,10 @@ __global__ void __launch_bounds__(256) fa_merge_kernel(FaMergeParams p) {
                                   p.gate_dtype);
         gate_factor = 1.0f / (1.0f + expf(-gv));
     }
-    grid_dependency_wait();
+    // The next launch may begin now: whatever it reads before its own dependency wait
+    // must not be written by this decode call (the appended rows, workspace, out, lse).
     launch_dependents();
+    grid_dependency_wait();
     const size_t parts = seq * p.n_splits * p.n_rows;
     merge_slice(p.part_o + parts * 256, p.part_ml + parts * 2, p.n_splits, p.n_rows, blockIdx.x, blockIdx.y, p.c,
                 p.scale, gate_factor, p.out + seq * p.n_rows * 256, p.lse ? p.lse + seq * p.n_rows : nullptr, sm);
@@ -911,8 +960,8 @@ __global__ void __launch_bounds__(256) fa_merge_small_kernel(FaMergeParams p, in
         gf.z = 1.0f / (1.0f + expf(-load_act(p.gate, g0 + 2, p.gate_dtype)));
         gf.w = 1.0f / (1.0f + expf(-load_act(p.gate, g0 + 3, p.gate_dtype)));
     }
+    launch_dependents();  // as in fa_merge_kernel
     grid_dependency_wait();
-    launch_dependents();
     const int64_t split0 = seq * p.n_splits;
     float2 ml[kSmallMergeSplits];
     float4 ov[kSmallMergeSplits];
@@ -945,6 +994,38 @@ __global__ void __launch_bounds__(256) fa_merge_small_kernel(FaMergeParams p, in
     const float4 y = make_float4(acc.x * inv * gf.x, acc.y * inv * gf.y, acc.z * inv * gf.z, acc.w * inv * gf.w);
     *reinterpret_cast<float4 *>(p.out + (seq * p.n_rows + row) * 256 + d) = y;
     if (p.lse && d == 0) p.lse[seq * p.n_rows + row] = L > 0.f ? M * p.scale + logf(L) : -INFINITY;
+}
+
+// Split merge fused with the cross-rank exchange of split-KV decode across GPUs
+// (sqmix_fa_decode_peers): one CTA per (output row, 32-dim slice) merges this rank's
+// split partials (as fa_merge_kernel), pushes the normalised slice and the row's LSE
+// into every peer's buffer and merges all ranks' (O, LSE) with the gate
+// (peer_exchange).  The decode grid of the same call is its only predecessor.
+struct FaPeerMergeParams {
+    FaMergeParams m;
+    PeerExchange px;
+};
+
+__global__ void __launch_bounds__(256) fa_merge_peers_kernel(FaPeerMergeParams p) {
+    __shared__ MergeSmem sm;
+    const int row = blockIdx.x, slice = blockIdx.y;
+    float gate_factor = 1.f;
+    if (p.m.gate && threadIdx.x < 32) {
+        const int qi = row >> 4, h = row & 15, d = slice * 32 + threadIdx.x;
+        const float gv = load_act(p.m.gate, qi * p.m.g_st + h * p.m.g_sh + d, p.m.gate_dtype);
+        gate_factor = 1.0f / (1.0f + expf(-gv));
+    }
+    launch_dependents();  // as in fa_merge_kernel
+    grid_dependency_wait();
+    float y_loc = 0.f, lse_loc = -INFINITY;
+    merge_slice_values(p.m.part_o, p.m.part_ml, p.m.n_splits, p.m.n_rows, row, slice, p.m.c, p.m.scale, sm, y_loc,
+                       lse_loc);
+    float y = 0.f, lse = -INFINITY;
+    if (!peer_exchange(p.px, row, slice, y_loc, lse_loc, kWaitLimitNs, y, lse)) return;
+    if (threadIdx.x < 32) {
+        p.m.out[static_cast<size_t>(row) * 256 + slice * 32 + threadIdx.x] = y * gate_factor;
+        if (p.m.lse && slice == 0 && threadIdx.x == 0) p.m.lse[row] = lse;
+    }
 }
 
 // Merge of normalised partials across GPUs: O = sum_p O_p e^(lse_p - L).
@@ -996,10 +1077,11 @@ struct FaBatch {
     int64_t q_sseq = 0, new_sseq = 0, g_sseq = 0;
 };
 
-template <int NQ, int WPH, int GPW, int NSTAGE, int MINB>
-static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, const FaBatch &bt = FaBatch()) {
+template <int NQ, int WPH, int GPW, int NSTAGE, int MINB, int VC>
+static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, const FaBatch &bt = FaBatch(),
+                     const PeerExchange *px = nullptr) {
     using L = FaCfg<NQ, WPH, GPW, NSTAGE, MINB>;
-    auto kernel = fa_decode_kernel<NQ, WPH, GPW, NSTAGE, MINB>;
+    auto kernel = fa_decode_kernel<NQ, WPH, GPW, NSTAGE, MINB, VC>;
     static std::atomic<uint64_t> attr_devices{0};
     {
         const cudaError_t e = set_smem_once(attr_devices, kernel, L::kTotal);
@@ -1078,6 +1160,14 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, cons
     mcfg.stream = st;
     mcfg.attrs = attr;
     mcfg.numAttrs = 1;
+    if (px) {  // the cross-rank exchange replaces the local merge's output stage
+        FaPeerMergeParams pp;
+        pp.m = mp;
+        pp.px = *px;
+        mcfg.gridDim = dim3(NQ * 16, kPeerSlices);
+        e = cudaLaunchKernelEx(&mcfg, fa_merge_peers_kernel, pp);
+        return cuda_status(e, "fa_merge_peers launch");
+    }
     if (n_splits <= kSmallMergeSplits) {
         // 64 threads per output row: n_seqs * NQ * 16 * 64 / 256 blocks
         mcfg.gridDim = dim3(static_cast<unsigned>(bt.n_seqs) * NQ * 4);
@@ -1089,7 +1179,7 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, cons
     return cuda_status(e, "fa_merge launch");
 }
 
-extern "C" int sqmix_fa_decode(const sqmix_fa_args *a, sqmix_stream_t stream) {
+static int fa_decode_impl(const sqmix_fa_args *a, const PeerExchange *px, sqmix_stream_t stream) {
     SQMIX_CHECK_ARG(a != nullptr, "fa_decode: null args");
     SQMIX_CHECK_ARG(a->q && a->k_cache && a->v_cache && a->n_kv && a->q_pos0 && a->out &&
                         a->workspace,
@@ -1116,16 +1206,22 @@ extern "C" int sqmix_fa_decode(const sqmix_fa_args *a, sqmix_stream_t stream) {
                                       (a->kv_new_dtype == SQMIX_F32 || a->kv_new_dtype == SQMIX_F16 ||
                                        a->kv_new_dtype == SQMIX_BF16)),
                     "fa_decode: fused append needs k_new/v_new [n_new][2][256] and a float dtype");
-    // Kernel configurations (warps per KV head x groups per warp, ring stages):
-    //   1: n_q 1, 4 warps/head x 2 groups per step, 5 x 36.9 KB slots
-    //   2: n_q 2, 4 warps/head x 1 group per step, 5 x 36.9 KB slots
-    //   3: n_q 1, 6 warps/head x 1 group per step, 3 x 55.3 KB slots
+    // Kernel configurations (warps per KV head x groups per warp, ring stages, V offset
+    // correction VC as described at fa_decode_kernel):
+    //   1: n_q 1, 4 warps/head x 2 groups per step, 5 x 36.9 KB slots, VC 0
+    //   2: n_q 2, 4 warps/head x 1 group per step, 5 x 36.9 KB slots, VC 1
+    //   3: n_q 1, 6 warps/head x 1 group per step, 3 x 55.3 KB slots, VC 0
+    //   4: n_q 1, 4 warps/head x 1 group per step, 2 x 36.9 KB slots, VC 2, <= 128
+    //      registers: two CTAs per SM (default split count 2 per SM)
+    //   5: configuration 3 with VC 2
+    //   6: configuration 2 with VC 2
     int cfg = a->config;
     // auto: configuration 3 for one query token (measured 4 % faster than 1 at 172K keys)
     if (cfg == 0) cfg = a->n_q == 1 ? 3 : 2;
-    SQMIX_CHECK_ARG(cfg >= 1 && cfg <= 3 && (cfg == 2) == (a->n_q == 2),
+    SQMIX_CHECK_ARG(cfg >= 1 && cfg <= 6 && (cfg == 2 || cfg == 6) == (a->n_q == 2),
                     "fa_decode: config %d does not serve n_q=%d", a->config, a->n_q);
-    int n_splits = a->n_splits > 0 ? a->n_splits : sqmix_device_sm_count(-1);
+    const int per_sm = cfg == 4 ? 2 : 1;
+    int n_splits = a->n_splits > 0 ? a->n_splits : per_sm * sqmix_device_sm_count(-1);
     SQMIX_CHECK_ARG(n_splits >= 1 && n_splits <= 4096, "fa_decode: n_splits=%d", n_splits);
     const size_t need = sqmix_fa_workspace_bytes(n_splits, a->n_q);
     if (a->workspace_bytes < need) {
@@ -1134,10 +1230,36 @@ extern "C" int sqmix_fa_decode(const sqmix_fa_args *a, sqmix_stream_t stream) {
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     switch (cfg) {
-        case 1: return launch_fa<1, 4, 2, 5, 1>(a, n_splits, st);
-        case 3: return launch_fa<1, 6, 1, 3, 1>(a, n_splits, st);
-        default: return launch_fa<2, 4, 1, 5, 1>(a, n_splits, st);
+        case 1: return launch_fa<1, 4, 2, 5, 1, 0>(a, n_splits, st, FaBatch(), px);
+        case 3: return launch_fa<1, 6, 1, 3, 1, 0>(a, n_splits, st, FaBatch(), px);
+        case 4: return launch_fa<1, 4, 1, 2, 2, 2>(a, n_splits, st, FaBatch(), px);
+        case 5: return launch_fa<1, 6, 1, 3, 1, 2>(a, n_splits, st, FaBatch(), px);
+        case 6: return launch_fa<2, 4, 1, 5, 1, 2>(a, n_splits, st, FaBatch(), px);
+        default: return launch_fa<2, 4, 1, 5, 1, 1>(a, n_splits, st, FaBatch(), px);
     }
+}
+
+extern "C" int sqmix_fa_decode(const sqmix_fa_args *a, sqmix_stream_t stream) {
+    return fa_decode_impl(a, nullptr, stream);
+}
+
+extern "C" int sqmix_fa_decode_peers(const sqmix_fa_args *a, const sqmix_peer_merge_args *pm,
+                                     sqmix_stream_t stream) {
+    SQMIX_CHECK_ARG(a != nullptr && pm != nullptr, "fa_decode_peers: null args");
+    SQMIX_CHECK_ARG(pm->n_ranks >= 1 && pm->n_ranks <= kPeerMaxRanks && pm->rank >= 0 && pm->rank < pm->n_ranks,
+                    "fa_decode_peers: rank %d of %d (at most %d ranks)", pm->rank, pm->n_ranks, kPeerMaxRanks);
+    SQMIX_CHECK_ARG(pm->n_slots >= 1 && pm->n_slots <= 4096 && pm->slot >= 0 && pm->slot < pm->n_slots,
+                    "fa_decode_peers: slot %d of %d", pm->slot, pm->n_slots);
+    SQMIX_CHECK_ARG(pm->rows == 16 * a->n_q, "fa_decode_peers: rows=%d must be 16 * n_q", pm->rows);
+    SQMIX_CHECK_ARG(pm->buffers != nullptr, "fa_decode_peers: null buffer array");
+    PeerExchange px;
+    px.n_ranks = pm->n_ranks;
+    px.rank = pm->rank;
+    px.slot = pm->slot;
+    px.n_slots = pm->n_slots;
+    px.bufs = const_cast<uint8_t *const *>(reinterpret_cast<const uint8_t *const *>(pm->buffers));
+    px.status = static_cast<uint32_t *>(pm->status);
+    return fa_decode_impl(a, &px, stream);
 }
 
 extern "C" int sqmix_fa_status(void *workspace, sqmix_stream_t stream) {
@@ -1306,5 +1428,5 @@ extern "C" int sqmix_fa_decode_batch(const sqmix_fa_batch_args *b, sqmix_stream_
     bt.g_sseq = b->gate_stride_seq;
     // configuration 3 (6 warps per KV head, 3 x 55.3 KB slots): measured 4.5 % faster
     // than configuration 1 on the 64-sequence batch of the mixer stack
-    return launch_fa<1, 6, 1, 3, 1>(&a, splits, reinterpret_cast<cudaStream_t>(stream), bt);
+    return launch_fa<1, 6, 1, 3, 1, 0>(&a, splits, reinterpret_cast<cudaStream_t>(stream), bt);
 }

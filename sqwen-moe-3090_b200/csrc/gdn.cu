@@ -39,6 +39,8 @@ struct GdnParams {
     int T_all;    // tokens per sequence in g, beta and out
     int64_t tok0; // first token of this launch within the sequence
     int state_ready;  // read the input state before waiting on the preceding kernel
+    int h_v_off;      // layer index of value head 0 (value-head sharding)
+    const float *dt_bias, *ssm_a;  // gate epilogue (ssm_a NULL: g, beta as given)
 };
 
 __device__ __forceinline__ float4 load4(const void *p, int64_t i, int dtype) {
@@ -88,7 +90,7 @@ __global__ void __launch_bounds__(256, JW == 8 ? 4 : 0) gdn_recurrent_kernel(Gdn
     const int h = static_cast<int>(hs % p.h_v);
     const int64_t seq = hs / p.h_v;
     if (seq >= p.n_seqs) return;
-    const int hk = h % p.h_k;
+    const int hk = (p.h_v_off + h) % p.h_k;
     // launched with programmatic stream serialisation: the launch overlaps the tail of
     // the kernel before it, whose results everything after griddepcontrol.wait may
     // use; with state_ready the caller guarantees that kernel writes neither the state
@@ -118,8 +120,9 @@ __global__ void __launch_bounds__(256, JW == 8 ? 4 : 0) gdn_recurrent_kernel(Gdn
             qq = l2norm4(qq, p.l2_eps);
         }
         const int64_t gb = (seq * p.T_all + tt) * p.h_v + h;
-        const float decay = expf(p.g[gb]);
-        const float bt = p.beta[gb];
+        float gl = p.g[gb], bt = p.beta[gb];
+        gdn_gates(gl, bt, p.dt_bias, p.ssm_a, p.h_v_off + h);
+        const float decay = expf(gl);
         const int64_t v_off = seq * p.v_sseq + tt * p.v_st + static_cast<int64_t>(h) * 128 + j0;
         float vj[JW];
 #pragma unroll
@@ -204,6 +207,9 @@ int gdn_launch_recurrent(const sqmix_gdn_args *a, int plane_in, int64_t tok_off,
     p.n_snap = n_snap;
     p.l2_eps = a->l2_eps;
     p.out = a->out;
+    p.h_v_off = a->h_v_offset;
+    p.dt_bias = a->dt_bias;
+    p.ssm_a = a->ssm_a;
     // columns per warp: 8 once that still leaves two waves of resident warps, else 4.
     // Measured on B200 (32 value heads, per layer): 4 columns beat 1 and 2 at every
     // batch from 1 to 32 (batch 8: 7.7 us against 13.5 with 1), 8 wins from batch 64.
@@ -238,8 +244,10 @@ extern "C" int sqmix_gdn_decode(const sqmix_gdn_args *a, sqmix_stream_t stream) 
                     "gdn_decode: null pointer argument");
     SQMIX_CHECK_ARG(a->dtype == SQMIX_F32 || a->dtype == SQMIX_F16 || a->dtype == SQMIX_BF16,
                     "gdn_decode: dtype %d", a->dtype);
-    SQMIX_CHECK_ARG(a->h_k >= 1 && a->h_v >= 1 && a->h_v % a->h_k == 0,
-                    "gdn_decode: h_v=%d must be a multiple of h_k=%d", a->h_v, a->h_k);
+    SQMIX_CHECK_ARG(a->h_k >= 1 && a->h_v >= 1 && a->h_v_offset >= 0 &&
+                        (a->h_v_offset > 0 || a->h_v % a->h_k == 0),
+                    "gdn_decode: h_v=%d must be a multiple of h_k=%d (h_v_offset=%d)", a->h_v, a->h_k,
+                    a->h_v_offset);
     SQMIX_CHECK_ARG(a->n_seqs >= 1 && a->n_tokens >= 1, "gdn_decode: n_seqs=%d T=%d", a->n_seqs,
                     a->n_tokens);
     SQMIX_CHECK_ARG(a->n_planes >= 1, "gdn_decode: n_planes=%d", a->n_planes);

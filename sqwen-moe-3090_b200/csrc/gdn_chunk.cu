@@ -71,6 +71,8 @@ struct ChunkParams {
     int64_t qk_st, v_st, qk_sseq, v_sseq;
     const float *g, *beta;
     int n_seqs, T_all, T, h_k, h_v, n_chunks;
+    int h_v_off;                   // layer index of value head 0 (value-head sharding)
+    const float *dt_bias, *ssm_a;  // gate epilogue (ssm_a NULL: g, beta as given)
     float l2_eps;
     float *ws;
     float *state;
@@ -137,7 +139,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     float *bt = G + kC;              // [64] beta
     float *gg = bt + kC;             // [64] g
     const int c = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
-    const int hk = h % p.h_k;
+    const int hk = (p.h_v_off + h) % p.h_k;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = c * kC;
     const int n_valid = min(kC, p.T - t0);
@@ -245,8 +247,14 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     }
     if (tid < kC) {
         const int64_t gb = (static_cast<int64_t>(seq) * p.T_all + t0 + tid) * p.h_v + h;
-        gg[tid] = tid < n_valid ? p.g[gb] : 0.f;
-        bt[tid] = tid < n_valid ? p.beta[gb] : 0.f;
+        float gv = 0.f, bv = 0.f;
+        if (tid < n_valid) {
+            gv = p.g[gb];
+            bv = p.beta[gb];
+            gdn_gates(gv, bv, p.dt_bias, p.ssm_a, p.h_v_off + h);
+        }
+        gg[tid] = gv;
+        bt[tid] = bv;
     }
     __syncthreads();
     if (warp == 0) {  // inclusive scan of g over the chunk (two values per lane)
@@ -737,8 +745,10 @@ extern "C" int sqmix_gdn_prefill(const sqmix_gdn_args *a, void *workspace, size_
                     "gdn_prefill: null pointer argument");
     SQMIX_CHECK_ARG(a->dtype == SQMIX_F32 || a->dtype == SQMIX_F16 || a->dtype == SQMIX_BF16,
                     "gdn_prefill: dtype %d", a->dtype);
-    SQMIX_CHECK_ARG(a->h_k >= 1 && a->h_v >= 1 && a->h_v % a->h_k == 0,
-                    "gdn_prefill: h_v=%d must be a multiple of h_k=%d", a->h_v, a->h_k);
+    SQMIX_CHECK_ARG(a->h_k >= 1 && a->h_v >= 1 && a->h_v_offset >= 0 &&
+                        (a->h_v_offset > 0 || a->h_v % a->h_k == 0),
+                    "gdn_prefill: h_v=%d must be a multiple of h_k=%d (h_v_offset=%d)", a->h_v, a->h_k,
+                    a->h_v_offset);
     SQMIX_CHECK_ARG(a->n_seqs >= 1 && a->n_seqs <= 65535 && a->n_tokens >= 1, "gdn_prefill: n_seqs=%d T=%d",
                     a->n_seqs, a->n_tokens);
     SQMIX_CHECK_ARG(a->n_planes >= 1, "gdn_prefill: n_planes=%d", a->n_planes);
@@ -785,6 +795,9 @@ extern "C" int sqmix_gdn_prefill(const sqmix_gdn_args *a, void *workspace, size_
     p.v_sseq = a->v_stride_seq;
     p.g = a->g;
     p.beta = a->beta;
+    p.h_v_off = a->h_v_offset;
+    p.dt_bias = a->dt_bias;
+    p.ssm_a = a->ssm_a;
     p.n_seqs = a->n_seqs;
     p.T_all = a->n_tokens;
     p.T = T_chunk;

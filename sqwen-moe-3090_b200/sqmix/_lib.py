@@ -109,7 +109,8 @@ class GdnArgs(ctypes.Structure):
         ("v_stride_seq", c_int64), ("g", c_void_p), ("beta", c_void_p), ("state", c_void_p),
         ("n_planes", c_int32), ("sel", c_void_p), ("n_seqs", c_int32), ("n_tokens", c_int32),
         ("h_k", c_int32), ("h_v", c_int32), ("n_snap", c_int32), ("l2_eps", c_float),
-        ("out", c_void_p), ("flags", c_int32),
+        ("out", c_void_p), ("flags", c_int32), ("h_v_offset", c_int32), ("dt_bias", c_void_p),
+        ("ssm_a", c_void_p),
     ]
 
 
@@ -158,7 +159,9 @@ _SIGNATURES = {
     "sqmix_peer_buffer_open": (ctypes.c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
     "sqmix_peer_buffer_close": (ctypes.c_int, [c_void_p]),
     "sqmix_peer_buffer_destroy": (ctypes.c_int, [c_void_p]),
+    "sqmix_peer_buffer_reset": (ctypes.c_int, [c_void_p, c_int32, c_void_p]),
     "sqmix_attn_merge_peers": (ctypes.c_int, [ctypes.POINTER(PeerMergeArgs), c_void_p]),
+    "sqmix_fa_decode_peers": (ctypes.c_int, [ctypes.POINTER(FaArgs), ctypes.POINTER(PeerMergeArgs), c_void_p]),
     "sqmix_fa_decode_batch": (ctypes.c_int, [ctypes.POINTER(FaBatchArgs), c_void_p]),
     "sqmix_gdn_prefill": (ctypes.c_int, [ctypes.POINTER(GdnArgs), c_void_p, c_size_t, c_void_p]),
     "sqmix_attn_merge_lse": (ctypes.c_int, [c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,

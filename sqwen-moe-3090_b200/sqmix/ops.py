@@ -302,7 +302,8 @@ def gated_delta_net(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.
                     sel: torch.Tensor | None = None, n_snap: int = 1, l2_eps: float = 0.0,
                     out: torch.Tensor | None = None, chunked: bool | None = None,
                     workspace: torch.Tensor | None = None, state_ready: bool = False,
-                    stream=None) -> torch.Tensor:
+                    h_v_offset: int = 0, dt_bias: torch.Tensor | None = None,
+                    ssm_a: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     """Gated delta rule over T tokens for n_seqs sequences.
 
     q, k [n_seqs][T][H_k][128]; v [n_seqs][T][H_v][128] (f32/bf16/f16); g, beta
@@ -313,6 +314,11 @@ def gated_delta_net(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.
     T >= GDN_CHUNK_MIN_T and the recurrent kernel (sqmix_gdn_decode) below.
     state_ready: the kernel launched just before on the stream writes neither the state
     nor sel (SQMIX_GDN_STATE_READY: the recurrent kernel reads the state early).
+    h_v_offset: value-head sharding -- the call's value head i is head h_v_offset + i of
+    the layer (q/k head (h_v_offset + i) % H_k; q and k hold all H_k heads).
+    ssm_a (and dt_bias), f32 [layer value heads]: g and beta are the raw projections
+    alpha and b; the kernels compute beta = sigmoid(b), g = softplus(alpha + dt_bias) *
+    ssm_a (gdn.rs:268-287).
     """
     _require_cuda(q, k, v, g, beta, state, sel)
     if q.dim() == 3:
@@ -333,7 +339,14 @@ def gated_delta_net(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.
         q=_ptr(q), k=_ptr(k), v=_ptr(v), dtype=_dt(q), qk_stride_tok=q.stride(1), v_stride_tok=v.stride(1),
         qk_stride_seq=q.stride(0), v_stride_seq=v.stride(0), g=_ptr(g), beta=_ptr(beta),
         state=_ptr(state), n_planes=int(n_planes), sel=_ptr(sel), n_seqs=n_seqs, n_tokens=T, h_k=H_k,
-        h_v=H_v, n_snap=int(n_snap), l2_eps=float(l2_eps), out=_ptr(out), flags=1 if state_ready else 0)
+        h_v=H_v, n_snap=int(n_snap), l2_eps=float(l2_eps), out=_ptr(out), flags=1 if state_ready else 0,
+        h_v_offset=int(h_v_offset), dt_bias=_ptr(dt_bias), ssm_a=_ptr(ssm_a))
+    for w in (dt_bias, ssm_a):
+        if w is not None and (w.dtype != torch.float32 or not w.is_contiguous() or not w.is_cuda
+                              or w.numel() < h_v_offset + H_v):
+            raise ValueError("dt_bias / ssm_a must be contiguous float32 CUDA tensors over the layer's value heads")
+    if dt_bias is not None and ssm_a is None:
+        raise ValueError("dt_bias needs ssm_a (the gate epilogue)")
     if chunked is None:
         chunked = T >= GDN_CHUNK_MIN_T
     if chunked:

@@ -1,13 +1,16 @@
 """Split-KV decode across ranks (one process per GPU, long-context decode).
 
 Each rank keeps a contiguous slice of every full-attention layer's keys in its own
-KvCache, computes normalised partial attention (O_p, LSE_p) over that slice with
-flash_attn_ext (RoPE positions offset by the slice start), and the partials of all
-ranks are gathered and merged with attn_merge_lse:
+KvCache, computes normalised partial attention (O_p, LSE_p) over that slice (RoPE
+positions offset by the slice start), and the partials of all ranks are merged:
     out = sum_p O_p exp(LSE_p - L) * sigmoid(gate),   L = log sum_p exp(LSE_p).
 This is exact: softmax over the union of disjoint key sets.  The step's new row is
-appended by the rank whose slice holds its position.  The gather is the only
-collective; with NCCL it runs over NVLink, with gloo on the host (tests).
+appended by the rank whose slice holds its position.
+
+PeerMerge.decode (sqmix_fa_decode_peers) does a layer in two launches: the decode and
+a split merge that exchanges the partials with the other ranks through peer memory
+over NVLink.  gather() + attn_merge_lse is the collective-library route (NCCL over
+NVLink, gloo on the host in the CPU tests).
 """
 from __future__ import annotations
 
@@ -16,8 +19,8 @@ from dataclasses import dataclass
 
 import torch
 
-from ._lib import PeerMergeArgs, check, lib
-from .ops import KV_PAD, _ptr, _stream
+from ._lib import SQMIX_FA_OVERLAP_PREV, PeerMergeArgs, check, lib
+from .ops import KV_PAD, _fa_args, _ptr, _stream, new_fa_workspace
 
 GROUP = 16  # slices start on 16-token groups of the tiled cache
 
@@ -144,6 +147,35 @@ class PeerMerge:
                           out=_ptr(out), lse_out=_ptr(lse_out), status=_ptr(self.status))
         check(lib().sqmix_attn_merge_peers(ctypes.byref(a), _stream(stream)), "attn_merge_peers")
         return out
+
+    def decode(self, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, capacity: int,
+               n_kv: torch.Tensor, q_pos0: torch.Tensor, slot: int, gate: torch.Tensor | None = None,
+               out: torch.Tensor | None = None, lse: torch.Tensor | None = None, scale: float = 1.0 / 16.0,
+               rope_n_rot: int = 0, rope_freq_base: float = 1e7, rope_pos_offset: int = 0,
+               workspace: torch.Tensor | None = None, n_splits: int = 0, config: int = 0,
+               k_new: torch.Tensor | None = None, v_new: torch.Tensor | None = None, overlap_prev: bool = False,
+               stream=None) -> torch.Tensor:
+        """One layer of split-KV decode (sqmix_fa_decode_peers): attention of q [n_q][16][256]
+        over this rank's key slice (n_kv, q_pos0 in slice rows; rope_pos_offset = the slice
+        start), the exchange with every other rank and the merged, gated output over all
+        ranks' keys in `out` [n_q][16][256] (and the merged LSE in `lse`).  Arguments as for
+        flash_attn_ext; the rank owning the step's rows passes k_new / v_new."""
+        if workspace is None:
+            workspace = new_fa_workspace(q.shape[0], n_splits, q.device)
+        a, out = _fa_args(q, k_cache, v_cache, capacity, n_kv, q_pos0, gate, scale, rope_n_rot, rope_freq_base,
+                          rope_pos_offset, out, lse, workspace, n_splits, config, k_new, v_new,
+                          SQMIX_FA_OVERLAP_PREV if overlap_prev else 0)
+        pm = PeerMergeArgs(n_ranks=self.world, rank=self.rank, slot=int(slot), n_slots=self.n_slots,
+                           rows=16 * a.n_q, buffers=_ptr(self.ptrs), status=_ptr(self.status))
+        check(lib().sqmix_fa_decode_peers(ctypes.byref(a), ctypes.byref(pm), _stream(stream)), "fa_decode_peers")
+        return out
+
+    def reset(self, stream=None) -> None:
+        """Zero this rank's buffer and status (every rank, after all have stopped calling):
+        the way back to a consistent state after a wait gave up."""
+        check(lib().sqmix_peer_buffer_reset(ctypes.c_void_p(self._own), self.n_slots, _stream(stream)),
+              "peer_buffer_reset")
+        self.status.zero_()
 
     def ok(self) -> bool:
         """False if a bounded wait for a peer gave up (synchronises)."""

@@ -79,10 +79,11 @@ def dequantized_cache(sq, oracle, kc, vc, cap, n_kv):
     return kd, vd
 
 
-@pytest.mark.parametrize("n_q", [1, 2])
-def test_decode_config3_172k_keys(sq, oracle, n_q):
-    """Configuration 3: 172 032 keys, default split count (one per SM), the step's n_q rows
-    appended by the decode kernel itself (n_new = n_q), RoPE 64 / 1e7, sigmoid gate."""
+@pytest.mark.parametrize("n_q,configs", [(1, (0, 3, 4, 5)), (2, (0, 2, 6))])
+def test_decode_config3_172k_keys(sq, oracle, n_q, configs):
+    """Configuration 3: 172 032 keys, default split count of each kernel configuration,
+    the step's n_q rows appended by the decode kernel itself (n_new = n_q; rewritten
+    identically by every configuration), RoPE 64 / 1e7, sigmoid gate."""
     n_kv = 172032
     q_pos0 = n_kv - n_q
     rng = np.random.default_rng(172032 + n_q)
@@ -94,20 +95,24 @@ def test_decode_config3_172k_keys(sq, oracle, n_q):
     kc, vc = import_rows(sq, oracle, k[:q_pos0], v[:q_pos0], cap)
     d_nkv = torch.tensor([n_kv], dtype=torch.int64, device="cuda")
     d_pos = torch.tensor([q_pos0], dtype=torch.int64, device="cuda")
-    lse = torch.empty((n_q, 16), dtype=torch.float32, device="cuda")
-    out = sq.flash_attn_ext(torch.from_numpy(q).cuda(), kc, vc, cap, d_nkv, d_pos, gate=torch.from_numpy(gate).cuda(),
-                            rope_n_rot=N_ROT, rope_freq_base=THETA, lse=lse,
-                            k_new=torch.from_numpy(k[q_pos0:]).cuda(), v_new=torch.from_numpy(v[q_pos0:]).cuda())
-    torch.cuda.synchronize()
-    got, got_lse = out.cpu().numpy(), lse.cpu().numpy()
+    results = {}
+    for config in configs:
+        lse = torch.empty((n_q, 16), dtype=torch.float32, device="cuda")
+        out = sq.flash_attn_ext(torch.from_numpy(q).cuda(), kc, vc, cap, d_nkv, d_pos,
+                                gate=torch.from_numpy(gate).cuda(), rope_n_rot=N_ROT, rope_freq_base=THETA, lse=lse,
+                                k_new=torch.from_numpy(k[q_pos0:]).cuda(), v_new=torch.from_numpy(v[q_pos0:]).cuda(),
+                                config=config)
+        torch.cuda.synchronize()
+        results[config] = (out.cpu().numpy(), lse.cpu().numpy())
     check_appended_rows(sq, oracle, kc, vc, cap, k[q_pos0:], v[q_pos0:], q_pos0)
     kd, vd = dequantized_cache(sq, oracle, kc, vc, cap, n_kv)
     del k, v
     want, wlse = oracle.attn(oracle.rope_text(q, q_pos0, THETA, N_ROT), kd, vd, gate, q_pos0=q_pos0, scale=1 / 16,
                              want_lse=True)
-    assert np.isfinite(got).all()
-    assert rel_err(got, want) <= ATTN_TOL
-    assert np.abs(got_lse - wlse).max() < 1e-3
+    for config, (got, got_lse) in results.items():
+        assert np.isfinite(got).all(), config
+        assert rel_err(got, want) <= ATTN_TOL, config
+        assert np.abs(got_lse - wlse).max() < 1e-3, config
 
 
 @pytest.mark.parametrize("T", [512, 2048])

@@ -138,12 +138,12 @@ def test_convert_roundtrip_and_layout(sq):
 
 # ------------------------------------------------------ attention decode ---
 
-def run_fa(sq, q, kc, vc, cap, n_kv, q_pos0, gate=None, rope=0, n_splits=0, lse=False):
+def run_fa(sq, q, kc, vc, cap, n_kv, q_pos0, gate=None, rope=0, n_splits=0, lse=False, config=0):
     dev_nkv = torch.tensor([n_kv], dtype=torch.int64, device="cuda")
     dev_pos = torch.tensor([q_pos0], dtype=torch.int64, device="cuda")
     lse_t = torch.empty((q.shape[0], 16), dtype=torch.float32, device="cuda") if lse else None
     out = sq.flash_attn_ext(q, kc, vc, cap, dev_nkv, dev_pos, gate=gate, rope_n_rot=rope,
-                            rope_freq_base=1e7, lse=lse_t, n_splits=n_splits)
+                            rope_freq_base=1e7, lse=lse_t, n_splits=n_splits, config=config)
     torch.cuda.synchronize()
     return out.cpu().numpy(), (lse_t.cpu().numpy() if lse else None)
 
@@ -212,15 +212,15 @@ def test_fa_decode_config0(sq, oracle):
 
 
 @pytest.mark.parametrize("n_kv", [1, 15, 16, 17, 31, 33, 64, 65, 255, 257, 1000])
-@pytest.mark.parametrize("n_q", [1, 2])
-def test_fa_decode_ragged(sq, oracle, n_kv, n_q):
+@pytest.mark.parametrize("n_q,config", [(1, 0), (2, 0), (1, 4), (2, 6)])
+def test_fa_decode_ragged(sq, oracle, n_kv, n_q, config):
     rng = np.random.default_rng(100 + n_kv * 3 + n_q)
     _, _, kq, vq, kd, vd = quantized_kv(oracle, rng, n_kv)
     cap = cap_for(n_kv)
     kc, vc = make_cache_from_rows(sq, kq, vq, cap)
     q = rng.standard_normal((n_q, 16, 256)).astype(np.float32)
     q_pos0 = max(n_kv - n_q, 0)
-    out, lse = run_fa(sq, torch.from_numpy(q).cuda(), kc, vc, cap, n_kv, q_pos0, lse=True)
+    out, lse = run_fa(sq, torch.from_numpy(q).cuda(), kc, vc, cap, n_kv, q_pos0, lse=True, config=config)
     want, wlse = oracle.attn(q, kd, vd, None, q_pos0=q_pos0, scale=1 / 16, want_lse=True)
     assert rel_err(out, want) <= ATTN_TOL
     assert np.abs(lse - wlse).max() < 1e-3
@@ -240,10 +240,13 @@ def test_fa_decode_split_counts(sq, oracle, n_splits):
     assert np.abs(lse - wlse).max() < 1e-3
 
 
+@pytest.mark.parametrize("config", [3, 4, 5])
 @pytest.mark.parametrize("n_kv,n_splits", [(1, 0), (17, 3), (257, 0), (1000, 7), (5000, 0), (5000, 300)])
-def test_fa_decode_config3_twelve_warps(sq, oracle, n_kv, n_splits):
-    """Configuration 3 (n_q 1, 6 warps per KV head, 3 x 55.3 KB ring slots): RoPE, gate,
-    lse and the fused append of the step's row, against the oracle."""
+def test_fa_decode_config3_twelve_warps(sq, oracle, n_kv, n_splits, config):
+    """The n_q = 1 configurations 3 (6 warps per KV head, 3 x 55.3 KB ring slots), 4 (two
+    CTAs per SM, 4 warps per KV head, the one-MMA V offset correction) and 5 (3 with that
+    correction): RoPE, gate, lse and the fused append of the step's row, against the
+    oracle."""
     rng = np.random.default_rng(90 + n_kv + n_splits)
     k = rng.standard_normal((n_kv, 2, 256)).astype(np.float32)
     v = rng.standard_normal((n_kv, 2, 256)).astype(np.float32)
@@ -262,7 +265,7 @@ def test_fa_decode_config3_twelve_warps(sq, oracle, n_kv, n_splits):
                             torch.tensor([n_kv], dtype=torch.int64, device="cuda"),
                             torch.tensor([q_pos0], dtype=torch.int64, device="cuda"),
                             gate=torch.from_numpy(gate).cuda(), rope_n_rot=64, rope_freq_base=1e7, lse=lse,
-                            k_new=kd_t[q_pos0:], v_new=vd_t[q_pos0:], workspace=ws, n_splits=n_splits, config=3)
+                            k_new=kd_t[q_pos0:], v_new=vd_t[q_pos0:], workspace=ws, n_splits=n_splits, config=config)
     torch.cuda.synchronize()
     sq.fa_status(ws)
     kq = oracle.q4_0_quantize(oracle.rope_text(k, 0, 1e7, 64).reshape(n_kv, 512))
@@ -277,10 +280,10 @@ def test_fa_decode_config3_twelve_warps(sq, oracle, n_kv, n_splits):
     assert np.abs(lse.cpu().numpy() - wlse).max() < 1e-3
 
 
-@pytest.mark.parametrize("n_q", [1, 2])
+@pytest.mark.parametrize("n_q,config", [(1, 0), (2, 0), (1, 4), (1, 5), (2, 6)])
 @pytest.mark.parametrize("n_splits", [1, 0])
 @pytest.mark.parametrize("v_amax", [1.0, 60000.0])
-def test_fa_decode_rising_scores(sq, oracle, n_q, n_splits, v_amax):
+def test_fa_decode_rising_scores(sq, oracle, n_q, config, n_splits, v_amax):
     """Scores that climb along the cache (about 0.3 log2 units per 16-token group), so the
     running maximum keeps moving past the lazy-update threshold in every warp, with V
     blocks up to `v_amax` (60000: P * V scale stays near the top of the f16 range)."""
@@ -301,7 +304,8 @@ def test_fa_decode_rising_scores(sq, oracle, n_q, n_splits, v_amax):
     cap = cap_for(n_kv)
     kc, vc = make_cache_from_rows(sq, kq, vq, cap)
     q_pos0 = n_kv - n_q
-    out, lse = run_fa(sq, torch.from_numpy(q).cuda(), kc, vc, cap, n_kv, q_pos0, n_splits=n_splits, lse=True)
+    out, lse = run_fa(sq, torch.from_numpy(q).cuda(), kc, vc, cap, n_kv, q_pos0, n_splits=n_splits, lse=True,
+                      config=config)
     want, wlse = oracle.attn(q, kd, vd, None, q_pos0=q_pos0, scale=1 / 16, want_lse=True)
     assert np.isfinite(out).all()
     assert rel_err(out, want) <= ATTN_TOL
