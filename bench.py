@@ -971,6 +971,7 @@ def bench_gdn(steps: int, warmup: int):
     res["prefill512"] = {"us": us, "tok_s": T / us * 1e6, "tflops_chunked_form": flops / us / 1e6,
                          "note": "one layer, chunk 64, eager launches"}
     res["front_end"] = bench_gdn_front(g, dev, steps, warmup, hbm, hbm_kind)
+    res["layer_decode"] = bench_gdn_layer(g, dev, steps, warmup, hbm, hbm_kind)
     res["config"] = "config1: 32 value heads over 16 q/k heads, d 128, bf16 q/k/v, fused L2 norm"
     return res
 
@@ -1059,6 +1060,54 @@ def stack_lengths():
     order, so the long splits start first)."""
     rng = np.random.default_rng(17)
     return np.sort(rng.integers(1024, 32768 + 1, STACK_SEQS))[::-1]
+
+
+def bench_gdn_layer(g, dev, steps: int, warmup: int, hbm: float, hbm_kind: str) -> dict:
+    """A whole GDN mixer decode step at batch 1 (config 1 shapes): the one-launch layer
+    (sqmix_gdn_layer_decode: conv + SiLU + L2 norm + gate epilogue + recurrence +
+    norm_gated) against the three launches it replaces (conv, recurrence with the gate
+    epilogue, norm_gated); 30 layers' buffers cycled (states 63 MB, conv planes 2.9 MB)."""
+    import torch
+
+    import sqmix
+
+    C, K, n_layers, reps = 8192, 4, 30, max(3, steps)
+    x = torch.randn((n_layers, 1, 1, C), generator=g, device=dev).to(torch.bfloat16)
+    w = torch.randn((n_layers, C, K), generator=g, device=dev) * 0.5
+    cst = torch.randn((n_layers, 1, 1, C, K - 1), generator=g, device=dev)
+    S = torch.randn((n_layers, 1, 1, 32, 128, 128), generator=g, device=dev) * 0.02
+    alpha = torch.randn((n_layers, 1, 1, 32), generator=g, device=dev)
+    braw = torch.randn((n_layers, 1, 1, 32), generator=g, device=dev)
+    dt = torch.randn((n_layers, 32), generator=g, device=dev)
+    ssm_a = -torch.exp(torch.rand((n_layers, 32), generator=g, device=dev) * 2.7)
+    z = torch.randn((n_layers, 1, 1, 32, 128), generator=g, device=dev).to(torch.bfloat16)
+    wn = torch.rand((n_layers, 128), generator=g, device=dev) + 0.5
+    y = torch.empty((1, 1, 32, 128), device=dev)
+    conv = torch.empty((1, 1, C), device=dev)
+    o = torch.empty((1, 1, 32, 128), device=dev)
+
+    def fused():
+        for l in range(n_layers):
+            sqmix.gdn_layer_decode(x[l], w[l], cst[l], alpha[l], braw[l], ssm_a[l], S[l], dt_bias=dt[l], l2_eps=1e-6,
+                                   z=z[l], norm_weight=wn[l], out=y, state_ready=True)
+
+    def three():
+        for l in range(n_layers):
+            sqmix.gdn_conv(x[l], w[l], cst[l], n_qk_channels=4096, l2_eps=1e-6, out=conv)
+            sqmix.gated_delta_net(conv[:, :, :2048].view(1, 1, 16, 128), conv[:, :, 2048:4096].view(1, 1, 16, 128),
+                                  conv[:, :, 4096:].view(1, 1, 32, 128), alpha[l], braw[l], S[l], out=o,
+                                  dt_bias=dt[l], ssm_a=ssm_a[l])
+            sqmix.head_norm(o[0], 1e-6, weight=wn[l], z=z[l, 0], out=y[0])
+
+    us_f = _graph_us(fused, n_layers, reps, warmup)
+    us_3 = _graph_us(three, n_layers, reps, warmup)
+    alg = 2 * GDN_STATE_BYTES + 2 * C * (K - 1) * 4 + C * K * 4 + C * 2 + 32 * 128 * (2 + 4) + 128 * 4
+    return {"us_per_layer_token": us_f, "three_launch_us": us_3, "alg_bytes": alg,
+            "achieved_gbs": alg / us_f / 1e3, "frac_of_hbm": alg / us_f / 1e3 / hbm, "peak_gbs": hbm,
+            "peak_kind": hbm_kind,
+            "note": "batch 1, 1 token: conv + SiLU + q/k L2 norm + beta/decay epilogue + recurrence + norm_gated; "
+                    "CUDA graph of 30 layers (buffers cycled); three_launch_us = sqmix_gdn_conv + sqmix_gdn_decode + "
+                    "sqmix_head_norm for the same work"}
 
 
 def bench_stack(steps: int, warmup: int, rank: int = 0, world: int = 1, local_rank: int = 0,

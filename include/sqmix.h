@@ -81,6 +81,7 @@ int sqmix_device_sm_count(int device);
 #define SQMIX_ABI_GDN_ARGS 5
 #define SQMIX_ABI_GDN_CONV_ARGS 6
 #define SQMIX_ABI_HEAD_NORM_ARGS 7
+#define SQMIX_ABI_GDN_LAYER_ARGS 8
 size_t sqmix_abi_struct_size(int32_t which);
 int32_t sqmix_abi_field_count(int32_t which);
 int64_t sqmix_abi_field_offset(int32_t which, int32_t field);
@@ -425,6 +426,51 @@ int sqmix_gdn_prefill(const sqmix_gdn_args *args, void *workspace, size_t worksp
  * caller wants a materialised plane).  Device pointers. */
 int sqmix_gdn_state_copy(float *dst, const float *src, int64_t plane_elems, int32_t n_planes,
                          sqmix_stream_t stream);
+
+/* A GDN mixer decode step in ONE launch (T = 1 or 2 tokens per sequence): the front
+ * end of sqmix_gdn_conv (short conv + SiLU over the resident history planes, q/k L2
+ * norm, history slots), the gate epilogue (beta = sigmoid(b), g = softplus(alpha +
+ * dt_bias) * ssm_a, gdn.rs:268-287), the recurrence of sqmix_gdn_decode (plane sel in,
+ * planes 0..n_snap-1 out) and norm_gated (rms_norm(o) * norm_weight * silu(z),
+ * gdn.rs:150-181), i.e. gdn.rs:290-577 between the projections and the output
+ * projection.  Whole layers only (no value-head offset); conv kernel 4; H_v = H_k or
+ * 2 H_k; head_dim 128.  Launched as clusters of 4 H_v / H_k CTAs per q/k head, with
+ * programmatic stream serialisation; SQMIX_GDN_STATE_READY: the kernel launched just
+ * before writes neither the state planes, the conv planes nor sel, and the state is
+ * read before waiting for it. */
+typedef struct sqmix_gdn_layer_args {
+    const void *x;            /* [n_seqs][T][C] qkv_mixed, C = (2 H_k + H_v) * 128 */
+    int32_t x_dtype;
+    int64_t x_stride_tok;
+    int64_t x_stride_seq;
+    const float *conv_weight; /* [C][kernel] ssm_conv1d */
+    float *conv_state;        /* [n_seqs][n_planes][C][kernel - 1] */
+    int32_t kernel;           /* 4 */
+    const float *alpha;       /* [n_seqs][T][H_v] W_alpha h */
+    const float *beta;        /* [n_seqs][T][H_v] W_beta h (before the sigmoid) */
+    const float *dt_bias;     /* nullable [H_v] ssm_dt */
+    const float *ssm_a;       /* [H_v] -exp(A_log) */
+    float *state;             /* [n_seqs][n_planes][H_v][128][128] */
+    int32_t n_planes;
+    const int32_t *sel;       /* nullable device I32 [n_seqs]: plane read (state and conv) */
+    int32_t n_snap;           /* 1 <= n_snap <= min(T, n_planes) */
+    int32_t n_seqs;
+    int32_t n_tokens;         /* 1 or 2 */
+    int32_t h_k;              /* 16 */
+    int32_t h_v;              /* 32 */
+    float l2_eps;             /* q/k L2 norm (norm_rms_eps); 0: none */
+    const void *z;            /* nullable [n_seqs][T][H_v][128] gate projection */
+    int32_t z_dtype;
+    int64_t z_stride_tok;
+    int64_t z_stride_seq;
+    const float *norm_weight; /* nullable: [128] ssm_norm, or per head (stride below) */
+    int64_t norm_weight_stride_head; /* 0: one row shared by all heads */
+    float norm_eps;           /* norm_rms_eps */
+    float *out;               /* [n_seqs][T][H_v][128] f32 */
+    int32_t flags;            /* SQMIX_GDN_STATE_READY or 0 */
+} sqmix_gdn_layer_args;
+
+int sqmix_gdn_layer_decode(const sqmix_gdn_layer_args *args, sqmix_stream_t stream);
 
 /* ========================================================================
  * GDN front end and the mixers' per-head norms

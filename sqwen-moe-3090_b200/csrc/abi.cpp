@@ -111,6 +111,24 @@ const size_t kHeadNorm[] = {
     OFF(sqmix_head_norm_args, out_stride_head),
 };
 
+const size_t kGdnLayer[] = {
+    OFF(sqmix_gdn_layer_args, x),              OFF(sqmix_gdn_layer_args, x_dtype),
+    OFF(sqmix_gdn_layer_args, x_stride_tok),   OFF(sqmix_gdn_layer_args, x_stride_seq),
+    OFF(sqmix_gdn_layer_args, conv_weight),    OFF(sqmix_gdn_layer_args, conv_state),
+    OFF(sqmix_gdn_layer_args, kernel),         OFF(sqmix_gdn_layer_args, alpha),
+    OFF(sqmix_gdn_layer_args, beta),           OFF(sqmix_gdn_layer_args, dt_bias),
+    OFF(sqmix_gdn_layer_args, ssm_a),          OFF(sqmix_gdn_layer_args, state),
+    OFF(sqmix_gdn_layer_args, n_planes),       OFF(sqmix_gdn_layer_args, sel),
+    OFF(sqmix_gdn_layer_args, n_snap),         OFF(sqmix_gdn_layer_args, n_seqs),
+    OFF(sqmix_gdn_layer_args, n_tokens),       OFF(sqmix_gdn_layer_args, h_k),
+    OFF(sqmix_gdn_layer_args, h_v),            OFF(sqmix_gdn_layer_args, l2_eps),
+    OFF(sqmix_gdn_layer_args, z),              OFF(sqmix_gdn_layer_args, z_dtype),
+    OFF(sqmix_gdn_layer_args, z_stride_tok),   OFF(sqmix_gdn_layer_args, z_stride_seq),
+    OFF(sqmix_gdn_layer_args, norm_weight),    OFF(sqmix_gdn_layer_args, norm_weight_stride_head),
+    OFF(sqmix_gdn_layer_args, norm_eps),       OFF(sqmix_gdn_layer_args, out),
+    OFF(sqmix_gdn_layer_args, flags),
+};
+
 #undef OFF
 
 struct Entry {
@@ -133,6 +151,7 @@ bool lookup(int32_t which, Entry *e) {
         case SQMIX_ABI_GDN_ARGS: *e = entry(sizeof(sqmix_gdn_args), kGdn); return true;
         case SQMIX_ABI_GDN_CONV_ARGS: *e = entry(sizeof(sqmix_gdn_conv_args), kGdnConv); return true;
         case SQMIX_ABI_HEAD_NORM_ARGS: *e = entry(sizeof(sqmix_head_norm_args), kHeadNorm); return true;
+        case SQMIX_ABI_GDN_LAYER_ARGS: *e = entry(sizeof(sqmix_gdn_layer_args), kGdnLayer); return true;
         default: return false;
     }
 }

@@ -33,6 +33,7 @@ SQMIX_ABI_PEER_MERGE_ARGS = 4
 SQMIX_ABI_GDN_ARGS = 5
 SQMIX_ABI_GDN_CONV_ARGS = 6
 SQMIX_ABI_HEAD_NORM_ARGS = 7
+SQMIX_ABI_GDN_LAYER_ARGS = 8
 
 ERROR_NAMES = {
     SQMIX_EINVAL: "SQMIX_EINVAL",
@@ -134,6 +135,18 @@ class HeadNormArgs(ctypes.Structure):
     ]
 
 
+class GdnLayerArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", c_void_p), ("x_dtype", c_int32), ("x_stride_tok", c_int64), ("x_stride_seq", c_int64),
+        ("conv_weight", c_void_p), ("conv_state", c_void_p), ("kernel", c_int32), ("alpha", c_void_p),
+        ("beta", c_void_p), ("dt_bias", c_void_p), ("ssm_a", c_void_p), ("state", c_void_p),
+        ("n_planes", c_int32), ("sel", c_void_p), ("n_snap", c_int32), ("n_seqs", c_int32),
+        ("n_tokens", c_int32), ("h_k", c_int32), ("h_v", c_int32), ("l2_eps", c_float), ("z", c_void_p),
+        ("z_dtype", c_int32), ("z_stride_tok", c_int64), ("z_stride_seq", c_int64), ("norm_weight", c_void_p),
+        ("norm_weight_stride_head", c_int64), ("norm_eps", c_float), ("out", c_void_p), ("flags", c_int32),
+    ]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "sqmix_version": (ctypes.c_char_p, []),
@@ -170,6 +183,7 @@ _SIGNATURES = {
     "sqmix_gdn_state_copy": (ctypes.c_int, [c_void_p, c_void_p, c_int64, c_int32, c_void_p]),
     "sqmix_gdn_conv": (ctypes.c_int, [ctypes.POINTER(GdnConvArgs), c_void_p]),
     "sqmix_head_norm": (ctypes.c_int, [ctypes.POINTER(HeadNormArgs), c_void_p]),
+    "sqmix_gdn_layer_decode": (ctypes.c_int, [ctypes.POINTER(GdnLayerArgs), c_void_p]),
     "sqmix_kvcache_create": (ctypes.c_int, [c_int32, c_int64, c_int32, ctypes.POINTER(c_void_p)]),
     "sqmix_kvcache_destroy": (None, [c_void_p]),
     "sqmix_kvcache_zero": (ctypes.c_int, [c_void_p, c_void_p]),

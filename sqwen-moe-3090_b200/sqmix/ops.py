@@ -22,7 +22,7 @@ import math
 import torch
 
 from ._lib import (SQMIX_BF16, SQMIX_F16, SQMIX_F32, SQMIX_FA_OVERLAP_PREV, FaArgs, FaBatchArgs, GdnArgs, GdnConvArgs,
-                   HeadNormArgs, KvAppendArgs, check, lib)
+                   GdnLayerArgs, HeadNormArgs, KvAppendArgs, check, lib)
 
 HEAD_DIM = 256
 N_HEAD = 16
@@ -427,6 +427,47 @@ def head_norm(x: torch.Tensor, eps: float = 1e-6, weight: torch.Tensor | None = 
                      n_tokens=T, n_heads=H, head_dim=d, eps=float(eps), out=_ptr(out),
                      out_stride_tok=out.stride(0), out_stride_head=out.stride(1))
     check(lib().sqmix_head_norm(ctypes.byref(a), _stream(stream)), "head_norm")
+    return out
+
+
+def gdn_layer_decode(x: torch.Tensor, conv_weight: torch.Tensor, conv_state: torch.Tensor, alpha: torch.Tensor,
+                     beta: torch.Tensor, ssm_a: torch.Tensor, state: torch.Tensor, h_k: int = 16, h_v: int = 32,
+                     dt_bias: torch.Tensor | None = None, n_planes: int = 1, sel: torch.Tensor | None = None,
+                     n_snap: int = 1, l2_eps: float = 1e-6, z: torch.Tensor | None = None,
+                     norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6, out: torch.Tensor | None = None,
+                     state_ready: bool = False, stream=None) -> torch.Tensor:
+    """A GDN mixer decode step in one launch (sqmix_gdn_layer_decode): x [n_seqs][T][C]
+    qkv_mixed (T = 1 or 2, C = (2 h_k + h_v) * 128); conv_weight [C][4]; conv_state
+    [n_seqs][n_planes][C][3] and state [n_seqs][n_planes][h_v][128][128] (updated in place,
+    input plane sel[seq]); alpha, beta [n_seqs][T][h_v] raw projections; ssm_a, dt_bias
+    [h_v]; z [n_seqs][T][h_v][128]; norm_weight [128] (or [h_v][128]).  Returns
+    norm_gated(o) [n_seqs][T][h_v][128] f32."""
+    _require_cuda(x, conv_weight, conv_state, alpha, beta, ssm_a, state, dt_bias, sel, z, norm_weight)
+    if x.dim() == 2:
+        x = x[None]
+    n_seqs, T, C = x.shape
+    if x.stride(-1) != 1:
+        raise ValueError("x rows must be contiguous")
+    for t in (alpha, beta, ssm_a, dt_bias, norm_weight, conv_weight, conv_state, state):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()):
+            raise ValueError("float32 contiguous tensors expected for the weights, gates and states")
+    if z is not None:
+        z = z.reshape(n_seqs, T, h_v, GDN_D)
+        if z.stride(-1) != 1 or z.stride(-2) != GDN_D:
+            raise ValueError("z heads must be contiguous [.., h_v, 128]")
+    if out is None:
+        out = torch.empty((n_seqs, T, h_v, GDN_D), dtype=torch.float32, device=x.device)
+    nw_sh = 0 if norm_weight is None or norm_weight.numel() == GDN_D else GDN_D
+    a = GdnLayerArgs(
+        x=_ptr(x), x_dtype=_dt(x), x_stride_tok=x.stride(1), x_stride_seq=x.stride(0),
+        conv_weight=_ptr(conv_weight), conv_state=_ptr(conv_state), kernel=conv_weight.shape[-1],
+        alpha=_ptr(alpha), beta=_ptr(beta), dt_bias=_ptr(dt_bias), ssm_a=_ptr(ssm_a), state=_ptr(state),
+        n_planes=int(n_planes), sel=_ptr(sel), n_snap=int(n_snap), n_seqs=n_seqs, n_tokens=T, h_k=int(h_k),
+        h_v=int(h_v), l2_eps=float(l2_eps), z=_ptr(z), z_dtype=_dt(z) if z is not None else 0,
+        z_stride_tok=z.stride(1) if z is not None else 0, z_stride_seq=z.stride(0) if z is not None else 0,
+        norm_weight=_ptr(norm_weight), norm_weight_stride_head=nw_sh, norm_eps=float(norm_eps), out=_ptr(out),
+        flags=1 if state_ready else 0)
+    check(lib().sqmix_gdn_layer_decode(ctypes.byref(a), _stream(stream)), "gdn_layer_decode")
     return out
 
 

@@ -210,6 +210,7 @@ def _abi_structs():
         "sqmix_gdn_args": (L.SQMIX_ABI_GDN_ARGS, L.GdnArgs),
         "sqmix_gdn_conv_args": (L.SQMIX_ABI_GDN_CONV_ARGS, L.GdnConvArgs),
         "sqmix_head_norm_args": (L.SQMIX_ABI_HEAD_NORM_ARGS, L.HeadNormArgs),
+        "sqmix_gdn_layer_args": (L.SQMIX_ABI_GDN_LAYER_ARGS, L.GdnLayerArgs),
     }
 
 
