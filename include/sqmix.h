@@ -82,6 +82,8 @@ int sqmix_device_sm_count(int device);
 #define SQMIX_ABI_GDN_CONV_ARGS 6
 #define SQMIX_ABI_HEAD_NORM_ARGS 7
 #define SQMIX_ABI_GDN_LAYER_ARGS 8
+#define SQMIX_ABI_GGML_FA_OP 9
+#define SQMIX_ABI_GGML_GDN_OP 10
 size_t sqmix_abi_struct_size(int32_t which);
 int32_t sqmix_abi_field_count(int32_t which);
 int64_t sqmix_abi_field_offset(int32_t which, int32_t field);
@@ -386,7 +388,7 @@ typedef struct sqmix_gdn_args {
      * recurrence): value head i of this call is head h_v_offset + i of the layer and
      * reads q/k head (h_v_offset + i) % h_k; q and k hold all h_k heads, while v, g,
      * beta, the state planes and out hold this call's h_v heads.  0 for a whole layer
-     * (which then needs h_v % h_k == 0, the tiling of gdn.rs:436-441). */
+     * (whose h_v is a multiple of h_k: the tiling of gdn.rs:436-441). */
     int32_t h_v_offset;
     /* Gate epilogue of the projections (gdn.rs:268-287).  ssm_a == NULL: g and beta are
      * the log-decay and beta themselves.  Otherwise g holds alpha = W_alpha h and beta
@@ -540,6 +542,77 @@ typedef struct sqmix_head_norm_args {
 } sqmix_head_norm_args;
 
 int sqmix_head_norm(const sqmix_head_norm_args *args, sqmix_stream_t stream);
+
+/* ========================================================================
+ * ggml custom-op bridge
+ *
+ * sqwen executes one ggml graph per step and replays it as a CUDA graph
+ * (src/engine/runner.rs:362-389); its FFI enumerates ggml's custom ops
+ * (GGML_OP_MAP_CUSTOM1..3, GGML_OP_CUSTOM: src/backend/ffi.rs:199-202).  The callbacks
+ * below have ggml's custom-op signature (ggml_custom_op_t: dst, thread ith of nth,
+ * userdata) so that a graph node built with ggml_custom_4d can run a sqmix kernel on
+ * the node's tensors: dst and its sources are read through ggml's tensor layout (the
+ * struct ggml_tensor that sqwen's FFI mirrors at src/backend/ffi.rs:22-39: type, ne[4],
+ * nb[4] in bytes, src[10], data), the kernel is launched by thread 0 on the stream in
+ * the userdata, and the status is stored there (the callback returns void).  Positions
+ * and lengths come from a device tensor, so a replayed graph stays correct with fixed
+ * pointers.  sqmix_ggml_*_args only translate a node into the argument struct (no CUDA
+ * call), for checking a graph's wiring.
+ *
+ * FA decode node (the tensors of ggml_flash_attn_ext, attn.rs:238-249):
+ *   dst    F32 [256, 16, T]  output (gated if src[4] is set)
+ *   src[0] Q   [256, T, 16]  F32 / F16 / BF16, any token and head strides (nb[0] = element)
+ *   src[1] K   tiled q4_0 cache as a Q4_0 tensor [512, capacity] (the bytes of ggml's
+ *              [n_embd_k_gqa, cap] q4_0 cache, kv.rs:124-134, in sqmix's tiled order)
+ *   src[2] V   likewise
+ *   src[3] I64 [2] device {n_kv, q_pos0}
+ *   src[4] gate [256, 16, T] or NULL
+ *   src[5] k_new, src[6] v_new: [256, 2, n_new] rows to append (both or neither)
+ * GDN decode node (ggml_gated_delta_net, gdn.rs:489-500):
+ *   dst    F32 [128, H_v, T, n_seqs]
+ *   src[0] q [128, H_k, T, n_seqs], src[1] k (same layout), src[2] v [128, H_v, T, n_seqs]
+ *          (F32 / F16 / BF16, heads contiguous)
+ *   src[3] g, src[4] beta: F32 [1, H_v, T, n_seqs] contiguous (raw alpha / b when the
+ *          op's ssm_a is set)
+ *   src[5] state F32 [128*128*H_v, n_planes, n_seqs]; src[6] sel I32 [n_seqs] or NULL
+ * ======================================================================== */
+struct ggml_tensor;
+
+typedef struct sqmix_ggml_fa_op {
+    float scale;
+    int32_t rope_n_rot;
+    float rope_freq_base;
+    int64_t rope_pos_offset;
+    int32_t n_splits;         /* 0: the default of the configuration */
+    int32_t config;
+    int32_t flags;            /* SQMIX_FA_* */
+    const float *q_norm;      /* nullable */
+    const float *k_norm;      /* nullable */
+    float norm_eps;
+    void *workspace;          /* NULL: sqmix_fa_decode_noalloc (no allocation in the callback) */
+    size_t workspace_bytes;
+    sqmix_stream_t stream;    /* the stream the graph runs on */
+    int32_t status;           /* out: SQMIX_OK or the error of the last call */
+} sqmix_ggml_fa_op;
+
+typedef struct sqmix_ggml_gdn_op {
+    int32_t n_snap;
+    float l2_eps;
+    int32_t flags;            /* SQMIX_GDN_* */
+    int32_t h_v_offset;
+    const float *dt_bias;     /* nullable */
+    const float *ssm_a;       /* nullable: g, beta are the log-decay and beta themselves */
+    sqmix_stream_t stream;
+    int32_t status;           /* out */
+} sqmix_ggml_gdn_op;
+
+int sqmix_ggml_fa_args(const struct ggml_tensor *dst, const sqmix_ggml_fa_op *op, sqmix_fa_args *out);
+int sqmix_ggml_gdn_args(const struct ggml_tensor *dst, const sqmix_ggml_gdn_op *op, sqmix_gdn_args *out);
+/* ggml_custom_op_t callbacks; userdata is the sqmix_ggml_*_op of the node. */
+void sqmix_ggml_fa_decode_op(struct ggml_tensor *dst, int ith, int nth, void *userdata);
+void sqmix_ggml_gdn_decode_op(struct ggml_tensor *dst, int ith, int nth, void *userdata);
+/* Byte size of the ggml tensor struct the bridge reads (336 on 64-bit hosts). */
+size_t sqmix_ggml_tensor_bytes(void);
 
 /* ========================================================================
  * Host-side state objects (the engine's bookkeeping, in C++)

@@ -129,6 +129,23 @@ const size_t kGdnLayer[] = {
     OFF(sqmix_gdn_layer_args, flags),
 };
 
+const size_t kGgmlFaOp[] = {
+    OFF(sqmix_ggml_fa_op, scale),           OFF(sqmix_ggml_fa_op, rope_n_rot),
+    OFF(sqmix_ggml_fa_op, rope_freq_base),  OFF(sqmix_ggml_fa_op, rope_pos_offset),
+    OFF(sqmix_ggml_fa_op, n_splits),        OFF(sqmix_ggml_fa_op, config),
+    OFF(sqmix_ggml_fa_op, flags),           OFF(sqmix_ggml_fa_op, q_norm),
+    OFF(sqmix_ggml_fa_op, k_norm),          OFF(sqmix_ggml_fa_op, norm_eps),
+    OFF(sqmix_ggml_fa_op, workspace),       OFF(sqmix_ggml_fa_op, workspace_bytes),
+    OFF(sqmix_ggml_fa_op, stream),          OFF(sqmix_ggml_fa_op, status),
+};
+
+const size_t kGgmlGdnOp[] = {
+    OFF(sqmix_ggml_gdn_op, n_snap),     OFF(sqmix_ggml_gdn_op, l2_eps),
+    OFF(sqmix_ggml_gdn_op, flags),      OFF(sqmix_ggml_gdn_op, h_v_offset),
+    OFF(sqmix_ggml_gdn_op, dt_bias),    OFF(sqmix_ggml_gdn_op, ssm_a),
+    OFF(sqmix_ggml_gdn_op, stream),     OFF(sqmix_ggml_gdn_op, status),
+};
+
 #undef OFF
 
 struct Entry {
@@ -152,6 +169,8 @@ bool lookup(int32_t which, Entry *e) {
         case SQMIX_ABI_GDN_CONV_ARGS: *e = entry(sizeof(sqmix_gdn_conv_args), kGdnConv); return true;
         case SQMIX_ABI_HEAD_NORM_ARGS: *e = entry(sizeof(sqmix_head_norm_args), kHeadNorm); return true;
         case SQMIX_ABI_GDN_LAYER_ARGS: *e = entry(sizeof(sqmix_gdn_layer_args), kGdnLayer); return true;
+        case SQMIX_ABI_GGML_FA_OP: *e = entry(sizeof(sqmix_ggml_fa_op), kGgmlFaOp); return true;
+        case SQMIX_ABI_GGML_GDN_OP: *e = entry(sizeof(sqmix_ggml_gdn_op), kGgmlGdnOp); return true;
         default: return false;
     }
 }

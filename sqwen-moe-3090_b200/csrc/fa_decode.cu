@@ -1216,8 +1216,9 @@ static int fa_decode_impl(const sqmix_fa_args *a, const PeerExchange *px, sqmix_
     //   5: configuration 3 with VC 2
     //   6: configuration 2 with VC 2
     int cfg = a->config;
-    // auto: configuration 3 for one query token (measured 4 % faster than 1 at 172K keys)
-    if (cfg == 0) cfg = a->n_q == 1 ? 3 : 2;
+    // auto: configuration 5 for one query token, 6 for two (172K keys x 10 layers on
+    // B200: 5 264.5, 3 276.9, 1 304.6, 4 291.9 us per token; 6 393.7, 2 430.9)
+    if (cfg == 0) cfg = a->n_q == 1 ? 5 : 6;
     SQMIX_CHECK_ARG(cfg >= 1 && cfg <= 6 && (cfg == 2 || cfg == 6) == (a->n_q == 2),
                     "fa_decode: config %d does not serve n_q=%d", a->config, a->n_q);
     const int per_sm = cfg == 4 ? 2 : 1;
@@ -1426,7 +1427,8 @@ extern "C" int sqmix_fa_decode_batch(const sqmix_fa_batch_args *b, sqmix_stream_
     bt.q_sseq = b->q_stride_seq;
     bt.new_sseq = b->new_stride_seq;
     bt.g_sseq = b->gate_stride_seq;
-    // configuration 3 (6 warps per KV head, 3 x 55.3 KB slots): measured 4.5 % faster
-    // than configuration 1 on the 64-sequence batch of the mixer stack
-    return launch_fa<1, 6, 1, 3, 1, 0>(&a, splits, reinterpret_cast<cudaStream_t>(stream), bt);
+    // configuration 5 (6 warps per KV head, 3 x 55.3 KB slots, one-MMA V correction);
+    // the 6-warp geometry measured 4.5 % faster than configuration 1 on the 64-sequence
+    // batch of the mixer stack
+    return launch_fa<1, 6, 1, 3, 1, 2>(&a, splits, reinterpret_cast<cudaStream_t>(stream), bt);
 }

@@ -745,10 +745,8 @@ extern "C" int sqmix_gdn_prefill(const sqmix_gdn_args *a, void *workspace, size_
                     "gdn_prefill: null pointer argument");
     SQMIX_CHECK_ARG(a->dtype == SQMIX_F32 || a->dtype == SQMIX_F16 || a->dtype == SQMIX_BF16,
                     "gdn_prefill: dtype %d", a->dtype);
-    SQMIX_CHECK_ARG(a->h_k >= 1 && a->h_v >= 1 && a->h_v_offset >= 0 &&
-                        (a->h_v_offset > 0 || a->h_v % a->h_k == 0),
-                    "gdn_prefill: h_v=%d must be a multiple of h_k=%d (h_v_offset=%d)", a->h_v, a->h_k,
-                    a->h_v_offset);
+    SQMIX_CHECK_ARG(a->h_k >= 1 && a->h_v >= 1 && a->h_v_offset >= 0, "gdn_prefill: h_k=%d h_v=%d h_v_offset=%d",
+                    a->h_k, a->h_v, a->h_v_offset);
     SQMIX_CHECK_ARG(a->n_seqs >= 1 && a->n_seqs <= 65535 && a->n_tokens >= 1, "gdn_prefill: n_seqs=%d T=%d",
                     a->n_seqs, a->n_tokens);
     SQMIX_CHECK_ARG(a->n_planes >= 1, "gdn_prefill: n_planes=%d", a->n_planes);

@@ -34,6 +34,8 @@ SQMIX_ABI_GDN_ARGS = 5
 SQMIX_ABI_GDN_CONV_ARGS = 6
 SQMIX_ABI_HEAD_NORM_ARGS = 7
 SQMIX_ABI_GDN_LAYER_ARGS = 8
+SQMIX_ABI_GGML_FA_OP = 9
+SQMIX_ABI_GGML_GDN_OP = 10
 
 ERROR_NAMES = {
     SQMIX_EINVAL: "SQMIX_EINVAL",
@@ -147,6 +149,35 @@ class GdnLayerArgs(ctypes.Structure):
     ]
 
 
+class GgmlFaOp(ctypes.Structure):
+    _fields_ = [
+        ("scale", c_float), ("rope_n_rot", c_int32), ("rope_freq_base", c_float), ("rope_pos_offset", c_int64),
+        ("n_splits", c_int32), ("config", c_int32), ("flags", c_int32), ("q_norm", c_void_p), ("k_norm", c_void_p),
+        ("norm_eps", c_float), ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("stream", c_void_p),
+        ("status", c_int32),
+    ]
+
+
+class GgmlGdnOp(ctypes.Structure):
+    _fields_ = [
+        ("n_snap", c_int32), ("l2_eps", c_float), ("flags", c_int32), ("h_v_offset", c_int32), ("dt_bias", c_void_p),
+        ("ssm_a", c_void_p), ("stream", c_void_p), ("status", c_int32),
+    ]
+
+
+class GgmlTensor(ctypes.Structure):
+    """ggml's struct ggml_tensor as sqwen's FFI declares it (src/backend/ffi.rs:22-39);
+    used to build graph nodes for the custom-op bridge."""
+
+
+GgmlTensor._fields_ = [
+    ("type", c_int32), ("buffer", c_void_p), ("ne", c_int64 * 4), ("nb", c_size_t * 4), ("op", c_int32),
+    ("op_params", c_int32 * 16), ("flags", c_int32), ("src", ctypes.POINTER(GgmlTensor) * 10),
+    ("view_src", ctypes.POINTER(GgmlTensor)), ("view_offs", c_size_t), ("data", c_void_p), ("name", ctypes.c_char * 64),
+    ("extra", c_void_p), ("padding", ctypes.c_char * 8),
+]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "sqmix_version": (ctypes.c_char_p, []),
@@ -184,6 +215,12 @@ _SIGNATURES = {
     "sqmix_gdn_conv": (ctypes.c_int, [ctypes.POINTER(GdnConvArgs), c_void_p]),
     "sqmix_head_norm": (ctypes.c_int, [ctypes.POINTER(HeadNormArgs), c_void_p]),
     "sqmix_gdn_layer_decode": (ctypes.c_int, [ctypes.POINTER(GdnLayerArgs), c_void_p]),
+    "sqmix_ggml_fa_args": (ctypes.c_int, [ctypes.POINTER(GgmlTensor), ctypes.POINTER(GgmlFaOp), ctypes.POINTER(FaArgs)]),
+    "sqmix_ggml_gdn_args": (ctypes.c_int, [ctypes.POINTER(GgmlTensor), ctypes.POINTER(GgmlGdnOp),
+                                           ctypes.POINTER(GdnArgs)]),
+    "sqmix_ggml_fa_decode_op": (None, [ctypes.POINTER(GgmlTensor), ctypes.c_int, ctypes.c_int, c_void_p]),
+    "sqmix_ggml_gdn_decode_op": (None, [ctypes.POINTER(GgmlTensor), ctypes.c_int, ctypes.c_int, c_void_p]),
+    "sqmix_ggml_tensor_bytes": (c_size_t, []),
     "sqmix_kvcache_create": (ctypes.c_int, [c_int32, c_int64, c_int32, ctypes.POINTER(c_void_p)]),
     "sqmix_kvcache_destroy": (None, [c_void_p]),
     "sqmix_kvcache_zero": (ctypes.c_int, [c_void_p, c_void_p]),

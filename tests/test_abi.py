@@ -211,6 +211,8 @@ def _abi_structs():
         "sqmix_gdn_conv_args": (L.SQMIX_ABI_GDN_CONV_ARGS, L.GdnConvArgs),
         "sqmix_head_norm_args": (L.SQMIX_ABI_HEAD_NORM_ARGS, L.HeadNormArgs),
         "sqmix_gdn_layer_args": (L.SQMIX_ABI_GDN_LAYER_ARGS, L.GdnLayerArgs),
+        "sqmix_ggml_fa_op": (L.SQMIX_ABI_GGML_FA_OP, L.GgmlFaOp),
+        "sqmix_ggml_gdn_op": (L.SQMIX_ABI_GGML_GDN_OP, L.GgmlGdnOp),
     }
 
 

