@@ -86,7 +86,7 @@ def test_gdn_decode_argument_validation_without_gpu(sqmix_lib):
     ok = dict(q=fake, k=fake, v=fake, dtype=sqmix_lib.SQMIX_F32, qk_stride_tok=16 * 128, v_stride_tok=32 * 128,
               qk_stride_seq=16 * 128, v_stride_seq=32 * 128, g=fake, beta=fake, state=fake, n_planes=1, sel=None,
               n_seqs=1, n_tokens=1, h_k=16, h_v=32, n_snap=1, l2_eps=0.0, out=fake, flags=0)
-    for bad in (dict(flags=2), dict(flags=-1), dict(n_snap=2), dict(h_v=30)):
+    for bad in (dict(flags=2), dict(flags=-1), dict(n_snap=2), dict(h_v=0), dict(h_v_offset=-1)):
         a = GdnArgs(**{**ok, **bad})
         assert L.sqmix_gdn_decode(ctypes.byref(a), None) == sqmix_lib.SQMIX_EINVAL, bad
 
