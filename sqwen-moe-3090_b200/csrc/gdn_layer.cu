@@ -15,8 +15,10 @@
 // read it: hk, hk + H_k, ...), CTA rank m * 4 + u handling value head hk + m * H_k,
 // value columns 32u .. 32u + 31.  With qwen35moe's 16 q/k and 32 value heads that is
 // 16 clusters of 8 = 128 CTAs per sequence.  A CTA (256 threads):
-//   1. before the grid-dependency wait: its conv taps and, under
-//      SQMIX_GDN_STATE_READY, its 32 state columns (4 per warp, 16 bytes per lane);
+//   1. before the grid-dependency wait: its conv taps, the norm weight and, under
+//      SQMIX_GDN_STATE_READY, its 32 state columns (4 per warp, 16 bytes per lane) and
+//      the conv history of the selected plane; after it, x, the raw gates and z in one
+//      batch of loads;
 //   2. conv + SiLU of the head's 128 q and 128 k channels (thread = channel) and of its
 //      32 v channels; q and k L2-normalised per token (warp sums, then shared memory);
 //   3. arrives on the cluster barrier once its reads of the conv-history plane are done
@@ -73,7 +75,7 @@ __device__ __forceinline__ void st_cluster_f32(uint32_t addr_cl, float v) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr_cl), "f"(v) : "memory");
 }
 
-__global__ void __launch_bounds__(256) gdn_layer_kernel(GdnLayerParams p) {
+__global__ void __launch_bounds__(256, 1) gdn_layer_kernel(GdnLayerParams p) {
     constexpr int K = kLayerK;
     __shared__ float qs[2][128], ks[2][128], vs[2][32], os[2][32];
     __shared__ float red[8][2];
@@ -99,37 +101,55 @@ __global__ void __launch_bounds__(256) gdn_layer_kernel(GdnLayerParams p) {
     float *st_seq = p.state + static_cast<int64_t>(seq) * p.n_planes * plane_elems;
     const int j0 = col0 + 4 * warp;  // this warp's first value column
     const int64_t col_off = (static_cast<int64_t>(hv) * 128 + j0) * 128 + 4 * lane;
+    const size_t cplane = static_cast<size_t>(C) * (K - 1);
+    float *cst = p.conv_state + static_cast<size_t>(seq) * p.n_planes * cplane;
+    // conv_input rows 0..K-2 (history) and K-1.. (the T new rows), q|k channel and v channel
+    float in[K - 1 + 2], inv[K - 1 + 2] = {};
     float4 S[4];
-    auto load_state = [&]() {
+    // The state columns and the conv history of the selected plane: under
+    // SQMIX_GDN_STATE_READY the previous kernel writes neither, so they are read before
+    // the dependency wait; the rest (x, the gates, z: the projections' outputs) after it,
+    // all issued together.
+    auto load_planes = [&]() {
         int plane = p.sel ? p.sel[seq] : 0;
         plane = min(max(plane, 0), p.n_planes - 1);
 #pragma unroll
         for (int c = 0; c < 4; ++c)
             S[c] = *reinterpret_cast<const float4 *>(st_seq + plane * plane_elems + col_off + c * 128);
+#pragma unroll
+        for (int r = 0; r < K - 1; ++r) in[r] = cst[plane * cplane + static_cast<size_t>(ch) * (K - 1) + r];
+        if (warp == 0) {
+#pragma unroll
+            for (int r = 0; r < K - 1; ++r) inv[r] = cst[plane * cplane + static_cast<size_t>(chv) * (K - 1) + r];
+        }
     };
-    if (p.state_ready) load_state();
+    const float nw = warp == 0 && p.norm_w ? p.norm_w[static_cast<int64_t>(hv) * p.norm_w_sh + col0 + lane] : 1.0f;
+    if (p.state_ready) load_planes();
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" :::);
-    if (!p.state_ready) load_state();
+    if (!p.state_ready) load_planes();
 
     // ---- 2. conv + SiLU (+ L2 norm of q, k) ----------------------------------------
-    const size_t cplane = static_cast<size_t>(C) * (K - 1);
-    float *cst = p.conv_state + static_cast<size_t>(seq) * p.n_planes * cplane;
-    int csel = p.sel ? p.sel[seq] : 0;
-    csel = min(max(csel, 0), p.n_planes - 1);
-    // conv_input rows 0..K-2 (history) and K-1.. (the T new rows), q|k channel and v channel
-    float in[K - 1 + 2], inv[K - 1 + 2] = {};
-#pragma unroll
-    for (int r = 0; r < K - 1; ++r) in[r] = cst[csel * cplane + static_cast<size_t>(ch) * (K - 1) + r];
-    if (warp == 0) {
-#pragma unroll
-        for (int r = 0; r < K - 1; ++r) inv[r] = cst[csel * cplane + static_cast<size_t>(chv) * (K - 1) + r];
-    }
     const int64_t xb = static_cast<int64_t>(seq) * p.x_ss;
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
         in[K - 1 + t] = t < p.T ? load_act(p.x, xb + t * p.x_st + ch, p.x_dtype) : 0.f;
         if (warp == 0) inv[K - 1 + t] = t < p.T ? load_act(p.x, xb + t * p.x_st + chv, p.x_dtype) : 0.f;
+    }
+    float graw = 0.f, braw = 0.f;  // the raw gates of token tid / 2 (threads 0 .. 2T-1)
+    if (tid < 2 * p.T) {
+        const int64_t gi = (static_cast<int64_t>(seq) * p.T + (tid >> 1)) * p.h_v + hv;
+        graw = p.alpha[gi];
+        braw = p.bproj[gi];
+    }
+    float zv[2] = {0.f, 0.f};
+    if (warp == 0 && p.z) {
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+            if (t < p.T)
+                zv[t] = load_act(p.z, static_cast<int64_t>(seq) * p.z_ss + t * p.z_st + static_cast<int64_t>(hv) * 128 +
+                                          col0 + lane,
+                                 p.z_dtype);
     }
     // every CTA of the cluster has read its history plane: the writers may go ahead
     // once all have arrived (they wait at the end)
@@ -153,8 +173,7 @@ __global__ void __launch_bounds__(256) gdn_layer_kernel(GdnLayerParams p) {
     }
     if (tid < 2 * p.T) {  // gate epilogue, one token per thread pair: g (even), beta (odd)
         const int t = tid >> 1;
-        const int64_t gi = (static_cast<int64_t>(seq) * p.T + t) * p.h_v + hv;
-        float g = p.alpha[gi], b = p.bproj[gi];
+        float g = graw, b = braw;
         gdn_gates(g, b, p.dt_bias, p.ssm_a, hv);
         if (tid & 1)
             gate_b[t] = b;
@@ -248,17 +267,13 @@ __global__ void __launch_bounds__(256) gdn_layer_kernel(GdnLayerParams p) {
     cluster_wait();
     if (warp == 0) {
         const int col = col0 + lane;
-        const float w = p.norm_w ? p.norm_w[static_cast<int64_t>(hv) * p.norm_w_sh + col] : 1.0f;
-        for (int t = 0; t < p.T; ++t) {
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            if (t >= p.T) break;
             const float tot = nsum[0][t] + nsum[1][t] + nsum[2][t] + nsum[3][t];
             float yv = ov[t] * (1.0f / sqrtf(tot / 128.0f + p.norm_eps));
-            yv = yv * w;
-            if (p.z) {
-                const float zv =
-                    load_act(p.z, static_cast<int64_t>(seq) * p.z_ss + t * p.z_st + static_cast<int64_t>(hv) * 128 + col,
-                             p.z_dtype);
-                yv = yv * silu_f(zv);
-            }
+            yv = yv * nw;
+            if (p.z) yv = yv * silu_f(zv[t]);
             p.out[((static_cast<int64_t>(seq) * p.T + t) * p.h_v + hv) * 128 + col] = yv;
         }
     }
