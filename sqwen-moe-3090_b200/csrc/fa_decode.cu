@@ -131,78 +131,73 @@ __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepco
 __device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // Log-sum-exp merge of the split partials for one 32-dim slice of one output row, by
-// a CTA of 256 threads (thread = dim lane x split group of 8).  The per-split weights
-// w_s = 2^((m_s - M) c) are computed once per split (not once per dim) into shared
-// memory; every partial load is issued before the first reduction, so a merge of up
-// to 8 * kPre splits costs one round trip to L2.  Reads bypass L1: the partials were
-// written by other CTAs.  gate_factor: sigmoid(gate) of this thread's output element
-// (1 without a gate), computed by the caller ahead of time.
-constexpr int kMergeMaxSplits = 4096;
+// a CTA of 256 threads: thread = dim lane x split group (8 groups, group g takes splits
+// g, g + 8, ...).  Each thread issues the loads of its group's splits at once (up to
+// kMergePre per pass: partial O of its dim and the split's (m, l), the latter the same
+// address for the whole warp) and folds them with a running maximum in registers; one
+// barrier then combines the 8 groups.  A merge of up to 8 * kMergePre splits is one
+// round trip to L2 and one barrier.  Reads bypass L1: the partials were written by
+// other CTAs.
+constexpr int kMergePre = 24;
 struct MergeSmem {
-    float w[kMergeMaxSplits];  // m_s, then the weight of split s
-    float l[kMergeMaxSplits];
     float red[8][33];
-    float wm[8];
+    float gm[8];  // per group: running maximum (score units) and sum of l weights
+    float gl[8];
 };
 
 // The merged values, valid in the first warp (lane = dim within the slice): y = the
 // normalised output of dim slice * 32 + lane, lse_row = the row's natural-log LSE.
 __device__ void merge_slice_values(const float *part_o, const float *part_ml, int n_splits, int n_rows, int row,
                                    int slice, float c, float scale, MergeSmem &sm, float &y_out, float &lse_row) {
-    constexpr int kPre = 24;  // o loads per thread issued up front (8 * 24 = 192 splits)
     const int tid = threadIdx.x, lane = tid & 31, grp = tid >> 5;
     const int d = slice * 32 + lane;
     const size_t sstride = static_cast<size_t>(n_rows) * 256;
     const float *po = part_o + static_cast<size_t>(row) * 256 + d;
-    const float *pml = part_ml + static_cast<size_t>(row) * 2;
-    float ov[kPre];
+    const float2 *pml = reinterpret_cast<const float2 *>(part_ml) + row;  // split s at pml[s * n_rows]
+    float m_g = -INFINITY, l_g = 0.f, acc = 0.f;
+    for (int s0 = grp; s0 < n_splits; s0 += 8 * kMergePre) {
+        float ov[kMergePre];
+        float2 ml[kMergePre];
 #pragma unroll
-    for (int j = 0; j < kPre; ++j) {
-        const int s = grp + 8 * j;
-        ov[j] = s < n_splits ? __ldcg(po + s * sstride) : 0.f;
+        for (int j = 0; j < kMergePre; ++j) {
+            const int s = s0 + 8 * j;
+            ov[j] = s < n_splits ? __ldcg(po + s * sstride) : 0.f;
+            ml[j] = s < n_splits ? __ldcg(pml + static_cast<size_t>(s) * n_rows) : make_float2(-INFINITY, 0.f);
+        }
+        float mx = m_g;
+#pragma unroll
+        for (int j = 0; j < kMergePre; ++j) mx = fmaxf(mx, ml[j].x);
+        if (mx > -INFINITY) {
+            const float a = ex2((m_g - mx) * c);  // 0 while nothing was folded (m_g = -inf)
+            acc *= a;
+            l_g *= a;
+#pragma unroll
+            for (int j = 0; j < kMergePre; ++j) {
+                const float w = ex2((ml[j].x - mx) * c);  // empty splits (m = -inf) weigh 0
+                acc = fmaf(ov[j], w, acc);
+                l_g = fmaf(ml[j].y, w, l_g);
+            }
+            m_g = mx;
+        }
     }
-    // running maxima: thread t holds splits t, t + 256, ...
-    float m_loc = -INFINITY;
-    for (int s = tid; s < n_splits; s += 256) {
-        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pml + static_cast<size_t>(s) * n_rows * 2));
-        sm.w[s] = ml.x;  // the weight replaces it below
-        sm.l[s] = ml.y;
-        m_loc = fmaxf(m_loc, ml.x);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) m_loc = fmaxf(m_loc, __shfl_xor_sync(0xffffffffu, m_loc, off));
-    if (lane == 0) sm.wm[grp] = m_loc;
-    __syncthreads();
-    float M = sm.wm[0];
-#pragma unroll
-    for (int i = 1; i < 8; ++i) M = fmaxf(M, sm.wm[i]);
-    // weights and the sum of l_s w_s
-    float l_loc = 0.f;
-    for (int s = tid; s < n_splits; s += 256) {
-        const float m = sm.w[s];
-        const float w = (m == -INFINITY) ? 0.f : ex2((m - M) * c);
-        sm.w[s] = w;
-        l_loc = fmaf(sm.l[s], w, l_loc);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) l_loc += __shfl_xor_sync(0xffffffffu, l_loc, off);
-    __syncthreads();  // weights visible; wm reused below
-    if (lane == 0) sm.wm[grp] = l_loc;
-    float acc = 0.f;
-#pragma unroll
-    for (int j = 0; j < kPre; ++j) {
-        const int s = grp + 8 * j;
-        if (s < n_splits) acc = fmaf(ov[j], sm.w[s], acc);
-    }
-    for (int s = grp + 8 * kPre; s < n_splits; s += 8) acc = fmaf(__ldcg(po + s * sstride), sm.w[s], acc);
     sm.red[grp][lane] = acc;
+    if (lane == 0) {
+        sm.gm[grp] = m_g;
+        sm.gl[grp] = l_g;
+    }
     __syncthreads();
     if (grp == 0) {
-        float L = 0.f, y = 0.f;
+        float M = sm.gm[0];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            L += sm.wm[i];
-            y += sm.red[i][lane];
+        for (int i = 1; i < 8; ++i) M = fmaxf(M, sm.gm[i]);
+        float L = 0.f, y = 0.f;
+        if (M > -INFINITY) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float w = ex2((sm.gm[i] - M) * c);
+                L = fmaf(sm.gl[i], w, L);
+                y = fmaf(sm.red[i][lane], w, y);
+            }
         }
         y_out = L > 0.f ? y / L : 0.f;
         lse_row = L > 0.f ? M * scale + logf(L) : -INFINITY;
@@ -306,7 +301,11 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
         bulk_g2s(dst, kcache + gr0 * kGroupBytes, bytes, &full_bar[s]);
         bulk_g2s(dst + L::kTileBytes, vcache + gr0 * kGroupBytes, bytes, &full_bar[s]);
     };
-    constexpr int kStagingBytes = (NQ * 16 * 256 + NQ * 2 * 512) * 4;
+    // Q rows are staged with a stride of kQRow = 257 floats: the fragment build below
+    // reads dims {d0, d0 + 2, d0 + 16, d0 + 18} of 8 rows at once per warp, which a stride
+    // of 256 maps onto 4 banks (8-way conflicts; 2-way with 257).
+    constexpr int kQRow = 257;
+    constexpr int kStagingBytes = (NQ * 16 * kQRow + NQ * 2 * 512) * 4;
     constexpr int kStagingSlots = (kStagingBytes + L::kStageBytes - 1) / L::kStageBytes;
     static_assert(kStagingSlots < NSTAGE, "staging must leave ring slots for the first tiles");
     // Slots filled before the dependency wait: the ring minus the staging slots, at most
@@ -382,10 +381,13 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     const int c = lane & 3;
 
     float *q_stage = reinterpret_cast<float *>(ring + (NSTAGE - kStagingSlots) * L::kStageBytes);
-    float *kv_stage = q_stage + NQ * 16 * 256;
+    float *kv_stage = q_stage + NQ * 16 * kQRow;
 #pragma unroll
     for (int k = 0; k < kQPer; ++k)
-        if (threadIdx.x + k * L::kThreads < kQElems) q_stage[threadIdx.x + k * L::kThreads] = qv[k];
+        if (threadIdx.x + k * L::kThreads < kQElems) {
+            const int e = threadIdx.x + k * L::kThreads;
+            q_stage[(e >> 8) * kQRow + (e & 255)] = qv[k];
+        }
     if (has_fresh) {
 #pragma unroll
         for (int k = 0; k < kKvPer; ++k)
@@ -404,7 +406,7 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
             float *x;
             const float *w;
             if (row < n_qrows) {
-                x = q_stage + row * 256;
+                x = q_stage + row * kQRow;
                 w = p.q_norm;
             } else {
                 const int kr = row - n_qrows;  // token kr / 2, head kr % 2 of the K rows
@@ -468,7 +470,7 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
         const int qi = (item >> 9) % NQ;
         const int kh = (item >> 9) / NQ;
         const int gg = ln >> 2, cc = ln & 3;
-        const int qrow = (qi * 16 + kh * 8 + gg) * 256;
+        const int qrow = (qi * 16 + kh * 8 + gg) * kQRow;
         const int d0 = 32 * b + 4 * cc + s;
         const int dims[4] = {d0, d0 + 2, d0 + 16, d0 + 18};
         float v[4];
@@ -531,6 +533,7 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     }
     const uint2 *qf_w = qf_s + (kvh * NQ) * 8 * 2 * 32 + lane;
     const float2 *kinit_w = reinterpret_cast<const float2 *>(kinit_s) + (kvh * NQ) * 8 * 4 + c;
+
     const float craw = p.c * kTwo24;  // scores below are in units of 2^-24
     // P = 2^((x - m) craw) stays <= 2^kLazyLog2 = 8 between moves of the running maximum,
     // so P * (V scale) stays finite in f16 for every V scale of an f16-range block
