@@ -37,8 +37,8 @@ sys.path.insert(0, os.path.join(REPO, "sqwen-moe-3090_b200"))
 N_LAYERS = 10
 N_KV = 172032
 # DRAM bytes of one decode launch at N_KV keys, from one ncu capture
-# (profiles/fa_decode_kernel_172k.txt): 99.17 MB read + 3.65 MB written.
-FA_NCU_TRAFFIC = 102_818_048
+# (profiles/fa_decode_kernel_172k.txt): 99.17 MB read + 4.18 MB written.
+FA_NCU_TRAFFIC = 103_347_712
 HEAD_DIM = 256
 N_HEAD = 16
 N_HEAD_KV = 2
@@ -1276,6 +1276,19 @@ def run_profile_case(case: str):
         b = torch.rand((n, 1, 32), generator=g, device=dev)
         for _ in range(3):
             sqmix.gated_delta_net(q, k, v, gg, b, S)
+    elif case == "gdnl":  # the one-launch GDN decode layer, batch 1 (4.6 MB per launch)
+        C = 8192
+        x = torch.randn((1, 1, C), generator=g, device=dev).to(torch.bfloat16)
+        w = torch.randn((C, 4), generator=g, device=dev) * 0.5
+        cst = torch.randn((1, 1, C, 3), generator=g, device=dev)
+        S = torch.randn((1, 1, 32, 128, 128), generator=g, device=dev) * 0.02
+        alpha = torch.randn((1, 1, 32), generator=g, device=dev)
+        braw = torch.randn((1, 1, 32), generator=g, device=dev)
+        ssm_a = -torch.exp(torch.rand((32,), generator=g, device=dev) * 2.7)
+        z = torch.randn((1, 1, 32, 128), generator=g, device=dev).to(torch.bfloat16)
+        wn = torch.rand((128,), generator=g, device=dev) + 0.5
+        for _ in range(3):
+            sqmix.gdn_layer_decode(x, w, cst, alpha, braw, ssm_a, S, l2_eps=1e-6, z=z, norm_weight=wn)
     else:
         raise SystemExit(f"unknown profile case {case}")
     torch.cuda.synchronize()
@@ -1293,7 +1306,7 @@ def main():
     ap.add_argument("--headline-only", action="store_true",
                     help="config 3 only (skip configs 0, 1, 2 and 4)")
     ap.add_argument("--nccl-merge", action="store_true", help="N > 1: all-gather + merge instead of the peer merge")
-    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn | gdnb | gdnp) and exit")
+    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn | gdnb | gdnp | gdnl) and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)

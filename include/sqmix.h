@@ -343,6 +343,10 @@ int sqmix_fa_decode_peers(const sqmix_fa_args *a, const sqmix_peer_merge_args *p
 #define SQMIX_FA_NOALLOC_MAX_SPLITS 160
 #define SQMIX_FA_NOALLOC_SCRATCH_BYTES 5284096
 int sqmix_fa_decode_noalloc(const sqmix_fa_args *args, sqmix_stream_t stream);
+/* Reads and clears the status word of the current device's static scratch, as
+ * sqmix_fa_status does for a workspace (SQMIX_OK, SQMIX_ETIMEOUT, SQMIX_ERANGE when n_kv
+ * exceeded the capacity and was clamped).  Synchronises the stream. */
+int sqmix_fa_noalloc_status(sqmix_stream_t stream);
 
 /* Merge n_parts normalised partial attentions (O_p, lse_p) over disjoint key sets
  * (split-KV across GPUs): out = sum_p O_p exp(lse_p - L) with L = log sum exp(lse_p),

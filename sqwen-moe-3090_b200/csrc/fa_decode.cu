@@ -1348,6 +1348,28 @@ extern "C" int sqmix_fa_decode_noalloc(const sqmix_fa_args *a, sqmix_stream_t st
     return sqmix_fa_decode(&b, stream);
 }
 
+// Status of the static scratch (device-side wait timeouts, n_kv beyond the capacity):
+// the status word sits in the array's header, whose address is private to this file.
+extern "C" int sqmix_fa_noalloc_status(sqmix_stream_t stream) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e, "fa_noalloc_status: current device");
+    SQMIX_CHECK_ARG(dev >= 0 && dev < kNoAllocMaxDevices, "fa_noalloc_status: device %d", dev);
+    void *scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_scratch[dev]) {
+            e = cudaGetSymbolAddress(&g_noalloc_scratch[dev], g_fa_noalloc_scratch);
+            if (e != cudaSuccess) {
+                g_noalloc_scratch[dev] = nullptr;
+                return cuda_status(e, "fa_noalloc_status: scratch symbol address");
+            }
+        }
+        scratch = g_noalloc_scratch[dev];
+    }
+    return sqmix_fa_status(scratch, stream);
+}
+
 // ---------------------------------------------------------------------------
 // Sequence-batched decode: one launch pair for n_seqs independent sequences, each
 // with its own tiled caches and device scalars (the batched decode of config 4).

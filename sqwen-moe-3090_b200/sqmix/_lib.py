@@ -194,6 +194,7 @@ _SIGNATURES = {
     "sqmix_fa_decode": (ctypes.c_int, [ctypes.POINTER(FaArgs), c_void_p]),
     "sqmix_fa_status": (ctypes.c_int, [c_void_p, c_void_p]),
     "sqmix_fa_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(FaArgs), c_void_p]),
+    "sqmix_fa_noalloc_status": (ctypes.c_int, [c_void_p]),
     "sqmix_fa_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32]),
     "sqmix_fa_prefill": (ctypes.c_int, [ctypes.POINTER(FaArgs), c_void_p]),
     "sqmix_gdn_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),

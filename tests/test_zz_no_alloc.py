@@ -70,3 +70,4 @@ def test_noalloc_matches_workspace_entry_point(n_q, n_splits):
         ref = want.cpu().numpy().astype(np.float64)
         assert np.isfinite(got).all()
         assert np.abs(got - ref).max() <= ATTN_TOL * np.abs(ref).max()
+    assert sq.lib().sqmix_fa_noalloc_status(stream) == sq.SQMIX_OK
