@@ -17,7 +17,7 @@
 // the scaled Q, K and the masked Q K^T) for all chunks and heads in parallel and
 // stores the matrices the scan multiplies with as split-bf16 tcgen05 operand images;
 // gdn_chunk_scan_kernel then walks the chunks of each head in order, one CTA per
-// (sequence, head, 64 value columns; value columns evolve independently), with the
+// (sequence, head, 32 value columns; value columns evolve independently), with the
 // three chunk products on the tensor cores (tcgen05, f32 accumulators in TMEM).
 // Every exponent is a difference G_t - G_s <= 0 or G_t <= 0, so nothing overflows.
 //
@@ -483,7 +483,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     }
 }
 
-// ---- phase 2: walk the chunks of one (sequence, head, 64 value columns) -------------
+// ---- phase 2: walk the chunks of one (sequence, head, 32 value columns) -------------
 // grid (kD / kSN, h_v, n_seqs), 128 threads (thread = TMEM lane = accumulator row,
 // all kSN columns of it); dynamic smem kScanSmem.  Per chunk, three split-bf16 tcgen05 MMA groups (hi*hi + hi*lo + lo*hi,
 // f32 accumulators in tensor memory):
