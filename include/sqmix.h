@@ -51,6 +51,9 @@ typedef struct CUstream_st *sqmix_stream_t;
 /* ---- element types (ggml type ids, src/backend/ffi.rs:44-101) ----------- */
 #define SQMIX_F32 0
 #define SQMIX_F16 1
+#define SQMIX_Q8_0 8   /* weight block formats of sqmix_mul_mat */
+#define SQMIX_Q4_K 12
+#define SQMIX_Q6_K 14
 #define SQMIX_BF16 30
 
 /* ---- fixed geometry ----------------------------------------------------- */
@@ -84,6 +87,7 @@ int sqmix_device_sm_count(int device);
 #define SQMIX_ABI_GDN_LAYER_ARGS 8
 #define SQMIX_ABI_GGML_FA_OP 9
 #define SQMIX_ABI_GGML_GDN_OP 10
+#define SQMIX_ABI_MUL_MAT_ARGS 11
 size_t sqmix_abi_struct_size(int32_t which);
 int32_t sqmix_abi_field_count(int32_t which);
 int64_t sqmix_abi_field_offset(int32_t which, int32_t field);
@@ -546,6 +550,41 @@ typedef struct sqmix_head_norm_args {
 } sqmix_head_norm_args;
 
 int sqmix_head_norm(const sqmix_head_norm_args *args, sqmix_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Mixer projections: ggml_mul_mat(w, x) (QG / K / V attn.rs:127-129, W_o attn.rs:285;
+ * qkv / z / beta / alpha gdn.rs:264-276, out gdn.rs:577):
+ *   y[t * y_stride + o] = sum_i W[o][i] * x[t * x_stride + i]
+ * for o < n_out, i < n_in, t < n_tokens.  W is ggml's [n_in, n_out] weight tensor: n_out
+ * contiguous rows (w_row_bytes = sqmix_mul_mat_row_bytes(w_type, n_in)) in a GGUF block
+ * format -- SQMIX_Q8_0, SQMIX_Q4_K, SQMIX_Q6_K -- or SQMIX_F32 / F16 / BF16 elements;
+ * 16-byte aligned, n_in a multiple of 256 up to 4096 (q6_K: a multiple of 2048).  x is
+ * f32 / f16 / bf16, y f32.  Dequantised weights times x are summed in f32 (ggml's CUDA
+ * backend quantises x to q8_1 for its quantised dot products; this is the more exact
+ * form).  Built for decode: each stream of W serves up to 4 tokens, so larger n_tokens
+ * read W once per 4 tokens.  The weights are read before the call's dependency on the
+ * previous kernel on the stream (programmatic dependent launch): W must not be written
+ * by that kernel.  `status` (device, may be NULL) receives bit 1 if a bounded wait of
+ * the kernel gave up.
+ * ------------------------------------------------------------------------ */
+typedef struct sqmix_mul_mat_args {
+    const void *w;
+    int32_t w_type;
+    int64_t w_row_bytes;
+    int64_t n_in;
+    int64_t n_out;
+    const void *x;
+    int32_t x_dtype;
+    int64_t x_stride;  /* elements between tokens of x */
+    int32_t n_tokens;
+    float *y;
+    int64_t y_stride;  /* elements between tokens of y */
+    uint32_t *status;
+} sqmix_mul_mat_args;
+
+/* Bytes of one weight row of n_in values in w_type (0: unsupported type or length). */
+int64_t sqmix_mul_mat_row_bytes(int32_t w_type, int64_t n_in);
+int sqmix_mul_mat(const sqmix_mul_mat_args *args, sqmix_stream_t stream);
 
 /* ========================================================================
  * ggml custom-op bridge

@@ -63,6 +63,12 @@ def lib():
         L.cpu_gdn_f32.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, i64, i64, i64, i64, f32p]
         L.oracle_set_threads.argtypes = [ctypes.c_int]
         L.oracle_set_threads.restype = ctypes.c_int
+        L.oracle_row_bytes.argtypes = [ctypes.c_int, i64]
+        L.oracle_row_bytes.restype = i64
+        L.oracle_dequant_row.argtypes = [u8p, ctypes.c_int, i64, f32p]
+        L.oracle_dequant_row.restype = ctypes.c_int
+        L.oracle_mul_mat.argtypes = [u8p, ctypes.c_int, i64, i64, i64, f32p, i64, ctypes.c_int, f32p, i64]
+        L.oracle_mul_mat.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -303,3 +309,41 @@ def gdn_gates(alpha, b, dt_bias, ssm_a):
     g = sp * np.asarray(ssm_a, dtype=np.float64)
     beta = 1.0 / (1.0 + np.exp(-np.asarray(b, dtype=np.float64)))
     return g.astype(np.float32), beta.astype(np.float32)
+
+
+# ggml type ids of the projection weights (src/backend/ffi.rs:44-101)
+GGML_F32, GGML_F16, GGML_Q8_0, GGML_Q4_K, GGML_Q6_K, GGML_BF16 = 0, 1, 8, 12, 14, 30
+
+
+def row_bytes(wtype: int, n: int) -> int:
+    """Bytes of one weight row of n values in ggml format wtype (0: unsupported)."""
+    return int(lib().oracle_row_bytes(int(wtype), int(n)))
+
+
+def dequant_rows(w: np.ndarray, wtype: int, n: int) -> np.ndarray:
+    """Rows of ggml-format bytes [rows][row_bytes] -> f32 [rows][n]."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    rb = row_bytes(wtype, n)
+    assert rb > 0 and w.shape[-1] == rb, (wtype, n, w.shape)
+    rows = w.size // rb
+    out = np.zeros((rows, n), dtype=np.float32)
+    u8p, f32p = ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(ctypes.c_float)
+    for r in range(rows):
+        rc = lib().oracle_dequant_row(w[r].ctypes.data_as(u8p), int(wtype), n, out[r].ctypes.data_as(f32p))
+        assert rc == 0
+    return out
+
+
+def mul_mat(w: np.ndarray, wtype: int, n_in: int, x: np.ndarray) -> np.ndarray:
+    """ggml_mul_mat(w, x): w [n_out][row_bytes] in format wtype, x [T][n_in] -> y [T][n_out]."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    rb = row_bytes(wtype, n_in)
+    assert rb > 0 and w.shape[-1] == rb
+    n_out = w.size // rb
+    xs, xp = _f32(np.asarray(x, dtype=np.float32).reshape(-1, n_in))
+    T = xs.shape[0]
+    y = np.zeros((T, n_out), dtype=np.float32)
+    rc = lib().oracle_mul_mat(w.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), int(wtype), rb, n_in, n_out, xp,
+                              n_in, T, y.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n_out)
+    assert rc == 0
+    return y

@@ -456,3 +456,119 @@ int oracle_set_threads(int n) {
     return 1;
 #endif
 }
+
+/* ---------------------------------------------------------- projections ---- */
+/* ggml_mul_mat(w, x) as sqwen builds the mixer projections (attn.rs:127-129 QG / K / V,
+ * attn.rs:285 W_o; gdn.rs:264-276 qkv / z / beta / alpha, gdn.rs:577 out): w is
+ * [n_in, n_out] (n_out rows of n_in elements in a ggml block format), x [n_in, T],
+ * y[t][o] = sum_i W[o][i] x[t][i].  The weight formats (ggml type ids of
+ * src/backend/ffi.rs:44-101), restated from their published block layouts and pinned
+ * bit-exactly against gguf-py 0.19.0's dequantizers (gguf/quants.py Q8_0, Q4_K, Q6_K):
+ *   Q8_0 (8):  34 bytes per 32 values: f16 d, 32 x int8 q;          w = d q
+ *   Q4_K (12): 144 bytes per 256: f16 d, f16 dmin, 12 bytes of 6-bit sub-block scales
+ *              and mins (8 sub-blocks of 32), 128 bytes of nibbles (bytes 32k..32k+31:
+ *              sub-block 2k in the low nibbles, 2k+1 in the high); w = d sc q - dmin m
+ *   Q6_K (14): 210 bytes per 256: ql[128] (low 4 bits), qh[64] (high 2 bits), int8
+ *              scales[16] (one per 16 values), f16 d;               w = d sc (q - 32)
+ *   F32 (0), F16 (1), BF16 (30): plain elements. */
+#define ORACLE_QK_K 256
+
+static void q4k_scale_min(int j, const uint8_t *s, int *sc, int *m) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *m = s[j + 4] & 63;
+    } else {
+        *sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+        *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+/* bytes of one row of n values, or 0 for an unsupported type / length */
+int64_t oracle_row_bytes(int type, int64_t n) {
+    switch (type) {
+        case 0: return 4 * n;
+        case 1: case 30: return 2 * n;
+        case 8: return n % 32 ? 0 : n / 32 * 34;
+        case 12: return n % ORACLE_QK_K ? 0 : n / ORACLE_QK_K * 144;
+        case 14: return n % ORACLE_QK_K ? 0 : n / ORACLE_QK_K * 210;
+        default: return 0;
+    }
+}
+
+/* one row of n values -> f32; returns 0, or -1 for an unsupported type */
+int oracle_dequant_row(const uint8_t *row, int type, int64_t n, float *out) {
+    if (oracle_row_bytes(type, n) == 0) return -1;
+    if (type == 0) {
+        memcpy(out, row, (size_t)n * 4);
+    } else if (type == 1) {
+        for (int64_t i = 0; i < n; i++) out[i] = oracle_f16_to_f32((uint16_t)(row[2 * i] | (row[2 * i + 1] << 8)));
+    } else if (type == 30) {
+        for (int64_t i = 0; i < n; i++) {
+            const uint32_t u = (uint32_t)(row[2 * i] | (row[2 * i + 1] << 8)) << 16;
+            memcpy(&out[i], &u, 4);
+        }
+    } else if (type == 8) {
+        for (int64_t b = 0; b < n / 32; b++) {
+            const uint8_t *blk = row + 34 * b;
+            const float d = oracle_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+            for (int i = 0; i < 32; i++) out[32 * b + i] = d * (float)(int8_t)blk[2 + i];
+        }
+    } else if (type == 12) {
+        for (int64_t b = 0; b < n / ORACLE_QK_K; b++) {
+            const uint8_t *blk = row + 144 * b;
+            const float d = oracle_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+            const float dmin = oracle_f16_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+            const uint8_t *qs = blk + 16;
+            for (int j = 0; j < 8; j++) {
+                int sc, m;
+                q4k_scale_min(j, blk + 4, &sc, &m);
+                const float ds = d * (float)sc, dm = dmin * (float)m;
+                for (int l = 0; l < 32; l++) {
+                    const int q = (qs[32 * (j >> 1) + l] >> (4 * (j & 1))) & 0xF;
+                    out[ORACLE_QK_K * b + 32 * j + l] = ds * (float)q - dm;
+                }
+            }
+        }
+    } else {  /* 14: Q6_K */
+        for (int64_t b = 0; b < n / ORACLE_QK_K; b++) {
+            const uint8_t *blk = row + 210 * b;
+            const uint8_t *ql = blk, *qh = blk + 128;
+            const int8_t *sc = (const int8_t *)(blk + 192);
+            const float d = oracle_f16_to_f32((uint16_t)(blk[208] | (blk[209] << 8)));
+            for (int e = 0; e < ORACLE_QK_K; e++) {
+                const int half = e / 128, r = e % 128, k = r / 32, l = r % 32;
+                const int lo = (ql[64 * half + 32 * (k & 1) + l] >> (4 * (k >> 1))) & 0xF;
+                const int hi = (qh[32 * half + l] >> (2 * k)) & 3;
+                const int q = (lo | (hi << 4)) - 32;
+                out[ORACLE_QK_K * b + e] = (d * (float)sc[8 * half + 2 * k + l / 16]) * (float)q;
+            }
+        }
+    }
+    return 0;
+}
+
+/* y[t * y_stride + o] = sum_i W[o][i] x[t * x_stride + i] (double accumulation of the
+ * dequantised f32 weights); returns -1 for an unsupported type / length */
+int oracle_mul_mat(const uint8_t *w, int type, int64_t row_bytes, int64_t n_in, int64_t n_out, const float *x,
+                   int64_t x_stride, int n_tokens, float *y, int64_t y_stride) {
+    if (oracle_row_bytes(type, n_in) == 0) return -1;
+    int bad = 0;
+#pragma omp parallel
+    {
+        float *wr = (float *)malloc((size_t)n_in * sizeof(float));
+#pragma omp for
+        for (int64_t o = 0; o < n_out; o++) {
+            if (!wr || oracle_dequant_row(w + o * row_bytes, type, n_in, wr) != 0) {
+                bad = 1;
+                continue;
+            }
+            for (int t = 0; t < n_tokens; t++) {
+                double acc = 0.0;
+                for (int64_t i = 0; i < n_in; i++) acc += (double)wr[i] * (double)x[t * x_stride + i];
+                y[t * y_stride + o] = (float)acc;
+            }
+        }
+        free(wr);
+    }
+    return bad ? -1 : 0;
+}

@@ -146,6 +146,15 @@ const size_t kGgmlGdnOp[] = {
     OFF(sqmix_ggml_gdn_op, stream),     OFF(sqmix_ggml_gdn_op, status),
 };
 
+const size_t kMulMat[] = {
+    OFF(sqmix_mul_mat_args, w),        OFF(sqmix_mul_mat_args, w_type),
+    OFF(sqmix_mul_mat_args, w_row_bytes), OFF(sqmix_mul_mat_args, n_in),
+    OFF(sqmix_mul_mat_args, n_out),    OFF(sqmix_mul_mat_args, x),
+    OFF(sqmix_mul_mat_args, x_dtype),  OFF(sqmix_mul_mat_args, x_stride),
+    OFF(sqmix_mul_mat_args, n_tokens), OFF(sqmix_mul_mat_args, y),
+    OFF(sqmix_mul_mat_args, y_stride), OFF(sqmix_mul_mat_args, status),
+};
+
 #undef OFF
 
 struct Entry {
@@ -171,6 +180,7 @@ bool lookup(int32_t which, Entry *e) {
         case SQMIX_ABI_GDN_LAYER_ARGS: *e = entry(sizeof(sqmix_gdn_layer_args), kGdnLayer); return true;
         case SQMIX_ABI_GGML_FA_OP: *e = entry(sizeof(sqmix_ggml_fa_op), kGgmlFaOp); return true;
         case SQMIX_ABI_GGML_GDN_OP: *e = entry(sizeof(sqmix_ggml_gdn_op), kGgmlGdnOp); return true;
+        case SQMIX_ABI_MUL_MAT_ARGS: *e = entry(sizeof(sqmix_mul_mat_args), kMulMat); return true;
         default: return false;
     }
 }

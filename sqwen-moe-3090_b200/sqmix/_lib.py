@@ -23,6 +23,9 @@ SQMIX_ERANGE = -6
 SQMIX_F32 = 0
 SQMIX_F16 = 1
 SQMIX_BF16 = 30
+SQMIX_Q8_0 = 8  # weight block formats of sqmix_mul_mat
+SQMIX_Q4_K = 12
+SQMIX_Q6_K = 14
 SQMIX_FA_OVERLAP_PREV = 1
 
 # struct ids of the library's ABI layout table (sqmix_abi_struct_size & co.)
@@ -36,6 +39,7 @@ SQMIX_ABI_HEAD_NORM_ARGS = 7
 SQMIX_ABI_GDN_LAYER_ARGS = 8
 SQMIX_ABI_GGML_FA_OP = 9
 SQMIX_ABI_GGML_GDN_OP = 10
+SQMIX_ABI_MUL_MAT_ARGS = 11
 
 ERROR_NAMES = {
     SQMIX_EINVAL: "SQMIX_EINVAL",
@@ -165,6 +169,14 @@ class GgmlGdnOp(ctypes.Structure):
     ]
 
 
+class MulMatArgs(ctypes.Structure):
+    _fields_ = [
+        ("w", c_void_p), ("w_type", c_int32), ("w_row_bytes", c_int64), ("n_in", c_int64), ("n_out", c_int64),
+        ("x", c_void_p), ("x_dtype", c_int32), ("x_stride", c_int64), ("n_tokens", c_int32), ("y", c_void_p),
+        ("y_stride", c_int64), ("status", c_void_p),
+    ]
+
+
 class GgmlTensor(ctypes.Structure):
     """ggml's struct ggml_tensor as sqwen's FFI declares it (src/backend/ffi.rs:22-39);
     used to build graph nodes for the custom-op bridge."""
@@ -216,6 +228,8 @@ _SIGNATURES = {
     "sqmix_gdn_conv": (ctypes.c_int, [ctypes.POINTER(GdnConvArgs), c_void_p]),
     "sqmix_head_norm": (ctypes.c_int, [ctypes.POINTER(HeadNormArgs), c_void_p]),
     "sqmix_gdn_layer_decode": (ctypes.c_int, [ctypes.POINTER(GdnLayerArgs), c_void_p]),
+    "sqmix_mul_mat_row_bytes": (c_int64, [c_int32, c_int64]),
+    "sqmix_mul_mat": (ctypes.c_int, [ctypes.POINTER(MulMatArgs), c_void_p]),
     "sqmix_ggml_fa_args": (ctypes.c_int, [ctypes.POINTER(GgmlTensor), ctypes.POINTER(GgmlFaOp), ctypes.POINTER(FaArgs)]),
     "sqmix_ggml_gdn_args": (ctypes.c_int, [ctypes.POINTER(GgmlTensor), ctypes.POINTER(GgmlGdnOp),
                                            ctypes.POINTER(GdnArgs)]),

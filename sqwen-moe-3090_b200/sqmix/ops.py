@@ -10,6 +10,8 @@ Names follow the ggml nodes they replace on sqwen's attention-mixer path:
   gated_delta_net  <- ggml_gated_delta_net (src/model/gdn.rs:489-500) with the
                       snapshot write-back (src/model/graph.rs:884-912) and plane
                       select (gdn.rs:445-463) done in place
+  mul_mat          <- ggml_mul_mat of the mixer projections on GGUF weights
+                      (src/model/attn.rs:127-129, 285; src/model/gdn.rs:264-276, 577)
 
 Every function launches on torch's current CUDA stream and raises SqmixError on a
 non-zero status, mirroring how the reference turns ggml failures into Err.
@@ -22,7 +24,7 @@ import math
 import torch
 
 from ._lib import (SQMIX_BF16, SQMIX_F16, SQMIX_F32, SQMIX_FA_OVERLAP_PREV, FaArgs, FaBatchArgs, GdnArgs, GdnConvArgs,
-                   GdnLayerArgs, HeadNormArgs, KvAppendArgs, check, lib)
+                   GdnLayerArgs, HeadNormArgs, KvAppendArgs, MulMatArgs, check, lib)
 
 HEAD_DIM = 256
 N_HEAD = 16
@@ -473,3 +475,32 @@ def gdn_layer_decode(x: torch.Tensor, conv_weight: torch.Tensor, conv_state: tor
 
 def rope_theta_scale(freq_base: float, n_rot: int) -> float:
     return math.pow(freq_base, -2.0 / n_rot)
+
+
+def mul_mat_row_bytes(w_type: int, n_in: int) -> int:
+    """Bytes of one weight row of n_in values in ggml format w_type (0: unsupported)."""
+    return int(lib().sqmix_mul_mat_row_bytes(int(w_type), int(n_in)))
+
+
+def mul_mat(w: torch.Tensor, w_type: int, n_in: int, x: torch.Tensor, out: torch.Tensor | None = None,
+            status: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """ggml_mul_mat(w, x): w [n_out][row bytes] (uint8, a GGUF block format: SQMIX_Q8_0 /
+    SQMIX_Q4_K / SQMIX_Q6_K) or [n_out][n_in] f32 / f16 / bf16 elements; x [T][n_in]
+    (f32 / f16 / bf16, rows contiguous).  Returns y [T][n_out] f32."""
+    rb = mul_mat_row_bytes(w_type, n_in)
+    if rb == 0:
+        raise ValueError(f"unsupported weight type {w_type} for n_in={n_in}")
+    if not w.is_contiguous() or w.numel() * w.element_size() % rb != 0:
+        raise ValueError("w must be contiguous rows of the format")
+    n_out = w.numel() * w.element_size() // rb
+    x2 = x.reshape(-1, n_in)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    T = x2.shape[0]
+    if out is None:
+        out = torch.empty((T, n_out), dtype=torch.float32, device=x.device)
+    a = MulMatArgs(w=w.data_ptr(), w_type=int(w_type), w_row_bytes=rb, n_in=n_in, n_out=n_out, x=x2.data_ptr(),
+                   x_dtype=_dt(x2), x_stride=x2.stride(0), n_tokens=T, y=out.data_ptr(), y_stride=out.stride(0),
+                   status=status.data_ptr() if status is not None else None)
+    check(lib().sqmix_mul_mat(ctypes.byref(a), _stream(stream)), "mul_mat")
+    return out

@@ -213,6 +213,7 @@ def _abi_structs():
         "sqmix_gdn_layer_args": (L.SQMIX_ABI_GDN_LAYER_ARGS, L.GdnLayerArgs),
         "sqmix_ggml_fa_op": (L.SQMIX_ABI_GGML_FA_OP, L.GgmlFaOp),
         "sqmix_ggml_gdn_op": (L.SQMIX_ABI_GGML_GDN_OP, L.GgmlGdnOp),
+        "sqmix_mul_mat_args": (L.SQMIX_ABI_MUL_MAT_ARGS, L.MulMatArgs),
     }
 
 
@@ -250,3 +251,37 @@ def test_integration_guide_rust_structs_match_header():
         assert rust[rname] == fields, rname
     for name in declared_functions():
         assert f"pub fn {name}(" in guide, f"INTEGRATION.md's extern block lacks {name}"
+
+
+def test_mul_mat_argument_validation_without_gpu(sqmix_lib):
+    from sqmix._lib import MulMatArgs
+
+    L = sqmix_lib.lib()
+    assert L.sqmix_mul_mat_row_bytes(sqmix_lib.SQMIX_Q4_K, 2048) == 8 * 144
+    assert L.sqmix_mul_mat_row_bytes(sqmix_lib.SQMIX_Q6_K, 4096) == 16 * 210
+    assert L.sqmix_mul_mat_row_bytes(sqmix_lib.SQMIX_Q8_0, 2048) == 8 * 272
+    assert L.sqmix_mul_mat_row_bytes(2, 2048) == 0  # q4_0 weights: not a projection format here
+    assert L.sqmix_mul_mat_row_bytes(sqmix_lib.SQMIX_F32, 100) == 0
+    fake = ctypes.c_void_p(4096)
+
+    def args(**kw):
+        base = dict(w=fake, w_type=sqmix_lib.SQMIX_Q4_K, w_row_bytes=8 * 144, n_in=2048, n_out=64, x=fake,
+                    x_dtype=sqmix_lib.SQMIX_F32, x_stride=2048, n_tokens=1, y=fake, y_stride=64)
+        base.update(kw)
+        return MulMatArgs(**base)
+
+    bad = [
+        dict(w_type=2, w_row_bytes=0),                             # unsupported block format
+        dict(n_in=8192, w_row_bytes=32 * 144, x_stride=8192),      # n_in above 4096
+        dict(n_in=300),                                            # not a multiple of 256
+        dict(w_row_bytes=8 * 144 + 16),                            # rows not contiguous
+        dict(w_type=sqmix_lib.SQMIX_Q6_K, n_in=512, w_row_bytes=2 * 210, x_stride=512),  # 420-byte rows
+        dict(w=ctypes.c_void_p(4096 + 8)),                         # w not 16-byte aligned
+        dict(n_tokens=0),
+        dict(x_stride=100),
+        dict(x_dtype=2),
+        dict(y=None),
+    ]
+    for kw in bad:
+        a = args(**kw)
+        assert L.sqmix_mul_mat(ctypes.byref(a), None) == sqmix_lib.SQMIX_EINVAL, kw

@@ -1,0 +1,114 @@
+"""GPU parity of the mixer projections (sqmix_mul_mat, ggml_mul_mat of attn.rs:127-129,
+285 and gdn.rs:264-276, 577) against the golden vectors (gguf-py's dequantizers) and the
+CPU oracle at the model's shapes (n_embd 2048, QG 8192, KV 512, d_inner 4096, conv 8192,
+32 value heads).
+
+Bar: max |gpu - ref| <= 1e-5 * max |ref| (f32 sums of dequantised weights against
+float64 sums of the same weights).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "proj_golden.npz")
+
+
+def rel_err(got, want):
+    return np.abs(np.asarray(got, np.float64) - want).max() / max(np.abs(want).max(), 1e-30)
+
+
+def random_rows(rng, wtype, n_in, n_out):
+    """Valid raw rows: random quant / scale bytes, finite f16 super-block scales."""
+    nb = n_out * n_in // 256
+
+    def f16(n, s):
+        return (rng.standard_normal(n) * s).astype(np.float16).view(np.uint8).reshape(n, 2)
+
+    if wtype == 12:
+        rows = np.concatenate([f16(nb, 1e-3), f16(nb, 1e-3), rng.integers(0, 256, (nb, 140), dtype=np.uint8)], 1)
+    elif wtype == 14:
+        rows = np.concatenate([rng.integers(0, 256, (nb, 208), dtype=np.uint8), f16(nb, 1e-3)], 1)
+    elif wtype == 8:
+        nb32 = n_out * n_in // 32
+        rows = np.concatenate([f16(nb32, 1e-3), rng.integers(0, 256, (nb32, 32), dtype=np.uint8)], 1)
+    else:
+        w = rng.standard_normal((n_out, n_in)).astype(np.float32) * 0.05
+        if wtype == 0:
+            return w.view(np.uint8).reshape(n_out, -1)
+        if wtype == 1:
+            return w.astype(np.float16).view(np.uint8).reshape(n_out, -1)
+        return (w.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8).reshape(n_out, -1)
+    return np.ascontiguousarray(rows).reshape(n_out, -1)
+
+
+@pytest.mark.parametrize("name,wtype", [("q4_k", 12), ("q6_k", 14), ("q8_0", 8)])
+def test_mul_mat_golden(name, wtype):
+    import sqmix
+
+    d = np.load(GOLDEN)
+    x = d[f"{name}_x"]
+    w = torch.from_numpy(d[f"{name}_w"]).cuda()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    y = sqmix.mul_mat(w, wtype, x.shape[1], torch.from_numpy(x).cuda(), status=status)
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), d[f"{name}_y"]) <= TOL
+    assert int(status.item()) == 0
+
+
+# (weight type, n_in, n_out, tokens, x dtype): the model's projections (Q4_K_M assigns
+# q4_K to most, q6_K to attn_v; ssm_alpha / ssm_beta have 32 rows), ragged row counts,
+# several passes of 4 tokens, half-precision activations
+CASES = [
+    (12, 2048, 8192, 1, torch.float32),   # QG / qkv
+    (14, 2048, 512, 2, torch.float32),    # attn_v, MTP verification
+    (12, 4096, 2048, 1, torch.float32),   # W_o / ssm_out
+    (8, 4096, 2048, 3, torch.float32),
+    (0, 2048, 32, 1, torch.float32),      # ssm_alpha as f32
+    (30, 2048, 37, 5, torch.bfloat16),    # ragged tile, two passes
+    (1, 1024, 100, 4, torch.float16),
+    (12, 256, 9, 9, torch.float32),       # one super-block per row, three passes
+]
+
+
+@pytest.mark.parametrize("wtype,n_in,n_out,T,xdt", CASES)
+def test_mul_mat_model_shapes_vs_oracle(oracle, wtype, n_in, n_out, T, xdt):
+    import sqmix
+
+    rng = np.random.default_rng(1000 + n_out + wtype)
+    rows = random_rows(rng, wtype, n_in, n_out)
+    x = torch.randn((T, n_in), generator=torch.Generator().manual_seed(n_in + T)).to(xdt)
+    want = oracle.mul_mat(rows, wtype, n_in, x.float().numpy())
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    y = sqmix.mul_mat(torch.from_numpy(rows).cuda(), wtype, n_in, x.cuda(), status=status)
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), want.astype(np.float64)) <= TOL
+    assert int(status.item()) == 0
+
+
+def test_mul_mat_strided_tokens_and_output():
+    """x and y with token strides larger than their rows (views into wider buffers)."""
+    import sqmix
+    from sqmix._lib import MulMatArgs, check, lib
+    import ctypes
+
+    rng = np.random.default_rng(7)
+    n_in, n_out, T = 2048, 64, 3
+    rows = random_rows(rng, 12, n_in, n_out)
+    xw = torch.randn((T, n_in + 64), device="cuda")
+    yw = torch.full((T, n_out + 16), 7.0, device="cuda")
+    w = torch.from_numpy(rows).cuda()
+    a = MulMatArgs(w=w.data_ptr(), w_type=12, w_row_bytes=sqmix.mul_mat_row_bytes(12, n_in), n_in=n_in, n_out=n_out,
+                   x=xw.data_ptr(), x_dtype=0, x_stride=n_in + 64, n_tokens=T, y=yw.data_ptr(), y_stride=n_out + 16)
+    check(lib().sqmix_mul_mat(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "mul_mat")
+    torch.cuda.synchronize()
+    import oracle as orc
+
+    want = orc.mul_mat(rows, 12, n_in, xw[:, :n_in].cpu().numpy())
+    got = yw.cpu().numpy()
+    assert rel_err(got[:, :n_out], want.astype(np.float64)) <= TOL
+    assert (got[:, n_out:] == 7.0).all()  # nothing written past the rows

@@ -408,3 +408,47 @@ def test_cpu_baseline_matches_checker(oracle):
     got_o = oracle.cpu_gdn_f32(qg, kg, vg, g, b, st)
     assert np.abs(got_o - want_o).max() <= 1e-4 * np.abs(want_o).max()
     assert np.abs(st - snaps[0]).max() <= 1e-4 * np.abs(snaps[0]).max()
+
+
+# ---------------------------------------------------------- projections ---
+PROJ_GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "proj_golden.npz")
+PROJ_TYPES = (("q4_k", 12), ("q6_k", 14), ("q8_0", 8))
+
+
+@pytest.mark.parametrize("name,wtype", PROJ_TYPES)
+def test_proj_dequant_bit_exact_vs_gguf_golden(oracle, name, wtype):
+    """q4_K / q6_K / q8_0 rows dequantised exactly as gguf-py's restatement of ggml's
+    block formats (the weights of ggml_mul_mat in attn.rs:127-129 / gdn.rs:264-276)."""
+    d = np.load(PROJ_GOLDEN)
+    n_in = d[f"{name}_x"].shape[1]
+    got = oracle.dequant_rows(d[f"{name}_w"], wtype, n_in)
+    assert np.array_equal(got.view(np.uint32), d[f"{name}_deq"].view(np.uint32))
+
+
+@pytest.mark.parametrize("name,wtype", PROJ_TYPES)
+def test_proj_mul_mat_vs_golden(oracle, name, wtype):
+    d = np.load(PROJ_GOLDEN)
+    n_in = d[f"{name}_x"].shape[1]
+    y = oracle.mul_mat(d[f"{name}_w"], wtype, n_in, d[f"{name}_x"])
+    ref = d[f"{name}_y"]
+    assert np.abs(y - ref).max() <= 1e-6 * np.abs(ref).max()
+
+
+def test_proj_row_bytes_and_float_types(oracle):
+    assert oracle.row_bytes(12, 2048) == 8 * 144
+    assert oracle.row_bytes(14, 2048) == 8 * 210
+    assert oracle.row_bytes(8, 2048) == 64 * 34
+    assert oracle.row_bytes(12, 100) == 0 and oracle.row_bytes(2, 256) == 0
+    rng = np.random.default_rng(5)
+    w = rng.standard_normal((5, 256)).astype(np.float32)
+    x = rng.standard_normal((2, 256)).astype(np.float32)
+    for wtype, raw in ((0, w), (1, w.astype(np.float16)), (30, None)):
+        if wtype == 30:  # bf16: the high halves of the f32 words
+            raw = (w.view(np.uint32) >> 16).astype(np.uint16)
+            deq = (raw.astype(np.uint32) << 16).view(np.float32)
+        else:
+            deq = raw.astype(np.float32)
+        rows = np.ascontiguousarray(raw).view(np.uint8).reshape(5, -1)
+        assert np.array_equal(oracle.dequant_rows(rows, wtype, 256), deq)
+        y = oracle.mul_mat(rows, wtype, 256, x)
+        assert np.allclose(y, x.astype(np.float64) @ deq.astype(np.float64).T, rtol=1e-6, atol=1e-6)
