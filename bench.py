@@ -1062,6 +1062,107 @@ def stack_lengths():
     return np.sort(rng.integers(1024, 32768 + 1, STACK_SEQS))[::-1]
 
 
+# Mixer projections of one token through the 40 layers (n_embd 2048): (name, ggml type,
+# n_in, n_out) per layer kind.  Types as a Q4_K_M model assigns them (attn_v q6_K, the
+# other large matrices q4_K; the 32-row ssm_beta / ssm_alpha kept f32).
+PROJ_FULL = [("attn_q", 12, 2048, 8192), ("attn_k", 12, 2048, 512), ("attn_v", 14, 2048, 512),
+             ("attn_output", 12, 4096, 2048)]
+PROJ_GDN = [("attn_qkv", 12, 2048, 8192), ("attn_gate", 12, 2048, 4096), ("ssm_beta", 0, 2048, 32),
+            ("ssm_alpha", 0, 2048, 32), ("ssm_out", 12, 4096, 2048)]
+
+
+def proj_weights(n_in, n_out, wtype, dev, seed):
+    """Random rows of a GGUF format with finite f16 scales (raw quant bytes are all valid)."""
+    import torch
+
+    import sqmix
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    if wtype == 0:
+        return (torch.randn((n_out, n_in), generator=g, device=dev) * 0.02).view(torch.uint8)
+    rb = sqmix.mul_mat_row_bytes(wtype, n_in)
+    w = torch.randint(0, 256, (n_out, rb), generator=g, dtype=torch.uint8, device=dev)
+    if wtype == 12:  # d, dmin = 2^-11
+        w.view(-1, 144)[:, 0:4] = torch.tensor([0, 16, 0, 16], dtype=torch.uint8, device=dev)
+    elif wtype == 14:
+        w.view(-1, 210)[:, 208:210] = torch.tensor([0, 16], dtype=torch.uint8, device=dev)
+    return w
+
+
+def bench_proj(steps: int, warmup: int) -> dict:
+    """The mixer projections of one decode token (T = 1) and of an MTP verification
+    step (T = 2) through all 40 layers: 10 x 4 + 30 x 5 = 190 sqmix_mul_mat calls on
+    distinct weights (735 MB > L2), captured in a CUDA graph."""
+    import torch
+
+    import sqmix
+
+    dev = torch.device("cuda", 0)
+    hbm, hbm_kind = peaks()
+    calls = []
+    seed = 0
+    for layer in range(40):
+        for name, wt, n_in, n_out in (PROJ_FULL if layer % 4 == 3 else PROJ_GDN):
+            seed += 1
+            calls.append((wt, n_in, n_out, proj_weights(n_in, n_out, wt, dev, seed)))
+    wbytes = sum(w.numel() for _, _, _, w in calls)
+    res = {"launches_per_token": len(calls), "weight_bytes": wbytes, "peak_gbs": hbm, "peak_kind": hbm_kind}
+    for T in (1, 2):
+        xs = {n: torch.randn((T, n), device=dev) for n in (2048, 4096)}
+        ys = {n: torch.empty((T, n), device=dev) for n in (32, 512, 2048, 4096, 8192)}
+
+        def step():
+            for wt, n_in, n_out, w in calls:
+                sqmix.mul_mat(w, wt, n_in, xs[n_in], out=ys[n_out])
+
+        us = _graph_us(step, 1, max(3, min(steps, 200)), warmup)
+        res[f"T{T}"] = {"us_per_step": us, "achieved_gbs": wbytes / us / 1e3, "frac_of_hbm": wbytes / us / 1e3 / hbm}
+    # the largest single projection, alone (QG / qkv: 2048 -> 8192 q4_K)
+    w = calls[0][3]
+    x1 = torch.randn((1, 2048), device=dev)
+    y1 = torch.empty((1, 8192), device=dev)
+    ws = [proj_weights(2048, 8192, 12, dev, 1000 + i) for i in range(16)]
+
+    def one():
+        for wi in ws:
+            sqmix.mul_mat(wi, 12, 2048, x1, out=y1)
+
+    us1 = _graph_us(one, len(ws), max(3, min(steps, 200)), warmup)
+    b1 = w.numel()
+    res["qkv_2048x8192_q4k"] = {"us": us1, "bytes": b1, "achieved_gbs": b1 / us1 / 1e3, "frac_of_hbm": b1 / us1 / 1e3 / hbm}
+    res["note"] = ("weights: random GGUF blocks with finite scales; the roofline is the weight stream (x and y are "
+                   "a few KB); one launch per matrix, a fixed per-launch cost of about 4 us dominates the small ones")
+    return res
+
+
+def cpu_baseline_proj() -> dict:
+    """The projections on the host cores with ggml-cpu's algorithm (x quantised to q8_K,
+    integer dots), on a bounded sample: one attn_qkv (2048 -> 8192 q4_K) at T = 1, scaled
+    by weight bytes to the 40 layers."""
+    oracle, cores = cpu_setup()
+    rng = np.random.default_rng(9)
+    rb = oracle.row_bytes(12, 2048)
+    w = rng.integers(0, 256, (8192, rb), dtype=np.uint8)
+    w.reshape(-1, 144)[:, 0:4] = np.array([0, 16, 0, 16], dtype=np.uint8)
+    x = rng.standard_normal((1, 2048)).astype(np.float32)
+    oracle.cpu_mul_mat(w, 12, 2048, x)
+    reps, t0 = 0, time.perf_counter()
+    while reps < 5 or time.perf_counter() - t0 < 1.0:
+        oracle.cpu_mul_mat(w, 12, 2048, x)
+        reps += 1
+    us = (time.perf_counter() - t0) / reps * 1e6
+    total_bytes = 0
+    for layer in range(40):
+        for _, wt, n_in, n_out in (PROJ_FULL if layer % 4 == 3 else PROJ_GDN):
+            total_bytes += oracle.row_bytes(wt, n_in) * n_out
+    scale = total_bytes / w.nbytes
+    return {"value": us * scale, "unit": "us/token", "qkv_us": us, "cores": cores, "kind": CPU_KIND,
+            "sample": f"{reps} runs of one 2048 -> 8192 q4_K projection (T = 1), scaled by weight bytes to the 190 "
+                      "projections of a token; C restatement of ggml-cpu's q4_K x q8_K integer dot products "
+                      "(oracle/cpu_ggml.c)"}
+
+
 def bench_gdn_layer(g, dev, steps: int, warmup: int, hbm: float, hbm_kind: str) -> dict:
     """A whole GDN mixer decode step at batch 1 (config 1 shapes): the one-launch layer
     (sqmix_gdn_layer_decode: conv + SiLU + L2 norm + gate epilogue + recurrence +
@@ -1339,12 +1440,14 @@ def main():
             res["config0"] = bench_config0(args.steps, args.warmup)
             res["prefill"] = bench_prefill(args.steps, args.warmup)
             res["gdn"] = bench_gdn(args.steps, args.warmup)
+            res["proj"] = bench_proj(args.steps, args.warmup)
         stack = bench_stack(args.steps, args.warmup, rank, world, local_rank)  # every rank (sharded)
         if res is not None:
             res["stack"] = stack
         if cpu_on:
             res["config0"]["cpu_baseline"] = cpu_baseline_config0()
             res["gdn"]["cpu_baseline"] = cpu_baseline_config1()
+            res["proj"]["cpu_baseline"] = cpu_baseline_proj()
             res["prefill"]["cpu_baseline"] = cpu_baseline_config2()
             res["stack"]["cpu_baseline"] = cpu_baseline_config4(stack_lengths())
     if res is not None:

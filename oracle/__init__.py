@@ -69,6 +69,8 @@ def lib():
         L.oracle_dequant_row.restype = ctypes.c_int
         L.oracle_mul_mat.argtypes = [u8p, ctypes.c_int, i64, i64, i64, f32p, i64, ctypes.c_int, f32p, i64]
         L.oracle_mul_mat.restype = ctypes.c_int
+        L.cpu_mul_mat.argtypes = [u8p, ctypes.c_int, i64, i64, i64, f32p, ctypes.c_int, f32p]
+        L.cpu_mul_mat.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -345,5 +347,21 @@ def mul_mat(w: np.ndarray, wtype: int, n_in: int, x: np.ndarray) -> np.ndarray:
     y = np.zeros((T, n_out), dtype=np.float32)
     rc = lib().oracle_mul_mat(w.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), int(wtype), rb, n_in, n_out, xp,
                               n_in, T, y.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n_out)
+    assert rc == 0
+    return y
+
+
+def cpu_mul_mat(w: np.ndarray, wtype: int, n_in: int, x: np.ndarray) -> np.ndarray:
+    """The timed CPU baseline of ggml_mul_mat: ggml-cpu's quantised dot products (x
+    quantised to q8_K / q8_0 per token), rows across threads.  Not the checker."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    rb = row_bytes(wtype, n_in)
+    assert rb > 0 and w.shape[-1] == rb
+    n_out = w.size // rb
+    xs, xp = _f32(np.asarray(x, dtype=np.float32).reshape(-1, n_in))
+    T = xs.shape[0]
+    y = np.zeros((T, n_out), dtype=np.float32)
+    rc = lib().cpu_mul_mat(w.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), int(wtype), rb, n_in, n_out, xp, T,
+                           y.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
     assert rc == 0
     return y

@@ -202,3 +202,175 @@ void cpu_gdn_f32(const float *q, const float *k, const float *v, const float *g,
         }
     }
 }
+
+/* ---------------------------------------------------------- projections ----
+ * ggml_mul_mat(w, x) of the mixer projections (attn.rs:127-129, 285; gdn.rs:264-276,
+ * 577) the way ggml-cpu runs it for quantised weights: x is quantised once per token to
+ * the weight's dot-product type -- q8_K (256-value blocks: f32 d, int8 q, int16 sums of
+ * 16) for q4_K / q6_K, q8_0 for q8_0 -- and every weight row is an integer dot product
+ * per block, scaled in f32.  f32 / f16 / bf16 weights: f32 dot products.  Rows are
+ * split across threads, as ggml splits the rows of a mul_mat. */
+#define QKK 256
+
+/* quantize_row_q8_K of one 256-value block: iscale = -127 / (the value of largest
+ * magnitude), q = round(iscale x) (at most 127), d = 1 / iscale, bsums of 16 values. */
+static void q8_k_block(const float *x, int8_t *q, float *d_out, int16_t *bsums) {
+    float amax = 0.0f, max = 0.0f;
+    for (int j = 0; j < QKK; j++) {
+        const float a = fabsf(x[j]);
+        if (a > amax) {
+            amax = a;
+            max = x[j];
+        }
+    }
+    if (amax == 0.0f) {
+        *d_out = 0.0f;
+        memset(q, 0, QKK);
+        memset(bsums, 0, 16 * sizeof(int16_t));
+        return;
+    }
+    const float iscale = -127.0f / max;
+    for (int j = 0; j < QKK; j++) {
+        int v = (int)lrintf(iscale * x[j]);
+        q[j] = (int8_t)(v > 127 ? 127 : v);
+    }
+    for (int j = 0; j < 16; j++) {
+        int s = 0;
+        for (int i = 0; i < 16; i++) s += q[16 * j + i];
+        bsums[j] = (int16_t)s;
+    }
+    *d_out = 1.0f / iscale;
+}
+
+static void q4k_scale_min_c(int j, const uint8_t *s, int *sc, int *m) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *m = s[j + 4] & 63;
+    } else {
+        *sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+        *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+/* vec_dot_q4_K_q8_K: d_x (d sum_j sc_j sum q4 q8) - d_x dmin sum_j m_j bsum_j */
+static float dot_q4_k_q8_k(const uint8_t *w, const int8_t *yq, const float *yd, const int16_t *ys, int n_blk) {
+    float sum = 0.0f;
+    for (int b = 0; b < n_blk; b++) {
+        const uint8_t *blk = w + 144 * b;
+        const uint8_t *qs = blk + 16;
+        const int8_t *y = yq + QKK * b;
+        const int16_t *bs = ys + 16 * b;
+        int32_t isum = 0, msum = 0;
+        for (int j = 0; j < 8; j++) {
+            int sc, m;
+            q4k_scale_min_c(j, blk + 4, &sc, &m);
+            int32_t s = 0;
+            const int sh = 4 * (j & 1);
+            for (int l = 0; l < 32; l++) s += ((qs[32 * (j >> 1) + l] >> sh) & 0xF) * (int32_t)y[32 * j + l];
+            isum += sc * s;
+            msum += m * (bs[2 * j] + bs[2 * j + 1]);
+        }
+        sum += yd[b] * (f16v(blk) * (float)isum - f16v(blk + 2) * (float)msum);
+    }
+    return sum;
+}
+
+/* vec_dot_q6_K_q8_K: d_x d sum_k sc_k sum (q6 - 32) q8 */
+static float dot_q6_k_q8_k(const uint8_t *w, const int8_t *yq, const float *yd, int n_blk) {
+    float sum = 0.0f;
+    for (int b = 0; b < n_blk; b++) {
+        const uint8_t *blk = w + 210 * b;
+        const int8_t *sc = (const int8_t *)(blk + 192);
+        const int8_t *y = yq + QKK * b;
+        int32_t isum = 0;
+        for (int k = 0; k < 16; k++) {
+            int32_t s = 0;
+            for (int i = 0; i < 16; i++) {
+                const int e = 16 * k + i, half = e / 128, r = e % 128, qq = r / 32, l = r % 32;
+                const int lo = (blk[64 * half + 32 * (qq & 1) + l] >> (4 * (qq >> 1))) & 0xF;
+                const int hi = (blk[128 + 32 * half + l] >> (2 * qq)) & 3;
+                s += ((lo | (hi << 4)) - 32) * (int32_t)y[e];
+            }
+            isum += sc[k] * s;
+        }
+        sum += yd[b] * f16v(blk + 208) * (float)isum;
+    }
+    return sum;
+}
+
+/* vec_dot_q8_0_q8_0: sum_b d_w d_x sum q_w q_x */
+static float dot_q8_0_q8_0(const uint8_t *w, const int8_t *yq, const float *yd, int n_blk) {
+    float sum = 0.0f;
+    for (int b = 0; b < n_blk; b++) {
+        const uint8_t *blk = w + 34 * b;
+        const int8_t *q = (const int8_t *)(blk + 2);
+        const int8_t *y = yq + QK * b;
+        int32_t s = 0;
+        for (int j = 0; j < QK; j++) s += (int32_t)q[j] * (int32_t)y[j];
+        sum += (float)s * (f16v(blk) * yd[b]);
+    }
+    return sum;
+}
+
+/* y[t * n_out + o] for w_type 8 / 12 / 14 (quantised) or 0 / 1 / 30; returns -1 for an
+ * unsupported type or length */
+int cpu_mul_mat(const uint8_t *w, int w_type, int64_t row_bytes, int64_t n_in, int64_t n_out, const float *x,
+                int n_tok, float *y) {
+    f16_table();
+    const int kq = w_type == 12 || w_type == 14;
+    if ((kq && n_in % QKK) || (w_type == 8 && n_in % QK)) return -1;
+    if (!kq && w_type != 8 && w_type != 0 && w_type != 1 && w_type != 30) return -1;
+    const int64_t n_blk = kq ? n_in / QKK : n_in / QK;
+    int8_t *yq = (int8_t *)malloc((size_t)n_tok * n_in);
+    float *yd = (float *)malloc((size_t)n_tok * n_blk * sizeof(float));
+    int16_t *ys = (int16_t *)malloc((size_t)n_tok * (n_in / 16 + 1) * sizeof(int16_t));
+    if (!yq || !yd || !ys) {
+        free(yq);
+        free(yd);
+        free(ys);
+        return -1;
+    }
+    if (kq || w_type == 8)
+        for (int t = 0; t < n_tok; t++)
+            for (int64_t b = 0; b < n_blk; b++) {
+                if (kq)
+                    q8_k_block(x + t * n_in + QKK * b, yq + t * n_in + QKK * b, yd + t * n_blk + b,
+                               ys + t * (n_in / 16) + 16 * b);
+                else
+                    q8_0_block(x + t * n_in + QK * b, yq + t * n_in + QK * b, yd + t * n_blk + b);
+            }
+#pragma omp parallel for schedule(static)
+    for (int64_t o = 0; o < n_out; o++) {
+        const uint8_t *wr = w + o * row_bytes;
+        for (int t = 0; t < n_tok; t++) {
+            float r;
+            if (w_type == 12)
+                r = dot_q4_k_q8_k(wr, yq + t * n_in, yd + t * n_blk, ys + t * (n_in / 16), (int)n_blk);
+            else if (w_type == 14)
+                r = dot_q6_k_q8_k(wr, yq + t * n_in, yd + t * n_blk, (int)n_blk);
+            else if (w_type == 8)
+                r = dot_q8_0_q8_0(wr, yq + t * n_in, yd + t * n_blk, (int)n_blk);
+            else {
+                float s = 0.0f;
+                for (int64_t i = 0; i < n_in; i++) {
+                    float wv;
+                    if (w_type == 0) {
+                        memcpy(&wv, wr + 4 * i, 4);
+                    } else if (w_type == 1) {
+                        wv = f16v(wr + 2 * i);
+                    } else {
+                        const uint32_t u = (uint32_t)(wr[2 * i] | (wr[2 * i + 1] << 8)) << 16;
+                        memcpy(&wv, &u, 4);
+                    }
+                    s += wv * x[t * n_in + i];
+                }
+                r = s;
+            }
+            y[t * n_out + o] = r;
+        }
+    }
+    free(yq);
+    free(yd);
+    free(ys);
+    return 0;
+}

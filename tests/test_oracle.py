@@ -452,3 +452,14 @@ def test_proj_row_bytes_and_float_types(oracle):
         assert np.array_equal(oracle.dequant_rows(rows, wtype, 256), deq)
         y = oracle.mul_mat(rows, wtype, 256, x)
         assert np.allclose(y, x.astype(np.float64) @ deq.astype(np.float64).T, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("name,wtype", PROJ_TYPES)
+def test_cpu_baseline_mul_mat_matches_checker(oracle, name, wtype):
+    """The timed ggml-cpu restatement (x quantised to q8_K / q8_0) agrees with the exact
+    checker to the accuracy of its 8-bit activations."""
+    d = np.load(PROJ_GOLDEN)
+    n_in = d[f"{name}_x"].shape[1]
+    y = oracle.cpu_mul_mat(d[f"{name}_w"], wtype, n_in, d[f"{name}_x"])
+    ref = d[f"{name}_y"]
+    assert np.abs(y - ref).max() <= 2e-2 * np.abs(ref).max()
