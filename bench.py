@@ -1092,34 +1092,56 @@ def proj_weights(n_in, n_out, wtype, dev, seed):
 
 def bench_proj(steps: int, warmup: int) -> dict:
     """The mixer projections of one decode token (T = 1) and of an MTP verification
-    step (T = 2) through all 40 layers: 10 x 4 + 30 x 5 = 190 sqmix_mul_mat calls on
-    distinct weights (735 MB > L2), captured in a CUDA graph."""
+    step (T = 2) through all 40 layers on distinct weights (735 MB > L2), captured in a
+    CUDA graph: the projections of one x go as one sqmix_mul_mat_group call (QG / K / V;
+    qkv / z / beta / alpha), W_o and ssm_out alone -- 10 x 2 + 30 x 2 = 80 calls, 110
+    launches (the f32 beta / alpha of a group take a launch of their own).  The 190
+    single sqmix_mul_mat calls are timed beside it at T = 1."""
     import torch
 
     import sqmix
 
     dev = torch.device("cuda", 0)
     hbm, hbm_kind = peaks()
-    calls = []
+    layers = []  # per layer: groups of (name, wt, n_in, n_out, w) sharing x
     seed = 0
     for layer in range(40):
+        groups = {}
         for name, wt, n_in, n_out in (PROJ_FULL if layer % 4 == 3 else PROJ_GDN):
             seed += 1
-            calls.append((wt, n_in, n_out, proj_weights(n_in, n_out, wt, dev, seed)))
-    wbytes = sum(w.numel() for _, _, _, w in calls)
-    res = {"launches_per_token": len(calls), "weight_bytes": wbytes, "peak_gbs": hbm, "peak_kind": hbm_kind}
+            groups.setdefault(n_in, []).append((name, wt, n_in, n_out, proj_weights(n_in, n_out, wt, dev, seed)))
+        layers.append(list(groups.values()))
+    calls = [c for groups in layers for grp in groups for c in grp]
+    n_launch = sum(len({wt in (8, 12, 14) for _, wt, _, _, _ in grp}) for groups in layers for grp in groups)
+    wbytes = sum(c[4].numel() for c in calls)
+    res = {"calls_per_token": sum(len(groups) for groups in layers), "launches_per_token": n_launch,
+           "weight_bytes": wbytes, "peak_gbs": hbm, "peak_kind": hbm_kind}
     for T in (1, 2):
         xs = {n: torch.randn((T, n), device=dev) for n in (2048, 4096)}
-        ys = {n: torch.empty((T, n), device=dev) for n in (32, 512, 2048, 4096, 8192)}
+        ys = {}
+        for name, _, _, n_out, _ in calls:
+            ys.setdefault(name, torch.empty((T, n_out), device=dev))
 
         def step():
-            for wt, n_in, n_out, w in calls:
-                sqmix.mul_mat(w, wt, n_in, xs[n_in], out=ys[n_out])
+            for groups in layers:
+                for grp in groups:
+                    if len(grp) == 1:
+                        name, wt, n_in, _, w = grp[0]
+                        sqmix.mul_mat(w, wt, n_in, xs[n_in], out=ys[name])
+                    else:
+                        sqmix.mul_mat_group([(w, wt) for _, wt, _, _, w in grp], grp[0][2], xs[grp[0][2]],
+                                            outs=[ys[name] for name, *_ in grp])
 
         us = _graph_us(step, 1, max(3, min(steps, 200)), warmup)
         res[f"T{T}"] = {"us_per_step": us, "achieved_gbs": wbytes / us / 1e3, "frac_of_hbm": wbytes / us / 1e3 / hbm}
+        if T == 1:
+            def step_single():
+                for name, wt, n_in, _, w in calls:
+                    sqmix.mul_mat(w, wt, n_in, xs[n_in], out=ys[name])
+
+            us = _graph_us(step_single, 1, max(3, min(steps, 200)), warmup)
+            res["T1_single_calls"] = {"calls": len(calls), "us_per_step": us, "frac_of_hbm": wbytes / us / 1e3 / hbm}
     # the largest single projection, alone (QG / qkv: 2048 -> 8192 q4_K)
-    w = calls[0][3]
     x1 = torch.randn((1, 2048), device=dev)
     y1 = torch.empty((1, 8192), device=dev)
     ws = [proj_weights(2048, 8192, 12, dev, 1000 + i) for i in range(16)]
@@ -1129,10 +1151,11 @@ def bench_proj(steps: int, warmup: int) -> dict:
             sqmix.mul_mat(wi, 12, 2048, x1, out=y1)
 
     us1 = _graph_us(one, len(ws), max(3, min(steps, 200)), warmup)
-    b1 = w.numel()
+    b1 = ws[0].numel()
     res["qkv_2048x8192_q4k"] = {"us": us1, "bytes": b1, "achieved_gbs": b1 / us1 / 1e3, "frac_of_hbm": b1 / us1 / 1e3 / hbm}
     res["note"] = ("weights: random GGUF blocks with finite scales; the roofline is the weight stream (x and y are "
-                   "a few KB); one launch per matrix, a fixed per-launch cost of about 4 us dominates the small ones")
+                   "a few KB); a launch has a fixed cost of a few us (the wait on the kernel before, staging x), "
+                   "paid once per group of projections of the same x")
     return res
 
 

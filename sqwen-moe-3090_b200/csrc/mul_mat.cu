@@ -7,17 +7,15 @@
 // f32 / f16 / bf16.  Dequantised weights times x are summed in f32.  (ggml's CUDA
 // backend quantises x to q8_1 for its quantised dot products; this path does not.)
 //
-// At decode a projection is a stream of its weight bytes.  One CTA per SM walks a
-// contiguous range of row tiles; a tile (one shared-memory slot) holds up to 8
-// consecutive rows -- contiguous bytes of the tensor -- brought in by a 1-D bulk copy
-// (TMA, no multicast) on an mbarrier ring.  The ring is filled before the grid-
-// dependency wait: the weights are model constants, only x comes from the kernel
-// before.  Warp w takes row w of a tile; lane l takes the 32-value sub-block l % 8 of the
-// row's 256-value units l / 8, l / 8 + 4, ..., dequantises it from shared memory into
-// registers and multiplies it with the staged tokens (f32 in shared memory, 32-value
-// sub-blocks padded to 36 floats so that the 8 lanes of a unit read 8 different bank
-// groups).  q4_K's min term uses the per-sub-block sums of x.  The warp then reduces
-// its lanes by shuffles.  A call handles up to kMaxPassTokens tokens per stream of W.
+// At decode a projection is a stream of its weight bytes.  A launch serves a group of
+// projections of the same x (a layer's QG / K / V, or qkv / z / beta / alpha): their
+// row tiles form one list, and each CTA walks a contiguous range of it, so the fixed
+// cost of a launch (the wait on the kernel before, staging x) is paid once per group.
+// Tiles reach shared memory by bulk copies (TMA, no multicast) on an mbarrier ring that
+// is filled before the grid-dependency wait: the weights are model constants, only x
+// comes from the kernel before.  Quantised tiles go through the tensor cores
+// (mul_mat_tc_kernel), f32 / f16 / bf16 tiles through FMAs (mul_mat_kernel).  A pass
+// serves up to kMaxPassTokens tokens per stream of W.
 #include <math.h>
 
 #include "common.cuh"
@@ -30,46 +28,46 @@ constexpr int kMmWarps = 8;
 constexpr int kMmThreads = kMmWarps * 32;
 constexpr int kMaxIn = 4096;          // n_in limit (the model's 2048 and 4096)
 constexpr int kMaxPassTokens = 4;     // tokens per stream of W
-constexpr int kSubPad = 36;           // floats per staged 32-value sub-block
+constexpr int kSubPad = 36;           // floats per staged 32-value sub-block (FMA path)
 constexpr int kRingBudget = 96 * 1024;
 constexpr int kMaxStages = 8;
-constexpr int kSlotMax = 32 * 1024;   // bytes of one slot (<= 8 rows)
+constexpr int kSlotMax = 32 * 1024;   // bytes of one FMA-path slot (<= 8 rows)
+constexpr int kMaxSeg = SQMIX_MUL_MAT_MAX_GROUP;
+
+// one projection of a launch
+struct MmSeg {
+    const uint8_t *w;
+    float *y;          // this pass's first token
+    int64_t y_stride;
+    int w_type;
+    int row_bytes;
+    int sstride;       // bytes between rows in a slot
+    int rows;          // rows per tile
+    int n_out;
+    int tile0;         // first tile of the projection in the launch's tile list
+};
 
 struct MmParams {
-    const uint8_t *w;
-    int w_type;
-    int64_t row_bytes;
-    int n_in, n_out;
+    MmSeg seg[kMaxSeg];
+    int n_seg, n_tiles;
+    int n_in;
     const void *x;
     int x_dtype;
     int64_t x_stride;
-    int n_tok;  // tokens of this pass (<= NT)
-    float *y;
-    int64_t y_stride;
+    int n_tok;         // tokens of this pass (<= NT)
     uint32_t *status;
-    int rows_per_slot, n_stages, slot_bytes;
-    int sstride;  // bytes between rows in a slot (tensor-core path: padded against bank conflicts)
+    int n_stages, slot_bytes;
 };
+
+// the projection that tile t of the launch belongs to
+__device__ __forceinline__ int seg_of(const MmParams &p, int t) {
+    int s = 0;
+    while (s + 1 < p.n_seg && t >= p.seg[s + 1].tile0) ++s;
+    return s;
+}
 
 __device__ __forceinline__ float f16_at(const uint8_t *p) {
     return __half2float(*reinterpret_cast<const __half *>(p));
-}
-
-// 32 bytes from a 2-byte aligned shared-memory address as 8 words
-__device__ __forceinline__ void ld32b(const uint8_t *p, uint32_t (&w)[8]) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    if ((a & 3) == 0) {
-        const uint32_t *q = reinterpret_cast<const uint32_t *>(p);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) w[i] = q[i];
-    } else {
-        const uint32_t *q = reinterpret_cast<const uint32_t *>(p - 2);
-        uint32_t r[9];
-#pragma unroll
-        for (int i = 0; i < 9; ++i) r[i] = q[i];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) w[i] = __byte_perm(r[i], r[i + 1], 0x5432);
-    }
 }
 
 // Unit (256 values) bytes per format; 0: unsupported.
@@ -78,60 +76,11 @@ __host__ __device__ constexpr int unit_bytes(int t) {
            : (t == SQMIX_F16 || t == SQMIX_BF16) ? 512 : 0;
 }
 
-// The 32 values of sub-block j (0..7) of one 256-value unit at `u` (shared memory).
-// For q4_K the min term is returned separately: value = v[l] - mterm.
+// The 32 values of sub-block j (0..7) of one 256-value unit at `u` (shared memory) of
+// a float-typed row.
 template <int WT>
-__device__ __forceinline__ void dequant_sub(const uint8_t *u, int j, float (&v)[32], float &mterm) {
-    mterm = 0.f;
-    if constexpr (WT == SQMIX_Q4_K) {
-        const float d = f16_at(u), dmin = f16_at(u + 2);
-        const uint8_t *s = u + 4;
-        int sc, m;
-        if (j < 4) {
-            sc = s[j] & 63;
-            m = s[j + 4] & 63;
-        } else {
-            sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
-            m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
-        }
-        const float ds = d * static_cast<float>(sc);
-        mterm = dmin * static_cast<float>(m);
-        const uint4 *q4 = reinterpret_cast<const uint4 *>(u + 16 + 32 * (j >> 1));
-        const uint4 a = q4[0], b = q4[1];
-        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        const int sh = 4 * (j & 1);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) v[4 * i + e] = ds * static_cast<float>((w[i] >> (8 * e + sh)) & 0xF);
-    } else if constexpr (WT == SQMIX_Q6_K) {
-        const int half = j >> 2, k = j & 3;
-        uint32_t ql[8], qh[8];
-        ld32b(u + 64 * half + 32 * (k & 1), ql);
-        ld32b(u + 128 + 32 * half, qh);
-        const int8_t *sc = reinterpret_cast<const int8_t *>(u + 192 + 8 * half + 2 * k);
-        const float d = f16_at(u + 208);
-        const float d0 = d * static_cast<float>(sc[0]), d1 = d * static_cast<float>(sc[1]);
-        const int lsh = 4 * (k >> 1), hsh = 2 * k;
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int lo = (ql[i] >> (8 * e + lsh)) & 0xF;
-                const int hi = (qh[i] >> (8 * e + hsh)) & 3;
-                const float q = static_cast<float>((lo | (hi << 4)) - 32);
-                v[4 * i + e] = (i < 4 ? d0 : d1) * q;
-            }
-    } else if constexpr (WT == SQMIX_Q8_0) {
-        const uint8_t *b = u + 34 * j;
-        const float d = f16_at(b);
-        uint32_t w[8];
-        ld32b(b + 2, w);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) v[4 * i + e] = d * static_cast<float>(static_cast<int8_t>((w[i] >> (8 * e)) & 0xFF));
-    } else if constexpr (WT == SQMIX_F32) {
+__device__ __forceinline__ void dequant_sub(const uint8_t *u, int j, float (&v)[32]) {
+    if constexpr (WT == SQMIX_F32) {
         const float4 *f = reinterpret_cast<const float4 *>(u + 128 * j);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -161,8 +110,15 @@ __device__ __forceinline__ void dequant_sub(const uint8_t *u, int j, float (&v)[
     }
 }
 
-template <int WT, int NT>
-__global__ void __launch_bounds__(kMmThreads, 1) mul_mat_kernel(MmParams p) {
+// ---- f32 / f16 / bf16 weights: FMAs -----------------------------------------------
+// A tile (one shared-memory slot) holds up to 8 consecutive rows of one projection --
+// contiguous bytes of its tensor -- brought in by one 1-D bulk copy.  Warp w takes row w
+// of a tile; lane l takes the 32-value sub-block l % 8 of the row's 256-value units l / 8,
+// l / 8 + 4, ..., and multiplies it with the staged tokens (f32 in shared memory,
+// 32-value sub-blocks padded to 36 floats so that the 8 lanes of a unit read 8
+// different bank groups).  The warp then reduces its lanes by shuffles.
+template <int NT>
+__global__ void __launch_bounds__(kMmThreads, 1) mul_mat_kernel(const __grid_constant__ MmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int ring_bytes = p.n_stages * p.slot_bytes;
     const int n_sub = p.n_in / 32;
@@ -173,9 +129,8 @@ __global__ void __launch_bounds__(kMmThreads, 1) mul_mat_kernel(MmParams p) {
     int *rel_cnt = reinterpret_cast<int *>(empty_bar + kMaxStages);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    const int n_tiles_all = (p.n_out + p.rows_per_slot - 1) / p.rows_per_slot;
-    const int tile0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * n_tiles_all) / gridDim.x);
-    const int tile1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * n_tiles_all) / gridDim.x);
+    const int tile0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * p.n_tiles) / gridDim.x);
+    const int tile1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * p.n_tiles) / gridDim.x);
     const int n_tiles = tile1 - tile0;
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.n_stages; ++s) {
@@ -188,11 +143,12 @@ __global__ void __launch_bounds__(kMmThreads, 1) mul_mat_kernel(MmParams p) {
     __syncthreads();
     auto issue = [&](int it) {  // tile tile0 + it into slot it % n_stages
         const int s = it % p.n_stages;
-        const int row0 = (tile0 + it) * p.rows_per_slot;
-        const int rows = min(p.rows_per_slot, p.n_out - row0);
-        const uint32_t bytes = static_cast<uint32_t>(rows * p.row_bytes);
+        const MmSeg &sg = p.seg[seg_of(p, tile0 + it)];
+        const int row0 = (tile0 + it - sg.tile0) * sg.rows;
+        const int rows = min(sg.rows, sg.n_out - row0);
+        const uint32_t bytes = static_cast<uint32_t>(rows * sg.row_bytes);
         mbar_arrive_expect_tx(&full_bar[s], bytes);
-        bulk_g2s(smem + s * p.slot_bytes, p.w + static_cast<int64_t>(row0) * p.row_bytes, bytes, &full_bar[s]);
+        bulk_g2s(smem + s * p.slot_bytes, sg.w + static_cast<int64_t>(row0) * sg.row_bytes, bytes, &full_bar[s]);
     };
     // the weights are constants of the model: stream them before the dependency wait
     if (threadIdx.x == 0)
@@ -235,15 +191,22 @@ __global__ void __launch_bounds__(kMmThreads, 1) mul_mat_kernel(MmParams p) {
         const int s = it % p.n_stages;
         if (!mbar_wait(&full_bar[s], (it / p.n_stages) & 1)) ok = false;
         if (__any_sync(0xffffffffu, !ok)) break;
-        const int row = (tile0 + it) * p.rows_per_slot + warp;
-        if (warp < p.rows_per_slot && row < p.n_out) {
-            const uint8_t *wr = smem + s * p.slot_bytes + warp * p.row_bytes;
+        const MmSeg &sg = p.seg[seg_of(p, tile0 + it)];
+        const int row = (tile0 + it - sg.tile0) * sg.rows + warp;
+        if (warp < sg.rows && row < sg.n_out) {
+            const uint8_t *wr = smem + s * p.slot_bytes + warp * sg.row_bytes;
+            const int ub = unit_bytes(sg.w_type);
             float acc[NT];
 #pragma unroll
             for (int t = 0; t < NT; ++t) acc[t] = 0.f;
             for (int un = lane >> 3; un < n_units; un += 4) {
-                float v[32], mterm;
-                dequant_sub<WT>(wr + un * unit_bytes(WT), j, v, mterm);
+                float v[32];
+                if (sg.w_type == SQMIX_F32)
+                    dequant_sub<SQMIX_F32>(wr + un * ub, j, v);
+                else if (sg.w_type == SQMIX_F16)
+                    dequant_sub<SQMIX_F16>(wr + un * ub, j, v);
+                else
+                    dequant_sub<SQMIX_BF16>(wr + un * ub, j, v);
                 const int sb = 8 * un + j;
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
@@ -257,7 +220,6 @@ __global__ void __launch_bounds__(kMmThreads, 1) mul_mat_kernel(MmParams p) {
                         a = fmaf(v[4 * q + 2], x.z, a);
                         a = fmaf(v[4 * q + 3], x.w, a);
                     }
-                    if constexpr (WT == SQMIX_Q4_K) a = fmaf(-mterm, xsum[t * n_sub + sb], a);
                     acc[t] += a;
                 }
             }
@@ -268,7 +230,7 @@ __global__ void __launch_bounds__(kMmThreads, 1) mul_mat_kernel(MmParams p) {
             if (lane == 0)
 #pragma unroll
                 for (int t = 0; t < NT; ++t)
-                    if (t < p.n_tok) p.y[static_cast<int64_t>(t) * p.y_stride + row] = acc[t];
+                    if (t < p.n_tok) sg.y[static_cast<int64_t>(t) * sg.y_stride + row] = acc[t];
         }
         // release the slot; the warp that releases it last refills it
         __syncwarp();
@@ -300,24 +262,32 @@ __global__ void __launch_bounds__(kMmThreads, 1) mul_mat_kernel(MmParams p) {
 }
 
 // ---- quantised weights on the tensor cores ---------------------------------------
-// The quantised formats go through mma.m16n8k16 (f16 operands, f32 accumulators): a
-// tile is 16 weight rows (the M of the MMA); the 8 warps split the 256-value units of
-// the contraction (warp w: units w, w + 8, ...), each warp moving on to the next tile
-// as soon as it is done (a slot is refilled by the warp that releases it last), and the
-// partial sums of a group of kTcGroup tiles are reduced through shared memory in a
-// fixed order.  The A operand holds exact small integers read straight from the
-// GGUF bytes: q4_K nibbles and q6_K 6-bit values masked into f16 words as subnormals
-// (value q * 2^-24; high q4_K nibbles carry an extra x16), q8_0 bytes through
-// 0x6400 | (q + 128) - 1152.  The K order inside a 16-value slice follows the bytes:
-// lane c's 32-bit word holds values 4c .. 4c + 3, k-pairs (2c, 2c + 1) = values (4c,
-// 4c + 2) and (2c + 8, 2c + 9) = (4c + 1, 4c + 3); the B operand (x) uses the same
-// order.  x is split as x = hi + lo in f16, two MMAs per product, so every product and
-// sum is exact to f32 rounding (|x| < 65504).  Each (row, scale block) result is scaled
-// in f32: q4_K by d sc 2^24 (2^20 for high nibbles) per 32 values, minus dmin m sum(x);
-// q6_K by d sc 2^24 per 16 values, minus 32 d sc sum(x); q8_0 by d per 32 values.  The
-// 4 lanes of a row group compute a quarter of a unit's scales each and pass them round
-// by shuffles.
+// q8_0 / q4_K / q6_K tiles go through mma.m16n8k16 (f16 operands, f32 accumulators): a
+// tile is 16 weight rows of one projection (the M of the MMA), one bulk copy per row
+// into a slot whose rows lie sstride bytes apart (sstride / 4 = 4 mod 8: the 8 row
+// groups of a fragment load hit 8 different groups of 4 banks).  The 8 warps split the
+// 256-value units of the contraction (warp w: units w, w + 8, ...), each warp moving on
+// to the next tile as soon as it is done (a slot is refilled by the warp that releases
+// it last), and the partial sums of a group of kTcGroup tiles are reduced through
+// shared memory in a fixed order.
+//
+// The A operand holds exact small integers read straight from the GGUF bytes: q4_K
+// nibbles and q6_K 6-bit values masked into f16 words as subnormals (value q 2^-24;
+// high q4_K nibbles carry an extra x16), q8_0 bytes through 0x6400 | (q + 128) - 1152.
+// The K order inside a 16-value slice follows the bytes: lane c's 32-bit word holds
+// values 4c .. 4c + 3, k-pairs (2c, 2c + 1) = values (4c, 4c + 2) and (2c + 8, 2c + 9) =
+// (4c + 1, 4c + 3); the B operand uses the same order.  x is split as x = hi + lo in
+// f16, and the two halves are two columns of B (column 2t: token t's hi, 2t + 1: its
+// lo), so one MMA serves 4 tokens and lane c of a row group ends with token c's sum in
+// (d0 + d1, d2 + d3) for rows g, g + 8: every product and sum is exact to f32 rounding
+// (|x| < 65504).  Each (row, scale block) result is scaled in f32: q4_K by d sc 2^24
+// (2^20 for high nibbles) per 32 values, minus dmin m sum(x); q6_K by d sc 2^24 per 16
+// values, minus 32 d sc sum(x); q8_0 by d per 32 values.  A warp decodes a unit's scales
+// once into its table (the 4 lanes of a row group a quarter each) and reads them back as
+// broadcasts.
 constexpr int kTcRows = 16;
+constexpr int kTcGroup = 4;   // tiles whose partial sums are reduced together
+constexpr int kFsStride = 18; // floats per row of a warp's scale table (the 8 row groups: 8 bank pairs)
 
 __device__ __forceinline__ uint32_t nib_lo(uint32_t w) { return w & 0x000F000Fu; }
 __device__ __forceinline__ uint32_t nib_hi(uint32_t w) { return w & 0x00F000F0u; }
@@ -333,27 +303,187 @@ __device__ __forceinline__ uint32_t i8_pair(uint32_t wx, uint32_t sel) {
     const __half2 h = u32_as_h2(__byte_perm(wx, 0x64646464u, sel));
     return h2_as_u32(__hsub2(h, __float2half2_rn(1152.0f)));
 }
+// d = A B (+ 0): a pure function of its operands, free for the scheduler to move
+__device__ __forceinline__ void mma_f16_zero(float (&d)[4], const uint32_t (&a)[4], uint2 b) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "f"(0.f));
+}
+// d += A B
+__device__ __forceinline__ void mma_f16_acc(float (&d)[4], const uint32_t (&a)[4], uint2 b) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
+}
+// B fragment of 16-value slice sl for lane (g, c): column g = token g / 2, hi (g even) or
+// lo (g odd); columns of absent tokens are zero
+template <int NT>
+__device__ __forceinline__ uint2 bfrag_at(const uint2 *bf, int sl, int g, int c) {
+    return g < 2 * NT ? bf[(sl * 2 * NT + g) * 4 + c] : make_uint2(0u, 0u);
+}
 
-constexpr int kTcGroup = 4;  // tiles whose partial sums are reduced together
+// One 256-value unit u of rows g, g + 8 (rg, rg8: the rows in the slot), token c of this
+// lane: y0 / y1 += the unit's dot products.  fst: the warp's scale table [16][kFsStride].
+template <int NT>
+__device__ __forceinline__ void unit_q4k(const uint8_t *rg, const uint8_t *rg8, int u, int g, int c,
+                                         const uint2 *bf, const float *xs32, int n_sub, float *fst, float &y0,
+                                         float &y1) {
+    __syncwarp();  // the previous unit's table reads are done
+    // lane c: (d sc 2^24 or 2^20, dmin m) of sub-blocks 2c, 2c + 1 of rows g, g + 8; the
+    // 12 scale bytes as three words (a unit starts 16-byte aligned in the slot)
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        const uint8_t *b = (rr ? rg8 : rg) + u * 144;
+        const float d = f16_at(b), dmin = f16_at(b + 2);
+        const uint32_t s0 = *reinterpret_cast<const uint32_t *>(b + 4);
+        const uint32_t s1 = *reinterpret_cast<const uint32_t *>(b + 8);
+        const uint32_t s2 = *reinterpret_cast<const uint32_t *>(b + 12);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int j = 2 * c + q, sh = 8 * (j & 3);
+            const uint32_t b0 = (s0 >> sh) & 0xFF, b1 = (s1 >> sh) & 0xFF, b2 = (s2 >> sh) & 0xFF;
+            const uint32_t sc = j < 4 ? b0 & 63 : (b2 & 0xF) | ((b0 >> 6) << 4);
+            const uint32_t m = j < 4 ? b1 & 63 : (b2 >> 4) | ((b1 >> 6) << 4);
+            *reinterpret_cast<float2 *>(fst + (8 * rr + g) * kFsStride + 2 * j) =
+                make_float2(d * static_cast<float>(sc) * (q ? 1048576.0f : 16777216.0f), dmin * static_cast<float>(m));
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // 32 bytes: sub-blocks 2k (low nibbles), 2k + 1 (high)
+        float al[4], ah[4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int off = u * 144 + 16 + 32 * k + 16 * h + 4 * c;
+            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(rg + off);
+            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(rg8 + off);
+            const uint32_t w0s = w0 >> 8, w1s = w1 >> 8;
+            const uint32_t alo[4] = {nib_lo(w0), nib_lo(w1), nib_lo(w0s), nib_lo(w1s)};
+            const uint32_t ahi[4] = {nib_hi(w0), nib_hi(w1), nib_hi(w0s), nib_hi(w1s)};
+            const uint2 bl = bfrag_at<NT>(bf, 2 * (8 * u + 2 * k) + h, g, c);
+            const uint2 bh = bfrag_at<NT>(bf, 2 * (8 * u + 2 * k + 1) + h, g, c);
+            if (h == 0) {
+                mma_f16_zero(al, alo, bl);
+                mma_f16_zero(ah, ahi, bh);
+            } else {
+                mma_f16_acc(al, alo, bl);
+                mma_f16_acc(ah, ahi, bh);
+            }
+        }
+#pragma unroll
+        for (int sbk = 0; sbk < 2; ++sbk) {
+            const int j = 2 * k + sbk;
+            const float *a = sbk ? ah : al;
+            const float2 f0 = *reinterpret_cast<const float2 *>(fst + g * kFsStride + 2 * j);
+            const float2 f1 = *reinterpret_cast<const float2 *>(fst + (g + 8) * kFsStride + 2 * j);
+            const float xj = c < NT ? xs32[c * n_sub + 8 * u + j] : 0.f;
+            y0 = fmaf(f0.x, a[0] + a[1], fmaf(-f0.y, xj, y0));
+            y1 = fmaf(f1.x, a[2] + a[3], fmaf(-f1.y, xj, y1));
+        }
+    }
+}
 
-template <int WT, int NT>
-__global__ void __launch_bounds__(kMmThreads, 2) mul_mat_tc_kernel(MmParams p) {
+template <int NT>
+__device__ __forceinline__ void unit_q6k(const uint8_t *rg, const uint8_t *rg8, int u, int g, int c,
+                                         const uint2 *bf, const float *xs16, int n_sl, float *fst, float &y0,
+                                         float &y1) {
+    __syncwarp();
+    // lane c: d sc of slices 4c .. 4c + 3 of rows g, g + 8
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        const uint8_t *b = (rr ? rg8 : rg) + u * 210;
+        const float d = f16_at(b + 208);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            fst[(8 * rr + g) * kFsStride + 4 * c + q] = d * static_cast<float>(static_cast<int8_t>(b[192 + 4 * c + q]));
+    }
+    __syncwarp();
+#pragma unroll 4
+    for (int q = 0; q < 16; ++q) {  // 16-value slice q of the unit: one scale
+        const int hh = q >> 3, k = (q >> 1) & 3, h = q & 1;
+        const int offl = u * 210 + 64 * hh + 32 * (k & 1) + 16 * h + 4 * c;
+        const int offh = u * 210 + 128 + 32 * hh + 16 * h + 4 * c;
+        const uint32_t l0 = ld_u32_2a(rg + offl) >> (4 * (k >> 1));
+        const uint32_t l1 = ld_u32_2a(rg8 + offl) >> (4 * (k >> 1));
+        const uint32_t h0 = ld_u32_2a(rg + offh) >> (2 * k), h1 = ld_u32_2a(rg8 + offh) >> (2 * k);
+        const uint32_t av[4] = {(l0 & 0x000F000Fu) | ((h0 & 0x00030003u) << 4),
+                                (l1 & 0x000F000Fu) | ((h1 & 0x00030003u) << 4),
+                                ((l0 >> 8) & 0x000F000Fu) | (((h0 >> 8) & 0x00030003u) << 4),
+                                ((l1 >> 8) & 0x000F000Fu) | (((h1 >> 8) & 0x00030003u) << 4)};
+        float a[4];
+        mma_f16_zero(a, av, bfrag_at<NT>(bf, 16 * u + q, g, c));
+        const float d0 = fst[g * kFsStride + q], d1 = fst[(g + 8) * kFsStride + q];
+        const float xq = c < NT ? xs16[c * n_sl + 16 * u + q] : 0.f;
+        y0 = fmaf(d0 * 16777216.0f, a[0] + a[1], fmaf(-32.0f * d0, xq, y0));
+        y1 = fmaf(d1 * 16777216.0f, a[2] + a[3], fmaf(-32.0f * d1, xq, y1));
+    }
+}
+
+template <int NT>
+__device__ __forceinline__ void unit_q8_0(const uint8_t *rg, const uint8_t *rg8, int u, int g, int c,
+                                          const uint2 *bf, float *fst, float &y0, float &y1) {
+    __syncwarp();
+    // lane c: d of blocks 2c, 2c + 1 of rows g, g + 8
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+            fst[(8 * rr + g) * kFsStride + 2 * c + q] = f16_at((rr ? rg8 : rg) + u * 272 + 34 * (2 * c + q));
+    __syncwarp();
+#pragma unroll 2
+    for (int j = 0; j < 8; ++j) {  // block j of the unit: 32 values, one d
+        float a[4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int off = u * 272 + 34 * j + 2 + 16 * h + 4 * c;
+            const uint32_t w0 = ld_u32_2a(rg + off) ^ 0x80808080u;
+            const uint32_t w1 = ld_u32_2a(rg8 + off) ^ 0x80808080u;
+            const uint32_t av[4] = {i8_pair(w0, 0x4240u), i8_pair(w1, 0x4240u), i8_pair(w0, 0x4341u),
+                                    i8_pair(w1, 0x4341u)};
+            const uint2 b = bfrag_at<NT>(bf, 2 * (8 * u + j) + h, g, c);
+            if (h == 0)
+                mma_f16_zero(a, av, b);
+            else
+                mma_f16_acc(a, av, b);
+        }
+        y0 = fmaf(fst[g * kFsStride + j], a[0] + a[1], y0);
+        y1 = fmaf(fst[(g + 8) * kFsStride + j], a[2] + a[3], y1);
+    }
+}
+
+// shared memory of mul_mat_tc_kernel after its ring
+__host__ __device__ constexpr size_t tc_extra_bytes(int nt, int n_in) {
+    return static_cast<size_t>(n_in / 16) * 2 * nt * 4 * 8 +                 // B fragments
+           static_cast<size_t>(nt) * (n_in / 16 + 1) * 4 +                    // 16-value sums
+           static_cast<size_t>(nt) * (n_in / 32 + 1) * 4 +                    // 32-value sums
+           static_cast<size_t>(kMmWarps) * 16 * kFsStride * 4 +               // scale tables
+           static_cast<size_t>(kTcGroup) * kMmWarps * 32 * 8 +                // partial sums
+           2 * kMaxStages * sizeof(uint64_t) + kMaxStages * sizeof(int) + 16;  // barriers
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kMmThreads, 2) mul_mat_tc_kernel(const __grid_constant__ MmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int ring_bytes = p.n_stages * p.slot_bytes;
     const int n_units = p.n_in / 256;
-    const int n_sl = p.n_in / 16;                                       // 16-value slices
-    uint4 *bfrag = reinterpret_cast<uint4 *>(smem + ring_bytes);        // [n_sl][NT][4 lanes c]
-    float *xs16 = reinterpret_cast<float *>(bfrag + n_sl * NT * 4);     // [NT][n_sl] slice sums
-    float4 *red = reinterpret_cast<float4 *>(xs16 + NT * n_sl);         // [kTcGroup][8 warps][32 lanes]
+    const int n_sl = p.n_in / 16, n_sub = p.n_in / 32;
+    const int xs16_st = n_sl + 1, xs32_st = n_sub + 1;  // token rows one bank apart
+    uint2 *bf = reinterpret_cast<uint2 *>(smem + ring_bytes);                  // [n_sl][2 NT][4 lanes c]
+    float *xs16 = reinterpret_cast<float *>(bf + n_sl * 2 * NT * 4);          // [NT][xs16_st]
+    float *xs32 = xs16 + NT * xs16_st;                                         // [NT][xs32_st]
+    float *fst_all = xs32 + NT * xs32_st;                                      // [8 warps][16][kFsStride]
+    float2 *red = reinterpret_cast<float2 *>(fst_all + kMmWarps * 16 * kFsStride);  // [kTcGroup][8][32]
     uint64_t *full_bar = reinterpret_cast<uint64_t *>(red + kTcGroup * kMmWarps * 32);
     uint64_t *empty_bar = full_bar + kMaxStages;
     int *rel_cnt = reinterpret_cast<int *>(empty_bar + kMaxStages);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
+    float *fst = fst_all + warp * 16 * kFsStride;
 
-    const int n_tiles_all = (p.n_out + kTcRows - 1) / kTcRows;
-    const int tile0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * n_tiles_all) / gridDim.x);
-    const int tile1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * n_tiles_all) / gridDim.x);
+    const int tile0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * p.n_tiles) / gridDim.x);
+    const int tile1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * p.n_tiles) / gridDim.x);
     const int n_tiles = tile1 - tile0;
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.n_stages; ++s) {
@@ -364,83 +494,65 @@ __global__ void __launch_bounds__(kMmThreads, 2) mul_mat_tc_kernel(MmParams p) {
         fence_mbar_init();
     }
     __syncthreads();
-    // one bulk copy per row: rows land sstride bytes apart, sstride / 4 = 4 mod 8, so the
-    // 8 row groups g of a fragment load hit 8 different groups of 4 banks
+    // one bulk copy per row, the lanes of one warp issuing a tile's rows together
     auto issue = [&](int it) {
         const int s = it % p.n_stages;
-        const int row0 = (tile0 + it) * kTcRows;
-        const int rows = min(kTcRows, p.n_out - row0);
-        mbar_arrive_expect_tx(&full_bar[s], static_cast<uint32_t>(rows * p.row_bytes));
-        for (int r = 0; r < rows; ++r)
-            bulk_g2s(smem + s * p.slot_bytes + r * p.sstride, p.w + static_cast<int64_t>(row0 + r) * p.row_bytes,
-                     static_cast<uint32_t>(p.row_bytes), &full_bar[s]);
+        const MmSeg &sg = p.seg[seg_of(p, tile0 + it)];
+        const int row0 = (tile0 + it - sg.tile0) * kTcRows;
+        const int rows = min(kTcRows, sg.n_out - row0);
+        if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], static_cast<uint32_t>(rows * sg.row_bytes));
+        __syncwarp();
+        if (lane < rows)
+            bulk_g2s(smem + s * p.slot_bytes + lane * sg.sstride, sg.w + static_cast<int64_t>(row0 + lane) * sg.row_bytes,
+                     static_cast<uint32_t>(sg.row_bytes), &full_bar[s]);
     };
     // the weights are constants of the model: stream them before the dependency wait
-    if (threadIdx.x == 0)
+    if (warp == 0)
         for (int it = 0; it < n_tiles && it < p.n_stages; ++it) issue(it);
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" :::);
 
-    // x -> B fragments (f16 hi / lo pairs in the K order above) and 16-value slice sums;
-    // entry idx = (slice, token, lane c) covers x values 16 slice + 4 c .. + 3, the loads
-    // of kXBatch strides in flight together (the entry count is a multiple of 64, so a
-    // warp's 32 entries are all in range or all out)
-    constexpr int kXBatch = 4;
-    const int n_ent = n_sl * NT * 4;
-    for (int base = threadIdx.x; base < n_ent; base += kMmThreads * kXBatch) {
-        float v[kXBatch][4];
+    // x -> the B fragments and slice sums of this warp's units (no other warp reads them):
+    // entry (slice l of unit u, token t, lane c) covers x values 16 (16 u + l) + 4 c .. + 3
+    for (int u = warp; u < n_units; u += kMmWarps) {
+        constexpr int kE = 2 * NT;  // 64 NT entries per unit
+        float v[kE][4];
 #pragma unroll
-        for (int bb = 0; bb < kXBatch; ++bb) {
-            const int idx = base + bb * kMmThreads;
-            const int t = (idx >> 2) % NT, sl = (idx >> 2) / NT, cc = idx & 3;
+        for (int e = 0; e < kE; ++e) {
+            const int idx = e * 32 + lane;
+            const int t = (idx >> 2) % NT, sl = 16 * u + (idx >> 2) / NT;
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-                v[bb][e] = idx < n_ent && t < p.n_tok
-                               ? load_act(p.x, static_cast<int64_t>(t) * p.x_stride + 16 * sl + 4 * cc + e, p.x_dtype)
-                               : 0.f;
+            for (int q = 0; q < 4; ++q)
+                v[e][q] = t < p.n_tok ? load_act(p.x, static_cast<int64_t>(t) * p.x_stride + 16 * sl + 4 * c + q, p.x_dtype)
+                                      : 0.f;
         }
 #pragma unroll
-        for (int bb = 0; bb < kXBatch; ++bb) {
-            const int idx = base + bb * kMmThreads;
-            if ((idx & ~31) < n_ent) {  // the warp's first entry: warps are wholly in or out
-                const int t = (idx >> 2) % NT, sl = (idx >> 2) / NT, cc = idx & 3;
-                __half hv[4], lv[4];
+        for (int e = 0; e < kE; ++e) {
+            const int idx = e * 32 + lane;
+            const int t = (idx >> 2) % NT, sl = 16 * u + (idx >> 2) / NT;
+            __half hv[4], lv[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    hv[e] = __float2half_rn(v[bb][e]);
-                    lv[e] = __float2half_rn(v[bb][e] - __half2float(hv[e]));
-                }
-                bfrag[idx] = make_uint4(h2_as_u32(__halves2half2(hv[0], hv[2])), h2_as_u32(__halves2half2(hv[1], hv[3])),
-                                        h2_as_u32(__halves2half2(lv[0], lv[2])), h2_as_u32(__halves2half2(lv[1], lv[3])));
-                float sum = (v[bb][0] + v[bb][1]) + (v[bb][2] + v[bb][3]);  // lanes c of a slice are consecutive
-                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-                if (cc == 0) xs16[t * n_sl + sl] = sum;
+            for (int q = 0; q < 4; ++q) {
+                hv[q] = __float2half_rn(v[e][q]);
+                lv[q] = __float2half_rn(v[e][q] - __half2float(hv[q]));
             }
+            bf[(sl * 2 * NT + 2 * t) * 4 + c] =
+                make_uint2(h2_as_u32(__halves2half2(hv[0], hv[2])), h2_as_u32(__halves2half2(hv[1], hv[3])));
+            bf[(sl * 2 * NT + 2 * t + 1) * 4 + c] =
+                make_uint2(h2_as_u32(__halves2half2(lv[0], lv[2])), h2_as_u32(__halves2half2(lv[1], lv[3])));
+            float sum = (v[e][0] + v[e][1]) + (v[e][2] + v[e][3]);  // lanes c of a slice are consecutive
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            if (c == 0) xs16[t * xs16_st + sl] = sum;
+        }
+        __syncwarp();
+        if (lane < 8 * NT) {
+            const int t = lane >> 3, j = lane & 7;
+            const float *s16 = xs16 + t * xs16_st + 16 * u + 2 * j;
+            xs32[t * xs32_st + 8 * u + j] = s16[0] + s16[1];
         }
     }
-    __syncthreads();
-
-    // this lane's B fragment of slice sl (zero for token columns g >= NT)
-    auto bload = [&](int sl, uint32_t (&bh)[2], uint32_t (&bl)[2]) {
-        if (g < NT) {
-            const uint4 b = bfrag[(sl * NT + g) * 4 + c];
-            bh[0] = b.x;
-            bh[1] = b.y;
-            bl[0] = b.z;
-            bl[1] = b.w;
-        } else {
-            bh[0] = bh[1] = bl[0] = bl[1] = 0u;
-        }
-    };
-    // sum of x over slices [sl0, sl0 + n) for the token columns 2c, 2c + 1
-    auto xsum2 = [&](int sl0, int n, float &s0, float &s1) {
-        s0 = s1 = 0.f;
-        for (int i = 0; i < n; ++i) {
-            if (2 * c < NT) s0 += xs16[(2 * c) * n_sl + sl0 + i];
-            if (2 * c + 1 < NT) s1 += xs16[(2 * c + 1) * n_sl + sl0 + i];
-        }
-    };
+    __syncwarp();
 
     bool ok = true;
     for (int gb = 0; gb < n_tiles && ok; gb += kTcGroup) {
@@ -452,171 +564,57 @@ __global__ void __launch_bounds__(kMmThreads, 2) mul_mat_tc_kernel(MmParams p) {
                 ok = false;
                 break;
             }
-            const uint8_t *rg = smem + s * p.slot_bytes + g * p.sstride;
-            const uint8_t *rg8 = rg + 8 * p.sstride;
-            float y[4] = {0.f, 0.f, 0.f, 0.f};
+            const MmSeg &sg = p.seg[seg_of(p, tile0 + it)];
+            const uint8_t *rg = smem + s * p.slot_bytes + g * sg.sstride;
+            const uint8_t *rg8 = rg + 8 * sg.sstride;
+            const int wt = sg.w_type;
+            float y0 = 0.f, y1 = 0.f;
             for (int u = warp; u < n_units; u += kMmWarps) {
-                if constexpr (WT == SQMIX_Q4_K) {
-                    // lane c: (d sc 2^24 or 2^20, dmin m) of sub-blocks 2c, 2c + 1 of rows g, g + 8
-                    float2 fs[2][2];
-#pragma unroll
-                    for (int rr = 0; rr < 2; ++rr) {
-                        const uint8_t *b = (rr ? rg8 : rg) + u * 144;
-                        const float d = f16_at(b), dmin = f16_at(b + 2);
-                        const uint8_t *sb = b + 4;
-#pragma unroll
-                        for (int q = 0; q < 2; ++q) {
-                            const int j = 2 * c + q;
-                            int sc, m;
-                            if (j < 4) {
-                                sc = sb[j] & 63;
-                                m = sb[j + 4] & 63;
-                            } else {
-                                sc = (sb[j + 4] & 0xF) | ((sb[j - 4] >> 6) << 4);
-                                m = (sb[j + 4] >> 4) | ((sb[j] >> 6) << 4);
-                            }
-                            fs[rr][q] = make_float2(d * static_cast<float>(sc) * (q ? 1048576.0f : 16777216.0f),
-                                                    dmin * static_cast<float>(m));
-                        }
-                    }
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {  // 32 bytes: sub-blocks 2k (low nibbles), 2k + 1 (high)
-                        float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int off = u * 144 + 16 + 32 * k + 16 * h + 4 * c;
-                            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(rg + off);
-                            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(rg8 + off);
-                            const uint32_t alo[4] = {nib_lo(w0), nib_lo(w1), nib_lo(w0 >> 8), nib_lo(w1 >> 8)};
-                            const uint32_t ahi[4] = {nib_hi(w0), nib_hi(w1), nib_hi(w0 >> 8), nib_hi(w1 >> 8)};
-                            uint32_t bh[2], bl[2];
-                            bload(2 * (8 * u + 2 * k) + h, bh, bl);
-                            mma_f16_16816(a0, alo, bh[0], bh[1], a0);
-                            mma_f16_16816(a0, alo, bl[0], bl[1], a0);
-                            bload(2 * (8 * u + 2 * k + 1) + h, bh, bl);
-                            mma_f16_16816(a1, ahi, bh[0], bh[1], a1);
-                            mma_f16_16816(a1, ahi, bl[0], bl[1], a1);
-                        }
-#pragma unroll
-                        for (int sbk = 0; sbk < 2; ++sbk) {  // sub-block 2k + sbk: lane 4 g' + k holds it
-                            const int sub = 8 * u + 2 * k + sbk;
-                            const float *a = sbk ? a1 : a0;
-                            const int src = 4 * g + k;
-                            const float f0x = __shfl_sync(0xffffffffu, fs[0][sbk].x, src);
-                            const float f0y = __shfl_sync(0xffffffffu, fs[0][sbk].y, src);
-                            const float f1x = __shfl_sync(0xffffffffu, fs[1][sbk].x, src);
-                            const float f1y = __shfl_sync(0xffffffffu, fs[1][sbk].y, src);
-                            float x0, x1;
-                            xsum2(2 * sub, 2, x0, x1);
-                            y[0] = fmaf(f0x, a[0], fmaf(-f0y, x0, y[0]));
-                            y[1] = fmaf(f0x, a[1], fmaf(-f0y, x1, y[1]));
-                            y[2] = fmaf(f1x, a[2], fmaf(-f1y, x0, y[2]));
-                            y[3] = fmaf(f1x, a[3], fmaf(-f1y, x1, y[3]));
-                        }
-                    }
-                } else if constexpr (WT == SQMIX_Q6_K) {
-                    // lane c: d sc of slices 4c .. 4c + 3 of rows g, g + 8
-                    float ds[2][4];
-#pragma unroll
-                    for (int rr = 0; rr < 2; ++rr) {
-                        const uint8_t *b = (rr ? rg8 : rg) + u * 210;
-                        const float d = f16_at(b + 208);
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) ds[rr][q] = d * static_cast<float>(static_cast<int8_t>(b[192 + 4 * c + q]));
-                    }
-#pragma unroll 4
-                    for (int q = 0; q < 16; ++q) {  // 16-value slice q of the unit: one scale
-                        const int hh = q >> 3, k = (q >> 1) & 3, h = q & 1;
-                        const int offl = u * 210 + 64 * hh + 32 * (k & 1) + 16 * h + 4 * c;
-                        const int offh = u * 210 + 128 + 32 * hh + 16 * h + 4 * c;
-                        const uint32_t l0 = ld_u32_2a(rg + offl) >> (4 * (k >> 1));
-                        const uint32_t l1 = ld_u32_2a(rg8 + offl) >> (4 * (k >> 1));
-                        const uint32_t h0 = ld_u32_2a(rg + offh) >> (2 * k), h1 = ld_u32_2a(rg8 + offh) >> (2 * k);
-                        const uint32_t av[4] = {(l0 & 0x000F000Fu) | ((h0 & 0x00030003u) << 4),
-                                                (l1 & 0x000F000Fu) | ((h1 & 0x00030003u) << 4),
-                                                ((l0 >> 8) & 0x000F000Fu) | (((h0 >> 8) & 0x00030003u) << 4),
-                                                ((l1 >> 8) & 0x000F000Fu) | (((h1 >> 8) & 0x00030003u) << 4)};
-                        float a[4] = {0.f, 0.f, 0.f, 0.f};
-                        uint32_t bh[2], bl[2];
-                        bload(16 * u + q, bh, bl);
-                        mma_f16_16816(a, av, bh[0], bh[1], a);
-                        mma_f16_16816(a, av, bl[0], bl[1], a);
-                        const int src = 4 * g + (q >> 2);
-                        const float d0 = __shfl_sync(0xffffffffu, ds[0][q & 3], src);
-                        const float d1 = __shfl_sync(0xffffffffu, ds[1][q & 3], src);
-                        float x0, x1;
-                        xsum2(16 * u + q, 1, x0, x1);
-                        y[0] = fmaf(d0 * 16777216.0f, a[0], fmaf(-32.0f * d0, x0, y[0]));
-                        y[1] = fmaf(d0 * 16777216.0f, a[1], fmaf(-32.0f * d0, x1, y[1]));
-                        y[2] = fmaf(d1 * 16777216.0f, a[2], fmaf(-32.0f * d1, x0, y[2]));
-                        y[3] = fmaf(d1 * 16777216.0f, a[3], fmaf(-32.0f * d1, x1, y[3]));
-                    }
-                } else {  // q8_0
-                    // lane c: d of blocks 2c, 2c + 1 of rows g, g + 8
-                    float dd[2][2];
-#pragma unroll
-                    for (int rr = 0; rr < 2; ++rr)
-#pragma unroll
-                        for (int q = 0; q < 2; ++q) dd[rr][q] = f16_at((rr ? rg8 : rg) + u * 272 + 34 * (2 * c + q));
-#pragma unroll 2
-                    for (int j = 0; j < 8; ++j) {  // block j of the unit: 32 values, one d
-                        float a[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int off = u * 272 + 34 * j + 2 + 16 * h + 4 * c;
-                            const uint32_t w0 = ld_u32_2a(rg + off) ^ 0x80808080u;
-                            const uint32_t w1 = ld_u32_2a(rg8 + off) ^ 0x80808080u;
-                            const uint32_t av[4] = {i8_pair(w0, 0x4240u), i8_pair(w1, 0x4240u), i8_pair(w0, 0x4341u),
-                                                    i8_pair(w1, 0x4341u)};
-                            uint32_t bh[2], bl[2];
-                            bload(2 * (8 * u + j) + h, bh, bl);
-                            mma_f16_16816(a, av, bh[0], bh[1], a);
-                            mma_f16_16816(a, av, bl[0], bl[1], a);
-                        }
-                        const int src = 4 * g + (j >> 1);
-                        const float d0 = __shfl_sync(0xffffffffu, dd[0][j & 1], src);
-                        const float d1 = __shfl_sync(0xffffffffu, dd[1][j & 1], src);
-                        y[0] = fmaf(d0, a[0], y[0]);
-                        y[1] = fmaf(d0, a[1], y[1]);
-                        y[2] = fmaf(d1, a[2], y[2]);
-                        y[3] = fmaf(d1, a[3], y[3]);
-                    }
-                }
+                if (wt == SQMIX_Q4_K)
+                    unit_q4k<NT>(rg, rg8, u, g, c, bf, xs32, xs32_st, fst, y0, y1);
+                else if (wt == SQMIX_Q6_K)
+                    unit_q6k<NT>(rg, rg8, u, g, c, bf, xs16, xs16_st, fst, y0, y1);
+                else
+                    unit_q8_0<NT>(rg, rg8, u, g, c, bf, fst, y0, y1);
             }
-            red[((it - gb) * kMmWarps + warp) * 32 + lane] = make_float4(y[0], y[1], y[2], y[3]);
+            red[((it - gb) * kMmWarps + warp) * 32 + lane] = make_float2(y0, y1);
             // release the slot; the warp that releases it last refills it
             __syncwarp();
+            int last = 0;
             if (lane == 0) {
                 mbar_arrive(&empty_bar[s]);
-                if (atomicAdd(&rel_cnt[s], 1) == kMmWarps - 1) {
-                    rel_cnt[s] = 0;
-                    if (it + p.n_stages < n_tiles) {
-                        // every warp has arrived: this wait returns at once
-                        if (mbar_wait(&empty_bar[s], (it / p.n_stages) & 1))
-                            issue(it + p.n_stages);
-                        else
-                            ok = false;
-                    }
-                }
+                last = atomicAdd(&rel_cnt[s], 1) == kMmWarps - 1;
+                if (last) rel_cnt[s] = 0;
             }
-            ok = __shfl_sync(0xffffffffu, ok, 0);
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last && it + p.n_stages < n_tiles) {
+                // every warp has arrived: this wait returns at once
+                int e_ok = 1;
+                if (lane == 0) e_ok = mbar_wait(&empty_bar[s], (it / p.n_stages) & 1);
+                if (__shfl_sync(0xffffffffu, e_ok, 0))
+                    issue(it + p.n_stages);
+                else
+                    ok = false;
+            }
         }
         if (__syncthreads_or(!ok)) {
             ok = false;
             break;
         }
-        // the group's outputs (tile, row r, token n): lane 4 (r % 8) + n / 2, register 2 (r / 8) + n % 2
+        // the group's outputs (tile, row r, token n): lane 4 (r % 8) + n, component r / 8
         for (int o = threadIdx.x; o < (ge - gb) * kTcRows * NT; o += kMmThreads) {
             const int tl = o / (kTcRows * NT), rem = o % (kTcRows * NT), r = rem / NT, n = rem % NT;
-            const int ln = 4 * (r & 7) + (n >> 1), reg = 2 * (r >> 3) + (n & 1);
+            const int ln = 4 * (r & 7) + n;
             float acc = 0.f;
 #pragma unroll
             for (int wv = 0; wv < kMmWarps; ++wv) {
-                const float4 q4 = red[(tl * kMmWarps + wv) * 32 + ln];
-                acc += reg == 0 ? q4.x : reg == 1 ? q4.y : reg == 2 ? q4.z : q4.w;
+                const float2 q2 = red[(tl * kMmWarps + wv) * 32 + ln];
+                acc += r < 8 ? q2.x : q2.y;
             }
-            const int row = (tile0 + gb + tl) * kTcRows + r;
-            if (row < p.n_out && n < p.n_tok) p.y[static_cast<int64_t>(n) * p.y_stride + row] = acc;
+            const int t = tile0 + gb + tl;
+            const MmSeg &sg = p.seg[seg_of(p, t)];
+            const int row = (t - sg.tile0) * kTcRows + r;
+            if (row < sg.n_out && n < p.n_tok) sg.y[static_cast<int64_t>(n) * sg.y_stride + row] = acc;
         }
         __syncthreads();  // the partial sums' space is reused by the next group
     }
@@ -631,31 +629,9 @@ __global__ void __launch_bounds__(kMmThreads, 2) mul_mat_tc_kernel(MmParams p) {
     }
 }
 
-template <int WT, int NT>
-int launch_mm_tc(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
-    auto kernel = mul_mat_tc_kernel<WT, NT>;
-    static std::atomic<uint64_t> attr_devices{0};
-    {
-        const cudaError_t e = set_smem_once(attr_devices, kernel, 227 * 1024);
-        if (e != cudaSuccess) return cuda_status(e, "mul_mat smem attribute");
-    }
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kMmThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cuda_status(cudaLaunchKernelEx(&cfg, kernel, p), "mul_mat launch");
-}
-
-template <int WT, int NT>
-int launch_mm(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
-    auto kernel = mul_mat_kernel<WT, NT>;
-    static std::atomic<uint64_t> attr_devices{0};
+template <typename K>
+int launch_pdl(K kernel, std::atomic<uint64_t> &attr_devices, const MmParams &p, int grid, size_t smem,
+               cudaStream_t st) {
     {
         const cudaError_t e = set_smem_once(attr_devices, kernel, 227 * 1024);
         if (e != cudaSuccess) return cuda_status(e, "mul_mat smem attribute");
@@ -674,21 +650,45 @@ int launch_mm(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
 }
 
 template <int NT>
-int launch_mm_tc_type(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
-    switch (p.w_type) {
-        case SQMIX_Q4_K: return launch_mm_tc<SQMIX_Q4_K, NT>(p, grid, smem, st);
-        case SQMIX_Q6_K: return launch_mm_tc<SQMIX_Q6_K, NT>(p, grid, smem, st);
-        default: return launch_mm_tc<SQMIX_Q8_0, NT>(p, grid, smem, st);
-    }
+int launch_tc(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
+    static std::atomic<uint64_t> attr_devices{0};
+    return launch_pdl(mul_mat_tc_kernel<NT>, attr_devices, p, grid, smem, st);
 }
 
 template <int NT>
-int launch_mm_type(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
-    switch (p.w_type) {
-        case SQMIX_F32: return launch_mm<SQMIX_F32, NT>(p, grid, smem, st);
-        case SQMIX_F16: return launch_mm<SQMIX_F16, NT>(p, grid, smem, st);
-        default: return launch_mm<SQMIX_BF16, NT>(p, grid, smem, st);
-    }
+int launch_fma(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
+    static std::atomic<uint64_t> attr_devices{0};
+    return launch_pdl(mul_mat_kernel<NT>, attr_devices, p, grid, smem, st);
+}
+
+bool tc_type(int t) { return t == SQMIX_Q4_K || t == SQMIX_Q6_K || t == SQMIX_Q8_0; }
+
+int64_t row_bytes_of(int32_t w_type, int64_t n_in) {
+    const int ub = unit_bytes(w_type);
+    if (ub == 0 || n_in <= 0 || n_in % 256 != 0) return 0;
+    return n_in / 256 * ub;
+}
+
+int check_entry(const sqmix_mul_mat_args *a, int i) {
+    SQMIX_CHECK_ARG(a->w && a->x && a->y, "mul_mat[%d]: null pointer argument", i);
+    SQMIX_CHECK_ARG(unit_bytes(a->w_type) != 0, "mul_mat[%d]: weight type %d (q8_0, q4_K, q6_K, f32, f16, bf16)", i,
+                    a->w_type);
+    SQMIX_CHECK_ARG(a->n_in >= 256 && a->n_in <= kMaxIn && a->n_in % 256 == 0,
+                    "mul_mat[%d]: n_in=%lld must be a multiple of 256 in [256, %d]", i, (long long)a->n_in, kMaxIn);
+    SQMIX_CHECK_ARG(a->n_out >= 1 && a->n_out <= (1 << 24), "mul_mat[%d]: n_out=%lld", i, (long long)a->n_out);
+    SQMIX_CHECK_ARG(a->n_tokens >= 1, "mul_mat[%d]: n_tokens=%d", i, a->n_tokens);
+    SQMIX_CHECK_ARG(a->x_dtype == SQMIX_F32 || a->x_dtype == SQMIX_F16 || a->x_dtype == SQMIX_BF16,
+                    "mul_mat[%d]: x dtype %d", i, a->x_dtype);
+    const int64_t rb = row_bytes_of(a->w_type, a->n_in);
+    SQMIX_CHECK_ARG(a->w_row_bytes == rb, "mul_mat[%d]: w_row_bytes=%lld, rows must be contiguous (%lld bytes)", i,
+                    (long long)a->w_row_bytes, (long long)rb);
+    // rows reach shared memory by 1-D bulk copies: 16-byte multiples (q6_K: n_in % 2048 == 0)
+    SQMIX_CHECK_ARG(rb % 16 == 0,
+                    "mul_mat[%d]: a row of %lld bytes is not a multiple of 16 (q6_K needs n_in %% 2048 == 0)", i,
+                    (long long)rb);
+    SQMIX_CHECK_ARG((reinterpret_cast<uintptr_t>(a->w) & 15) == 0, "mul_mat[%d]: w must be 16-byte aligned", i);
+    SQMIX_CHECK_ARG(a->x_stride >= a->n_in && a->y_stride >= a->n_out, "mul_mat[%d]: token strides too small", i);
+    return SQMIX_OK;
 }
 
 }  // namespace
@@ -696,91 +696,108 @@ int launch_mm_type(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
 
 using namespace sqmix;
 
-extern "C" int64_t sqmix_mul_mat_row_bytes(int32_t w_type, int64_t n_in) {
-    const int ub = unit_bytes(w_type);
-    if (ub == 0 || n_in <= 0 || n_in % 256 != 0) return 0;
-    return n_in / 256 * ub;
+extern "C" int64_t sqmix_mul_mat_row_bytes(int32_t w_type, int64_t n_in) { return row_bytes_of(w_type, n_in); }
+
+extern "C" int sqmix_mul_mat_group(const sqmix_mul_mat_args *args, int32_t n, sqmix_stream_t stream) {
+    SQMIX_CHECK_ARG(args != nullptr, "mul_mat: null args");
+    SQMIX_CHECK_ARG(n >= 1 && n <= SQMIX_MUL_MAT_MAX_GROUP, "mul_mat_group: n=%d must be in [1, %d]", n,
+                    SQMIX_MUL_MAT_MAX_GROUP);
+    for (int i = 0; i < n; ++i) {
+        const int rc = check_entry(&args[i], i);
+        if (rc != SQMIX_OK) return rc;
+    }
+    const sqmix_mul_mat_args &a0 = args[0];
+    for (int i = 1; i < n; ++i)
+        SQMIX_CHECK_ARG(args[i].x == a0.x && args[i].x_dtype == a0.x_dtype && args[i].x_stride == a0.x_stride &&
+                            args[i].n_tokens == a0.n_tokens && args[i].n_in == a0.n_in,
+                        "mul_mat_group: entry %d does not share x (pointer, dtype, stride, n_tokens, n_in) with entry 0",
+                        i);
+    // the launch's projections: quantised ones on the tensor cores, float ones on FMAs
+    MmParams tc = {}, fm = {};
+    int tc_idx[kMaxSeg], fm_idx[kMaxSeg];
+    int max_sstride = 0, max_fm_slot = 0;
+    for (int i = 0; i < n; ++i) {
+        const int64_t rb = row_bytes_of(args[i].w_type, args[i].n_in);
+        MmParams &p = tc_type(args[i].w_type) ? tc : fm;
+        MmSeg &sg = p.seg[p.n_seg];
+        sg.w = static_cast<const uint8_t *>(args[i].w);
+        sg.y_stride = args[i].y_stride;
+        sg.w_type = args[i].w_type;
+        sg.row_bytes = static_cast<int>(rb);
+        sg.n_out = static_cast<int>(args[i].n_out);
+        sg.tile0 = p.n_tiles;
+        if (&p == &tc) {
+            sg.rows = kTcRows;
+            sg.sstride = static_cast<int>((rb / 4) % 8 == 0 ? rb + 16 : rb);  // rb / 4 is 0 or 4 mod 8
+            max_sstride = std::max(max_sstride, sg.sstride);
+            tc_idx[p.n_seg] = i;
+        } else {
+            sg.rows = static_cast<int>(std::min<int64_t>(kMmWarps, std::max<int64_t>(1, kSlotMax / rb)));
+            sg.sstride = sg.row_bytes;
+            max_fm_slot = std::max(max_fm_slot, sg.rows * sg.row_bytes);
+            fm_idx[p.n_seg] = i;
+        }
+        p.n_tiles += (sg.n_out + sg.rows - 1) / sg.rows;
+        ++p.n_seg;
+    }
+    const int sms = sqmix_device_sm_count(-1);
+    if (sms <= 0) return cuda_status(cudaErrorInvalidDevice, "mul_mat device");
+    for (MmParams *pp : {&tc, &fm}) {
+        pp->n_in = static_cast<int>(a0.n_in);
+        pp->x_dtype = a0.x_dtype;
+        pp->x_stride = a0.x_stride;
+        pp->status = a0.status;
+    }
+    tc.slot_bytes = (kTcRows * max_sstride + 127) / 128 * 128;
+    fm.slot_bytes = (max_fm_slot + 127) / 128 * 128;
+    constexpr size_t kSmemMax = 227 * 1024;
+    // two CTAs per SM when a ring of at least 2 slots fits beside the rest (more warps to
+    // hide the latency of the dequant / MMA chains), else one
+    constexpr size_t kSmemHalf = 113 * 1024 - 1024;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int elt = a0.x_dtype == SQMIX_F32 ? 4 : 2;
+    for (int t0 = 0; t0 < a0.n_tokens; t0 += kMaxPassTokens) {
+        const int nt = std::min(kMaxPassTokens, a0.n_tokens - t0);
+        const int NT = nt <= 1 ? 1 : nt <= 2 ? 2 : 4;
+        const void *xp = static_cast<const uint8_t *>(a0.x) + static_cast<int64_t>(t0) * a0.x_stride * elt;
+        if (tc.n_seg > 0) {
+            MmParams q = tc;
+            q.x = xp;
+            q.n_tok = nt;
+            for (int s = 0; s < q.n_seg; ++s) q.seg[s].y = args[tc_idx[s]].y + static_cast<int64_t>(t0) * q.seg[s].y_stride;
+            const size_t extra = tc_extra_bytes(NT, q.n_in);
+            const size_t budget = extra + 2 * static_cast<size_t>(q.slot_bytes) <= kSmemHalf ? kSmemHalf : kSmemMax;
+            if (extra + 2 * static_cast<size_t>(q.slot_bytes) > budget)
+                return cuda_status(cudaErrorInvalidValue, "mul_mat shared memory");
+            q.n_stages = static_cast<int>(std::min<size_t>(kMaxStages, (budget - extra) / q.slot_bytes));
+            const size_t smem = static_cast<size_t>(q.n_stages) * q.slot_bytes + extra;
+            const int grid = std::min(q.n_tiles, (budget == kSmemHalf ? 2 : 1) * sms);
+            const int rc = NT == 1 ? launch_tc<1>(q, grid, smem, st)
+                           : NT == 2 ? launch_tc<2>(q, grid, smem, st)
+                                     : launch_tc<4>(q, grid, smem, st);
+            if (rc != SQMIX_OK) return rc;
+        }
+        if (fm.n_seg > 0) {
+            MmParams q = fm;
+            q.x = xp;
+            q.n_tok = nt;
+            for (int s = 0; s < q.n_seg; ++s) q.seg[s].y = args[fm_idx[s]].y + static_cast<int64_t>(t0) * q.seg[s].y_stride;
+            q.n_stages = std::max(2, std::min(kMaxStages, kRingBudget / q.slot_bytes));
+            const size_t smem = static_cast<size_t>(q.n_stages) * q.slot_bytes +
+                                static_cast<size_t>(NT) * (q.n_in / 32) * (kSubPad + 1) * sizeof(float) +
+                                2 * kMaxStages * sizeof(uint64_t) + kMaxStages * sizeof(int) + 16;
+            if (smem > kSmemMax) return cuda_status(cudaErrorInvalidValue, "mul_mat shared memory");
+            const int grid = std::min(q.n_tiles, sms);
+            const int rc = NT == 1 ? launch_fma<1>(q, grid, smem, st)
+                           : NT == 2 ? launch_fma<2>(q, grid, smem, st)
+                                     : launch_fma<4>(q, grid, smem, st);
+            if (rc != SQMIX_OK) return rc;
+        }
+    }
+    return SQMIX_OK;
 }
 
 extern "C" int sqmix_mul_mat(const sqmix_mul_mat_args *a, sqmix_stream_t stream) {
     SQMIX_CHECK_ARG(a != nullptr, "mul_mat: null args");
-    SQMIX_CHECK_ARG(a->w && a->x && a->y, "mul_mat: null pointer argument");
-    SQMIX_CHECK_ARG(unit_bytes(a->w_type) != 0, "mul_mat: weight type %d (q8_0, q4_K, q6_K, f32, f16, bf16)",
-                    a->w_type);
-    SQMIX_CHECK_ARG(a->n_in >= 256 && a->n_in <= kMaxIn && a->n_in % 256 == 0,
-                    "mul_mat: n_in=%lld must be a multiple of 256 in [256, %d]", (long long)a->n_in, kMaxIn);
-    SQMIX_CHECK_ARG(a->n_out >= 1 && a->n_out <= (1 << 24), "mul_mat: n_out=%lld", (long long)a->n_out);
-    SQMIX_CHECK_ARG(a->n_tokens >= 1, "mul_mat: n_tokens=%d", a->n_tokens);
-    SQMIX_CHECK_ARG(a->x_dtype == SQMIX_F32 || a->x_dtype == SQMIX_F16 || a->x_dtype == SQMIX_BF16,
-                    "mul_mat: x dtype %d", a->x_dtype);
-    const int64_t rb = sqmix_mul_mat_row_bytes(a->w_type, a->n_in);
-    SQMIX_CHECK_ARG(a->w_row_bytes == rb, "mul_mat: w_row_bytes=%lld, rows must be contiguous (%lld bytes)",
-                    (long long)a->w_row_bytes, (long long)rb);
-    // rows reach shared memory by 1-D bulk copies: 16-byte multiples (q6_K: n_in % 2048 == 0)
-    SQMIX_CHECK_ARG(rb % 16 == 0, "mul_mat: a row of %lld bytes is not a multiple of 16 (q6_K needs n_in %% 2048 == 0)",
-                    (long long)rb);
-    SQMIX_CHECK_ARG((reinterpret_cast<uintptr_t>(a->w) & 15) == 0, "mul_mat: w must be 16-byte aligned");
-    SQMIX_CHECK_ARG(a->x_stride >= a->n_in && a->y_stride >= a->n_out, "mul_mat: token strides too small");
-    MmParams p;
-    p.w = static_cast<const uint8_t *>(a->w);
-    p.w_type = a->w_type;
-    p.row_bytes = rb;
-    p.n_in = static_cast<int>(a->n_in);
-    p.n_out = static_cast<int>(a->n_out);
-    p.x_dtype = a->x_dtype;
-    p.x_stride = a->x_stride;
-    p.y_stride = a->y_stride;
-    p.status = a->status;
-    const bool tc = a->w_type == SQMIX_Q4_K || a->w_type == SQMIX_Q6_K || a->w_type == SQMIX_Q8_0;
-    p.rows_per_slot = tc ? kTcRows : static_cast<int>(std::min<int64_t>(kMmWarps, std::max<int64_t>(1, kSlotMax / rb)));
-    p.sstride = static_cast<int>(tc && (rb / 4) % 8 == 0 ? rb + 16 : rb);
-    p.slot_bytes = static_cast<int>((p.rows_per_slot * static_cast<int64_t>(p.sstride) + 127) / 128 * 128);
-    p.n_stages = std::max(2, std::min(kMaxStages, kRingBudget / p.slot_bytes));
-    const int n_tiles = (p.n_out + p.rows_per_slot - 1) / p.rows_per_slot;
-    const int grid = std::min(n_tiles, sqmix_device_sm_count(-1));
-    if (grid <= 0) return cuda_status(cudaErrorInvalidDevice, "mul_mat device");
-    constexpr size_t kSmemMax = 227 * 1024;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int elt = a->x_dtype == SQMIX_F32 ? 4 : 2;
-    for (int t0 = 0; t0 < a->n_tokens; t0 += kMaxPassTokens) {
-        const int nt = std::min(kMaxPassTokens, a->n_tokens - t0);
-        p.x = static_cast<const uint8_t *>(a->x) + static_cast<int64_t>(t0) * a->x_stride * elt;
-        p.y = a->y + static_cast<int64_t>(t0) * a->y_stride;
-        p.n_tok = nt;
-        const int NT = nt <= 1 ? 1 : nt <= 2 ? 2 : 4;
-        int rc;
-        if (tc) {
-            // B fragments, slice sums, the cross-warp partial sums of a group of tiles
-            const size_t extra = static_cast<size_t>(p.n_in) * NT * 4 + static_cast<size_t>(NT) * (p.n_in / 16) * 4 +
-                                 static_cast<size_t>(kTcGroup) * kMmWarps * 32 * 16 +
-                                 2 * kMaxStages * sizeof(uint64_t) + kMaxStages * sizeof(int) + 16;
-            // two CTAs per SM when the ring of at least 2 slots allows (more warps to hide
-            // the latency of the dequant / MMA chains), else one
-            MmParams q = p;
-            constexpr size_t kSmemHalf = 113 * 1024 - 1024;
-            const size_t budget = extra + 2 * static_cast<size_t>(q.slot_bytes) <= kSmemHalf ? kSmemHalf : kSmemMax;
-            q.n_stages = static_cast<int>(std::min<size_t>(q.n_stages, (budget - extra) / q.slot_bytes));
-            if (q.n_stages < 2) return cuda_status(cudaErrorInvalidValue, "mul_mat shared memory");
-            const size_t smem = static_cast<size_t>(q.n_stages) * q.slot_bytes + extra;
-            const int grid_tc = std::min(n_tiles, (budget == kSmemHalf ? 2 : 1) * sqmix_device_sm_count(-1));
-            if (NT == 1)
-                rc = launch_mm_tc_type<1>(q, grid_tc, smem, st);
-            else if (NT == 2)
-                rc = launch_mm_tc_type<2>(q, grid_tc, smem, st);
-            else
-                rc = launch_mm_tc_type<4>(q, grid_tc, smem, st);
-        } else {
-            const size_t smem = static_cast<size_t>(p.n_stages) * p.slot_bytes +
-                                static_cast<size_t>(NT) * (p.n_in / 32) * (kSubPad + 1) * sizeof(float) +
-                                2 * kMaxStages * sizeof(uint64_t) + kMaxStages * sizeof(int) + 16;
-            if (NT == 1)
-                rc = launch_mm_type<1>(p, grid, smem, st);
-            else if (NT == 2)
-                rc = launch_mm_type<2>(p, grid, smem, st);
-            else
-                rc = launch_mm_type<4>(p, grid, smem, st);
-        }
-        if (rc != SQMIX_OK) return rc;
-    }
-    return SQMIX_OK;
+    return sqmix_mul_mat_group(a, 1, stream);
 }

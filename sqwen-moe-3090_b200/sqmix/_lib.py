@@ -23,6 +23,7 @@ SQMIX_ERANGE = -6
 SQMIX_F32 = 0
 SQMIX_F16 = 1
 SQMIX_BF16 = 30
+SQMIX_MUL_MAT_MAX_GROUP = 8  # projections of one sqmix_mul_mat_group call
 SQMIX_Q8_0 = 8  # weight block formats of sqmix_mul_mat
 SQMIX_Q4_K = 12
 SQMIX_Q6_K = 14
@@ -230,6 +231,7 @@ _SIGNATURES = {
     "sqmix_gdn_layer_decode": (ctypes.c_int, [ctypes.POINTER(GdnLayerArgs), c_void_p]),
     "sqmix_mul_mat_row_bytes": (c_int64, [c_int32, c_int64]),
     "sqmix_mul_mat": (ctypes.c_int, [ctypes.POINTER(MulMatArgs), c_void_p]),
+    "sqmix_mul_mat_group": (ctypes.c_int, [ctypes.POINTER(MulMatArgs), c_int32, c_void_p]),
     "sqmix_ggml_fa_args": (ctypes.c_int, [ctypes.POINTER(GgmlTensor), ctypes.POINTER(GgmlFaOp), ctypes.POINTER(FaArgs)]),
     "sqmix_ggml_gdn_args": (ctypes.c_int, [ctypes.POINTER(GgmlTensor), ctypes.POINTER(GgmlGdnOp),
                                            ctypes.POINTER(GdnArgs)]),

@@ -23,7 +23,7 @@ import math
 
 import torch
 
-from ._lib import (SQMIX_BF16, SQMIX_F16, SQMIX_F32, SQMIX_FA_OVERLAP_PREV, FaArgs, FaBatchArgs, GdnArgs, GdnConvArgs,
+from ._lib import (SQMIX_BF16, SQMIX_F16, SQMIX_F32, SQMIX_FA_OVERLAP_PREV, SQMIX_MUL_MAT_MAX_GROUP, FaArgs, FaBatchArgs, GdnArgs, GdnConvArgs,
                    GdnLayerArgs, HeadNormArgs, KvAppendArgs, MulMatArgs, check, lib)
 
 HEAD_DIM = 256
@@ -482,25 +482,51 @@ def mul_mat_row_bytes(w_type: int, n_in: int) -> int:
     return int(lib().sqmix_mul_mat_row_bytes(int(w_type), int(n_in)))
 
 
-def mul_mat(w: torch.Tensor, w_type: int, n_in: int, x: torch.Tensor, out: torch.Tensor | None = None,
-            status: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-    """ggml_mul_mat(w, x): w [n_out][row bytes] (uint8, a GGUF block format: SQMIX_Q8_0 /
-    SQMIX_Q4_K / SQMIX_Q6_K) or [n_out][n_in] f32 / f16 / bf16 elements; x [T][n_in]
-    (f32 / f16 / bf16, rows contiguous).  Returns y [T][n_out] f32."""
+def _mul_mat_entry(w: torch.Tensor, w_type: int, n_in: int, x2: torch.Tensor, out: torch.Tensor | None,
+                   status: torch.Tensor | None):
     rb = mul_mat_row_bytes(w_type, n_in)
     if rb == 0:
         raise ValueError(f"unsupported weight type {w_type} for n_in={n_in}")
     if not w.is_contiguous() or w.numel() * w.element_size() % rb != 0:
         raise ValueError("w must be contiguous rows of the format")
     n_out = w.numel() * w.element_size() // rb
-    x2 = x.reshape(-1, n_in)
-    if x2.stride(1) != 1:
-        x2 = x2.contiguous()
     T = x2.shape[0]
     if out is None:
-        out = torch.empty((T, n_out), dtype=torch.float32, device=x.device)
+        out = torch.empty((T, n_out), dtype=torch.float32, device=x2.device)
     a = MulMatArgs(w=w.data_ptr(), w_type=int(w_type), w_row_bytes=rb, n_in=n_in, n_out=n_out, x=x2.data_ptr(),
                    x_dtype=_dt(x2), x_stride=x2.stride(0), n_tokens=T, y=out.data_ptr(), y_stride=out.stride(0),
                    status=status.data_ptr() if status is not None else None)
+    return a, out
+
+
+def _tokens(x: torch.Tensor, n_in: int) -> torch.Tensor:
+    x2 = x.reshape(-1, n_in)
+    return x2 if x2.stride(1) == 1 else x2.contiguous()
+
+
+def mul_mat(w: torch.Tensor, w_type: int, n_in: int, x: torch.Tensor, out: torch.Tensor | None = None,
+            status: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """ggml_mul_mat(w, x): w [n_out][row bytes] (uint8, a GGUF block format: SQMIX_Q8_0 /
+    SQMIX_Q4_K / SQMIX_Q6_K) or [n_out][n_in] f32 / f16 / bf16 elements; x [T][n_in]
+    (f32 / f16 / bf16, rows contiguous).  Returns y [T][n_out] f32."""
+    a, out = _mul_mat_entry(w, w_type, n_in, _tokens(x, n_in), out, status)
     check(lib().sqmix_mul_mat(ctypes.byref(a), _stream(stream)), "mul_mat")
     return out
+
+
+def mul_mat_group(weights, n_in: int, x: torch.Tensor, outs=None, status: torch.Tensor | None = None,
+                  stream=None) -> list:
+    """Several ggml_mul_mat of the same x in one pass (sqmix_mul_mat_group): weights is a
+    list of (w, w_type) as for mul_mat, outs an optional list of y tensors (None entries
+    are allocated).  Returns the list of y [T][n_out] f32."""
+    if not 1 <= len(weights) <= SQMIX_MUL_MAT_MAX_GROUP:
+        raise ValueError(f"a group has 1..{SQMIX_MUL_MAT_MAX_GROUP} projections, not {len(weights)}")
+    x2 = _tokens(x, n_in)
+    outs = list(outs) if outs is not None else [None] * len(weights)
+    arr = (MulMatArgs * len(weights))()
+    res = []
+    for i, ((w, w_type), o) in enumerate(zip(weights, outs)):
+        arr[i], o = _mul_mat_entry(w, w_type, n_in, x2, o, status if i == 0 else None)
+        res.append(o)
+    check(lib().sqmix_mul_mat_group(arr, len(weights), _stream(stream)), "mul_mat_group")
+    return res

@@ -285,3 +285,33 @@ def test_mul_mat_argument_validation_without_gpu(sqmix_lib):
     for kw in bad:
         a = args(**kw)
         assert L.sqmix_mul_mat(ctypes.byref(a), None) == sqmix_lib.SQMIX_EINVAL, kw
+
+
+def test_mul_mat_group_argument_validation_without_gpu(sqmix_lib):
+    """A group takes 1..SQMIX_MUL_MAT_MAX_GROUP entries that share x (pointer, dtype,
+    stride, tokens, n_in); each entry is checked as sqmix_mul_mat checks it."""
+    from sqmix._lib import MulMatArgs
+
+    L = sqmix_lib.lib()
+    fake = ctypes.c_void_p(4096)
+
+    def entry(**kw):
+        base = dict(w=fake, w_type=sqmix_lib.SQMIX_Q4_K, w_row_bytes=8 * 144, n_in=2048, n_out=64, x=fake,
+                    x_dtype=sqmix_lib.SQMIX_F32, x_stride=2048, n_tokens=1, y=fake, y_stride=64)
+        base.update(kw)
+        return MulMatArgs(**base)
+
+    def group(*entries, n=None):
+        arr = (MulMatArgs * max(1, len(entries)))(*entries)
+        return L.sqmix_mul_mat_group(arr, len(entries) if n is None else n, None)
+
+    assert sqmix_lib.SQMIX_MUL_MAT_MAX_GROUP == 8
+    assert group(entry(), n=0) == sqmix_lib.SQMIX_EINVAL
+    assert group(*[entry() for _ in range(9)]) == sqmix_lib.SQMIX_EINVAL
+    assert group(entry(), entry(x=ctypes.c_void_p(8192))) == sqmix_lib.SQMIX_EINVAL      # another x
+    assert group(entry(), entry(x_stride=4096)) == sqmix_lib.SQMIX_EINVAL               # another stride
+    assert group(entry(), entry(n_tokens=2)) == sqmix_lib.SQMIX_EINVAL
+    assert group(entry(), entry(x_dtype=sqmix_lib.SQMIX_BF16)) == sqmix_lib.SQMIX_EINVAL
+    assert group(entry(), entry(w_row_bytes=8 * 144 + 16)) == sqmix_lib.SQMIX_EINVAL    # a bad second entry
+    assert b"mul_mat[1]" in L.sqmix_last_error()
+    assert L.sqmix_mul_mat_group(None, 1, None) == sqmix_lib.SQMIX_EINVAL

@@ -112,3 +112,45 @@ def test_mul_mat_strided_tokens_and_output():
     got = yw.cpu().numpy()
     assert rel_err(got[:, :n_out], want.astype(np.float64)) <= TOL
     assert (got[:, n_out:] == 7.0).all()  # nothing written past the rows
+
+
+@pytest.mark.parametrize("T", [1, 2, 6])
+def test_mul_mat_group_matches_single_calls_and_oracle(oracle, T):
+    """One sqmix_mul_mat_group over projections of the same x -- a ragged q4_K (tiles
+    that end inside the tile list), q6_K, q8_0 and two float-typed matrices (the
+    32-row beta / alpha) -- equals one sqmix_mul_mat per entry bit for bit, and the
+    oracle within the bar; T = 6 takes two passes."""
+    import sqmix
+
+    rng = np.random.default_rng(4242 + T)
+    n_in = 2048
+    specs = [(12, 1000), (14, 512), (8, 40), (0, 32), (30, 32), (12, 16)]
+    rows = [random_rows(rng, wt, n_in, n_out) for wt, n_out in specs]
+    ws = [torch.from_numpy(r).cuda() for r in rows]
+    x = torch.randn((T, n_in), generator=torch.Generator().manual_seed(T)).cuda()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    got = sqmix.mul_mat_group([(w, wt) for w, (wt, _) in zip(ws, specs)], n_in, x, status=status)
+    single = [sqmix.mul_mat(w, wt, n_in, x) for w, (wt, _) in zip(ws, specs)]
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    xh = x.cpu().numpy()
+    for (wt, n_out), r, g, s in zip(specs, rows, got, single):
+        assert g.shape == (T, n_out)
+        assert torch.equal(g, s), (wt, n_out)
+        assert rel_err(g.cpu().numpy(), oracle.mul_mat(r, wt, n_in, xh).astype(np.float64)) <= TOL, (wt, n_out)
+
+
+def test_mul_mat_group_bf16_x_4096_inputs(oracle):
+    """A group at n_in = 4096 (two units per warp) with bf16 activations and 3 tokens."""
+    import sqmix
+
+    rng = np.random.default_rng(99)
+    n_in, T = 4096, 3
+    specs = [(12, 2048), (8, 64)]
+    rows = [random_rows(rng, wt, n_in, n_out) for wt, n_out in specs]
+    x = torch.randn((T, n_in), generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    got = sqmix.mul_mat_group([(torch.from_numpy(r).cuda(), wt) for r, (wt, _) in zip(rows, specs)], n_in, x.cuda())
+    torch.cuda.synchronize()
+    for (wt, n_out), r, g in zip(specs, rows, got):
+        want = oracle.mul_mat(r, wt, n_in, x.float().numpy())
+        assert rel_err(g.cpu().numpy(), want.astype(np.float64)) <= TOL, (wt, n_out)
