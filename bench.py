@@ -1094,9 +1094,8 @@ def bench_proj(steps: int, warmup: int) -> dict:
     """The mixer projections of one decode token (T = 1) and of an MTP verification
     step (T = 2) through all 40 layers on distinct weights (735 MB > L2), captured in a
     CUDA graph: the projections of one x go as one sqmix_mul_mat_group call (QG / K / V;
-    qkv / z / beta / alpha), W_o and ssm_out alone -- 10 x 2 + 30 x 2 = 80 calls, 110
-    launches (the f32 beta / alpha of a group take a launch of their own).  The 190
-    single sqmix_mul_mat calls are timed beside it at T = 1."""
+    qkv / z / beta / alpha), W_o and ssm_out alone -- 10 x 2 + 30 x 2 = 80 calls, one
+    launch each.  The 190 single sqmix_mul_mat calls are timed beside it at T = 1."""
     import torch
 
     import sqmix
@@ -1112,7 +1111,7 @@ def bench_proj(steps: int, warmup: int) -> dict:
             groups.setdefault(n_in, []).append((name, wt, n_in, n_out, proj_weights(n_in, n_out, wt, dev, seed)))
         layers.append(list(groups.values()))
     calls = [c for groups in layers for grp in groups for c in grp]
-    n_launch = sum(len({wt in (8, 12, 14) for _, wt, _, _, _ in grp}) for groups in layers for grp in groups)
+    n_launch = sum(len(groups) for groups in layers)  # one launch per call at T <= 4
     wbytes = sum(c[4].numel() for c in calls)
     res = {"calls_per_token": sum(len(groups) for groups in layers), "launches_per_token": n_launch,
            "weight_bytes": wbytes, "peak_gbs": hbm, "peak_kind": hbm_kind}
@@ -1413,6 +1412,12 @@ def run_profile_case(case: str):
         wn = torch.rand((128,), generator=g, device=dev) + 0.5
         for _ in range(3):
             sqmix.gdn_layer_decode(x, w, cst, alpha, braw, ssm_a, S, l2_eps=1e-6, z=z, norm_weight=wn)
+    elif case == "mm":  # a GDN layer's input projections as one group, T = 1 (14.7 MB per launch)
+        x = torch.randn((1, 2048), generator=g, device=dev)
+        groups = [[(proj_weights(n_in, n_out, wt, dev, 10 * i + j), wt)
+                   for j, (_, wt, n_in, n_out) in enumerate(PROJ_GDN[:4])] for i in range(3)]
+        for grp in groups:
+            sqmix.mul_mat_group(grp, 2048, x)
     else:
         raise SystemExit(f"unknown profile case {case}")
     torch.cuda.synchronize()
@@ -1430,7 +1435,7 @@ def main():
     ap.add_argument("--headline-only", action="store_true",
                     help="config 3 only (skip configs 0, 1, 2 and 4)")
     ap.add_argument("--nccl-merge", action="store_true", help="N > 1: all-gather + merge instead of the peer merge")
-    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn | gdnb | gdnp | gdnl) and exit")
+    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn | gdnb | gdnp | gdnl | mm) and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)

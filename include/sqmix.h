@@ -589,9 +589,9 @@ int sqmix_mul_mat(const sqmix_mul_mat_args *args, sqmix_stream_t stream);
 /* A group of projections of the same x -- a layer's QG / K / V (attn.rs:127-129), or its
  * qkv / z / beta / alpha (gdn.rs:264-276) -- in one pass over x: args[0 .. n) must agree
  * on x, x_dtype, x_stride, n_tokens and n_in; each has its own w, w_type, n_out and y
- * (y must not overlap x).  The quantised weights of the group share one launch per 4
- * tokens, the float-typed ones another.  Bounded-wait failures go to args[0].status.
- * Same results, to the bit, as one sqmix_mul_mat per entry. */
+ * (y must not overlap x).  The group is one launch per 4 tokens.  Bounded-wait
+ * failures go to args[0].status.  Same results, to the bit, as one sqmix_mul_mat per
+ * entry. */
 #define SQMIX_MUL_MAT_MAX_GROUP 8
 int sqmix_mul_mat_group(const sqmix_mul_mat_args *args, int32_t n, sqmix_stream_t stream);
 

@@ -13,9 +13,9 @@
 // cost of a launch (the wait on the kernel before, staging x) is paid once per group.
 // Tiles reach shared memory by bulk copies (TMA, no multicast) on an mbarrier ring that
 // is filled before the grid-dependency wait: the weights are model constants, only x
-// comes from the kernel before.  Quantised tiles go through the tensor cores
-// (mul_mat_tc_kernel), f32 / f16 / bf16 tiles through FMAs (mul_mat_kernel).  A pass
-// serves up to kMaxPassTokens tokens per stream of W.
+// comes from the kernel before.  Quantised tiles go through the tensor cores, f32 / f16
+// / bf16 tiles through FMAs, in the same kernel.  A pass serves up to kMaxPassTokens
+// tokens per stream of W.
 #include <math.h>
 
 #include "common.cuh"
@@ -26,12 +26,11 @@ namespace {
 
 constexpr int kMmWarps = 8;
 constexpr int kMmThreads = kMmWarps * 32;
+constexpr int kMmCtasPerSm = 2;       // CTAs per SM the registers are budgeted for
 constexpr int kMaxIn = 4096;          // n_in limit (the model's 2048 and 4096)
 constexpr int kMaxPassTokens = 4;     // tokens per stream of W
-constexpr int kSubPad = 36;           // floats per staged 32-value sub-block (FMA path)
-constexpr int kRingBudget = 96 * 1024;
 constexpr int kMaxStages = 8;
-constexpr int kSlotMax = 32 * 1024;   // bytes of one FMA-path slot (<= 8 rows)
+constexpr int kFloatSlot = 16 * 1024; // slot bytes of a launch of float-typed weights only
 constexpr int kMaxSeg = SQMIX_MUL_MAT_MAX_GROUP;
 
 // one projection of a launch
@@ -42,7 +41,7 @@ struct MmSeg {
     int w_type;
     int row_bytes;
     int sstride;       // bytes between rows in a slot
-    int rows;          // rows per tile
+    int rows;          // rows per tile: 16 for the quantised formats
     int n_out;
     int tile0;         // first tile of the projection in the launch's tile list
 };
@@ -55,6 +54,7 @@ struct MmParams {
     int x_dtype;
     int64_t x_stride;
     int n_tok;         // tokens of this pass (<= NT)
+    int has_float;     // x is also staged in f32 for float-typed rows
     uint32_t *status;
     int n_stages, slot_bytes;
 };
@@ -76,196 +76,12 @@ __host__ __device__ constexpr int unit_bytes(int t) {
            : (t == SQMIX_F16 || t == SQMIX_BF16) ? 512 : 0;
 }
 
-// The 32 values of sub-block j (0..7) of one 256-value unit at `u` (shared memory) of
-// a float-typed row.
-template <int WT>
-__device__ __forceinline__ void dequant_sub(const uint8_t *u, int j, float (&v)[32]) {
-    if constexpr (WT == SQMIX_F32) {
-        const float4 *f = reinterpret_cast<const float4 *>(u + 128 * j);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 x = f[i];
-            v[4 * i] = x.x;
-            v[4 * i + 1] = x.y;
-            v[4 * i + 2] = x.z;
-            v[4 * i + 3] = x.w;
-        }
-    } else {  // f16 / bf16
-        const uint4 *h = reinterpret_cast<const uint4 *>(u + 64 * j);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint4 x = h[i];
-            const uint32_t w[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                float2 f;
-                if constexpr (WT == SQMIX_BF16)
-                    f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[e]));
-                else
-                    f = __half22float2(*reinterpret_cast<const __half2 *>(&w[e]));
-                v[8 * i + 2 * e] = f.x;
-                v[8 * i + 2 * e + 1] = f.y;
-            }
-        }
-    }
-}
-
-// ---- f32 / f16 / bf16 weights: FMAs -----------------------------------------------
-// A tile (one shared-memory slot) holds up to 8 consecutive rows of one projection --
-// contiguous bytes of its tensor -- brought in by one 1-D bulk copy.  Warp w takes row w
-// of a tile; lane l takes the 32-value sub-block l % 8 of the row's 256-value units l / 8,
-// l / 8 + 4, ..., and multiplies it with the staged tokens (f32 in shared memory,
-// 32-value sub-blocks padded to 36 floats so that the 8 lanes of a unit read 8
-// different bank groups).  The warp then reduces its lanes by shuffles.
-template <int NT>
-__global__ void __launch_bounds__(kMmThreads, 1) mul_mat_kernel(const __grid_constant__ MmParams p) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    const int ring_bytes = p.n_stages * p.slot_bytes;
-    const int n_sub = p.n_in / 32;
-    float *xs = reinterpret_cast<float *>(smem + ring_bytes);  // [NT][n_sub][kSubPad]
-    float *xsum = xs + NT * n_sub * kSubPad;                   // [NT][n_sub]
-    uint64_t *full_bar = reinterpret_cast<uint64_t *>(xsum + NT * n_sub);
-    uint64_t *empty_bar = full_bar + kMaxStages;
-    int *rel_cnt = reinterpret_cast<int *>(empty_bar + kMaxStages);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    const int tile0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * p.n_tiles) / gridDim.x);
-    const int tile1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * p.n_tiles) / gridDim.x);
-    const int n_tiles = tile1 - tile0;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < p.n_stages; ++s) {
-            mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], kMmWarps);
-            rel_cnt[s] = 0;
-        }
-        fence_mbar_init();
-    }
-    __syncthreads();
-    auto issue = [&](int it) {  // tile tile0 + it into slot it % n_stages
-        const int s = it % p.n_stages;
-        const MmSeg &sg = p.seg[seg_of(p, tile0 + it)];
-        const int row0 = (tile0 + it - sg.tile0) * sg.rows;
-        const int rows = min(sg.rows, sg.n_out - row0);
-        const uint32_t bytes = static_cast<uint32_t>(rows * sg.row_bytes);
-        mbar_arrive_expect_tx(&full_bar[s], bytes);
-        bulk_g2s(smem + s * p.slot_bytes, sg.w + static_cast<int64_t>(row0) * sg.row_bytes, bytes, &full_bar[s]);
-    };
-    // the weights are constants of the model: stream them before the dependency wait
-    if (threadIdx.x == 0)
-        for (int it = 0; it < n_tiles && it < p.n_stages; ++it) issue(it);
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" :::);
-
-    // tokens -> xs (padded sub-blocks) and their sub-block sums: a warp takes 32
-    // consecutive values (one sub-block) per step, coalesced, with the loads of
-    // kXBatch steps in flight together, and sums each sub-block by shuffles
-    constexpr int kXBatch = 8;
-    const int n_x = NT * p.n_in;  // a multiple of 256: every step is warp-uniform
-    for (int base0 = warp * 32; base0 < n_x; base0 += kMmThreads * kXBatch) {
-        float v[kXBatch];
-#pragma unroll
-        for (int b = 0; b < kXBatch; ++b) {
-            const int idx = base0 + b * kMmThreads + lane;
-            const int t = idx / p.n_in, i = idx - t * p.n_in;
-            v[b] = idx < n_x && t < p.n_tok ? load_act(p.x, static_cast<int64_t>(t) * p.x_stride + i, p.x_dtype) : 0.f;
-        }
-#pragma unroll
-        for (int b = 0; b < kXBatch; ++b) {
-            const int idx = base0 + b * kMmThreads + lane;
-            if (base0 + b * kMmThreads < n_x) {
-                const int t = idx / p.n_in, i = idx - t * p.n_in;
-                xs[(t * n_sub + (i >> 5)) * kSubPad + (i & 31)] = v[b];
-                float sum = v[b];
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-                if (lane == 0) xsum[t * n_sub + (i >> 5)] = sum;
-            }
-        }
-    }
-    __syncthreads();
-
-    const int n_units = p.n_in / 256;
-    const int j = lane & 7;
-    bool ok = true;
-    for (int it = 0; it < n_tiles; ++it) {
-        const int s = it % p.n_stages;
-        if (!mbar_wait(&full_bar[s], (it / p.n_stages) & 1)) ok = false;
-        if (__any_sync(0xffffffffu, !ok)) break;
-        const MmSeg &sg = p.seg[seg_of(p, tile0 + it)];
-        const int row = (tile0 + it - sg.tile0) * sg.rows + warp;
-        if (warp < sg.rows && row < sg.n_out) {
-            const uint8_t *wr = smem + s * p.slot_bytes + warp * sg.row_bytes;
-            const int ub = unit_bytes(sg.w_type);
-            float acc[NT];
-#pragma unroll
-            for (int t = 0; t < NT; ++t) acc[t] = 0.f;
-            for (int un = lane >> 3; un < n_units; un += 4) {
-                float v[32];
-                if (sg.w_type == SQMIX_F32)
-                    dequant_sub<SQMIX_F32>(wr + un * ub, j, v);
-                else if (sg.w_type == SQMIX_F16)
-                    dequant_sub<SQMIX_F16>(wr + un * ub, j, v);
-                else
-                    dequant_sub<SQMIX_BF16>(wr + un * ub, j, v);
-                const int sb = 8 * un + j;
-#pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    const float4 *xv = reinterpret_cast<const float4 *>(xs + (t * n_sub + sb) * kSubPad);
-                    float a = 0.f;
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float4 x = xv[q];
-                        a = fmaf(v[4 * q], x.x, a);
-                        a = fmaf(v[4 * q + 1], x.y, a);
-                        a = fmaf(v[4 * q + 2], x.z, a);
-                        a = fmaf(v[4 * q + 3], x.w, a);
-                    }
-                    acc[t] += a;
-                }
-            }
-#pragma unroll
-            for (int t = 0; t < NT; ++t)
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], off);
-            if (lane == 0)
-#pragma unroll
-                for (int t = 0; t < NT; ++t)
-                    if (t < p.n_tok) sg.y[static_cast<int64_t>(t) * sg.y_stride + row] = acc[t];
-        }
-        // release the slot; the warp that releases it last refills it
-        __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(&empty_bar[s]);
-            if (atomicAdd(&rel_cnt[s], 1) == kMmWarps - 1) {
-                rel_cnt[s] = 0;
-                if (it + p.n_stages < n_tiles) {
-                    // every warp has arrived: this wait returns at once
-                    if (mbar_wait(&empty_bar[s], (it / p.n_stages) & 1))
-                        issue(it + p.n_stages);
-                    else
-                        ok = false;
-                }
-            }
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-    }
-    if (__syncthreads_or(!ok)) {
-        if (threadIdx.x == 0 && p.status) atomicOr(p.status, 1u);
-        // never leave with a bulk copy still writing into shared memory: wait (bounded)
-        // for the copies of the last slots
-        if (threadIdx.x == 0) {
-            const int first = n_tiles > p.n_stages ? n_tiles - p.n_stages : 0;
-            for (int it = first; it < n_tiles; ++it)
-                if (!mbar_wait(&full_bar[it % p.n_stages], (it / p.n_stages) & 1)) break;
-        }
-    }
-}
-
-// ---- quantised weights on the tensor cores ---------------------------------------
+// ---- the tiles ---------------------------------------------------------------------
 // q8_0 / q4_K / q6_K tiles go through mma.m16n8k16 (f16 operands, f32 accumulators): a
 // tile is 16 weight rows of one projection (the M of the MMA), one bulk copy per row
 // into a slot whose rows lie sstride bytes apart (sstride / 4 = 4 mod 8: the 8 row
-// groups of a fragment load hit 8 different groups of 4 banks).  The 8 warps split the
+// groups of a fragment load hit 8 different groups of 4 banks).  A float-typed tile
+// holds as many rows as fit the slot (unit_float).  The 8 warps split the
 // 256-value units of the contraction (warp w: units w, w + 8, ...), each warp moving on
 // to the next tile as soon as it is done (a slot is refilled by the warp that releases
 // it last), and the partial sums of a group of kTcGroup tiles are reduced through
@@ -453,9 +269,57 @@ __device__ __forceinline__ void unit_q8_0(const uint8_t *rg, const uint8_t *rg8,
     }
 }
 
+// f32 / f16 / bf16 rows (the 32-row beta / alpha): FMAs in f32.  Lane l takes values
+// 256 u + 8 l .. + 7 of each of the tile's rows against x in f32 (xf: [NT][n_in]); each
+// (row, token) sum is reduced over the warp by shuffles, and lane (g, c) keeps rows g,
+// g + 8 of token c, as the tensor-core units leave them.
+template <int NT>
+__device__ __forceinline__ void unit_float(const uint8_t *slot, int sstride, int rows, int wt, int u, int lane,
+                                           const float *xf, int n_in, int g, int c, float &y0, float &y1) {
+    float xv[NT][8];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const float4 *xp = reinterpret_cast<const float4 *>(xf + t * n_in + 256 * u + 8 * lane);
+        const float4 a = xp[0], b = xp[1];
+        xv[t][0] = a.x, xv[t][1] = a.y, xv[t][2] = a.z, xv[t][3] = a.w;
+        xv[t][4] = b.x, xv[t][5] = b.y, xv[t][6] = b.z, xv[t][7] = b.w;
+    }
+    for (int r = 0; r < rows; ++r) {
+        float w[8];
+        if (wt == SQMIX_F32) {
+            const float4 *wp = reinterpret_cast<const float4 *>(slot + r * sstride + u * 1024 + 32 * lane);
+            const float4 a = wp[0], b = wp[1];
+            w[0] = a.x, w[1] = a.y, w[2] = a.z, w[3] = a.w, w[4] = b.x, w[5] = b.y, w[6] = b.z, w[7] = b.w;
+        } else {
+            const uint4 h = *reinterpret_cast<const uint4 *>(slot + r * sstride + u * 512 + 16 * lane);
+            const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = wt == SQMIX_BF16 ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&hw[e]))
+                                                  : __half22float2(*reinterpret_cast<const __half2 *>(&hw[e]));
+                w[2 * e] = f.x;
+                w[2 * e + 1] = f.y;
+            }
+        }
+        float mine = 0.f;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float a = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a = fmaf(w[i], xv[t][i], a);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+            if (t == 0 || c == t) mine = a;
+        }
+        if (r == g) y0 += mine;
+        if (r == g + 8) y1 += mine;
+    }
+}
+
 // shared memory of mul_mat_tc_kernel after its ring
-__host__ __device__ constexpr size_t tc_extra_bytes(int nt, int n_in) {
+__host__ __device__ constexpr size_t tc_extra_bytes(int nt, int n_in, bool has_float) {
     return static_cast<size_t>(n_in / 16) * 2 * nt * 4 * 8 +                 // B fragments
+           (has_float ? static_cast<size_t>(nt) * n_in * 4 : 0) +             // x in f32
            static_cast<size_t>(nt) * (n_in / 16 + 1) * 4 +                    // 16-value sums
            static_cast<size_t>(nt) * (n_in / 32 + 1) * 4 +                    // 32-value sums
            static_cast<size_t>(kMmWarps) * 16 * kFsStride * 4 +               // scale tables
@@ -464,14 +328,15 @@ __host__ __device__ constexpr size_t tc_extra_bytes(int nt, int n_in) {
 }
 
 template <int NT>
-__global__ void __launch_bounds__(kMmThreads, 2) mul_mat_tc_kernel(const __grid_constant__ MmParams p) {
+__global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const __grid_constant__ MmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int ring_bytes = p.n_stages * p.slot_bytes;
     const int n_units = p.n_in / 256;
     const int n_sl = p.n_in / 16, n_sub = p.n_in / 32;
     const int xs16_st = n_sl + 1, xs32_st = n_sub + 1;  // token rows one bank apart
     uint2 *bf = reinterpret_cast<uint2 *>(smem + ring_bytes);                  // [n_sl][2 NT][4 lanes c]
-    float *xs16 = reinterpret_cast<float *>(bf + n_sl * 2 * NT * 4);          // [NT][xs16_st]
+    float *xf = reinterpret_cast<float *>(bf + n_sl * 2 * NT * 4);            // [NT][n_in] if has_float
+    float *xs16 = xf + (p.has_float ? NT * p.n_in : 0);                        // [NT][xs16_st]
     float *xs32 = xs16 + NT * xs16_st;                                         // [NT][xs32_st]
     float *fst_all = xs32 + NT * xs32_st;                                      // [8 warps][16][kFsStride]
     float2 *red = reinterpret_cast<float2 *>(fst_all + kMmWarps * 16 * kFsStride);  // [kTcGroup][8][32]
@@ -498,8 +363,8 @@ __global__ void __launch_bounds__(kMmThreads, 2) mul_mat_tc_kernel(const __grid_
     auto issue = [&](int it) {
         const int s = it % p.n_stages;
         const MmSeg &sg = p.seg[seg_of(p, tile0 + it)];
-        const int row0 = (tile0 + it - sg.tile0) * kTcRows;
-        const int rows = min(kTcRows, sg.n_out - row0);
+        const int row0 = (tile0 + it - sg.tile0) * sg.rows;
+        const int rows = min(sg.rows, sg.n_out - row0);
         if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], static_cast<uint32_t>(rows * sg.row_bytes));
         __syncwarp();
         if (lane < rows)
@@ -551,6 +416,14 @@ __global__ void __launch_bounds__(kMmThreads, 2) mul_mat_tc_kernel(const __grid_
             const float *s16 = xs16 + t * xs16_st + 16 * u + 2 * j;
             xs32[t * xs32_st + 8 * u + j] = s16[0] + s16[1];
         }
+        if (p.has_float)  // f32 x for float-typed rows: lane l keeps values 256 u + 8 l .. + 7
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int i = 256 * u + 8 * lane + q;
+                    xf[t * p.n_in + i] = t < p.n_tok ? load_act(p.x, static_cast<int64_t>(t) * p.x_stride + i, p.x_dtype) : 0.f;
+                }
     }
     __syncwarp();
 
@@ -574,8 +447,11 @@ __global__ void __launch_bounds__(kMmThreads, 2) mul_mat_tc_kernel(const __grid_
                     unit_q4k<NT>(rg, rg8, u, g, c, bf, xs32, xs32_st, fst, y0, y1);
                 else if (wt == SQMIX_Q6_K)
                     unit_q6k<NT>(rg, rg8, u, g, c, bf, xs16, xs16_st, fst, y0, y1);
-                else
+                else if (wt == SQMIX_Q8_0)
                     unit_q8_0<NT>(rg, rg8, u, g, c, bf, fst, y0, y1);
+                else
+                    unit_float<NT>(smem + s * p.slot_bytes, sg.sstride, min(sg.rows, sg.n_out - (tile0 + it - sg.tile0) * sg.rows),
+                                   wt, u, lane, xf, p.n_in, g, c, y0, y1);
             }
             red[((it - gb) * kMmWarps + warp) * 32 + lane] = make_float2(y0, y1);
             // release the slot; the warp that releases it last refills it
@@ -613,8 +489,8 @@ __global__ void __launch_bounds__(kMmThreads, 2) mul_mat_tc_kernel(const __grid_
             }
             const int t = tile0 + gb + tl;
             const MmSeg &sg = p.seg[seg_of(p, t)];
-            const int row = (t - sg.tile0) * kTcRows + r;
-            if (row < sg.n_out && n < p.n_tok) sg.y[static_cast<int64_t>(n) * sg.y_stride + row] = acc;
+            const int row = (t - sg.tile0) * sg.rows + r;
+            if (r < sg.rows && row < sg.n_out && n < p.n_tok) sg.y[static_cast<int64_t>(n) * sg.y_stride + row] = acc;
         }
         __syncthreads();  // the partial sums' space is reused by the next group
     }
@@ -650,13 +526,7 @@ int launch_pdl(K kernel, std::atomic<uint64_t> &attr_devices, const MmParams &p,
 }
 
 template <int NT>
-int launch_tc(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
-    static std::atomic<uint64_t> attr_devices{0};
-    return launch_pdl(mul_mat_tc_kernel<NT>, attr_devices, p, grid, smem, st);
-}
-
-template <int NT>
-int launch_fma(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
+int launch_mm(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
     static std::atomic<uint64_t> attr_devices{0};
     return launch_pdl(mul_mat_kernel<NT>, attr_devices, p, grid, smem, st);
 }
@@ -712,13 +582,22 @@ extern "C" int sqmix_mul_mat_group(const sqmix_mul_mat_args *args, int32_t n, sq
                             args[i].n_tokens == a0.n_tokens && args[i].n_in == a0.n_in,
                         "mul_mat_group: entry %d does not share x (pointer, dtype, stride, n_tokens, n_in) with entry 0",
                         i);
-    // the launch's projections: quantised ones on the tensor cores, float ones on FMAs
-    MmParams tc = {}, fm = {};
-    int tc_idx[kMaxSeg], fm_idx[kMaxSeg];
-    int max_sstride = 0, max_fm_slot = 0;
+    // the launch's tile list: the projections in call order, 16-row tiles for the
+    // quantised formats, float-typed rows as many as fit the slot (up to 16)
+    MmParams p = {};
+    int max_sstride = 0;
+    int64_t max_float_rb = 0;
     for (int i = 0; i < n; ++i) {
         const int64_t rb = row_bytes_of(args[i].w_type, args[i].n_in);
-        MmParams &p = tc_type(args[i].w_type) ? tc : fm;
+        if (tc_type(args[i].w_type))
+            max_sstride = std::max(max_sstride, static_cast<int>((rb / 4) % 8 == 0 ? rb + 16 : rb));  // rb / 4: 0 or 4 mod 8
+        else
+            max_float_rb = std::max(max_float_rb, rb);
+    }
+    p.slot_bytes = static_cast<int>(std::max<int64_t>(max_sstride > 0 ? kTcRows * max_sstride : kFloatSlot, max_float_rb));
+    p.slot_bytes = (p.slot_bytes + 127) / 128 * 128;
+    for (int i = 0; i < n; ++i) {
+        const int64_t rb = row_bytes_of(args[i].w_type, args[i].n_in);
         MmSeg &sg = p.seg[p.n_seg];
         sg.w = static_cast<const uint8_t *>(args[i].w);
         sg.y_stride = args[i].y_stride;
@@ -726,73 +605,48 @@ extern "C" int sqmix_mul_mat_group(const sqmix_mul_mat_args *args, int32_t n, sq
         sg.row_bytes = static_cast<int>(rb);
         sg.n_out = static_cast<int>(args[i].n_out);
         sg.tile0 = p.n_tiles;
-        if (&p == &tc) {
+        if (tc_type(sg.w_type)) {
             sg.rows = kTcRows;
-            sg.sstride = static_cast<int>((rb / 4) % 8 == 0 ? rb + 16 : rb);  // rb / 4 is 0 or 4 mod 8
-            max_sstride = std::max(max_sstride, sg.sstride);
-            tc_idx[p.n_seg] = i;
+            sg.sstride = static_cast<int>((rb / 4) % 8 == 0 ? rb + 16 : rb);
         } else {
-            sg.rows = static_cast<int>(std::min<int64_t>(kMmWarps, std::max<int64_t>(1, kSlotMax / rb)));
+            sg.rows = static_cast<int>(std::min<int64_t>(kTcRows, p.slot_bytes / rb));
             sg.sstride = sg.row_bytes;
-            max_fm_slot = std::max(max_fm_slot, sg.rows * sg.row_bytes);
-            fm_idx[p.n_seg] = i;
+            p.has_float = 1;
         }
         p.n_tiles += (sg.n_out + sg.rows - 1) / sg.rows;
         ++p.n_seg;
     }
     const int sms = sqmix_device_sm_count(-1);
     if (sms <= 0) return cuda_status(cudaErrorInvalidDevice, "mul_mat device");
-    for (MmParams *pp : {&tc, &fm}) {
-        pp->n_in = static_cast<int>(a0.n_in);
-        pp->x_dtype = a0.x_dtype;
-        pp->x_stride = a0.x_stride;
-        pp->status = a0.status;
-    }
-    tc.slot_bytes = (kTcRows * max_sstride + 127) / 128 * 128;
-    fm.slot_bytes = (max_fm_slot + 127) / 128 * 128;
-    constexpr size_t kSmemMax = 227 * 1024;
-    // two CTAs per SM when a ring of at least 2 slots fits beside the rest (more warps to
-    // hide the latency of the dequant / MMA chains), else one
-    constexpr size_t kSmemHalf = 113 * 1024 - 1024;
+    p.n_in = static_cast<int>(a0.n_in);
+    p.x_dtype = a0.x_dtype;
+    p.x_stride = a0.x_stride;
+    p.status = a0.status;
+    // as many CTAs per SM (up to kMmCtasPerSm) as leave room for a ring of at least 2
+    // slots beside the rest: more warps to hide the latency of the dequant / MMA chains
+    auto smem_budget = [](int ctas) { return static_cast<size_t>(228 * 1024 / ctas - 1024); };
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int elt = a0.x_dtype == SQMIX_F32 ? 4 : 2;
     for (int t0 = 0; t0 < a0.n_tokens; t0 += kMaxPassTokens) {
         const int nt = std::min(kMaxPassTokens, a0.n_tokens - t0);
         const int NT = nt <= 1 ? 1 : nt <= 2 ? 2 : 4;
-        const void *xp = static_cast<const uint8_t *>(a0.x) + static_cast<int64_t>(t0) * a0.x_stride * elt;
-        if (tc.n_seg > 0) {
-            MmParams q = tc;
-            q.x = xp;
-            q.n_tok = nt;
-            for (int s = 0; s < q.n_seg; ++s) q.seg[s].y = args[tc_idx[s]].y + static_cast<int64_t>(t0) * q.seg[s].y_stride;
-            const size_t extra = tc_extra_bytes(NT, q.n_in);
-            const size_t budget = extra + 2 * static_cast<size_t>(q.slot_bytes) <= kSmemHalf ? kSmemHalf : kSmemMax;
-            if (extra + 2 * static_cast<size_t>(q.slot_bytes) > budget)
-                return cuda_status(cudaErrorInvalidValue, "mul_mat shared memory");
-            q.n_stages = static_cast<int>(std::min<size_t>(kMaxStages, (budget - extra) / q.slot_bytes));
-            const size_t smem = static_cast<size_t>(q.n_stages) * q.slot_bytes + extra;
-            const int grid = std::min(q.n_tiles, (budget == kSmemHalf ? 2 : 1) * sms);
-            const int rc = NT == 1 ? launch_tc<1>(q, grid, smem, st)
-                           : NT == 2 ? launch_tc<2>(q, grid, smem, st)
-                                     : launch_tc<4>(q, grid, smem, st);
-            if (rc != SQMIX_OK) return rc;
-        }
-        if (fm.n_seg > 0) {
-            MmParams q = fm;
-            q.x = xp;
-            q.n_tok = nt;
-            for (int s = 0; s < q.n_seg; ++s) q.seg[s].y = args[fm_idx[s]].y + static_cast<int64_t>(t0) * q.seg[s].y_stride;
-            q.n_stages = std::max(2, std::min(kMaxStages, kRingBudget / q.slot_bytes));
-            const size_t smem = static_cast<size_t>(q.n_stages) * q.slot_bytes +
-                                static_cast<size_t>(NT) * (q.n_in / 32) * (kSubPad + 1) * sizeof(float) +
-                                2 * kMaxStages * sizeof(uint64_t) + kMaxStages * sizeof(int) + 16;
-            if (smem > kSmemMax) return cuda_status(cudaErrorInvalidValue, "mul_mat shared memory");
-            const int grid = std::min(q.n_tiles, sms);
-            const int rc = NT == 1 ? launch_fma<1>(q, grid, smem, st)
-                           : NT == 2 ? launch_fma<2>(q, grid, smem, st)
-                                     : launch_fma<4>(q, grid, smem, st);
-            if (rc != SQMIX_OK) return rc;
-        }
+        MmParams q = p;
+        q.x = static_cast<const uint8_t *>(a0.x) + static_cast<int64_t>(t0) * a0.x_stride * elt;
+        q.n_tok = nt;
+        for (int s = 0; s < q.n_seg; ++s) q.seg[s].y = args[s].y + static_cast<int64_t>(t0) * q.seg[s].y_stride;
+        const size_t extra = tc_extra_bytes(NT, q.n_in, q.has_float != 0);
+        int ctas = kMmCtasPerSm;
+        while (ctas > 1 && extra + 2 * static_cast<size_t>(q.slot_bytes) > smem_budget(ctas)) --ctas;
+        const size_t budget = std::min<size_t>(smem_budget(ctas), 227 * 1024);
+        if (extra + 2 * static_cast<size_t>(q.slot_bytes) > budget)
+            return cuda_status(cudaErrorInvalidValue, "mul_mat shared memory");
+        q.n_stages = static_cast<int>(std::min<size_t>(kMaxStages, (budget - extra) / q.slot_bytes));
+        const size_t smem = static_cast<size_t>(q.n_stages) * q.slot_bytes + extra;
+        const int grid = std::min(q.n_tiles, ctas * sms);
+        const int rc = NT == 1 ? launch_mm<1>(q, grid, smem, st)
+                       : NT == 2 ? launch_mm<2>(q, grid, smem, st)
+                                 : launch_mm<4>(q, grid, smem, st);
+        if (rc != SQMIX_OK) return rc;
     }
     return SQMIX_OK;
 }
