@@ -103,7 +103,7 @@ __host__ __device__ constexpr int unit_bytes(int t) {
 // broadcasts.
 constexpr int kTcRows = 16;
 constexpr int kTcGroup = 4;   // tiles whose partial sums are reduced together
-constexpr int kFsStride = 18; // floats per row of a warp's scale table (the 8 row groups: 8 bank pairs)
+constexpr int kTabStride = 36; // floats per row group g of a warp's scale table (g at 4-bank offsets)
 
 __device__ __forceinline__ uint32_t nib_lo(uint32_t w) { return w & 0x000F000Fu; }
 __device__ __forceinline__ uint32_t nib_hi(uint32_t w) { return w & 0x00F000F0u; }
@@ -141,30 +141,43 @@ __device__ __forceinline__ uint2 bfrag_at(const uint2 *bf, int sl, int g, int c)
 }
 
 // One 256-value unit u of rows g, g + 8 (rg, rg8: the rows in the slot), token c of this
-// lane: y0 / y1 += the unit's dot products.  fst: the warp's scale table [16][kFsStride].
+// lane: y0 / y1 += the unit's dot products.  tab: the warp's scale table, [8 row groups g]
+// [kTabStride] floats, entry e of row group g holding row g's and row g + 8's scales.
 template <int NT>
 __device__ __forceinline__ void unit_q4k(const uint8_t *rg, const uint8_t *rg8, int u, int g, int c,
-                                         const uint2 *bf, const float *xs32, int n_sub, float *fst, float &y0,
+                                         const uint2 *bf, const float *xs32, int xs32_st, float *tab, float &y0,
                                          float &y1) {
     __syncwarp();  // the previous unit's table reads are done
-    // lane c: (d sc 2^24 or 2^20, dmin m) of sub-blocks 2c, 2c + 1 of rows g, g + 8; the
-    // 12 scale bytes as three words (a unit starts 16-byte aligned in the slot)
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-        const uint8_t *b = (rr ? rg8 : rg) + u * 144;
+    // lane (g, c) decodes row g + 8 (c / 2), sub-blocks 4 (c % 2) .. + 3: the 12 scale bytes
+    // as three words (a unit starts 16-byte aligned in the slot), four 6-bit scales / mins
+    // per word; entry j = (d sc 2^24 or 2^20, dmin m) of row g, then of row g + 8
+    {
+        const int rh = c >> 1;
+        const uint8_t *b = (rh ? rg8 : rg) + u * 144;
         const float d = f16_at(b), dmin = f16_at(b + 2);
         const uint32_t s0 = *reinterpret_cast<const uint32_t *>(b + 4);
         const uint32_t s1 = *reinterpret_cast<const uint32_t *>(b + 8);
         const uint32_t s2 = *reinterpret_cast<const uint32_t *>(b + 12);
+        const bool upper = c & 1;
+        const uint32_t sc4 = upper ? (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u) : s0 & 0x3F3F3F3Fu;
+        const uint32_t m4 = upper ? ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u) : s1 & 0x3F3F3F3Fu;
+        const float dl = d * 16777216.0f, dh = d * 1048576.0f;
+        float *e = tab + g * kTabStride + 16 * (c & 1) + 2 * rh;
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const int j = 2 * c + q, sh = 8 * (j & 3);
-            const uint32_t b0 = (s0 >> sh) & 0xFF, b1 = (s1 >> sh) & 0xFF, b2 = (s2 >> sh) & 0xFF;
-            const uint32_t sc = j < 4 ? b0 & 63 : (b2 & 0xF) | ((b0 >> 6) << 4);
-            const uint32_t m = j < 4 ? b1 & 63 : (b2 >> 4) | ((b1 >> 6) << 4);
-            *reinterpret_cast<float2 *>(fst + (8 * rr + g) * kFsStride + 2 * j) =
-                make_float2(d * static_cast<float>(sc) * (q ? 1048576.0f : 16777216.0f), dmin * static_cast<float>(m));
-        }
+        for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<float2 *>(e + 4 * q) =
+                make_float2((q & 1 ? dh : dl) * static_cast<float>((sc4 >> (8 * q)) & 0xFF),
+                            dmin * static_cast<float>((m4 >> (8 * q)) & 0xFF));
+    }
+    // this lane's token c: the unit's 32-value sums of x
+    float xj[8];
+    if (c < NT) {
+        const float4 *xp = reinterpret_cast<const float4 *>(xs32 + c * xs32_st + 8 * u);
+        const float4 x0 = xp[0], x1 = xp[1];
+        xj[0] = x0.x, xj[1] = x0.y, xj[2] = x0.z, xj[3] = x0.w, xj[4] = x1.x, xj[5] = x1.y, xj[6] = x1.z, xj[7] = x1.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xj[j] = 0.f;
     }
     __syncwarp();
 #pragma unroll
@@ -192,28 +205,27 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *rg, const uint8_t *rg8, 
         for (int sbk = 0; sbk < 2; ++sbk) {
             const int j = 2 * k + sbk;
             const float *a = sbk ? ah : al;
-            const float2 f0 = *reinterpret_cast<const float2 *>(fst + g * kFsStride + 2 * j);
-            const float2 f1 = *reinterpret_cast<const float2 *>(fst + (g + 8) * kFsStride + 2 * j);
-            const float xj = c < NT ? xs32[c * n_sub + 8 * u + j] : 0.f;
-            y0 = fmaf(f0.x, a[0] + a[1], fmaf(-f0.y, xj, y0));
-            y1 = fmaf(f1.x, a[2] + a[3], fmaf(-f1.y, xj, y1));
+            const float4 f = *reinterpret_cast<const float4 *>(tab + g * kTabStride + 4 * j);
+            y0 = fmaf(f.x, a[0] + a[1], fmaf(-f.y, xj[j], y0));
+            y1 = fmaf(f.z, a[2] + a[3], fmaf(-f.w, xj[j], y1));
         }
     }
 }
 
 template <int NT>
 __device__ __forceinline__ void unit_q6k(const uint8_t *rg, const uint8_t *rg8, int u, int g, int c,
-                                         const uint2 *bf, const float *xs16, int n_sl, float *fst, float &y0,
+                                         const uint2 *bf, const float *xs16, int xs16_st, float *tab, float &y0,
                                          float &y1) {
     __syncwarp();
-    // lane c: d sc of slices 4c .. 4c + 3 of rows g, g + 8
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-        const uint8_t *b = (rr ? rg8 : rg) + u * 210;
-        const float d = f16_at(b + 208);
+    // lane c: d sc of slices 4c .. 4c + 3; entry q = (row g, row g + 8)
+    {
+        const uint8_t *b0 = rg + u * 210, *b1 = rg8 + u * 210;
+        const float d0 = f16_at(b0 + 208), d1 = f16_at(b1 + 208);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-            fst[(8 * rr + g) * kFsStride + 4 * c + q] = d * static_cast<float>(static_cast<int8_t>(b[192 + 4 * c + q]));
+            *reinterpret_cast<float2 *>(tab + g * kTabStride + 2 * (4 * c + q)) =
+                make_float2(d0 * static_cast<float>(static_cast<int8_t>(b0[192 + 4 * c + q])),
+                            d1 * static_cast<float>(static_cast<int8_t>(b1[192 + 4 * c + q])));
     }
     __syncwarp();
 #pragma unroll 4
@@ -230,8 +242,9 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *rg, const uint8_t *rg8, 
                                 ((l1 >> 8) & 0x000F000Fu) | (((h1 >> 8) & 0x00030003u) << 4)};
         float a[4];
         mma_f16_zero(a, av, bfrag_at<NT>(bf, 16 * u + q, g, c));
-        const float d0 = fst[g * kFsStride + q], d1 = fst[(g + 8) * kFsStride + q];
-        const float xq = c < NT ? xs16[c * n_sl + 16 * u + q] : 0.f;
+        const float2 dd = *reinterpret_cast<const float2 *>(tab + g * kTabStride + 2 * q);
+        const float d0 = dd.x, d1 = dd.y;
+        const float xq = c < NT ? xs16[c * xs16_st + 16 * u + q] : 0.f;
         y0 = fmaf(d0 * 16777216.0f, a[0] + a[1], fmaf(-32.0f * d0, xq, y0));
         y1 = fmaf(d1 * 16777216.0f, a[2] + a[3], fmaf(-32.0f * d1, xq, y1));
     }
@@ -239,14 +252,13 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *rg, const uint8_t *rg8, 
 
 template <int NT>
 __device__ __forceinline__ void unit_q8_0(const uint8_t *rg, const uint8_t *rg8, int u, int g, int c,
-                                          const uint2 *bf, float *fst, float &y0, float &y1) {
+                                          const uint2 *bf, float *tab, float &y0, float &y1) {
     __syncwarp();
-    // lane c: d of blocks 2c, 2c + 1 of rows g, g + 8
+    // lane c: d of blocks 2c, 2c + 1; entry j = (row g, row g + 8)
 #pragma unroll
-    for (int rr = 0; rr < 2; ++rr)
-#pragma unroll
-        for (int q = 0; q < 2; ++q)
-            fst[(8 * rr + g) * kFsStride + 2 * c + q] = f16_at((rr ? rg8 : rg) + u * 272 + 34 * (2 * c + q));
+    for (int q = 0; q < 2; ++q)
+        *reinterpret_cast<float2 *>(tab + g * kTabStride + 2 * (2 * c + q)) =
+            make_float2(f16_at(rg + u * 272 + 34 * (2 * c + q)), f16_at(rg8 + u * 272 + 34 * (2 * c + q)));
     __syncwarp();
 #pragma unroll 2
     for (int j = 0; j < 8; ++j) {  // block j of the unit: 32 values, one d
@@ -264,8 +276,9 @@ __device__ __forceinline__ void unit_q8_0(const uint8_t *rg, const uint8_t *rg8,
             else
                 mma_f16_acc(a, av, b);
         }
-        y0 = fmaf(fst[g * kFsStride + j], a[0] + a[1], y0);
-        y1 = fmaf(fst[(g + 8) * kFsStride + j], a[2] + a[3], y1);
+        const float2 dd = *reinterpret_cast<const float2 *>(tab + g * kTabStride + 2 * j);
+        y0 = fmaf(dd.x, a[0] + a[1], y0);
+        y1 = fmaf(dd.y, a[2] + a[3], y1);
     }
 }
 
@@ -320,9 +333,9 @@ __device__ __forceinline__ void unit_float(const uint8_t *slot, int sstride, int
 __host__ __device__ constexpr size_t tc_extra_bytes(int nt, int n_in, bool has_float) {
     return static_cast<size_t>(n_in / 16) * 2 * nt * 4 * 8 +                 // B fragments
            (has_float ? static_cast<size_t>(nt) * n_in * 4 : 0) +             // x in f32
-           static_cast<size_t>(nt) * (n_in / 16 + 1) * 4 +                    // 16-value sums
-           static_cast<size_t>(nt) * (n_in / 32 + 1) * 4 +                    // 32-value sums
-           static_cast<size_t>(kMmWarps) * 16 * kFsStride * 4 +               // scale tables
+           static_cast<size_t>(nt) * (n_in / 16 + 4) * 4 +                    // 16-value sums
+           static_cast<size_t>(nt) * (n_in / 32 + 4) * 4 +                    // 32-value sums
+           static_cast<size_t>(kMmWarps) * 8 * kTabStride * 4 +               // scale tables
            static_cast<size_t>(kTcGroup) * kMmWarps * 32 * 8 +                // partial sums
            2 * kMaxStages * sizeof(uint64_t) + kMaxStages * sizeof(int) + 16;  // barriers
 }
@@ -333,19 +346,19 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
     const int ring_bytes = p.n_stages * p.slot_bytes;
     const int n_units = p.n_in / 256;
     const int n_sl = p.n_in / 16, n_sub = p.n_in / 32;
-    const int xs16_st = n_sl + 1, xs32_st = n_sub + 1;  // token rows one bank apart
+    const int xs16_st = n_sl + 4, xs32_st = n_sub + 4;  // token rows 4 banks apart, 16-byte aligned
     uint2 *bf = reinterpret_cast<uint2 *>(smem + ring_bytes);                  // [n_sl][2 NT][4 lanes c]
     float *xf = reinterpret_cast<float *>(bf + n_sl * 2 * NT * 4);            // [NT][n_in] if has_float
     float *xs16 = xf + (p.has_float ? NT * p.n_in : 0);                        // [NT][xs16_st]
     float *xs32 = xs16 + NT * xs16_st;                                         // [NT][xs32_st]
-    float *fst_all = xs32 + NT * xs32_st;                                      // [8 warps][16][kFsStride]
-    float2 *red = reinterpret_cast<float2 *>(fst_all + kMmWarps * 16 * kFsStride);  // [kTcGroup][8][32]
+    float *tab_all = xs32 + NT * xs32_st;                                      // [8 warps][8][kTabStride]
+    float2 *red = reinterpret_cast<float2 *>(tab_all + kMmWarps * 8 * kTabStride);  // [kTcGroup][8][32]
     uint64_t *full_bar = reinterpret_cast<uint64_t *>(red + kTcGroup * kMmWarps * 32);
     uint64_t *empty_bar = full_bar + kMaxStages;
     int *rel_cnt = reinterpret_cast<int *>(empty_bar + kMaxStages);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
-    float *fst = fst_all + warp * 16 * kFsStride;
+    float *tab = tab_all + warp * 8 * kTabStride;
 
     const int tile0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * p.n_tiles) / gridDim.x);
     const int tile1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * p.n_tiles) / gridDim.x);
@@ -444,11 +457,11 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
             float y0 = 0.f, y1 = 0.f;
             for (int u = warp; u < n_units; u += kMmWarps) {
                 if (wt == SQMIX_Q4_K)
-                    unit_q4k<NT>(rg, rg8, u, g, c, bf, xs32, xs32_st, fst, y0, y1);
+                    unit_q4k<NT>(rg, rg8, u, g, c, bf, xs32, xs32_st, tab, y0, y1);
                 else if (wt == SQMIX_Q6_K)
-                    unit_q6k<NT>(rg, rg8, u, g, c, bf, xs16, xs16_st, fst, y0, y1);
+                    unit_q6k<NT>(rg, rg8, u, g, c, bf, xs16, xs16_st, tab, y0, y1);
                 else if (wt == SQMIX_Q8_0)
-                    unit_q8_0<NT>(rg, rg8, u, g, c, bf, fst, y0, y1);
+                    unit_q8_0<NT>(rg, rg8, u, g, c, bf, tab, y0, y1);
                 else
                     unit_float<NT>(smem + s * p.slot_bytes, sg.sstride, min(sg.rows, sg.n_out - (tile0 + it - sg.tile0) * sg.rows),
                                    wt, u, lane, xf, p.n_in, g, c, y0, y1);
