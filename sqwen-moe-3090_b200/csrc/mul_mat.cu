@@ -179,35 +179,41 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *rg, const uint8_t *rg8, 
 #pragma unroll
         for (int j = 0; j < 8; ++j) xj[j] = 0.f;
     }
-    __syncwarp();
+    // two halves of the unit: the MMAs of a half do not need the table, so the first
+    // half's overlap the table's stores; the __syncwarp before the first epilogue makes
+    // the table visible
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {  // 32 bytes: sub-blocks 2k (low nibbles), 2k + 1 (high)
-        float al[4], ah[4];
+    for (int half = 0; half < 2; ++half) {
+        float acc[4][4];  // sub-blocks 4 half + 0 .. 3
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int off = u * 144 + 16 + 32 * k + 16 * h + 4 * c;
-            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(rg + off);
-            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(rg8 + off);
-            const uint32_t w0s = w0 >> 8, w1s = w1 >> 8;
-            const uint32_t alo[4] = {nib_lo(w0), nib_lo(w1), nib_lo(w0s), nib_lo(w1s)};
-            const uint32_t ahi[4] = {nib_hi(w0), nib_hi(w1), nib_hi(w0s), nib_hi(w1s)};
-            const uint2 bl = bfrag_at<NT>(bf, 2 * (8 * u + 2 * k) + h, g, c);
-            const uint2 bh = bfrag_at<NT>(bf, 2 * (8 * u + 2 * k + 1) + h, g, c);
-            if (h == 0) {
-                mma_f16_zero(al, alo, bl);
-                mma_f16_zero(ah, ahi, bh);
-            } else {
-                mma_f16_acc(al, alo, bl);
-                mma_f16_acc(ah, ahi, bh);
+        for (int kk = 0; kk < 2; ++kk) {  // 32 bytes: sub-blocks 2k (low nibbles), 2k + 1 (high)
+            const int k = 2 * half + kk;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int off = u * 144 + 16 + 32 * k + 16 * h + 4 * c;
+                const uint32_t w0 = *reinterpret_cast<const uint32_t *>(rg + off);
+                const uint32_t w1 = *reinterpret_cast<const uint32_t *>(rg8 + off);
+                const uint32_t w0s = w0 >> 8, w1s = w1 >> 8;
+                const uint32_t alo[4] = {nib_lo(w0), nib_lo(w1), nib_lo(w0s), nib_lo(w1s)};
+                const uint32_t ahi[4] = {nib_hi(w0), nib_hi(w1), nib_hi(w0s), nib_hi(w1s)};
+                const uint2 bl = bfrag_at<NT>(bf, 2 * (8 * u + 2 * k) + h, g, c);
+                const uint2 bh = bfrag_at<NT>(bf, 2 * (8 * u + 2 * k + 1) + h, g, c);
+                if (h == 0) {
+                    mma_f16_zero(acc[2 * kk], alo, bl);
+                    mma_f16_zero(acc[2 * kk + 1], ahi, bh);
+                } else {
+                    mma_f16_acc(acc[2 * kk], alo, bl);
+                    mma_f16_acc(acc[2 * kk + 1], ahi, bh);
+                }
             }
         }
+        if (half == 0) __syncwarp();
 #pragma unroll
-        for (int sbk = 0; sbk < 2; ++sbk) {
-            const int j = 2 * k + sbk;
-            const float *a = sbk ? ah : al;
+        for (int jj = 0; jj < 4; ++jj) {
+            const int j = 4 * half + jj;
             const float4 f = *reinterpret_cast<const float4 *>(tab + g * kTabStride + 4 * j);
-            y0 = fmaf(f.x, a[0] + a[1], fmaf(-f.y, xj[j], y0));
-            y1 = fmaf(f.z, a[2] + a[3], fmaf(-f.w, xj[j], y1));
+            y0 = fmaf(f.x, acc[jj][0] + acc[jj][1], fmaf(-f.y, xj[j], y0));
+            y1 = fmaf(f.z, acc[jj][2] + acc[jj][3], fmaf(-f.w, xj[j], y1));
         }
     }
 }
@@ -390,6 +396,9 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" :::);
 
+    // f32 x rows 16-byte aligned: 4 values per load
+    const bool x_vec = p.x_dtype == SQMIX_F32 &&
+                       ((reinterpret_cast<uintptr_t>(p.x) | static_cast<uintptr_t>(p.x_stride * 4)) & 15) == 0;
     // x -> the B fragments and slice sums of this warp's units (no other warp reads them):
     // entry (slice l of unit u, token t, lane c) covers x values 16 (16 u + l) + 4 c .. + 3
     for (int u = warp; u < n_units; u += kMmWarps) {
@@ -399,10 +408,16 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
         for (int e = 0; e < kE; ++e) {
             const int idx = e * 32 + lane;
             const int t = (idx >> 2) % NT, sl = 16 * u + (idx >> 2) / NT;
+            const int64_t i0 = static_cast<int64_t>(t) * p.x_stride + 16 * sl + 4 * c;
+            if (t >= p.n_tok) {
+                v[e][0] = v[e][1] = v[e][2] = v[e][3] = 0.f;
+            } else if (x_vec) {
+                const float4 xv = *reinterpret_cast<const float4 *>(static_cast<const float *>(p.x) + i0);
+                v[e][0] = xv.x, v[e][1] = xv.y, v[e][2] = xv.z, v[e][3] = xv.w;
+            } else {
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                v[e][q] = t < p.n_tok ? load_act(p.x, static_cast<int64_t>(t) * p.x_stride + 16 * sl + 4 * c + q, p.x_dtype)
-                                      : 0.f;
+                for (int q = 0; q < 4; ++q) v[e][q] = load_act(p.x, i0 + q, p.x_dtype);
+            }
         }
 #pragma unroll
         for (int e = 0; e < kE; ++e) {
@@ -431,12 +446,22 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
         }
         if (p.has_float)  // f32 x for float-typed rows: lane l keeps values 256 u + 8 l .. + 7
 #pragma unroll
-            for (int t = 0; t < NT; ++t)
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const int i = 256 * u + 8 * lane + q;
-                    xf[t * p.n_in + i] = t < p.n_tok ? load_act(p.x, static_cast<int64_t>(t) * p.x_stride + i, p.x_dtype) : 0.f;
+            for (int t = 0; t < NT; ++t) {
+                float4 *dst = reinterpret_cast<float4 *>(xf + t * p.n_in + 256 * u + 8 * lane);
+                const int64_t i0 = static_cast<int64_t>(t) * p.x_stride + 256 * u + 8 * lane;
+                if (t >= p.n_tok) {
+                    dst[0] = dst[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                } else if (x_vec) {
+                    const float4 *src = reinterpret_cast<const float4 *>(static_cast<const float *>(p.x) + i0);
+                    dst[0] = src[0];
+                    dst[1] = src[1];
+                } else {
+                    dst[0] = make_float4(load_act(p.x, i0, p.x_dtype), load_act(p.x, i0 + 1, p.x_dtype),
+                                         load_act(p.x, i0 + 2, p.x_dtype), load_act(p.x, i0 + 3, p.x_dtype));
+                    dst[1] = make_float4(load_act(p.x, i0 + 4, p.x_dtype), load_act(p.x, i0 + 5, p.x_dtype),
+                                         load_act(p.x, i0 + 6, p.x_dtype), load_act(p.x, i0 + 7, p.x_dtype));
                 }
+            }
     }
     __syncwarp();
 

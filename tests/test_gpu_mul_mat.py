@@ -90,8 +90,10 @@ def test_mul_mat_model_shapes_vs_oracle(oracle, wtype, n_in, n_out, T, xdt):
     assert int(status.item()) == 0
 
 
-def test_mul_mat_strided_tokens_and_output():
-    """x and y with token strides larger than their rows (views into wider buffers)."""
+@pytest.mark.parametrize("x_pad", [64, 3])
+def test_mul_mat_strided_tokens_and_output(x_pad):
+    """x and y with token strides larger than their rows (views into wider buffers); a
+    pad of 3 floats leaves the rows of x 4-byte aligned only."""
     import sqmix
     from sqmix._lib import MulMatArgs, check, lib
     import ctypes
@@ -99,11 +101,11 @@ def test_mul_mat_strided_tokens_and_output():
     rng = np.random.default_rng(7)
     n_in, n_out, T = 2048, 64, 3
     rows = random_rows(rng, 12, n_in, n_out)
-    xw = torch.randn((T, n_in + 64), device="cuda")
+    xw = torch.randn((T, n_in + x_pad), device="cuda")
     yw = torch.full((T, n_out + 16), 7.0, device="cuda")
     w = torch.from_numpy(rows).cuda()
     a = MulMatArgs(w=w.data_ptr(), w_type=12, w_row_bytes=sqmix.mul_mat_row_bytes(12, n_in), n_in=n_in, n_out=n_out,
-                   x=xw.data_ptr(), x_dtype=0, x_stride=n_in + 64, n_tokens=T, y=yw.data_ptr(), y_stride=n_out + 16)
+                   x=xw.data_ptr(), x_dtype=0, x_stride=n_in + x_pad, n_tokens=T, y=yw.data_ptr(), y_stride=n_out + 16)
     check(lib().sqmix_mul_mat(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "mul_mat")
     torch.cuda.synchronize()
     import oracle as orc
