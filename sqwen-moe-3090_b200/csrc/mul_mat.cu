@@ -40,7 +40,7 @@ struct MmSeg {
     int64_t y_stride;
     int w_type;
     int row_bytes;
-    int sstride;       // bytes between rows in a slot
+    int sstride;       // quantised: bytes between row pairs in a slot; float: between rows
     int rows;          // rows per tile: 16 for the quantised formats
     int n_out;
     int tile0;         // first tile of the projection in the launch's tile list
@@ -70,6 +70,9 @@ __device__ __forceinline__ float f16_at(const uint8_t *p) {
     return __half2float(*reinterpret_cast<const __half *>(p));
 }
 
+// The block formats that go through the tensor cores.
+__host__ __device__ constexpr bool quant_type(int t) { return t == SQMIX_Q4_K || t == SQMIX_Q6_K || t == SQMIX_Q8_0; }
+
 // Unit (256 values) bytes per format; 0: unsupported.
 __host__ __device__ constexpr int unit_bytes(int t) {
     return t == SQMIX_Q4_K ? 144 : t == SQMIX_Q6_K ? 210 : t == SQMIX_Q8_0 ? 272 : t == SQMIX_F32 ? 1024
@@ -78,10 +81,12 @@ __host__ __device__ constexpr int unit_bytes(int t) {
 
 // ---- the tiles ---------------------------------------------------------------------
 // q8_0 / q4_K / q6_K tiles go through mma.m16n8k16 (f16 operands, f32 accumulators): a
-// tile is 16 weight rows of one projection (the M of the MMA), one bulk copy per row
-// into a slot whose rows lie sstride bytes apart (sstride / 4 = 4 mod 8: the 8 row
-// groups of a fragment load hit 8 different groups of 4 banks).  A float-typed tile
-// holds as many rows as fit the slot (unit_float).  The 8 warps split the
+// tile is 16 weight rows of one projection (the M of the MMA), brought in as 8 bulk
+// copies of two consecutive rows each, the pairs sstride = 2 row_bytes + 16 bytes apart
+// in the slot (sstride / 4 = 4 mod 8).  MMA row g is the pair's first row, MMA row g + 8
+// its second: the 8 row groups of a fragment load then hit 8 different groups of 4
+// banks.  A float-typed tile holds as many rows as fit the slot, in one copy
+// (unit_float).  The 8 warps split the
 // 256-value units of the contraction (warp w: units w, w + 8, ...), each warp moving on
 // to the next tile as soon as it is done (a slot is refilled by the warp that releases
 // it last), and the partial sums of a group of kTcGroup tiles are reduced through
@@ -378,7 +383,8 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
         fence_mbar_init();
     }
     __syncthreads();
-    // one bulk copy per row, the lanes of one warp issuing a tile's rows together
+    // quantised tiles: one bulk copy per row pair, the lanes of one warp issuing them
+    // together; float tiles: one copy
     auto issue = [&](int it) {
         const int s = it % p.n_stages;
         const MmSeg &sg = p.seg[seg_of(p, tile0 + it)];
@@ -386,9 +392,14 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
         const int rows = min(sg.rows, sg.n_out - row0);
         if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], static_cast<uint32_t>(rows * sg.row_bytes));
         __syncwarp();
-        if (lane < rows)
-            bulk_g2s(smem + s * p.slot_bytes + lane * sg.sstride, sg.w + static_cast<int64_t>(row0 + lane) * sg.row_bytes,
-                     static_cast<uint32_t>(sg.row_bytes), &full_bar[s]);
+        const uint8_t *src = sg.w + static_cast<int64_t>(row0) * sg.row_bytes;
+        if (!quant_type(sg.w_type)) {
+            if (lane == 0) bulk_g2s(smem + s * p.slot_bytes, src, static_cast<uint32_t>(rows * sg.row_bytes), &full_bar[s]);
+        } else if (2 * lane < rows) {
+            const int nr = min(2, rows - 2 * lane);
+            bulk_g2s(smem + s * p.slot_bytes + lane * sg.sstride, src + static_cast<int64_t>(2 * lane) * sg.row_bytes,
+                     static_cast<uint32_t>(nr * sg.row_bytes), &full_bar[s]);
+        }
     };
     // the weights are constants of the model: stream them before the dependency wait
     if (warp == 0)
@@ -476,8 +487,8 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
                 break;
             }
             const MmSeg &sg = p.seg[seg_of(p, tile0 + it)];
-            const uint8_t *rg = smem + s * p.slot_bytes + g * sg.sstride;
-            const uint8_t *rg8 = rg + 8 * sg.sstride;
+            const uint8_t *rg = smem + s * p.slot_bytes + g * sg.sstride;  // tile row 2g: MMA row g
+            const uint8_t *rg8 = rg + sg.row_bytes;                           // tile row 2g + 1: MMA row g + 8
             const int wt = sg.w_type;
             float y0 = 0.f, y1 = 0.f;
             for (int u = warp; u < n_units; u += kMmWarps) {
@@ -515,7 +526,8 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
             ok = false;
             break;
         }
-        // the group's outputs (tile, row r, token n): lane 4 (r % 8) + n, component r / 8
+        // the group's outputs (tile, MMA row r, token n): lane 4 (r % 8) + n, component r / 8;
+        // MMA row r is tile row 2 (r % 8) + r / 8 of a quantised tile, row r of a float tile
         for (int o = threadIdx.x; o < (ge - gb) * kTcRows * NT; o += kMmThreads) {
             const int tl = o / (kTcRows * NT), rem = o % (kTcRows * NT), r = rem / NT, n = rem % NT;
             const int ln = 4 * (r & 7) + n;
@@ -527,7 +539,8 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
             }
             const int t = tile0 + gb + tl;
             const MmSeg &sg = p.seg[seg_of(p, t)];
-            const int row = (t - sg.tile0) * sg.rows + r;
+            const int tr = quant_type(sg.w_type) ? 2 * (r & 7) + (r >> 3) : r;
+            const int row = (t - sg.tile0) * sg.rows + tr;
             if (r < sg.rows && row < sg.n_out && n < p.n_tok) sg.y[static_cast<int64_t>(n) * sg.y_stride + row] = acc;
         }
         __syncthreads();  // the partial sums' space is reused by the next group
@@ -568,8 +581,6 @@ int launch_mm(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
     static std::atomic<uint64_t> attr_devices{0};
     return launch_pdl(mul_mat_kernel<NT>, attr_devices, p, grid, smem, st);
 }
-
-bool tc_type(int t) { return t == SQMIX_Q4_K || t == SQMIX_Q6_K || t == SQMIX_Q8_0; }
 
 int64_t row_bytes_of(int32_t w_type, int64_t n_in) {
     const int ub = unit_bytes(w_type);
@@ -627,12 +638,12 @@ extern "C" int sqmix_mul_mat_group(const sqmix_mul_mat_args *args, int32_t n, sq
     int64_t max_float_rb = 0;
     for (int i = 0; i < n; ++i) {
         const int64_t rb = row_bytes_of(args[i].w_type, args[i].n_in);
-        if (tc_type(args[i].w_type))
-            max_sstride = std::max(max_sstride, static_cast<int>((rb / 4) % 8 == 0 ? rb + 16 : rb));  // rb / 4: 0 or 4 mod 8
+        if (quant_type(args[i].w_type))
+            max_sstride = std::max(max_sstride, static_cast<int>(2 * rb + 16));
         else
             max_float_rb = std::max(max_float_rb, rb);
     }
-    p.slot_bytes = static_cast<int>(std::max<int64_t>(max_sstride > 0 ? kTcRows * max_sstride : kFloatSlot, max_float_rb));
+    p.slot_bytes = static_cast<int>(std::max<int64_t>(max_sstride > 0 ? kTcRows / 2 * max_sstride : kFloatSlot, max_float_rb));
     p.slot_bytes = (p.slot_bytes + 127) / 128 * 128;
     for (int i = 0; i < n; ++i) {
         const int64_t rb = row_bytes_of(args[i].w_type, args[i].n_in);
@@ -643,9 +654,9 @@ extern "C" int sqmix_mul_mat_group(const sqmix_mul_mat_args *args, int32_t n, sq
         sg.row_bytes = static_cast<int>(rb);
         sg.n_out = static_cast<int>(args[i].n_out);
         sg.tile0 = p.n_tiles;
-        if (tc_type(sg.w_type)) {
+        if (quant_type(sg.w_type)) {
             sg.rows = kTcRows;
-            sg.sstride = static_cast<int>((rb / 4) % 8 == 0 ? rb + 16 : rb);
+            sg.sstride = static_cast<int>(2 * rb + 16);  // rb / 4 is 0 or 4 mod 8: sstride / 4 is 4 mod 8
         } else {
             sg.rows = static_cast<int>(std::min<int64_t>(kTcRows, p.slot_bytes / rb));
             sg.sstride = sg.row_bytes;
