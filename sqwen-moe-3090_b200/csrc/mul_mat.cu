@@ -24,9 +24,9 @@
 namespace sqmix {
 namespace {
 
-constexpr int kMmWarps = 8;
-constexpr int kMmThreads = kMmWarps * 32;
-constexpr int kMmCtasPerSm = 2;       // CTAs per SM the registers are budgeted for
+// A CTA has W = 8 warps (two CTAs per SM) or, for 16 or more units per row, W = 16 (one
+// CTA per SM, one unit per warp); either way at most 128 registers a thread.
+constexpr int kMmRegThreads = 512;    // threads per SM the registers are budgeted for
 constexpr int kMaxIn = 4096;          // n_in limit (the model's 2048 and 4096)
 constexpr int kMaxPassTokens = 4;     // tokens per stream of W
 constexpr int kMaxStages = 8;
@@ -341,18 +341,18 @@ __device__ __forceinline__ void unit_float(const uint8_t *slot, int sstride, int
 }
 
 // shared memory of mul_mat_tc_kernel after its ring
-__host__ __device__ constexpr size_t tc_extra_bytes(int nt, int n_in, bool has_float) {
+__host__ __device__ constexpr size_t tc_extra_bytes(int nt, int w, int n_in, bool has_float) {
     return static_cast<size_t>(n_in / 16) * 2 * nt * 4 * 8 +                 // B fragments
            (has_float ? static_cast<size_t>(nt) * n_in * 4 : 0) +             // x in f32
            static_cast<size_t>(nt) * (n_in / 16 + 4) * 4 +                    // 16-value sums
            static_cast<size_t>(nt) * (n_in / 32 + 4) * 4 +                    // 32-value sums
-           static_cast<size_t>(kMmWarps) * 8 * kTabStride * 4 +               // scale tables
-           static_cast<size_t>(kTcGroup) * kMmWarps * 32 * 8 +                // partial sums
+           static_cast<size_t>(w) * 8 * kTabStride * 4 +                      // scale tables
+           static_cast<size_t>(kTcGroup) * w * 32 * 8 +                       // partial sums
            2 * kMaxStages * sizeof(uint64_t) + kMaxStages * sizeof(int) + 16;  // barriers
 }
 
-template <int NT>
-__global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const __grid_constant__ MmParams p) {
+template <int NT, int W>
+__global__ void __launch_bounds__(W * 32, kMmRegThreads / (W * 32)) mul_mat_kernel(const __grid_constant__ MmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int ring_bytes = p.n_stages * p.slot_bytes;
     const int n_units = p.n_in / 256;
@@ -363,8 +363,8 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
     float *xs16 = xf + (p.has_float ? NT * p.n_in : 0);                        // [NT][xs16_st]
     float *xs32 = xs16 + NT * xs16_st;                                         // [NT][xs32_st]
     float *tab_all = xs32 + NT * xs32_st;                                      // [8 warps][8][kTabStride]
-    float2 *red = reinterpret_cast<float2 *>(tab_all + kMmWarps * 8 * kTabStride);  // [kTcGroup][8][32]
-    uint64_t *full_bar = reinterpret_cast<uint64_t *>(red + kTcGroup * kMmWarps * 32);
+    float2 *red = reinterpret_cast<float2 *>(tab_all + W * 8 * kTabStride);   // [kTcGroup][W][32]
+    uint64_t *full_bar = reinterpret_cast<uint64_t *>(red + kTcGroup * W * 32);
     uint64_t *empty_bar = full_bar + kMaxStages;
     int *rel_cnt = reinterpret_cast<int *>(empty_bar + kMaxStages);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.n_stages; ++s) {
             mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], kMmWarps);
+            mbar_init(&empty_bar[s], W);
             rel_cnt[s] = 0;
         }
         fence_mbar_init();
@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
                        ((reinterpret_cast<uintptr_t>(p.x) | static_cast<uintptr_t>(p.x_stride * 4)) & 15) == 0;
     // x -> the B fragments and slice sums of this warp's units (no other warp reads them):
     // entry (slice l of unit u, token t, lane c) covers x values 16 (16 u + l) + 4 c .. + 3
-    for (int u = warp; u < n_units; u += kMmWarps) {
+    for (int u = warp; u < n_units; u += W) {
         constexpr int kE = 2 * NT;  // 64 NT entries per unit
         float v[kE][4];
 #pragma unroll
@@ -491,7 +491,7 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
             const uint8_t *rg8 = rg + sg.row_bytes;                           // tile row 2g + 1: MMA row g + 8
             const int wt = sg.w_type;
             float y0 = 0.f, y1 = 0.f;
-            for (int u = warp; u < n_units; u += kMmWarps) {
+            for (int u = warp; u < n_units; u += W) {
                 if (wt == SQMIX_Q4_K)
                     unit_q4k<NT>(rg, rg8, u, g, c, bf, xs32, xs32_st, tab, y0, y1);
                 else if (wt == SQMIX_Q6_K)
@@ -502,13 +502,13 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
                     unit_float<NT>(smem + s * p.slot_bytes, sg.sstride, min(sg.rows, sg.n_out - (tile0 + it - sg.tile0) * sg.rows),
                                    wt, u, lane, xf, p.n_in, g, c, y0, y1);
             }
-            red[((it - gb) * kMmWarps + warp) * 32 + lane] = make_float2(y0, y1);
+            red[((it - gb) * W + warp) * 32 + lane] = make_float2(y0, y1);
             // release the slot; the warp that releases it last refills it
             __syncwarp();
             int last = 0;
             if (lane == 0) {
                 mbar_arrive(&empty_bar[s]);
-                last = atomicAdd(&rel_cnt[s], 1) == kMmWarps - 1;
+                last = atomicAdd(&rel_cnt[s], 1) == W - 1;
                 if (last) rel_cnt[s] = 0;
             }
             last = __shfl_sync(0xffffffffu, last, 0);
@@ -528,13 +528,13 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
         }
         // the group's outputs (tile, MMA row r, token n): lane 4 (r % 8) + n, component r / 8;
         // MMA row r is tile row 2 (r % 8) + r / 8 of a quantised tile, row r of a float tile
-        for (int o = threadIdx.x; o < (ge - gb) * kTcRows * NT; o += kMmThreads) {
+        for (int o = threadIdx.x; o < (ge - gb) * kTcRows * NT; o += W * 32) {
             const int tl = o / (kTcRows * NT), rem = o % (kTcRows * NT), r = rem / NT, n = rem % NT;
             const int ln = 4 * (r & 7) + n;
             float acc = 0.f;
 #pragma unroll
-            for (int wv = 0; wv < kMmWarps; ++wv) {
-                const float2 q2 = red[(tl * kMmWarps + wv) * 32 + ln];
+            for (int wv = 0; wv < W; ++wv) {
+                const float2 q2 = red[(tl * W + wv) * 32 + ln];
                 acc += r < 8 ? q2.x : q2.y;
             }
             const int t = tile0 + gb + tl;
@@ -557,7 +557,7 @@ __global__ void __launch_bounds__(kMmThreads, kMmCtasPerSm) mul_mat_kernel(const
 }
 
 template <typename K>
-int launch_pdl(K kernel, std::atomic<uint64_t> &attr_devices, const MmParams &p, int grid, size_t smem,
+int launch_pdl(K kernel, std::atomic<uint64_t> &attr_devices, const MmParams &p, int grid, int threads, size_t smem,
                cudaStream_t st) {
     {
         const cudaError_t e = set_smem_once(attr_devices, kernel, 227 * 1024);
@@ -568,7 +568,7 @@ int launch_pdl(K kernel, std::atomic<uint64_t> &attr_devices, const MmParams &p,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kMmThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cfg.attrs = attr;
@@ -576,10 +576,17 @@ int launch_pdl(K kernel, std::atomic<uint64_t> &attr_devices, const MmParams &p,
     return cuda_status(cudaLaunchKernelEx(&cfg, kernel, p), "mul_mat launch");
 }
 
-template <int NT>
+template <int NT, int W>
 int launch_mm(const MmParams &p, int grid, size_t smem, cudaStream_t st) {
     static std::atomic<uint64_t> attr_devices{0};
-    return launch_pdl(mul_mat_kernel<NT>, attr_devices, p, grid, smem, st);
+    return launch_pdl(mul_mat_kernel<NT, W>, attr_devices, p, grid, W * 32, smem, st);
+}
+
+template <int W>
+int launch_mm_nt(int NT, const MmParams &p, int grid, size_t smem, cudaStream_t st) {
+    return NT == 1 ? launch_mm<1, W>(p, grid, smem, st)
+           : NT == 2 ? launch_mm<2, W>(p, grid, smem, st)
+                     : launch_mm<4, W>(p, grid, smem, st);
 }
 
 int64_t row_bytes_of(int32_t w_type, int64_t n_in) {
@@ -671,8 +678,9 @@ extern "C" int sqmix_mul_mat_group(const sqmix_mul_mat_args *args, int32_t n, sq
     p.x_dtype = a0.x_dtype;
     p.x_stride = a0.x_stride;
     p.status = a0.status;
-    // as many CTAs per SM (up to kMmCtasPerSm) as leave room for a ring of at least 2
-    // slots beside the rest: more warps to hide the latency of the dequant / MMA chains
+    // 16 warps (one per unit) for rows of 16 or more units when a ring of 2 slots fits
+    // beside the rest, else 8; as many CTAs per SM as the registers allow and leave room
+    // for a ring of at least 2 slots
     auto smem_budget = [](int ctas) { return static_cast<size_t>(228 * 1024 / ctas - 1024); };
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int elt = a0.x_dtype == SQMIX_F32 ? 4 : 2;
@@ -683,8 +691,13 @@ extern "C" int sqmix_mul_mat_group(const sqmix_mul_mat_args *args, int32_t n, sq
         q.x = static_cast<const uint8_t *>(a0.x) + static_cast<int64_t>(t0) * a0.x_stride * elt;
         q.n_tok = nt;
         for (int s = 0; s < q.n_seg; ++s) q.seg[s].y = args[s].y + static_cast<int64_t>(t0) * q.seg[s].y_stride;
-        const size_t extra = tc_extra_bytes(NT, q.n_in, q.has_float != 0);
-        int ctas = kMmCtasPerSm;
+        const int W = q.n_in / 256 >= 16 &&
+                              tc_extra_bytes(NT, 16, q.n_in, q.has_float != 0) + 2 * static_cast<size_t>(q.slot_bytes) <=
+                                  227 * 1024
+                          ? 16
+                          : 8;
+        const size_t extra = tc_extra_bytes(NT, W, q.n_in, q.has_float != 0);
+        int ctas = kMmRegThreads / (W * 32);
         while (ctas > 1 && extra + 2 * static_cast<size_t>(q.slot_bytes) > smem_budget(ctas)) --ctas;
         const size_t budget = std::min<size_t>(smem_budget(ctas), 227 * 1024);
         if (extra + 2 * static_cast<size_t>(q.slot_bytes) > budget)
@@ -692,9 +705,7 @@ extern "C" int sqmix_mul_mat_group(const sqmix_mul_mat_args *args, int32_t n, sq
         q.n_stages = static_cast<int>(std::min<size_t>(kMaxStages, (budget - extra) / q.slot_bytes));
         const size_t smem = static_cast<size_t>(q.n_stages) * q.slot_bytes + extra;
         const int grid = std::min(q.n_tiles, ctas * sms);
-        const int rc = NT == 1 ? launch_mm<1>(q, grid, smem, st)
-                       : NT == 2 ? launch_mm<2>(q, grid, smem, st)
-                                 : launch_mm<4>(q, grid, smem, st);
+        const int rc = W == 16 ? launch_mm_nt<16>(NT, q, grid, smem, st) : launch_mm_nt<8>(NT, q, grid, smem, st);
         if (rc != SQMIX_OK) return rc;
     }
     return SQMIX_OK;
