@@ -1347,17 +1347,18 @@ def run_profile_case(case: str):
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev)
     g.manual_seed(7)
-    if case == "fa":
+    if case in ("fa", "fa2"):  # decode at 172K keys; fa2: the n_q = 2 MTP verification
+        nq = 2 if case == "fa2" else 1
         kc, vc = sqmix.new_kv_cache(N_KV), sqmix.new_kv_cache(N_KV)
         for a in range(0, N_KV, 16384):
             n = min(16384, N_KV - a)
             sqmix.set_rows_q4_0(torch.randn((n, 2, 256), generator=g, device=dev),
                                 torch.randn((n, 2, 256), generator=g, device=dev),
                                 torch.arange(a, a + n, device=dev), kc, vc, N_KV)
-        q = torch.randn((1, N_HEAD, HEAD_DIM), generator=g, device=dev)
-        gate = torch.randn((1, N_HEAD, HEAD_DIM), generator=g, device=dev)
-        d = torch.tensor([N_KV, N_KV - 1], dtype=torch.int64, device=dev)
-        ws = sqmix.new_fa_workspace(1, 0, dev)
+        q = torch.randn((nq, N_HEAD, HEAD_DIM), generator=g, device=dev)
+        gate = torch.randn((nq, N_HEAD, HEAD_DIM), generator=g, device=dev)
+        d = torch.tensor([N_KV, N_KV - nq], dtype=torch.int64, device=dev)
+        ws = sqmix.new_fa_workspace(nq, 0, dev)
         for _ in range(3):
             sqmix.flash_attn_ext(q, kc, vc, N_KV, d[0:1], d[1:2], gate=gate, rope_n_rot=N_ROT,
                                  rope_freq_base=FREQ_BASE, workspace=ws)
@@ -1435,7 +1436,7 @@ def main():
     ap.add_argument("--headline-only", action="store_true",
                     help="config 3 only (skip configs 0, 1, 2 and 4)")
     ap.add_argument("--nccl-merge", action="store_true", help="N > 1: all-gather + merge instead of the peer merge")
-    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | pf | gdn | gdnb | gdnp | gdnl | mm) and exit")
+    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | fa2 | pf | gdn | gdnb | gdnp | gdnl | mm) and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)

@@ -20,7 +20,7 @@ OUT = os.path.join(HERE, "sqmix", "libsqmix.so")
 INCLUDE = os.path.join(REPO, "include")
 
 SOURCES = ["host.cpp", "abi.cpp", "ggml_bridge.cpp", "kv_append.cu", "fa_decode.cu", "fa_prefill.cu", "gdn.cu", "gdn_chunk.cu", "gdn_front.cu",
-           "gdn_layer.cu", "peer_merge.cu", "mul_mat.cu"]
+           "gdn_layer.cu", "peer_merge.cu", "mul_mat.cu", "mul_mat_gemm.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", INCLUDE, "-I", CSRC,
          "--expt-relaxed-constexpr"]

@@ -22,6 +22,11 @@
 #include "sqmix.h"
 
 namespace sqmix {
+// the prefill form (mul_mat_gemm.cu) for a validated group; its 128 x 128 output tiles
+// (0: x not usable by the form)
+int mul_mat_gemm_launch(const sqmix_mul_mat_args *args, int n, cudaStream_t st);
+int mul_mat_gemm_tiles(const sqmix_mul_mat_args *args, int n);
+
 namespace {
 
 // A CTA has W = 8 warps (two CTAs per SM) or, for 16 or more units per row, W = 16 (one
@@ -29,6 +34,12 @@ namespace {
 constexpr int kMmRegThreads = 512;    // threads per SM the registers are budgeted for
 constexpr int kMaxIn = 4096;          // n_in limit (the model's 2048 and 4096)
 constexpr int kMaxPassTokens = 4;     // tokens per stream of W
+// The tensor-core GEMM form (mul_mat_gemm.cu) takes n_tokens >= kGemmTokens, or >=
+// kGemmMinTokens when its tiles fill at least kGemmMinTiles of the grid (measured
+// crossovers against ceil(n_tokens / 4) passes of the decode form)
+constexpr int kGemmTokens = 128;
+constexpr int kGemmMinTokens = 48;
+constexpr int kGemmMinTiles = 48;
 constexpr int kMaxStages = 8;
 constexpr int kFloatSlot = 16 * 1024; // slot bytes of a launch of float-typed weights only
 constexpr int kMaxSeg = SQMIX_MUL_MAT_MAX_GROUP;
@@ -638,6 +649,11 @@ extern "C" int sqmix_mul_mat_group(const sqmix_mul_mat_args *args, int32_t n, sq
                             args[i].n_tokens == a0.n_tokens && args[i].n_in == a0.n_in,
                         "mul_mat_group: entry %d does not share x (pointer, dtype, stride, n_tokens, n_in) with entry 0",
                         i);
+    if (a0.n_tokens >= kGemmMinTokens) {  // the GEMM form needs x rows 16-byte aligned (tiles 0 otherwise)
+        const int tiles = mul_mat_gemm_tiles(args, n);
+        if (tiles > 0 && (a0.n_tokens >= kGemmTokens || tiles >= kGemmMinTiles))
+            return mul_mat_gemm_launch(args, n, reinterpret_cast<cudaStream_t>(stream));
+    }
     // the launch's tile list: the projections in call order, 16-row tiles for the
     // quantised formats, float-typed rows as many as fit the slot (up to 16)
     MmParams p = {};

@@ -156,3 +156,67 @@ def test_mul_mat_group_bf16_x_4096_inputs(oracle):
     for (wt, n_out), r, g in zip(specs, rows, got):
         want = oracle.mul_mat(r, wt, n_in, x.float().numpy())
         assert rel_err(g.cpu().numpy(), want.astype(np.float64)) <= TOL, (wt, n_out)
+
+
+# The prefill form (n_tokens >= 128, or >= 48 with at least 48 output tiles of 128 x
+# 128): a tcgen05 GEMM on f16 operands (each dequantised weight and each x value rounded
+# once to f16), f32 accumulation.  Bar: max |gpu - ref| <= 3e-3 * max |ref| against the
+# float64 sums of the exact dequantised weights.
+PREFILL_TOL = 3e-3
+PREFILL_CASES = [
+    (12, 2048, 300, 130, torch.float32),   # ragged weight tile, ragged second token tile
+    (12, 2048, 6144, 48, torch.float32),   # the smallest batch of the form (48 tiles)
+    (14, 2048, 128, 128, torch.bfloat16),  # attn_v's format
+    (8, 4096, 200, 256, torch.float32),
+    (0, 2048, 32, 137, torch.float32),     # the 32-row f32 beta / alpha
+    (30, 2048, 40, 300, torch.float16),
+    (1, 1024, 128, 129, torch.float32),
+    (12, 4096, 512, 512, torch.float32),   # W_o / ssm_out at a pp512 batch
+]
+
+
+@pytest.mark.parametrize("wtype,n_in,n_out,T,xdt", PREFILL_CASES)
+def test_mul_mat_prefill_gemm_vs_oracle(oracle, wtype, n_in, n_out, T, xdt):
+    import sqmix
+
+    rng = np.random.default_rng(2000 + n_out + wtype + T)
+    rows = random_rows(rng, wtype, n_in, n_out)
+    x = torch.randn((T, n_in), generator=torch.Generator().manual_seed(T + n_in)).to(xdt)
+    want = oracle.mul_mat(rows, wtype, n_in, x.float().numpy())
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    y = sqmix.mul_mat(torch.from_numpy(rows).cuda(), wtype, n_in, x.cuda(), status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert rel_err(y.cpu().numpy(), want.astype(np.float64)) <= PREFILL_TOL
+
+
+@pytest.mark.parametrize("x_pad", [8, 3])
+def test_mul_mat_prefill_group_and_strides(oracle, x_pad):
+    """A prefill group (q4_K, q6_K, f32 rows) of one strided x into strided outputs; a pad
+    of 3 floats leaves the rows of x 4-byte aligned only (no tensor-map staging)."""
+    import ctypes
+
+    from sqmix._lib import MulMatArgs, check, lib
+
+    rng = np.random.default_rng(31)
+    n_in, T = 2048, 130
+    specs = [(12, 1000), (14, 512), (0, 32)]
+    rows = [random_rows(rng, wt, n_in, n_out) for wt, n_out in specs]
+    ws = [torch.from_numpy(r).cuda() for r in rows]
+    xw = torch.randn((T, n_in + x_pad), generator=torch.Generator().manual_seed(3)).cuda()
+    ys = [torch.full((T, n_out + 5), 7.0, device="cuda") for _, n_out in specs]
+    import sqmix
+
+    arr = (MulMatArgs * len(specs))()
+    for i, ((wt, n_out), w, y) in enumerate(zip(specs, ws, ys)):
+        arr[i] = MulMatArgs(w=w.data_ptr(), w_type=wt, w_row_bytes=sqmix.mul_mat_row_bytes(wt, n_in), n_in=n_in,
+                            n_out=n_out, x=xw.data_ptr(), x_dtype=0, x_stride=n_in + x_pad, n_tokens=T, y=y.data_ptr(),
+                            y_stride=n_out + 5)
+    check(lib().sqmix_mul_mat_group(arr, len(specs), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+          "mul_mat_group")
+    torch.cuda.synchronize()
+    xh = xw[:, :n_in].cpu().numpy()
+    for (wt, n_out), r, y in zip(specs, rows, ys):
+        got = y.cpu().numpy()
+        assert rel_err(got[:, :n_out], oracle.mul_mat(r, wt, n_in, xh).astype(np.float64)) <= PREFILL_TOL, wt
+        assert (got[:, n_out:] == 7.0).all()
