@@ -559,13 +559,17 @@ int sqmix_head_norm(const sqmix_head_norm_args *args, sqmix_stream_t stream);
  * contiguous rows (w_row_bytes = sqmix_mul_mat_row_bytes(w_type, n_in)) in a GGUF block
  * format -- SQMIX_Q8_0, SQMIX_Q4_K, SQMIX_Q6_K -- or SQMIX_F32 / F16 / BF16 elements;
  * 16-byte aligned, n_in a multiple of 256 up to 4096 (q6_K: a multiple of 2048).  x is
- * f32 / f16 / bf16, y f32.  Dequantised weights times x are summed in f32 (ggml's CUDA
- * backend quantises x to q8_1 for its quantised dot products; this is the more exact
- * form).  Built for decode: each stream of W serves up to 4 tokens, so larger n_tokens
- * read W once per 4 tokens.  The weights are read before the call's dependency on the
- * previous kernel on the stream (programmatic dependent launch): W must not be written
- * by that kernel.  `status` (device, may be NULL) receives bit 1 if a bounded wait of
- * the kernel gave up.
+ * f32 / f16 / bf16, y f32.  Two forms:
+ *   - decode (n_tokens below the prefill threshold): each stream of W serves up to 4
+ *     tokens; dequantised weights times x summed f32-exactly (ggml's CUDA backend
+ *     quantises x to q8_1 for its quantised dot products; this is the more exact form);
+ *   - prefill (n_tokens >= 128, or >= 48 when the call has at least 48 tiles of 128
+ *     rows x 128 tokens; x rows 16-byte aligned): a tensor-core GEMM whose operands are
+ *     tf32 for f32 x (weights and x truncated to a 10-bit mantissa) or x's 16-bit type,
+ *     sums in f32 -- about 1e-3 of max |y|, as ggml's dequantise-to-16-bit GEMM path.
+ * The weights are read before the call's dependency on the previous kernel on the
+ * stream (programmatic dependent launch): W must not be written by that kernel.
+ * `status` (device, may be NULL) receives bit 1 if a bounded wait of the kernel gave up.
  * ------------------------------------------------------------------------ */
 typedef struct sqmix_mul_mat_args {
     const void *w;
