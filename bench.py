@@ -1140,6 +1140,24 @@ def bench_proj(steps: int, warmup: int) -> dict:
 
             us = _graph_us(step_single, 1, max(3, min(steps, 200)), warmup)
             res["T1_single_calls"] = {"calls": len(calls), "us_per_step": us, "frac_of_hbm": wbytes / us / 1e3 / hbm}
+    # a 512-token prefill batch through the same 80 calls: the tensor-core GEMM form
+    T = 512
+    xs = {n: torch.randn((T, n), device=dev) for n in (2048, 4096)}
+    ys = {}
+    for name, _, _, n_out, _ in calls:
+        ys.setdefault(name, torch.empty((T, n_out), device=dev))
+
+    def step_prefill():
+        for groups in layers:
+            for grp in groups:
+                sqmix.mul_mat_group([(w, wt) for _, wt, _, _, w in grp], grp[0][2], xs[grp[0][2]],
+                                    outs=[ys[name] for name, *_ in grp])
+
+    us = _graph_us(step_prefill, 1, max(3, min(steps, 10)), warmup)
+    flop = 2.0 * T * sum(n_in * n_out for _, _, n_in, n_out, _ in calls)
+    res["prefill_T512"] = {"us_per_step": us, "tflops": flop / us / 1e6,
+                           "frac_of_measured_bf16_peak": flop / us / 1e6 / tensor_peak()[0],
+                           "note": "f32 x: tf32 tensor-core operands (half the bf16 rate)"}
     # the largest single projection, alone (QG / qkv: 2048 -> 8192 q4_K)
     x1 = torch.randn((1, 2048), device=dev)
     y1 = torch.empty((1, 8192), device=dev)
