@@ -1437,6 +1437,12 @@ def run_profile_case(case: str):
                    for j, (_, wt, n_in, n_out) in enumerate(PROJ_GDN[:4])] for i in range(3)]
         for grp in groups:
             sqmix.mul_mat_group(grp, 2048, x)
+    elif case == "mmp":  # the same group at a 512-token prefill batch (the tensor-core GEMM form)
+        x = torch.randn((512, 2048), generator=g, device=dev)
+        groups = [[(proj_weights(n_in, n_out, wt, dev, 10 * i + j), wt)
+                   for j, (_, wt, n_in, n_out) in enumerate(PROJ_GDN[:4])] for i in range(3)]
+        for grp in groups:
+            sqmix.mul_mat_group(grp, 2048, x)
     else:
         raise SystemExit(f"unknown profile case {case}")
     torch.cuda.synchronize()
@@ -1454,7 +1460,7 @@ def main():
     ap.add_argument("--headline-only", action="store_true",
                     help="config 3 only (skip configs 0, 1, 2 and 4)")
     ap.add_argument("--nccl-merge", action="store_true", help="N > 1: all-gather + merge instead of the peer merge")
-    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | fa2 | pf | gdn | gdnb | gdnp | gdnl | mm) and exit")
+    ap.add_argument("--profile", default=None, help="run a small ncu case (fa | fa2 | pf | gdn | gdnb | gdnp | gdnl | mm | mmp) and exit")
     args = ap.parse_args()
     if args.profile:
         run_profile_case(args.profile)
