@@ -41,21 +41,25 @@ namespace {
 constexpr int kGM = 128;            // weight rows per item (MMA M)
 constexpr int kGN = 128;            // tokens per item (MMA N)
 constexpr int kGK = 64;             // contraction values per stage
-constexpr int kGStages = 4;         // stages in flight (weight columns and x slots)
-constexpr int kGPrefetch = 4;       // stages of weight bytes requested into L2 ahead
+constexpr int kGStages = 3;         // stages in flight (weight columns and x slots)
+constexpr int kGWDepth = 3;         // weight boxes in flight
 constexpr int kGWarps = 12;
 constexpr int kGThreads = kGWarps * 32;
 constexpr int kGProdWarp0 = 4;
 constexpr int kGProdWarps = 8;
 constexpr int kGMaxSeg = SQMIX_MUL_MAT_MAX_GROUP;
 constexpr int kGXSlot = kGN * kGK * 4;   // 32 KB: one stage of x (f32: two 16 KB boxes; 16-bit: one)
-constexpr int kGBarOff = kGStages * kGXSlot;
-constexpr int kGSmem = kGBarOff + 256 + 1024;  // + slack for the 1024-byte alignment of the ring
+constexpr int kGWBoxMax = 272;          // bytes of a weight row in one weight box (q8_0's unit)
+constexpr int kGWSlot = kGM * kGWBoxMax;  // one weight box of 128 rows
+constexpr int kGWOff = kGStages * kGXSlot;
+constexpr int kGBarOff = kGWOff + kGWDepth * kGWSlot;
+constexpr int kGSmem = kGBarOff + 256 + 1024;  // + slack for the 1024-byte alignment of the rings
 // tensor memory: the accumulator (128 columns), then kGStages stages of 64 weight columns
 constexpr uint32_t kGTmemCols = 512;
 constexpr uint32_t kGAcol0 = kGN;
 
 struct GemmSeg {
+    CUtensorMap wmap;  // the weight rows in boxes of 128 rows (one unit of 256 values, or one stage of float rows)
     const uint8_t *w;
     float *y;
     int64_t y_stride;
@@ -64,6 +68,7 @@ struct GemmSeg {
     int n_out;
     int item0;    // first item of the projection
     int m_tiles;  // ceil(n_out / kGM)
+    int box_rows; // rows of a weight box: min(kGM, n_out)
 };
 
 struct GemmParams {
@@ -75,77 +80,73 @@ struct GemmParams {
     uint32_t *status;
 };
 
-__device__ __forceinline__ uint4 ldg_nc4(const void *p) {
-    uint4 r;
-    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-    return r;
-}
-__device__ __forceinline__ uint32_t ldg_nc(const void *p) {
-    uint32_t r;
-    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
-    return r;
-}
 __device__ __forceinline__ float f16_bits(uint32_t h) { return __half2float(__ushort_as_half(static_cast<unsigned short>(h))); }
 // An integer 0 <= q < 2^23 (the low bits of w selected by mask after a shift) as a float,
 // exactly, on the integer and FMA pipes: 2^23 + q has q as its mantissa.
 __device__ __forceinline__ float small_int_f32(uint32_t bits) { return __uint_as_float(0x4B000000u | bits) - 8388608.0f; }
 
-// The producers work one stage ahead: the raw weight words of stage k + 1 are loaded into
-// registers before stage k is converted, so that the load latency overlaps the work.
-// Raw weights of 32 consecutive values k0 .. k0 + 31 (k0 % 32 == 0) of row `wr`:
+// Raw weight words of 32 consecutive values k0 .. k0 + 31 (k0 % 32 == 0) of a row:
 //   q4_K: [0..3] the unit's 16-byte header, [4..11] the 32 nibble bytes;
 //   q6_K: [0..8] ql and [9..17] qh as the aligned words covering them, [18] the word
 //         holding d, [19] the word holding the two int8 scales;
 //   q8_0: [0..8] the aligned words covering the 32 int8, [9] the word holding d;
 //   f32:  [0..31]; f16 / bf16: [0..15].
-__device__ __forceinline__ const uint32_t *aligned_word(const uint8_t *p) {
+// A weight box: 128 rows x wbox_bytes(type) bytes, covering `spb` stages of 64 values
+// (a 256-value unit of the block formats -- q6_K's unit at its 16-byte-aligned start
+// below -- or one stage of float rows)
+__host__ __device__ constexpr int wbox_bytes(int t) {
+    return t == SQMIX_Q4_K ? 144 : t == SQMIX_Q6_K ? 224 : t == SQMIX_Q8_0 ? 272 : t == SQMIX_F32 ? 256 : 128;
+}
+__host__ __device__ constexpr int wbox_stages(int t) { return t == SQMIX_F32 || t == SQMIX_F16 || t == SQMIX_BF16 ? 1 : 4; }
+
+// The raw words of 32 consecutive values k0 .. k0 + 31 of a row whose current weight box
+// starts at `rb` in shared memory
+__device__ __forceinline__ const uint32_t *sm_word(const uint8_t *p) {
     return reinterpret_cast<const uint32_t *>(reinterpret_cast<uintptr_t>(p) & ~static_cast<uintptr_t>(3));
 }
-__device__ __forceinline__ void load_w32(const uint8_t *wr, int wt, int k0, uint32_t (&r)[32]) {
+__device__ __forceinline__ void load_w32s(const uint8_t *rb, int wt, int k0, uint32_t (&r)[32]) {
     if (wt == SQMIX_Q4_K) {
-        const int u = k0 >> 8, j = (k0 >> 5) & 7;
-        const uint8_t *ub = wr + u * 144;
-        const uint4 h = ldg_nc4(ub), q0 = ldg_nc4(ub + 16 + 32 * (j >> 1)), q1 = ldg_nc4(ub + 32 + 32 * (j >> 1));
+        const int j = (k0 >> 5) & 7;
+        const uint4 h = *reinterpret_cast<const uint4 *>(rb);
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(rb + 16 + 32 * (j >> 1));
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(rb + 32 + 32 * (j >> 1));
         r[0] = h.x, r[1] = h.y, r[2] = h.z, r[3] = h.w;
         r[4] = q0.x, r[5] = q0.y, r[6] = q0.z, r[7] = q0.w, r[8] = q1.x, r[9] = q1.y, r[10] = q1.z, r[11] = q1.w;
     } else if (wt == SQMIX_Q6_K) {
         const int u = k0 >> 8, i0 = k0 & 255, hh = i0 >> 7, kq = (i0 & 127) >> 5;
-        const uint8_t *ub = wr + u * 210;
-        const uint32_t *ql = aligned_word(ub + 64 * hh + 32 * (kq & 1)), *qh = aligned_word(ub + 128 + 32 * hh);
-        const bool mis = u & 1;  // u * 210 = 2 mod 4 for odd u
+        const uint8_t *ub = rb + ((210 * u) & 15);  // the unit inside its 16-byte-aligned box
+        const uint32_t *ql = sm_word(ub + 64 * hh + 32 * (kq & 1)), *qh = sm_word(ub + 128 + 32 * hh);
 #pragma unroll
         for (int i = 0; i < 9; ++i) {
-            r[i] = i < 8 || mis ? ldg_nc(ql + i) : 0u;
-            r[9 + i] = i < 8 || mis ? ldg_nc(qh + i) : 0u;
+            r[i] = ql[i];
+            r[9 + i] = qh[i];
         }
-        r[18] = ldg_nc(aligned_word(ub + 208));
-        r[19] = ldg_nc(aligned_word(ub + 192 + 8 * hh + 2 * kq));
+        r[18] = *sm_word(ub + 208);
+        r[19] = *sm_word(ub + 192 + 8 * hh + 2 * kq);
     } else if (wt == SQMIX_Q8_0) {
-        const int b = k0 >> 5;
-        const uint8_t *bb = wr + b * 34;
-        const uint32_t *q = aligned_word(bb + 2);
-        const bool mis = !(b & 1);  // b * 34 + 2 = 2 mod 4 for even b
+        const uint8_t *bb = rb + 34 * ((k0 >> 5) & 7);
+        const uint32_t *q = sm_word(bb + 2);
 #pragma unroll
-        for (int i = 0; i < 9; ++i) r[i] = i < 8 || mis ? ldg_nc(q + i) : 0u;
-        r[9] = ldg_nc(aligned_word(bb));
+        for (int i = 0; i < 9; ++i) r[i] = q[i];
+        r[9] = *sm_word(bb);
     } else if (wt == SQMIX_F32) {
-        const uint8_t *fp = wr + static_cast<int64_t>(k0) * 4;
+        const uint4 *f = reinterpret_cast<const uint4 *>(rb + 4 * (k0 & 63));
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const uint4 a = ldg_nc4(fp + 16 * i);
+            const uint4 a = f[i];
             r[4 * i] = a.x, r[4 * i + 1] = a.y, r[4 * i + 2] = a.z, r[4 * i + 3] = a.w;
         }
     } else {
-        const uint8_t *hp = wr + static_cast<int64_t>(k0) * 2;
+        const uint4 *f = reinterpret_cast<const uint4 *>(rb + 2 * (k0 & 63));
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint4 a = ldg_nc4(hp + 16 * i);
+            const uint4 a = f[i];
             r[4 * i] = a.x, r[4 * i + 1] = a.y, r[4 * i + 2] = a.z, r[4 * i + 3] = a.w;
         }
     }
 }
 
-// The raw words of load_w32 as 32 f32 values (K order), each computed as ggml
+// The raw words of load_w32s as 32 f32 values (K order), each computed as ggml
 // dequantises it
 __device__ __forceinline__ void conv_w32(const uint32_t (&r)[32], int wt, int k0, float (&v)[32]) {
     if (wt == SQMIX_Q4_K) {
@@ -230,12 +231,15 @@ __host__ __device__ constexpr uint32_t idesc_tf32_f32(int m, int n) {
 __global__ void __launch_bounds__(kGThreads, 1) mul_mat_gemm_kernel(const __grid_constant__ GemmParams p) {
     extern __shared__ uint8_t gsm_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t *ring_x = sm;  // kGStages slots of x boxes
+    uint8_t *ring_x = sm;           // kGStages slots of x boxes
+    uint8_t *ring_w = sm + kGWOff;  // kGWDepth slots of weight boxes
     uint64_t *afull = reinterpret_cast<uint64_t *>(sm + kGBarOff);  // weight columns stored (producer warps)
     uint64_t *xfull = afull + kGStages;                              // x boxes landed (transaction bytes)
     uint64_t *sempty = xfull + kGStages;                             // the stage's MMAs are done
     uint64_t *done = sempty + kGStages;                              // an item's MMAs are done
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    uint64_t *wfull = done + 1;                                      // weight boxes landed
+    uint64_t *wempty = wfull + kGWDepth;                             // weight boxes converted (producer warps)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(wempty + kGWDepth);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool f32x = p.x_dtype == SQMIX_F32;
@@ -247,6 +251,10 @@ __global__ void __launch_bounds__(kGThreads, 1) mul_mat_gemm_kernel(const __grid
             mbar_init(&sempty[s], 1);
         }
         mbar_init(done, 1);
+        for (int s = 0; s < kGWDepth; ++s) {
+            mbar_init(&wfull[s], 1);
+            mbar_init(&wempty[s], kGProdWarps);
+        }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -263,6 +271,8 @@ __global__ void __launch_bounds__(kGThreads, 1) mul_mat_gemm_kernel(const __grid
     bool ok = true;
     int done_phase = 0;
     int x_issued = 0;  // global stages whose x boxes were requested (warp 1, lane 0)
+    int w_issued = 0;  // weight boxes requested (warp 2, lane 0)
+    int wblk0 = 0;     // weight boxes of the items before this one (every thread counts them)
     for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
         int si = 0;
         while (si + 1 < p.n_seg && item >= p.seg[si + 1].item0) ++si;
@@ -271,26 +281,31 @@ __global__ void __launch_bounds__(kGThreads, 1) mul_mat_gemm_kernel(const __grid
         const int m0 = (rel / p.t_tiles) * kGM, t0 = (rel % p.t_tiles) * kGN;
         // stage counter continues across items: stage k of this item is ring use g0 + k
         const int g0 = ((item - blockIdx.x) / gridDim.x) * n_k;
+        const int spb = wbox_stages(sg.w_type), wbytes = wbox_bytes(sg.w_type);
         if (warp >= kGProdWarp0) {
             const int q = warp & 3, h = (warp - kGProdWarp0) >> 2;
             const int r = 32 * q + lane;
-            const bool row_ok = m0 + r < sg.n_out;
-            const uint8_t *wr = sg.w + static_cast<int64_t>(row_ok ? m0 + r : 0) * sg.row_bytes;
-            const int64_t wstage = static_cast<int64_t>(sg.row_bytes) * kGK / p.n_in;  // weight bytes of a stage
             const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
-            // one stage: dequantise the raw words `rw` (loaded a stage ahead) and store them
-            // into the stage's weight columns once the MMAs of their previous use are done
-            auto stage = [&](int kc, const uint32_t (&rw)[32]) -> bool {
+            for (int kc = 0; kc < n_k; ++kc) {
                 const int gs = g0 + kc, s = gs % kGStages;
+                const int gb = wblk0 + kc / spb, ws = gb % kGWDepth;
+                if (kc % spb == 0 && !*abort_flag && !mbar_wait(&wfull[ws], (gb / kGWDepth) & 1)) *abort_flag = 1;
+                if (*abort_flag) break;
                 float v[32];
-                if (row_ok) {
-                    conv_w32(rw, sg.w_type, kc * kGK + 32 * h, v);
+                if (r < sg.box_rows) {
+                    uint32_t raw[32];
+                    load_w32s(ring_w + ws * kGWSlot + r * wbytes, sg.w_type, kc * kGK + 32 * h, raw);
+                    conv_w32(raw, sg.w_type, kc * kGK + 32 * h, v);
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] = 0.f;
                 }
+                if (kc % spb == spb - 1) {  // the box is converted: release it to the issuer
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&wempty[ws]);
+                }
                 if (gs >= kGStages && !*abort_flag && !mbar_wait(&sempty[s], ((gs / kGStages) - 1) & 1)) *abort_flag = 1;
-                if (*abort_flag) return false;
+                if (*abort_flag) break;
                 tc::fence_after();
                 const uint32_t col = tmem + lane_base + kGAcol0 + s * kGK;
                 if (f32x) {
@@ -315,29 +330,6 @@ __global__ void __launch_bounds__(kGThreads, 1) mul_mat_gemm_kernel(const __grid
                 tc::fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&afull[s]);
-                return true;
-            };
-            // the weight bytes of stage kc + kGPrefetch into L2
-            auto prefetch_w = [&](int kc) {
-                if (row_ok && h == 0 && kc + kGPrefetch < n_k) {
-                    const uint8_t *pf = wr + (kc + kGPrefetch) * wstage;
-                    for (int64_t o = 0; o < wstage; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(pf + o));
-                }
-            };
-            if (row_ok && h == 0)
-                for (int k = 0; k < kGPrefetch && k < n_k; ++k)
-                    for (int64_t o = 0; o < wstage; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(wr + k * wstage + o));
-            // weight words a stage ahead in two register sets, used alternately
-            uint32_t wa[32], wb[32];
-            if (row_ok) load_w32(wr, sg.w_type, 32 * h, wa);
-            for (int kc = 0; kc < n_k; kc += 2) {
-                prefetch_w(kc);
-                if (row_ok && kc + 1 < n_k) load_w32(wr, sg.w_type, (kc + 1) * kGK + 32 * h, wb);
-                if (!stage(kc, wa)) break;
-                if (kc + 1 >= n_k) break;
-                prefetch_w(kc + 1);
-                if (row_ok && kc + 2 < n_k) load_w32(wr, sg.w_type, (kc + 2) * kGK + 32 * h, wa);
-                if (!stage(kc + 1, wb)) break;
             }
         } else if (warp == 0) {
             if (lane == 0) {
@@ -382,6 +374,28 @@ __global__ void __launch_bounds__(kGThreads, 1) mul_mat_gemm_kernel(const __grid
             }
             __syncwarp();
         }
+        if (warp == 2) {
+            if (lane == 0) {
+                const int nb = n_k / spb;
+                for (int b = 0; b < nb; ++b) {
+                    const int gb = wblk0 + b, ws = gb % kGWDepth;
+                    if (gb >= kGWDepth && !*abort_flag && !mbar_wait(&wempty[ws], ((gb / kGWDepth) - 1) & 1)) *abort_flag = 1;
+                    if (*abort_flag) break;
+                    // box column: the unit's 16-byte-aligned first byte (in elements of the map),
+                    // or the stage's first value for float rows
+                    int x0;
+                    if (sg.w_type == SQMIX_Q4_K) x0 = 144 * b;
+                    else if (sg.w_type == SQMIX_Q6_K) x0 = (210 * b) & ~15;
+                    else if (sg.w_type == SQMIX_Q8_0) x0 = 136 * b;  // 16-bit elements
+                    else x0 = 64 * b;
+                    mbar_arrive_expect_tx(&wfull[ws], static_cast<uint32_t>(sg.box_rows * wbytes));
+                    tma_load_2d(ring_w + ws * kGWSlot, &sg.wmap, x0, m0, &wfull[ws]);
+                    w_issued = gb + 1;
+                }
+            }
+            __syncwarp();
+        }
+        wblk0 += n_k / spb;
         // epilogue: warps 0-3 (tensor-memory lanes 32 warp ..)
         if (warp < 4) {
             if (!mbar_wait(done, done_phase & 1)) *abort_flag = 1;
@@ -412,6 +426,9 @@ __global__ void __launch_bounds__(kGThreads, 1) mul_mat_gemm_kernel(const __grid
         }
     }
     if (!ok && threadIdx.x == 0 && p.status) atomicOr(p.status, 1u);
+    if (!ok && warp == 2 && lane == 0)
+        for (int g = w_issued > kGWDepth ? w_issued - kGWDepth : 0; g < w_issued; ++g)
+            if (!mbar_wait(&wfull[g % kGWDepth], (g / kGWDepth) & 1)) break;
     if (!ok && warp == 1 && lane == 0) {
         // never exit with a tensor-map load still writing into shared memory: wait (bounded)
         // for the last requests (earlier ones were consumed before their slots were reused)
@@ -466,6 +483,7 @@ int mul_mat_gemm_launch(const sqmix_mul_mat_args *args, int n, cudaStream_t st) 
         const int64_t elt = a0.x_dtype == SQMIX_F32 ? 4 : 2;
         const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
         if (!enc) return cuda_status(cudaErrorNotSupported, "mul_mat gemm tensor map encoder");
+        // (the weight maps below use the same encoder)
         const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a0.n_in), static_cast<cuuint64_t>(a0.n_tokens)};
         const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a0.x_stride * elt)};
         const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elt), static_cast<cuuint32_t>(kGN)};
@@ -478,8 +496,42 @@ int mul_mat_gemm_launch(const sqmix_mul_mat_args *args, int n, cudaStream_t st) 
             CUDA_SUCCESS)
             return cuda_status(cudaErrorInvalidValue, "mul_mat gemm tensor map of x");
     }
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
     for (int i = 0; i < n; ++i) {
         GemmSeg &sg = p.seg[p.n_seg++];
+        {  // the weight rows as boxes of 128 rows x wbox_bytes (no swizzle; rows beyond n_out read as zeros)
+            const int wt = args[i].w_type;
+            const int64_t rb = args[i].w_row_bytes;
+            CUtensorMapDataType dt;
+            cuuint64_t dims[2];
+            cuuint32_t box[2];
+            if (wt == SQMIX_Q8_0) {
+                dt = CU_TENSOR_MAP_DATA_TYPE_UINT16;
+                dims[0] = static_cast<cuuint64_t>(rb / 2);
+                box[0] = static_cast<cuuint32_t>(wbox_bytes(wt) / 2);
+            } else if (wt == SQMIX_F32) {
+                dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+                dims[0] = static_cast<cuuint64_t>(a0.n_in);
+                box[0] = kGK;
+            } else if (wt == SQMIX_F16 || wt == SQMIX_BF16) {
+                dt = CU_TENSOR_MAP_DATA_TYPE_UINT16;
+                dims[0] = static_cast<cuuint64_t>(a0.n_in);
+                box[0] = kGK;
+            } else {  // q4_K, q6_K as bytes
+                dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+                dims[0] = static_cast<cuuint64_t>(rb);
+                box[0] = static_cast<cuuint32_t>(wbox_bytes(wt));
+            }
+            dims[1] = static_cast<cuuint64_t>(args[i].n_out);
+            box[1] = static_cast<cuuint32_t>(std::min<int64_t>(kGM, args[i].n_out));
+            sg.box_rows = static_cast<int>(box[1]);
+            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(rb)};
+            const cuuint32_t es[2] = {1, 1};
+            if (enc(&sg.wmap, dt, 2, const_cast<void *>(args[i].w), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+                CUDA_SUCCESS)
+                return cuda_status(cudaErrorInvalidValue, "mul_mat gemm tensor map of w");
+        }
         sg.w = static_cast<const uint8_t *>(args[i].w);
         sg.y = args[i].y;
         sg.y_stride = args[i].y_stride;
