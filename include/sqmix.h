@@ -563,8 +563,8 @@ int sqmix_head_norm(const sqmix_head_norm_args *args, sqmix_stream_t stream);
  *   - decode (n_tokens below the prefill threshold): each stream of W serves up to 4
  *     tokens; dequantised weights times x summed f32-exactly (ggml's CUDA backend
  *     quantises x to q8_1 for its quantised dot products; this is the more exact form);
- *   - prefill (n_tokens >= 128, or >= 48 when the call has at least 48 tiles of 128
- *     rows x 128 tokens; x rows 16-byte aligned): a tensor-core GEMM whose operands are
+ *   - prefill (n_tokens >= 128; >= 48 when the call has at least 48 tiles of 128 rows x
+ *     128 tokens, >= 16 with at least 96; x rows 16-byte aligned): a tensor-core GEMM whose operands are
  *     tf32 for f32 x (weights and x truncated to a 10-bit mantissa) or x's 16-bit type,
  *     sums in f32 -- about 1e-3 of max |y|, as ggml's dequantise-to-16-bit GEMM path.
  * The weights are read before the call's dependency on the previous kernel on the

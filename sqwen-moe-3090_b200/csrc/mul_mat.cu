@@ -34,12 +34,13 @@ namespace {
 constexpr int kMmRegThreads = 512;    // threads per SM the registers are budgeted for
 constexpr int kMaxIn = 4096;          // n_in limit (the model's 2048 and 4096)
 constexpr int kMaxPassTokens = 4;     // tokens per stream of W
-// The tensor-core GEMM form (mul_mat_gemm.cu) takes n_tokens >= kGemmTokens, or >=
-// kGemmMinTokens when its tiles fill at least kGemmMinTiles of the grid (measured
-// crossovers against ceil(n_tokens / 4) passes of the decode form)
+// The tensor-core GEMM form (mul_mat_gemm.cu) takes n_tokens >= kGemmTokens, >= 48 when
+// its tiles fill at least 48 CTAs, >= 16 when at least 96 (measured crossovers against
+// ceil(n_tokens / 4) passes of the decode form: the GEMM's time hardly depends on the
+// batch below 128 tokens, the decode form's grows with every 4)
 constexpr int kGemmTokens = 128;
-constexpr int kGemmMinTokens = 48;
-constexpr int kGemmMinTiles = 48;
+constexpr int kGemmMinTokens = 16;
+__host__ constexpr int gemm_min_tiles(int n_tokens) { return n_tokens >= 48 ? 48 : 96; }
 constexpr int kMaxStages = 8;
 constexpr int kFloatSlot = 16 * 1024; // slot bytes of a launch of float-typed weights only
 constexpr int kMaxSeg = SQMIX_MUL_MAT_MAX_GROUP;
@@ -651,7 +652,7 @@ extern "C" int sqmix_mul_mat_group(const sqmix_mul_mat_args *args, int32_t n, sq
                         i);
     if (a0.n_tokens >= kGemmMinTokens) {  // the GEMM form needs x rows 16-byte aligned (tiles 0 otherwise)
         const int tiles = mul_mat_gemm_tiles(args, n);
-        if (tiles > 0 && (a0.n_tokens >= kGemmTokens || tiles >= kGemmMinTiles))
+        if (tiles > 0 && (a0.n_tokens >= kGemmTokens || tiles >= gemm_min_tiles(a0.n_tokens)))
             return mul_mat_gemm_launch(args, n, reinterpret_cast<cudaStream_t>(stream));
     }
     // the launch's tile list: the projections in call order, 16-row tiles for the

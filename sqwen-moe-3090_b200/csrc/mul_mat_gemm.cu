@@ -1,5 +1,5 @@
-// mul_mat_gemm.cu -- the mixer projections at prefill (n_tokens >= 128, or >= 48 with
-// enough output tiles): ggml_mul_mat(w, x) as a tensor-core GEMM,
+// mul_mat_gemm.cu -- the mixer projections at prefill (n_tokens >= 128, or fewer with
+// enough output tiles; mul_mat.cu decides): ggml_mul_mat(w, x) as a tensor-core GEMM,
 //     Y[t][o] = sum_i W[o][i] x[t][i].
 //
 // An item is a 128 x 128 tile of Y (128 weight rows of one projection x 128 tokens); the

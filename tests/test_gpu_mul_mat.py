@@ -158,14 +158,15 @@ def test_mul_mat_group_bf16_x_4096_inputs(oracle):
         assert rel_err(g.cpu().numpy(), want.astype(np.float64)) <= TOL, (wt, n_out)
 
 
-# The prefill form (n_tokens >= 128, or >= 48 with at least 48 output tiles of 128 x
-# 128): a tcgen05 GEMM on f16 operands (each dequantised weight and each x value rounded
-# once to f16), f32 accumulation.  Bar: max |gpu - ref| <= 3e-3 * max |ref| against the
+# The prefill form (n_tokens >= 128; >= 48 with at least 48 output tiles of 128 x 128,
+# >= 16 with at least 96): a tcgen05 GEMM on tf32 operands for f32 x (f16 / bf16 for
+# 16-bit x), f32 accumulation.  Bar: max |gpu - ref| <= 3e-3 * max |ref| against the
 # float64 sums of the exact dequantised weights.
 PREFILL_TOL = 3e-3
 PREFILL_CASES = [
     (12, 2048, 300, 130, torch.float32),   # ragged weight tile, ragged second token tile
-    (12, 2048, 6144, 48, torch.float32),   # the smallest batch of the form (48 tiles)
+    (12, 2048, 6144, 48, torch.float32),   # 48 tokens with 48 tiles
+    (12, 2048, 12288, 16, torch.float32),  # 16 tokens with 96 tiles
     (14, 2048, 128, 128, torch.bfloat16),  # attn_v's format
     (8, 4096, 200, 256, torch.float32),
     (0, 2048, 32, 137, torch.float32),     # the 32-row f32 beta / alpha
