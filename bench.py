@@ -1197,7 +1197,16 @@ def cpu_baseline_proj() -> dict:
         for _, wt, n_in, n_out in (PROJ_FULL if layer % 4 == 3 else PROJ_GDN):
             total_bytes += oracle.row_bytes(wt, n_in) * n_out
     scale = total_bytes / w.nbytes
+    # a prefill batch: the same dot products per token, 8 tokens per sample
+    x8 = rng.standard_normal((8, 2048)).astype(np.float32)
+    reps8, t0 = 0, time.perf_counter()
+    while reps8 < 3 or time.perf_counter() - t0 < 1.0:
+        oracle.cpu_mul_mat(w, 12, 2048, x8)
+        reps8 += 1
+    us8 = (time.perf_counter() - t0) / reps8 * 1e6
     return {"value": us * scale, "unit": "us/token", "qkv_us": us, "cores": cores, "kind": CPU_KIND,
+            "prefill_T512": {"value": us8 * 64 * scale, "unit": "us per 512 tokens",
+                             "sample": f"{reps8} runs of the same projection at T = 8, scaled by 64 and by weight bytes"},
             "sample": f"{reps} runs of one 2048 -> 8192 q4_K projection (T = 1), scaled by weight bytes to the 190 "
                       "projections of a token; C restatement of ggml-cpu's q4_K x q8_K integer dot products "
                       "(oracle/cpu_ggml.c)"}
