@@ -41,8 +41,8 @@ namespace {
 constexpr int kGM = 128;            // weight rows per item (MMA M)
 constexpr int kGN = 128;            // tokens per item (MMA N)
 constexpr int kGK = 64;             // contraction values per stage
-constexpr int kGStages = 3;         // stages in flight (weight columns and x slots)
-constexpr int kGWDepth = 3;         // weight boxes in flight
+constexpr int kGStages = 4;         // stages in flight (weight columns and x slots)
+constexpr int kGWDepth = 2;         // weight boxes in flight
 constexpr int kGWarps = 12;
 constexpr int kGThreads = kGWarps * 32;
 constexpr int kGProdWarp0 = 4;
