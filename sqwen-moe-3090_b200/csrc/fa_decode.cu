@@ -131,14 +131,14 @@ __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepco
 __device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // Log-sum-exp merge of the split partials for one 32-dim slice of one output row, by
-// a CTA of 256 threads: thread = dim lane x split group (8 groups, group g takes splits
-// g, g + 8, ...).  Each thread issues the loads of its group's splits at once (up to
-// kMergePre per pass: partial O of its dim and the split's (m, l), the latter the same
-// address for the whole warp) and folds them with a running maximum in registers; one
-// barrier then combines the 8 groups.  A merge of up to 8 * kMergePre splits is one
-// round trip to L2 and one barrier.  Reads bypass L1: the partials were written by
-// other CTAs.
-constexpr int kMergePre = 24;
+// a CTA of 256 threads: 8 warps x 4 split groups x 8 dim quads (warp w, group q takes
+// splits 32 j + 4 w + q; the lane's quad is 4 consecutive dims, one 16-byte load per
+// split).  Each thread issues the loads of its splits at once (up to kMergePre per
+// pass: partial O of its dims and the split's (m, l)) and folds them with a running
+// maximum in registers; the four groups of a warp fold by shuffles and one barrier
+// combines the 8 warps.  A merge of up to 32 * kMergePre splits is one pass.  Reads
+// bypass L1: the partials were written by other CTAs.
+constexpr int kMergePre = 5;
 struct MergeSmem {
     float red[8][33];
     float gm[8];  // per group: running maximum (score units) and sum of l weights
@@ -149,19 +149,26 @@ struct MergeSmem {
 // normalised output of dim slice * 32 + lane, lse_row = the row's natural-log LSE.
 __device__ void merge_slice_values(const float *part_o, const float *part_ml, int n_splits, int n_rows, int row,
                                    int slice, float c, float scale, MergeSmem &sm, float &y_out, float &lse_row) {
+    // Lane (q, dq) of warp grp reads dims 4 dq .. 4 dq + 3 of the slice from splits
+    // s = 32 j + 4 grp + q as one 16-byte load each: a warp request covers four splits,
+    // so a CTA issues about a tenth of the requests that one 4-byte load per split and
+    // lane would take (measured on B200: the per-SM request count, not the L2 round
+    // trip, bounded the merge).
     const int tid = threadIdx.x, lane = tid & 31, grp = tid >> 5;
-    const int d = slice * 32 + lane;
+    const int dq = lane & 7, q = lane >> 3;
     const size_t sstride = static_cast<size_t>(n_rows) * 256;
-    const float *po = part_o + static_cast<size_t>(row) * 256 + d;
+    const float *po = part_o + static_cast<size_t>(row) * 256 + slice * 32 + 4 * dq;
     const float2 *pml = reinterpret_cast<const float2 *>(part_ml) + row;  // split s at pml[s * n_rows]
-    float m_g = -INFINITY, l_g = 0.f, acc = 0.f;
-    for (int s0 = grp; s0 < n_splits; s0 += 8 * kMergePre) {
-        float ov[kMergePre];
+    float m_g = -INFINITY, l_g = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 4 * grp + q; s0 < n_splits; s0 += 32 * kMergePre) {
+        float4 ov[kMergePre];
         float2 ml[kMergePre];
 #pragma unroll
         for (int j = 0; j < kMergePre; ++j) {
-            const int s = s0 + 8 * j;
-            ov[j] = s < n_splits ? __ldcg(po + s * sstride) : 0.f;
+            const int s = s0 + 32 * j;
+            ov[j] = s < n_splits ? __ldcg(reinterpret_cast<const float4 *>(po + s * sstride))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
             ml[j] = s < n_splits ? __ldcg(pml + static_cast<size_t>(s) * n_rows) : make_float2(-INFINITY, 0.f);
         }
         float mx = m_g;
@@ -169,18 +176,47 @@ __device__ void merge_slice_values(const float *part_o, const float *part_ml, in
         for (int j = 0; j < kMergePre; ++j) mx = fmaxf(mx, ml[j].x);
         if (mx > -INFINITY) {
             const float a = ex2((m_g - mx) * c);  // 0 while nothing was folded (m_g = -inf)
-            acc *= a;
+            acc.x *= a;
+            acc.y *= a;
+            acc.z *= a;
+            acc.w *= a;
             l_g *= a;
 #pragma unroll
             for (int j = 0; j < kMergePre; ++j) {
                 const float w = ex2((ml[j].x - mx) * c);  // empty splits (m = -inf) weigh 0
-                acc = fmaf(ov[j], w, acc);
+                acc.x = fmaf(ov[j].x, w, acc.x);
+                acc.y = fmaf(ov[j].y, w, acc.y);
+                acc.z = fmaf(ov[j].z, w, acc.z);
+                acc.w = fmaf(ov[j].w, w, acc.w);
                 l_g = fmaf(ml[j].y, w, l_g);
             }
             m_g = mx;
         }
     }
-    sm.red[grp][lane] = acc;
+    // fold the four split groups of the warp (lanes dq, dq + 8, dq + 16, dq + 24)
+#pragma unroll
+    for (int off = 8; off < 32; off <<= 1) {
+        const float m_o = __shfl_xor_sync(0xffffffffu, m_g, off);
+        const float l_o = __shfl_xor_sync(0xffffffffu, l_g, off);
+        const float4 a_o = make_float4(__shfl_xor_sync(0xffffffffu, acc.x, off),
+                                       __shfl_xor_sync(0xffffffffu, acc.y, off),
+                                       __shfl_xor_sync(0xffffffffu, acc.z, off),
+                                       __shfl_xor_sync(0xffffffffu, acc.w, off));
+        const float mn = fmaxf(m_g, m_o);
+        if (mn > -INFINITY) {
+            const float wa = ex2((m_g - mn) * c), wb = ex2((m_o - mn) * c);  // -inf sides weigh 0
+            acc = make_float4(fmaf(acc.x, wa, a_o.x * wb), fmaf(acc.y, wa, a_o.y * wb),
+                              fmaf(acc.z, wa, a_o.z * wb), fmaf(acc.w, wa, a_o.w * wb));
+            l_g = fmaf(l_g, wa, l_o * wb);
+            m_g = mn;
+        }
+    }
+    if (q == 0) {
+        sm.red[grp][4 * dq + 0] = acc.x;
+        sm.red[grp][4 * dq + 1] = acc.y;
+        sm.red[grp][4 * dq + 2] = acc.z;
+        sm.red[grp][4 * dq + 3] = acc.w;
+    }
     if (lane == 0) {
         sm.gm[grp] = m_g;
         sm.gl[grp] = l_g;
