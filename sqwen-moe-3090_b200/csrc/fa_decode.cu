@@ -46,12 +46,16 @@
 namespace sqmix {
 
 constexpr int kFaWsHeader = 256;  // [0] u32 error bits
+#ifndef SQMIX_FA_DECODE_MAXREG
+#define SQMIX_FA_DECODE_MAXREG 152
+#endif
 
 struct FaDecodeParams {
     const void *q;
     int q_dtype;
     int64_t q_st;
     int64_t q_sh;
+    int q_vec;  // Q's base and strides allow one load per 4 consecutive elements
     uint8_t *k_cache;
     uint8_t *v_cache;
     const int64_t *n_kv;
@@ -91,6 +95,9 @@ template <int NQ, int WPH, int GPW, int NSTAGE, int MINB>
 struct FaCfg {
     static constexpr int kWarps = 2 * WPH;
     static constexpr int kThreads = kWarps * 32;
+    // The 12-warp one-token configurations run capped at SQMIX_FA_DECODE_MAXREG registers
+    // per thread, so that a CTA of their split merge fits on the SM beside the decode CTA.
+    static constexpr bool kCapped = NQ == 1 && WPH == 6;
     // One ring slot holds WPH groups (16 * WPH tokens) of K and of V; a compute step
     // consumes GPW consecutive slots, warp (h, u) taking group u of each.
     static constexpr int kTileGroups = WPH;
@@ -139,16 +146,20 @@ __device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontr
 // combines the 8 warps.  A merge of up to 32 * kMergePre splits is one pass.  Reads
 // bypass L1: the partials were written by other CTAs.
 constexpr int kMergePre = 5;
-struct MergeSmem {
-    float red[8][33];
-    float gm[8];  // per group: running maximum (score units) and sum of l weights
-    float gl[8];
+template <int NW>
+struct MergeSmemT {
+    float red[NW][33];
+    float gm[NW];  // per warp: running maximum (score units) and sum of l weights
+    float gl[NW];
 };
+using MergeSmem = MergeSmemT<8>;
 
 // The merged values, valid in the first warp (lane = dim within the slice): y = the
 // normalised output of dim slice * 32 + lane, lse_row = the row's natural-log LSE.
+template <int NW, int PRE = kMergePre>
 __device__ void merge_slice_values(const float *part_o, const float *part_ml, int n_splits, int n_rows, int row,
-                                   int slice, float c, float scale, MergeSmem &sm, float &y_out, float &lse_row) {
+                                   int slice, float c, float scale, MergeSmemT<NW> &sm, float &y_out,
+                                   float &lse_row) {
     // Lane (q, dq) of warp grp reads dims 4 dq .. 4 dq + 3 of the slice from splits
     // s = 32 j + 4 grp + q as one 16-byte load each: a warp request covers four splits,
     // so a CTA issues about a tenth of the requests that one 4-byte load per split and
@@ -161,19 +172,20 @@ __device__ void merge_slice_values(const float *part_o, const float *part_ml, in
     const float2 *pml = reinterpret_cast<const float2 *>(part_ml) + row;  // split s at pml[s * n_rows]
     float m_g = -INFINITY, l_g = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s0 = 4 * grp + q; s0 < n_splits; s0 += 32 * kMergePre) {
-        float4 ov[kMergePre];
-        float2 ml[kMergePre];
+    // Warps grp >= NW (a larger CTA folding in the NW-warp order) take no splits.
+    for (int s0 = grp < NW ? 4 * grp + q : n_splits; s0 < n_splits; s0 += 4 * NW * PRE) {
+        float4 ov[PRE];
+        float2 ml[PRE];
 #pragma unroll
-        for (int j = 0; j < kMergePre; ++j) {
-            const int s = s0 + 32 * j;
+        for (int j = 0; j < PRE; ++j) {
+            const int s = s0 + 4 * NW * j;
             ov[j] = s < n_splits ? __ldcg(reinterpret_cast<const float4 *>(po + s * sstride))
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
             ml[j] = s < n_splits ? __ldcg(pml + static_cast<size_t>(s) * n_rows) : make_float2(-INFINITY, 0.f);
         }
         float mx = m_g;
 #pragma unroll
-        for (int j = 0; j < kMergePre; ++j) mx = fmaxf(mx, ml[j].x);
+        for (int j = 0; j < PRE; ++j) mx = fmaxf(mx, ml[j].x);
         if (mx > -INFINITY) {
             const float a = ex2((m_g - mx) * c);  // 0 while nothing was folded (m_g = -inf)
             acc.x *= a;
@@ -182,7 +194,7 @@ __device__ void merge_slice_values(const float *part_o, const float *part_ml, in
             acc.w *= a;
             l_g *= a;
 #pragma unroll
-            for (int j = 0; j < kMergePre; ++j) {
+            for (int j = 0; j < PRE; ++j) {
                 const float w = ex2((ml[j].x - mx) * c);  // empty splits (m = -inf) weigh 0
                 acc.x = fmaf(ov[j].x, w, acc.x);
                 acc.y = fmaf(ov[j].y, w, acc.y);
@@ -211,13 +223,13 @@ __device__ void merge_slice_values(const float *part_o, const float *part_ml, in
             m_g = mn;
         }
     }
-    if (q == 0) {
+    if (q == 0 && grp < NW) {
         sm.red[grp][4 * dq + 0] = acc.x;
         sm.red[grp][4 * dq + 1] = acc.y;
         sm.red[grp][4 * dq + 2] = acc.z;
         sm.red[grp][4 * dq + 3] = acc.w;
     }
-    if (lane == 0) {
+    if (lane == 0 && grp < NW) {
         sm.gm[grp] = m_g;
         sm.gl[grp] = l_g;
     }
@@ -225,11 +237,11 @@ __device__ void merge_slice_values(const float *part_o, const float *part_ml, in
     if (grp == 0) {
         float M = sm.gm[0];
 #pragma unroll
-        for (int i = 1; i < 8; ++i) M = fmaxf(M, sm.gm[i]);
+        for (int i = 1; i < NW; ++i) M = fmaxf(M, sm.gm[i]);
         float L = 0.f, y = 0.f;
         if (M > -INFINITY) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < NW; ++i) {
                 const float w = ex2((sm.gm[i] - M) * c);
                 L = fmaf(sm.gl[i], w, L);
                 y = fmaf(sm.red[i][lane], w, y);
@@ -240,11 +252,12 @@ __device__ void merge_slice_values(const float *part_o, const float *part_ml, in
     }
 }
 
+template <int NW, int PRE = kMergePre>
 __device__ void merge_slice(const float *part_o, const float *part_ml, int n_splits, int n_rows, int row,
                             int slice, float c, float scale, float gate_factor, float *out, float *lse,
-                            MergeSmem &sm) {
+                            MergeSmemT<NW> &sm) {
     float y = 0.f, lse_row = 0.f;
-    merge_slice_values(part_o, part_ml, n_splits, n_rows, row, slice, c, scale, sm, y, lse_row);
+    merge_slice_values<NW, PRE>(part_o, part_ml, n_splits, n_rows, row, slice, c, scale, sm, y, lse_row);
     if (threadIdx.x < 32) {
         out[static_cast<size_t>(row) * 256 + slice * 32 + threadIdx.x] = y * gate_factor;
         if (lse && slice == 0 && threadIdx.x == 0) lse[row] = lse_row;
@@ -263,8 +276,7 @@ __device__ void merge_slice(const float *part_o, const float *part_ml, int n_spl
 //      P' = f16(P d): the difference is the f16 rounding of P', about 2^-12 of each
 //      term, well inside the attention tolerance.
 template <int NQ, int WPH, int GPW, int NSTAGE, int MINB, int VC>
-__global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, MINB)
-    fa_decode_kernel(FaDecodeParams p) {
+__device__ __forceinline__ void fa_decode_body(const FaDecodeParams &p) {
     using L = FaCfg<NQ, WPH, GPW, NSTAGE, MINB>;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *ring = smem;
@@ -384,15 +396,56 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     launch_dependents();
 
     // ---- Q and the step's new K/V rows (produced by earlier kernels: after the wait) --
+    const int kvh = warp / WPH;  // KV head
+    const int u = warp % WPH;    // first group of this warp within the tile
+    const int g = lane >> 2;
+    const int c = lane & 3;
+    // Direct fragments (no fused Q norm, RoPE pairs (i, i + 16), (i, i + 32) or none):
+    // warp u < 4 of a KV head builds the Q^T fragments of blocks 2u and 2u + 1 from
+    // registers.  Lane (g, c) needs dims 32b + 4c .. + 3 (A) and 32b + 16 + 4c .. + 3
+    // (B) of head 8 kvh + g, and the RoPE partner of each of them is in the same lane
+    // (A/B of block 1 for pairs 32 apart, B of block 0 for pairs 16 apart), so neither
+    // a staged copy of Q nor a barrier sits between the loads and the fragments.
+    // One query token only: with two, the direct path's registers push the 255-register
+    // main loop into more spills (measured at 172K keys: 40.1 against 38.7 us per layer).
+    static_assert(WPH >= 4, "direct fragments: four warps per KV head build the 8 blocks");
+    constexpr bool kDirectQ = NQ == 1;
+    const bool fastq = kDirectQ && !p.q_norm && (half == 0 || half == 16 || half == 32);
     constexpr int kQElems = NQ * 16 * 256;
     constexpr int kQPer = (kQElems + L::kThreads - 1) / L::kThreads;
     float qv[kQPer];
+    float qa[NQ][2][4], qb[NQ][2][4];  // direct path: [qi][block 2u + bb][element]
+    if (fastq) {
+        if (u < 4) {
 #pragma unroll
-    for (int k = 0; k < kQPer; ++k) {
-        const int e = threadIdx.x + k * L::kThreads;  // [qi][head][256]
-        qv[k] = e < kQElems ? load_act(p.q, seq * p.q_sseq + (e >> 12) * p.q_st + ((e >> 8) & 15) * p.q_sh + (e & 255),
-                                       p.q_dtype)
-                            : 0.f;
+            for (int qi = 0; qi < NQ; ++qi)
+#pragma unroll
+                for (int bb = 0; bb < 2; ++bb) {
+                    const int64_t row = seq * p.q_sseq + qi * p.q_st + (kvh * 8 + g) * p.q_sh;
+                    const int64_t da = row + 32 * (2 * u + bb) + 4 * c, db = da + 16;
+                    if (p.q_vec && p.q_dtype == SQMIX_F32) {
+                        const float4 x = *reinterpret_cast<const float4 *>(static_cast<const float *>(p.q) + da);
+                        const float4 y = *reinterpret_cast<const float4 *>(static_cast<const float *>(p.q) + db);
+                        qa[qi][bb][0] = x.x, qa[qi][bb][1] = x.y, qa[qi][bb][2] = x.z, qa[qi][bb][3] = x.w;
+                        qb[qi][bb][0] = y.x, qb[qi][bb][1] = y.y, qb[qi][bb][2] = y.z, qb[qi][bb][3] = y.w;
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            qa[qi][bb][j] = load_act(p.q, da + j, p.q_dtype);
+                            qb[qi][bb][j] = load_act(p.q, db + j, p.q_dtype);
+                        }
+                    }
+                }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < kQPer; ++k) {
+            const int e = threadIdx.x + k * L::kThreads;  // [qi][head][256]
+            qv[k] = e < kQElems ? load_act(p.q, seq * p.q_sseq + (e >> 12) * p.q_st + ((e >> 8) & 15) * p.q_sh +
+                                                    (e & 255),
+                                           p.q_dtype)
+                                : 0.f;
+        }
     }
     constexpr int kKvElems = NQ * 2 * 512;
     constexpr int kKvPer = (kKvElems + L::kThreads - 1) / L::kThreads;
@@ -408,22 +461,21 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
                                  : 0.f;
         }
     }
-    if (producer) fill(NSTAGE - kStagingSlots, has_fresh ? q_pos0 : INT64_MAX);
-
-
-    const int kvh = warp / WPH;  // KV head
-    const int u = warp % WPH;    // first group of this warp within the tile
-    const int g = lane >> 2;
-    const int c = lane & 3;
+    // The staging slots of the ring hold Q (unless its fragments are built directly) and
+    // the fused append's rows; otherwise they are free for tiles at once.
+    const bool staging_used = !fastq || has_fresh;
+    if (producer) fill(staging_used ? NSTAGE - kStagingSlots : NSTAGE, has_fresh ? q_pos0 : INT64_MAX);
 
     float *q_stage = reinterpret_cast<float *>(ring + (NSTAGE - kStagingSlots) * L::kStageBytes);
     float *kv_stage = q_stage + NQ * 16 * kQRow;
+    if (!fastq) {
 #pragma unroll
-    for (int k = 0; k < kQPer; ++k)
-        if (threadIdx.x + k * L::kThreads < kQElems) {
-            const int e = threadIdx.x + k * L::kThreads;
-            q_stage[(e >> 8) * kQRow + (e & 255)] = qv[k];
-        }
+        for (int k = 0; k < kQPer; ++k)
+            if (threadIdx.x + k * L::kThreads < kQElems) {
+                const int e = threadIdx.x + k * L::kThreads;
+                q_stage[(e >> 8) * kQRow + (e & 255)] = qv[k];
+            }
+    }
     if (has_fresh) {
 #pragma unroll
         for (int k = 0; k < kKvPer; ++k)
@@ -431,7 +483,58 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     }
     (void)kvv;
 
-    __syncthreads();  // staged Q / new rows and the RoPE table are visible
+    float *kinit_s = reinterpret_cast<float *>(smem + L::kKinitOffset);
+    if (fastq && u < 4) {
+#pragma unroll
+        for (int qi = 0; qi < NQ; ++qi) {
+            // RoPE (attn.rs:183-204) with the rounding steps of kv_row_elem: lower dim x,
+            // upper partner y, (x c - y s, y c + x s) with the angle of the lower index
+            const float2 *tab = rope_s + qi * 32;
+            if (u == 0 && half == 32) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 ca = tab[4 * c + j], cb = tab[16 + 4 * c + j];
+                    const float x0 = qa[qi][0][j], y0 = qa[qi][1][j], x1 = qb[qi][0][j], y1 = qb[qi][1][j];
+                    qa[qi][0][j] = __fsub_rn(__fmul_rn(x0, ca.x), __fmul_rn(y0, ca.y));
+                    qa[qi][1][j] = __fadd_rn(__fmul_rn(x0, ca.y), __fmul_rn(y0, ca.x));
+                    qb[qi][0][j] = __fsub_rn(__fmul_rn(x1, cb.x), __fmul_rn(y1, cb.y));
+                    qb[qi][1][j] = __fadd_rn(__fmul_rn(x1, cb.y), __fmul_rn(y1, cb.x));
+                }
+            } else if (u == 0 && half == 16) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 ca = tab[4 * c + j];
+                    const float x0 = qa[qi][0][j], y0 = qb[qi][0][j];
+                    qa[qi][0][j] = __fsub_rn(__fmul_rn(x0, ca.x), __fmul_rn(y0, ca.y));
+                    qb[qi][0][j] = __fadd_rn(__fmul_rn(x0, ca.y), __fmul_rn(y0, ca.x));
+                }
+            }
+#pragma unroll
+            for (int bb = 0; bb < 2; ++bb) {
+                const int b = 2 * u + bb;
+                float t[2];
+#pragma unroll
+                for (int s = 0; s < 2; ++s) {  // k-slice s: dims 4c + s, + 2, + 16, + 18 of the block
+                    const uint2 f = make_uint2(pack_half2(qa[qi][bb][s], qa[qi][bb][s + 2]),
+                                               pack_half2(qb[qi][bb][s] * 0.0625f, qb[qi][bb][s + 2] * 0.0625f));
+                    qf_s[(((kvh * NQ + qi) * 8 + b) * 2 + s) * 32 + lane] = f;
+                    const float2 lo = __half22float2(u32_as_h2(f.x));
+                    const float2 hi = __half22float2(u32_as_h2(f.y));
+                    t[s] = (lo.x + lo.y) + 16.0f * (hi.x + hi.y);
+                }
+                // K offset term of (kvh, qi, b, head g): the 8 terms of the row's 4 lanes,
+                // summed in the order of the staged path (slice, then lane)
+                float sum = 0.f;
+#pragma unroll
+                for (int s = 0; s < 2; ++s)
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) sum += __shfl_sync(0xffffffffu, t[s], 4 * g + cc);
+                if (c == 0) kinit_s[((kvh * NQ + qi) * 8 + b) * 8 + g] = -8.0f / kTwo24 * sum;
+            }
+        }
+    }
+
+    __syncthreads();  // staged Q / new rows, direct fragments and the RoPE table are visible
 
     // ---- optional head RMS norm (attn.rs:66-84) of the staged Q rows and new K rows,
     // in place before RoPE: one warp per 256-wide row, (x * (1 / sqrt(mean + eps))) * w ----
@@ -494,50 +597,53 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
         asm volatile("fence.proxy.async.global;" ::: "memory");
     }
 
-    // ---- Q^T fragments (f16) with RoPE -------------------------------------------
-    // k-slot kappa of k-slice s of block b maps to dim
-    //   32b + (kappa < 8 ? 4(kappa/2) + 2(kappa%2) : 16 + 4((kappa-8)/2) + 2(kappa%2)) + s
-    // (the order in which a 32-bit load of qs[4c..4c+3] delivers nibbles); lane (g, c)
-    // supplies head 8*kvh + g, k-slots {2c, 2c+1} and {2c+8, 2c+9} (the latter / 16).
-    for (int item = threadIdx.x; item < 2 * NQ * 8 * 2 * 32; item += L::kThreads) {
-        const int ln = item & 31;
-        const int s = (item >> 5) & 1;
-        const int b = (item >> 6) & 7;
-        const int qi = (item >> 9) % NQ;
-        const int kh = (item >> 9) / NQ;
-        const int gg = ln >> 2, cc = ln & 3;
-        const int qrow = (qi * 16 + kh * 8 + gg) * kQRow;
-        const int d0 = 32 * b + 4 * cc + s;
-        const int dims[4] = {d0, d0 + 2, d0 + 16, d0 + 18};
-        float v[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] = kv_row_elem(q_stage, qrow, dims[e], SQMIX_F32, p.rope_n_rot, rope_s + qi * 32);
-        qf_s[item] = make_uint2(pack_half2(v[0], v[1]), pack_half2(v[2] * 0.0625f, v[3] * 0.0625f));
+    if (!fastq) {
+        // ---- Q^T fragments (f16) with RoPE -------------------------------------------
+        // k-slot kappa of k-slice s of block b maps to dim
+        //   32b + (kappa < 8 ? 4(kappa/2) + 2(kappa%2) : 16 + 4((kappa-8)/2) + 2(kappa%2)) + s
+        // (the order in which a 32-bit load of qs[4c..4c+3] delivers nibbles); lane (g, c)
+        // supplies head 8*kvh + g, k-slots {2c, 2c+1} and {2c+8, 2c+9} (the latter / 16).
+        for (int item = threadIdx.x; item < 2 * NQ * 8 * 2 * 32; item += L::kThreads) {
+            const int ln = item & 31;
+            const int s = (item >> 5) & 1;
+            const int b = (item >> 6) & 7;
+            const int qi = (item >> 9) % NQ;
+            const int kh = (item >> 9) / NQ;
+            const int gg = ln >> 2, cc = ln & 3;
+            const int qrow = (qi * 16 + kh * 8 + gg) * kQRow;
+            const int d0 = 32 * b + 4 * cc + s;
+            const int dims[4] = {d0, d0 + 2, d0 + 16, d0 + 18};
+            float v[4];
+    #pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] = kv_row_elem(q_stage, qrow, dims[e], SQMIX_F32, p.rope_n_rot, rope_s + qi * 32);
+            qf_s[item] = make_uint2(pack_half2(v[0], v[1]), pack_half2(v[2] * 0.0625f, v[3] * 0.0625f));
+        }
+        __syncthreads();
+        // K offset term per (kvh, query, block, head): -8 * 2^-24 * sum_j q_j over the
+        // block, from the exact f16 values the MMA consumes (hi slots hold q / 16).
+        if (threadIdx.x < 2 * NQ * 8 * 8) {
+            const int h8 = threadIdx.x & 7;
+            const int b = (threadIdx.x >> 3) & 7;
+            const int qk = threadIdx.x >> 6;  // kvh * NQ + qi
+            float sum = 0.f;
+    #pragma unroll
+            for (int ss = 0; ss < 2; ++ss)
+    #pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    const uint2 x = qf_s[((qk * 8 + b) * 2 + ss) * 32 + 4 * h8 + cc];
+                    const float2 lo = __half22float2(u32_as_h2(x.x));
+                    const float2 hi = __half22float2(u32_as_h2(x.y));
+                    sum += (lo.x + lo.y) + 16.0f * (hi.x + hi.y);
+                }
+            kinit_s[threadIdx.x] = -8.0f / kTwo24 * sum;
+        }
     }
-    __syncthreads();
-    // K offset term per (kvh, query, block, head): -8 * 2^-24 * sum_j q_j over the
-    // block, from the exact f16 values the MMA consumes (hi slots hold q / 16).
-    float *kinit_s = reinterpret_cast<float *>(smem + L::kKinitOffset);
-    if (threadIdx.x < 2 * NQ * 8 * 8) {
-        const int h8 = threadIdx.x & 7;
-        const int b = (threadIdx.x >> 3) & 7;
-        const int qk = threadIdx.x >> 6;  // kvh * NQ + qi
-        float sum = 0.f;
-#pragma unroll
-        for (int ss = 0; ss < 2; ++ss)
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                const uint2 x = qf_s[((qk * 8 + b) * 2 + ss) * 32 + 4 * h8 + cc];
-                const float2 lo = __half22float2(u32_as_h2(x.x));
-                const float2 hi = __half22float2(u32_as_h2(x.y));
-                sum += (lo.x + lo.y) + 16.0f * (hi.x + hi.y);
-            }
-        kinit_s[threadIdx.x] = -8.0f / kTwo24 * sum;
-    }
-    __syncthreads();  // the staging slots are free from here on
-    if (producer) {  // staging slots and tiles held back for the fused append
-        const int first = n_tiles < NSTAGE ? n_tiles : NSTAGE;
-        while (issued < first) issue(issued++);
+    if (staging_used) {
+        __syncthreads();  // the staging slots are free from here on
+        if (producer) {  // staging slots and tiles held back for the fused append
+            const int first = n_tiles < NSTAGE ? n_tiles : NSTAGE;
+            while (issued < first) issue(issued++);
+        }
     }
 
     float o[NQ][8][2][4];
@@ -939,6 +1045,19 @@ __global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, M
     }
 }
 
+// The decode kernel: launch bounds from the CTA's threads and MINB CTAs per SM, or, for
+// the 12-warp one-token configurations, a cap of SQMIX_FA_DECODE_MAXREG registers (so
+// that a merge CTA fits beside it; fa_merge_narrow_kernel).
+template <int NQ, int WPH, int GPW, int NSTAGE, int MINB, int VC>
+__global__ void __launch_bounds__(FaCfg<NQ, WPH, GPW, NSTAGE, MINB>::kThreads, MINB)
+    fa_decode_kernel(FaDecodeParams p) {
+    fa_decode_body<NQ, WPH, GPW, NSTAGE, MINB, VC>(p);
+}
+template <int NQ, int WPH, int GPW, int NSTAGE, int MINB, int VC>
+__global__ void __maxnreg__(SQMIX_FA_DECODE_MAXREG) fa_decode_capped_kernel(FaDecodeParams p) {
+    fa_decode_body<NQ, WPH, GPW, NSTAGE, MINB, VC>(p);
+}
+
 // Split merge, launched right behind the decode kernel (programmatic dependent launch:
 // its CTAs are scheduled as soon as the decode grid starts and wait for it to finish).
 struct FaMergeParams {
@@ -957,8 +1076,9 @@ struct FaMergeParams {
     int64_t g_sseq;  // gate elements between sequences (batch: blockIdx.z = sequence)
 };
 
-__global__ void __launch_bounds__(256) fa_merge_kernel(FaMergeParams p) {
-    __shared__ MergeSmem sm;
+template <int NW, int PRE>
+__device__ __forceinline__ void fa_merge_body(const FaMergeParams &p) {
+    __shared__ MergeSmemT<NW> sm;
     const size_t seq = blockIdx.z;
     // The gate is an input of the decode call, produced before the decode kernel; the
     // decode kernel triggers this launch only after its own dependency wait, so the
@@ -975,8 +1095,23 @@ __global__ void __launch_bounds__(256) fa_merge_kernel(FaMergeParams p) {
     launch_dependents();
     grid_dependency_wait();
     const size_t parts = seq * p.n_splits * p.n_rows;
-    merge_slice(p.part_o + parts * 256, p.part_ml + parts * 2, p.n_splits, p.n_rows, blockIdx.x, blockIdx.y, p.c,
+    merge_slice<NW, PRE>(p.part_o + parts * 256, p.part_ml + parts * 2, p.n_splits, p.n_rows, blockIdx.x, blockIdx.y, p.c,
                 p.scale, gate_factor, p.out + seq * p.n_rows * 256, p.lse ? p.lse + seq * p.n_rows : nullptr, sm);
+}
+
+__global__ void __launch_bounds__(256) fa_merge_kernel(FaMergeParams p) { fa_merge_body<8, kMergePre>(p); }
+
+// The 4-warp merge for the capped one-token decode configurations: at most
+// kMergeNarrowRegs registers, so that one of its CTAs fits on an SM beside a decode CTA
+// (12 warps x SQMIX_FA_DECODE_MAXREG registers).  Its CTAs are then placed while the
+// decode grid runs and the next decode's CTAs take each SM as soon as this decode's
+// CTA leaves it, instead of queueing behind merge CTAs.
+constexpr int kMergeNarrowRegs = (65536 - 12 * 32 * SQMIX_FA_DECODE_MAXREG) / 128 / 8 * 8;
+static_assert(kMergeNarrowRegs >= 48, "the narrow merge needs at least 48 registers");
+// with 80 registers its 16 split groups hold 10 splits each in flight (160 in one pass)
+constexpr int kMergeNarrowPre = kMergeNarrowRegs >= 80 ? 10 : 5;
+__global__ void __maxnreg__(kMergeNarrowRegs) fa_merge_narrow_kernel(FaMergeParams p) {
+    fa_merge_body<4, kMergeNarrowPre>(p);
 }
 
 // Split merge for few splits per sequence (at most kSmallMergeSplits, as in a sequence
@@ -1045,8 +1180,12 @@ struct FaPeerMergeParams {
     PeerExchange px;
 };
 
+// NWM: the warp order of the local merge, the same as the one-GPU merge of the decode
+// configuration (4 for the capped one-token configurations), so that the local
+// partial equals that of sqmix_fa_decode bit for bit.
+template <int NWM, int PRE>
 __global__ void __launch_bounds__(256) fa_merge_peers_kernel(FaPeerMergeParams p) {
-    __shared__ MergeSmem sm;
+    __shared__ MergeSmemT<NWM> sm;
     const int row = blockIdx.x, slice = blockIdx.y;
     float gate_factor = 1.f;
     if (p.m.gate && threadIdx.x < 32) {
@@ -1057,8 +1196,8 @@ __global__ void __launch_bounds__(256) fa_merge_peers_kernel(FaPeerMergeParams p
     launch_dependents();  // as in fa_merge_kernel
     grid_dependency_wait();
     float y_loc = 0.f, lse_loc = -INFINITY;
-    merge_slice_values(p.m.part_o, p.m.part_ml, p.m.n_splits, p.m.n_rows, row, slice, p.m.c, p.m.scale, sm, y_loc,
-                       lse_loc);
+    merge_slice_values<NWM, PRE>(p.m.part_o, p.m.part_ml, p.m.n_splits, p.m.n_rows, row, slice, p.m.c, p.m.scale,
+                                 sm, y_loc, lse_loc);
     float y = 0.f, lse = -INFINITY;
     if (!peer_exchange(p.px, row, slice, y_loc, lse_loc, kWaitLimitNs, y, lse)) return;
     if (threadIdx.x < 32) {
@@ -1120,7 +1259,12 @@ template <int NQ, int WPH, int GPW, int NSTAGE, int MINB, int VC>
 static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, const FaBatch &bt = FaBatch(),
                      const PeerExchange *px = nullptr) {
     using L = FaCfg<NQ, WPH, GPW, NSTAGE, MINB>;
-    auto kernel = fa_decode_kernel<NQ, WPH, GPW, NSTAGE, MINB, VC>;
+    auto kernel = [] {
+        if constexpr (L::kCapped)
+            return fa_decode_capped_kernel<NQ, WPH, GPW, NSTAGE, MINB, VC>;
+        else
+            return fa_decode_kernel<NQ, WPH, GPW, NSTAGE, MINB, VC>;
+    }();
     static std::atomic<uint64_t> attr_devices{0};
     {
         const cudaError_t e = set_smem_once(attr_devices, kernel, L::kTotal);
@@ -1163,6 +1307,8 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, cons
     p.caps = bt.caps;
     p.q_sseq = bt.q_sseq;
     p.new_sseq = bt.new_sseq;
+    p.q_vec = reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && p.q_st % 4 == 0 && p.q_sh % 4 == 0 &&
+              p.q_sseq % 4 == 0;
 
     // Both kernels are launched with programmatic stream serialisation so that each
     // one's prologue overlaps the tail of the kernel before it (also inside CUDA graphs).
@@ -1204,7 +1350,10 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, cons
         pp.m = mp;
         pp.px = *px;
         mcfg.gridDim = dim3(NQ * 16, kPeerSlices);
-        e = cudaLaunchKernelEx(&mcfg, fa_merge_peers_kernel, pp);
+        if (L::kCapped)
+            e = cudaLaunchKernelEx(&mcfg, fa_merge_peers_kernel<4, kMergeNarrowPre>, pp);
+        else
+            e = cudaLaunchKernelEx(&mcfg, fa_merge_peers_kernel<8, kMergePre>, pp);
         return cuda_status(e, "fa_merge_peers launch");
     }
     if (n_splits <= kSmallMergeSplits) {
@@ -1214,7 +1363,12 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, cons
         return cuda_status(e, "fa_merge launch");
     }
     mcfg.gridDim = dim3(NQ * 16, 8, bt.n_seqs);
-    e = cudaLaunchKernelEx(&mcfg, fa_merge_kernel, mp);
+    if (L::kCapped) {
+        mcfg.blockDim = dim3(128);
+        e = cudaLaunchKernelEx(&mcfg, fa_merge_narrow_kernel, mp);
+    } else {
+        e = cudaLaunchKernelEx(&mcfg, fa_merge_kernel, mp);
+    }
     return cuda_status(e, "fa_merge launch");
 }
 
