@@ -115,8 +115,7 @@ struct FaCfg {
     static constexpr int kBarOffset = kRopeOffset + NQ * 32 * 8;
     static constexpr int kRelOffset = kBarOffset + 2 * NSTAGE * 8;  // [NSTAGE] release counters
     static constexpr int kRedMlOffset = kRelOffset + ((NSTAGE * 4 + 15) / 16) * 16;
-    static constexpr int kWtsOffset = kRedMlOffset + kWarps * NQ * 8 * 2 * 4;  // [qi][16][WPH + 2]
-    static constexpr int kTotal = kWtsOffset + NQ * 16 * (WPH + 2) * 4;
+    static constexpr int kTotal = kRedMlOffset + kWarps * NQ * 8 * 2 * 4;
 };
 
 
@@ -990,27 +989,8 @@ __device__ __forceinline__ void fa_decode_body(const FaDecodeParams &p) {
     __syncthreads();
 
     // ---- combine the warps of each KV head, write this split's partial --------
-    // One thread per (query, head) turns the warps' running maxima into weights.
-    float *wts = reinterpret_cast<float *>(smem + L::kWtsOffset);
-    if (threadIdx.x < NQ * 16) {
-        const int qi = threadIdx.x >> 4, head = threadIdx.x & 15;
-        const int kh = head >> 3, h8 = head & 7;
-        float M = -INFINITY;
-#pragma unroll
-        for (int wv = 0; wv < WPH; ++wv) M = fmaxf(M, red_ml[(((kh * WPH + wv) * NQ + qi) * 8 + h8) * 2]);
-        float lsum = 0.f;
-        float *wrow = wts + (qi * 16 + head) * (WPH + 2);
-#pragma unroll
-        for (int wv = 0; wv < WPH; ++wv) {
-            const float *ml = red_ml + (((kh * WPH + wv) * NQ + qi) * 8 + h8) * 2;
-            const float w = (ml[0] == -INFINITY) ? 0.f : ex2((ml[0] - M) * p.c);
-            wrow[wv] = w;
-            lsum = fmaf(ml[1], w, lsum);
-        }
-        wrow[WPH] = M;
-        wrow[WPH + 1] = lsum;
-    }
-    __syncthreads();
+    // Each thread turns the warps' running maxima of its (query, head) row into weights
+    // itself (WPH exponentials per 4 dims), which saves a pass and a barrier.
     const size_t split = static_cast<size_t>(seq) * gridDim.x + blockIdx.x;
     float *po = p.part_o + split * NQ * 16 * 256;
     float *pml = p.part_ml + split * NQ * 16 * 2;
@@ -1025,13 +1005,21 @@ __device__ __forceinline__ void fa_decode_body(const FaDecodeParams &p) {
         const int head = (i >> 6) & 15;
         const int qi = i >> 10;
         const int kh = head >> 3, h8 = head & 7;
-        const float *wrow = wts + (qi * 16 + head) * (WPH + 2);
+        float2 ml[WPH];
+        float M = -INFINITY;
+#pragma unroll
+        for (int wv = 0; wv < WPH; ++wv) {
+            ml[wv] = *reinterpret_cast<const float2 *>(red_ml + (((kh * WPH + wv) * NQ + qi) * 8 + h8) * 2);
+            M = fmaxf(M, ml[wv].x);
+        }
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        float lsum = 0.f;
 #pragma unroll
         for (int wv = 0; wv < WPH; ++wv) {
             const float4 x = *reinterpret_cast<const float4 *>(
                 red_o + ((static_cast<size_t>(kh * WPH + wv) * NQ + qi) * 8 + h8) * L::kRedStride + d);
-            const float w = wrow[wv];
+            const float w = (ml[wv].x == -INFINITY) ? 0.f : ex2((ml[wv].x - M) * p.c);
+            lsum = fmaf(ml[wv].y, w, lsum);
             acc.x = fmaf(x.x, w, acc.x);
             acc.y = fmaf(x.y, w, acc.y);
             acc.z = fmaf(x.z, w, acc.z);
@@ -1039,8 +1027,8 @@ __device__ __forceinline__ void fa_decode_body(const FaDecodeParams &p) {
         }
         *reinterpret_cast<float4 *>(po + (qi * 16 + head) * 256 + d) = acc;
         if (d == 0) {
-            pml[(qi * 16 + head) * 2 + 0] = wrow[WPH];
-            pml[(qi * 16 + head) * 2 + 1] = wrow[WPH + 1];
+            pml[(qi * 16 + head) * 2 + 0] = M;
+            pml[(qi * 16 + head) * 2 + 1] = lsum;
         }
     }
 }
