@@ -37,8 +37,8 @@ sys.path.insert(0, os.path.join(REPO, "sqwen-moe-3090_b200"))
 N_LAYERS = 10
 N_KV = 172032
 # DRAM bytes of one decode launch at N_KV keys, from one ncu capture
-# (profiles/fa_decode_kernel_172k.txt): 99.17 MB read + 4.18 MB written.
-FA_NCU_TRAFFIC = 103_347_712
+# (profiles/fa_decode_kernel_172k.txt): 99.18 MB read + 3.89 MB written.
+FA_NCU_TRAFFIC = 103_068_672
 HEAD_DIM = 256
 N_HEAD = 16
 N_HEAD_KV = 2
@@ -703,7 +703,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                    "cuda_graph": used_graph, "cross_gpu_merge": merge_kind},
         "tokens_per_s": 1e6 / us_per_token,
         "roofline": {"bound": "hbm",
-                     "kernel": "fa_decode_kernel + fa_merge_kernel (split-KV attention, PDL-chained pair)",
+                     "kernel": "fa_decode_capped_kernel + fa_merge_narrow_kernel (split-KV attention, PDL-chained pair)",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": peak_kind, "traffic": FA_NCU_TRAFFIC if n_local == N_KV else None,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode launch "

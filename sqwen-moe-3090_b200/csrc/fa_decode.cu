@@ -1168,11 +1168,11 @@ struct FaPeerMergeParams {
     PeerExchange px;
 };
 
-// NWM: the warp order of the local merge, the same as the one-GPU merge of the decode
-// configuration (4 for the capped one-token configurations), so that the local
-// partial equals that of sqmix_fa_decode bit for bit.
+// NWM warps, in the order of the one-GPU merge of the same decode configuration (4 for
+// the capped one-token configurations, whose merge CTA fits beside a decode CTA), so that
+// the local partial equals that of sqmix_fa_decode bit for bit.
 template <int NWM, int PRE>
-__global__ void __launch_bounds__(256) fa_merge_peers_kernel(FaPeerMergeParams p) {
+__device__ __forceinline__ void fa_merge_peers_body(const FaPeerMergeParams &p) {
     __shared__ MergeSmemT<NWM> sm;
     const int row = blockIdx.x, slice = blockIdx.y;
     float gate_factor = 1.f;
@@ -1192,6 +1192,13 @@ __global__ void __launch_bounds__(256) fa_merge_peers_kernel(FaPeerMergeParams p
         p.m.out[static_cast<size_t>(row) * 256 + slice * 32 + threadIdx.x] = y * gate_factor;
         if (p.m.lse && slice == 0 && threadIdx.x == 0) p.m.lse[row] = lse;
     }
+}
+
+__global__ void __launch_bounds__(256) fa_merge_peers_kernel(FaPeerMergeParams p) {
+    fa_merge_peers_body<8, kMergePre>(p);
+}
+__global__ void __maxnreg__(kMergeNarrowRegs) fa_merge_peers_narrow_kernel(FaPeerMergeParams p) {
+    fa_merge_peers_body<4, kMergeNarrowPre>(p);
 }
 
 // Merge of normalised partials across GPUs: O = sum_p O_p e^(lse_p - L).
@@ -1338,10 +1345,12 @@ static int launch_fa(const sqmix_fa_args *a, int n_splits, cudaStream_t st, cons
         pp.m = mp;
         pp.px = *px;
         mcfg.gridDim = dim3(NQ * 16, kPeerSlices);
-        if (L::kCapped)
-            e = cudaLaunchKernelEx(&mcfg, fa_merge_peers_kernel<4, kMergeNarrowPre>, pp);
-        else
-            e = cudaLaunchKernelEx(&mcfg, fa_merge_peers_kernel<8, kMergePre>, pp);
+        if (L::kCapped) {
+            mcfg.blockDim = dim3(128);
+            e = cudaLaunchKernelEx(&mcfg, fa_merge_peers_narrow_kernel, pp);
+        } else {
+            e = cudaLaunchKernelEx(&mcfg, fa_merge_peers_kernel, pp);
+        }
         return cuda_status(e, "fa_merge_peers launch");
     }
     if (n_splits <= kSmallMergeSplits) {

@@ -86,10 +86,10 @@ __device__ __forceinline__ uint64_t peer_globaltimer() {
     return t;
 }
 
-// The exchange of one (row, 32-dim slice) of the split-KV result, by a CTA of 256
-// threads.  Warp 0's lanes hold this rank's normalised partial for dims slice*32 +
+// The exchange of one (row, 32-dim slice) of the split-KV result, by a CTA of two or
+// more warps.  Warp 0's lanes hold this rank's normalised partial for dims slice*32 +
 // lane in y_loc and the row's LSE in lse_loc.  Pushes them into every other rank's
-// buffer, waits (bounded by wait_ns; warps 1.. poll one peer's words each, in this
+// buffer, waits (bounded by wait_ns; warps 1.. poll the peers' words in turn, in this
 // rank's own memory) for every peer's publication of the same slot, and merges: y = sum_r O_r e^{lse_r - L},
 // lse = L = log sum_r e^{lse_r} (natural log).  Returns, in warp 0, whether every peer
 // arrived; on a timeout it sets bit 1 of *status and the caller writes nothing.
@@ -119,9 +119,12 @@ __device__ inline bool peer_exchange(const PeerExchange &px, int row, int slice,
         }
         s_val[px.rank][lane] = y_loc;
         if (lane == 0) s_val[px.rank][32] = lse_loc;
-    } else if (warp < px.n_ranks) {
-        const int src = warp - 1 < px.rank ? warp - 1 : warp;  // warps 1.. poll one peer each
-        {
+    } else {
+        // warps 1.. poll the peers in turn (warp w: peers w - 1, w - 1 + (warps - 1), ...;
+        // one peer each when the CTA has n_ranks warps or more)
+        const int n_warps = blockDim.x >> 5;
+        for (int k = warp - 1; k < px.n_ranks - 1; k += n_warps - 1) {
+            const int src = k < px.rank ? k : k + 1;
             const uint64_t *w = reinterpret_cast<const uint64_t *>(px.bufs[px.rank]) +
                                 peer_word(L, px.slot, par, src, row, slice, 0);
             bool ok = true;
@@ -138,9 +141,12 @@ __device__ inline bool peer_exchange(const PeerExchange &px, int row, int slice,
                 }
                 s_val[src][j] = __uint_as_float(v.x);
             }
-            if (!ok) {
-                s_ok = 0;
-                if (px.status) atomicOr(px.status, 1u);
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (lane == 0) {
+                    s_ok = 0;
+                    if (px.status) atomicOr(px.status, 1u);
+                }
+                break;
             }
         }
     }
