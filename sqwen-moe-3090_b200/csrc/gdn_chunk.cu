@@ -126,6 +126,11 @@ constexpr size_t kPrepSmem = kPrepImg + kKQImgBytes + 64 + 1024;  // + barrier, 
 
 __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     extern __shared__ uint8_t prep_raw[];
+    // q, k, v, g and beta come from the kernels before (programmatic dependent launch);
+    // the trigger comes after the wait, so the scan may read what was written two
+    // launches back (the state) before its own wait.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
     float *sm = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(prep_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *kq_img = reinterpret_cast<uint8_t *>(sm) + kPrepImg;
     uint64_t *mma_bar = reinterpret_cast<uint64_t *>(kq_img + kKQImgBytes);
@@ -573,11 +578,9 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(ChunkParams p) {
     const uint32_t tmem = *tmem_slot;
     const int row = tid;  // accumulator row (TMEM lane)
     const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
-    if (tid == 0) {
-        issue_a1(0);
-        issue_a34(0);
-    }
-    // row i = row of the state block, columns j0 .. j0 + kSN - 1: S[i][j] at ((h*128 + j)*128 + i)
+    // row i = row of the state block, columns j0 .. j0 + kSN - 1: S[i][j] at ((h*128 + j)*128 + i).
+    // The state and sel were written two or more launches back (the prep kernel triggers
+    // this launch only after its own dependency wait): read before this kernel's wait.
     const int64_t plane_elems = static_cast<int64_t>(p.h_v) * kD * kD;
     float *st_seq = p.state + static_cast<int64_t>(seq) * p.n_planes * plane_elems;
     int plane = p.sel ? p.sel[seq] : 0;
@@ -587,6 +590,13 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(ChunkParams p) {
 #pragma unroll
     for (int j = 0; j < kSN; ++j) srow[j] = st_seq[plane * plane_elems + (static_cast<int64_t>(h) * kD + j0 + j) * kD + row];
     store_k_col(sm + kSmBS, sm + kSmBS + 2 * kBSRegion, kBSRegion, row, srow);
+    // the chunk records come from the prep kernel
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+    if (tid == 0) {
+        issue_a1(0);
+        issue_a34(0);
+    }
 
     constexpr uint32_t idesc = tc::idesc_bf16_f32(128, kSN, 1, 0);
     // split-bf16 products: (A hi, B hi), (A hi, B lo), (A lo, B hi); A MN-major, B the
@@ -809,11 +819,24 @@ extern "C" int sqmix_gdn_prefill(const sqmix_gdn_args *a, void *workspace, size_
     p.sel = a->sel;
     p.plane_out = a->n_snap - 1;
     p.out = a->out;
-    gdn_chunk_prep_kernel<<<dim3(p.n_chunks, a->h_v, a->n_seqs), 256, kPrepSmem, st>>>(p);
-    cudaError_t e = cudaGetLastError();
+    // both kernels with programmatic stream serialisation: the prep overlaps the tail of
+    // the kernel before it, the scan's set-up and state load the prep's last CTAs
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.n_chunks, a->h_v, a->n_seqs);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = kPrepSmem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gdn_chunk_prep_kernel, p);
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill prep launch");
-    gdn_chunk_scan_kernel<<<dim3(kD / kSN, a->h_v, a->n_seqs), 128, kScanSmem, st>>>(p);
-    e = cudaGetLastError();
+    cfg.gridDim = dim3(kD / kSN, a->h_v, a->n_seqs);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = kScanSmem;
+    e = cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel, p);
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill scan launch");
     if (a->n_snap > 1)
         // the tail reads the plane the scan kernel just wrote: no early state read
