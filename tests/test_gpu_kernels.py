@@ -724,3 +724,36 @@ def test_fa_status_clean_after_runs(sq, oracle):
         sq.fa_status(ws)
     assert e.value.code == sq.SQMIX_ERANGE
     sq.fa_status(ws)  # cleared
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n_q", [1, 2])
+@pytest.mark.parametrize("n_rot", [0, 32, 48, 64])
+def test_fa_decode_rope_widths(sq, oracle, n_q, n_rot):
+    """Partial RoPE of width n_rot on Q inside the decode (attn.rs:183-204): widths 0, 32
+    and 64 build the one-token Q fragments from registers (each rotation pair in one
+    lane), 48 and every two-token query take the staged path; fused append of the new
+    rows with the same width."""
+    rng = np.random.default_rng(90 + n_rot + n_q)
+    n_kv = 777
+    k = rng.standard_normal((n_kv, 2, 256)).astype(np.float32)
+    v = rng.standard_normal((n_kv, 2, 256)).astype(np.float32)
+    q = rng.standard_normal((n_q, 16, 256)).astype(np.float32)
+    gate = rng.standard_normal((n_q, 16, 256)).astype(np.float32)
+    q_pos0 = n_kv - n_q
+    cap = cap_for(n_kv)
+    kc, vc = sq.new_kv_cache(cap), sq.new_kv_cache(cap)
+    sq.set_rows_q4_0(torch.from_numpy(k[:q_pos0]).cuda(), torch.from_numpy(v[:q_pos0]).cuda(),
+                     torch.arange(q_pos0, device="cuda"), kc, vc, cap, rope_n_rot=n_rot, rope_freq_base=1e7)
+    out = sq.flash_attn_ext(torch.from_numpy(q).cuda(), kc, vc, cap,
+                            torch.tensor([n_kv], dtype=torch.int64, device="cuda"),
+                            torch.tensor([q_pos0], dtype=torch.int64, device="cuda"),
+                            gate=torch.from_numpy(gate).cuda(), rope_n_rot=n_rot, rope_freq_base=1e7,
+                            k_new=torch.from_numpy(k[q_pos0:]).cuda(), v_new=torch.from_numpy(v[q_pos0:]).cuda())
+    torch.cuda.synchronize()
+    kr = oracle.rope_text(k, 0, 1e7, n_rot) if n_rot else k
+    kd = oracle.q4_0_dequantize(oracle.q4_0_quantize(kr.reshape(n_kv, 512)), 512).reshape(n_kv, 2, 256)
+    vd = oracle.q4_0_dequantize(oracle.q4_0_quantize(v.reshape(n_kv, 512)), 512).reshape(n_kv, 2, 256)
+    qr = oracle.rope_text(q, q_pos0, 1e7, n_rot) if n_rot else q
+    want = oracle.attn(qr, kd, vd, gate, q_pos0=q_pos0, scale=1 / 16)
+    assert rel_err(out.cpu().numpy(), want) <= ATTN_TOL
