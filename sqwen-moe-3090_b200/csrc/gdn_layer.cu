@@ -264,21 +264,10 @@ __global__ void __launch_bounds__(256, 1) gdn_layer_kernel(GdnLayerParams p) {
         }
     }
     cluster_arrive();  // phase 2: this CTA's shares of the norm sums are stored
-    cluster_wait();
-    if (warp == 0) {
-        const int col = col0 + lane;
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            if (t >= p.T) break;
-            const float tot = nsum[0][t] + nsum[1][t] + nsum[2][t] + nsum[3][t];
-            float yv = ov[t] * (1.0f / sqrtf(tot / 128.0f + p.norm_eps));
-            yv = yv * nw;
-            if (p.z) yv = yv * silu_f(zv[t]);
-            p.out[((static_cast<int64_t>(seq) * p.T + t) * p.h_v + hv) * 128 + col] = yv;
-        }
-    }
-
     // ---- 6. conv-history slots: plane s <- conv_input rows [T - s, T - s + K - 1) ---
+    // (every CTA of the cluster has read the history plane: phase 1 above).  Issued
+    // between the phase-2 arrive and wait: before the arrive, its release would wait for
+    // these global stores; here they drain while the head's norm sums arrive.
     for (int s = 0; s < p.n_snap; ++s) {
         const int r0 = p.T - s;
         if (rank == 0) {  // the q/k channels of this head, once per cluster
@@ -300,6 +289,19 @@ __global__ void __launch_bounds__(256, 1) gdn_layer_kernel(GdnLayerParams p) {
                     if (rr == r0 + r) v = inv[rr];
                 cst[s * cplane + static_cast<size_t>(chv) * (K - 1) + r] = v;
             }
+        }
+    }
+    cluster_wait();
+    if (warp == 0) {
+        const int col = col0 + lane;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            if (t >= p.T) break;
+            const float tot = nsum[0][t] + nsum[1][t] + nsum[2][t] + nsum[3][t];
+            float yv = ov[t] * (1.0f / sqrtf(tot / 128.0f + p.norm_eps));
+            yv = yv * nw;
+            if (p.z) yv = yv * silu_f(zv[t]);
+            p.out[((static_cast<int64_t>(seq) * p.T + t) * p.h_v + hv) * 128 + col] = yv;
         }
     }
 }
