@@ -149,6 +149,13 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     const int t0 = c * kC;
     const int n_valid = min(kC, p.T - t0);
 
+    // The raw gates of token tid, loaded with the rows below (one round trip for both).
+    float graw = 0.f, braw = 0.f;
+    if (tid < kC && tid < n_valid) {
+        const int64_t gb = (static_cast<int64_t>(seq) * p.T_all + t0 + tid) * p.h_v + h;
+        graw = p.g[gb];
+        braw = p.beta[gb];
+    }
     // rows: warp w loads rows w, w+8, ..., w+56.  The raw words of every row are loaded
     // before any is converted, so all 24 loads of a thread are in flight together.
     {
@@ -251,11 +258,10 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
         }
     }
     if (tid < kC) {
-        const int64_t gb = (static_cast<int64_t>(seq) * p.T_all + t0 + tid) * p.h_v + h;
         float gv = 0.f, bv = 0.f;
         if (tid < n_valid) {
-            gv = p.g[gb];
-            bv = p.beta[gb];
+            gv = graw;
+            bv = braw;
             gdn_gates(gv, bv, p.dt_bias, p.ssm_a, p.h_v_off + h);
         }
         gg[tid] = gv;
@@ -343,9 +349,12 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
             }
     }
     // B = [diag(beta e^G) K | diag(beta) V] (K index s = token, N = 256) as the MN-major
-    // split-bf16 image over the consumed [K ; Q] image: 4 blocks of 64 columns x 64 rows
+    // split-bf16 image over the consumed [K ; Q] image: 4 blocks of 64 columns x 64 rows.
+    // Warp w builds block w / 2, rows 32 (w % 2) + lane: the rows a quarter-warp reads
+    // (stride kLd) and the 16-byte chunks it stores (swizzled by row) fall in distinct
+    // banks (four lanes per row, one per block, hit the same banks four ways).
     {
-        const int s2 = tid >> 2, blk = tid & 3;
+        const int s2 = tid & 63, blk = tid >> 6;
         const float *src = blk < 2 ? Ks + s2 * kLd + 64 * blk : Vs + s2 * kLd + 64 * (blk - 2);
         const float f = bt[s2] * (blk < 2 ? eG[s2] : 1.f);
         float v[64];
