@@ -434,7 +434,8 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     // ---- epilogue: the chunk record --------------------------------------------------
     //   warps 0, 1: W rows t (TMEM lanes 0..63, columns 0..127) -> A1 rows t (K-major)
     //   warps 4, 5: U rows t (TMEM lanes 0..63, columns 128..255) -> U f32
-    //   warps 2, 3: Qs rows t -> A1 rows 64 + t;  warps 6, 7: K' rows t (A4), M rows s (A3)
+    //   warps 2, 3: Qs rows t -> A1 rows 64 + t;  warps 6, 7: K' rows t (A4);
+    //   warps 4, 5 also M rows s (A3), so that no warp converts more than two row images
     uint8_t *wsc = chunk_ws(p, seq, h, c);
     float *Ub = reinterpret_cast<float *>(wsc + kOffUb);
     const float GC = G[kC - 1];
@@ -459,6 +460,12 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
                 for (int q = 0; q < 16; ++q) urow[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
             }
         }
+        if (cb != 0) {  // warps 4, 5 (U needs no conversion): M rows s (A3) as well
+            float v[kC];
+#pragma unroll
+            for (int t2 = 0; t2 < kC; ++t2) v[t2] = Mq[t2 * (kC + 1) + t];
+            store_mn_row(wsc + kOffA3, wsc + kOffA3 + kA3Bytes / 2, t, v);
+        }
     } else if (warp == 2 || warp == 3) {
         const int t = tid - 64;
         const float f = eG[t] * (1.0f / sqrtf(128.0f));
@@ -479,10 +486,6 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
             for (int i = 0; i < 64; ++i) v[i] = Ks[t * kLd + 64 * blk + i] * dk;
             store_mn_row(wsc + kOffA4 + blk * kC * 128, wsc + kOffA4 + kA4Bytes / 2 + blk * kC * 128, t, v);
         }
-        float v[kC];
-#pragma unroll
-        for (int t2 = 0; t2 < kC; ++t2) v[t2] = Mq[t2 * (kC + 1) + t];
-        store_mn_row(wsc + kOffA3, wsc + kOffA3 + kA3Bytes / 2, t, v);
     }
     if (tid == 0) reinterpret_cast<float *>(wsc + kOffSb)[0] = expf(GC);
     tc::fence_before();
