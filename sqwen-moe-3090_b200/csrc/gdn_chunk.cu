@@ -379,15 +379,27 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
             x[cc][0] = l == col ? 1.f : 0.f;
             x[cc][1] = l + 32 == col ? 1.f : 0.f;
         }
+        // Steps that change nothing are skipped (the chain of column 8w .. 8w + 7 starts at
+        // row 8w: the rows above are zero; from step 32 on, rows < 32 are final since
+        // A_ts = 0 for t < s), so warp w runs 63 - 8w steps and the second half updates
+        // one row per lane.  The skipped updates would add exact zeros.
+        const int s_first = 8 * warp;
 #pragma unroll 2
-        for (int s2 = 0; s2 < kC - 1; ++s2) {
+        for (int s2 = s_first; s2 < 32; ++s2) {
             const float a0 = At[s2 * kLdA + l], a1 = At[s2 * kLdA + l + 32];
-            const int src = s2 & 31;
-            const bool hi = s2 >= 32;
 #pragma unroll
             for (int cc = 0; cc < 8; ++cc) {
-                const float xs = __shfl_sync(0xffffffffu, hi ? x[cc][1] : x[cc][0], src);
+                const float xs = __shfl_sync(0xffffffffu, x[cc][0], s2);
                 x[cc][0] = fmaf(-a0, xs, x[cc][0]);
+                x[cc][1] = fmaf(-a1, xs, x[cc][1]);
+            }
+        }
+#pragma unroll 2
+        for (int s2 = s_first > 32 ? s_first : 32; s2 < kC - 1; ++s2) {
+            const float a1 = At[s2 * kLdA + l + 32];
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                const float xs = __shfl_sync(0xffffffffu, x[cc][1], s2 - 32);
                 x[cc][1] = fmaf(-a1, xs, x[cc][1]);
             }
         }
