@@ -363,8 +363,8 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
         store_mn_row(kq_img + blk * kC * 128, kq_img + 4 * kC * 128 + blk * kC * 128, s2, v);
     }
     __syncthreads();  // A complete; V consumed (its space takes the T image below)
-    // T = (I + A)^-1 by right-looking forward substitution: warp w solves columns
-    // 8w .. 8w + 7, lane l holding rows l and l + 32 of each.  At step s, row s of every
+    // T = (I + A)^-1 by right-looking forward substitution: a warp solves 8 columns,
+    // lane l holding rows l and l + 32 of each.  At step s, row s of every
     // column is final; it is broadcast from its lane and subtracted, times A_ts, from
     // all rows t (A_ts = 0 for t <= s, so earlier rows are unchanged).  A is read
     // transposed (At[s][t]: conflict-free).  Column j of T is row j of the MN-major
@@ -372,18 +372,22 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
     uint8_t *t_img = reinterpret_cast<uint8_t *>(Vs);  // hi 8 KB | lo 8 KB (1024-aligned)
     {
         const int l = lane;
+        // column block of this warp: warps w and w + 4 (one scheduler) take blocks w and
+        // 7 - w, whose chains (63 - 8 block steps) add up to the same length on every
+        // scheduler
+        const int cb = warp < 4 ? warp : 11 - warp;
         float x[8][2];
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
-            const int col = 8 * warp + cc;
+            const int col = 8 * cb + cc;
             x[cc][0] = l == col ? 1.f : 0.f;
             x[cc][1] = l + 32 == col ? 1.f : 0.f;
         }
-        // Steps that change nothing are skipped (the chain of column 8w .. 8w + 7 starts at
-        // row 8w: the rows above are zero; from step 32 on, rows < 32 are final since
-        // A_ts = 0 for t < s), so warp w runs 63 - 8w steps and the second half updates
+        // Steps that change nothing are skipped (the chain of columns 8b .. 8b + 7 starts at
+        // row 8b: the rows above are zero; from step 32 on, rows < 32 are final since
+        // A_ts = 0 for t < s), so block b takes 63 - 8b steps and the second half updates
         // one row per lane.  The skipped updates would add exact zeros.
-        const int s_first = 8 * warp;
+        const int s_first = 8 * cb;
 #pragma unroll 2
         for (int s2 = s_first; s2 < 32; ++s2) {
             const float a0 = At[s2 * kLdA + l], a1 = At[s2 * kLdA + l + 32];
@@ -405,7 +409,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
         }
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
-            const int col = 8 * warp + cc;
+            const int col = 8 * cb + cc;
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const int t = l + 32 * e;
