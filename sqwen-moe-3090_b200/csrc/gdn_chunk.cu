@@ -215,11 +215,21 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
                     fk[r] += __shfl_xor_sync(0xffffffffu, fk[r], off);
                     fq[r] += __shfl_xor_sync(0xffffffffu, fq[r], off);
                 }
+            // every lane holds the 16 sums; lane i < 16 turns sum i (k rows, then q rows)
+            // into its factor and the warp shares them (one square root and division per
+            // lane instead of sixteen, the same arithmetic)
             const float r2 = 1.0f / sqrtf(128.0f);
+            float mine = fk[0];
 #pragma unroll
             for (int r = 0; r < 8; ++r) {
-                fk[r] = 1.0f / sqrtf(fk[r] / 128.0f + p.l2_eps / 128.0f) * r2;
-                fq[r] = 1.0f / sqrtf(fq[r] / 128.0f + p.l2_eps / 128.0f) * r2;
+                mine = lane == r ? fk[r] : mine;
+                mine = lane == 8 + r ? fq[r] : mine;
+            }
+            const float f = 1.0f / sqrtf(mine / 128.0f + p.l2_eps / 128.0f) * r2;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                fk[r] = __shfl_sync(0xffffffffu, f, r);
+                fq[r] = __shfl_sync(0xffffffffu, f, 8 + r);
             }
         }
 #pragma unroll
