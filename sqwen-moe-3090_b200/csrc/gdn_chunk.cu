@@ -92,6 +92,15 @@ __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16 &hi, __nv_bflo
     hi = __float2bfloat16_rn(x);
     lo = __float2bfloat16_rn(x - __bfloat162float(hi));
 }
+// split_bf16 of two values at once, as packed words (a in the low half): the same
+// roundings with paired conversions
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
 // One 64-element row r of an MN-major 128-byte-swizzled block, as hi and lo images
 // (generic-proxy stores; the row is 128 bytes, chunk q at q ^ (r & 7)).
 __device__ __forceinline__ void store_mn_row(uint8_t *blk_hi, uint8_t *blk_lo, int r, const float *v) {
@@ -99,13 +108,7 @@ __device__ __forceinline__ void store_mn_row(uint8_t *blk_hi, uint8_t *blk_lo, i
     for (int q = 0; q < 8; ++q) {
         uint32_t h[4], l[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            __nv_bfloat16 h0, l0, h1, l1;
-            split_bf16(v[8 * q + 2 * e], h0, l0);
-            split_bf16(v[8 * q + 2 * e + 1], h1, l1);
-            h[e] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
-            l[e] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
-        }
+        for (int e = 0; e < 4; ++e) split_bf16x2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1], h[e], l[e]);
         const int off = r * 128 + ((q ^ (r & 7)) << 4);
         *reinterpret_cast<uint4 *>(blk_hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
         *reinterpret_cast<uint4 *>(blk_lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
@@ -252,15 +255,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(ChunkParams p) {
                 const int row = t + 64 * which;
                 uint32_t hw[2], lw[2];
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    __nv_bfloat16 h0, l0, h1, l1;
-                    split_bf16(xv[2 * e], h0, l0);
-                    split_bf16(xv[2 * e + 1], h1, l1);
-                    hw[e] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) |
-                            (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
-                    lw[e] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) |
-                            (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
-                }
+                for (int e = 0; e < 2; ++e) split_bf16x2(xv[2 * e], xv[2 * e + 1], hw[e], lw[e]);
                 const int off = (lane >> 4) * 16384 + row * 128 + ((((lane & 15) >> 1) ^ (row & 7)) << 4) + (lane & 1) * 8;
                 *reinterpret_cast<uint2 *>(kq_img + off) = make_uint2(hw[0], hw[1]);
                 *reinterpret_cast<uint2 *>(kq_img + kKQImgBytes / 2 + off) = make_uint2(lw[0], lw[1]);
