@@ -121,28 +121,43 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(ConvParams p) {
     }
     const bool norm = p.eps > 0.f && hb * 128 < p.n_qk;
     float *o = p.out + (static_cast<size_t>(seq) * p.T + t0) * p.C + c0;
+    float y[TC][4];
 #pragma unroll
-    for (int j = 0; j < TC; ++j) {
-        float y[4];
+    for (int j = 0; j < TC; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             float s = 0.f;
 #pragma unroll
             for (int k = 0; k < K; ++k) s = __fadd_rn(s, __fmul_rn(in[j + k][e], w[e][k]));
-            y[e] = silu(s);
+            y[j][e] = silu(s);
         }
-        if (norm) {  // x / ||x|| as scale(rms_norm(x, eps / 128), 1 / sqrt(128)), gdn.rs:133-142
-            float ss = y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3];
+    if (norm) {  // x / ||x|| as scale(rms_norm(x, eps / 128), 1 / sqrt(128)), gdn.rs:133-142
+        float ss[TC];
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-            const float sc = 1.0f / sqrtf(ss / 128.0f + p.eps / 128.0f);
-            const float s2 = 1.0f / sqrtf(128.0f);
+        for (int j = 0; j < TC; ++j) ss[j] = y[j][0] * y[j][0] + y[j][1] * y[j][1] + y[j][2] * y[j][2] + y[j][3] * y[j][3];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) y[e] = (y[e] * sc) * s2;
+        for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int j = 0; j < TC; ++j) ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], off);
+        // every lane holds the TC sums; lane j turns token j's into its factor and the
+        // warp shares them (one square root and division per lane instead of TC)
+        float mine = ss[0];
+#pragma unroll
+        for (int j = 1; j < TC; ++j) mine = lane == j ? ss[j] : mine;
+        const float f = 1.0f / sqrtf(mine / 128.0f + p.eps / 128.0f);
+        const float s2 = 1.0f / sqrtf(128.0f);
+#pragma unroll
+        for (int j = 0; j < TC; ++j) {
+            const float sc = __shfl_sync(0xffffffffu, f, j);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) y[j][e] = (y[j][e] * sc) * s2;
         }
-        if (j < nt)
-            *reinterpret_cast<float4 *>(o + static_cast<size_t>(j) * p.C) = make_float4(y[0], y[1], y[2], y[3]);
     }
+#pragma unroll
+    for (int j = 0; j < TC; ++j)
+        if (j < nt)
+            *reinterpret_cast<float4 *>(o + static_cast<size_t>(j) * p.C) =
+                make_float4(y[j][0], y[j][1], y[j][2], y[j][3]);
 
     // History slots (first chunk only, after all of its reads): plane s <- conv_input
     // rows [max(T - s, 0), +K-1).  Rows held in in[] (the history and this chunk's x
